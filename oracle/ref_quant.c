@@ -1,0 +1,518 @@
+/*
+ * oracle/ref_quant.c -- det-quant restated in C, plus the CLI runtime canary
+ * and quant-kernel-hash generators (TEST INFRASTRUCTURE, see ref.h).
+ *
+ * Follows crates/det-quant/src/lib.rs (scalar paths; the reference's SIMD
+ * paths are bit-equal to them by its own test at lib.rs:1246-1262) and
+ * crates/det-cli/src/main.rs:146-388.
+ */
+#include <stdlib.h>
+
+#include "ref.h"
+#include "ref_internal.h"
+
+int ref_rmsnorm(const float* x, const float* w, size_t n, float eps, float* out);
+
+/* det-quant lib.rs:175-181 */
+static int32_t round_half_away_from_zero_i32(float x) {
+    if (x < 0.0f) return f32_as_i32(x - 0.5f);
+    return f32_as_i32(x + 0.5f);
+}
+
+/* det-quant lib.rs:184-187 */
+static int32_t nearest_i32_ggml(float x) {
+    float val = x + 12582912.0f;
+    return ((int32_t)f2u(val) & 0x007fffff) - 0x00400000;
+}
+
+/* det-quant lib.rs:111-137 */
+static int quantize_q8a_block(const float* in, ref_q8a_block* out) {
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float x = in[i];
+        if (!isfinite_f(x)) return REF_ERR_NONFINITE;
+        float ax = x < 0.0f ? -x : x;
+        if (ax > amax) amax = ax;
+    }
+    memset(out->q, 0, 32);
+    if (amax == 0.0f) {
+        out->d = 0.0f;
+        return REF_OK;
+    }
+    float d = amax / 127.0f;
+    for (int i = 0; i < 32; i++) {
+        int32_t r = round_half_away_from_zero_i32(in[i] / d);
+        if (r < -127) r = -127;
+        if (r > 127) r = 127;
+        out->q[i] = (int8_t)r;
+    }
+    out->d = d;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:139-172 */
+static int quantize_q8k_block(const float* in, ref_q8k_block* out) {
+    float amax = 0.0f, max = 0.0f;
+    for (int i = 0; i < 256; i++) {
+        float x = in[i];
+        if (!isfinite_f(x)) return REF_ERR_NONFINITE;
+        float ax = x < 0.0f ? -x : x;
+        if (ax > amax) {
+            amax = ax;
+            max = x;
+        }
+    }
+    memset(out->q, 0, sizeof out->q);
+    memset(out->bsums, 0, sizeof out->bsums);
+    if (amax == 0.0f) {
+        out->d = 0.0f;
+        return REF_OK;
+    }
+    float iscale = -127.0f / max;
+    for (int i = 0; i < 256; i++) {
+        int32_t r = nearest_i32_ggml(iscale * in[i]);
+        if (r > 127) r = 127;
+        out->q[i] = (int8_t)r;
+    }
+    for (int b = 0; b < 16; b++) {
+        int16_t s = 0;
+        for (int j = 0; j < 16; j++) s = (int16_t)(s + out->q[16 * b + j]);
+        out->bsums[b] = s;
+    }
+    out->d = 1.0f / iscale;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:67-80 (an empty or ragged input is InvalidBlockLength,
+ * which det-model maps to Shape) */
+int ref_quantize_q8a(const float* x, size_t n, ref_q8a_block* out) {
+    if (n == 0 || n % 32 != 0) return REF_ERR_SHAPE;
+    for (size_t b = 0; b < n / 32; b++) {
+        int st = quantize_q8a_block(x + 32 * b, out + b);
+        if (st) return st;
+    }
+    return REF_OK;
+}
+
+/* det-quant lib.rs:92-105 */
+int ref_quantize_q8k(const float* x, size_t n, ref_q8k_block* out) {
+    if (n == 0 || n % 256 != 0) return REF_ERR_SHAPE;
+    for (size_t b = 0; b < n / 256; b++) {
+        int st = quantize_q8k_block(x + 256 * b, out + b);
+        if (st) return st;
+    }
+    return REF_OK;
+}
+
+int ref_quantize_q8a_flat(const float* x, size_t n, float* d, int8_t* q) {
+    if (n == 0 || n % 32 != 0) return REF_ERR_SHAPE;
+    ref_q8a_block* blk = (ref_q8a_block*)malloc(sizeof(ref_q8a_block) * (n / 32));
+    if (!blk) return REF_ERR_ALLOC;
+    int st = ref_quantize_q8a(x, n, blk);
+    if (st == REF_OK) {
+        for (size_t b = 0; b < n / 32; b++) {
+            d[b] = blk[b].d;
+            memcpy(q + 32 * b, blk[b].q, 32);
+        }
+    }
+    free(blk);
+    return st;
+}
+
+int ref_quantize_q8k_flat(const float* x, size_t n, float* d, int8_t* q, int16_t* bsums) {
+    if (n == 0 || n % 256 != 0) return REF_ERR_SHAPE;
+    ref_q8k_block* blk = (ref_q8k_block*)malloc(sizeof(ref_q8k_block) * (n / 256));
+    if (!blk) return REF_ERR_ALLOC;
+    int st = ref_quantize_q8k(x, n, blk);
+    if (st == REF_OK) {
+        for (size_t b = 0; b < n / 256; b++) {
+            d[b] = blk[b].d;
+            memcpy(q + 256 * b, blk[b].q, 256);
+            if (bsums) memcpy(bsums + 16 * b, blk[b].bsums, 32);
+        }
+    }
+    free(blk);
+    return st;
+}
+
+/* det-quant lib.rs:423-430 (scalar block kernel) */
+float ref_dot_q8_0_q8a_block(const ref_q8a_block* w, const ref_q8a_block* a) {
+    int32_t isum = 0;
+    for (int i = 0; i < 32; i++) isum += (int32_t)w->q[i] * (int32_t)a->q[i];
+    float scale = w->d * a->d;
+    return scale * (float)isum;
+}
+
+/* det-quant lib.rs:455-466 */
+float ref_dot_q4_0_q8a_block(const ref_q4_0_block* w, const ref_q8a_block* a) {
+    int32_t isum = 0;
+    for (int i = 0; i < 16; i++) {
+        uint8_t p = w->qs[i];
+        int32_t lo = (int32_t)(p & 0x0f) - 8;
+        int32_t hi = (int32_t)(p >> 4) - 8;
+        isum += lo * (int32_t)a->q[i];
+        isum += hi * (int32_t)a->q[i + 16];
+    }
+    float scale = w->d * a->d;
+    return scale * (float)isum;
+}
+
+/* det-quant lib.rs:237-257 */
+int ref_dot_q8_0_q8a(const ref_q8a_block* w, const ref_q8a_block* a, size_t nb, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sum = 0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        if (!isfinite_f(w[b].d) || !isfinite_f(a[b].d)) return REF_ERR_NONFINITE;
+        float c = ref_dot_q8_0_q8a_block(&w[b], &a[b]);
+        if (!isfinite_f(c)) return REF_ERR_NONFINITE;
+        sum += c;
+        if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+    }
+    *out = sum;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:259-279 */
+int ref_dot_q4_0_q8a(const ref_q4_0_block* w, const ref_q8a_block* a, size_t nb, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sum = 0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        if (!isfinite_f(w[b].d) || !isfinite_f(a[b].d)) return REF_ERR_NONFINITE;
+        float c = ref_dot_q4_0_q8a_block(&w[b], &a[b]);
+        if (!isfinite_f(c)) return REF_ERR_NONFINITE;
+        sum += c;
+        if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+    }
+    *out = sum;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:519-529 */
+static void q4_k_scale_min(const uint8_t s[12], int idx, uint8_t* scale, uint8_t* min) {
+    if (idx < 4) {
+        *scale = s[idx] & 0x3f;
+        *min = s[idx + 4] & 0x3f;
+    } else {
+        *scale = (uint8_t)((s[idx + 4] & 0x0f) | ((s[idx - 4] >> 6) << 4));
+        *min = (uint8_t)((s[idx + 4] >> 4) | ((s[idx] >> 6) << 4));
+    }
+}
+
+/* det-quant lib.rs:506-517 */
+float ref_q4_k_value(const ref_q4k_block* w, size_t index) {
+    int sub = (int)(index / 32);
+    int within = (int)(index % 32);
+    uint8_t sc, mn;
+    q4_k_scale_min(w->scales, sub, &sc, &mn);
+    uint8_t byte = w->qs[(sub / 2) * 32 + within];
+    uint8_t q = (sub % 2 == 0) ? (byte & 0x0f) : (byte >> 4);
+    return (w->d * (float)sc) * (float)q - (w->dmin * (float)mn);
+}
+
+/* det-quant lib.rs:536-553 */
+static int8_t q6_k_quant(const ref_q6k_block* w, size_t index) {
+    size_t half = index / 128, within = index % 128, l = within % 32, part = within / 32;
+    size_t ql_base = half * 64, qh_base = half * 32;
+    uint8_t ql;
+    int shift;
+    switch (part) {
+        case 0: ql = w->ql[ql_base + l] & 0x0f; shift = 0; break;
+        case 1: ql = w->ql[ql_base + l + 32] & 0x0f; shift = 2; break;
+        case 2: ql = w->ql[ql_base + l] >> 4; shift = 4; break;
+        default: ql = w->ql[ql_base + l + 32] >> 4; shift = 6; break;
+    }
+    uint8_t high = (uint8_t)(((w->qh[qh_base + l] >> shift) & 0x03) << 4);
+    return (int8_t)((int8_t)(ql | high) - 32);
+}
+
+/* det-quant lib.rs:555-568 */
+static size_t q6_k_scale_index(size_t index) {
+    size_t half = index / 128, within = index % 128, l = within % 32, part = within / 32;
+    return half * 8 + l / 16 + 2 * part;
+}
+
+/* det-quant lib.rs:531-534 */
+float ref_q6_k_value(const ref_q6k_block* w, size_t index) {
+    return (w->d * (float)w->scales[q6_k_scale_index(index)]) * (float)q6_k_quant(w, index);
+}
+
+/* det-quant lib.rs:281-315: one f32 chain over every element of the row */
+int ref_dot_q4_k_q8a(const ref_q4k_block* w, const ref_q8a_block* a, size_t nb, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sum = 0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        if (!isfinite_f(w[b].d) || !isfinite_f(w[b].dmin)) return REF_ERR_NONFINITE;
+        const ref_q8a_block* ab = a + b * 8;
+        for (size_t i = 0; i < 256; i++) {
+            const ref_q8a_block* ai = ab + i / 32;
+            if (!isfinite_f(ai->d)) return REF_ERR_NONFINITE;
+            float weight = ref_q4_k_value(&w[b], i);
+            float act = ai->d * (float)ai->q[i % 32];
+            float prod = weight * act;
+            if (!isfinite_f(prod)) return REF_ERR_NONFINITE;
+            sum += prod;
+            if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+        }
+    }
+    *out = sum;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:317-351 (defined in the reference, unused by the model) */
+int ref_dot_q6_k_q8a(const ref_q6k_block* w, const ref_q8a_block* a, size_t nb, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sum = 0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        if (!isfinite_f(w[b].d)) return REF_ERR_NONFINITE;
+        const ref_q8a_block* ab = a + b * 8;
+        for (size_t i = 0; i < 256; i++) {
+            const ref_q8a_block* ai = ab + i / 32;
+            if (!isfinite_f(ai->d)) return REF_ERR_NONFINITE;
+            float weight = ref_q6_k_value(&w[b], i);
+            float act = ai->d * (float)ai->q[i % 32];
+            float prod = weight * act;
+            if (!isfinite_f(prod)) return REF_ERR_NONFINITE;
+            sum += prod;
+            if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+        }
+    }
+    *out = sum;
+    return REF_OK;
+}
+
+/* det-quant lib.rs:353-397: 8 exact i32 lane sums per block, 8 f32 lane
+ * accumulators, then a sequential 8-term sum */
+int ref_dot_q6_k_q8k(const ref_q6k_block* w, const ref_q8k_block* a, size_t nb, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (size_t b = 0; b < nb; b++) {
+        if (!isfinite_f(w[b].d) || !isfinite_f(a[b].d)) return REF_ERR_NONFINITE;
+        int32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        size_t off = 0;
+        for (int s = 0; s < 16; s++) {
+            int32_t scale = w[b].scales[s];
+            for (int rep = 0; rep < 2; rep++) {
+                for (int lane = 0; lane < 8; lane++)
+                    aux[lane] += scale * (int32_t)a[b].q[off + lane] * (int32_t)q6_k_quant(&w[b], off + lane);
+                off += 8;
+            }
+        }
+        float d = w[b].d * a[b].d;
+        if (!isfinite_f(d)) return REF_ERR_NONFINITE;
+        for (int lane = 0; lane < 8; lane++) {
+            sums[lane] += d * (float)aux[lane];
+            if (!isfinite_f(sums[lane])) return REF_ERR_NONFINITE;
+        }
+    }
+    float sum = 0.0f;
+    for (int lane = 0; lane < 8; lane++) {
+        sum += sums[lane];
+        if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+    }
+    *out = sum;
+    return REF_OK;
+}
+
+/* ---- deterministic block generators: det-cli main.rs:273-388 ------------- */
+static ref_q8a_block gen_q8_block(uint32_t seed) {
+    ref_q8a_block b;
+    uint32_t x = seed;
+    for (int i = 0; i < 32; i++) {
+        x = x * 1103515245u + 12345u;
+        b.q[i] = (int8_t)((int16_t)((x >> 16) % 255) - 127);
+    }
+    b.d = u2f(0x3c000000u + (seed & 0xff));
+    return b;
+}
+
+static ref_q8a_block gen_q8a_block(uint32_t seed) {
+    ref_q8a_block b;
+    uint32_t x = seed;
+    for (int i = 0; i < 32; i++) {
+        x = x * 22695477u + 1u;
+        b.q[i] = (int8_t)((int16_t)((x >> 17) % 255) - 127);
+    }
+    b.d = u2f(0x3d000000u + (seed & 0xff));
+    return b;
+}
+
+static ref_q4_0_block gen_q4_block(uint32_t seed) {
+    ref_q4_0_block b;
+    uint32_t x = seed;
+    for (int i = 0; i < 16; i++) {
+        x = x * 747796405u + 2891336453u;
+        uint8_t lo = (uint8_t)((x >> 8) & 0x0f);
+        uint8_t hi = (uint8_t)((x >> 20) & 0x0f);
+        b.qs[i] = (uint8_t)(lo | (hi << 4));
+    }
+    b.d = u2f(0x3c800000u + (seed & 0xff));
+    return b;
+}
+
+static ref_q4k_block gen_q4k_block(uint32_t seed) {
+    ref_q4k_block b;
+    memset(&b, 0, sizeof b);
+    uint32_t x = seed;
+    for (int i = 0; i < 4; i++) {
+        x = x * 1664525u + 1013904223u;
+        uint8_t scale = (uint8_t)((x >> 10) & 0x3f);
+        x = x * 22695477u + 1u;
+        uint8_t min = (uint8_t)((x >> 11) & 0x3f);
+        b.scales[i] = scale & 0x3f;
+        b.scales[i + 4] = min & 0x3f;
+    }
+    for (int i = 4; i < 8; i++) {
+        x = x * 747796405u + 2891336453u;
+        uint8_t scale = (uint8_t)((x >> 8) & 0x3f);
+        x = x * 1103515245u + 12345u;
+        uint8_t min = (uint8_t)((x >> 12) & 0x3f);
+        b.scales[i + 4] = (uint8_t)((scale & 0x0f) | ((min & 0x0f) << 4));
+        b.scales[i - 4] |= (uint8_t)((scale >> 4) << 6);
+        b.scales[i] |= (uint8_t)((min >> 4) << 6);
+    }
+    for (int i = 0; i < 128; i++) {
+        x = x * 1103515245u + 12345u;
+        uint8_t lo = (uint8_t)((x >> 16) & 0x0f);
+        x = x * 747796405u + 2891336453u;
+        uint8_t hi = (uint8_t)((x >> 20) & 0x0f);
+        b.qs[i] = (uint8_t)(lo | (hi << 4));
+    }
+    b.d = u2f(0x3b000000u + (seed & 0xff));
+    b.dmin = u2f(0x3a800000u + ((seed >> 8) & 0xff));
+    return b;
+}
+
+static ref_q6k_block gen_q6_block(uint32_t seed) {
+    ref_q6k_block b;
+    uint32_t x = seed;
+    for (int i = 0; i < 128; i++) {
+        x = x * 1664525u + 1013904223u;
+        b.ql[i] = (uint8_t)(x >> 13);
+    }
+    for (int i = 0; i < 64; i++) {
+        x = x * 22695477u + 1u;
+        b.qh[i] = (uint8_t)(x >> 11);
+    }
+    for (int i = 0; i < 16; i++) {
+        x = x * 747796405u + 2891336453u;
+        b.scales[i] = (int8_t)((int16_t)((x >> 16) % 127) - 63);
+    }
+    b.d = u2f(0x3b800000u + (seed & 0xff));
+    return b;
+}
+
+static void gen_q8a_blocks_for_q4k(uint32_t seed, ref_q8a_block out[8]) {
+    for (uint32_t i = 0; i < 8; i++) out[i] = gen_q8a_block(seed + i * 0x85ebca6bu);
+}
+
+static ref_q8k_block gen_q8k_block_for_q6(uint32_t seed) {
+    float in[256];
+    for (uint32_t i = 0; i < 256; i++) {
+        uint32_t x = (seed + i * 0x9e3779b9u) * 747796405u + 2891336453u;
+        in[i] = (float)(((int32_t)(x >> 9) % 4093) - 2046) / 257.0f;
+    }
+    ref_q8k_block b;
+    quantize_q8k_block(in, &b);
+    return b;
+}
+
+/* det-cli main.rs:146-224 */
+int ref_runtime_canary_hash(uint8_t out[32]) {
+    ref_sha256_ctx h;
+    ref_sha256_init(&h);
+    for (uint32_t seed = 0; seed < 16; seed++) {
+        ref_q8a_block q8 = gen_q8_block(seed);
+        ref_q4_0_block q4 = gen_q4_block(seed ^ 0xa5a55a5au);
+        ref_q8a_block a = gen_q8a_block(seed * 1664525u + 1013904223u);
+        ref_q4k_block q4k = gen_q4k_block(seed ^ 0x9e3779b9u);
+        ref_q8a_block a4k[8];
+        gen_q8a_blocks_for_q4k(seed, a4k);
+        ref_q6k_block q6 = gen_q6_block(seed ^ 0x517cc1b7u);
+        ref_q8k_block a6 = gen_q8k_block_for_q6(seed);
+        float y8 = ref_dot_q8_0_q8a_block(&q8, &a);
+        float y4 = ref_dot_q4_0_q8a_block(&q4, &a);
+        float y4k, y6;
+        int st = ref_dot_q4_k_q8a(&q4k, a4k, 1, &y4k);
+        if (st) return st;
+        st = ref_dot_q6_k_q8k(&q6, &a6, 1, &y6);
+        if (st) return st;
+        if (!isfinite_f(y8) || !isfinite_f(y4)) return REF_ERR_NONFINITE;
+        sha_update_f32(&h, y8);
+        sha_update_f32(&h, y4);
+        sha_update_f32(&h, y4k);
+        sha_update_f32(&h, y6);
+    }
+    float qin[32];
+    for (int i = 0; i < 32; i++) {
+        if (i == 0) qin[i] = u2f(1);
+        else if (i == 1) qin[i] = -u2f(2);
+        else qin[i] = (float)((i % 11) - 5) * 0.03125f;
+    }
+    ref_q8a_block q;
+    quantize_q8a_block(qin, &q);
+    sha_update_f32(&h, q.d);
+    for (int i = 0; i < 32; i++) {
+        uint8_t b = (uint8_t)q.q[i];
+        ref_sha256_update(&h, &b, 1);
+    }
+    float x[8] = {u2f(1), -0.75f, 1.25f, -2.0f, 3.5f, -4.25f, 0.5f, -0.125f};
+    float w[8] = {1.0f, -0.5f, 0.25f, -1.5f, 2.0f, -2.5f, 0.75f, -0.25f};
+    float rms[8];
+    int st = ref_rmsnorm(x, w, 8, 1e-5f, rms);
+    if (st) return st;
+    for (int i = 0; i < 8; i++) sha_update_f32(&h, rms[i]);
+    float logits[11] = {0.0f, -1.0f, 3.25f, 3.25f, -88.5f, u2f(1), -12.0f, 0.5f, -0.25f, 2.0f, -1000.0f};
+    uint32_t freq[11];
+    uint64_t cum[11], total;
+    st = ref_logits_to_cdf(logits, 11, freq, cum, &total);
+    if (st) return st;
+    for (int i = 0; i < 11; i++) {
+        uint8_t le[4] = {(uint8_t)freq[i], (uint8_t)(freq[i] >> 8), (uint8_t)(freq[i] >> 16), (uint8_t)(freq[i] >> 24)};
+        ref_sha256_update(&h, le, 4);
+    }
+    for (int i = 0; i < 11; i++) {
+        uint8_t le[8];
+        for (int k = 0; k < 8; k++) le[k] = (uint8_t)(cum[i] >> (8 * k));
+        ref_sha256_update(&h, le, 8);
+    }
+    uint8_t le[8];
+    for (int k = 0; k < 8; k++) le[k] = (uint8_t)(total >> (8 * k));
+    ref_sha256_update(&h, le, 8);
+    ref_sha256_final(&h, out);
+    return REF_OK;
+}
+
+/* det-cli main.rs:233-271 */
+int ref_quant_kernel_hash(uint8_t out[32]) {
+    ref_sha256_ctx h;
+    ref_sha256_init(&h);
+    for (uint32_t seed = 0; seed < 1000000u; seed++) {
+        ref_q8a_block q8 = gen_q8_block(seed);
+        ref_q4_0_block q4 = gen_q4_block(seed ^ 0xa5a55a5au);
+        ref_q8a_block a = gen_q8a_block(seed * 1664525u + 1013904223u);
+        float y8 = ref_dot_q8_0_q8a_block(&q8, &a);
+        float y4 = ref_dot_q4_0_q8a_block(&q4, &a);
+        if (!isfinite_f(y8) || !isfinite_f(y4)) return REF_ERR_NONFINITE;
+        sha_update_f32(&h, y8);
+        sha_update_f32(&h, y4);
+    }
+    for (uint32_t seed = 0; seed < 4096u; seed++) {
+        ref_q4k_block q4k = gen_q4k_block(seed ^ 0x9e3779b9u);
+        ref_q8a_block a4k[8];
+        gen_q8a_blocks_for_q4k(seed, a4k);
+        float y;
+        int st = ref_dot_q4_k_q8a(&q4k, a4k, 1, &y);
+        if (st) return st;
+        sha_update_f32(&h, y);
+    }
+    for (uint32_t seed = 0; seed < 4096u; seed++) {
+        ref_q6k_block q6 = gen_q6_block(seed ^ 0x517cc1b7u);
+        ref_q8k_block a6 = gen_q8k_block_for_q6(seed);
+        float y;
+        int st = ref_dot_q6_k_q8k(&q6, &a6, 1, &y);
+        if (st) return st;
+        sha_update_f32(&h, y);
+    }
+    ref_sha256_final(&h, out);
+    return REF_OK;
+}
