@@ -1,0 +1,302 @@
+// codec.cpp -- compress / decompress on the device forward.
+//
+// Reproduces det-cli's windowed codec (crates/det-cli/src/main.rs:433-855):
+// a fixed window of n_ctx positions, overlap n_ctx/4, KV reset and replay of
+// the overlap tokens at positions 0.. when the window fills, the uniform CDF
+// while the window is empty, byte escapes that do not advance the model, the
+// 56-byte DTLZ header (crates/det-coder/src/file.rs) and the canonical
+// re-encode check of decompress.
+//
+// Encode is teacher-forced, so the whole schedule is known up front: the
+// symbols are mapped to (window, logits position) pairs, each window's tokens
+// run through the device in chunks of up to `kChunk` positions, and the
+// ranges of all symbols whose logits a chunk produced come back in one call.
+// The range coder consumes them in symbol order, so the payload is the same
+// byte stream the one-token-at-a-time reference produces.  Positions whose
+// logits no symbol uses (the last token of a full window, overlap tokens of a
+// window nobody reads from) are skipped; that changes no output.
+#include <algorithm>
+#include <cstdlib>
+
+#include "host_common.h"
+
+using namespace det;
+
+namespace {
+
+constexpr uint32_t kChunk = 64;
+constexpr uint32_t kEscapes = 256;
+
+// next_window_start (det-cli main.rs:772-778)
+size_t next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t overlap) {
+  const size_t d = pos > ws ? pos - ws : 0;
+  if (d >= n_ctx) return pos > overlap ? pos - overlap : 0;
+  return ws;
+}
+
+// validate_window (det-cli main.rs:810-826)
+det_status validate_window(size_t n_ctx, size_t overlap, size_t model_ctx) {
+  if (n_ctx == 0 || n_ctx > model_ctx || overlap >= n_ctx) return DET_ERR_WINDOW;
+  return DET_OK;
+}
+
+struct SymbolPlan {
+  int32_t window;  // -1: uniform CDF (empty context)
+  int32_t pos;     // logits position within the window
+};
+
+struct WindowPlan {
+  size_t start;   // token index of position 0
+  size_t needed;  // positions that must be forwarded (max logits pos + 1)
+};
+
+// Encode the symbol stream (encode_symbols_with_model, main.rs:523-552).
+det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_ctx, uint32_t overlap, int escapes,
+                       std::vector<uint8_t>* payload) {
+  if (det_status st = validate_window(n_ctx, overlap, (size_t)m->cfg.ctx)) return st;
+  const uint32_t V = (uint32_t)m->vocab;
+  const uint32_t tail = escapes ? kEscapes : 0;
+  if ((uint64_t)V + tail > (1u << 18)) return DET_ERR_CDF_TOO_MANY_SYMBOLS;
+  const uint64_t symbols_total = (uint64_t)V + tail;
+  // ---- plan: replay the reference state machine on indices only
+  std::vector<uint32_t> tokens;
+  std::vector<SymbolPlan> plan(n);
+  std::vector<WindowPlan> windows;
+  windows.push_back({0, 0});
+  size_t ws = 0, clen = 0;
+  for (size_t i = 0; i < n; i++) {
+    const size_t pos = tokens.size();
+    const size_t nws = next_window_start(pos, ws, n_ctx, overlap);
+    if (nws != ws) {  // replay (main.rs:691-701)
+      ws = nws;
+      clen = pos - ws;
+      windows.push_back({ws, 0});
+    }
+    const uint32_t s = sym[i];
+    if (clen == 0) {
+      if (s >= symbols_total) return DET_ERR_CDF_SYMBOL_OUT_OF_RANGE;
+      plan[i] = {-1, 0};
+    } else {
+      if (s >= symbols_total) return DET_ERR_CDF_SYMBOL_OUT_OF_RANGE;
+      plan[i] = {(int32_t)windows.size() - 1, (int32_t)(clen - 1)};
+      WindowPlan& w = windows.back();
+      w.needed = std::max(w.needed, clen);
+    }
+    if (escapes && s >= V) continue;
+    if (s >= V) return DET_ERR_CDF_SYMBOL_OUT_OF_RANGE;
+    tokens.push_back(s);
+    clen++;
+  }
+  // ---- execute window by window, chunk by chunk
+  RangeEncoder enc;
+  size_t next = 0;  // next symbol to encode
+  auto drain_uniform = [&]() -> det_status {
+    while (next < n && plan[next].window < 0) {
+      if (det_status st = enc.encode(sym[next], 1, symbols_total)) return st;
+      next++;
+    }
+    return DET_OK;
+  };
+  if (det_status st = drain_uniform()) return st;
+  det_session* s = nullptr;
+  bool need_device = false;
+  for (const auto& w : windows)
+    if (w.needed) need_device = true;
+  if (need_device)
+    if (det_status st = det_session_create(m, n_ctx, kChunk, &s)) return st;
+  std::vector<uint32_t> rows, qsym;
+  std::vector<det_symbol_range> ranges;
+  det_status st = DET_OK;
+  for (size_t wi = 0; wi < windows.size() && !st; wi++) {
+    const WindowPlan& w = windows[wi];
+    if (w.needed == 0) continue;
+    if (wi > 0) st = det_session_reset(s);
+    for (size_t p0 = 0; p0 < w.needed && !st; p0 += kChunk) {
+      const uint32_t cnt = (uint32_t)std::min<size_t>(kChunk, w.needed - p0);
+      st = det_forward(s, tokens.data() + w.start + p0, cnt, (uint32_t)p0, nullptr);
+      if (st) break;
+      rows.clear();
+      qsym.clear();
+      size_t j = next;
+      for (; j < n; j++) {
+        const SymbolPlan& sp = plan[j];
+        if (sp.window < 0) {
+          // a uniform symbol after a device window can only follow a window
+          // with no tokens, which cannot happen mid-stream
+          break;
+        }
+        if ((size_t)sp.window != wi || (size_t)sp.pos >= p0 + cnt) break;
+        rows.push_back((uint32_t)(sp.pos - p0));
+        qsym.push_back(sym[j]);
+      }
+      ranges.resize(rows.size());
+      if (!rows.empty()) st = det_symbol_ranges(s, rows.data(), qsym.data(), (uint32_t)rows.size(), escapes,
+                                                ranges.data());
+      for (size_t k = 0; k < rows.size() && !st; k++) st = enc.encode(ranges[k].cum, ranges[k].freq, ranges[k].total);
+      next = j;
+      if (!st) st = drain_uniform();
+    }
+  }
+  if (s) det_session_free(s);
+  if (st) return st;
+  if (next != n) return DET_ERR_WINDOW;
+  *payload = enc.finish();
+  return DET_OK;
+}
+
+det_status copy_out(const std::vector<uint8_t>& v, uint8_t** out, size_t* out_len) {
+  uint8_t* p = static_cast<uint8_t*>(std::malloc(v.size() ? v.size() : 1));
+  if (!p) return DET_ERR_ALLOC;
+  if (!v.empty()) std::memcpy(p, v.data(), v.size());
+  *out = p;
+  *out_len = v.size();
+  return DET_OK;
+}
+
+// LoadedModel checks (det-cli main.rs:954-1008)
+det_status codec_model_checks(det_model* m) {
+  if (m->tok_status) return m->tok_status;
+  if (m->tok_vocab != (size_t)m->vocab) return DET_ERR_VOCAB_MISMATCH;
+  if ((uint64_t)m->vocab + kEscapes > (1u << 18)) return DET_ERR_CDF_TOO_MANY_SYMBOLS;
+  return DET_OK;
+}
+
+void put_le(uint8_t* p, uint64_t v, int n) {
+  for (int i = 0; i < n; i++) p[i] = (uint8_t)(v >> (8 * i));
+}
+uint64_t get_le(const uint8_t* p, int n) {
+  uint64_t v = 0;
+  for (int i = n - 1; i >= 0; i--) v = (v << 8) | p[i];
+  return v;
+}
+
+}  // namespace
+
+extern "C" {
+
+det_status det_encode_symbols(det_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx, uint32_t overlap,
+                              int byte_escapes, uint8_t** out, size_t* out_len) {
+  if (!m || (!symbols && n) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  std::vector<uint8_t> payload;
+  if (det_status st = encode_impl(m, symbols, n, n_ctx, overlap, byte_escapes, &payload)) return st;
+  return copy_out(payload, out, out_len);
+}
+
+// compress (det-cli main.rs:433-463)
+det_status det_compress(det_model* m, const uint8_t* input, size_t len, uint32_t n_ctx, uint8_t** out,
+                        size_t* out_len) {
+  if (!m || (!input && len) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  if (det_status st = codec_model_checks(m)) return st;
+  const uint32_t V = (uint32_t)m->vocab;
+  std::vector<uint32_t> sym(len);
+  for (size_t i = 0; i < len; i++) {  // codec_symbols (det-token lib.rs:150-180)
+    const int32_t t = m->byte_to_token[input[i]];
+    sym[i] = t >= 0 ? (uint32_t)t : V + input[i];
+  }
+  const uint32_t ctx = n_ctx ? n_ctx : (uint32_t)m->cfg.ctx;
+  const uint32_t overlap = ctx / 4;
+  std::vector<uint8_t> payload;
+  if (det_status st = encode_impl(m, sym.data(), len, ctx, overlap, 1, &payload)) return st;
+  std::vector<uint8_t> file(56 + payload.size());
+  std::memcpy(file.data(), "DTLZ", 4);  // DtlzHeader::encode (file.rs:28-38)
+  put_le(&file[4], 1, 2);
+  put_le(&file[6], 1, 2);  // FLAG_BYTE_ESCAPES
+  std::memcpy(&file[8], m->sha, 32);
+  put_le(&file[40], ctx, 4);
+  put_le(&file[44], overlap, 4);
+  put_le(&file[48], len, 8);
+  std::memcpy(&file[56], payload.data(), payload.size());
+  return copy_out(file, out, out_len);
+}
+
+// decompress (det-cli main.rs:465-511) with decode_bytes_with_model
+// (:585-630): one symbol at a time (the next token depends on the decoded
+// one), then the canonical re-encode through the chunked encoder.
+det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t** out, size_t* out_len) {
+  if (!m || (!dtlz && len) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  // DtlzHeader::decode (file.rs:58-90)
+  if (len < 56) return DET_ERR_FILE_TOO_SHORT;
+  if (std::memcmp(dtlz, "DTLZ", 4) != 0) return DET_ERR_FILE_BAD_MAGIC;
+  if (get_le(dtlz + 4, 2) != 1) return DET_ERR_FILE_UNSUPPORTED_VERSION;
+  const uint32_t flags = (uint32_t)get_le(dtlz + 6, 2);
+  if (flags & ~1u) return DET_ERR_FILE_UNSUPPORTED_FLAGS;
+  const uint32_t n_ctx = (uint32_t)get_le(dtlz + 40, 4), overlap = (uint32_t)get_le(dtlz + 44, 4);
+  const uint64_t orig_len = get_le(dtlz + 48, 8);
+  if (n_ctx == 0) return DET_ERR_FILE_INVALID_CONTEXT;
+  if (overlap >= n_ctx) return DET_ERR_FILE_INVALID_OVERLAP;
+  if (det_status st = codec_model_checks(m)) return st;
+  if (std::memcmp(m->sha, dtlz + 8, 32) != 0) return DET_ERR_MODEL_HASH_MISMATCH;
+  if (det_status st = validate_window(n_ctx, overlap, (size_t)m->cfg.ctx)) return st;
+  const int escapes = (flags & 1) != 0;
+  const uint32_t V = (uint32_t)m->vocab, tail = escapes ? kEscapes : 0;
+  const uint64_t symbols_total = (uint64_t)V + tail;
+  const uint8_t* payload = dtlz + 56;
+  const size_t plen = len - 56;
+  RangeDecoder dec;
+  if (det_status st = dec.init(payload, plen)) return st;
+  det_session* s = nullptr;
+  if (det_status st = det_session_create(m, n_ctx, kChunk, &s)) return st;
+  std::vector<uint8_t> bytes;
+  std::vector<uint32_t> ctx, syms;
+  size_t ws = 0, clen = 0;
+  uint32_t last_row = 0;
+  det_status st = DET_OK;
+  while (!st && bytes.size() < orig_len) {
+    const size_t pos = ctx.size();
+    const size_t nws = next_window_start(pos, ws, n_ctx, overlap);
+    if (nws != ws) {  // replay the overlap as chunked prefill
+      ws = nws;
+      clen = 0;
+      st = det_session_reset(s);
+      for (size_t p = ws; p < pos && !st; p += kChunk) {
+        const uint32_t cnt = (uint32_t)std::min<size_t>(kChunk, pos - p);
+        st = det_forward(s, ctx.data() + p, cnt, (uint32_t)clen, nullptr);
+        clen += cnt;
+        last_row = cnt - 1;
+      }
+      if (st) break;
+    }
+    uint32_t symbol;
+    if (clen == 0) {  // uniform CDF (decode_symbol, main.rs:813-827)
+      uint64_t value;
+      if ((st = dec.decode_freq(symbols_total, &value))) break;
+      symbol = (uint32_t)value;
+      if ((st = dec.advance(value, 1, symbols_total))) break;
+    } else {
+      uint64_t total, value;
+      det_symbol_range r;
+      if ((st = det_decoder_total(s, last_row, escapes, &total))) break;
+      if ((st = dec.decode_freq(total, &value))) break;
+      if ((st = det_decoder_lookup(s, last_row, escapes, value, &symbol, &r))) break;
+      if ((st = dec.advance(r.cum, r.freq, r.total))) break;
+    }
+    // decode_codec_symbol / detokenize_bytes (det-token lib.rs:182-199, 310-322)
+    int byte;
+    if (symbol < V) {
+      byte = symbol < m->token_to_byte.size() ? m->token_to_byte[symbol] : -1;
+      if (byte < 0) { st = DET_ERR_TOKENIZER; break; }
+    } else if (escapes && symbol < V + kEscapes) {
+      byte = (int)(symbol - V);
+    } else {
+      st = DET_ERR_TOKENIZER;
+      break;
+    }
+    bytes.push_back((uint8_t)byte);
+    syms.push_back(symbol);
+    if (escapes && symbol >= V) continue;
+    ctx.push_back(symbol);
+    if (clen >= n_ctx) { st = DET_ERR_WINDOW; break; }
+    st = det_forward(s, &symbol, 1, (uint32_t)clen, nullptr);
+    clen++;
+    last_row = 0;
+  }
+  det_session_free(s);
+  if (st) return st;
+  std::vector<uint8_t> canon;
+  if ((st = encode_impl(m, syms.data(), syms.size(), n_ctx, overlap, escapes, &canon))) return st;
+  if (canon.size() != plen || std::memcmp(canon.data(), payload, plen) != 0) return DET_ERR_NONCANONICAL;
+  bytes.resize((size_t)orig_len);
+  return copy_out(bytes, out, out_len);
+}
+
+}  // extern "C"

@@ -1,0 +1,169 @@
+// host_common.h -- host-side structures of libdetgpu.so (not public ABI).
+#pragma once
+
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/detgpu.h"
+#include "internal.h"
+
+namespace det {
+
+// ---- SHA-256 (FIPS 180-4); the logits hash and the model file hash -------
+class Sha256 {
+ public:
+  Sha256();
+  void update(const void* data, size_t len);
+  void finish(uint8_t out[32]);
+
+ private:
+  void block(const uint8_t* p);
+  uint32_t st_[8];
+  uint64_t len_ = 0;
+  uint8_t buf_[64];
+  size_t n_ = 0;
+};
+
+// ---- 64-bit range coder: RangeEncoder / RangeDecoder
+// (crates/det-coder/src/range.rs:11-178) ------------------------------------
+class RangeEncoder {
+ public:
+  det_status encode(uint64_t cum, uint64_t freq, uint64_t total);
+  std::vector<uint8_t> finish();
+
+ private:
+  uint64_t low_ = 0, range_ = ~0ull;
+  std::vector<uint8_t> out_;
+};
+
+class RangeDecoder {
+ public:
+  det_status init(const uint8_t* data, size_t len);
+  det_status decode_freq(uint64_t total, uint64_t* value);
+  det_status advance(uint64_t cum, uint64_t freq, uint64_t total);
+
+ private:
+  det_status next_byte(uint8_t* b);
+  uint64_t low_ = 0, code_ = 0, range_ = ~0ull;
+  bool pending_ = false;
+  uint64_t pend_range_ = 0, pend_total_ = 0;
+  const uint8_t* in_ = nullptr;
+  size_t len_ = 0, pos_ = 0;
+};
+
+// ---- GGUF reader (crates/det-gguf/src/lib.rs:156-528) ---------------------
+enum GgufErr : int {
+  GG_OK = 0, GG_BAD_MAGIC, GG_UNSUPPORTED_VERSION, GG_TRUNCATED, GG_UNSUPPORTED_VALUE_TYPE, GG_INVALID_UTF8,
+  GG_INVALID_TENSOR_OFFSET, GG_INVALID_TENSOR_SHAPE, GG_TENSOR_NOT_FOUND, GG_METADATA_NOT_FOUND,
+  GG_DUPLICATE_METADATA_KEY, GG_DUPLICATE_TENSOR_NAME, GG_INVALID_BOOL, GG_METADATA_TYPE_MISMATCH,
+  GG_UNSUPPORTED_TENSOR_TYPE
+};
+
+enum GgufValueType : uint32_t {
+  GV_U8 = 0, GV_I8, GV_U16, GV_I16, GV_U32, GV_I32, GV_F32, GV_BOOL, GV_STRING, GV_ARRAY, GV_U64, GV_I64, GV_F64
+};
+
+struct GgufValue {
+  uint32_t type = 0, elem_type = 0;
+  uint64_t bits = 0;       // scalar payload
+  double real = 0.0;       // F32/F64 payload
+  std::string str;         // GV_STRING
+  std::vector<std::string> strs;  // string arrays
+  const uint8_t* raw = nullptr;   // other arrays: little-endian payload
+  uint64_t count = 0;
+};
+
+struct GgufTensor {
+  std::string name;
+  std::vector<uint64_t> dims;
+  uint32_t type = 0;
+  uint64_t offset = 0;
+};
+
+class Gguf {
+ public:
+  int parse(const uint8_t* bytes, size_t len);
+  const GgufValue* find(const std::string& key) const;
+  int get_u32(const std::string& key, uint32_t* out) const;
+  int get_f32(const std::string& key, float* out) const;
+  int tensor(const std::string& name, const GgufTensor** out) const;
+  int tensor_bytes(const std::string& name, const uint8_t** data, size_t* len) const;
+  static int type_size(uint32_t type, uint64_t* bytes_per_block, uint64_t* block);
+  static int element_count(const GgufTensor& t, uint64_t* n);
+
+  std::vector<std::pair<std::string, GgufValue>> kv;
+  std::vector<GgufTensor> tensors;
+  size_t data_offset = 0;
+
+ private:
+  const uint8_t* bytes_ = nullptr;
+  size_t len_ = 0;
+};
+
+// ---- model ------------------------------------------------------------------
+struct LayerDev {
+  DevMatrix wq, wk, wv, wo, gate, up, down;
+  float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+};
+
+struct ModelCfg {
+  int L = 0, d = 0, dff = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, ctx = 0, pairing = 0;
+  float eps = 0, attn_scale = 0, rope_base = 0;
+};
+
+}  // namespace det
+
+struct det_model {
+  int device = 0;
+  det::ModelCfg cfg;
+  int vocab = 0;
+  uint8_t sha[32];
+  // byte-fallback tokenizer (det-token lib.rs:228-326)
+  det_status tok_status = DET_OK;
+  int32_t byte_to_token[256];
+  std::vector<int16_t> token_to_byte;
+  size_t tok_vocab = 0;
+  det::DevMatrix tok_embd, output;
+  bool tied = false;
+  std::vector<det::LayerDev> layers;
+  float* output_norm = nullptr;
+  std::vector<void*> allocations;
+  uint32_t weight_types[9] = {0};
+  bool has_bias = false;
+  size_t weight_bytes = 0;  // device bytes of all weight matrices
+  det_stats agg{};          // stats of finished sessions
+};
+
+struct det_session {
+  det_model* m = nullptr;
+  int n_ctx = 0, max_chunk = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // activations [max_chunk][*]
+  float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *tmp = nullptr;
+  float *gate = nullptr, *up = nullptr, *ff = nullptr, *logits = nullptr;
+  float* qa_d = nullptr;
+  int8_t* qa_q = nullptr;
+  float* qk_d = nullptr;
+  int8_t* qk_q = nullptr;
+  float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *score_scratch = nullptr;
+  float *cdf_e = nullptr, *cdf_z = nullptr;
+  uint32_t *d_tokens = nullptr, *d_rows = nullptr, *d_syms = nullptr, *d_err = nullptr;
+  uint64_t *d_out = nullptr, *d_value = nullptr;
+  // pinned staging
+  uint32_t *h_tokens = nullptr, *h_rows = nullptr, *h_syms = nullptr, *h_err = nullptr;
+  uint64_t *h_out = nullptr, *h_value = nullptr;
+  int last_n = 0;
+  std::vector<uint8_t> cdf_ready;
+  det_stats stats{};
+  std::vector<void*> allocations;
+  // profiling: event pairs around GEMV launches, resolved at the next sync
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<std::pair<double, double>> prof_pending;  // (bytes, weight bytes) per recorded pair
+};
+
+namespace det {
+extern bool g_profiling;
+}

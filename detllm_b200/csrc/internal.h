@@ -1,0 +1,80 @@
+// internal.h -- types shared by the host side (host.cpp) and the CUDA kernels
+// (kernels.cu) of libdetgpu.so.  Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace det {
+
+// ggml tensor types on this path (det-gguf lib.rs:58-96)
+enum : int { GT_F32 = 0, GT_F16 = 1, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q4_K = 12, GT_Q6_K = 14 };
+
+// Device error-flag bits (one uint32 per session, OR-ed by kernels)
+enum : uint32_t {
+  ERRF_NONFINITE = 1u,        // ModelError::NonFinite
+  ERRF_CDF_NONFINITE = 2u,    // CdfError::NonFiniteLogit
+  ERRF_CDF_TOTAL = 4u,        // CdfError::TotalTooLarge
+  ERRF_SHAPE = 8u,            // ModelError::Shape (bad token id etc.)
+  ERRF_DECODE = 16u,          // value outside the decoder distribution
+};
+
+// A weight matrix in device memory.  Layouts (rows x cols, nb blocks/row):
+//   F32  : f[rows][cols]
+//   Q8_0 : q int8 [rows][cols], d f16 bits [rows][nb]
+//   Q4_0 : q uint8 [rows][cols/2] (GGUF nibble order per 32-block), d [rows][nb]
+//   Q4_K : q uint8 [rows][nb][144] (GGUF super-blocks, 16-byte aligned)
+//   Q6_K : q uint8 [rows][nb][208] (ql | qh | scales), d [rows][nb]
+struct DevMatrix {
+  int type = GT_F32;
+  int rows = 0, cols = 0, nb = 0;
+  const void* q = nullptr;
+  const uint16_t* d = nullptr;
+  const float* f = nullptr;
+};
+
+// Quantised activations for `T` positions of length K (row stride K).
+struct DevActs {
+  const float* x = nullptr;    // f32 [T][K]
+  const float* qa_d = nullptr; // Q8A scales [T][K/32]
+  const int8_t* qa_q = nullptr;// Q8A quants [T][K]
+  const float* qk_d = nullptr; // Q8_K scales [T][K/256]
+  const int8_t* qk_q = nullptr;// Q8_K quants [T][K]
+};
+
+// epilogue modes of a GEMV/GEMM
+enum : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
+
+struct Launch {
+  cudaStream_t stream;
+  uint32_t* err;        // device error flag
+  uint64_t* launches;   // host counter of kernels launched
+};
+
+// ---- launchers (kernels.cu) ------------------------------------------------
+cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,
+                              float rope_base);
+cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* tokens, int T, float* x);
+cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h);
+cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
+cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
+cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                        int epi, const float* bias);
+cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, int pos0, int n_head,
+                              int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
+                              const float* sin_t, float* kc, float* vc, int n_ctx);
+cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, int pos0,
+                             int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
+                             float* score_scratch);
+cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T);
+cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, const uint32_t* rows, int nrows,
+                               float* e, float* z);
+cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
+                              const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3);
+cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n);
+cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
+                                  const uint64_t* value, uint64_t* out4);
+
+}  // namespace det

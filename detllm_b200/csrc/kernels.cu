@@ -1,0 +1,780 @@
+// kernels.cu -- sm_100a kernels of libdetgpu.so (layer ops, attention, CDF).
+//
+// Each kernel reproduces the reference's arithmetic in the reference's order;
+// the comment on each names the Rust function it follows.  All f32 math goes
+// through det::fadd/fmul/fdiv (explicitly rounded, never contracted).  Any
+// non-finite intermediate the reference would reject sets a bit in the
+// session's device error flag, which the host turns into DET_ERR_NONFINITE.
+#include <cuda_runtime.h>
+
+#include "dev_math.cuh"
+#include "internal.h"
+
+namespace det {
+
+namespace {
+
+DI void flag(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
+
+template <int NT>
+DI float block_max(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < NT / 32 ? red[l] : -INFINITY;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <int NT>
+DI unsigned long long block_sum_u64(unsigned long long v, unsigned long long* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < NT / 32 ? red[l] : 0ull;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// ---- dequantisation helpers (det-quant lib.rs:506-568) --------------------
+DI void q4k_scale_min(const uint8_t* s, int idx, int& sc, int& mn) {
+  if (idx < 4) {
+    sc = s[idx] & 0x3f;
+    mn = s[idx + 4] & 0x3f;
+  } else {
+    sc = (s[idx + 4] & 0x0f) | ((s[idx - 4] >> 6) << 4);
+    mn = (s[idx + 4] >> 4) | ((s[idx] >> 6) << 4);
+  }
+}
+
+// q4_k_value on a raw 144-byte super-block
+DI float q4k_value(const uint8_t* blk, int index) {
+  const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+  const float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+  const int sub = index >> 5, within = index & 31;
+  int sc, mn;
+  q4k_scale_min(blk + 4, sub, sc, mn);
+  const uint8_t byte = blk[16 + (sub >> 1) * 32 + within];
+  const int q = (sub & 1) ? (byte >> 4) : (byte & 0x0f);
+  return fsub(fmul(fmul(d, (float)sc), (float)q), fmul(dmin, (float)mn));
+}
+
+// q6_k_quant on a 208-byte body (ql[128] | qh[64] | scales[16])
+DI int q6k_quant(const uint8_t* body, int index) {
+  const int half = index >> 7, within = index & 127, l = within & 31, part = within >> 5;
+  const uint8_t* ql = body;
+  const uint8_t* qh = body + 128;
+  int v, shift;
+  switch (part) {
+    case 0: v = ql[half * 64 + l] & 0x0f; shift = 0; break;
+    case 1: v = ql[half * 64 + l + 32] & 0x0f; shift = 2; break;
+    case 2: v = ql[half * 64 + l] >> 4; shift = 4; break;
+    default: v = ql[half * 64 + l + 32] >> 4; shift = 6; break;
+  }
+  const int high = ((qh[half * 32 + l] >> shift) & 0x03) << 4;
+  return (v | high) - 32;
+}
+
+DI int q6k_scale_index(int index) {
+  const int half = index >> 7, within = index & 127, l = within & 31, part = within >> 5;
+  return half * 8 + (l >> 4) + 2 * part;
+}
+
+DI float q6k_value(const uint8_t* body, float d, int index) {
+  const int8_t sc = (int8_t)body[192 + q6k_scale_index(index)];
+  return fmul(fmul(d, (float)sc), (float)q6k_quant(body, index));
+}
+
+// ---- RoPE table: RopeTables::llama (det-model lib.rs:813-846) ------------
+__global__ void rope_table_kernel(float* cos_t, float* sin_t, int positions, int half, int rope_dim,
+                                  float rope_base) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)positions * half) return;
+  const int pos = (int)(i / half), j = (int)(i % half);
+  const double ln_base = log_det((double)rope_base);
+  const double exponent = ddiv(-(double)(2 * j), (double)rope_dim);
+  const double omega = exp_det(dmul(exponent, ln_base));
+  const double phi = dmul((double)pos, omega);
+  cos_t[i] = __double2float_rn(cos_det(phi));
+  sin_t[i] = __double2float_rn(sin_det(phi));
+}
+
+// ---- embedding row: write_row_validated (det-model lib.rs:667-746) --------
+__global__ void embed_kernel(DevMatrix m, const uint32_t* tokens, int T, float* x, uint32_t* err) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const uint32_t tok = tokens[t];
+  if (tok >= (uint32_t)m.rows) {
+    if (threadIdx.x == 0) flag(err, ERRF_SHAPE);
+    return;
+  }
+  const int K = m.cols;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v;
+    switch (m.type) {
+      case GT_F32: v = m.f[(size_t)tok * K + i]; break;
+      case GT_Q8_0: {
+        const int8_t q = ((const int8_t*)m.q)[(size_t)tok * K + i];
+        v = fmul(f16_bits_to_f32(m.d[(size_t)tok * m.nb + (i >> 5)]), (float)q);
+        break;
+      }
+      case GT_Q4_0: {
+        const uint8_t* qs = (const uint8_t*)m.q + (size_t)tok * (K / 2) + (i >> 5) * 16;
+        const int j = i & 31;
+        const int nib = j < 16 ? (qs[j] & 0x0f) : (qs[j - 16] >> 4);
+        v = fmul(f16_bits_to_f32(m.d[(size_t)tok * m.nb + (i >> 5)]), (float)(nib - 8));
+        break;
+      }
+      case GT_Q4_K:
+        v = q4k_value((const uint8_t*)m.q + ((size_t)tok * m.nb + (i >> 8)) * 144, i & 255);
+        break;
+      default: {  // GT_Q6_K
+        const size_t b = (size_t)tok * m.nb + (i >> 8);
+        v = q6k_value((const uint8_t*)m.q + b * 208, f16_bits_to_f32(m.d[b]), i & 255);
+        break;
+      }
+    }
+    if (!finite(v)) flag(err, ERRF_NONFINITE);
+    x[(size_t)t * K + i] = v;
+  }
+}
+
+// ---- rmsnorm (det-model lib.rs:2053-2073) ----------------------------------
+// sum_squares_f32_ref: lane l accumulates x[i]^2 for i = l (mod 8) in order.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
+                               float* __restrict__ h, uint32_t* err) {
+  const int t = blockIdx.x;
+  const float* xr = x + (size_t)t * n;
+  __shared__ float lanes[8];
+  __shared__ float r_s;
+  if (threadIdx.x < 8) {
+    float acc = 0.0f;
+    int i = threadIdx.x;
+    for (; i + 24 < n; i += 32) {
+      const float a0 = xr[i], a1 = xr[i + 8], a2 = xr[i + 16], a3 = xr[i + 24];
+      acc = fadd(acc, fmul(a0, a0));
+      acc = fadd(acc, fmul(a1, a1));
+      acc = fadd(acc, fmul(a2, a2));
+      acc = fadd(acc, fmul(a3, a3));
+    }
+    for (; i < n; i += 8) acc = fadd(acc, fmul(xr[i], xr[i]));
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float ss = finish8(lanes);
+    const float m = fdiv(ss, __int2float_rn(n));
+    const float r = fdiv(1.0f, __fsqrt_rn(fadd(m, eps)));
+    if (!finite(r)) flag(err, ERRF_NONFINITE);
+    r_s = r;
+  }
+  __syncthreads();
+  const float r = r_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float xi = xr[i];
+    const float v = fmul(fmul(xi, r), w[i]);
+    if (!finite(v) || !finite(xi)) flag(err, ERRF_NONFINITE);
+    h[(size_t)t * n + i] = v;
+  }
+}
+
+// ---- Q8A quantiser: try_quantize_q8a_block (det-quant lib.rs:111-137) ------
+// one warp per 32-element block; amax by shuffle (max is order-free)
+__global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, float* __restrict__ qd,
+                                 int8_t* __restrict__ qq, uint32_t* err) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= nblocks) return;
+  const int l = threadIdx.x & 31;
+  const float v = x[(size_t)b * 32 + l];
+  if (!finite(v)) flag(err, ERRF_NONFINITE);
+  float amax = fabsf(v);
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  int q = 0;
+  float d = 0.0f;
+  if (amax != 0.0f) {
+    d = fdiv(amax, 127.0f);
+    const float s = fdiv(v, d);
+    int r = v < 0.0f ? __float2int_rz(fsub(s, 0.5f)) : __float2int_rz(fadd(s, 0.5f));
+    q = max(-127, min(127, r));
+  }
+  qq[(size_t)b * 32 + l] = (int8_t)q;
+  if (l == 0) qd[b] = d;
+}
+
+// ---- Q8_K quantiser: try_quantize_q8k_block (det-quant lib.rs:139-172) ----
+// one warp per 256-element block; the signed max is x at the FIRST index with
+// the largest |x| (carried as (|x|, index) through the reduction).
+__global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, float* __restrict__ qd,
+                                 int8_t* __restrict__ qq, uint32_t* err) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= nblocks) return;
+  const int l = threadIdx.x & 31;
+  const float* xb = x + (size_t)b * 256;
+  float v[8];
+  float amax = 0.0f;
+  int idx = 0x7fffffff;
+  for (int k = 0; k < 8; k++) {
+    const int i = l * 8 + k;
+    v[k] = xb[i];
+    if (!finite(v[k])) flag(err, ERRF_NONFINITE);
+    const float ax = fabsf(v[k]);
+    if (ax > amax) {
+      amax = ax;
+      idx = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (oa > amax || (oa == amax && oi < idx)) {
+      amax = oa;
+      idx = oi;
+    }
+  }
+  if (amax == 0.0f) {
+    for (int k = 0; k < 8; k++) qq[(size_t)b * 256 + l * 8 + k] = 0;
+    if (l == 0) qd[b] = 0.0f;
+    return;
+  }
+  const float mx = xb[idx];
+  const float iscale = fdiv(-127.0f, mx);
+  for (int k = 0; k < 8; k++) {
+    const float val = fadd(fmul(iscale, v[k]), 12582912.0f);
+    int r = (int)(__float_as_uint(val) & 0x007fffffu) - 0x00400000;
+    qq[(size_t)b * 256 + l * 8 + k] = (int8_t)min(127, r);
+  }
+  if (l == 0) qd[b] = fdiv(1.0f, iscale);
+}
+
+// ---- generic GEMV: one thread per (row, position) running the reference's
+// own loop.  Exact for every type; used for F32, Q4_K and Q6_K and as the
+// fallback shape for the others. ------------------------------------------
+DI float dot_row(const DevMatrix& m, const DevActs& a, int r, int t) {
+  const int K = m.cols;
+  switch (m.type) {
+    case GT_F32: {  // dot_f32_ref (det-num reduce.rs:2-11)
+      const float* w = m.f + (size_t)r * K;
+      const float* x = a.x + (size_t)t * K;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int i = 0; i < K; i++) acc[i & 7] = fadd(acc[i & 7], fmul(w[i], x[i]));
+      return finish8(acc);
+    }
+    case GT_Q8_0: {  // dot_q8_0_q8a (det-quant lib.rs:237-257, 423-430)
+      const int* w = (const int*)((const int8_t*)m.q + (size_t)r * K);
+      const int* q = (const int*)(a.qa_q + (size_t)t * K);
+      const uint16_t* wd = m.d + (size_t)r * m.nb;
+      const float* ad = a.qa_d + (size_t)t * m.nb;
+      float sum = 0.0f;
+      for (int b = 0; b < m.nb; b++) {
+        int isum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) isum = __dp4a(w[b * 8 + k], q[b * 8 + k], isum);
+        const float scale = fmul(f16_bits_to_f32(wd[b]), ad[b]);
+        sum = fadd(sum, fmul(scale, __int2float_rn(isum)));
+      }
+      return sum;
+    }
+    case GT_Q4_0: {  // dot_q4_0_q8a (det-quant lib.rs:259-279, 455-466)
+      const uint8_t* w = (const uint8_t*)m.q + (size_t)r * (K / 2);
+      const int8_t* q = a.qa_q + (size_t)t * K;
+      const uint16_t* wd = m.d + (size_t)r * m.nb;
+      const float* ad = a.qa_d + (size_t)t * m.nb;
+      float sum = 0.0f;
+      for (int b = 0; b < m.nb; b++) {
+        int isum = 0;
+        for (int i = 0; i < 16; i++) {
+          const uint8_t p = w[b * 16 + i];
+          isum += ((int)(p & 0x0f) - 8) * (int)q[b * 32 + i];
+          isum += ((int)(p >> 4) - 8) * (int)q[b * 32 + i + 16];
+        }
+        const float scale = fmul(f16_bits_to_f32(wd[b]), ad[b]);
+        sum = fadd(sum, fmul(scale, __int2float_rn(isum)));
+      }
+      return sum;
+    }
+    case GT_Q4_K: {  // dot_q4_k_q8a (det-quant lib.rs:281-315): one f32 chain
+      const uint8_t* w = (const uint8_t*)m.q + (size_t)r * m.nb * 144;
+      const int8_t* q = a.qa_q + (size_t)t * K;
+      const float* ad = a.qa_d + (size_t)t * (K / 32);
+      float sum = 0.0f;
+      for (int b = 0; b < m.nb; b++) {
+        const uint8_t* blk = w + (size_t)b * 144;
+        const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+        const float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+        for (int sub = 0; sub < 8; sub++) {
+          int sc, mn;
+          q4k_scale_min(blk + 4, sub, sc, mn);
+          const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+          const float a_d = ad[b * 8 + sub];
+          const uint8_t* qs = blk + 16 + (sub >> 1) * 32;
+          const int8_t* aq = q + b * 256 + sub * 32;
+          for (int i = 0; i < 32; i++) {
+            const int qv = (sub & 1) ? (qs[i] >> 4) : (qs[i] & 0x0f);
+            const float weight = fsub(fmul(dsc, (float)qv), dmn);
+            const float act = fmul(a_d, (float)aq[i]);
+            sum = fadd(sum, fmul(weight, act));
+          }
+        }
+      }
+      return sum;
+    }
+    default: {  // GT_Q6_K: dot_q6_k_q8k (det-quant lib.rs:353-397)
+      const uint8_t* w = (const uint8_t*)m.q + (size_t)r * m.nb * 208;
+      const uint16_t* wd = m.d + (size_t)r * m.nb;
+      const int8_t* q = a.qk_q + (size_t)t * K;
+      const float* ad = a.qk_d + (size_t)t * m.nb;
+      float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int b = 0; b < m.nb; b++) {
+        const uint8_t* body = w + (size_t)b * 208;
+        int aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int s = 0; s < 16; s++) {
+          const int scale = (int8_t)body[192 + s];
+          for (int rep = 0; rep < 2; rep++) {
+            const int off = s * 16 + rep * 8;
+#pragma unroll
+            for (int ln = 0; ln < 8; ln++)
+              aux[ln] += scale * (int)q[b * 256 + off + ln] * q6k_quant(body, off + ln);
+          }
+        }
+        const float dd = fmul(f16_bits_to_f32(wd[b]), ad[b]);
+#pragma unroll
+        for (int ln = 0; ln < 8; ln++) sums[ln] = fadd(sums[ln], fmul(dd, __int2float_rn(aux[ln])));
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int ln = 0; ln < 8; ln++) sum = fadd(sum, sums[ln]);
+      return sum;
+    }
+  }
+}
+
+DI void epilogue_store(float v, int r, int t, float* out, int out_ld, int epi, const float* bias, uint32_t* err) {
+  if (!finite(v)) flag(err, ERRF_NONFINITE);
+  float* dst = out + (size_t)t * out_ld + r;
+  if (epi == EPI_BIAS) {
+    v = fadd(v, bias[r]);
+    if (!finite(v)) flag(err, ERRF_NONFINITE);
+    *dst = v;
+  } else if (epi == EPI_RESIDUAL) {
+    const float y = fadd(*dst, v);
+    if (!finite(y)) flag(err, ERRF_NONFINITE);
+    *dst = y;
+  } else {
+    *dst = v;
+  }
+}
+
+// grid: x = position-major tiles so consecutive CTAs share rows (L2 reuse)
+__global__ void gemv_generic_kernel(DevMatrix m, DevActs a, int T, float* out, int out_ld, int epi,
+                                    const float* bias, uint32_t* err) {
+  const int r = blockIdx.y * blockDim.x + threadIdx.x;
+  const int t = blockIdx.x;
+  if (r >= m.rows || t >= T) return;
+  epilogue_store(dot_row(m, a, r, t), r, t, out, out_ld, epi, bias, err);
+}
+
+// ---- RoPE + KV store: apply_rope (det-model lib.rs:2011-2051) and
+// KvCache::store (:883-913) ------------------------------------------------
+__global__ void rope_store_kernel(float* q, float* k, const float* v, int pos0, int n_head, int n_head_kv,
+                                  int hd, int half, int pairing, const float* cos_t, const float* sin_t, float* kc,
+                                  float* vc, int n_ctx, uint32_t* err) {
+  const int t = blockIdx.x;
+  const int pos = pos0 + t;
+  const float* cs = cos_t + (size_t)pos * half;
+  const float* sn = sin_t + (size_t)pos * half;
+  float* qt = q + (size_t)t * n_head * hd;
+  float* kt = k + (size_t)t * n_head_kv * hd;
+  const float* vt = v + (size_t)t * n_head_kv * hd;
+  const int nq = n_head * half, nk = n_head_kv * half;
+  for (int i = threadIdx.x; i < nq + nk; i += blockDim.x) {
+    float* base = i < nq ? qt : kt;
+    const int ii = i < nq ? i : i - nq;
+    const int head = ii / half, j = ii % half;
+    int a, b;
+    if (pairing == 0) {
+      a = head * hd + 2 * j;
+      b = a + 1;
+    } else {
+      a = head * hd + j;
+      b = a + half;
+    }
+    const float x0 = base[a], x1 = base[b];
+    const float c = cs[j], s = sn[j];
+    const float y0 = fsub(fmul(x0, c), fmul(x1, s));
+    const float y1 = fadd(fmul(x0, s), fmul(x1, c));
+    if (!finite(y0) || !finite(y1) || !finite(x0) || !finite(x1)) flag(err, ERRF_NONFINITE);
+    base[a] = y0;
+    base[b] = y1;
+  }
+  __syncthreads();
+  // KV store for every kv head (K after RoPE)
+  for (int i = threadIdx.x; i < n_head_kv * hd; i += blockDim.x) {
+    const int kh = i / hd, dd = i % hd;
+    const size_t off = ((size_t)kh * n_ctx + pos) * hd + dd;
+    const float kv = kt[i], vv = vt[i];
+    if (!finite(kv) || !finite(vv)) flag(err, ERRF_NONFINITE);
+    kc[off] = kv;
+    vc[off] = vv;
+  }
+}
+
+// ---- attention for one (position, head): attention_one_head
+// (det-model lib.rs:2300-2418) ---------------------------------------------
+constexpr int ATT_THREADS = 256;
+
+__global__ void attention_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                 const float* __restrict__ vc, int pos0, int n_head, int n_head_kv, int hd,
+                                 int n_ctx, float scale, float* __restrict__ out, float* __restrict__ scratch,
+                                 int smem_scores, uint32_t* err) {
+  extern __shared__ float sm[];
+  __shared__ float red[32];
+  __shared__ float lanes[8];
+  __shared__ float z_s;
+  const int t = blockIdx.x, head = blockIdx.y;
+  const int len = pos0 + t + 1;
+  const int kvh = head / (n_head / n_head_kv);
+  const float* kb = kc + (size_t)kvh * n_ctx * hd;
+  const float* vb = vc + (size_t)kvh * n_ctx * hd;
+  float* o = out + ((size_t)t * n_head + head) * hd;
+  if (len == 1) {  // score_len == 1 copies V (:2319-2322)
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) o[d] = vb[d];
+    return;
+  }
+  float* qs = sm;  // hd floats
+  float* sc = smem_scores ? sm + hd : scratch + ((size_t)t * n_head + head) * n_ctx;
+  const float* qh = q + ((size_t)t * n_head + head) * hd;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    qs[d] = qh[d];
+    if (!finite(qh[d])) flag(err, ERRF_NONFINITE);
+  }
+  __syncthreads();
+  // scores: dot_f32_ref(q, k_j) * scale (:2335-2359)
+  float lmax = -INFINITY;
+  for (int j = threadIdx.x; j < len; j += blockDim.x) {
+    const float* kj = kb + (size_t)j * hd;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (hd & 7) {  // head dims that are not a multiple of 8 (tiny fixtures)
+      for (int i = 0; i < hd; i++) acc[i & 7] = fadd(acc[i & 7], fmul(qs[i], kj[i]));
+    } else for (int i = 0; i < hd; i += 8) {
+      const float4 k0 = *reinterpret_cast<const float4*>(kj + i);
+      const float4 k1 = *reinterpret_cast<const float4*>(kj + i + 4);
+      acc[0] = fadd(acc[0], fmul(qs[i + 0], k0.x));
+      acc[1] = fadd(acc[1], fmul(qs[i + 1], k0.y));
+      acc[2] = fadd(acc[2], fmul(qs[i + 2], k0.z));
+      acc[3] = fadd(acc[3], fmul(qs[i + 3], k0.w));
+      acc[4] = fadd(acc[4], fmul(qs[i + 4], k1.x));
+      acc[5] = fadd(acc[5], fmul(qs[i + 5], k1.y));
+      acc[6] = fadd(acc[6], fmul(qs[i + 6], k1.z));
+      acc[7] = fadd(acc[7], fmul(qs[i + 7], k1.w));
+    }
+    const float s = fmul(finish8(acc), scale);
+    if (!finite(s)) flag(err, ERRF_NONFINITE);
+    sc[j] = s;
+    lmax = fmaxf(lmax, s);
+  }
+  const float mx = block_max<ATT_THREADS>(lmax, red);
+  // softmax_in_place (:2361-2388): e = expf(max(s - m, -88))
+  for (int j = threadIdx.x; j < len; j += blockDim.x) {
+    const float dlt = fsub(sc[j], mx);
+    sc[j] = expf_det(dlt > -88.0f ? dlt : -88.0f);
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {  // sum_f32_ref: 8 ordered lane chains
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < len; j += 8) acc = fadd(acc, sc[j]);
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float z = finish8(lanes);
+    if (!finite(z) || z == 0.0f) flag(err, ERRF_NONFINITE);
+    z_s = z;
+  }
+  __syncthreads();
+  const float z = z_s;
+  for (int j = threadIdx.x; j < len; j += blockDim.x) sc[j] = fdiv(sc[j], z);
+  __syncthreads();
+  // attention_weighted_value (:2390-2418): o[d] += p_j * v_j[d], j ascending
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < len; j++) acc = fadd(acc, fmul(sc[j], vb[(size_t)j * hd + d]));
+    if (!finite(acc)) flag(err, ERRF_NONFINITE);
+    o[d] = acc;
+  }
+}
+
+// ---- swiglu (det-model lib.rs:2420-2434) ---------------------------------
+__global__ void swiglu_kernel(const float* g, const float* u, float* out, long long n, uint32_t* err) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = g[i], uv = u[i];
+  const float y = fmul(silu_det(gv), uv);
+  if (!finite(y) || !finite(gv) || !finite(uv)) flag(err, ERRF_NONFINITE);
+  out[i] = y;
+}
+
+// ---- logits -> CDF (det-coder cdf.rs:138-245) ----------------------------
+constexpr int CDF_THREADS = 512;
+
+// per row: max, e_i = expf(max(l_i - m, -88)), Z = sum_f32_ref(e)
+__global__ void cdf_prepare_kernel(const float* __restrict__ logits, int V, const uint32_t* rows,
+                                   float* __restrict__ e, float* __restrict__ z, uint32_t* err) {
+  __shared__ float red[32];
+  __shared__ float lanes[8];
+  const uint32_t row = rows[blockIdx.x];
+  const float* l = logits + (size_t)row * V;
+  float* er = e + (size_t)row * V;
+  float lmax = -INFINITY;
+  bool bad = false;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = l[i];
+    if (!finite(v)) bad = true;
+    lmax = fmaxf(lmax, v);
+  }
+  if (bad) flag(err, ERRF_CDF_NONFINITE);
+  const float mx = block_max<CDF_THREADS>(lmax, red);
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float d = fsub(l[i], mx);
+    er[i] = expf_det(d > -88.0f ? d : -88.0f);
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    float acc = 0.0f;
+    int i = threadIdx.x;
+    for (; i + 56 < V; i += 64) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = er[i + 8 * k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = fadd(acc, v[k]);
+    }
+    for (; i < V; i += 8) acc = fadd(acc, er[i]);
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) z[row] = finish8(lanes);
+}
+
+DI uint32_t freq_of(float e, float z) {  // ((e / Z) * 2^24) as u32 + 1
+  return __float2uint_rz(fmul(fdiv(e, z), 16777216.0f)) + 1u;
+}
+
+// one CTA per query: (cum, freq, total) of symbols[i] under row rows[i]
+__global__ void cdf_ranges_kernel(const float* __restrict__ e, const float* __restrict__ z, int V, int tail,
+                                  const uint32_t* rows, const uint32_t* symbols, uint64_t* out3, uint32_t* err) {
+  __shared__ unsigned long long red[32];
+  const uint32_t row = rows[blockIdx.x];
+  const uint32_t sym = symbols[blockIdx.x];
+  const float* er = e + (size_t)row * V;
+  const float zz = z[row];
+  unsigned long long tot = 0, cum = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const uint32_t f = freq_of(er[i], zz);
+    tot += f;
+    if ((uint32_t)i < sym) cum += f;
+  }
+  tot = block_sum_u64<CDF_THREADS>(tot, red);
+  cum = block_sum_u64<CDF_THREADS>(cum, red);
+  if (threadIdx.x == 0) {
+    uint64_t freq;
+    if (sym < (uint32_t)V) {
+      freq = freq_of(er[sym], zz);
+    } else {
+      cum = tot + (sym - (uint32_t)V);
+      freq = 1;
+    }
+    const uint64_t total = tot + (uint64_t)tail;
+    if (total >= (1ull << 31)) flag(err, ERRF_CDF_TOTAL);
+    out3[3 * blockIdx.x + 0] = cum;
+    out3[3 * blockIdx.x + 1] = freq;
+    out3[3 * blockIdx.x + 2] = total;
+  }
+}
+
+// decoder: symbol with cum <= value < cum + freq (DecoderDistribution::
+// symbol_range, cdf.rs:392-425), by block-wide exclusive scans of the
+// (exact integer) frequencies.  out4 = {symbol, cum, freq, total}
+__global__ void decoder_lookup_kernel(const float* __restrict__ e, const float* __restrict__ z, int V, int tail,
+                                      uint32_t row, const uint64_t* value_p, uint64_t* out4, uint32_t* err) {
+  __shared__ unsigned long long wsum[32];
+  __shared__ unsigned long long base_s;
+  __shared__ int found;
+  const float* er = e + (size_t)row * V;
+  const float zz = z[row];
+  const unsigned long long value = *value_p;
+  if (threadIdx.x == 0) {
+    base_s = 0;
+    found = 0;
+  }
+  __syncthreads();
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  for (int start = 0; start < V; start += blockDim.x) {
+    const int i = start + threadIdx.x;
+    const unsigned long long f = i < V ? freq_of(er[i], zz) : 0ull;
+    unsigned long long inc = f;
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long n = __shfl_up_sync(0xffffffffu, inc, o);
+      if (l >= o) inc += n;
+    }
+    if (l == 31) wsum[w] = inc;
+    __syncthreads();
+    if (w == 0) {
+      unsigned long long s = l < (int)(blockDim.x >> 5) ? wsum[l] : 0ull;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, s, o);
+        if (l >= o) s += n;
+      }
+      wsum[l] = s;  // inclusive warp prefix
+    }
+    __syncthreads();
+    const unsigned long long base = base_s;
+    const unsigned long long excl = base + (w ? wsum[w - 1] : 0ull) + inc - f;
+    if (i < V && excl <= value && value < excl + f) {
+      out4[0] = (uint64_t)i;
+      out4[1] = excl;
+      out4[2] = f;
+      found = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) base_s = base + wsum[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const unsigned long long tot = base_s;
+    const unsigned long long total = tot + (unsigned long long)tail;
+    out4[3] = total;
+    if (!found) {
+      const unsigned long long off = value - tot;
+      if (value >= tot && off < (unsigned long long)tail) {
+        out4[0] = (uint64_t)V + off;
+        out4[1] = value;
+        out4[2] = 1;
+      } else {
+        flag(err, ERRF_DECODE);
+      }
+    }
+  }
+}
+
+__global__ void expf_kernel(const float* x, float* y, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = expf_det(x[i]);
+}
+
+}  // namespace
+
+cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n) {
+  expf_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+// ---- launchers ---------------------------------------------------------------
+static inline cudaError_t post(const Launch& L) {
+  if (L.launches) ++*L.launches;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,
+                              float rope_base) {
+  const long long n = (long long)positions * half;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, L.stream>>>(cos_t, sin_t, positions, half, rope_dim,
+                                                                       rope_base);
+  return post(L);
+}
+
+cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* tokens, int T, float* x) {
+  embed_kernel<<<T, 256, 0, L.stream>>>(m, tokens, T, x, L.err);
+  return post(L);
+}
+
+cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h) {
+  rmsnorm_kernel<<<T, 256, 0, L.stream>>>(x, w, n, eps, h, L.err);
+  return post(L);
+}
+
+cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
+  const int nb = T * (K / 32);
+  quant_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, qd, qq, L.err);
+  return post(L);
+}
+
+cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
+  const int nb = T * (K / 256);
+  quant_q8k_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, qd, qq, L.err);
+  return post(L);
+}
+
+cudaError_t launch_gemv_fast(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                             int epi, const float* bias, bool* handled);
+
+cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                        int epi, const float* bias) {
+  bool handled = false;
+  cudaError_t e = launch_gemv_fast(L, m, a, T, out, out_ld, epi, bias, &handled);
+  if (handled || e != cudaSuccess) return e;
+  dim3 grid(T, (m.rows + 127) / 128);
+  gemv_generic_kernel<<<grid, 128, 0, L.stream>>>(m, a, T, out, out_ld, epi, bias, L.err);
+  return post(L);
+}
+
+cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, int pos0, int n_head,
+                              int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
+                              const float* sin_t, float* kc, float* vc, int n_ctx) {
+  rope_store_kernel<<<T, 256, 0, L.stream>>>(q, k, v, pos0, n_head, n_head_kv, head_dim, rope_dim / 2, pairing,
+                                             cos_t, sin_t, kc, vc, n_ctx, L.err);
+  return post(L);
+}
+
+cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, int pos0,
+                             int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
+                             float* score_scratch) {
+  const size_t need = (size_t)(head_dim + n_ctx) * sizeof(float);
+  const int smem_scores = need <= 160 * 1024 ? 1 : 0;
+  const size_t smem = smem_scores ? need : head_dim * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(T, n_head);
+  attention_kernel<<<grid, ATT_THREADS, smem, L.stream>>>(q, kc, vc, pos0, n_head, n_head_kv, head_dim, n_ctx,
+                                                          scale, out, score_scratch, smem_scores, L.err);
+  return post(L);
+}
+
+cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T) {
+  const long long tot = (long long)n * T;
+  swiglu_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, L.stream>>>(g, u, out, tot, L.err);
+  return post(L);
+}
+
+cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, const uint32_t* rows, int nrows,
+                               float* e, float* z) {
+  cdf_prepare_kernel<<<nrows, CDF_THREADS, 0, L.stream>>>(logits, V, rows, e, z, L.err);
+  return post(L);
+}
+
+cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
+                              const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3) {
+  cdf_ranges_kernel<<<n, CDF_THREADS, 0, L.stream>>>(e, z, V, tail, rows, symbols, out3, L.err);
+  return post(L);
+}
+
+cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
+                                  const uint64_t* value, uint64_t* out4) {
+  decoder_lookup_kernel<<<1, 1024, 0, L.stream>>>(e, z, V, tail, row, value, out4, L.err);
+  return post(L);
+}
+
+}  // namespace det

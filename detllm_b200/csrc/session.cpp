@@ -1,0 +1,499 @@
+// session.cpp -- det_session: device workspace, KV cache and RoPE table of one
+// context window, the chunked teacher-forced forward, and the logits -> CDF
+// entry points.
+//
+// The layer sequence follows forward_one_with_workspace
+// (crates/det-model/src/lib.rs:1249-1400); a chunk of n tokens runs every op
+// for all n positions before the next op, which leaves each position's
+// arithmetic unchanged (each reduction stays within one position).
+#include <algorithm>
+#include <cstdlib>
+
+#include "host_common.h"
+
+using namespace det;
+
+bool det::g_profiling = false;
+
+namespace {
+
+det_status cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return DET_OK;
+  if (e == cudaErrorMemoryAllocation) return DET_ERR_DEVICE_OOM;
+  return DET_ERR_CUDA;
+}
+
+template <typename T>
+det_status dalloc(det_session* s, T** p, size_t count) {
+  void* q = nullptr;
+  const cudaError_t e = cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 256));
+  if (e != cudaSuccess) return cuda_status(e);
+  s->allocations.push_back(q);
+  *p = static_cast<T*>(q);
+  return DET_OK;
+}
+
+template <typename T>
+det_status halloc(det_session* s, T** p, size_t count) {
+  void* q = nullptr;
+  if (cudaMallocHost(&q, std::max<size_t>(count * sizeof(T), 64)) != cudaSuccess) return DET_ERR_ALLOC;
+  *p = static_cast<T*>(q);
+  return DET_OK;
+}
+
+bool needs_q8a(int type) { return type == GT_Q8_0 || type == GT_Q4_0 || type == GT_Q4_K; }
+
+void add_stats(det_stats* a, const det_stats& b) {
+  a->forward_ms += b.forward_ms;
+  a->cdf_ms += b.cdf_ms;
+  a->launches += b.launches;
+  a->h2d_bytes += b.h2d_bytes;
+  a->d2h_bytes += b.d2h_bytes;
+  a->tokens += b.tokens;
+  a->gemm_ms += b.gemm_ms;
+  a->gemm_launches += b.gemm_launches;
+  a->gemm_bytes += b.gemm_bytes;
+  a->gemm_weight_bytes += b.gemm_weight_bytes;
+}
+
+void free_session(det_session* s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  add_stats(&s->m->agg, s->stats);
+  for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
+  for (void* p : s->allocations) cudaFree(p);
+  for (void* p : {(void*)s->h_tokens, (void*)s->h_rows, (void*)s->h_syms, (void*)s->h_err, (void*)s->h_out,
+                  (void*)s->h_value})
+    if (p) cudaFreeHost(p);
+  for (auto& e : s->ev)
+    if (e) cudaEventDestroy(e);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+Launch launch_of(det_session* s) { return Launch{s->stream, s->d_err, &s->stats.launches}; }
+
+// Reads and clears the device error flag (synchronises the stream), and
+// resolves pending profile events.
+det_status take_error(det_session* s, bool cdf) {
+  cudaError_t e = cudaMemcpyAsync(s->h_err, s->d_err, 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  for (size_t i = 0; i < s->prof_pending.size(); i++) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, s->prof_events[2 * i], s->prof_events[2 * i + 1]) == cudaSuccess) {
+      s->stats.gemm_ms += ms;
+      s->stats.gemm_launches++;
+      s->stats.gemm_bytes += s->prof_pending[i].first;
+      s->stats.gemm_weight_bytes += s->prof_pending[i].second;
+    }
+  }
+  s->prof_pending.clear();
+  const uint32_t f = *s->h_err;
+  if (f) cudaMemsetAsync(s->d_err, 0, 4, s->stream);
+  if (f & ERRF_SHAPE) return DET_ERR_SHAPE;
+  if (f & ERRF_NONFINITE) return DET_ERR_NONFINITE;
+  if (cdf && (f & ERRF_CDF_NONFINITE)) return DET_ERR_CDF_NONFINITE_LOGIT;
+  if (cdf && (f & ERRF_CDF_TOTAL)) return DET_ERR_CDF_TOTAL_TOO_LARGE;
+  if (f & ERRF_DECODE) return DET_ERR_DECODE;
+  if (f) return DET_ERR_CUDA;
+  return DET_OK;
+}
+
+// quantise `x` (T x K) for a matrix of type `type` into the session buffers
+cudaError_t quantise_for(det_session* s, int type, const float* x, int K, int T, DevActs* a, int* have) {
+  a->x = x;
+  const Launch L = launch_of(s);
+  if (needs_q8a(type) && !(*have & 1)) {
+    cudaError_t e = launch_quant_q8a(L, x, K, T, s->qa_d, s->qa_q);
+    if (e != cudaSuccess) return e;
+    *have |= 1;
+  }
+  if (type == GT_Q6_K && !(*have & 2)) {
+    cudaError_t e = launch_quant_q8k(L, x, K, T, s->qk_d, s->qk_q);
+    if (e != cudaSuccess) return e;
+    *have |= 2;
+  }
+  a->qa_d = s->qa_d;
+  a->qa_q = s->qa_q;
+  a->qk_d = s->qk_d;
+  a->qk_q = s->qk_q;
+  return cudaSuccess;
+}
+
+#define CK(expr)                                   \
+  do {                                             \
+    const cudaError_t e_ = (expr);                 \
+    if (e_ != cudaSuccess) return cuda_status(e_); \
+  } while (0)
+
+double bytes_per_weight(int type) {
+  switch (type) {
+    case GT_Q8_0: return 34.0 / 32.0;
+    case GT_Q4_0: return 18.0 / 32.0;
+    case GT_Q4_K: return 144.0 / 256.0;
+    case GT_Q6_K: return 210.0 / 256.0;
+    default: return 4.0;
+  }
+}
+
+// launch_gemv with optional per-launch event timing (det_set_profiling)
+cudaError_t gemv(det_session* s, const DevMatrix& W, const DevActs& a, int T, float* out, int ld, int epi,
+                 const float* bias) {
+  const Launch L = launch_of(s);
+  if (!g_profiling) return launch_gemv(L, W, a, T, out, ld, epi, bias);
+  const size_t i = s->prof_pending.size();
+  while (s->prof_events.size() < 2 * (i + 1)) {
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreate(&ev);
+    if (e != cudaSuccess) return e;
+    s->prof_events.push_back(ev);
+  }
+  cudaError_t e = cudaEventRecord(s->prof_events[2 * i], s->stream);
+  if (e == cudaSuccess) e = launch_gemv(L, W, a, T, out, ld, epi, bias);
+  if (e == cudaSuccess) e = cudaEventRecord(s->prof_events[2 * i + 1], s->stream);
+  const double wbytes = (double)W.rows * W.cols * bytes_per_weight(W.type);
+  const double abytes = (double)T * W.cols *
+                        (W.type == GT_Q6_K ? 1.0 + 4.0 / 256.0 : (W.type == GT_F32 ? 4.0 : 1.0 + 4.0 / 32.0));
+  const double obytes = (double)T * W.rows * (epi == EPI_RESIDUAL ? 8.0 : 4.0);
+  s->prof_pending.emplace_back(wbytes + abytes + obytes, wbytes);
+  return e;
+}
+
+// forward_one_with_workspace for positions pos0 .. pos0+T-1 (tokens already
+// on the device in s->d_tokens)
+det_status forward_chunk(det_session* s, int T, int pos0) {
+  det_model* m = s->m;
+  const ModelCfg& c = m->cfg;
+  const Launch L = launch_of(s);
+  const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
+  const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
+  CK(launch_embed(L, m->tok_embd, s->d_tokens, T, s->x));
+  for (int l = 0; l < c.L; l++) {
+    const LayerDev& W = m->layers[(size_t)l];
+    CK(launch_rmsnorm(L, s->x, W.attn_norm, c.d, c.eps, T, s->h));
+    DevActs a;
+    int have = 0;
+    // one Q8A of h shared by q/k/v (:1284-1292); Q8_K recomputed per Q6_K
+    // matrix in the reference gives the same blocks, so it is made once too
+    CK(quantise_for(s, W.wq.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, W.wk.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, W.wv.type, s->h, c.d, T, &a, &have));
+    CK(gemv(s,W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
+    CK(gemv(s,W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
+    CK(gemv(s,W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+    float* kc = s->kc + (size_t)l * kv_layer;
+    float* vc = s->vc + (size_t)l * kv_layer;
+    CK(launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
+                         s->rope_sin, kc, vc, s->n_ctx));
+    CK(launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
+                        s->score_scratch));
+    have = 0;
+    CK(quantise_for(s, W.wo.type, s->attn, qd, T, &a, &have));
+    CK(gemv(s,W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+    CK(launch_rmsnorm(L, s->x, W.ffn_norm, c.d, c.eps, T, s->h));
+    have = 0;
+    CK(quantise_for(s, W.gate.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, W.up.type, s->h, c.d, T, &a, &have));
+    CK(gemv(s,W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
+    CK(gemv(s,W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+    CK(launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T));
+    have = 0;
+    CK(quantise_for(s, W.down.type, s->ff, c.dff, T, &a, &have));
+    CK(gemv(s,W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+  }
+  CK(launch_rmsnorm(L, s->x, m->output_norm, c.d, c.eps, T, s->h));
+  DevActs a;
+  int have = 0;
+  CK(quantise_for(s, m->output.type, s->h, c.d, T, &a, &have));
+  CK(gemv(s,m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
+  return DET_OK;
+}
+
+// e/z for the listed rows of the last forward (once per row per forward)
+det_status prepare_rows(det_session* s, const uint32_t* rows, uint32_t n) {
+  std::vector<uint32_t> need;
+  for (uint32_t i = 0; i < n; i++)
+    if (!s->cdf_ready[rows[i]]) {
+      s->cdf_ready[rows[i]] = 1;
+      need.push_back(rows[i]);
+    }
+  if (need.empty()) return DET_OK;
+  // staging slots [1024, 2048) of h_rows; the query rows use [0, 1024)
+  std::memcpy(s->h_rows + 1024, need.data(), need.size() * 4);
+  CK(cudaMemcpyAsync(s->d_rows, s->h_rows + 1024, need.size() * 4, cudaMemcpyHostToDevice, s->stream));
+  s->stats.h2d_bytes += need.size() * 4;
+  CK(launch_cdf_prepare(launch_of(s), s->logits, s->m->vocab, s->d_rows, (int)need.size(), s->cdf_e, s->cdf_z));
+  return DET_OK;
+}
+
+det_status check_symbols(det_session* s, int tail) {
+  const uint64_t V = (uint64_t)s->m->vocab;
+  if (V + (uint64_t)tail > (1u << 18)) return DET_ERR_CDF_TOO_MANY_SYMBOLS;
+  return DET_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out) {
+  if (!m || !out) return DET_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  const ModelCfg& c = m->cfg;
+  // RoPE phases pos * omega stay below 2^20 * pi/2 (the range of the
+  // restated rem_pio2) for windows up to 2^20 positions.
+  if (n_ctx == 0 || (int)n_ctx > c.ctx || n_ctx > (1u << 20) || max_chunk == 0 || max_chunk > 1024)
+    return DET_ERR_SHAPE;
+  if (cudaSetDevice(m->device) != cudaSuccess) return DET_ERR_CUDA;
+  det_session* s = new (std::nothrow) det_session();
+  if (!s) return DET_ERR_ALLOC;
+  s->m = m;
+  s->n_ctx = (int)n_ctx;
+  s->max_chunk = (int)std::min<uint32_t>(max_chunk, n_ctx);
+  const size_t T = (size_t)s->max_chunk;
+  const size_t qd = (size_t)c.nh * c.hd, kvd = (size_t)c.nkv * c.hd;
+  const size_t kmax = std::max({(size_t)c.d, (size_t)c.dff, qd});
+  const size_t kv = (size_t)c.L * c.nkv * n_ctx * c.hd;
+  det_status st = DET_OK;
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) st = DET_ERR_CUDA;
+  for (auto& e : s->ev)
+    if (!st && cudaEventCreate(&e) != cudaSuccess) st = DET_ERR_CUDA;
+  if (!st) st = dalloc(s, &s->x, T * c.d);
+  if (!st) st = dalloc(s, &s->h, T * c.d);
+  if (!st) st = dalloc(s, &s->tmp, T * c.d);
+  if (!st) st = dalloc(s, &s->q, T * qd);
+  if (!st) st = dalloc(s, &s->attn, T * qd);
+  if (!st) st = dalloc(s, &s->k, T * kvd);
+  if (!st) st = dalloc(s, &s->v, T * kvd);
+  if (!st) st = dalloc(s, &s->gate, T * c.dff);
+  if (!st) st = dalloc(s, &s->up, T * c.dff);
+  if (!st) st = dalloc(s, &s->ff, T * c.dff);
+  if (!st) st = dalloc(s, &s->logits, T * (size_t)m->vocab);
+  if (!st) st = dalloc(s, &s->qa_d, T * (kmax / 32 + 1));
+  if (!st) st = dalloc(s, &s->qa_q, T * kmax + 64);
+  if (!st) st = dalloc(s, &s->qk_d, T * (kmax / 256 + 1));
+  if (!st) st = dalloc(s, &s->qk_q, T * kmax + 64);
+  if (!st) st = dalloc(s, &s->kc, kv);
+  if (!st) st = dalloc(s, &s->vc, kv);
+  if (!st) st = dalloc(s, &s->rope_cos, (size_t)n_ctx * (c.rope_dim / 2));
+  if (!st) st = dalloc(s, &s->rope_sin, (size_t)n_ctx * (c.rope_dim / 2));
+  if (!st && (size_t)(c.hd + n_ctx) * 4 > 160 * 1024) st = dalloc(s, &s->score_scratch, T * c.nh * (size_t)n_ctx);
+  if (!st) st = dalloc(s, &s->cdf_e, T * (size_t)m->vocab);
+  if (!st) st = dalloc(s, &s->cdf_z, T);
+  if (!st) st = dalloc(s, &s->d_tokens, T);
+  if (!st) st = dalloc(s, &s->d_rows, 2048);
+  if (!st) st = dalloc(s, &s->d_syms, std::max<size_t>(T, 1024) * 4);
+  if (!st) st = dalloc(s, &s->d_out, std::max<size_t>(T, 1024) * 4 * 3);
+  if (!st) st = dalloc(s, &s->d_value, 8);
+  if (!st) st = dalloc(s, &s->d_err, 4);
+  if (!st) st = halloc(s, &s->h_tokens, T);
+  if (!st) st = halloc(s, &s->h_rows, 2048);
+  if (!st) st = halloc(s, &s->h_syms, std::max<size_t>(T, 1024) * 4);
+  if (!st) st = halloc(s, &s->h_out, std::max<size_t>(T, 1024) * 4 * 3);
+  if (!st) st = halloc(s, &s->h_value, 8);
+  if (!st) st = halloc(s, &s->h_err, 4);
+  if (!st && cudaMemsetAsync(s->d_err, 0, 4, s->stream) != cudaSuccess) st = DET_ERR_CUDA;
+  if (!st) st = cuda_status(cudaMemsetAsync(s->kc, 0, kv * 4, s->stream));
+  if (!st) st = cuda_status(cudaMemsetAsync(s->vc, 0, kv * 4, s->stream));
+  if (!st)
+    st = cuda_status(launch_rope_table(launch_of(s), s->rope_cos, s->rope_sin, (int)n_ctx, c.rope_dim / 2,
+                                       c.rope_dim, c.rope_base));
+  if (!st) st = take_error(s, false);
+  if (st) {
+    free_session(s);
+    return st;
+  }
+  s->cdf_ready.assign(T, 0);
+  *out = s;
+  return DET_OK;
+}
+
+void det_session_free(det_session* s) { free_session(s); }
+
+det_status det_session_reset(det_session* s) {
+  if (!s) return DET_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(s->m->device);
+  const ModelCfg& c = s->m->cfg;
+  const size_t kv = (size_t)c.L * c.nkv * s->n_ctx * c.hd;
+  // KvCache::new is all zeros; a replayed window only reads positions it
+  // has written, so clearing is for exact state parity, not correctness.
+  CK(cudaMemsetAsync(s->kc, 0, kv * 4, s->stream));
+  CK(cudaMemsetAsync(s->vc, 0, kv * 4, s->stream));
+  s->last_n = 0;
+  return DET_OK;
+}
+
+det_status det_forward(det_session* s, const uint32_t* tokens, uint32_t n, uint32_t pos0, float* logits_out) {
+  if (!s || !tokens) return DET_ERR_INVALID_ARGUMENT;
+  if (n == 0 || (int)n > s->max_chunk || (uint64_t)pos0 + n > (uint64_t)s->n_ctx) return DET_ERR_SHAPE;
+  det_model* m = s->m;
+  for (uint32_t i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)m->vocab || tokens[i] >= (uint32_t)m->tok_embd.rows) return DET_ERR_SHAPE;
+  cudaSetDevice(m->device);
+  std::memcpy(s->h_tokens, tokens, n * 4);
+  CK(cudaMemcpyAsync(s->d_tokens, s->h_tokens, n * 4, cudaMemcpyHostToDevice, s->stream));
+  s->stats.h2d_bytes += n * 4;
+  CK(cudaEventRecord(s->ev[0], s->stream));
+  det_status st = forward_chunk(s, (int)n, (int)pos0);
+  if (st) return st;
+  CK(cudaEventRecord(s->ev[1], s->stream));
+  s->last_n = (int)n;
+  s->stats.tokens += n;
+  std::fill(s->cdf_ready.begin(), s->cdf_ready.end(), 0);
+  if (logits_out) {
+    const size_t bytes = (size_t)n * m->vocab * 4;
+    CK(cudaMemcpyAsync(logits_out, s->logits, bytes, cudaMemcpyDeviceToHost, s->stream));
+    s->stats.d2h_bytes += bytes;
+  }
+  st = take_error(s, false);
+  float ms = 0.0f;
+  if (cudaEventElapsedTime(&ms, s->ev[0], s->ev[1]) == cudaSuccess) s->stats.forward_ms += ms;
+  if (st) s->last_n = 0;
+  return st;
+}
+
+det_status det_symbol_ranges(det_session* s, const uint32_t* rows, const uint32_t* symbols, uint32_t n,
+                             int byte_escapes, det_symbol_range* out) {
+  if (!s || (!symbols && n) || (!out && n)) return DET_ERR_INVALID_ARGUMENT;
+  if (n == 0) return DET_OK;
+  const int tail = byte_escapes ? 256 : 0;
+  if (det_status st = check_symbols(s, tail)) return st;
+  const uint32_t V = (uint32_t)s->m->vocab;
+  cudaSetDevice(s->m->device);
+  const uint32_t cap = 1024;
+  for (uint32_t base = 0; base < n; base += cap) {
+    const uint32_t cnt = std::min(cap, n - base);
+    for (uint32_t i = 0; i < cnt; i++) {
+      const uint32_t r = rows ? rows[base + i] : base + i;
+      if (r >= (uint32_t)s->last_n) return DET_ERR_SHAPE;
+      if (symbols[base + i] >= V + (uint32_t)tail) return DET_ERR_CDF_SYMBOL_OUT_OF_RANGE;
+      s->h_rows[i] = r;
+      s->h_syms[i] = symbols[base + i];
+    }
+    CK(cudaEventRecord(s->ev[2], s->stream));
+    if (det_status st = prepare_rows(s, s->h_rows, cnt)) return st;
+    CK(cudaMemcpyAsync(s->d_rows + 1024, s->h_rows, cnt * 4, cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->d_syms, s->h_syms, cnt * 4, cudaMemcpyHostToDevice, s->stream));
+    s->stats.h2d_bytes += cnt * 8;
+    CK(launch_cdf_ranges(launch_of(s), s->cdf_e, s->cdf_z, (int)V, tail, s->d_rows + 1024, s->d_syms, (int)cnt,
+                         s->d_out));
+    CK(cudaEventRecord(s->ev[3], s->stream));
+    CK(cudaMemcpyAsync(s->h_out, s->d_out, cnt * 24, cudaMemcpyDeviceToHost, s->stream));
+    s->stats.d2h_bytes += cnt * 24;
+    if (det_status st = take_error(s, true)) return st;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, s->ev[2], s->ev[3]) == cudaSuccess) s->stats.cdf_ms += ms;
+    for (uint32_t i = 0; i < cnt; i++) {
+      out[base + i].cum = s->h_out[3 * i];
+      out[base + i].freq = (uint32_t)s->h_out[3 * i + 1];
+      out[base + i].reserved = 0;
+      out[base + i].total = s->h_out[3 * i + 2];
+    }
+  }
+  return DET_OK;
+}
+
+det_status det_decoder_total(det_session* s, uint32_t row, int byte_escapes, uint64_t* total) {
+  if (!s || !total) return DET_ERR_INVALID_ARGUMENT;
+  const uint32_t sym = 0;
+  det_symbol_range r;
+  det_status st = det_symbol_ranges(s, &row, &sym, 1, byte_escapes, &r);
+  if (st) return st;
+  *total = r.total;
+  return DET_OK;
+}
+
+det_status det_decoder_lookup(det_session* s, uint32_t row, int byte_escapes, uint64_t value, uint32_t* symbol,
+                              det_symbol_range* out) {
+  if (!s || !symbol || !out) return DET_ERR_INVALID_ARGUMENT;
+  const int tail = byte_escapes ? 256 : 0;
+  if (det_status st = check_symbols(s, tail)) return st;
+  if (row >= (uint32_t)s->last_n) return DET_ERR_SHAPE;
+  cudaSetDevice(s->m->device);
+  if (det_status st = prepare_rows(s, &row, 1)) return st;
+  *s->h_value = value;
+  CK(cudaMemcpyAsync(s->d_value, s->h_value, 8, cudaMemcpyHostToDevice, s->stream));
+  CK(launch_decoder_lookup(launch_of(s), s->cdf_e, s->cdf_z, s->m->vocab, tail, row, s->d_value, s->d_out));
+  CK(cudaMemcpyAsync(s->h_out, s->d_out, 32, cudaMemcpyDeviceToHost, s->stream));
+  s->stats.h2d_bytes += 8;
+  s->stats.d2h_bytes += 32;
+  if (det_status st = take_error(s, true)) return st;
+  if (value >= s->h_out[3]) return DET_ERR_DECODE;
+  *symbol = (uint32_t)s->h_out[0];
+  out->cum = s->h_out[1];
+  out->freq = (uint32_t)s->h_out[2];
+  out->reserved = 0;
+  out->total = s->h_out[3];
+  return DET_OK;
+}
+
+det_status det_logits_hash(det_model* m, const uint32_t* tokens, size_t n, uint32_t chunk, uint8_t out[32]) {
+  if (!m || !tokens || !out) return DET_ERR_INVALID_ARGUMENT;
+  // validate_logits_request (det-model lib.rs:1467-1483)
+  if (n == 0 || chunk == 0 || n > (size_t)m->cfg.ctx) return DET_ERR_SHAPE;
+  for (size_t i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)m->tok_embd.rows) return DET_ERR_SHAPE;
+  det_session* s;
+  const uint32_t T = std::min<uint32_t>(chunk, 256);
+  if (det_status st = det_session_create(m, (uint32_t)n, T, &s)) return st;
+  std::vector<float> buf((size_t)T * m->vocab);
+  Sha256 h;
+  det_status st = DET_OK;
+  for (size_t p = 0; p < n && !st; p += T) {
+    const uint32_t cnt = (uint32_t)std::min<size_t>(T, n - p);
+    st = det_forward(s, tokens + p, cnt, (uint32_t)p, buf.data());
+    if (!st) h.update(buf.data(), (size_t)cnt * m->vocab * 4);  // little-endian f32 bits
+  }
+  det_session_free(s);
+  if (!st) h.finish(out);
+  return st;
+}
+
+det_status det_device_expf(int device, const float* x, float* y, size_t n) {
+  if ((!x || !y) && n) return DET_ERR_INVALID_ARGUMENT;
+  int cnt = 0;
+  if (cudaGetDeviceCount(&cnt) != cudaSuccess || cnt == 0) return DET_ERR_NO_DEVICE;
+  if (device < 0 || device >= cnt) return DET_ERR_INVALID_ARGUMENT;
+  if (n == 0) return DET_OK;
+  CK(cudaSetDevice(device));
+  float *dx = nullptr, *dy = nullptr;
+  const size_t chunk = std::min<size_t>(n, (size_t)1 << 26);
+  CK(cudaMalloc(&dx, chunk * 4));
+  if (cudaMalloc(&dy, chunk * 4) != cudaSuccess) {
+    cudaFree(dx);
+    return DET_ERR_DEVICE_OOM;
+  }
+  cudaError_t e = cudaSuccess;
+  for (size_t b = 0; b < n && e == cudaSuccess; b += chunk) {
+    const size_t c = std::min(chunk, n - b);
+    e = cudaMemcpy(dx, x + b, c * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_expf(nullptr, dx, dy, (long long)c);
+    if (e == cudaSuccess) e = cudaMemcpy(y + b, dy, c * 4, cudaMemcpyDeviceToHost);
+  }
+  cudaFree(dx);
+  cudaFree(dy);
+  return cuda_status(e);
+}
+
+det_status det_session_stats(det_session* s, det_stats* out, int reset) {
+  if (!s || !out) return DET_ERR_INVALID_ARGUMENT;
+  *out = s->stats;
+  if (reset) s->stats = det_stats{};
+  return DET_OK;
+}
+
+det_status det_model_stats(det_model* m, det_stats* out, int reset) {
+  if (!m || !out) return DET_ERR_INVALID_ARGUMENT;
+  *out = m->agg;
+  if (reset) m->agg = det_stats{};
+  return DET_OK;
+}
+
+det_status det_set_profiling(int enable) {
+  g_profiling = enable != 0;
+  return DET_OK;
+}
+
+}  // extern "C"

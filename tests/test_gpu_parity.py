@@ -1,0 +1,173 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle.
+
+Integer / byte / index results must be bit-exact, and so must every float:
+the reference's numerics are normative (fixed reduction order, explicit
+rounding), so the tolerance for logits is zero ULP.
+"""
+import numpy as np
+import pytest
+
+from detllm_b200 import synth as S
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def D():
+    import detllm_b200
+
+    assert detllm_b200.device_count() > 0, "gpu tests need a CUDA device"
+    return detllm_b200
+
+
+SPECS = {
+    "q8_0": S.ModelSpec(n_layer=2, d=256, d_ff=512, n_head=4, n_head_kv=2, vocab=1024, ctx=64),
+    "q4k_q6k": S.ModelSpec(n_layer=2, d=256, d_ff=512, n_head=4, n_head_kv=2, vocab=1024, ctx=64,
+                           t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
+                           t_out=S.GT_Q6_K, seed=5),
+    "qwen2_bias_tied_q4_0": S.ModelSpec(arch="qwen2", n_layer=2, d=128, d_ff=256, n_head=2, n_head_kv=1, vocab=600,
+                                        ctx=64, tied=True, qkv_bias=True, rope_base=1e6, t_attn=S.GT_Q4_0, seed=9),
+    "f16_f32_escapes": S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=2, vocab=300, ctx=32,
+                                   t_embd=S.GT_F16, t_attn=S.GT_F32, t_gate_up=S.GT_F16, t_down=S.GT_Q8_0,
+                                   t_out=S.GT_F32, escape_bytes=(10, 32, 65), seed=3),
+}
+
+
+@pytest.fixture(scope="module")
+def models():
+    return {k: S.build_gguf(v) for k, v in SPECS.items()}
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_device_expf_matches_vendored_expf(D, oracle):
+    # every 251st bit pattern of the f32 space plus dense sweeps where the
+    # algorithm changes branch (expf.rs:47-80) and the softmax/CDF range
+    pats = np.arange(0, 2**32, 251, dtype=np.uint64).astype(np.uint32)
+    dense = [np.linspace(-104.0, 89.0, 2_000_001, dtype=np.float32).view(np.uint32)]
+    for c in (0x42AEAC50, 0x42B17218, 0x42CFF1B5, 0x3EB17218, 0x3F851592, 0x39000000):
+        for s in (0, 0x80000000):
+            dense.append(np.arange(c - 4096, c + 4096, dtype=np.uint32) | s)
+    x = np.concatenate([pats] + dense).view(np.float32)
+    got = D.device_expf(x)
+    want = oracle.expf(x)
+    ok = (bits(got) == bits(want)) | (np.isnan(got) & np.isnan(want))
+    assert ok.all(), (x[~ok][:5], got[~ok][:5], want[~ok][:5])
+
+
+@pytest.mark.parametrize("name", ["tiny-f32", "tiny-qmix"])
+@pytest.mark.parametrize("chunk", [1, 2, 3, 6])
+def test_fixture_logits_hash(D, goldens, fixtures, name, chunk):
+    # testdata/*.logits.sha256 through det_logits_hash
+    m = D.Model(fixtures[name])
+    h = m.logits_hash_for_tokens_chunked(goldens["tokens"], chunk)
+    assert h.hex() == goldens[name.replace("-", "_") + "_logits_sha256"]
+
+
+@pytest.mark.parametrize("name", list(SPECS))
+@pytest.mark.parametrize("chunk", [1, 7, 24])
+def test_logits_bit_exact(D, oracle, models, name, chunk):
+    spec = SPECS[name]
+    toks = S.zipf_tokens(24, spec.vocab, seed=hash(name) % 1000)
+    want = oracle.Model(models[name]).logits(toks)
+    got = D.Model(models[name]).logits_for_tokens(toks, chunk=chunk)
+    assert got.shape == want.shape
+    diff = np.nonzero(bits(got) != bits(want))
+    assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
+
+
+@pytest.mark.parametrize("name", ["q8_0", "q4k_q6k"])
+def test_symbol_ranges_and_decoder(D, oracle, models, name):
+    spec = SPECS[name]
+    m = D.Model(models[name])
+    toks = S.zipf_tokens(16, spec.vocab, seed=3)
+    rng = np.random.default_rng(0)
+    with m.session(n_ctx=32, max_chunk=16) as s:
+        logits = s.forward(toks, 0, want_logits=True)
+        rows = rng.integers(0, 16, 200).astype(np.uint32)
+        syms = rng.integers(0, spec.vocab + 256, 200).astype(np.uint32)
+        syms[:8] = [0, spec.vocab - 1, spec.vocab, spec.vocab + 255, 1, 2, 3, 4]
+        got = s.symbol_ranges(syms, rows, byte_escapes=True)
+        for i in range(200):
+            assert tuple(int(v) for v in got[i]) == oracle.symbol_range(logits[rows[i]], int(syms[i]), True)
+        got_ne = s.symbol_ranges(syms % spec.vocab, rows, byte_escapes=False)
+        for i in range(0, 200, 7):
+            want = oracle.symbol_range(logits[rows[i]], int(syms[i] % spec.vocab), False)
+            assert tuple(int(v) for v in got_ne[i]) == want
+        for row in (0, 5, 15):
+            total = s.decoder_total(row)
+            assert total == oracle.decoder_total(logits[row])
+            for value in list(rng.integers(0, total, 40)) + [0, total - 1, total - 256, total - 257]:
+                got = s.decoder_lookup(row, int(value))
+                assert got == oracle.decoder_lookup(logits[row], int(value))
+
+
+@pytest.mark.parametrize("name", ["tiny-f32", "tiny-qmix"])
+def test_fixture_codec_bytes(D, oracle, goldens, fixtures, name):
+    # testdata_cli.rs:220-310 cases + docs/validation.md codec sizes
+    m = D.Model(fixtures[name])
+    cases = [b"", goldens["tiny_tokens_txt"].encode(), goldens["smoke_input"].encode(),
+             "detllm deterministic 圧縮 smoke\n復元一致\n".encode(), bytes(range(256)) + b"detllm"]
+    for data in cases:
+        got = D.compress(m, data, 8)
+        assert got == oracle.compress(fixtures[name], data, 8), (name, len(data))
+        assert D.decompress(m, got) == data
+    tok = goldens["tiny_tokens_txt"].encode()
+    assert len(D.compress(m, tok, 8)) == goldens["tokens_txt_codec"][name]["dtlz"]
+
+
+@pytest.mark.parametrize("name", list(SPECS))
+@pytest.mark.parametrize("n_ctx", [9, 64])
+def test_codec_bytes_synthetic(D, oracle, models, name, n_ctx):
+    spec = SPECS[name]
+    n_ctx = min(n_ctx, spec.ctx)
+    data = S.markov_text(120, seed=5) + bytes(range(0, 256, 5))
+    m = D.Model(models[name])
+    got = D.compress(m, data, n_ctx)
+    assert got == oracle.compress(models[name], data, n_ctx)
+    assert D.decompress(m, got) == data
+
+
+def test_encode_symbols_streams(D, oracle, models):
+    spec = SPECS["q8_0"]
+    g = models["q8_0"]
+    rng = np.random.default_rng(1)
+    m, om = D.Model(g), oracle.Model(g)
+    for n_ctx, overlap in ((8, 2), (3, 1), (5, 0), (64, 16)):
+        syms = rng.integers(0, spec.vocab + 256, 90).astype(np.uint32)
+        assert m.encode_symbols(syms, n_ctx, overlap) == om.encode_symbols(syms, n_ctx, overlap)
+        toks = rng.integers(0, spec.vocab, 90).astype(np.uint32)
+        assert m.encode_symbols(toks, n_ctx, overlap, False) == om.encode_symbols(toks, n_ctx, overlap, False)
+
+
+def test_decompress_rejections(D, oracle, fixtures):
+    m = D.Model(fixtures["tiny-f32"])
+    d = D.compress(m, b"detllm", 8)
+    with pytest.raises(D.DetError) as e:
+        D.decompress(m, d + b"\0")
+    assert e.value.code in (59, 41)
+    with pytest.raises(D.DetError) as e:
+        D.decompress(D.Model(fixtures["tiny-qmix"]), d)
+    assert e.value.code == 58
+    with pytest.raises(D.DetError) as e:
+        D.decompress(m, d[:40])
+    assert e.value.code == 48
+
+
+def test_nonfinite_is_an_error_like_the_reference(D, oracle):
+    # DET-4: an overflowing activation is rejected, not propagated
+    spec = S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=2, vocab=300, ctx=16, t_embd=S.GT_F32,
+                       t_attn=S.GT_F32, t_gate_up=S.GT_F32, t_down=S.GT_F32, t_out=S.GT_F32)
+    g = bytearray(S.build_gguf(spec))
+    # output_norm.weight (the 64 floats just before the last tensor) set to
+    # 3e38: the final RMSNorm output overflows wherever |x * r| > 1.14
+    n = 300 * 64 * 4
+    g[len(g) - n - 256:len(g) - n] = np.full(64, 3e38, "<f4").tobytes()
+    g = bytes(g)
+    with pytest.raises(oracle.OracleError) as eo:
+        oracle.Model(g).logits([1, 2])
+    with pytest.raises(D.DetError) as eg:
+        D.Model(g).logits_for_tokens([1, 2])
+    assert eo.value.code == eg.value.code == 2
