@@ -1,0 +1,305 @@
+#!/usr/bin/env python3
+"""Benchmark: encode tokens/s of the detllm token loop on B200.
+
+Workload: a TinyLlama-1.1B-shaped decoder with
+random-init Q8_0 weights (22 layers, d 2048, 32/4 heads, FFN 5632, vocab
+32000), 4096 Zipf(1.1) token ids encoded as codec symbols at n_ctx 2048
+(overlap 512, one window rollover), forward chunk 64.  One step = one full
+compress of that stream: teacher-forced forward -> logits -> CDF ranges ->
+host range coder, through det_encode_symbols.
+
+* value: tokens of all ranks / max over ranks of the device time of the
+  timed steps (CUDA events on the session stream: forward + CDF kernels).
+* e2e: same tokens / max over ranks of the wall time of the C-ABI calls with
+  host buffers (symbols in, payload out; host<->device copies and host range
+  coding inside).
+* roofline: per-launch CUDA-event timing of the weight GEMV/GEMM kernels in
+  one profiled step (algorithmic bytes / time) against MEASURED_PEAKS.json.
+* cpu_baseline / --impl reference: the C restatement of the reference CPU
+  path (oracle/, all host threads) on a bounded prefix of the same stream.
+
+Multi-GPU (torchrun, one rank per GPU): independent compression segments,
+one model replica per GPU, no data-path collective (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = "tinyllama-q8_0"
+N_TOKENS = 4096
+N_CTX = 2048
+OVERLAP = N_CTX // 4
+METRIC = "encode tokens/s (logits+CDF+code)"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_init(gpus):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        rank, local = int(os.environ["RANK"]), int(os.environ.get("LOCAL_RANK", os.environ["RANK"]))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        return rank, ws, local
+    if gpus > 1:
+        raise SystemExit("--gpus > 1 needs torchrun (one rank per GPU)")
+    return 0, 1, 0
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def all_max(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_bytes(rank, ws):
+    """Build the seeded GGUF once per box (rank 0), shared through /tmp."""
+    from detllm_b200 import synth as S
+
+    spec = S.CONFIGS[CONFIG]
+    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{CONFIG}_s{spec.seed}.gguf")
+    if rank == 0 and not os.path.exists(path):
+        t = time.time()
+        data = S.build_gguf(spec)
+        with open(path + ".part", "wb") as f:
+            f.write(data)
+        os.replace(path + ".part", path)
+        log(f"built {path} ({len(data) / 1e9:.2f} GB) in {time.time() - t:.1f}s")
+    barrier(ws)
+    with open(path, "rb") as f:
+        return spec, f.read()
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local):
+        self.local = local
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.local}", f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.p:
+            self.p.terminate()
+            self.p.wait(timeout=10)
+
+    def summary(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def oracle_sample(spec, gguf, tokens, budget_s=20.0):
+    """Time the CPU oracle on a bounded prefix (encode of the first S symbols)."""
+    from oracle import oracle as O
+
+    O.build()
+    t = time.time()
+    om = O.Model(gguf)
+    load_s = time.time() - t
+    t = time.time()
+    om.encode_symbols(tokens[:2], N_CTX, OVERLAP)
+    per_tok = max((time.time() - t) / 2, 1e-4)
+    s = int(max(4, min(len(tokens), budget_s / per_tok)))
+    t = time.time()
+    om.encode_symbols(tokens[:s], N_CTX, OVERLAP)
+    dt = time.time() - t
+    om.close()
+    return s, dt, load_s
+
+
+def run_reference(args):
+    rank, ws, local = dist_init(args.gpus)
+    if rank != 0:
+        return
+    from detllm_b200 import synth as S
+
+    spec, gguf = model_bytes(0, 1)
+    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7)
+    from oracle import oracle as O
+
+    O.build()
+    om = O.Model(gguf)
+    per = []
+    sample = args.ref_sample
+    for i in range(args.warmup + args.steps):
+        t = time.time()
+        om.encode_symbols(tokens[:sample], N_CTX, OVERLAP)
+        if i >= args.warmup:
+            per.append(time.time() - t)
+    tps = sample * len(per) / sum(per)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(per) / len(per),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
+        "data": "synthetic (seeded random-init weights, Zipf tokens)",
+        "config": {"workload": f"{CONFIG} encode, first {sample} of {N_TOKENS} Zipf tokens per step, n_ctx {N_CTX}",
+                   "global_batch": sample, "seq_len": N_CTX, "parallelism": "cpu"},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"first {sample} tokens of the {N_TOKENS}-token stream per step"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run(args):
+    import numpy as np
+
+    rank, ws, local = dist_init(args.gpus)
+    import detllm_b200 as D
+    from detllm_b200 import synth as S
+
+    spec, gguf = model_bytes(rank, ws)
+    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7 + rank)  # one segment per rank
+    t = time.time()
+    model = D.Model(gguf, device=local)
+    log(f"rank {rank}: model on cuda:{local} in {time.time() - t:.1f}s")
+    import torch
+
+    torch.cuda.set_device(local)
+    for _ in range(args.warmup):
+        model.encode_symbols(tokens, N_CTX, OVERLAP)
+    model.stats(reset=True)
+    barrier(ws)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            payload = model.encode_symbols(tokens, N_CTX, OVERLAP)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    barrier(ws)
+    st = model.stats(reset=True)
+    dev_s = (st.forward_ms + st.cdf_ms) / 1000.0
+    dev_max, wall_max = all_max(dev_s, ws), all_max(wall, ws)
+    # one profiled step for the per-launch GEMV/GEMM roofline
+    D.set_profiling(True)
+    model.encode_symbols(tokens, N_CTX, OVERLAP)
+    D.set_profiling(False)
+    prof = model.stats(reset=True)
+    if rank != 0:
+        return
+    total_tokens = N_TOKENS * args.steps * ws
+    peak, peak_kind = peaks()
+    achieved = prof.gemm_bytes / (prof.gemm_ms / 1000.0) / 1e9 if prof.gemm_ms > 0 else None
+    line = {
+        "metric": METRIC, "value": total_tokens / dev_max, "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
+        "data": "synthetic (seeded random-init weights, Zipf(1.1) tokens)",
+        "config": {"workload": f"{CONFIG} encode: {N_TOKENS} Zipf tokens per rank, n_ctx {N_CTX}, overlap {OVERLAP}, "
+                               f"chunk 64", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
+                   "parallelism": f"segments{ws}", "l2": "weights 1.17 GB per step > 126 MB L2 (no flush)"},
+        "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
+                "d2h_bytes_per_step": st.d2h_bytes // args.steps},
+        "gpu_launches": int(st.launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if achieved else None, "traffic": None,
+                     "kernel": "weight GEMV/GEMM (Q8_0 x Q8A)", "peak_kind": peak_kind,
+                     "launches": int(prof.gemm_launches), "ms_per_launch": prof.gemm_ms / max(prof.gemm_launches, 1),
+                     "bytes_per_launch": prof.gemm_bytes / max(prof.gemm_launches, 1),
+                     "share_of_device_time": prof.gemm_ms / max(prof.forward_ms + prof.cdf_ms, 1e-9)},
+        "clocks": clk.summary(),
+        "payload_bytes": len(payload),
+        "weight_bytes_per_token": S.weight_bytes_per_token(spec),
+    }
+    if ws == 1 and not args.no_cpu_baseline:
+        s, dt, load_s = oracle_sample(spec, gguf, tokens)
+        line["cpu_baseline"] = {"value": s / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"encode of the first {s} tokens of the stream (~{dt:.0f}s)"}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
+def main():
+    global N_TOKENS
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--ref-sample", type=int, default=16, help="tokens per reference step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=N_TOKENS,
+                    help="tokens per rank per step (the benchmark uses 4096; smaller values are for profiling)")
+    args = ap.parse_args()
+    N_TOKENS = args.tokens
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -103,7 +103,7 @@ det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_c
   for (const auto& w : windows)
     if (w.needed) need_device = true;
   if (need_device)
-    if (det_status st = det_session_create(m, n_ctx, kChunk, &s)) return st;
+    if (det_status st = session_acquire(m, n_ctx, kChunk, &s)) return st;
   std::vector<uint32_t> rows, qsym;
   std::vector<det_symbol_range> ranges;
   det_status st = DET_OK;
@@ -137,7 +137,6 @@ det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_c
       if (!st) st = drain_uniform();
     }
   }
-  if (s) det_session_free(s);
   if (st) return st;
   if (next != n) return DET_ERR_WINDOW;
   *payload = enc.finish();
@@ -235,7 +234,8 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
   RangeDecoder dec;
   if (det_status st = dec.init(payload, plen)) return st;
   det_session* s = nullptr;
-  if (det_status st = det_session_create(m, n_ctx, kChunk, &s)) return st;
+  if (det_status st = session_acquire(m, n_ctx, kChunk, &s)) return st;
+  if (det_status st = det_session_reset(s)) return st;
   std::vector<uint8_t> bytes;
   std::vector<uint32_t> ctx, syms;
   size_t ws = 0, clen = 0;
@@ -290,7 +290,6 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
     clen++;
     last_row = 0;
   }
-  det_session_free(s);
   if (st) return st;
   std::vector<uint8_t> canon;
   if ((st = encode_impl(m, syms.data(), syms.size(), n_ctx, overlap, escapes, &canon))) return st;

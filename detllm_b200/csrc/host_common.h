@@ -134,6 +134,10 @@ struct det_model {
   bool has_bias = false;
   size_t weight_bytes = 0;  // device bytes of all weight matrices
   det_stats agg{};          // stats of finished sessions
+  // session reused by the model-level entry points (encode / decode /
+  // logits hash) so repeated calls skip allocation, RoPE table and graph
+  // capture; those entry points are not re-entrant on one model
+  det_session* cached = nullptr;
 };
 
 struct det_session {
@@ -152,9 +156,17 @@ struct det_session {
   float *cdf_e = nullptr, *cdf_z = nullptr;
   uint32_t *d_tokens = nullptr, *d_rows = nullptr, *d_syms = nullptr, *d_err = nullptr;
   uint64_t *d_out = nullptr, *d_value = nullptr;
+  int* d_pos = nullptr;  // first position of the current chunk (read by RoPE / attention)
   // pinned staging
   uint32_t *h_tokens = nullptr, *h_rows = nullptr, *h_syms = nullptr, *h_err = nullptr;
   uint64_t *h_out = nullptr, *h_value = nullptr;
+  int* h_pos = nullptr;
+  // one CUDA graph per chunk size: copies of tokens / pos0 + the whole forward
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    uint64_t kernels = 0;
+  };
+  std::vector<Graph> graphs;  // indexed by chunk size
   int last_n = 0;
   std::vector<uint8_t> cdf_ready;
   det_stats stats{};
@@ -166,4 +178,7 @@ struct det_session {
 
 namespace det {
 extern bool g_profiling;
+// model-owned session for the model-level entry points (not re-entrant)
+det_status session_acquire(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out);
+void session_release_cached(det_model* m);
 }

@@ -27,8 +27,15 @@ enum : uint32_t {
 //   Q4_0 : q uint8 [rows][cols/2] (GGUF nibble order per 32-block), d [rows][nb]
 //   Q4_K : q uint8 [rows][nb][144] (GGUF super-blocks, 16-byte aligned)
 //   Q6_K : q uint8 [rows][nb][208] (ql | qh | scales), d [rows][nb]
+// Layouts of Q8_0 / Q4_0 matrices:
+//   LAYOUT_ROWMAJOR: as above
+//   LAYOUT_MMA16   : 16-row tiles of per-block records in m16n8k32 A-fragment
+//                    order (gemm.cu documents the record format)
+enum : int { LAYOUT_ROWMAJOR = 0, LAYOUT_MMA16 = 1 };
+
 struct DevMatrix {
   int type = GT_F32;
+  int layout = LAYOUT_ROWMAJOR;
   int rows = 0, cols = 0, nb = 0;
   const void* q = nullptr;
   const uint16_t* d = nullptr;
@@ -62,12 +69,14 @@ cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, floa
 cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                         int epi, const float* bias);
-cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, int pos0, int n_head,
+cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, const int* pos0, int n_head,
                               int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
                               const float* sin_t, float* kc, float* vc, int n_ctx);
-cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, int pos0,
+cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, const int* pos0,
                              int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
                              float* score_scratch);
+// floats of global score scratch launch_attention needs (0: scores stay in smem)
+size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx);
 cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T);
 cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, const uint32_t* rows, int nrows,
                                float* e, float* z);

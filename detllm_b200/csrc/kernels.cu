@@ -125,16 +125,23 @@ __global__ void embed_kernel(DevMatrix m, const uint32_t* tokens, int T, float* 
     float v;
     switch (m.type) {
       case GT_F32: v = m.f[(size_t)tok * K + i]; break;
-      case GT_Q8_0: {
-        const int8_t q = ((const int8_t*)m.q)[(size_t)tok * K + i];
-        v = fmul(f16_bits_to_f32(m.d[(size_t)tok * m.nb + (i >> 5)]), (float)q);
-        break;
-      }
-      case GT_Q4_0: {
-        const uint8_t* qs = (const uint8_t*)m.q + (size_t)tok * (K / 2) + (i >> 5) * 16;
-        const int j = i & 31;
-        const int nib = j < 16 ? (qs[j] & 0x0f) : (qs[j - 16] >> 4);
-        v = fmul(f16_bits_to_f32(m.d[(size_t)tok * m.nb + (i >> 5)]), (float)(nib - 8));
+      case GT_Q8_0:
+      case GT_Q4_0: {  // tile records (gemm.cu): element (tok, i) of the block
+        const bool q8 = m.type == GT_Q8_0;
+        const int rb = q8 ? 544 : 288, qb = q8 ? 512 : 256;
+        const int rr = (int)(tok & 15), g = rr & 7, hi = rr >> 3, b = i >> 5, c = i & 31;
+        const uint8_t* rec = (const uint8_t*)m.q + ((size_t)(tok >> 4) * m.nb + b) * rb;
+        const int lane = g * 4 + ((c & 15) >> 2);
+        int qv;
+        if (q8) {
+          qv = (int8_t)rec[lane * 16 + hi * 4 + (c >= 16 ? 8 : 0) + (c & 3)];
+        } else {  // Q4_0: element j < 16 low nibble of byte j, else high nibble
+          const uint8_t byte = rec[lane * 8 + hi * 4 + (c & 3)];
+          qv = (c < 16 ? (byte & 0x0f) : (byte >> 4)) - 8;
+        }
+        const uint32_t sw = *reinterpret_cast<const uint32_t*>(rec + qb + 4 * g);
+        const float d = f16_bits_to_f32((uint16_t)(hi ? (sw >> 16) : (sw & 0xffffu)));
+        v = fmul(d, (float)qv);
         break;
       }
       case GT_Q4_K:
@@ -153,23 +160,33 @@ __global__ void embed_kernel(DevMatrix m, const uint32_t* tokens, int T, float* 
 
 // ---- rmsnorm (det-model lib.rs:2053-2073) ----------------------------------
 // sum_squares_f32_ref: lane l accumulates x[i]^2 for i = l (mod 8) in order.
+// The row is staged in shared memory by all threads (coalesced), then eight
+// threads run the eight ordered lane chains out of shared memory.
+constexpr int RMS_MAX_SMEM = 16384;  // floats staged per row (larger rows read global)
+
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
                                float* __restrict__ h, uint32_t* err) {
+  extern __shared__ float xs[];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * n;
   __shared__ float lanes[8];
   __shared__ float r_s;
+  const bool staged = n <= RMS_MAX_SMEM;
+  if (staged)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
+  __syncthreads();
+  const float* src = staged ? xs : xr;
   if (threadIdx.x < 8) {
     float acc = 0.0f;
     int i = threadIdx.x;
-    for (; i + 24 < n; i += 32) {
-      const float a0 = xr[i], a1 = xr[i + 8], a2 = xr[i + 16], a3 = xr[i + 24];
-      acc = fadd(acc, fmul(a0, a0));
-      acc = fadd(acc, fmul(a1, a1));
-      acc = fadd(acc, fmul(a2, a2));
-      acc = fadd(acc, fmul(a3, a3));
+    for (; i + 56 < n; i += 64) {
+      float a[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) a[k] = src[i + 8 * k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = fadd(acc, fmul(a[k], a[k]));
     }
-    for (; i < n; i += 8) acc = fadd(acc, fmul(xr[i], xr[i]));
+    for (; i < n; i += 8) acc = fadd(acc, fmul(src[i], src[i]));
     lanes[threadIdx.x] = acc;
   }
   __syncthreads();
@@ -271,39 +288,6 @@ DI float dot_row(const DevMatrix& m, const DevActs& a, int r, int t) {
       for (int i = 0; i < K; i++) acc[i & 7] = fadd(acc[i & 7], fmul(w[i], x[i]));
       return finish8(acc);
     }
-    case GT_Q8_0: {  // dot_q8_0_q8a (det-quant lib.rs:237-257, 423-430)
-      const int* w = (const int*)((const int8_t*)m.q + (size_t)r * K);
-      const int* q = (const int*)(a.qa_q + (size_t)t * K);
-      const uint16_t* wd = m.d + (size_t)r * m.nb;
-      const float* ad = a.qa_d + (size_t)t * m.nb;
-      float sum = 0.0f;
-      for (int b = 0; b < m.nb; b++) {
-        int isum = 0;
-#pragma unroll
-        for (int k = 0; k < 8; k++) isum = __dp4a(w[b * 8 + k], q[b * 8 + k], isum);
-        const float scale = fmul(f16_bits_to_f32(wd[b]), ad[b]);
-        sum = fadd(sum, fmul(scale, __int2float_rn(isum)));
-      }
-      return sum;
-    }
-    case GT_Q4_0: {  // dot_q4_0_q8a (det-quant lib.rs:259-279, 455-466)
-      const uint8_t* w = (const uint8_t*)m.q + (size_t)r * (K / 2);
-      const int8_t* q = a.qa_q + (size_t)t * K;
-      const uint16_t* wd = m.d + (size_t)r * m.nb;
-      const float* ad = a.qa_d + (size_t)t * m.nb;
-      float sum = 0.0f;
-      for (int b = 0; b < m.nb; b++) {
-        int isum = 0;
-        for (int i = 0; i < 16; i++) {
-          const uint8_t p = w[b * 16 + i];
-          isum += ((int)(p & 0x0f) - 8) * (int)q[b * 32 + i];
-          isum += ((int)(p >> 4) - 8) * (int)q[b * 32 + i + 16];
-        }
-        const float scale = fmul(f16_bits_to_f32(wd[b]), ad[b]);
-        sum = fadd(sum, fmul(scale, __int2float_rn(isum)));
-      }
-      return sum;
-    }
     case GT_Q4_K: {  // dot_q4_k_q8a (det-quant lib.rs:281-315): one f32 chain
       const uint8_t* w = (const uint8_t*)m.q + (size_t)r * m.nb * 144;
       const int8_t* q = a.qa_q + (size_t)t * K;
@@ -387,11 +371,11 @@ __global__ void gemv_generic_kernel(DevMatrix m, DevActs a, int T, float* out, i
 
 // ---- RoPE + KV store: apply_rope (det-model lib.rs:2011-2051) and
 // KvCache::store (:883-913) ------------------------------------------------
-__global__ void rope_store_kernel(float* q, float* k, const float* v, int pos0, int n_head, int n_head_kv,
+__global__ void rope_store_kernel(float* q, float* k, const float* v, const int* pos0p, int n_head, int n_head_kv,
                                   int hd, int half, int pairing, const float* cos_t, const float* sin_t, float* kc,
                                   float* vc, int n_ctx, uint32_t* err) {
   const int t = blockIdx.x;
-  const int pos = pos0 + t;
+  const int pos = *pos0p + t;
   const float* cs = cos_t + (size_t)pos * half;
   const float* sn = sin_t + (size_t)pos * half;
   float* qt = q + (size_t)t * n_head * hd;
@@ -435,7 +419,7 @@ __global__ void rope_store_kernel(float* q, float* k, const float* v, int pos0, 
 constexpr int ATT_THREADS = 256;
 
 __global__ void attention_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                                 const float* __restrict__ vc, int pos0, int n_head, int n_head_kv, int hd,
+                                 const float* __restrict__ vc, const int* pos0p, int n_head, int n_head_kv, int hd,
                                  int n_ctx, float scale, float* __restrict__ out, float* __restrict__ scratch,
                                  int smem_scores, uint32_t* err) {
   extern __shared__ float sm[];
@@ -443,7 +427,7 @@ __global__ void attention_kernel(const float* __restrict__ q, const float* __res
   __shared__ float lanes[8];
   __shared__ float z_s;
   const int t = blockIdx.x, head = blockIdx.y;
-  const int len = pos0 + t + 1;
+  const int len = *pos0p + t + 1;
   const int kvh = head / (n_head / n_head_kv);
   const float* kb = kc + (size_t)kvh * n_ctx * hd;
   const float* vb = vc + (size_t)kvh * n_ctx * hd;
@@ -515,6 +499,138 @@ __global__ void attention_kernel(const float* __restrict__ q, const float* __res
   }
 }
 
+// ---- attention, GQA-grouped: one CTA per (position, KV head) computes every
+// query head that shares the KV head, so each K/V row is staged in shared
+// memory once for the whole group.  Same arithmetic as attention_kernel:
+// scores by dot_f32_ref * scale, softmax with expf(max(s - m, -88)) and the
+// 8-lane Z, then o[d] += p_j * v_j[d] for j ascending (one thread per chain).
+constexpr int ATG_THREADS = 512;
+constexpr int ATG_J = 64;  // K/V rows per staged chunk
+
+__global__ void __launch_bounds__(ATG_THREADS)
+    attention_gqa_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                         const int* pos0p, int n_head, int n_head_kv, int hd, int n_ctx, float scale,
+                         float* __restrict__ out, float* __restrict__ scratch, int smem_scores, uint32_t* err) {
+  extern __shared__ __align__(16) float sm[];
+  const int t = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
+  const int gsz = n_head / n_head_kv, h0 = kvh * gsz;
+  const int len = *pos0p + t + 1;
+  const float* kb = kc + (size_t)kvh * n_ctx * hd;
+  const float* vb = vc + (size_t)kvh * n_ctx * hd;
+  float* ob = out + ((size_t)t * n_head + h0) * hd;
+  if (len == 1) {  // score_len == 1 copies V (:2319-2322)
+    for (int i = tid; i < gsz * hd; i += ATG_THREADS) ob[i] = vb[i % hd];
+    return;
+  }
+  const bool vec = (hd & 7) == 0;
+  const int ks = vec ? hd + 4 : hd + 1;  // padded K row stride (floats)
+  float* qs = sm;                         // [gsz][hd]
+  float* kvs = qs + gsz * hd;             // [ATG_J][ks]  (K chunk, then V chunk)
+  float* sc = smem_scores ? kvs + ATG_J * ks : scratch + ((size_t)t * n_head + h0) * n_ctx;  // [gsz][n_ctx]
+  __shared__ float zs[32];
+  const float* qg = q + ((size_t)t * n_head + h0) * hd;
+  for (int i = tid; i < gsz * hd; i += ATG_THREADS) {
+    const float v = qg[i];
+    if (!finite(v)) flag(err, ERRF_NONFINITE);
+    qs[i] = v;
+  }
+  // ---- scores (:2335-2359)
+  for (int jc = 0; jc < len; jc += ATG_J) {
+    const int cnt = min(ATG_J, len - jc);
+    __syncthreads();  // previous chunk consumed
+    for (int i = tid; i < cnt * hd; i += ATG_THREADS) {
+      const int jj = i / hd, d = i - jj * hd;
+      kvs[jj * ks + d] = kb[(size_t)(jc + jj) * hd + d];
+    }
+    __syncthreads();
+    for (int pr = tid; pr < gsz * cnt; pr += ATG_THREADS) {
+      const int h = pr / cnt, jj = pr - h * cnt;
+      const float* qh = qs + h * hd;
+      const float* kr = kvs + jj * ks;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (vec) {
+        for (int i = 0; i < hd; i += 8) {
+          const float4 k0 = *reinterpret_cast<const float4*>(kr + i);
+          const float4 k1 = *reinterpret_cast<const float4*>(kr + i + 4);
+          acc[0] = fadd(acc[0], fmul(qh[i + 0], k0.x));
+          acc[1] = fadd(acc[1], fmul(qh[i + 1], k0.y));
+          acc[2] = fadd(acc[2], fmul(qh[i + 2], k0.z));
+          acc[3] = fadd(acc[3], fmul(qh[i + 3], k0.w));
+          acc[4] = fadd(acc[4], fmul(qh[i + 4], k1.x));
+          acc[5] = fadd(acc[5], fmul(qh[i + 5], k1.y));
+          acc[6] = fadd(acc[6], fmul(qh[i + 6], k1.z));
+          acc[7] = fadd(acc[7], fmul(qh[i + 7], k1.w));
+        }
+      } else {
+        for (int i = 0; i < hd; i++) acc[i & 7] = fadd(acc[i & 7], fmul(qh[i], kr[i]));
+      }
+      const float s = fmul(finish8(acc), scale);
+      if (!finite(s)) flag(err, ERRF_NONFINITE);
+      sc[(size_t)h * n_ctx + jc + jj] = s;
+    }
+  }
+  __syncthreads();
+  // ---- softmax per head (:2361-2388): one warp per head
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int h = warp; h < gsz; h += ATG_THREADS / 32) {
+    float* s = sc + (size_t)h * n_ctx;
+    float m = -INFINITY;
+    for (int j = lane; j < len; j += 32) m = fmaxf(m, s[j]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int j = lane; j < len; j += 32) {
+      const float dlt = fsub(s[j], m);
+      s[j] = expf_det(dlt > -88.0f ? dlt : -88.0f);
+    }
+    __syncwarp();
+    float acc = 0.0f;  // sum_f32_ref: lanes 0..7 run the ordered lane chains
+    if (lane < 8) {
+      int j = lane;
+      for (; j + 56 < len; j += 64) {
+        float e[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) e[k] = s[j + 8 * k];
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+      }
+      for (; j < len; j += 8) acc = fadd(acc, s[j]);
+    }
+    float a[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) a[k] = __shfl_sync(0xffffffffu, acc, k);
+    const float z = finish8(a);
+    if (lane == 0 && (!finite(z) || z == 0.0f)) flag(err, ERRF_NONFINITE);
+    for (int j = lane; j < len; j += 32) s[j] = fdiv(s[j], z);
+  }
+  // ---- o[d] += p_j * v_j[d], j ascending (:2390-2418): one thread per chain
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nch = gsz * hd;
+  for (int jc = 0; jc < len; jc += ATG_J) {
+    const int cnt = min(ATG_J, len - jc);
+    __syncthreads();  // scores final / previous V chunk consumed
+    for (int i = tid; i < cnt * hd; i += ATG_THREADS) kvs[i] = vb[(size_t)jc * hd + i];
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int idx = tid + c * ATG_THREADS;
+      if (idx < nch) {
+        const int h = idx / hd, d = idx - h * hd;
+        const float* p = sc + (size_t)h * n_ctx + jc;
+        float acc = o[c];
+        for (int jj = 0; jj < cnt; jj++) acc = fadd(acc, fmul(p[jj], kvs[jj * hd + d]));
+        o[c] = acc;
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const int idx = tid + c * ATG_THREADS;
+    if (idx < nch) {
+      if (!finite(o[c])) flag(err, ERRF_NONFINITE);
+      ob[idx] = o[c];
+    }
+  }
+}
+
 // ---- swiglu (det-model lib.rs:2420-2434) ---------------------------------
 __global__ void swiglu_kernel(const float* g, const float* u, float* out, long long n, uint32_t* err) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -527,6 +643,7 @@ __global__ void swiglu_kernel(const float* g, const float* u, float* out, long l
 
 // ---- logits -> CDF (det-coder cdf.rs:138-245) ----------------------------
 constexpr int CDF_THREADS = 512;
+constexpr int CDF_CHUNK = 4096;  // floats per shared-memory chunk (multiple of 8)
 
 // per row: max, e_i = expf(max(l_i - m, -88)), Z = sum_f32_ref(e)
 __global__ void cdf_prepare_kernel(const float* __restrict__ logits, int V, const uint32_t* rows,
@@ -545,24 +662,39 @@ __global__ void cdf_prepare_kernel(const float* __restrict__ logits, int V, cons
   }
   if (bad) flag(err, ERRF_CDF_NONFINITE);
   const float mx = block_max<CDF_THREADS>(lmax, red);
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float d = fsub(l[i], mx);
-    er[i] = expf_det(d > -88.0f ? d : -88.0f);
-  }
-  __syncthreads();
-  if (threadIdx.x < 8) {
-    float acc = 0.0f;
-    int i = threadIdx.x;
-    for (; i + 56 < V; i += 64) {
-      float v[8];
+  // Double-buffered through shared memory: while lanes 0..7 of warp 0 run
+  // the eight ordered Z chains (sum_f32_ref) over chunk c-1, warps 1..15
+  // compute e_i = expf(max(l_i - m, -88)) for chunk c (and store it for the
+  // frequency pass).  CDF_CHUNK is a multiple of 8, so chunk boundaries keep
+  // every lane's elements in order.
+  __shared__ float ebuf[2][CDF_CHUNK];
+  const int nchunk = (V + CDF_CHUNK - 1) / CDF_CHUNK;
+  float acc = 0.0f;
+  for (int c = 0; c <= nchunk; c++) {
+    if (threadIdx.x >= 32 && c < nchunk) {
+      const int base = c * CDF_CHUNK, cnt = min(CDF_CHUNK, V - base);
+      for (int i = threadIdx.x - 32; i < cnt; i += blockDim.x - 32) {
+        const float d = fsub(l[base + i], mx);
+        const float e = expf_det(d > -88.0f ? d : -88.0f);
+        ebuf[c & 1][i] = e;
+        er[base + i] = e;
+      }
+    } else if (threadIdx.x < 8 && c > 0) {
+      const int base = (c - 1) * CDF_CHUNK, cnt = min(CDF_CHUNK, V - base);
+      const float* eb = ebuf[(c - 1) & 1];
+      int i = threadIdx.x;
+      for (; i + 56 < cnt; i += 64) {
+        float v[8];
 #pragma unroll
-      for (int k = 0; k < 8; k++) v[k] = er[i + 8 * k];
+        for (int k = 0; k < 8; k++) v[k] = eb[i + 8 * k];
 #pragma unroll
-      for (int k = 0; k < 8; k++) acc = fadd(acc, v[k]);
+        for (int k = 0; k < 8; k++) acc = fadd(acc, v[k]);
+      }
+      for (; i < cnt; i += 8) acc = fadd(acc, eb[i]);
     }
-    for (; i < V; i += 8) acc = fadd(acc, er[i]);
-    lanes[threadIdx.x] = acc;
+    __syncthreads();
   }
+  if (threadIdx.x < 8) lanes[threadIdx.x] = acc;
   __syncthreads();
   if (threadIdx.x == 0) z[row] = finish8(lanes);
 }
@@ -700,7 +832,12 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
 }
 
 cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h) {
-  rmsnorm_kernel<<<T, 256, 0, L.stream>>>(x, w, n, eps, h, L.err);
+  const size_t smem = n <= RMS_MAX_SMEM ? (size_t)n * sizeof(float) : 0;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  rmsnorm_kernel<<<T, 256, smem, L.stream>>>(x, w, n, eps, h, L.err);
   return post(L);
 }
 
@@ -729,7 +866,7 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   return post(L);
 }
 
-cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, int pos0, int n_head,
+cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, const int* pos0, int n_head,
                               int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
                               const float* sin_t, float* kc, float* vc, int n_ctx) {
   rope_store_kernel<<<T, 256, 0, L.stream>>>(q, k, v, pos0, n_head, n_head_kv, head_dim, rope_dim / 2, pairing,
@@ -737,9 +874,44 @@ cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* 
   return post(L);
 }
 
-cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, int pos0,
+namespace {
+// shared-memory plan of attention_gqa_kernel: returns false when the group
+// is too wide for it (more than 4 chains per thread)
+bool gqa_plan(int n_head, int n_head_kv, int hd, int n_ctx, size_t* smem, int* smem_scores) {
+  const int gsz = n_head / n_head_kv;
+  if ((size_t)gsz * hd > 4 * (size_t)ATG_THREADS) return false;
+  const int ks = (hd & 7) == 0 ? hd + 4 : hd + 1;
+  const size_t base = ((size_t)gsz * hd + (size_t)ATG_J * ks) * sizeof(float);
+  const size_t with_scores = base + (size_t)gsz * n_ctx * sizeof(float);
+  *smem_scores = with_scores <= 200 * 1024 ? 1 : 0;
+  *smem = *smem_scores ? with_scores : base;
+  return true;
+}
+}  // namespace
+
+size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx) {
+  size_t smem;
+  int in_smem;
+  if (gqa_plan(n_head, n_head_kv, hd, n_ctx, &smem, &in_smem)) return in_smem ? 0 : (size_t)T * n_head * n_ctx;
+  return (size_t)(hd + n_ctx) * sizeof(float) <= 160 * 1024 ? 0 : (size_t)T * n_head * n_ctx;
+}
+
+cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, const int* pos0,
                              int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
                              float* score_scratch) {
+  size_t gsmem;
+  int gscores;
+  if (gqa_plan(n_head, n_head_kv, head_dim, n_ctx, &gsmem, &gscores)) {
+    if (gsmem > 48 * 1024) {
+      cudaError_t e =
+          cudaFuncSetAttribute(attention_gqa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem);
+      if (e != cudaSuccess) return e;
+    }
+    dim3 grid(T, n_head_kv);
+    attention_gqa_kernel<<<grid, ATG_THREADS, gsmem, L.stream>>>(q, kc, vc, pos0, n_head, n_head_kv, head_dim, n_ctx,
+                                                                 scale, out, score_scratch, gscores, L.err);
+    return post(L);
+  }
   const size_t need = (size_t)(head_dim + n_ctx) * sizeof(float);
   const int smem_scores = need <= 160 * 1024 ? 1 : 0;
   const size_t smem = smem_scores ? need : head_dim * sizeof(float);

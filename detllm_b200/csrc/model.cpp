@@ -194,6 +194,42 @@ struct Loader {
     }
     if (rows == 0 || cols == 0) return DET_ERR_SHAPE;
     void* p;
+    if (t->type == GT_Q8_0 || t->type == GT_Q4_0) {
+      // tensor-core tile records (gemm.cu): one record per (16-row tile, block)
+      const bool q8 = t->type == GT_Q8_0;
+      const size_t qb = q8 ? 512 : 256, rb = qb + 32, per_row = q8 ? 32 : 16;
+      const size_t tiles = (rows + 15) / 16;
+      std::vector<uint8_t> recs(tiles * nb * rb, 0);
+      for (size_t tl = 0; tl < tiles; tl++)
+        for (size_t b = 0; b < nb; b++) {
+          uint8_t* r = &recs[(tl * nb + b) * rb];
+          for (int lane = 0; lane < 32; lane++) {
+            const size_t g = (size_t)lane / 4, tg = (size_t)lane % 4;
+            for (int hi = 0; hi < 2; hi++) {
+              const size_t row = tl * 16 + g + 8 * hi;
+              if (row >= rows) continue;
+              const uint8_t* src = &q[(row * nb + b) * per_row];
+              if (q8) {
+                std::memcpy(r + lane * 16 + hi * 4, src + tg * 4, 4);
+                std::memcpy(r + lane * 16 + 8 + hi * 4, src + 16 + tg * 4, 4);
+              } else {
+                std::memcpy(r + lane * 8 + hi * 4, src + tg * 4, 4);
+              }
+            }
+          }
+          for (size_t g = 0; g < 8; g++) {
+            const size_t r0 = tl * 16 + g, r1 = r0 + 8;
+            const uint16_t d0 = r0 < rows ? d[r0 * nb + b] : 0, d1 = r1 < rows ? d[r1 * nb + b] : 0;
+            const uint32_t w = (uint32_t)d0 | ((uint32_t)d1 << 16);
+            std::memcpy(r + qb + 4 * g, &w, 4);
+          }
+        }
+      if (det_status st = upload(recs.data(), recs.size(), &p)) return st;
+      out->q = p;
+      out->layout = LAYOUT_MMA16;
+      m->weight_bytes += recs.size();
+      return DET_OK;
+    }
     if (det_status st = upload(q.data(), q.size(), &p)) return st;
     out->q = p;
     m->weight_bytes += q.size();
@@ -385,6 +421,7 @@ void free_model(det_model* m) {
   if (!m) return;
   int cur;
   if (cudaGetDevice(&cur) == cudaSuccess && cur != m->device) cudaSetDevice(m->device);
+  session_release_cached(m);
   for (void* p : m->allocations) cudaFree(p);
   delete m;
 }

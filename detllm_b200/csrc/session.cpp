@@ -15,6 +15,35 @@ using namespace det;
 
 bool det::g_profiling = false;
 
+namespace det {
+void free_session_impl(det_session* s);
+
+// The model's cached session (created on first use, replaced when a caller
+// needs a different window or chunk size).  Released by det_model_free.
+det_status session_acquire(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out) {
+  det_session* c = m->cached;
+  if (c && c->n_ctx == (int)n_ctx && c->max_chunk == (int)std::min(max_chunk, n_ctx)) {
+    *out = c;
+    return DET_OK;
+  }
+  if (c) {
+    m->cached = nullptr;
+    free_session_impl(c);
+  }
+  det_status st = det_session_create(m, n_ctx, max_chunk, out);
+  if (!st) m->cached = *out;
+  return st;
+}
+
+void session_release_cached(det_model* m) {
+  if (m->cached) {
+    det_session* c = m->cached;
+    m->cached = nullptr;
+    free_session_impl(c);
+  }
+}
+}  // namespace det
+
 namespace {
 
 det_status cuda_status(cudaError_t e) {
@@ -62,15 +91,23 @@ void free_session(det_session* s) {
   if (s->stream) cudaStreamSynchronize(s->stream);
   add_stats(&s->m->agg, s->stats);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
+  for (auto& g : s->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
   for (void* p : s->allocations) cudaFree(p);
   for (void* p : {(void*)s->h_tokens, (void*)s->h_rows, (void*)s->h_syms, (void*)s->h_err, (void*)s->h_out,
-                  (void*)s->h_value})
+                  (void*)s->h_value, (void*)s->h_pos})
     if (p) cudaFreeHost(p);
   for (auto& e : s->ev)
     if (e) cudaEventDestroy(e);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
 }
+
+}  // namespace
+
+void det::free_session_impl(det_session* s) { free_session(s); }
+
+namespace {
 
 Launch launch_of(det_session* s) { return Launch{s->stream, s->d_err, &s->stats.launches}; }
 
@@ -102,9 +139,9 @@ det_status take_error(det_session* s, bool cdf) {
 }
 
 // quantise `x` (T x K) for a matrix of type `type` into the session buffers
-cudaError_t quantise_for(det_session* s, int type, const float* x, int K, int T, DevActs* a, int* have) {
+cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float* x, int K, int T, DevActs* a,
+                         int* have) {
   a->x = x;
-  const Launch L = launch_of(s);
   if (needs_q8a(type) && !(*have & 1)) {
     cudaError_t e = launch_quant_q8a(L, x, K, T, s->qa_d, s->qa_q);
     if (e != cudaSuccess) return e;
@@ -139,9 +176,8 @@ double bytes_per_weight(int type) {
 }
 
 // launch_gemv with optional per-launch event timing (det_set_profiling)
-cudaError_t gemv(det_session* s, const DevMatrix& W, const DevActs& a, int T, float* out, int ld, int epi,
-                 const float* bias) {
-  const Launch L = launch_of(s);
+cudaError_t gemv(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T, float* out, int ld,
+                 int epi, const float* bias) {
   if (!g_profiling) return launch_gemv(L, W, a, T, out, ld, epi, bias);
   const size_t i = s->prof_pending.size();
   while (s->prof_events.size() < 2 * (i + 1)) {
@@ -161,12 +197,14 @@ cudaError_t gemv(det_session* s, const DevMatrix& W, const DevActs& a, int T, fl
   return e;
 }
 
-// forward_one_with_workspace for positions pos0 .. pos0+T-1 (tokens already
-// on the device in s->d_tokens)
-det_status forward_chunk(det_session* s, int T, int pos0) {
+// forward_one_with_workspace for positions pos0 .. pos0+T-1, pos0 = *d_pos
+// (tokens and pos0 already on the device)
+det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
   det_model* m = s->m;
   const ModelCfg& c = m->cfg;
-  const Launch L = launch_of(s);
+  Launch L = launch_of(s);
+  L.launches = launch_counter;
+  const int* pos0 = s->d_pos;
   const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
   const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
   CK(launch_embed(L, m->tok_embd, s->d_tokens, T, s->x));
@@ -177,12 +215,12 @@ det_status forward_chunk(det_session* s, int T, int pos0) {
     int have = 0;
     // one Q8A of h shared by q/k/v (:1284-1292); Q8_K recomputed per Q6_K
     // matrix in the reference gives the same blocks, so it is made once too
-    CK(quantise_for(s, W.wq.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, W.wk.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, W.wv.type, s->h, c.d, T, &a, &have));
-    CK(gemv(s,W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
-    CK(gemv(s,W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
-    CK(gemv(s,W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+    CK(quantise_for(s, L,W.wq.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L,W.wk.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L,W.wv.type, s->h, c.d, T, &a, &have));
+    CK(gemv(s, L,W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
+    CK(gemv(s, L,W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
+    CK(gemv(s, L,W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
     float* kc = s->kc + (size_t)l * kv_layer;
     float* vc = s->vc + (size_t)l * kv_layer;
     CK(launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
@@ -190,24 +228,66 @@ det_status forward_chunk(det_session* s, int T, int pos0) {
     CK(launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
                         s->score_scratch));
     have = 0;
-    CK(quantise_for(s, W.wo.type, s->attn, qd, T, &a, &have));
-    CK(gemv(s,W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+    CK(quantise_for(s, L,W.wo.type, s->attn, qd, T, &a, &have));
+    CK(gemv(s, L,W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
     CK(launch_rmsnorm(L, s->x, W.ffn_norm, c.d, c.eps, T, s->h));
     have = 0;
-    CK(quantise_for(s, W.gate.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, W.up.type, s->h, c.d, T, &a, &have));
-    CK(gemv(s,W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
-    CK(gemv(s,W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+    CK(quantise_for(s, L,W.gate.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L,W.up.type, s->h, c.d, T, &a, &have));
+    CK(gemv(s, L,W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
+    CK(gemv(s, L,W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
     CK(launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T));
     have = 0;
-    CK(quantise_for(s, W.down.type, s->ff, c.dff, T, &a, &have));
-    CK(gemv(s,W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+    CK(quantise_for(s, L,W.down.type, s->ff, c.dff, T, &a, &have));
+    CK(gemv(s, L,W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
   }
   CK(launch_rmsnorm(L, s->x, m->output_norm, c.d, c.eps, T, s->h));
   DevActs a;
   int have = 0;
-  CK(quantise_for(s, m->output.type, s->h, c.d, T, &a, &have));
-  CK(gemv(s,m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
+  CK(quantise_for(s, L,m->output.type, s->h, c.d, T, &a, &have));
+  CK(gemv(s, L, m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
+  return DET_OK;
+}
+
+// H2D copies of the chunk's tokens and first position, then the forward
+det_status enqueue_forward(det_session* s, int T, uint64_t* launch_counter) {
+  CK(cudaMemcpyAsync(s->d_tokens, s->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, s->stream));
+  CK(cudaMemcpyAsync(s->d_pos, s->h_pos, 4, cudaMemcpyHostToDevice, s->stream));
+  return forward_chunk(s, T, launch_counter);
+}
+
+bool graphs_enabled() {
+  static const int off = [] {
+    const char* e = std::getenv("DETGPU_NO_GRAPHS");
+    return e && *e && *e != '0' ? 1 : 0;
+  }();
+  return !off && !g_profiling;
+}
+
+// Runs the chunk forward through a CUDA graph captured once per chunk size
+// (the kernels read pos0 from device memory, so one graph serves every chunk).
+det_status run_forward(det_session* s, int T) {
+  if (!graphs_enabled()) return enqueue_forward(s, T, &s->stats.launches);
+  if ((int)s->graphs.size() <= T) s->graphs.resize((size_t)T + 1);
+  det_session::Graph& gr = s->graphs[(size_t)T];
+  if (!gr.exec) {
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    uint64_t count = 0;
+    const det_status st = enqueue_forward(s, T, &count);
+    const cudaError_t ec = cudaStreamEndCapture(s->stream, &graph);
+    if (st) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    CK(ec);
+    const cudaError_t ei = cudaGraphInstantiate(&gr.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(ei);
+    gr.kernels = count;
+  }
+  CK(cudaGraphLaunch(gr.exec, s->stream));
+  s->stats.launches += gr.kernels;
   return DET_OK;
 }
 
@@ -279,10 +359,15 @@ det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, 
   if (!st) st = dalloc(s, &s->vc, kv);
   if (!st) st = dalloc(s, &s->rope_cos, (size_t)n_ctx * (c.rope_dim / 2));
   if (!st) st = dalloc(s, &s->rope_sin, (size_t)n_ctx * (c.rope_dim / 2));
-  if (!st && (size_t)(c.hd + n_ctx) * 4 > 160 * 1024) st = dalloc(s, &s->score_scratch, T * c.nh * (size_t)n_ctx);
+  if (!st) {
+    const size_t sf = attention_scratch_floats((int)T, c.nh, c.nkv, c.hd, (int)n_ctx);
+    if (sf) st = dalloc(s, &s->score_scratch, sf);
+  }
   if (!st) st = dalloc(s, &s->cdf_e, T * (size_t)m->vocab);
   if (!st) st = dalloc(s, &s->cdf_z, T);
   if (!st) st = dalloc(s, &s->d_tokens, T);
+  if (!st) st = dalloc(s, &s->d_pos, 1);
+  if (!st) st = halloc(s, &s->h_pos, 1);
   if (!st) st = dalloc(s, &s->d_rows, 2048);
   if (!st) st = dalloc(s, &s->d_syms, std::max<size_t>(T, 1024) * 4);
   if (!st) st = dalloc(s, &s->d_out, std::max<size_t>(T, 1024) * 4 * 3);
@@ -333,10 +418,10 @@ det_status det_forward(det_session* s, const uint32_t* tokens, uint32_t n, uint3
     if (tokens[i] >= (uint32_t)m->vocab || tokens[i] >= (uint32_t)m->tok_embd.rows) return DET_ERR_SHAPE;
   cudaSetDevice(m->device);
   std::memcpy(s->h_tokens, tokens, n * 4);
-  CK(cudaMemcpyAsync(s->d_tokens, s->h_tokens, n * 4, cudaMemcpyHostToDevice, s->stream));
-  s->stats.h2d_bytes += n * 4;
+  *s->h_pos = (int)pos0;
+  s->stats.h2d_bytes += n * 4 + 4;
   CK(cudaEventRecord(s->ev[0], s->stream));
-  det_status st = forward_chunk(s, (int)n, (int)pos0);
+  det_status st = run_forward(s, (int)n);
   if (st) return st;
   CK(cudaEventRecord(s->ev[1], s->stream));
   s->last_n = (int)n;
@@ -487,6 +572,10 @@ det_status det_session_stats(det_session* s, det_stats* out, int reset) {
 det_status det_model_stats(det_model* m, det_stats* out, int reset) {
   if (!m || !out) return DET_ERR_INVALID_ARGUMENT;
   *out = m->agg;
+  if (m->cached) {  // include the live cached session
+    add_stats(out, m->cached->stats);
+    if (reset) m->cached->stats = det_stats{};
+  }
   if (reset) m->agg = det_stats{};
   return DET_OK;
 }
