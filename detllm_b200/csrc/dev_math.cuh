@@ -370,6 +370,20 @@ DI float finish8(const float a[8]) {
   return fadd(fadd(fadd(a[0], a[1]), fadd(a[2], a[3])), fadd(fadd(a[4], a[5]), fadd(a[6], a[7])));
 }
 
+// ---- Q8A activation layout ---------------------------------------------------
+// Quantised activations of T positions x K elements are stored block-major
+// in groups of 64 positions: for group G and block b, 64 consecutive 32-byte
+// position blocks, then the next block.  Within a position block the two
+// 16-byte halves are swapped for positions with bit 2 set, which makes the
+// tensor-core B-fragment reads from shared memory bank-conflict free.  One
+// (group, block) slab is 2 KiB of quants and 256 B of f32 scales, so a GEMM
+// stage is a few contiguous bulk copies.
+constexpr int Q8A_GROUP = 64;
+DI size_t q8a_slot(int nb, int t, int b) { return ((size_t)(t >> 6) * nb + b) * Q8A_GROUP + (t & 63); }
+DI int q8a_swz(int t) { return ((t >> 2) & 1) << 4; }
+// byte of element i (0..31) of block b of position t
+DI size_t q8a_elem(int nb, int t, int b, int i) { return q8a_slot(nb, t, b) * 32 + (size_t)(i ^ q8a_swz(t)); }
+
 // Exact int32 -> f32 for |v| < 2^22 via the 1.5*2^23 bias: the bits of
 // (0x4B400000 + v) read as f32 equal 12582912 + v exactly.
 DI float exact_small_int_to_f32(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }

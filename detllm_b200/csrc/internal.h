@@ -19,6 +19,7 @@ enum : uint32_t {
   ERRF_CDF_TOTAL = 4u,        // CdfError::TotalTooLarge
   ERRF_SHAPE = 8u,            // ModelError::Shape (bad token id etc.)
   ERRF_DECODE = 16u,          // value outside the decoder distribution
+  ERRF_TIMEOUT = 32u,         // a bounded device-side wait gave up
 };
 
 // A weight matrix in device memory.  Layouts (rows x cols, nb blocks/row):
@@ -45,8 +46,8 @@ struct DevMatrix {
 // Quantised activations for `T` positions of length K (row stride K).
 struct DevActs {
   const float* x = nullptr;    // f32 [T][K]
-  const float* qa_d = nullptr; // Q8A scales [T][K/32]
-  const int8_t* qa_q = nullptr;// Q8A quants [T][K]
+  const float* qa_d = nullptr; // Q8A scales, q8a_slot order (dev_math.cuh)
+  const int8_t* qa_q = nullptr;// Q8A quants, q8a_elem order, 64-position groups
   const float* qk_d = nullptr; // Q8_K scales [T][K/256]
   const int8_t* qk_q = nullptr;// Q8_K quants [T][K]
 };

@@ -208,12 +208,14 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 }
 
 // ---- Q8A quantiser: try_quantize_q8a_block (det-quant lib.rs:111-137) ------
-// one warp per 32-element block; amax by shuffle (max is order-free)
-__global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, float* __restrict__ qd,
+// one warp per 32-element block; amax by shuffle (max is order-free); the
+// output goes to the Q8A layout (dev_math.cuh)
+__global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, int nbk, float* __restrict__ qd,
                                  int8_t* __restrict__ qq, uint32_t* err) {
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= nblocks) return;
   const int l = threadIdx.x & 31;
+  const int t = b / nbk, kb = b - t * nbk;
   const float v = x[(size_t)b * 32 + l];
   if (!finite(v)) flag(err, ERRF_NONFINITE);
   float amax = fabsf(v);
@@ -226,8 +228,8 @@ __global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, float
     int r = v < 0.0f ? __float2int_rz(fsub(s, 0.5f)) : __float2int_rz(fadd(s, 0.5f));
     q = max(-127, min(127, r));
   }
-  qq[(size_t)b * 32 + l] = (int8_t)q;
-  if (l == 0) qd[b] = d;
+  qq[q8a_elem(nbk, t, kb, l)] = (int8_t)q;
+  if (l == 0) qd[q8a_slot(nbk, t, kb)] = d;
 }
 
 // ---- Q8_K quantiser: try_quantize_q8k_block (det-quant lib.rs:139-172) ----
@@ -290,8 +292,7 @@ DI float dot_row(const DevMatrix& m, const DevActs& a, int r, int t) {
     }
     case GT_Q4_K: {  // dot_q4_k_q8a (det-quant lib.rs:281-315): one f32 chain
       const uint8_t* w = (const uint8_t*)m.q + (size_t)r * m.nb * 144;
-      const int8_t* q = a.qa_q + (size_t)t * K;
-      const float* ad = a.qa_d + (size_t)t * (K / 32);
+      const int nbk = K / 32;
       float sum = 0.0f;
       for (int b = 0; b < m.nb; b++) {
         const uint8_t* blk = w + (size_t)b * 144;
@@ -301,13 +302,15 @@ DI float dot_row(const DevMatrix& m, const DevActs& a, int r, int t) {
           int sc, mn;
           q4k_scale_min(blk + 4, sub, sc, mn);
           const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-          const float a_d = ad[b * 8 + sub];
+          const int kb = b * 8 + sub;
+          const float a_d = a.qa_d[q8a_slot(nbk, t, kb)];
           const uint8_t* qs = blk + 16 + (sub >> 1) * 32;
-          const int8_t* aq = q + b * 256 + sub * 32;
+          const int8_t* aq = a.qa_q + q8a_slot(nbk, t, kb) * 32;
+          const int swz = q8a_swz(t);
           for (int i = 0; i < 32; i++) {
             const int qv = (sub & 1) ? (qs[i] >> 4) : (qs[i] & 0x0f);
             const float weight = fsub(fmul(dsc, (float)qv), dmn);
-            const float act = fmul(a_d, (float)aq[i]);
+            const float act = fmul(a_d, (float)aq[i ^ swz]);
             sum = fadd(sum, fmul(weight, act));
           }
         }
@@ -843,7 +846,7 @@ cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int 
 
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
   const int nb = T * (K / 32);
-  quant_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, qd, qq, L.err);
+  quant_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, K / 32, qd, qq, L.err);
   return post(L);
 }
 

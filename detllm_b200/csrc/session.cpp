@@ -134,6 +134,7 @@ det_status take_error(det_session* s, bool cdf) {
   if (cdf && (f & ERRF_CDF_NONFINITE)) return DET_ERR_CDF_NONFINITE_LOGIT;
   if (cdf && (f & ERRF_CDF_TOTAL)) return DET_ERR_CDF_TOTAL_TOO_LARGE;
   if (f & ERRF_DECODE) return DET_ERR_DECODE;
+  if (f & ERRF_TIMEOUT) return DET_ERR_TIMEOUT;
   if (f) return DET_ERR_CUDA;
   return DET_OK;
 }
@@ -351,8 +352,14 @@ det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, 
   if (!st) st = dalloc(s, &s->up, T * c.dff);
   if (!st) st = dalloc(s, &s->ff, T * c.dff);
   if (!st) st = dalloc(s, &s->logits, T * (size_t)m->vocab);
-  if (!st) st = dalloc(s, &s->qa_d, T * (kmax / 32 + 1));
-  if (!st) st = dalloc(s, &s->qa_q, T * kmax + 64);
+  // Q8A buffers cover whole 64-position groups; the padding positions stay
+  // zero so the chunk GEMM may read (and discard) them.
+  const size_t Tg = (T + 63) / 64 * 64;
+  if (!st) st = dalloc(s, &s->qa_d, Tg * (kmax / 32));
+  if (!st) st = dalloc(s, &s->qa_q, Tg * kmax);
+  if (!st && (cudaMemset(s->qa_d, 0, Tg * (kmax / 32) * sizeof(float)) != cudaSuccess ||
+              cudaMemset(s->qa_q, 0, Tg * kmax) != cudaSuccess))
+    st = DET_ERR_CUDA;
   if (!st) st = dalloc(s, &s->qk_d, T * (kmax / 256 + 1));
   if (!st) st = dalloc(s, &s->qk_q, T * kmax + 64);
   if (!st) st = dalloc(s, &s->kc, kv);
