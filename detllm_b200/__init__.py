@@ -100,6 +100,7 @@ def lib():
             "det_device_expf": (I, [I, P, P, SZ]),
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
             "det_set_profiling": (I, [I]),
+            "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -20,6 +20,7 @@ enum : uint32_t {
   ERRF_SHAPE = 8u,            // ModelError::Shape (bad token id etc.)
   ERRF_DECODE = 16u,          // value outside the decoder distribution
   ERRF_TIMEOUT = 32u,         // a bounded device-side wait gave up
+  ERRF_SYMBOL = 64u,          // CdfError::SymbolOutOfRange found on the device
 };
 
 // A weight matrix in device memory.  Layouts (rows x cols, nb blocks/row):

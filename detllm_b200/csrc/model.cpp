@@ -522,6 +522,7 @@ const char* det_status_string(det_status s) {
     case DET_ERR_DEVICE_OOM: return "device out of memory";
     case DET_ERR_TIMEOUT: return "timed out";
     case DET_ERR_COLLECTIVE: return "collective failed";
+    case DET_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch array";
     default: return "unknown status";
   }
 }

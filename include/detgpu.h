@@ -74,7 +74,8 @@ enum {
     DET_ERR_NO_DEVICE = 65,
     DET_ERR_DEVICE_OOM = 66,
     DET_ERR_TIMEOUT = 67,
-    DET_ERR_COLLECTIVE = 68
+    DET_ERR_COLLECTIVE = 68,
+    DET_ERR_SCRATCH_LIMIT = 69 /* request larger than a fixed scratch array */
 };
 
 /* RoPE pairing (det-model lib.rs:40-44) */
@@ -194,6 +195,27 @@ det_status det_session_stats(det_session* s, det_stats* out, int reset);
 det_status det_model_stats(det_model* model, det_stats* out, int reset);
 /* per-launch GEMV/GEMM timing (adds two event records per launch) */
 det_status det_set_profiling(int enable);
+
+/* ---- symbol ranges without allocation (no counterpart in the reference) --
+ * For callers that cannot allocate device memory inside a call: code running
+ * while a CUDA graph is captured, engines that fix their memory budget at
+ * start-up, runtimes whose allocator is not cudaMalloc.  Same result as
+ * det_symbol_ranges with rows == NULL, but every buffer is the caller's
+ * device memory: logits (n x vocab f32, row-major), symbols (n u32) and out
+ * (n det_symbol_range).  Runs on the calling thread's current device, on
+ * `stream` (a cudaStream_t; NULL = the legacy default stream), and waits for
+ * that stream before it returns the status.
+ * Working memory is one fixed array in device memory that every GPU loading
+ * this library holds until exit: DET_NOALLOC_MAX_FLOATS floats of exp values
+ * plus per-row words, about 8 MiB.  Requests with n > DET_NOALLOC_MAX_ROWS or
+ * n * vocab > DET_NOALLOC_MAX_FLOATS return DET_ERR_SCRATCH_LIMIT.  The first
+ * call on a device looks up the array's device address; make that first call
+ * before any stream capture.  All calls on a device share the array: calls
+ * whose work overlaps on the GPU race and must be ordered by the caller. */
+#define DET_NOALLOC_MAX_ROWS 1024u
+#define DET_NOALLOC_MAX_FLOATS (1u << 21)
+det_status det_symbol_ranges_noalloc(const float* logits, uint32_t n, uint32_t vocab, const uint32_t* symbols,
+                                     int byte_escapes, det_symbol_range* out, void* stream);
 
 #ifdef __cplusplus
 }
