@@ -1,0 +1,381 @@
+// attention.cu -- causal GQA attention for a chunk of T positions, exact to
+// the reference's f32 arithmetic, in three tiled kernels.
+//
+// Reference: attention_one_head and its helpers (crates/det-model/src/
+// lib.rs:2298-2418).  For a query at position p (score_len = p + 1):
+//   s_j  = dot_f32_ref(q, k_j) * scale              (8 interleaved lanes, then
+//                                                    the fixed combine tree)
+//   e_j  = exp_f32(max(s_j - max_j s_j, -88)),  z = sum_f32_ref(e)
+//   p_j  = e_j / z
+//   o[d] = sum over j = 0, 1, ... of p_j * v_j[d]   (one ordered chain per d)
+// and score_len == 1 copies v_0.  No step may be reassociated, so every
+// product and sum here is a separately rounded f32 operation on the CUDA
+// cores; what the kernels change is only which thread does which chain and
+// how operands reach it:
+//
+//   attn_scores   one CTA per (64-key tile, block of queries, KV head):
+//                 the 64 query-head rows of a GQA group block share each K
+//                 tile in shared memory; a thread owns a 4 x 4 tile of dots
+//                 and runs their eight lane chains one lane at a time
+//                 (lane-major operand layout), combining finished lanes in
+//                 the reference's tree order, so 16 dots need ~64 registers.
+//   attn_softmax  one warp per (position, head) row: max, e_j, the eight
+//                 ordered z chains, p_j = e_j / z, written back in place.
+//   attn_pv       one CTA per (block of query-head rows, KV head): P and V
+//                 tiles staged in shared memory, a thread owns 4 rows x 4
+//                 dims = 16 independent ordered chains over j.
+//
+// Rows of different queries in one CTA have different score lengths; the
+// PV chains of shorter rows see p = 0 for the extra keys, and adding
+// 0 * v (v finite, the chain never -0) leaves an f32 sum unchanged.
+#include <cuda_runtime.h>
+
+#include "dev_math.cuh"
+#include "internal.h"
+
+namespace det {
+namespace {
+
+DI unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+// two separately rounded products (packed IEEE multiply)
+DI float2 mul2(float a0, float a1, float b0, float b1) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a0, a1)), "l"(pk2(b0, b1)));
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+  return o;
+}
+
+// ---- scores -------------------------------------------------------------------
+constexpr int QK_ROWS = 64;  // query-head rows per CTA
+constexpr int QK_KEYS = 64;  // keys per CTA
+constexpr int QK_THREADS = 256;
+
+// lane-major position of element d within a row of HD floats: the HD/8
+// elements of lane l (d = 8i + l) are contiguous
+template <int HD>
+DI int lm(int d) {
+  return (d & 7) * (HD / 8) + (d >> 3);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __restrict__ q,
+                                                                 const float* __restrict__ kc, const int* pos0p,
+                                                                 int T, int n_head, int gsz, int qb, int n_ctx,
+                                                                 float scale, float* __restrict__ S, uint32_t* err) {
+  constexpr int RS = HD + 4;  // padded row stride (floats): conflict-free strided rows
+  constexpr int PER = HD / 8; // elements per lane chain
+  extern __shared__ float4 qk_smem[];
+  float* qs = reinterpret_cast<float*>(qk_smem);  // [QK_ROWS][RS]
+  float* ks = qs + QK_ROWS * RS;                  // [QK_KEYS][RS]
+  const int pos0 = *pos0p;
+  const int j0 = blockIdx.x * QK_KEYS;
+  const int t0 = blockIdx.y * qb;
+  const int kvh = blockIdx.z;
+  const int tq = min(qb, T - t0);  // queries in this block
+  const int jmax = pos0 + t0 + tq;  // longest score row of the block
+  if (j0 >= jmax) return;
+  const int tid = threadIdx.x;
+  const int rows = tq * gsz;
+
+  // stage Q rows (m = qi * gsz + hh) and K rows j0.. in lane-major order
+  for (int i = tid; i < QK_ROWS * (HD / 4); i += QK_THREADS) {
+    const int m = i / (HD / 4), d4 = (i - m * (HD / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (m < rows) {
+      const int qi = m / gsz, hh = m - qi * gsz;
+      v = *reinterpret_cast<const float4*>(q + ((size_t)(t0 + qi) * n_head + kvh * gsz + hh) * HD + d4);
+      if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
+    }
+    float* r = qs + m * RS;
+    r[lm<HD>(d4)] = v.x;
+    r[lm<HD>(d4 + 1)] = v.y;
+    r[lm<HD>(d4 + 2)] = v.z;
+    r[lm<HD>(d4 + 3)] = v.w;
+  }
+  for (int i = tid; i < QK_KEYS * (HD / 4); i += QK_THREADS) {
+    const int jj = i / (HD / 4), d4 = (i - jj * (HD / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j0 + jj < jmax) {
+      v = *reinterpret_cast<const float4*>(kc + ((size_t)kvh * n_ctx + j0 + jj) * HD + d4);
+      if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
+    }
+    float* r = ks + jj * RS;
+    r[lm<HD>(d4)] = v.x;
+    r[lm<HD>(d4 + 1)] = v.y;
+    r[lm<HD>(d4 + 2)] = v.z;
+    r[lm<HD>(d4 + 3)] = v.w;
+  }
+  __syncthreads();
+
+  // thread tile: rows mt + 16r, keys jt + 16c
+  const int warp = tid >> 5, lane = tid & 31;
+  const int mt = 2 * warp + (lane >> 4), jt = lane & 15;
+  float t01[4][4], t03[4][4], t45[4][4], a[4][4], b[4][4];
+
+  // one lane chain for the 16 dots: acc[r][c] = sum over i of q[8i+l] k[8i+l]
+  auto chain = [&](int l, float (&acc)[4][4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) acc[r][c] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; i += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) qv[r] = *reinterpret_cast<const float4*>(qs + (mt + 16 * r) * RS + l * PER + i);
+#pragma unroll
+      for (int c = 0; c < 4; c++) kv[c] = *reinterpret_cast<const float4*>(ks + (jt + 16 * c) * RS + l * PER + i);
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float2 p01 = mul2(qv[r].x, qv[r].y, kv[c].x, kv[c].y);
+          const float2 p23 = mul2(qv[r].z, qv[r].w, kv[c].z, kv[c].w);
+          float s = acc[r][c];
+          s = fadd(s, p01.x);
+          s = fadd(s, p01.y);
+          s = fadd(s, p23.x);
+          s = fadd(s, p23.y);
+          acc[r][c] = s;
+        }
+    }
+  };
+  auto add_into = [&](float (&dst)[4][4], const float (&x)[4][4], const float (&y)[4][4]) {
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) dst[r][c] = fadd(x[r][c], y[r][c]);
+  };
+  // finish_8lane: ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 + l7))
+  chain(0, a);
+  chain(1, b);
+  add_into(t01, a, b);
+  chain(2, a);
+  chain(3, b);
+  add_into(a, a, b);
+  add_into(t03, t01, a);
+  chain(4, a);
+  chain(5, b);
+  add_into(t45, a, b);
+  chain(6, a);
+  chain(7, b);
+  add_into(a, a, b);
+  add_into(a, t45, a);
+  add_into(a, t03, a);
+
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int m = mt + 16 * r;
+    if (m >= rows) continue;
+    const int qi = m / gsz, hh = m - qi * gsz;
+    const int t = t0 + qi;
+    const int len = pos0 + t + 1;
+    if (len == 1) continue;  // score_len == 1 copies v_0 (no scores)
+    float* srow = S + ((size_t)t * n_head + kvh * gsz + hh) * n_ctx;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int j = j0 + jt + 16 * c;
+      if (j < len) {
+        const float s = fmul(a[r][c], scale);
+        if (!finite(s)) atomicOr(err, ERRF_NONFINITE);
+        srow[j] = s;
+      }
+    }
+  }
+}
+
+// ---- softmax: one warp per row, in place ---------------------------------------
+constexpr int SM_ROWS_PER_CTA = 4;
+
+__global__ void __launch_bounds__(SM_ROWS_PER_CTA * 32) attn_softmax_kernel(float* __restrict__ S, const int* pos0p,
+                                                                            int T, int n_head, int n_ctx,
+                                                                            uint32_t* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * SM_ROWS_PER_CTA + warp;
+  if (row >= T * n_head) return;
+  const int t = row / n_head;
+  const int len = *pos0p + t + 1;
+  if (len == 1) return;
+  float* s = S + (size_t)row * n_ctx;
+  float mx = -INFINITY;
+  for (int j = lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int j = lane; j < len; j += 32) {
+    const float d = fsub(s[j], mx);
+    s[j] = expf_det(d > -88.0f ? d : -88.0f);
+  }
+  __syncwarp();
+  // sum_f32_ref: lane l < 8 runs the ordered chain over j = l, l + 8, ...
+  float acc = 0.0f;
+  if (lane < 8) {
+    int j = lane;
+    for (; j + 56 < len; j += 64) {
+      float e[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) e[k] = s[j + 8 * k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+    }
+    for (; j < len; j += 8) acc = fadd(acc, s[j]);
+  }
+  float l8[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) l8[k] = __shfl_sync(0xffffffffu, acc, k);
+  const float z = finish8(l8);
+  if (!finite(z) || z == 0.0f) {
+    if (lane == 0) atomicOr(err, ERRF_NONFINITE);
+    return;
+  }
+  for (int j = lane; j < len; j += 32) {
+    const float p = fdiv(s[j], z);
+    if (!finite(p)) atomicOr(err, ERRF_NONFINITE);
+    s[j] = p;
+  }
+}
+
+// ---- P x V ----------------------------------------------------------------------
+constexpr int PV_ROWS = 32;  // query-head rows per CTA
+constexpr int PV_KEYS = 32;  // keys per staged tile
+
+template <int HD>
+__global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const float* __restrict__ P,
+                                                                           const float* __restrict__ vc,
+                                                                           const int* pos0p, int T, int n_head,
+                                                                           int gsz, int qb, int n_ctx,
+                                                                           float* __restrict__ out, uint32_t* err) {
+  constexpr int NT = (PV_ROWS / 4) * (HD / 4);
+  __shared__ __align__(16) float ps[PV_KEYS][PV_ROWS + 4];  // p, transposed: 4 rows per 16 bytes
+  __shared__ __align__(16) float vs[PV_KEYS][HD];
+  const int pos0 = *pos0p;
+  const int t0 = blockIdx.x * qb;
+  const int kvh = blockIdx.y;
+  const int tq = min(qb, T - t0);
+  const int rows = tq * gsz;
+  const int jmax = pos0 + t0 + tq;
+  const int tid = threadIdx.x;
+  const int mt = tid / (HD / 4), dt = tid - mt * (HD / 4);
+  const float* vb = vc + (size_t)kvh * n_ctx * HD;
+
+  float o[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) o[r][c] = 0.0f;
+
+  for (int jc = 0; jc < jmax; jc += PV_KEYS) {
+    __syncthreads();  // previous tile consumed
+    // P tile: row m, keys jc.. (0 past the row's score length)
+    for (int i = tid; i < PV_ROWS * PV_KEYS; i += NT) {
+      const int m = i / PV_KEYS, jj = i - m * PV_KEYS;
+      float p = 0.0f;
+      if (m < rows) {
+        const int qi = m / gsz, hh = m - qi * gsz;
+        const int t = t0 + qi;
+        if (jc + jj < pos0 + t + 1) p = P[((size_t)t * n_head + kvh * gsz + hh) * n_ctx + jc + jj];
+      }
+      ps[jj][m] = p;
+    }
+    // V tile: rows jc.. (contiguous)
+    for (int i = tid; i < PV_KEYS * (HD / 4); i += NT) {
+      const int jj = i / (HD / 4), d4 = (i - jj * (HD / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (jc + jj < jmax) {
+        v = *reinterpret_cast<const float4*>(vb + (size_t)(jc + jj) * HD + d4);
+        if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
+      }
+      *reinterpret_cast<float4*>(&vs[jj][d4]) = v;
+    }
+    __syncthreads();
+    const int cnt = min(PV_KEYS, jmax - jc);
+#pragma unroll 4
+    for (int jj = 0; jj < cnt; jj++) {
+      const float4 p4 = *reinterpret_cast<const float4*>(&ps[jj][mt * 4]);
+      const float4 v4 = *reinterpret_cast<const float4*>(&vs[jj][dt * 4]);
+      const float pr[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const float2 a = mul2(pr[r], pr[r], v4.x, v4.y);
+        const float2 b = mul2(pr[r], pr[r], v4.z, v4.w);
+        o[r][0] = fadd(o[r][0], a.x);
+        o[r][1] = fadd(o[r][1], a.y);
+        o[r][2] = fadd(o[r][2], b.x);
+        o[r][3] = fadd(o[r][3], b.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int m = mt * 4 + r;
+    if (m >= rows) continue;
+    const int qi = m / gsz, hh = m - qi * gsz;
+    const int t = t0 + qi;
+    float* ob = out + ((size_t)t * n_head + kvh * gsz + hh) * HD + dt * 4;
+    float4 v;
+    if (pos0 + t == 0) {  // score_len == 1 copies v_0 (lib.rs:2319-2322)
+      v = *reinterpret_cast<const float4*>(vb + dt * 4);
+    } else {
+      v = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
+      if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
+    }
+    *reinterpret_cast<float4*>(ob) = v;
+  }
+}
+
+template <int HD>
+constexpr int qk_smem_bytes() {
+  return (QK_ROWS + QK_KEYS) * (HD + 4) * (int)sizeof(float);
+}
+
+template <int HD>
+cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const float* vc, int T, const int* pos0,
+                         int n_head, int n_head_kv, int n_ctx, float scale, float* out, float* S) {
+  const int gsz = n_head / n_head_kv;
+  const int qb = QK_ROWS / gsz;
+  constexpr int smem = qk_smem_bytes<HD>();
+  static unsigned long long attr_set = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && (dev >= 64 || !(attr_set >> dev & 1ull))) {
+    cudaError_t e = cudaFuncSetAttribute(attn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) attr_set |= 1ull << dev;
+  }
+  dim3 g1((n_ctx + QK_KEYS - 1) / QK_KEYS, (T + qb - 1) / qb, n_head_kv);
+  attn_scores_kernel<HD><<<g1, QK_THREADS, smem, L.stream>>>(q, kc, pos0, T, n_head, gsz, qb, n_ctx, scale, S,
+                                                             L.err);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int rows = T * n_head;
+  attn_softmax_kernel<<<(rows + SM_ROWS_PER_CTA - 1) / SM_ROWS_PER_CTA, SM_ROWS_PER_CTA * 32, 0, L.stream>>>(
+      S, pos0, T, n_head, n_ctx, L.err);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int qb2 = PV_ROWS / gsz;
+  dim3 g3((T + qb2 - 1) / qb2, n_head_kv);
+  attn_pv_kernel<HD><<<g3, (PV_ROWS / 4) * (HD / 4), 0, L.stream>>>(S, vc, pos0, T, n_head, gsz, qb2, n_ctx, out,
+                                                                    L.err);
+  if (L.launches) *L.launches += 3;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool attention_tiled_supported(int n_head, int n_head_kv, int head_dim) {
+  if (n_head_kv <= 0 || n_head % n_head_kv) return false;
+  const int gsz = n_head / n_head_kv;
+  return (head_dim == 64 || head_dim == 128) && gsz <= PV_ROWS;
+}
+
+cudaError_t launch_attention_tiled(const Launch& L, const float* q, const float* kc, const float* vc, int T,
+                                   const int* pos0, int n_head, int n_head_kv, int head_dim, int n_ctx, float scale,
+                                   float* out, float* S) {
+  if (head_dim == 64) return launch_tiled<64>(L, q, kc, vc, T, pos0, n_head, n_head_kv, n_ctx, scale, out, S);
+  return launch_tiled<128>(L, q, kc, vc, T, pos0, n_head, n_head_kv, n_ctx, scale, out, S);
+}
+
+}  // namespace det

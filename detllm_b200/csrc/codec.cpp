@@ -24,7 +24,7 @@ using namespace det;
 
 namespace {
 
-constexpr uint32_t kChunk = 64;
+constexpr uint32_t kChunk = 256;
 constexpr uint32_t kEscapes = 256;
 
 // next_window_start (det-cli main.rs:772-778)

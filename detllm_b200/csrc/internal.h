@@ -77,6 +77,11 @@ cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* 
 cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, const int* pos0,
                              int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
                              float* score_scratch);
+// tiled three-kernel attention (attention.cu) for head_dim 64 / 128
+bool attention_tiled_supported(int n_head, int n_head_kv, int head_dim);
+cudaError_t launch_attention_tiled(const Launch& L, const float* q, const float* kc, const float* vc, int T,
+                                   const int* pos0, int n_head, int n_head_kv, int head_dim, int n_ctx, float scale,
+                                   float* out, float* S);
 // floats of global score scratch launch_attention needs (0: scores stay in smem)
 size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx);
 cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T);

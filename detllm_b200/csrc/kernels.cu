@@ -893,6 +893,7 @@ bool gqa_plan(int n_head, int n_head_kv, int hd, int n_ctx, size_t* smem, int* s
 }  // namespace
 
 size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx) {
+  if (attention_tiled_supported(n_head, n_head_kv, hd)) return (size_t)T * n_head * n_ctx;
   size_t smem;
   int in_smem;
   if (gqa_plan(n_head, n_head_kv, hd, n_ctx, &smem, &in_smem)) return in_smem ? 0 : (size_t)T * n_head * n_ctx;
@@ -902,6 +903,9 @@ size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_
 cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, const float* vc, int T, const int* pos0,
                              int n_head, int n_head_kv, int head_dim, int n_ctx, float scale, float* out,
                              float* score_scratch) {
+  if (attention_tiled_supported(n_head, n_head_kv, head_dim))
+    return launch_attention_tiled(L, q, kc, vc, T, pos0, n_head, n_head_kv, head_dim, n_ctx, scale, out,
+                                  score_scratch);
   size_t gsmem;
   int gscores;
   if (gqa_plan(n_head, n_head_kv, head_dim, n_ctx, &gsmem, &gscores)) {

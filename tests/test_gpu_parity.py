@@ -33,9 +33,39 @@ SPECS = {
 }
 
 
+# Longer windows: several 64-key tiles, several query blocks per chunk,
+# GQA groups of 8 and 7 (a 63-row block) and head_dim 128.
+LONG_SPECS = {
+    "hd64_gqa8": S.ModelSpec(n_layer=2, d=512, d_ff=256, n_head=8, n_head_kv=1, vocab=512, ctx=320, seed=21),
+    "hd64_gqa7_qwen2": S.ModelSpec(arch="qwen2", n_layer=1, d=448, d_ff=256, n_head=7, n_head_kv=1, vocab=400,
+                                   ctx=320, qkv_bias=True, rope_base=1e6, seed=22),
+    "hd128_gqa2": S.ModelSpec(n_layer=1, d=256, d_ff=256, n_head=2, n_head_kv=1, vocab=512, ctx=320,
+                              t_attn=S.GT_Q4_0, seed=23),
+}
+
+
 @pytest.fixture(scope="module")
 def models():
     return {k: S.build_gguf(v) for k, v in SPECS.items()}
+
+
+@pytest.fixture(scope="module")
+def long_models(oracle):
+    out = {}
+    for k, spec in LONG_SPECS.items():
+        g = S.build_gguf(spec)
+        toks = S.zipf_tokens(300, spec.vocab, seed=len(k))
+        out[k] = (g, toks, oracle.Model(g).logits(toks))
+    return out
+
+
+@pytest.mark.parametrize("name", list(LONG_SPECS))
+@pytest.mark.parametrize("chunk", [37, 128, 300])
+def test_long_window_logits_bit_exact(D, long_models, name, chunk):
+    g, toks, want = long_models[name]
+    got = D.Model(g).logits_for_tokens(toks, chunk=chunk)
+    diff = np.nonzero(bits(got) != bits(want))
+    assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
 
 
 def bits(a):
