@@ -16,7 +16,9 @@
 // and 4t+16..4t+19 of the block (the PTX m16n8k32 .s8 A-fragment map), and
 // scale word g = f16 d[g] | f16 d[g+8] << 16.  A record is exactly
 // 16 rows x (34 or 18) bytes, the GGUF size, so HBM bytes per weight are
-// unchanged, and a tile's records are contiguous.
+// unchanged, and a tile's records are contiguous.  Matrices that read the
+// same activations (q/k/v, gate/up) are stored back to back as one matrix
+// and run as one launch whose rows map to several outputs (OutSegs).
 //
 // Activations use the Q8A layout of dev_math.cuh (64-position groups,
 // block-major, 16-byte-half swizzle).
@@ -25,13 +27,13 @@
 // block's |isum| <= 32*127*127) the MMA result read as f32 is
 // 12582912 + isum exactly, so one FADD recovers (f32)isum.
 //
-// Chunk kernel (T > 16 positions): a CTA owns one 16-row tile and one group
-// of 64 positions (4 warps x 16 positions).  Each pipeline stage is SB
-// blocks: SB weight records, the SB (group, block) activation slabs and their
-// scales -- three contiguous ranges moved by TMA bulk copies
-// (cp.async.bulk) that one thread issues, completing on an mbarrier.  Every
-// mbarrier wait is bounded (globaltimer); on timeout the kernel flags
-// ERRF_TIMEOUT and stops issuing work instead of spinning.
+// Chunk kernel (T > 16 positions): a CTA owns two 16-row tiles and one group
+// of 64 positions; each of its 4 warps owns 16 rows x 32 positions, so one
+// A fragment feeds four MMAs.  Each pipeline stage is SB blocks: the two
+// tiles' SB weight records, the SB (group, block) activation slabs and their
+// scales -- contiguous ranges moved by TMA bulk copies (cp.async.bulk) that
+// one thread issues, completing on an mbarrier.  Every mbarrier wait is
+// bounded (globaltimer); on timeout the kernel flags ERRF_TIMEOUT and stops.
 #include <cuda_runtime.h>
 
 #include "dev_math.cuh"
@@ -109,17 +111,55 @@ struct Rec<GT_Q4_0> {
 DI float lo_half(uint32_t w) { return f16_bits_to_f32((uint16_t)(w & 0xffffu)); }
 DI float hi_half(uint32_t w) { return f16_bits_to_f32((uint16_t)(w >> 16)); }
 
-DI void store_out(float v, int r, int p, float* out, int out_ld, int epi, const float* bias, uint32_t* err) {
+// The output segment that holds matrix row `row` (segments are whole tiles,
+// except that the last one may end inside its last tile).
+struct SegView {
+  float* out;
+  const float* bias;
+  int ld, epi, row0, rows;
+};
+DI SegView seg_for(const OutSegs& o, int row) {
+  SegView v{o.s[0].out, o.s[0].bias, o.s[0].ld, o.s[0].epi, 0, o.s[0].rows};
+  int base = o.s[0].rows;
+#pragma unroll
+  for (int k = 1; k < kMaxOutSegs; k++) {
+    if (k < o.n && row >= base) v = SegView{o.s[k].out, o.s[k].bias, o.s[k].ld, o.s[k].epi, base, o.s[k].rows};
+    base += o.s[k].rows;
+  }
+  return v;
+}
+
+DI void store_out(float v, int lr, int p, const SegView& sg, uint32_t* err) {
   if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  float* dst = out + (size_t)p * out_ld + r;
-  if (epi == EPI_BIAS) {
-    v = fadd(v, bias[r]);
+  float* dst = sg.out + (size_t)p * sg.ld + lr;
+  if (sg.epi == EPI_BIAS) {
+    v = fadd(v, sg.bias[lr]);
     if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  } else if (epi == EPI_RESIDUAL) {
+  } else if (sg.epi == EPI_RESIDUAL) {
     v = fadd(*dst, v);
     if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
   }
   *dst = v;
+}
+
+// acc[j] holds rows (g, g+8) x positions (pbase + 8j + 2tg, +1)
+template <int NJ>
+DI void store_tile(const float2 (&acc)[NJ][2], int tile, int pbase, int T, const OutSegs& o, int g, int tg,
+                   uint32_t* err) {
+  const SegView sg = seg_for(o, tile * 16);
+  const int r0 = tile * 16 - sg.row0 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int pa = pbase + 8 * j + 2 * tg, pb = pa + 1;
+    if (r0 < sg.rows) {
+      if (pa < T) store_out(acc[j][0].x, r0, pa, sg, err);
+      if (pb < T) store_out(acc[j][0].y, r0, pb, sg, err);
+    }
+    if (r1 < sg.rows) {
+      if (pa < T) store_out(acc[j][1].x, r1, pa, sg, err);
+      if (pb < T) store_out(acc[j][1].y, r1, pb, sg, err);
+    }
+  }
 }
 
 // One n8 tile: B fragments of positions (pos .. pos+7) of block slab `ab`
@@ -141,16 +181,27 @@ DI void n8_step(const int (&a)[4], float2 dlo, float2 dhi, const uint8_t* ab, co
   fold2(acc[1], dhi, adv, i23);
 }
 
+// A fragment + scales of one record, then NJ n8 tiles starting at `pos`
+template <int QT, int NJ>
+DI void block_step(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg,
+                   float2 (&acc)[NJ][2]) {
+  int a[4];
+  Rec<QT>::frag(r, lane, a);
+  const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
+  const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
+#pragma unroll
+  for (int j = 0; j < NJ; j++) n8_step(a, dlo, dhi, ab, sb, pos + 8 * j, g, tg, acc[j]);
+}
+
 // ---- small-T kernel (decode and short chunks): 4 warps per 16-row tile,
 // 16 positions per warp, operands straight from global/L1 ---------------------
 constexpr int SM_WARPS = 4;
 
 template <int QT>
-__global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t* __restrict__ W, int rows, int nb,
+__global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t* __restrict__ W, int nb,
                                                                    const int8_t* __restrict__ aq,
                                                                    const float* __restrict__ ad, int T,
-                                                                   float* __restrict__ out, int out_ld, int epi,
-                                                                   const float* __restrict__ bias, uint32_t* err) {
+                                                                   const OutSegs o, uint32_t* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tg = lane & 3;
   const int pw = warp * 16;  // positions pw .. pw+15 of the first 64-group
@@ -161,41 +212,26 @@ __global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t
   for (int j = 0; j < 2; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
 #pragma unroll 2
   for (int b = 0; b < nb; b++) {
-    const uint8_t* r = rec + (size_t)b * Rec<QT>::bytes;
-    int a[4];
-    Rec<QT>::frag(r, lane, a);
-    const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes) + g);
-    const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
     const uint8_t* ab = reinterpret_cast<const uint8_t*>(aq) + (size_t)b * Q8A_GROUP * 32;  // group 0
     const float* sb = ad + (size_t)b * Q8A_GROUP;
-#pragma unroll
-    for (int j = 0; j < 2; j++) n8_step(a, dlo, dhi, ab, sb, pw + 8 * j, g, tg, acc[j]);
+    block_step<QT, 2>(rec + (size_t)b * Rec<QT>::bytes, ab, sb, pw, lane, g, tg, acc);
   }
-  const int r0 = blockIdx.x * 16 + g, r1 = r0 + 8;
-#pragma unroll
-  for (int j = 0; j < 2; j++) {
-    const int pa = pw + 8 * j + 2 * tg, pb = pa + 1;
-    if (r0 < rows) {
-      if (pa < T) store_out(acc[j][0].x, r0, pa, out, out_ld, epi, bias, err);
-      if (pb < T) store_out(acc[j][0].y, r0, pb, out, out_ld, epi, bias, err);
-    }
-    if (r1 < rows) {
-      if (pa < T) store_out(acc[j][1].x, r1, pa, out, out_ld, epi, bias, err);
-      if (pb < T) store_out(acc[j][1].y, r1, pb, out, out_ld, epi, bias, err);
-    }
-  }
+  store_tile<2>(acc, blockIdx.x, pw, T, o, g, tg, err);
 }
 
 // ---- chunk kernel: TMA bulk-copy pipeline -------------------------------------
-constexpr int CK_WARPS = 4;
+constexpr int CK_TILES = 2;   // 16-row tiles per CTA
+constexpr int CK_WARPS = 4;   // warp w: tile w >> 1, positions 32 * (w & 1) ..
 constexpr int CK_THREADS = CK_WARPS * 32;
+constexpr int CK_NJ = 4;      // n8 tiles per warp (32 positions)
 constexpr int CK_SB = 4;      // blocks per stage
-constexpr int CK_STAGES = 6;
+constexpr int CK_STAGES = 4;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // mbarrier wait bound (2 s)
 
 template <int QT>
 struct ChunkSmem {
-  static constexpr int w_bytes = CK_SB * Rec<QT>::bytes;
+  static constexpr int w_tile = CK_SB * Rec<QT>::bytes;
+  static constexpr int w_bytes = CK_TILES * w_tile;
   static constexpr int a_bytes = CK_SB * Q8A_GROUP * 32;
   static constexpr int s_bytes = CK_SB * Q8A_GROUP * 4;
   static constexpr int stage = w_bytes + a_bytes + s_bytes;
@@ -238,32 +274,34 @@ DI bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 
 template <int QT>
-DI void issue_stage(uint8_t* sbuf, uint32_t bar, int st, int nb, const uint8_t* wtile, const int8_t* aslab,
-                    const float* sslab) {
+DI void issue_stage(uint8_t* sbuf, uint32_t bar, int st, int nb, int ntile, const uint8_t* wtile,
+                    const int8_t* aslab, const float* sslab) {
   using S = ChunkSmem<QT>;
   const int b0 = st * CK_SB, nrec = min(CK_SB, nb - b0);
   const uint32_t wb = (uint32_t)(nrec * Rec<QT>::bytes), abytes = (uint32_t)(nrec * Q8A_GROUP * 32),
                  sbytes = (uint32_t)(nrec * Q8A_GROUP * 4);
-  mbar_expect_tx(bar, wb + abytes + sbytes);
-  bulk_g2s(smem_u32(sbuf), wtile + (size_t)b0 * Rec<QT>::bytes, wb, bar);
+  mbar_expect_tx(bar, wb * ntile + abytes + sbytes);
+  for (int i = 0; i < ntile; i++)
+    bulk_g2s(smem_u32(sbuf + i * S::w_tile), wtile + ((size_t)i * nb + b0) * Rec<QT>::bytes, wb, bar);
   bulk_g2s(smem_u32(sbuf + S::w_bytes), aslab + (size_t)b0 * Q8A_GROUP * 32, abytes, bar);
   bulk_g2s(smem_u32(sbuf + S::w_bytes + S::a_bytes), sslab + (size_t)b0 * Q8A_GROUP, sbytes, bar);
 }
 
 template <int QT>
-__global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* __restrict__ W, int rows, int nb,
+__global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* __restrict__ W, int tiles, int nb,
                                                                 const int8_t* __restrict__ aq,
                                                                 const float* __restrict__ ad, int T,
-                                                                float* __restrict__ out, int out_ld, int epi,
-                                                                const float* __restrict__ bias, uint32_t* err) {
+                                                                const OutSegs o, uint32_t* err) {
   using S = ChunkSmem<QT>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tg = lane & 3;
+  const int tile0 = blockIdx.x * CK_TILES;
+  const int ntile = min(CK_TILES, tiles - tile0);
+  const int wt = warp >> 1;             // this warp's tile within the CTA
   const int grp = blockIdx.y;           // 64-position group
-  const int p0 = grp * Q8A_GROUP;
-  const int pw = warp * 16;             // this warp's positions within the group
-  const uint8_t* wtile = W + (size_t)blockIdx.x * nb * Rec<QT>::bytes;
+  const int pw = 32 * (warp & 1);       // this warp's positions within the group
+  const uint8_t* wtile = W + (size_t)tile0 * nb * Rec<QT>::bytes;
   const int8_t* aslab = aq + (size_t)grp * nb * Q8A_GROUP * 32;
   const float* sslab = ad + (size_t)grp * nb * Q8A_GROUP;
   const int nst = (nb + CK_SB - 1) / CK_SB;
@@ -274,32 +312,33 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
     for (int s = 0; s < CK_STAGES; s++) mbar_init(bar0 + 8 * s, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     for (; issued < CK_STAGES && issued < nst; issued++)
-      issue_stage<QT>(smem + issued * S::stage, bar0 + 8 * issued, issued, nb, wtile, aslab, sslab);
+      issue_stage<QT>(smem + issued * S::stage, bar0 + 8 * issued, issued, nb, ntile, wtile, aslab, sslab);
   }
   __syncthreads();
 
-  float2 acc[2][2];
+  float2 acc[CK_NJ][2];
 #pragma unroll
-  for (int j = 0; j < 2; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
+  for (int j = 0; j < CK_NJ; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
+  const bool active = wt < ntile && grp * Q8A_GROUP + pw < T;
 
   for (int st = 0; st < nst; st++) {
     const int slot = st % CK_STAGES;
     const bool ok = mbar_wait(bar0 + 8 * slot, (uint32_t)((st / CK_STAGES) & 1));
-    if (ok) {
+    if (ok && active) {
       const uint8_t* sbuf = smem + slot * S::stage;
+      const uint8_t* wbuf = sbuf + wt * S::w_tile;
       const uint8_t* abuf = sbuf + S::w_bytes;
       const float* sbf = reinterpret_cast<const float*>(sbuf + S::w_bytes + S::a_bytes);
       const int nblk = min(CK_SB, nb - st * CK_SB);
-      for (int bb = 0; bb < nblk; bb++) {
-        const uint8_t* r = sbuf + bb * Rec<QT>::bytes;
-        int a[4];
-        Rec<QT>::frag(r, lane, a);
-        const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
-        const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
-        const uint8_t* ab = abuf + bb * Q8A_GROUP * 32;
-        const float* sb = sbf + bb * Q8A_GROUP;
+      if (nblk == CK_SB) {
 #pragma unroll
-        for (int j = 0; j < 2; j++) n8_step(a, dlo, dhi, ab, sb, pw + 8 * j, g, tg, acc[j]);
+        for (int bb = 0; bb < CK_SB; bb++)
+          block_step<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
+                                lane, g, tg, acc);
+      } else {
+        for (int bb = 0; bb < nblk; bb++)
+          block_step<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
+                                lane, g, tg, acc);
       }
     }
     // every warp is done with this slot; the OR makes the abort decision
@@ -314,28 +353,15 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
     }
     if (threadIdx.x == 0 && issued < nst) {
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      issue_stage<QT>(smem + slot * S::stage, bar0 + 8 * slot, issued, nb, wtile, aslab, sslab);
+      issue_stage<QT>(smem + slot * S::stage, bar0 + 8 * slot, issued, nb, ntile, wtile, aslab, sslab);
       issued++;
     }
   }
-  const int r0 = blockIdx.x * 16 + g, r1 = r0 + 8;
-#pragma unroll
-  for (int j = 0; j < 2; j++) {
-    const int pa = p0 + pw + 8 * j + 2 * tg, pb = pa + 1;
-    if (r0 < rows) {
-      if (pa < T) store_out(acc[j][0].x, r0, pa, out, out_ld, epi, bias, err);
-      if (pb < T) store_out(acc[j][0].y, r0, pb, out, out_ld, epi, bias, err);
-    }
-    if (r1 < rows) {
-      if (pa < T) store_out(acc[j][1].x, r1, pa, out, out_ld, epi, bias, err);
-      if (pb < T) store_out(acc[j][1].y, r1, pb, out, out_ld, epi, bias, err);
-    }
-  }
+  if (active) store_tile<CK_NJ>(acc, tile0 + wt, grp * Q8A_GROUP + pw, T, o, g, tg, err);
 }
 
 template <int QT>
-cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
-                         int epi, const float* bias) {
+cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   constexpr int smem = ChunkSmem<QT>::total;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
@@ -345,35 +371,42 @@ cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, 
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set |= 1ull << dev;
   }
-  dim3 grid((m.rows + 15) / 16, (T + Q8A_GROUP - 1) / Q8A_GROUP);
-  gemm_chunk_kernel<QT><<<grid, CK_THREADS, smem, L.stream>>>((const uint8_t*)m.q, m.rows, m.nb, a.qa_q, a.qa_d, T,
-                                                              out, out_ld, epi, bias, L.err);
+  const int tiles = (m.rows + 15) / 16;
+  dim3 grid((tiles + CK_TILES - 1) / CK_TILES, (T + Q8A_GROUP - 1) / Q8A_GROUP);
+  gemm_chunk_kernel<QT><<<grid, CK_THREADS, smem, L.stream>>>((const uint8_t*)m.q, tiles, m.nb, a.qa_q, a.qa_d, T, o,
+                                                              L.err);
   return cudaGetLastError();
 }
 
 }  // namespace
+
+cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
+  cudaError_t e;
+  if (T > 16) {
+    e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, o) : launch_chunk<GT_Q4_0>(L, m, a, T, o);
+  } else {
+    const dim3 grid((m.rows + 15) / 16);
+    if (m.type == GT_Q8_0)
+      gemm_small_kernel<GT_Q8_0><<<grid, SM_WARPS * 32, 0, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T,
+                                                                        o, L.err);
+    else
+      gemm_small_kernel<GT_Q4_0><<<grid, SM_WARPS * 32, 0, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T,
+                                                                        o, L.err);
+    e = cudaGetLastError();
+  }
+  if (L.launches) ++*L.launches;
+  return e;
+}
 
 cudaError_t launch_gemv_fast(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                              int epi, const float* bias, bool* handled) {
   *handled = false;
   if (m.layout != LAYOUT_MMA16) return cudaSuccess;
   *handled = true;
-  cudaError_t e;
-  if (T > 16) {
-    e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, out, out_ld, epi, bias)
-                          : launch_chunk<GT_Q4_0>(L, m, a, T, out, out_ld, epi, bias);
-  } else {
-    const dim3 grid((m.rows + 15) / 16);
-    if (m.type == GT_Q8_0)
-      gemm_small_kernel<GT_Q8_0><<<grid, SM_WARPS * 32, 0, L.stream>>>(
-          (const uint8_t*)m.q, m.rows, m.nb, a.qa_q, a.qa_d, T, out, out_ld, epi, bias, L.err);
-    else
-      gemm_small_kernel<GT_Q4_0><<<grid, SM_WARPS * 32, 0, L.stream>>>(
-          (const uint8_t*)m.q, m.rows, m.nb, a.qa_q, a.qa_d, T, out, out_ld, epi, bias, L.err);
-    e = cudaGetLastError();
-  }
-  if (L.launches) ++*L.launches;
-  return e;
+  OutSegs o;
+  o.n = 1;
+  o.s[0] = OutSeg{m.rows, out, out_ld, epi, bias};
+  return launch_gemm_mma16(L, m, a, T, o);
 }
 
 }  // namespace det

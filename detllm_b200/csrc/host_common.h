@@ -105,6 +105,8 @@ class Gguf {
 // ---- model ------------------------------------------------------------------
 struct LayerDev {
   DevMatrix wq, wk, wv, wo, gate, up, down;
+  // q|k|v and gate|up stored back to back (rows == 0: not fused)
+  DevMatrix wqkv, wgu;
   float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
 };
 

@@ -56,6 +56,23 @@ struct DevActs {
 // epilogue modes of a GEMV/GEMM
 enum : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
 
+// Output of a GEMM over a matrix that is several matrices stored back to
+// back (q|k|v, gate|up): rows [sum of earlier rows, + rows) of the launch go
+// to out[p * ld + r] with their own epilogue.  All but the last segment
+// hold a multiple of 16 rows.
+constexpr int kMaxOutSegs = 3;
+struct OutSeg {
+  int rows = 0;
+  float* out = nullptr;
+  int ld = 0;
+  int epi = 0;
+  const float* bias = nullptr;
+};
+struct OutSegs {
+  OutSeg s[kMaxOutSegs];
+  int n = 0;
+};
+
 struct Launch {
   cudaStream_t stream;
   uint32_t* err;        // device error flag
@@ -69,6 +86,8 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
 cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h);
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
 cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
+// LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
+cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                         int epi, const float* bias);
 cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, const int* pos0, int n_head,

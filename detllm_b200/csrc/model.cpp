@@ -242,6 +242,45 @@ struct Loader {
   }
 };
 
+// Store matrices that read the same activations (q/k/v, gate/up) back to back
+// as one LAYOUT_MMA16 matrix so one launch covers them; each part's `q` then
+// points into the fused buffer.  Leaves *fused empty (rows 0) when the parts
+// cannot be fused: other types or layouts, different widths, or a part other
+// than the last whose rows are not a multiple of 16.
+det_status fuse_matrices(det_model* m, DevMatrix* const* parts, int n, DevMatrix* fused) {
+  *fused = DevMatrix();
+  size_t bytes = 0;
+  int rows = 0;
+  for (int i = 0; i < n; i++) {
+    const DevMatrix& p = *parts[i];
+    if (p.layout != LAYOUT_MMA16 || p.type != parts[0]->type || p.cols != parts[0]->cols) return DET_OK;
+    if (i + 1 < n && p.rows % 16) return DET_OK;
+    rows += p.rows;
+  }
+  const size_t rec = parts[0]->type == GT_Q8_0 ? 544 : 288;
+  for (int i = 0; i < n; i++) bytes += (size_t)((parts[i]->rows + 15) / 16) * parts[i]->nb * rec;
+  void* buf = nullptr;
+  if (cudaMalloc(&buf, bytes) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  m->allocations.push_back(buf);
+  size_t off = 0;
+  for (int i = 0; i < n; i++) {
+    DevMatrix& p = *parts[i];
+    const size_t b = (size_t)((p.rows + 15) / 16) * p.nb * rec;
+    uint8_t* dst = static_cast<uint8_t*>(buf) + off;
+    if (cudaMemcpy(dst, p.q, b, cudaMemcpyDeviceToDevice) != cudaSuccess) return DET_ERR_CUDA;
+    void* old = const_cast<void*>(p.q);
+    for (auto& a : m->allocations)
+      if (a == old) a = nullptr;
+    cudaFree(old);
+    p.q = dst;
+    off += b;
+  }
+  *fused = *parts[0];
+  fused->rows = rows;
+  fused->q = buf;
+  return DET_OK;
+}
+
 // optional metadata helpers (det-model lib.rs:1566-1645)
 det_status opt_u32(const Gguf& g, const std::string& k, uint32_t* v, bool* present) {
   const int e = g.get_u32(k, v);
@@ -458,6 +497,10 @@ det_status load_impl(const uint8_t* bytes, size_t len, det_model* m) {
     if ((st = ld.matrix(p + "ffn_gate.weight", c.dff, c.d, &L.gate, &ty[4]))) return st;
     if ((st = ld.matrix(p + "ffn_up.weight", c.dff, c.d, &L.up, &ty[5]))) return st;
     if ((st = ld.matrix(p + "ffn_down.weight", c.d, c.dff, &L.down, &ty[6]))) return st;
+    DevMatrix* qkv[3] = {&L.wq, &L.wk, &L.wv};
+    if ((st = fuse_matrices(m, qkv, 3, &L.wqkv))) return st;
+    DevMatrix* gu[2] = {&L.gate, &L.up};
+    if ((st = fuse_matrices(m, gu, 2, &L.wgu))) return st;
     if (l == 0) {
       for (int i = 0; i < 7; i++) m->weight_types[1 + i] = ty[i];
       m->has_bias = L.bq != nullptr;

@@ -176,10 +176,12 @@ double bytes_per_weight(int type) {
   }
 }
 
-// launch_gemv with optional per-launch event timing (det_set_profiling)
-cudaError_t gemv(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T, float* out, int ld,
-                 int epi, const float* bias) {
-  if (!g_profiling) return launch_gemv(L, W, a, T, out, ld, epi, bias);
+// A weight GEMV/GEMM launch with optional per-launch event timing
+// (det_set_profiling); `launch` enqueues it.  Algorithmic bytes: weights,
+// quantised activations and outputs (read + write for residual outputs).
+template <typename F>
+cudaError_t timed_gemm(det_session* s, const DevMatrix& W, int T, double out_bytes_per_pos, F&& launch) {
+  if (!g_profiling) return launch();
   const size_t i = s->prof_pending.size();
   while (s->prof_events.size() < 2 * (i + 1)) {
     cudaEvent_t ev;
@@ -188,14 +190,27 @@ cudaError_t gemv(det_session* s, const Launch& L, const DevMatrix& W, const DevA
     s->prof_events.push_back(ev);
   }
   cudaError_t e = cudaEventRecord(s->prof_events[2 * i], s->stream);
-  if (e == cudaSuccess) e = launch_gemv(L, W, a, T, out, ld, epi, bias);
+  if (e == cudaSuccess) e = launch();
   if (e == cudaSuccess) e = cudaEventRecord(s->prof_events[2 * i + 1], s->stream);
   const double wbytes = (double)W.rows * W.cols * bytes_per_weight(W.type);
   const double abytes = (double)T * W.cols *
                         (W.type == GT_Q6_K ? 1.0 + 4.0 / 256.0 : (W.type == GT_F32 ? 4.0 : 1.0 + 4.0 / 32.0));
-  const double obytes = (double)T * W.rows * (epi == EPI_RESIDUAL ? 8.0 : 4.0);
-  s->prof_pending.emplace_back(wbytes + abytes + obytes, wbytes);
+  s->prof_pending.emplace_back(wbytes + abytes + (double)T * out_bytes_per_pos, wbytes);
   return e;
+}
+
+cudaError_t gemv(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T, float* out, int ld,
+                 int epi, const float* bias) {
+  return timed_gemm(s, W, T, W.rows * (epi == EPI_RESIDUAL ? 8.0 : 4.0),
+                    [&] { return launch_gemv(L, W, a, T, out, ld, epi, bias); });
+}
+
+// one launch over a fused (back-to-back) matrix
+cudaError_t gemm_fused(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T,
+                       const OutSegs& o) {
+  double ob = 0;
+  for (int k = 0; k < o.n; k++) ob += o.s[k].rows * (o.s[k].epi == EPI_RESIDUAL ? 8.0 : 4.0);
+  return timed_gemm(s, W, T, ob, [&] { return launch_gemm_mma16(L, W, a, T, o); });
 }
 
 // forward_one_with_workspace for positions pos0 .. pos0+T-1, pos0 = *d_pos
@@ -219,9 +234,18 @@ det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
     CK(quantise_for(s, L,W.wq.type, s->h, c.d, T, &a, &have));
     CK(quantise_for(s, L,W.wk.type, s->h, c.d, T, &a, &have));
     CK(quantise_for(s, L,W.wv.type, s->h, c.d, T, &a, &have));
-    CK(gemv(s, L,W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
-    CK(gemv(s, L,W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
-    CK(gemv(s, L,W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+    if (W.wqkv.rows) {
+      OutSegs o;
+      o.n = 3;
+      o.s[0] = OutSeg{W.wq.rows, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq};
+      o.s[1] = OutSeg{W.wk.rows, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk};
+      o.s[2] = OutSeg{W.wv.rows, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv};
+      CK(gemm_fused(s, L, W.wqkv, a, T, o));
+    } else {
+      CK(gemv(s, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
+      CK(gemv(s, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
+      CK(gemv(s, L, W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+    }
     float* kc = s->kc + (size_t)l * kv_layer;
     float* vc = s->vc + (size_t)l * kv_layer;
     CK(launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
@@ -235,8 +259,16 @@ det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
     have = 0;
     CK(quantise_for(s, L,W.gate.type, s->h, c.d, T, &a, &have));
     CK(quantise_for(s, L,W.up.type, s->h, c.d, T, &a, &have));
-    CK(gemv(s, L,W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
-    CK(gemv(s, L,W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+    if (W.wgu.rows) {
+      OutSegs o;
+      o.n = 2;
+      o.s[0] = OutSeg{W.gate.rows, s->gate, c.dff, EPI_STORE, nullptr};
+      o.s[1] = OutSeg{W.up.rows, s->up, c.dff, EPI_STORE, nullptr};
+      CK(gemm_fused(s, L, W.wgu, a, T, o));
+    } else {
+      CK(gemv(s, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
+      CK(gemv(s, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+    }
     CK(launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T));
     have = 0;
     CK(quantise_for(s, L,W.down.type, s->ff, c.dff, T, &a, &have));
