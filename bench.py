@@ -4,7 +4,7 @@
 Workload: a TinyLlama-1.1B-shaped decoder with
 random-init Q8_0 weights (22 layers, d 2048, 32/4 heads, FFN 5632, vocab
 32000), 4096 Zipf(1.1) token ids encoded as codec symbols at n_ctx 2048
-(overlap 512, one window rollover), forward chunk 256.  One step = one full
+(overlap 512, one window rollover), forward chunk 512.  One step = one full
 compress of that stream: teacher-forced forward -> logits -> CDF ranges ->
 host range coder, through det_encode_symbols.
 
@@ -241,9 +241,11 @@ def run(args):
     dev_max, wall_max = all_max(dev_s, ws), all_max(wall, ws)
     # one profiled step for the per-launch GEMV/GEMM roofline
     D.set_profiling(True)
+    model.profile(reset=True)
     model.encode_symbols(tokens, N_CTX, OVERLAP)
     D.set_profiling(False)
     prof = model.stats(reset=True)
+    kprof = model.profile(reset=True)
     if rank != 0:
         return
     total_tokens = N_TOKENS * args.steps * ws
@@ -255,7 +257,7 @@ def run(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
         "data": "synthetic (seeded random-init weights, Zipf(1.1) tokens)",
         "config": {"workload": f"{CONFIG} encode: {N_TOKENS} Zipf tokens per rank, n_ctx {N_CTX}, overlap {OVERLAP}, "
-                               f"chunk 256", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
+                               f"chunk {os.environ.get('DETGPU_CHUNK', '512')}", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
                    "parallelism": f"segments{ws}", "l2": "weights 1.17 GB per step > 126 MB L2 (no flush)"},
         "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},
@@ -266,6 +268,9 @@ def run(args):
                      "launches": int(prof.gemm_launches), "ms_per_launch": prof.gemm_ms / max(prof.gemm_launches, 1),
                      "bytes_per_launch": prof.gemm_bytes / max(prof.gemm_launches, 1),
                      "share_of_device_time": prof.gemm_ms / max(prof.forward_ms + prof.cdf_ms, 1e-9)},
+        "kernels": {k: {"launches": n, "ms": round(ms, 3), "share": round(ms / max(sum(v[1] for v in kprof.values()),
+                                                                                  1e-9), 4)}
+                    for k, (n, ms) in kprof.items() if n},
         "clocks": clk.summary(),
         "payload_bytes": len(payload),
         "weight_bytes_per_token": S.weight_bytes_per_token(spec),

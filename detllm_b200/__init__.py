@@ -100,6 +100,7 @@ def lib():
             "det_device_expf": (I, [I, P, P, SZ]),
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
             "det_set_profiling": (I, [I]),
+            "det_model_profile": (I, [P, C.c_char_p, SZ, I]),
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
         }
         for name, (res, args) in sig.items():
@@ -198,6 +199,15 @@ class Model:
         st = Stats()
         _check(lib().det_model_stats(self._h, C.byref(st), int(reset)), "det_model_stats")
         return st
+
+    def profile(self, reset: bool = False) -> dict:
+        """Per-kernel-group device time gathered while profiling was on:
+        {group: (launches, milliseconds)}."""
+        import json
+
+        buf = C.create_string_buffer(4096)
+        _check(lib().det_model_profile(self._h, buf, len(buf), int(reset)), "det_model_profile")
+        return {k: (int(v[0]), float(v[1])) for k, v in json.loads(buf.value.decode()).items()}
 
     def session(self, n_ctx: int, max_chunk: int = 64) -> "Session":
         return Session(self, n_ctx, max_chunk)

@@ -9,7 +9,7 @@
 //
 // Encode is teacher-forced, so the whole schedule is known up front: the
 // symbols are mapped to (window, logits position) pairs, each window's tokens
-// run through the device in chunks of up to `kChunk` positions, and the
+// run through the device in chunks of up to `encode_chunk()` positions, and the
 // ranges of all symbols whose logits a chunk produced come back in one call.
 // The range coder consumes them in symbol order, so the payload is the same
 // byte stream the one-token-at-a-time reference produces.  Positions whose
@@ -24,7 +24,17 @@ using namespace det;
 
 namespace {
 
-constexpr uint32_t kChunk = 256;
+// Positions per forward launch sequence: larger chunks give the GEMMs and
+// attention more parallel work per weight pass.  DETGPU_CHUNK overrides the
+// default (16 .. 1024); the output bytes do not depend on it.
+uint32_t encode_chunk() {
+  static const uint32_t c = [] {
+    const char* e = std::getenv("DETGPU_CHUNK");
+    const long v = e ? std::strtol(e, nullptr, 10) : 0;
+    return v >= 16 && v <= 1024 ? (uint32_t)v : 512u;
+  }();
+  return c;
+}
 constexpr uint32_t kEscapes = 256;
 
 // next_window_start (det-cli main.rs:772-778)
@@ -103,7 +113,7 @@ det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_c
   for (const auto& w : windows)
     if (w.needed) need_device = true;
   if (need_device)
-    if (det_status st = session_acquire(m, n_ctx, kChunk, &s)) return st;
+    if (det_status st = session_acquire(m, n_ctx, encode_chunk(), &s)) return st;
   std::vector<uint32_t> rows, qsym;
   std::vector<det_symbol_range> ranges;
   det_status st = DET_OK;
@@ -111,8 +121,9 @@ det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_c
     const WindowPlan& w = windows[wi];
     if (w.needed == 0) continue;
     if (wi > 0) st = det_session_reset(s);
-    for (size_t p0 = 0; p0 < w.needed && !st; p0 += kChunk) {
-      const uint32_t cnt = (uint32_t)std::min<size_t>(kChunk, w.needed - p0);
+    const uint32_t chunk = (uint32_t)s->max_chunk;
+    for (size_t p0 = 0; p0 < w.needed && !st; p0 += chunk) {
+      const uint32_t cnt = (uint32_t)std::min<size_t>(chunk, w.needed - p0);
       st = det_forward(s, tokens.data() + w.start + p0, cnt, (uint32_t)p0, nullptr);
       if (st) break;
       rows.clear();
@@ -234,7 +245,7 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
   RangeDecoder dec;
   if (det_status st = dec.init(payload, plen)) return st;
   det_session* s = nullptr;
-  if (det_status st = session_acquire(m, n_ctx, kChunk, &s)) return st;
+  if (det_status st = session_acquire(m, n_ctx, encode_chunk(), &s)) return st;
   if (det_status st = det_session_reset(s)) return st;
   std::vector<uint8_t> bytes;
   std::vector<uint32_t> ctx, syms;
@@ -248,8 +259,8 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
       ws = nws;
       clen = 0;
       st = det_session_reset(s);
-      for (size_t p = ws; p < pos && !st; p += kChunk) {
-        const uint32_t cnt = (uint32_t)std::min<size_t>(kChunk, pos - p);
+      for (size_t p = ws; p < pos && !st; p += (size_t)s->max_chunk) {
+        const uint32_t cnt = (uint32_t)std::min<size_t>((size_t)s->max_chunk, pos - p);
         st = det_forward(s, ctx.data() + p, cnt, (uint32_t)clen, nullptr);
         clen += cnt;
         last_row = cnt - 1;

@@ -28,12 +28,14 @@
 // 12582912 + isum exactly, so one FADD recovers (f32)isum.
 //
 // Chunk kernel (T > 16 positions): a CTA owns two 16-row tiles and one group
-// of 64 positions; each of its 4 warps owns 16 rows x 32 positions, so one
-// A fragment feeds four MMAs.  Each pipeline stage is SB blocks: the two
-// tiles' SB weight records, the SB (group, block) activation slabs and their
-// scales -- contiguous ranges moved by TMA bulk copies (cp.async.bulk) that
-// one thread issues, completing on an mbarrier.  Every mbarrier wait is
-// bounded (globaltimer); on timeout the kernel flags ERRF_TIMEOUT and stops.
+// of 64 positions; each of its 4 compute warps owns 16 rows x 32 positions,
+// so one A fragment feeds four MMAs, and B fragments come from shared memory
+// by ldmatrix.  Each pipeline stage is SB blocks: the two tiles' SB weight
+// records, the SB (group, block) activation slabs and their scales --
+// contiguous ranges moved by TMA bulk copies (cp.async.bulk) that a producer
+// warp issues, completing on a "full" mbarrier; compute warps release a slot
+// through an "empty" mbarrier.  Every mbarrier wait is bounded
+// (globaltimer); on timeout the kernel flags ERRF_TIMEOUT and stops.
 #include <cuda_runtime.h>
 
 #include "dev_math.cuh"
@@ -43,7 +45,7 @@ namespace det {
 namespace {
 
 DI void mma_s8(int (&c)[4], const int (&a)[4], int b0, int b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -181,6 +183,49 @@ DI void n8_step(const int (&a)[4], float2 dlo, float2 dhi, const uint8_t* ab, co
   fold2(acc[1], dhi, adv, i23);
 }
 
+// B fragments of two n8 tiles (positions pos .. pos+15 of slab `ab`) with one
+// ldmatrix.x4: matrices (pos..pos+7, bytes 0-15), (pos..pos+7, 16-31),
+// (pos+8..pos+15, 0-15), (pos+8..pos+15, 16-31); lane i gives the row address
+// of row i%8 of matrix i/8, so the half swizzle is applied per row.
+DI void ldsm_b_pair(const uint8_t* ab, int pos, int lane, int (&b)[4]) {
+  const int mi = lane >> 3, p = pos + ((mi >> 1) << 3) + (lane & 7);
+  const uint32_t addr = (uint32_t)__cvta_generic_to_shared(ab + p * 32 + (((mi & 1) << 4) ^ (((p >> 2) & 1) << 4)));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+               : "r"(addr));
+}
+
+// MMA + fold of one n8 tile whose B fragments are already in registers
+DI void n8_fold(const int (&a)[4], float2 dlo, float2 dhi, int b0v, int b1v, const float* sb, int pos, int tg,
+                float2 (&acc)[2]) {
+  const float2 bias2 = make_float2(-12582912.0f, -12582912.0f);
+  int c[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
+  mma_s8(c, a, b0v, b1v);
+  const float2 adv = *reinterpret_cast<const float2*>(sb + pos + 2 * tg);
+  const float2 i01 = add2(make_float2(__int_as_float(c[0]), __int_as_float(c[1])), bias2);
+  const float2 i23 = add2(make_float2(__int_as_float(c[2]), __int_as_float(c[3])), bias2);
+  fold2(acc[0], dlo, adv, i01);
+  fold2(acc[1], dhi, adv, i23);
+}
+
+// one record against NJ n8 tiles starting at `pos`, B fragments by ldmatrix
+// (shared-memory slabs only)
+template <int QT, int NJ>
+DI void block_step_sm(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg,
+                      float2 (&acc)[NJ][2]) {
+  static_assert(NJ % 2 == 0, "n8 tiles come in ldmatrix pairs");
+  int a[4];
+  Rec<QT>::frag(r, lane, a);
+  const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
+  const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
+  int b[NJ / 2][4];
+#pragma unroll
+  for (int j = 0; j < NJ / 2; j++) ldsm_b_pair(ab, pos + 16 * j, lane, b[j]);
+#pragma unroll
+  for (int j = 0; j < NJ; j++) n8_fold(a, dlo, dhi, b[j >> 1][2 * (j & 1)], b[j >> 1][2 * (j & 1) + 1], sb, pos + 8 * j,
+                                       tg, acc[j]);
+}
+
 // A fragment + scales of one record, then NJ n8 tiles starting at `pos`
 template <int QT, int NJ>
 DI void block_step(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg,
@@ -219,11 +264,15 @@ __global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t
   store_tile<2>(acc, blockIdx.x, pw, T, o, g, tg, err);
 }
 
-// ---- chunk kernel: TMA bulk-copy pipeline -------------------------------------
+// ---- chunk kernel: warp-specialised TMA bulk-copy pipeline ------------------
+// Warps 0-3 compute (warp w: tile w >> 1, positions 32 * (w & 1) ..); warp 4
+// is the producer, one lane of which issues the stage copies.  full[s]
+// completes when stage s's bytes have landed; empty[s] when all four compute
+// warps have finished with it.  No CTA-wide barrier inside the loop.
 constexpr int CK_TILES = 2;   // 16-row tiles per CTA
-constexpr int CK_WARPS = 4;   // warp w: tile w >> 1, positions 32 * (w & 1) ..
-constexpr int CK_THREADS = CK_WARPS * 32;
-constexpr int CK_NJ = 4;      // n8 tiles per warp (32 positions)
+constexpr int CK_CWARPS = 4;  // compute warps
+constexpr int CK_THREADS = (CK_CWARPS + 1) * 32;
+constexpr int CK_NJ = 4;      // n8 tiles per compute warp (32 positions)
 constexpr int CK_SB = 4;      // blocks per stage
 constexpr int CK_STAGES = 4;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // mbarrier wait bound (2 s)
@@ -235,7 +284,7 @@ struct ChunkSmem {
   static constexpr int a_bytes = CK_SB * Q8A_GROUP * 32;
   static constexpr int s_bytes = CK_SB * Q8A_GROUP * 4;
   static constexpr int stage = w_bytes + a_bytes + s_bytes;
-  static constexpr int bars = CK_STAGES * 8;
+  static constexpr int bars = 2 * CK_STAGES * 8;
   static constexpr int total = stage * CK_STAGES + bars;
 };
 
@@ -246,6 +295,9 @@ DI void mbar_init(uint32_t bar, uint32_t count) {
 }
 DI void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+DI void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
 DI void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
@@ -295,36 +347,58 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
   using S = ChunkSmem<QT>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tg = lane & 3;
   const int tile0 = blockIdx.x * CK_TILES;
   const int ntile = min(CK_TILES, tiles - tile0);
-  const int wt = warp >> 1;             // this warp's tile within the CTA
-  const int grp = blockIdx.y;           // 64-position group
-  const int pw = 32 * (warp & 1);       // this warp's positions within the group
-  const uint8_t* wtile = W + (size_t)tile0 * nb * Rec<QT>::bytes;
-  const int8_t* aslab = aq + (size_t)grp * nb * Q8A_GROUP * 32;
-  const float* sslab = ad + (size_t)grp * nb * Q8A_GROUP;
+  const int grp = blockIdx.y;  // 64-position group
   const int nst = (nb + CK_SB - 1) / CK_SB;
-  const uint32_t bar0 = smem_u32(smem + S::stage * CK_STAGES);
-  int issued = 0;  // stages issued so far (meaningful in thread 0)
+  const uint32_t full0 = smem_u32(smem + S::stage * CK_STAGES);
+  const uint32_t empty0 = full0 + 8 * CK_STAGES;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < CK_STAGES; s++) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < CK_STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, CK_CWARPS);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    for (; issued < CK_STAGES && issued < nst; issued++)
-      issue_stage<QT>(smem + issued * S::stage, bar0 + 8 * issued, issued, nb, ntile, wtile, aslab, sslab);
   }
   __syncthreads();
 
+  if (warp == CK_CWARPS) {  // ---- producer
+    if (lane != 0) return;
+    const uint8_t* wtile = W + (size_t)tile0 * nb * Rec<QT>::bytes;
+    const int8_t* aslab = aq + (size_t)grp * nb * Q8A_GROUP * 32;
+    const float* sslab = ad + (size_t)grp * nb * Q8A_GROUP;
+    int st = 0;
+    for (; st < nst; st++) {
+      const int slot = st % CK_STAGES;
+      if (st >= CK_STAGES && !mbar_wait(empty0 + 8 * slot, (uint32_t)((st / CK_STAGES - 1) & 1))) {
+        atomicOr(err, ERRF_TIMEOUT);
+        break;
+      }
+      issue_stage<QT>(smem + slot * S::stage, full0 + 8 * slot, st, nb, ntile, wtile, aslab, sslab);
+    }
+    // the CTA's shared memory must outlive every copy issued into it
+    for (int s2 = max(0, st - CK_STAGES); s2 < st; s2++)
+      mbar_wait(full0 + 8 * (s2 % CK_STAGES), (uint32_t)((s2 / CK_STAGES) & 1));
+    return;
+  }
+
+  // ---- compute warps
+  const int g = lane >> 2, tg = lane & 3;
+  const int wt = warp >> 1;        // this warp's tile within the CTA
+  const int pw = 32 * (warp & 1);  // this warp's positions within the group
+  const bool active = wt < ntile && grp * Q8A_GROUP + pw < T;
   float2 acc[CK_NJ][2];
 #pragma unroll
   for (int j = 0; j < CK_NJ; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
-  const bool active = wt < ntile && grp * Q8A_GROUP + pw < T;
 
   for (int st = 0; st < nst; st++) {
     const int slot = st % CK_STAGES;
-    const bool ok = mbar_wait(bar0 + 8 * slot, (uint32_t)((st / CK_STAGES) & 1));
-    if (ok && active) {
+    if (!mbar_wait(full0 + 8 * slot, (uint32_t)((st / CK_STAGES) & 1))) {
+      if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
+      return;
+    }
+    if (active) {
       const uint8_t* sbuf = smem + slot * S::stage;
       const uint8_t* wbuf = sbuf + wt * S::w_tile;
       const uint8_t* abuf = sbuf + S::w_bytes;
@@ -333,29 +407,16 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
       if (nblk == CK_SB) {
 #pragma unroll
         for (int bb = 0; bb < CK_SB; bb++)
-          block_step<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
-                                lane, g, tg, acc);
+          block_step_sm<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
+                                   lane, g, tg, acc);
       } else {
         for (int bb = 0; bb < nblk; bb++)
-          block_step<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
-                                lane, g, tg, acc);
+          block_step_sm<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
+                                   lane, g, tg, acc);
       }
     }
-    // every warp is done with this slot; the OR makes the abort decision
-    // uniform across the CTA
-    if (__syncthreads_or(!ok)) {
-      if (threadIdx.x == 0) {
-        atomicOr(err, ERRF_TIMEOUT);
-        // let the copies still in flight land before the CTA exits
-        for (int s2 = st; s2 < issued; s2++) mbar_wait(bar0 + 8 * (s2 % CK_STAGES), (uint32_t)((s2 / CK_STAGES) & 1));
-      }
-      return;
-    }
-    if (threadIdx.x == 0 && issued < nst) {
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      issue_stage<QT>(smem + slot * S::stage, bar0 + 8 * slot, issued, nb, ntile, wtile, aslab, sslab);
-      issued++;
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * slot);
   }
   if (active) store_tile<CK_NJ>(acc, tile0 + wt, grp * Q8A_GROUP + pw, T, o, g, tg, err);
 }

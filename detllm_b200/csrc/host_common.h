@@ -117,6 +117,34 @@ struct ModelCfg {
 
 }  // namespace det
 
+namespace det {
+// Device-time profile of one forward (det_set_profiling): an event pair
+// around every launch, grouped by what the launch computes.
+enum ProfTag : int {
+  PT_EMBED,
+  PT_NORM,
+  PT_QUANT,
+  PT_GEMM_QKV,
+  PT_ROPE,
+  PT_ATTENTION,
+  PT_GEMM_O,
+  PT_GEMM_GATE_UP,
+  PT_SWIGLU,
+  PT_GEMM_DOWN,
+  PT_GEMM_OUT,
+  PT_CDF,
+  PT_COUNT
+};
+struct ProfTags {
+  double ms[PT_COUNT] = {};
+  uint64_t n[PT_COUNT] = {};
+};
+struct ProfEntry {
+  int tag;
+  double bytes, wbytes;  // algorithmic bytes of a weight GEMM (0 otherwise)
+};
+}  // namespace det
+
 struct det_model {
   int device = 0;
   det::ModelCfg cfg;
@@ -136,11 +164,13 @@ struct det_model {
   bool has_bias = false;
   size_t weight_bytes = 0;  // device bytes of all weight matrices
   det_stats agg{};          // stats of finished sessions
+  det::ProfTags prof_agg;   // per-kernel profile of finished sessions
   // session reused by the model-level entry points (encode / decode /
   // logits hash) so repeated calls skip allocation, RoPE table and graph
   // capture; those entry points are not re-entrant on one model
   det_session* cached = nullptr;
 };
+
 
 struct det_session {
   det_model* m = nullptr;
@@ -173,9 +203,10 @@ struct det_session {
   std::vector<uint8_t> cdf_ready;
   det_stats stats{};
   std::vector<void*> allocations;
-  // profiling: event pairs around GEMV launches, resolved at the next sync
+  // profiling: event pairs around launches, resolved at the next sync
   std::vector<cudaEvent_t> prof_events;
-  std::vector<std::pair<double, double>> prof_pending;  // (bytes, weight bytes) per recorded pair
+  std::vector<det::ProfEntry> prof_pending;
+  det::ProfTags prof;
 };
 
 namespace det {

@@ -83,7 +83,9 @@ struct Launch {
 cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,
                               float rope_base);
 cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* tokens, int T, float* x);
-cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h);
+// qd / qq non-null and n % 32 == 0: also writes the Q8A quantisation of h
+cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h,
+                           float* qd = nullptr, int8_t* qq = nullptr);
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
 cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
@@ -103,7 +105,9 @@ cudaError_t launch_attention_tiled(const Launch& L, const float* q, const float*
                                    float* out, float* S);
 // floats of global score scratch launch_attention needs (0: scores stay in smem)
 size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx);
-cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T);
+// qd / qq non-null and n % 32 == 0: also writes the Q8A quantisation of out
+cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T,
+                          float* qd = nullptr, int8_t* qq = nullptr);
 cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, const uint32_t* rows, int nrows,
                                float* e, float* z);
 cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,

@@ -158,14 +158,65 @@ __global__ void embed_kernel(DevMatrix m, const uint32_t* tokens, int T, float* 
   }
 }
 
+// ---- Q8A quantiser: try_quantize_q8a_block (det-quant lib.rs:111-137) ------
+// One warp quantises one 32-element block, lane l holding element l; amax by
+// shuffle (max is order-free); the output goes to the Q8A layout
+// (dev_math.cuh).  Callers have checked v for finiteness.
+DI void q8a_block_warp(float v, int l, int nbk, int t, int kb, float* __restrict__ qd, int8_t* __restrict__ qq) {
+  float amax = fabsf(v);
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  int q = 0;
+  float d = 0.0f;
+  if (amax != 0.0f) {
+    d = fdiv(amax, 127.0f);
+    const float s = fdiv(v, d);
+    int r = v < 0.0f ? __float2int_rz(fsub(s, 0.5f)) : __float2int_rz(fadd(s, 0.5f));
+    q = max(-127, min(127, r));
+  }
+  qq[q8a_elem(nbk, t, kb, l)] = (int8_t)q;
+  if (l == 0) qd[q8a_slot(nbk, t, kb)] = d;
+}
+
+// one warp per block of x (T x K, row-major)
+__global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, int nbk, float* __restrict__ qd,
+                                 int8_t* __restrict__ qq, uint32_t* err) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= nblocks) return;
+  const int l = threadIdx.x & 31;
+  const int t = b / nbk, kb = b - t * nbk;
+  const float v = x[(size_t)b * 32 + l];
+  if (!finite(v)) flag(err, ERRF_NONFINITE);
+  q8a_block_warp(v, l, nbk, t, kb, qd, qq);
+}
+
+// swiglu (det-model lib.rs:2420-2434) with the Q8A quantisation of its
+// output fused in: one warp per 32-element block of the T x n output
+__global__ void swiglu_q8a_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
+                                  int nblocks, int nbk, float* __restrict__ qd, int8_t* __restrict__ qq,
+                                  uint32_t* err) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= nblocks) return;
+  const int l = threadIdx.x & 31;
+  const int t = b / nbk, kb = b - t * nbk;
+  const size_t i = (size_t)b * 32 + l;
+  const float gv = g[i], uv = u[i];
+  const float y = fmul(silu_det(gv), uv);
+  if (!finite(y) || !finite(gv) || !finite(uv)) flag(err, ERRF_NONFINITE);
+  out[i] = y;
+  q8a_block_warp(y, l, nbk, t, kb, qd, qq);
+}
+
 // ---- rmsnorm (det-model lib.rs:2053-2073) ----------------------------------
 // sum_squares_f32_ref: lane l accumulates x[i]^2 for i = l (mod 8) in order.
 // The row is staged in shared memory by all threads (coalesced), then eight
 // threads run the eight ordered lane chains out of shared memory.
 constexpr int RMS_MAX_SMEM = 16384;  // floats staged per row (larger rows read global)
 
+// When qd / qq are given (n a multiple of 32), the normalised row is also
+// quantised to Q8A: warp w takes blocks w, w + 8, ... of the row.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
-                               float* __restrict__ h, uint32_t* err) {
+                               float* __restrict__ h, float* __restrict__ qd, int8_t* __restrict__ qq,
+                               uint32_t* err) {
   extern __shared__ float xs[];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * n;
@@ -199,37 +250,24 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   }
   __syncthreads();
   const float r = r_s;
+  if (qq) {
+    const int nbk = n / 32, l = threadIdx.x & 31;
+    for (int kb = threadIdx.x >> 5; kb < nbk; kb += blockDim.x >> 5) {
+      const int i = kb * 32 + l;
+      const float xi = src[i];
+      const float v = fmul(fmul(xi, r), w[i]);
+      if (!finite(v) || !finite(xi)) flag(err, ERRF_NONFINITE);
+      h[(size_t)t * n + i] = v;
+      q8a_block_warp(v, l, nbk, t, kb, qd, qq);
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float xi = xr[i];
+    const float xi = src[i];
     const float v = fmul(fmul(xi, r), w[i]);
     if (!finite(v) || !finite(xi)) flag(err, ERRF_NONFINITE);
     h[(size_t)t * n + i] = v;
   }
-}
-
-// ---- Q8A quantiser: try_quantize_q8a_block (det-quant lib.rs:111-137) ------
-// one warp per 32-element block; amax by shuffle (max is order-free); the
-// output goes to the Q8A layout (dev_math.cuh)
-__global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, int nbk, float* __restrict__ qd,
-                                 int8_t* __restrict__ qq, uint32_t* err) {
-  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (b >= nblocks) return;
-  const int l = threadIdx.x & 31;
-  const int t = b / nbk, kb = b - t * nbk;
-  const float v = x[(size_t)b * 32 + l];
-  if (!finite(v)) flag(err, ERRF_NONFINITE);
-  float amax = fabsf(v);
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  int q = 0;
-  float d = 0.0f;
-  if (amax != 0.0f) {
-    d = fdiv(amax, 127.0f);
-    const float s = fdiv(v, d);
-    int r = v < 0.0f ? __float2int_rz(fsub(s, 0.5f)) : __float2int_rz(fadd(s, 0.5f));
-    q = max(-127, min(127, r));
-  }
-  qq[q8a_elem(nbk, t, kb, l)] = (int8_t)q;
-  if (l == 0) qd[q8a_slot(nbk, t, kb)] = d;
 }
 
 // ---- Q8_K quantiser: try_quantize_q8k_block (det-quant lib.rs:139-172) ----
@@ -834,13 +872,15 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
   return post(L);
 }
 
-cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h) {
+cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h,
+                           float* qd, int8_t* qq) {
   const size_t smem = n <= RMS_MAX_SMEM ? (size_t)n * sizeof(float) : 0;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  rmsnorm_kernel<<<T, 256, smem, L.stream>>>(x, w, n, eps, h, L.err);
+  if (n % 32) qd = nullptr, qq = nullptr;
+  rmsnorm_kernel<<<T, 256, smem, L.stream>>>(x, w, n, eps, h, qd, qq, L.err);
   return post(L);
 }
 
@@ -932,7 +972,13 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
   return post(L);
 }
 
-cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T) {
+cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float* out, int n, int T, float* qd,
+                          int8_t* qq) {
+  if (qq && n % 32 == 0) {
+    const int nb = T * (n / 32);
+    swiglu_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(g, u, out, nb, n / 32, qd, qq, L.err);
+    return post(L);
+  }
   const long long tot = (long long)n * T;
   swiglu_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, L.stream>>>(g, u, out, tot, L.err);
   return post(L);

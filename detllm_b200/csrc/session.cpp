@@ -7,6 +7,7 @@
 // for all n positions before the next op, which leaves each position's
 // arithmetic unchanged (each reduction stays within one position).
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 
 #include "host_common.h"
@@ -85,11 +86,28 @@ void add_stats(det_stats* a, const det_stats& b) {
   a->gemm_weight_bytes += b.gemm_weight_bytes;
 }
 
+void add_prof(ProfTags* a, const ProfTags& b) {
+  for (int i = 0; i < PT_COUNT; i++) {
+    a->ms[i] += b.ms[i];
+    a->n[i] += b.n[i];
+  }
+}
+
+bool is_gemm_tag(int tag) {
+  return tag == PT_GEMM_QKV || tag == PT_GEMM_O || tag == PT_GEMM_GATE_UP || tag == PT_GEMM_DOWN ||
+         tag == PT_GEMM_OUT;
+}
+
+const char* const kProfTagNames[PT_COUNT] = {"embed",  "rmsnorm",       "quantise", "gemm_qkv", "rope_store",
+                                             "attention", "gemm_o",     "gemm_gate_up", "swiglu", "gemm_down",
+                                             "gemm_output", "cdf"};
+
 void free_session(det_session* s) {
   if (!s) return;
   cudaSetDevice(s->m->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   add_stats(&s->m->agg, s->stats);
+  add_prof(&s->m->prof_agg, s->prof);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   for (auto& g : s->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
@@ -120,10 +138,15 @@ det_status take_error(det_session* s, bool cdf) {
   for (size_t i = 0; i < s->prof_pending.size(); i++) {
     float ms = 0.0f;
     if (cudaEventElapsedTime(&ms, s->prof_events[2 * i], s->prof_events[2 * i + 1]) == cudaSuccess) {
-      s->stats.gemm_ms += ms;
-      s->stats.gemm_launches++;
-      s->stats.gemm_bytes += s->prof_pending[i].first;
-      s->stats.gemm_weight_bytes += s->prof_pending[i].second;
+      const ProfEntry& pe = s->prof_pending[i];
+      s->prof.ms[pe.tag] += ms;
+      s->prof.n[pe.tag]++;
+      if (is_gemm_tag(pe.tag)) {
+        s->stats.gemm_ms += ms;
+        s->stats.gemm_launches++;
+        s->stats.gemm_bytes += pe.bytes;
+        s->stats.gemm_weight_bytes += pe.wbytes;
+      }
     }
   }
   s->prof_pending.clear();
@@ -137,27 +160,6 @@ det_status take_error(det_session* s, bool cdf) {
   if (f & ERRF_TIMEOUT) return DET_ERR_TIMEOUT;
   if (f) return DET_ERR_CUDA;
   return DET_OK;
-}
-
-// quantise `x` (T x K) for a matrix of type `type` into the session buffers
-cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float* x, int K, int T, DevActs* a,
-                         int* have) {
-  a->x = x;
-  if (needs_q8a(type) && !(*have & 1)) {
-    cudaError_t e = launch_quant_q8a(L, x, K, T, s->qa_d, s->qa_q);
-    if (e != cudaSuccess) return e;
-    *have |= 1;
-  }
-  if (type == GT_Q6_K && !(*have & 2)) {
-    cudaError_t e = launch_quant_q8k(L, x, K, T, s->qk_d, s->qk_q);
-    if (e != cudaSuccess) return e;
-    *have |= 2;
-  }
-  a->qa_d = s->qa_d;
-  a->qa_q = s->qa_q;
-  a->qk_d = s->qk_d;
-  a->qk_q = s->qk_q;
-  return cudaSuccess;
 }
 
 #define CK(expr)                                   \
@@ -176,11 +178,10 @@ double bytes_per_weight(int type) {
   }
 }
 
-// A weight GEMV/GEMM launch with optional per-launch event timing
-// (det_set_profiling); `launch` enqueues it.  Algorithmic bytes: weights,
-// quantised activations and outputs (read + write for residual outputs).
+// A launch with optional event timing (det_set_profiling); `launch`
+// enqueues it.  `bytes` / `wbytes`: algorithmic bytes of a weight GEMM.
 template <typename F>
-cudaError_t timed_gemm(det_session* s, const DevMatrix& W, int T, double out_bytes_per_pos, F&& launch) {
+cudaError_t timed(det_session* s, int tag, double bytes, double wbytes, F&& launch) {
   if (!g_profiling) return launch();
   const size_t i = s->prof_pending.size();
   while (s->prof_events.size() < 2 * (i + 1)) {
@@ -192,25 +193,66 @@ cudaError_t timed_gemm(det_session* s, const DevMatrix& W, int T, double out_byt
   cudaError_t e = cudaEventRecord(s->prof_events[2 * i], s->stream);
   if (e == cudaSuccess) e = launch();
   if (e == cudaSuccess) e = cudaEventRecord(s->prof_events[2 * i + 1], s->stream);
-  const double wbytes = (double)W.rows * W.cols * bytes_per_weight(W.type);
-  const double abytes = (double)T * W.cols *
-                        (W.type == GT_Q6_K ? 1.0 + 4.0 / 256.0 : (W.type == GT_F32 ? 4.0 : 1.0 + 4.0 / 32.0));
-  s->prof_pending.emplace_back(wbytes + abytes + (double)T * out_bytes_per_pos, wbytes);
+  s->prof_pending.push_back(ProfEntry{tag, bytes, wbytes});
   return e;
 }
 
-cudaError_t gemv(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T, float* out, int ld,
-                 int epi, const float* bias) {
-  return timed_gemm(s, W, T, W.rows * (epi == EPI_RESIDUAL ? 8.0 : 4.0),
+// A weight GEMV/GEMM launch: algorithmic bytes are the weights, the
+// quantised activations and the outputs (read + write for residual outputs).
+template <typename F>
+cudaError_t timed_gemm(det_session* s, int tag, const DevMatrix& W, int T, double out_bytes_per_pos, F&& launch) {
+  const double wbytes = (double)W.rows * W.cols * bytes_per_weight(W.type);
+  const double abytes = (double)T * W.cols *
+                        (W.type == GT_Q6_K ? 1.0 + 4.0 / 256.0 : (W.type == GT_F32 ? 4.0 : 1.0 + 4.0 / 32.0));
+  return timed(s, tag, wbytes + abytes + (double)T * out_bytes_per_pos, wbytes, launch);
+}
+
+cudaError_t gemv(det_session* s, int tag, const Launch& L, const DevMatrix& W, const DevActs& a, int T, float* out,
+                 int ld, int epi, const float* bias) {
+  return timed_gemm(s, tag, W, T, W.rows * (epi == EPI_RESIDUAL ? 8.0 : 4.0),
                     [&] { return launch_gemv(L, W, a, T, out, ld, epi, bias); });
 }
 
 // one launch over a fused (back-to-back) matrix
-cudaError_t gemm_fused(det_session* s, const Launch& L, const DevMatrix& W, const DevActs& a, int T,
+cudaError_t gemm_fused(det_session* s, int tag, const Launch& L, const DevMatrix& W, const DevActs& a, int T,
                        const OutSegs& o) {
   double ob = 0;
   for (int k = 0; k < o.n; k++) ob += o.s[k].rows * (o.s[k].epi == EPI_RESIDUAL ? 8.0 : 4.0);
-  return timed_gemm(s, W, T, ob, [&] { return launch_gemm_mma16(L, W, a, T, o); });
+  return timed_gemm(s, tag, W, T, ob, [&] { return launch_gemm_mma16(L, W, a, T, o); });
+}
+
+// quantise `x` (T x K) for a matrix of type `type` into the session buffers
+cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float* x, int K, int T, DevActs* a,
+                         int* have) {
+  a->x = x;
+  if (needs_q8a(type) && !(*have & 1)) {
+    cudaError_t e = timed(s, PT_QUANT, 0, 0, [&] { return launch_quant_q8a(L, x, K, T, s->qa_d, s->qa_q); });
+    if (e != cudaSuccess) return e;
+    *have |= 1;
+  }
+  if (type == GT_Q6_K && !(*have & 2)) {
+    cudaError_t e = timed(s, PT_QUANT, 0, 0, [&] { return launch_quant_q8k(L, x, K, T, s->qk_d, s->qk_q); });
+    if (e != cudaSuccess) return e;
+    *have |= 2;
+  }
+  a->qa_d = s->qa_d;
+  a->qa_q = s->qa_q;
+  a->qk_d = s->qk_d;
+  a->qk_q = s->qk_q;
+  return cudaSuccess;
+}
+
+// RMSNorm of x into s->h; when `q8a` (a consumer reads Q8A and K % 32 == 0)
+// the same launch writes the Q8A quantisation of h and marks it present
+cudaError_t norm(det_session* s, const Launch& L, const float* w, int K, int T, bool q8a, int* have) {
+  const ModelCfg& c = s->m->cfg;
+  q8a = q8a && K % 32 == 0;
+  cudaError_t e = timed(s, PT_NORM, 0, 0, [&] {
+    return q8a ? launch_rmsnorm(L, s->x, w, K, c.eps, T, s->h, s->qa_d, s->qa_q)
+               : launch_rmsnorm(L, s->x, w, K, c.eps, T, s->h);
+  });
+  if (q8a) *have |= 1;
+  return e;
 }
 
 // forward_one_with_workspace for positions pos0 .. pos0+T-1, pos0 = *d_pos
@@ -223,62 +265,73 @@ det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
   const int* pos0 = s->d_pos;
   const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
   const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
-  CK(launch_embed(L, m->tok_embd, s->d_tokens, T, s->x));
+  CK(timed(s, PT_EMBED, 0, 0, [&] { return launch_embed(L, m->tok_embd, s->d_tokens, T, s->x); }));
   for (int l = 0; l < c.L; l++) {
     const LayerDev& W = m->layers[(size_t)l];
-    CK(launch_rmsnorm(L, s->x, W.attn_norm, c.d, c.eps, T, s->h));
     DevActs a;
     int have = 0;
+    CK(norm(s, L, W.attn_norm, c.d, T, needs_q8a(W.wq.type) || needs_q8a(W.wk.type) || needs_q8a(W.wv.type),
+            &have));
     // one Q8A of h shared by q/k/v (:1284-1292); Q8_K recomputed per Q6_K
     // matrix in the reference gives the same blocks, so it is made once too
-    CK(quantise_for(s, L,W.wq.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L,W.wk.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L,W.wv.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L, W.wq.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L, W.wk.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L, W.wv.type, s->h, c.d, T, &a, &have));
     if (W.wqkv.rows) {
       OutSegs o;
       o.n = 3;
       o.s[0] = OutSeg{W.wq.rows, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq};
       o.s[1] = OutSeg{W.wk.rows, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk};
       o.s[2] = OutSeg{W.wv.rows, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv};
-      CK(gemm_fused(s, L, W.wqkv, a, T, o));
+      CK(gemm_fused(s, PT_GEMM_QKV, L, W.wqkv, a, T, o));
     } else {
-      CK(gemv(s, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
-      CK(gemv(s, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
-      CK(gemv(s, L, W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+      CK(gemv(s, PT_GEMM_QKV, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
+      CK(gemv(s, PT_GEMM_QKV, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
+      CK(gemv(s, PT_GEMM_QKV, L, W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
     }
     float* kc = s->kc + (size_t)l * kv_layer;
     float* vc = s->vc + (size_t)l * kv_layer;
-    CK(launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
-                         s->rope_sin, kc, vc, s->n_ctx));
-    CK(launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
-                        s->score_scratch));
+    CK(timed(s, PT_ROPE, 0, 0, [&] {
+      return launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
+                               s->rope_sin, kc, vc, s->n_ctx);
+    }));
+    CK(timed(s, PT_ATTENTION, 0, 0, [&] {
+      return launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
+                              s->score_scratch);
+    }));
     have = 0;
-    CK(quantise_for(s, L,W.wo.type, s->attn, qd, T, &a, &have));
-    CK(gemv(s, L,W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
-    CK(launch_rmsnorm(L, s->x, W.ffn_norm, c.d, c.eps, T, s->h));
+    CK(quantise_for(s, L, W.wo.type, s->attn, qd, T, &a, &have));
+    CK(gemv(s, PT_GEMM_O, L, W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
     have = 0;
-    CK(quantise_for(s, L,W.gate.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L,W.up.type, s->h, c.d, T, &a, &have));
+    CK(norm(s, L, W.ffn_norm, c.d, T, needs_q8a(W.gate.type) || needs_q8a(W.up.type), &have));
+    CK(quantise_for(s, L, W.gate.type, s->h, c.d, T, &a, &have));
+    CK(quantise_for(s, L, W.up.type, s->h, c.d, T, &a, &have));
     if (W.wgu.rows) {
       OutSegs o;
       o.n = 2;
       o.s[0] = OutSeg{W.gate.rows, s->gate, c.dff, EPI_STORE, nullptr};
       o.s[1] = OutSeg{W.up.rows, s->up, c.dff, EPI_STORE, nullptr};
-      CK(gemm_fused(s, L, W.wgu, a, T, o));
+      CK(gemm_fused(s, PT_GEMM_GATE_UP, L, W.wgu, a, T, o));
     } else {
-      CK(gemv(s, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
-      CK(gemv(s, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+      CK(gemv(s, PT_GEMM_GATE_UP, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
+      CK(gemv(s, PT_GEMM_GATE_UP, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
     }
-    CK(launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T));
     have = 0;
-    CK(quantise_for(s, L,W.down.type, s->ff, c.dff, T, &a, &have));
-    CK(gemv(s, L,W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+    // swiglu also quantises its output to Q8A when the down matrix reads it
+    const bool ff_q8a = needs_q8a(W.down.type) && c.dff % 32 == 0;
+    CK(timed(s, PT_SWIGLU, 0, 0, [&] {
+      return ff_q8a ? launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T, s->qa_d, s->qa_q)
+                    : launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T);
+    }));
+    if (ff_q8a) have |= 1;
+    CK(quantise_for(s, L, W.down.type, s->ff, c.dff, T, &a, &have));
+    CK(gemv(s, PT_GEMM_DOWN, L, W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
   }
-  CK(launch_rmsnorm(L, s->x, m->output_norm, c.d, c.eps, T, s->h));
   DevActs a;
   int have = 0;
-  CK(quantise_for(s, L,m->output.type, s->h, c.d, T, &a, &have));
-  CK(gemv(s, L, m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
+  CK(norm(s, L, m->output_norm, c.d, T, needs_q8a(m->output.type), &have));
+  CK(quantise_for(s, L, m->output.type, s->h, c.d, T, &a, &have));
+  CK(gemv(s, PT_GEMM_OUT, L, m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
   return DET_OK;
 }
 
@@ -337,7 +390,10 @@ det_status prepare_rows(det_session* s, const uint32_t* rows, uint32_t n) {
   std::memcpy(s->h_rows + 1024, need.data(), need.size() * 4);
   CK(cudaMemcpyAsync(s->d_rows, s->h_rows + 1024, need.size() * 4, cudaMemcpyHostToDevice, s->stream));
   s->stats.h2d_bytes += need.size() * 4;
-  CK(launch_cdf_prepare(launch_of(s), s->logits, s->m->vocab, s->d_rows, (int)need.size(), s->cdf_e, s->cdf_z));
+  CK(timed(s, PT_CDF, 0, 0, [&] {
+    return launch_cdf_prepare(launch_of(s), s->logits, s->m->vocab, s->d_rows, (int)need.size(), s->cdf_e,
+                              s->cdf_z);
+  }));
   return DET_OK;
 }
 
@@ -501,8 +557,10 @@ det_status det_symbol_ranges(det_session* s, const uint32_t* rows, const uint32_
     CK(cudaMemcpyAsync(s->d_rows + 1024, s->h_rows, cnt * 4, cudaMemcpyHostToDevice, s->stream));
     CK(cudaMemcpyAsync(s->d_syms, s->h_syms, cnt * 4, cudaMemcpyHostToDevice, s->stream));
     s->stats.h2d_bytes += cnt * 8;
-    CK(launch_cdf_ranges(launch_of(s), s->cdf_e, s->cdf_z, (int)V, tail, s->d_rows + 1024, s->d_syms, (int)cnt,
-                         s->d_out));
+    CK(timed(s, PT_CDF, 0, 0, [&] {
+      return launch_cdf_ranges(launch_of(s), s->cdf_e, s->cdf_z, (int)V, tail, s->d_rows + 1024, s->d_syms, (int)cnt,
+                              s->d_out);
+    }));
     CK(cudaEventRecord(s->ev[3], s->stream));
     CK(cudaMemcpyAsync(s->h_out, s->d_out, cnt * 24, cudaMemcpyDeviceToHost, s->stream));
     s->stats.d2h_bytes += cnt * 24;
@@ -539,7 +597,9 @@ det_status det_decoder_lookup(det_session* s, uint32_t row, int byte_escapes, ui
   if (det_status st = prepare_rows(s, &row, 1)) return st;
   *s->h_value = value;
   CK(cudaMemcpyAsync(s->d_value, s->h_value, 8, cudaMemcpyHostToDevice, s->stream));
-  CK(launch_decoder_lookup(launch_of(s), s->cdf_e, s->cdf_z, s->m->vocab, tail, row, s->d_value, s->d_out));
+  CK(timed(s, PT_CDF, 0, 0, [&] {
+    return launch_decoder_lookup(launch_of(s), s->cdf_e, s->cdf_z, s->m->vocab, tail, row, s->d_value, s->d_out);
+  }));
   CK(cudaMemcpyAsync(s->h_out, s->d_out, 32, cudaMemcpyDeviceToHost, s->stream));
   s->stats.h2d_bytes += 8;
   s->stats.d2h_bytes += 32;
@@ -616,6 +676,27 @@ det_status det_model_stats(det_model* m, det_stats* out, int reset) {
     if (reset) m->cached->stats = det_stats{};
   }
   if (reset) m->agg = det_stats{};
+  return DET_OK;
+}
+
+det_status det_model_profile(det_model* m, char* out, size_t cap, int reset) {
+  if (!m || (!out && cap)) return DET_ERR_INVALID_ARGUMENT;
+  ProfTags p = m->prof_agg;
+  if (m->cached) {
+    add_prof(&p, m->cached->prof);
+    if (reset) m->cached->prof = ProfTags{};
+  }
+  if (reset) m->prof_agg = ProfTags{};
+  std::string js = "{";
+  for (int i = 0; i < PT_COUNT; i++) {
+    char buf[128];
+    std::snprintf(buf, sizeof buf, "%s\"%s\": [%llu, %.6f]", i ? ", " : "", kProfTagNames[i],
+                  (unsigned long long)p.n[i], p.ms[i]);
+    js += buf;
+  }
+  js += "}";
+  if (js.size() + 1 > cap) return DET_ERR_INVALID_ARGUMENT;
+  std::memcpy(out, js.c_str(), js.size() + 1);
   return DET_OK;
 }
 

@@ -193,8 +193,13 @@ det_status det_session_stats(det_session* s, det_stats* out, int reset);
 /* sums of the stats of every session the model has run, including the ones
  * det_encode_symbols / det_compress / det_decompress / det_logits_hash make */
 det_status det_model_stats(det_model* model, det_stats* out, int reset);
-/* per-launch GEMV/GEMM timing (adds two event records per launch) */
+/* per-launch device timing of every kernel (adds two event records per
+ * launch and turns CUDA graphs off while enabled) */
 det_status det_set_profiling(int enable);
+/* The per-kernel profile gathered while profiling was enabled, summed over
+ * the model's sessions, as a JSON object {"<kernel group>": [launches,
+ * milliseconds], ...} written to out (cap bytes including the NUL). */
+det_status det_model_profile(det_model* model, char* out, size_t cap, int reset);
 
 /* ---- symbol ranges without allocation (no counterpart in the reference) --
  * For callers that cannot allocate device memory inside a call: code running
