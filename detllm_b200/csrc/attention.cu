@@ -30,6 +30,8 @@
 // 0 * v (v finite, the chain never -0) leaves an f32 sum unchanged.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "dev_math.cuh"
 #include "internal.h"
 
@@ -66,7 +68,8 @@ template <int HD>
 __global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __restrict__ q,
                                                                  const float* __restrict__ kc, const int* pos0p,
                                                                  int T, int n_head, int gsz, int qb, int n_ctx,
-                                                                 float scale, float* __restrict__ S, uint32_t* err) {
+                                                                 int s_ld, float scale, float* __restrict__ S,
+                                                                 uint32_t* err) {
   constexpr int RS = HD + 4;  // padded row stride (floats): conflict-free strided rows
   constexpr int PER = HD / 8; // elements per lane chain
   extern __shared__ float4 qk_smem[];
@@ -176,7 +179,7 @@ __global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __
     const int t = t0 + qi;
     const int len = pos0 + t + 1;
     if (len == 1) continue;  // score_len == 1 copies v_0 (no scores)
-    float* srow = S + ((size_t)t * n_head + kvh * gsz + hh) * n_ctx;
+    float* srow = S + ((size_t)t * n_head + kvh * gsz + hh) * s_ld;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
       const int j = j0 + jt + 16 * c;
@@ -189,25 +192,35 @@ __global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __
   }
 }
 
-// ---- softmax: one warp per row, in place ---------------------------------------
-constexpr int SM_ROWS_PER_CTA = 4;
+// ---- softmax: one warp per row ---------------------------------------------------
+// The row is staged in shared memory (when it fits) so the eight ordered z
+// chains read on-chip.  p_j is written back in place, and the row is zeroed
+// from its score length up to the end of the 32-key tile that the PV kernel
+// reads past it (at most 31 keys further).
+constexpr int SM_SMEM_FLOATS = 12288;  // largest staged row set per CTA
 
-__global__ void __launch_bounds__(SM_ROWS_PER_CTA * 32) attn_softmax_kernel(float* __restrict__ S, const int* pos0p,
-                                                                            int T, int n_head, int n_ctx,
-                                                                            uint32_t* err) {
+template <bool STAGED>
+__global__ void attn_softmax_kernel(float* __restrict__ S, const int* pos0p, int T, int n_head, int s_ld, int rpc,
+                                    uint32_t* err) {
+  extern __shared__ float sm_rows[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * SM_ROWS_PER_CTA + warp;
+  const int row = blockIdx.x * rpc + warp;
   if (row >= T * n_head) return;
   const int t = row / n_head;
   const int len = *pos0p + t + 1;
   if (len == 1) return;
-  float* s = S + (size_t)row * n_ctx;
+  float* s = S + (size_t)row * s_ld;
+  float* b = STAGED ? sm_rows + (size_t)warp * s_ld : s;
   float mx = -INFINITY;
-  for (int j = lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
+  for (int j = lane; j < len; j += 32) {
+    const float v = s[j];
+    if (STAGED) b[j] = v;
+    mx = fmaxf(mx, v);
+  }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   for (int j = lane; j < len; j += 32) {
-    const float d = fsub(s[j], mx);
-    s[j] = expf_det(d > -88.0f ? d : -88.0f);
+    const float d = fsub(b[j], mx);
+    b[j] = expf_det(d > -88.0f ? d : -88.0f);
   }
   __syncwarp();
   // sum_f32_ref: lane l < 8 runs the ordered chain over j = l, l + 8, ...
@@ -217,11 +230,11 @@ __global__ void __launch_bounds__(SM_ROWS_PER_CTA * 32) attn_softmax_kernel(floa
     for (; j + 56 < len; j += 64) {
       float e[8];
 #pragma unroll
-      for (int k = 0; k < 8; k++) e[k] = s[j + 8 * k];
+      for (int k = 0; k < 8; k++) e[k] = b[j + 8 * k];
 #pragma unroll
       for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
     }
-    for (; j < len; j += 8) acc = fadd(acc, s[j]);
+    for (; j < len; j += 8) acc = fadd(acc, b[j]);
   }
   float l8[8];
 #pragma unroll
@@ -232,34 +245,70 @@ __global__ void __launch_bounds__(SM_ROWS_PER_CTA * 32) attn_softmax_kernel(floa
     return;
   }
   for (int j = lane; j < len; j += 32) {
-    const float p = fdiv(s[j], z);
+    const float p = fdiv(b[j], z);
     if (!finite(p)) atomicOr(err, ERRF_NONFINITE);
     s[j] = p;
   }
+  const int zend = min(s_ld, (len + 31 + 31) & ~31);
+  for (int j = len + lane; j < zend; j += 32) s[j] = 0.0f;
 }
 
 // ---- P x V ----------------------------------------------------------------------
+// P and V tiles of PV_KEYS keys are double-buffered in shared memory with
+// cp.async; P stays row-major, so one 16-byte load gives 4 keys of a row.
 constexpr int PV_ROWS = 32;  // query-head rows per CTA
 constexpr int PV_KEYS = 32;  // keys per staged tile
+constexpr int PV_PS = PV_KEYS + 4;  // padded P row (floats)
+
+DI void cp_async16(void* sdst, const void* gsrc) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(sdst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+DI void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+DI void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 template <int HD>
 __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const float* __restrict__ P,
                                                                            const float* __restrict__ vc,
                                                                            const int* pos0p, int T, int n_head,
-                                                                           int gsz, int qb, int n_ctx,
+                                                                           int gsz, int qb, int n_ctx, int s_ld,
                                                                            float* __restrict__ out, uint32_t* err) {
   constexpr int NT = (PV_ROWS / 4) * (HD / 4);
-  __shared__ __align__(16) float ps[PV_KEYS][PV_ROWS + 4];  // p, transposed: 4 rows per 16 bytes
-  __shared__ __align__(16) float vs[PV_KEYS][HD];
+  __shared__ __align__(16) float ps[2][PV_ROWS][PV_PS];
+  __shared__ __align__(16) float vs[2][PV_KEYS][HD];
   const int pos0 = *pos0p;
   const int t0 = blockIdx.x * qb;
   const int kvh = blockIdx.y;
   const int tq = min(qb, T - t0);
   const int rows = tq * gsz;
-  const int jmax = pos0 + t0 + tq;
+  const int jmax = pos0 + t0 + tq;  // longest score row of the block
   const int tid = threadIdx.x;
   const int mt = tid / (HD / 4), dt = tid - mt * (HD / 4);
   const float* vb = vc + (size_t)kvh * n_ctx * HD;
+
+  // tile k -> buffer k & 1: P rows (zero past each row's length, written by
+  // the softmax), V rows below jmax (zeros above, never read from memory)
+  auto load_tile = [&](int k) {
+    const int jc = k * PV_KEYS, bf = k & 1;
+    for (int i = tid; i < PV_ROWS * (PV_KEYS / 4); i += NT) {
+      const int m = i / (PV_KEYS / 4), c4 = (i - m * (PV_KEYS / 4)) * 4;
+      if (m < rows) {
+        const int qi = m / gsz, hh = m - qi * gsz;
+        cp_async16(&ps[bf][m][c4], P + ((size_t)(t0 + qi) * n_head + kvh * gsz + hh) * s_ld + jc + c4);
+      }
+    }
+    for (int i = tid; i < PV_KEYS * (HD / 4); i += NT) {
+      const int jj = i / (HD / 4), d4 = (i - jj * (HD / 4)) * 4;
+      if (jc + jj < jmax)
+        cp_async16(&vs[bf][jj][d4], vb + (size_t)(jc + jj) * HD + d4);
+      else
+        *reinterpret_cast<float4*>(&vs[bf][jj][d4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
+  };
 
   float o[4][4];
 #pragma unroll
@@ -267,46 +316,39 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
 #pragma unroll
     for (int c = 0; c < 4; c++) o[r][c] = 0.0f;
 
-  for (int jc = 0; jc < jmax; jc += PV_KEYS) {
-    __syncthreads();  // previous tile consumed
-    // P tile: row m, keys jc.. (0 past the row's score length)
-    for (int i = tid; i < PV_ROWS * PV_KEYS; i += NT) {
-      const int m = i / PV_KEYS, jj = i - m * PV_KEYS;
-      float p = 0.0f;
-      if (m < rows) {
-        const int qi = m / gsz, hh = m - qi * gsz;
-        const int t = t0 + qi;
-        if (jc + jj < pos0 + t + 1) p = P[((size_t)t * n_head + kvh * gsz + hh) * n_ctx + jc + jj];
-      }
-      ps[jj][m] = p;
+  const int ntile = (jmax + PV_KEYS - 1) / PV_KEYS;
+  load_tile(0);
+  for (int k = 0; k < ntile; k++) {
+    if (k + 1 < ntile) {
+      load_tile(k + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    // V tile: rows jc.. (contiguous)
-    for (int i = tid; i < PV_KEYS * (HD / 4); i += NT) {
-      const int jj = i / (HD / 4), d4 = (i - jj * (HD / 4)) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (jc + jj < jmax) {
-        v = *reinterpret_cast<const float4*>(vb + (size_t)(jc + jj) * HD + d4);
-        if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
-      }
-      *reinterpret_cast<float4*>(&vs[jj][d4]) = v;
-    }
-    __syncthreads();
-    const int cnt = min(PV_KEYS, jmax - jc);
-#pragma unroll 4
-    for (int jj = 0; jj < cnt; jj++) {
-      const float4 p4 = *reinterpret_cast<const float4*>(&ps[jj][mt * 4]);
-      const float4 v4 = *reinterpret_cast<const float4*>(&vs[jj][dt * 4]);
-      const float pr[4] = {p4.x, p4.y, p4.z, p4.w};
+    __syncthreads();  // tile k visible to every thread
+    const int bf = k & 1;
+#pragma unroll 2
+    for (int jj = 0; jj < PV_KEYS; jj += 4) {
+      float4 p4[4], v4[4];
 #pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const float2 a = mul2(pr[r], pr[r], v4.x, v4.y);
-        const float2 b = mul2(pr[r], pr[r], v4.z, v4.w);
-        o[r][0] = fadd(o[r][0], a.x);
-        o[r][1] = fadd(o[r][1], a.y);
-        o[r][2] = fadd(o[r][2], b.x);
-        o[r][3] = fadd(o[r][3], b.y);
+      for (int r = 0; r < 4; r++) p4[r] = *reinterpret_cast<const float4*>(&ps[bf][mt * 4 + r][jj]);
+#pragma unroll
+      for (int c = 0; c < 4; c++) v4[c] = *reinterpret_cast<const float4*>(&vs[bf][jj + c][dt * 4]);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const float pr = c == 0 ? p4[r].x : c == 1 ? p4[r].y : c == 2 ? p4[r].z : p4[r].w;
+          const float2 a = mul2(pr, pr, v4[c].x, v4[c].y);
+          const float2 b = mul2(pr, pr, v4[c].z, v4[c].w);
+          o[r][0] = fadd(o[r][0], a.x);
+          o[r][1] = fadd(o[r][1], a.y);
+          o[r][2] = fadd(o[r][2], b.x);
+          o[r][3] = fadd(o[r][3], b.y);
+        }
       }
     }
+    __syncthreads();  // buffer k & 1 free for tile k + 2
   }
 #pragma unroll
   for (int r = 0; r < 4; r++) {
@@ -319,12 +361,18 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
     if (pos0 + t == 0) {  // score_len == 1 copies v_0 (lib.rs:2319-2322)
       v = *reinterpret_cast<const float4*>(vb + dt * 4);
     } else {
+      // a non-finite value of V below jmax reaches this row or the block's
+      // longest row (whose p_j are all > 0), as in the reference's check
       v = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
       if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
     }
     *reinterpret_cast<float4*>(ob) = v;
   }
 }
+
+// score rows are padded to whole 32-key tiles (16-byte aligned, and the PV
+// kernel's last tile stays inside the row)
+int score_ld(int n_ctx) { return (n_ctx + 31) & ~31; }
 
 template <int HD>
 constexpr int qk_smem_bytes() {
@@ -345,25 +393,33 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set |= 1ull << dev;
   }
+  const int s_ld = score_ld(n_ctx);
   dim3 g1((n_ctx + QK_KEYS - 1) / QK_KEYS, (T + qb - 1) / qb, n_head_kv);
-  attn_scores_kernel<HD><<<g1, QK_THREADS, smem, L.stream>>>(q, kc, pos0, T, n_head, gsz, qb, n_ctx, scale, S,
+  attn_scores_kernel<HD><<<g1, QK_THREADS, smem, L.stream>>>(q, kc, pos0, T, n_head, gsz, qb, n_ctx, s_ld, scale, S,
                                                              L.err);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows = T * n_head;
-  attn_softmax_kernel<<<(rows + SM_ROWS_PER_CTA - 1) / SM_ROWS_PER_CTA, SM_ROWS_PER_CTA * 32, 0, L.stream>>>(
-      S, pos0, T, n_head, n_ctx, L.err);
+  const int rpc = std::max(1, std::min(4, SM_SMEM_FLOATS / s_ld));
+  if (s_ld <= SM_SMEM_FLOATS) {
+    attn_softmax_kernel<true><<<(rows + rpc - 1) / rpc, rpc * 32, (size_t)rpc * s_ld * sizeof(float), L.stream>>>(
+        S, pos0, T, n_head, s_ld, rpc, L.err);
+  } else {
+    attn_softmax_kernel<false><<<(rows + 3) / 4, 4 * 32, 0, L.stream>>>(S, pos0, T, n_head, s_ld, 4, L.err);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int qb2 = PV_ROWS / gsz;
   dim3 g3((T + qb2 - 1) / qb2, n_head_kv);
-  attn_pv_kernel<HD><<<g3, (PV_ROWS / 4) * (HD / 4), 0, L.stream>>>(S, vc, pos0, T, n_head, gsz, qb2, n_ctx, out,
-                                                                    L.err);
+  attn_pv_kernel<HD><<<g3, (PV_ROWS / 4) * (HD / 4), 0, L.stream>>>(S, vc, pos0, T, n_head, gsz, qb2, n_ctx, s_ld,
+                                                                    out, L.err);
   if (L.launches) *L.launches += 3;
   return cudaGetLastError();
 }
 
 }  // namespace
+
+size_t attention_tiled_scratch_floats(int T, int n_head, int n_ctx) { return (size_t)T * n_head * score_ld(n_ctx); }
 
 bool attention_tiled_supported(int n_head, int n_head_kv, int head_dim) {
   if (n_head_kv <= 0 || n_head % n_head_kv) return false;

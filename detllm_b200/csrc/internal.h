@@ -100,6 +100,7 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
                              float* score_scratch);
 // tiled three-kernel attention (attention.cu) for head_dim 64 / 128
 bool attention_tiled_supported(int n_head, int n_head_kv, int head_dim);
+size_t attention_tiled_scratch_floats(int T, int n_head, int n_ctx);
 cudaError_t launch_attention_tiled(const Launch& L, const float* q, const float* kc, const float* vc, int T,
                                    const int* pos0, int n_head, int n_head_kv, int head_dim, int n_ctx, float scale,
                                    float* out, float* S);

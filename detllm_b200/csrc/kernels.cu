@@ -933,7 +933,7 @@ bool gqa_plan(int n_head, int n_head_kv, int hd, int n_ctx, size_t* smem, int* s
 }  // namespace
 
 size_t attention_scratch_floats(int T, int n_head, int n_head_kv, int hd, int n_ctx) {
-  if (attention_tiled_supported(n_head, n_head_kv, hd)) return (size_t)T * n_head * n_ctx;
+  if (attention_tiled_supported(n_head, n_head_kv, hd)) return attention_tiled_scratch_floats(T, n_head, n_ctx);
   size_t smem;
   int in_smem;
   if (gqa_plan(n_head, n_head_kv, hd, n_ctx, &smem, &in_smem)) return in_smem ? 0 : (size_t)T * n_head * n_ctx;
