@@ -51,6 +51,16 @@ DI float2 mul2(float a0, float a1, float b0, float b1) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
   return o;
 }
+// acc + p for two pairs, each rounded once: written as fma(p, one, acc) with
+// `one` == 1.0 a kernel argument, because a packed add fed by a packed
+// multiply is contracted into a fused multiply-add by the code generator
+DI float2 add_by_fma2(float2 p, float one, float2 acc) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(p.x, p.y)), "l"(pk2(one, one)), "l"(pk2(acc.x, acc.y)));
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+  return o;
+}
 
 // ---- scores -------------------------------------------------------------------
 constexpr int QK_ROWS = 64;  // query-head rows per CTA
@@ -64,6 +74,13 @@ DI int lm(int d) {
   return (d & 7) * (HD / 8) + (d >> 3);
 }
 
+// Shared-memory operands, both lane-major (element d of a row at lm(d)):
+//   Q: 32 pair-rows; pair-row P holds query-head rows (P & 15) + 32 (P >> 4)
+//      and that + 16 interleaved, element e at [2e] and [2e + 1];
+//   K: 64 key rows, every element stored twice ([2e] and [2e + 1]).
+// One 16-byte load of each then gives two elements for two rows x one key,
+// and the two rows' lane chains advance together: a packed multiply and a
+// packed fma(p, one, acc) (an exact add) per element pair.
 template <int HD>
 __global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __restrict__ q,
                                                                  const float* __restrict__ kc, const int* pos0p,
@@ -275,7 +292,8 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
                                                                            const float* __restrict__ vc,
                                                                            const int* pos0p, int T, int n_head,
                                                                            int gsz, int qb, int n_ctx, int s_ld,
-                                                                           float* __restrict__ out, uint32_t* err) {
+                                                                           float one, float* __restrict__ out,
+                                                                           uint32_t* err) {
   constexpr int NT = (PV_ROWS / 4) * (HD / 4);
   __shared__ __align__(16) float ps[2][PV_ROWS][PV_PS];
   __shared__ __align__(16) float vs[2][PV_KEYS][HD];
@@ -310,11 +328,9 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
     cp_async_commit();
   };
 
-  float o[4][4];
+  float2 o[4][2];  // rows mt*4 + r, dims (dt*4, +1) and (dt*4 + 2, +3)
 #pragma unroll
-  for (int r = 0; r < 4; r++)
-#pragma unroll
-    for (int c = 0; c < 4; c++) o[r][c] = 0.0f;
+  for (int r = 0; r < 4; r++) o[r][0] = o[r][1] = make_float2(0.f, 0.f);
 
   const int ntile = (jmax + PV_KEYS - 1) / PV_KEYS;
   load_tile(0);
@@ -339,12 +355,8 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
 #pragma unroll
         for (int r = 0; r < 4; r++) {
           const float pr = c == 0 ? p4[r].x : c == 1 ? p4[r].y : c == 2 ? p4[r].z : p4[r].w;
-          const float2 a = mul2(pr, pr, v4[c].x, v4[c].y);
-          const float2 b = mul2(pr, pr, v4[c].z, v4[c].w);
-          o[r][0] = fadd(o[r][0], a.x);
-          o[r][1] = fadd(o[r][1], a.y);
-          o[r][2] = fadd(o[r][2], b.x);
-          o[r][3] = fadd(o[r][3], b.y);
+          o[r][0] = add_by_fma2(mul2(pr, pr, v4[c].x, v4[c].y), one, o[r][0]);
+          o[r][1] = add_by_fma2(mul2(pr, pr, v4[c].z, v4[c].w), one, o[r][1]);
         }
       }
     }
@@ -363,7 +375,7 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
     } else {
       // a non-finite value of V below jmax reaches this row or the block's
       // longest row (whose p_j are all > 0), as in the reference's check
-      v = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
+      v = make_float4(o[r][0].x, o[r][0].y, o[r][1].x, o[r][1].y);
       if (!finite(v.x) || !finite(v.y) || !finite(v.z) || !finite(v.w)) atomicOr(err, ERRF_NONFINITE);
     }
     *reinterpret_cast<float4*>(ob) = v;
@@ -412,7 +424,7 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
   const int qb2 = PV_ROWS / gsz;
   dim3 g3((T + qb2 - 1) / qb2, n_head_kv);
   attn_pv_kernel<HD><<<g3, (PV_ROWS / 4) * (HD / 4), 0, L.stream>>>(S, vc, pos0, T, n_head, gsz, qb2, n_ctx, s_ld,
-                                                                    out, L.err);
+                                                                    1.0f, out, L.err);
   if (L.launches) *L.launches += 3;
   return cudaGetLastError();
 }

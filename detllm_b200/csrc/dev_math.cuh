@@ -377,9 +377,17 @@ DI float finish8(const float a[8]) {
 // 16-byte halves are swapped for positions with bit 2 set, which makes the
 // tensor-core B-fragment reads from shared memory bank-conflict free.  One
 // (group, block) slab is 2 KiB of quants and 256 B of f32 scales, so a GEMM
-// stage is a few contiguous bulk copies.
+// stage is a few contiguous bulk copies.  The 64 scales of a slab are
+// permuted within each half of 32 positions: position 8j + 2u + e sits at
+// 8u + 2j + e, so the tensor-core lane with column pair u reads the scales
+// of its positions (8j + 2u, +1), j = 0..3, as 8 contiguous floats.
 constexpr int Q8A_GROUP = 64;
 DI size_t q8a_slot(int nb, int t, int b) { return ((size_t)(t >> 6) * nb + b) * Q8A_GROUP + (t & 63); }
+DI int q8a_sperm(int p) { return (p & 32) | (((p >> 1) & 3) << 3) | (((p >> 3) & 3) << 1) | (p & 1); }
+// index of the scale of block b of position t
+DI size_t q8a_dslot(int nb, int t, int b) {
+  return ((size_t)(t >> 6) * nb + b) * Q8A_GROUP + q8a_sperm(t & 63);
+}
 DI int q8a_swz(int t) { return ((t >> 2) & 1) << 4; }
 // byte of element i (0..31) of block b of position t
 DI size_t q8a_elem(int nb, int t, int b, int i) { return q8a_slot(nb, t, b) * 32 + (size_t)(i ^ q8a_swz(t)); }

@@ -30,7 +30,7 @@
 // Chunk kernel (T > 16 positions): a CTA owns two 16-row tiles and one group
 // of 64 positions; each of its 4 compute warps owns 16 rows x 32 positions,
 // so one A fragment feeds four MMAs, and B fragments come from shared memory
-// by ldmatrix.  Each pipeline stage is SB blocks: the two tiles' SB weight
+// by ldmatrix.  Each pipeline stage is SB (8) blocks: the two tiles' SB weight
 // records, the SB (group, block) activation slabs and their scales --
 // contiguous ranges moved by TMA bulk copies (cp.async.bulk) that a producer
 // warp issues, completing on a "full" mbarrier; compute warps release a slot
@@ -74,16 +74,22 @@ DI float2 mul2(float2 a, float2 b) {
   return unpack2(r);
 }
 
+DI float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pack2(a)), "l"(pack2(b)), "l"(pack2(c)));
+  return unpack2(r);
+}
+
 // One fold step for two (row, position) pairs sharing a weight scale:
 //   acc += (d * ad) * isum      (two roundings in the product, one in the add)
-// The multiplies run packed; the accumulate uses scalar __fadd_rn.  (A packed
-// multiply feeding a packed add was contracted into a fused multiply-add by
-// the code generator, which changes the rounding; scalar __fadd_rn is never
-// contracted.)
-DI void fold2(float2& acc, float2 d, float2 adv, float2 iv) {
+// The multiplies run packed.  A packed add fed by a packed multiply is
+// contracted into a fused multiply-add by the code generator (one rounding
+// fewer), so the add is written as fma(c, one, acc) with `one` == 1.0 a
+// kernel argument: c * 1 is exact, the fma rounds once, like the add, and
+// the compiler cannot see that the multiplier is 1.
+DI void fold2(float2& acc, float2 d, float2 adv, float2 iv, float2 one) {
   const float2 c = mul2(mul2(d, adv), iv);
-  acc.x = __fadd_rn(acc.x, c.x);
-  acc.y = __fadd_rn(acc.y, c.y);
+  acc = fma2(c, one, acc);
 }
 
 template <int QT>
@@ -164,11 +170,25 @@ DI void store_tile(const float2 (&acc)[NJ][2], int tile, int pbase, int T, const
   }
 }
 
-// One n8 tile: B fragments of positions (pos .. pos+7) of block slab `ab`
-// (64 x 32 B, swizzled), their scales `sb`, and the fold into acc.
-DI void n8_step(const int (&a)[4], float2 dlo, float2 dhi, const uint8_t* ab, const float* sb, int pos, int g, int tg,
-                float2 (&acc)[2]) {
+// The activation scales of positions (pos + 2tg, +1) and (pos + 8 + 2tg, +1)
+// of a slab (pos a multiple of 16): adjacent in the permuted scale order.
+DI float4 adv_pair16(const float* sb, int pos, int tg) {
+  return *reinterpret_cast<const float4*>(sb + (pos & 32) + 8 * tg + ((pos & 16) >> 2));
+}
+
+// int32 MMA results (biased) -> exact f32 isums, then the two folds
+DI void fold_n8(const int (&c)[4], float2 dlo, float2 dhi, float2 adv, float2 one, float2 (&acc)[2]) {
   const float2 bias2 = make_float2(-12582912.0f, -12582912.0f);
+  const float2 i01 = add2(make_float2(__int_as_float(c[0]), __int_as_float(c[1])), bias2);
+  const float2 i23 = add2(make_float2(__int_as_float(c[2]), __int_as_float(c[3])), bias2);
+  fold2(acc[0], dlo, adv, i01, one);
+  fold2(acc[1], dhi, adv, i23, one);
+}
+
+// One n8 tile: B fragments of positions (pos .. pos+7) of block slab `ab`
+// (64 x 32 B, swizzled) from global memory, and the fold into acc.
+DI void n8_step(const int (&a)[4], float2 dlo, float2 dhi, const uint8_t* ab, float2 adv, int pos, int g, int tg,
+                float2 one, float2 (&acc)[2]) {
   const int pl = pos + g;
   const int swz = ((pl >> 2) & 1) << 4;
   const uint8_t* ap = ab + pl * 32 + tg * 4;
@@ -176,11 +196,7 @@ DI void n8_step(const int (&a)[4], float2 dlo, float2 dhi, const uint8_t* ab, co
   const int b1v = *reinterpret_cast<const int*>(ap + (16 ^ swz));
   int c[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
   mma_s8(c, a, b0v, b1v);
-  const float2 adv = *reinterpret_cast<const float2*>(sb + pos + 2 * tg);
-  const float2 i01 = add2(make_float2(__int_as_float(c[0]), __int_as_float(c[1])), bias2);
-  const float2 i23 = add2(make_float2(__int_as_float(c[2]), __int_as_float(c[3])), bias2);
-  fold2(acc[0], dlo, adv, i01);
-  fold2(acc[1], dhi, adv, i23);
+  fold_n8(c, dlo, dhi, adv, one, acc);
 }
 
 // B fragments of two n8 tiles (positions pos .. pos+15 of slab `ab`) with one
@@ -195,47 +211,51 @@ DI void ldsm_b_pair(const uint8_t* ab, int pos, int lane, int (&b)[4]) {
                : "r"(addr));
 }
 
-// MMA + fold of one n8 tile whose B fragments are already in registers
-DI void n8_fold(const int (&a)[4], float2 dlo, float2 dhi, int b0v, int b1v, const float* sb, int pos, int tg,
-                float2 (&acc)[2]) {
-  const float2 bias2 = make_float2(-12582912.0f, -12582912.0f);
-  int c[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
-  mma_s8(c, a, b0v, b1v);
-  const float2 adv = *reinterpret_cast<const float2*>(sb + pos + 2 * tg);
-  const float2 i01 = add2(make_float2(__int_as_float(c[0]), __int_as_float(c[1])), bias2);
-  const float2 i23 = add2(make_float2(__int_as_float(c[2]), __int_as_float(c[3])), bias2);
-  fold2(acc[0], dlo, adv, i01);
-  fold2(acc[1], dhi, adv, i23);
-}
-
-// one record against NJ n8 tiles starting at `pos`, B fragments by ldmatrix
-// (shared-memory slabs only)
-template <int QT, int NJ>
-DI void block_step_sm(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg,
-                      float2 (&acc)[NJ][2]) {
-  static_assert(NJ % 2 == 0, "n8 tiles come in ldmatrix pairs");
-  int a[4];
-  Rec<QT>::frag(r, lane, a);
-  const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
-  const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
-  int b[NJ / 2][4];
+// One chunk-kernel warp's work on NB blocks of a stage: 16 rows (one record
+// per block) x 32 positions starting at `pos` (0 or 32), B fragments by
+// ldmatrix.  All MMAs of the stage are issued first, then the folds run in
+// block order, so the MMA latency overlaps the previous folds.
+template <int QT, int NB>
+DI void stage_blocks(const uint8_t* wbuf, const uint8_t* abuf, const float* sbf, int pos, int lane, int g, int tg,
+                     float2 one, float2 (&acc)[4][2]) {
+  int c[NB][4][4];
 #pragma unroll
-  for (int j = 0; j < NJ / 2; j++) ldsm_b_pair(ab, pos + 16 * j, lane, b[j]);
+  for (int bb = 0; bb < NB; bb++) {
+    int a[4];
+    Rec<QT>::frag(wbuf + bb * Rec<QT>::bytes, lane, a);
+    int b[2][4];
+    ldsm_b_pair(abuf + bb * Q8A_GROUP * 32, pos, lane, b[0]);
+    ldsm_b_pair(abuf + bb * Q8A_GROUP * 32, pos + 16, lane, b[1]);
 #pragma unroll
-  for (int j = 0; j < NJ; j++) n8_fold(a, dlo, dhi, b[j >> 1][2 * (j & 1)], b[j >> 1][2 * (j & 1) + 1], sb, pos + 8 * j,
-                                       tg, acc[j]);
+    for (int j = 0; j < 4; j++) {
+      c[bb][j][0] = c[bb][j][1] = c[bb][j][2] = c[bb][j][3] = 0x4B400000;
+      mma_s8(c[bb][j], a, b[j >> 1][2 * (j & 1)], b[j >> 1][2 * (j & 1) + 1]);
+    }
+  }
+#pragma unroll
+  for (int bb = 0; bb < NB; bb++) {
+    const uint32_t sw = *reinterpret_cast<const uint32_t*>(wbuf + bb * Rec<QT>::bytes + Rec<QT>::qbytes + 4 * g);
+    const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
+    const float4 s0 = adv_pair16(sbf + bb * Q8A_GROUP, pos, tg);
+    const float4 s1 = adv_pair16(sbf + bb * Q8A_GROUP, pos + 16, tg);
+    fold_n8(c[bb][0], dlo, dhi, make_float2(s0.x, s0.y), one, acc[0]);
+    fold_n8(c[bb][1], dlo, dhi, make_float2(s0.z, s0.w), one, acc[1]);
+    fold_n8(c[bb][2], dlo, dhi, make_float2(s1.x, s1.y), one, acc[2]);
+    fold_n8(c[bb][3], dlo, dhi, make_float2(s1.z, s1.w), one, acc[3]);
+  }
 }
 
 // A fragment + scales of one record, then NJ n8 tiles starting at `pos`
-template <int QT, int NJ>
-DI void block_step(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg,
-                   float2 (&acc)[NJ][2]) {
+template <int QT>
+DI void block_step(const uint8_t* r, const uint8_t* ab, const float* sb, int pos, int lane, int g, int tg, float2 one,
+                   float2 (&acc)[2][2]) {
   int a[4];
   Rec<QT>::frag(r, lane, a);
-  const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
+  const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes) + g);
   const float2 dlo = make_float2(lo_half(sw), lo_half(sw)), dhi = make_float2(hi_half(sw), hi_half(sw));
-#pragma unroll
-  for (int j = 0; j < NJ; j++) n8_step(a, dlo, dhi, ab, sb, pos + 8 * j, g, tg, acc[j]);
+  const float4 s = adv_pair16(sb, pos, tg);
+  n8_step(a, dlo, dhi, ab, make_float2(s.x, s.y), pos, g, tg, one, acc[0]);
+  n8_step(a, dlo, dhi, ab, make_float2(s.z, s.w), pos + 8, g, tg, one, acc[1]);
 }
 
 // ---- small-T kernel (decode and short chunks): 4 warps per 16-row tile,
@@ -259,7 +279,7 @@ __global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t
   for (int b = 0; b < nb; b++) {
     const uint8_t* ab = reinterpret_cast<const uint8_t*>(aq) + (size_t)b * Q8A_GROUP * 32;  // group 0
     const float* sb = ad + (size_t)b * Q8A_GROUP;
-    block_step<QT, 2>(rec + (size_t)b * Rec<QT>::bytes, ab, sb, pw, lane, g, tg, acc);
+    block_step<QT>(rec + (size_t)b * Rec<QT>::bytes, ab, sb, pw, lane, g, tg, make_float2(o.one, o.one), acc);
   }
   store_tile<2>(acc, blockIdx.x, pw, T, o, g, tg, err);
 }
@@ -273,19 +293,22 @@ constexpr int CK_TILES = 2;   // 16-row tiles per CTA
 constexpr int CK_CWARPS = 4;  // compute warps
 constexpr int CK_THREADS = (CK_CWARPS + 1) * 32;
 constexpr int CK_NJ = 4;      // n8 tiles per compute warp (32 positions)
-constexpr int CK_SB = 4;      // blocks per stage
-constexpr int CK_STAGES = 4;
+// pipeline shape: SB blocks per stage, STAGES stages in flight
+template <int SB_, int STAGES_>
+struct CkCfg {
+  static constexpr int SB = SB_, STAGES = STAGES_;
+};
 constexpr unsigned long long kWaitNs = 2000000000ull;  // mbarrier wait bound (2 s)
 
-template <int QT>
+template <int QT, class C>
 struct ChunkSmem {
-  static constexpr int w_tile = CK_SB * Rec<QT>::bytes;
+  static constexpr int w_tile = C::SB * Rec<QT>::bytes;
   static constexpr int w_bytes = CK_TILES * w_tile;
-  static constexpr int a_bytes = CK_SB * Q8A_GROUP * 32;
-  static constexpr int s_bytes = CK_SB * Q8A_GROUP * 4;
+  static constexpr int a_bytes = C::SB * Q8A_GROUP * 32;
+  static constexpr int s_bytes = C::SB * Q8A_GROUP * 4;
   static constexpr int stage = w_bytes + a_bytes + s_bytes;
-  static constexpr int bars = 2 * CK_STAGES * 8;
-  static constexpr int total = stage * CK_STAGES + bars;
+  static constexpr int bars = 2 * C::STAGES * 8;
+  static constexpr int total = stage * C::STAGES + bars;
 };
 
 DI uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -325,11 +348,11 @@ DI bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-template <int QT>
+template <int QT, class C>
 DI void issue_stage(uint8_t* sbuf, uint32_t bar, int st, int nb, int ntile, const uint8_t* wtile,
                     const int8_t* aslab, const float* sslab) {
-  using S = ChunkSmem<QT>;
-  const int b0 = st * CK_SB, nrec = min(CK_SB, nb - b0);
+  using S = ChunkSmem<QT, C>;
+  const int b0 = st * C::SB, nrec = min(C::SB, nb - b0);
   const uint32_t wb = (uint32_t)(nrec * Rec<QT>::bytes), abytes = (uint32_t)(nrec * Q8A_GROUP * 32),
                  sbytes = (uint32_t)(nrec * Q8A_GROUP * 4);
   mbar_expect_tx(bar, wb * ntile + abytes + sbytes);
@@ -339,23 +362,23 @@ DI void issue_stage(uint8_t* sbuf, uint32_t bar, int st, int nb, int ntile, cons
   bulk_g2s(smem_u32(sbuf + S::w_bytes + S::a_bytes), sslab + (size_t)b0 * Q8A_GROUP, sbytes, bar);
 }
 
-template <int QT>
+template <int QT, class C>
 __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* __restrict__ W, int tiles, int nb,
                                                                 const int8_t* __restrict__ aq,
                                                                 const float* __restrict__ ad, int T,
                                                                 const OutSegs o, uint32_t* err) {
-  using S = ChunkSmem<QT>;
+  using S = ChunkSmem<QT, C>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile0 = blockIdx.x * CK_TILES;
   const int ntile = min(CK_TILES, tiles - tile0);
   const int grp = blockIdx.y;  // 64-position group
-  const int nst = (nb + CK_SB - 1) / CK_SB;
-  const uint32_t full0 = smem_u32(smem + S::stage * CK_STAGES);
-  const uint32_t empty0 = full0 + 8 * CK_STAGES;
+  const int nst = (nb + C::SB - 1) / C::SB;
+  const uint32_t full0 = smem_u32(smem + S::stage * C::STAGES);
+  const uint32_t empty0 = full0 + 8 * C::STAGES;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < CK_STAGES; s++) {
+    for (int s = 0; s < C::STAGES; s++) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, CK_CWARPS);
     }
@@ -370,16 +393,16 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
     const float* sslab = ad + (size_t)grp * nb * Q8A_GROUP;
     int st = 0;
     for (; st < nst; st++) {
-      const int slot = st % CK_STAGES;
-      if (st >= CK_STAGES && !mbar_wait(empty0 + 8 * slot, (uint32_t)((st / CK_STAGES - 1) & 1))) {
+      const int slot = st % C::STAGES;
+      if (st >= C::STAGES && !mbar_wait(empty0 + 8 * slot, (uint32_t)((st / C::STAGES - 1) & 1))) {
         atomicOr(err, ERRF_TIMEOUT);
         break;
       }
-      issue_stage<QT>(smem + slot * S::stage, full0 + 8 * slot, st, nb, ntile, wtile, aslab, sslab);
+      issue_stage<QT, C>(smem + slot * S::stage, full0 + 8 * slot, st, nb, ntile, wtile, aslab, sslab);
     }
     // the CTA's shared memory must outlive every copy issued into it
-    for (int s2 = max(0, st - CK_STAGES); s2 < st; s2++)
-      mbar_wait(full0 + 8 * (s2 % CK_STAGES), (uint32_t)((s2 / CK_STAGES) & 1));
+    for (int s2 = max(0, st - C::STAGES); s2 < st; s2++)
+      mbar_wait(full0 + 8 * (s2 % C::STAGES), (uint32_t)((s2 / C::STAGES) & 1));
     return;
   }
 
@@ -388,13 +411,14 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
   const int wt = warp >> 1;        // this warp's tile within the CTA
   const int pw = 32 * (warp & 1);  // this warp's positions within the group
   const bool active = wt < ntile && grp * Q8A_GROUP + pw < T;
+  const float2 one = make_float2(o.one, o.one);
   float2 acc[CK_NJ][2];
 #pragma unroll
   for (int j = 0; j < CK_NJ; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
 
   for (int st = 0; st < nst; st++) {
-    const int slot = st % CK_STAGES;
-    if (!mbar_wait(full0 + 8 * slot, (uint32_t)((st / CK_STAGES) & 1))) {
+    const int slot = st % C::STAGES;
+    if (!mbar_wait(full0 + 8 * slot, (uint32_t)((st / C::STAGES) & 1))) {
       if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
       return;
     }
@@ -403,16 +427,13 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
       const uint8_t* wbuf = sbuf + wt * S::w_tile;
       const uint8_t* abuf = sbuf + S::w_bytes;
       const float* sbf = reinterpret_cast<const float*>(sbuf + S::w_bytes + S::a_bytes);
-      const int nblk = min(CK_SB, nb - st * CK_SB);
-      if (nblk == CK_SB) {
-#pragma unroll
-        for (int bb = 0; bb < CK_SB; bb++)
-          block_step_sm<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
-                                   lane, g, tg, acc);
+      const int nblk = min(C::SB, nb - st * C::SB);
+      if (nblk == C::SB) {
+        stage_blocks<QT, C::SB>(wbuf, abuf, sbf, pw, lane, g, tg, one, acc);
       } else {
         for (int bb = 0; bb < nblk; bb++)
-          block_step_sm<QT, CK_NJ>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw,
-                                   lane, g, tg, acc);
+          stage_blocks<QT, 1>(wbuf + bb * Rec<QT>::bytes, abuf + bb * Q8A_GROUP * 32, sbf + bb * Q8A_GROUP, pw, lane,
+                              g, tg, one, acc);
       }
     }
     __syncwarp();
@@ -421,22 +442,30 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
   if (active) store_tile<CK_NJ>(acc, tile0 + wt, grp * Q8A_GROUP + pw, T, o, g, tg, err);
 }
 
-template <int QT>
-cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
-  constexpr int smem = ChunkSmem<QT>::total;
+template <int QT, class C>
+cudaError_t launch_chunk_cfg(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
+  constexpr int smem = ChunkSmem<QT, C>::total;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(attr_set >> dev & 1ull)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_chunk_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_chunk_kernel<QT, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int tiles = (m.rows + 15) / 16;
   dim3 grid((tiles + CK_TILES - 1) / CK_TILES, (T + Q8A_GROUP - 1) / Q8A_GROUP);
-  gemm_chunk_kernel<QT><<<grid, CK_THREADS, smem, L.stream>>>((const uint8_t*)m.q, tiles, m.nb, a.qa_q, a.qa_d, T, o,
+  gemm_chunk_kernel<QT, C><<<grid, CK_THREADS, smem, L.stream>>>((const uint8_t*)m.q, tiles, m.nb, a.qa_q, a.qa_d, T, o,
                                                               L.err);
   return cudaGetLastError();
+}
+
+// 8 blocks per stage, 2 stages: 54 KB of shared memory, 4 CTAs per SM; the
+// 32 MMAs a warp issues per stage hide their latency behind the folds
+// (measured against 2..16 blocks per stage and 2..6 stages)
+template <int QT>
+cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
+  return launch_chunk_cfg<QT, CkCfg<8, 2>>(L, m, a, T, o);
 }
 
 }  // namespace

@@ -71,6 +71,9 @@ struct OutSeg {
 struct OutSegs {
   OutSeg s[kMaxOutSegs];
   int n = 0;
+  // 1.0, passed at run time: the GEMM writes its exact adds as fma(x, one,
+  // acc), which the compiler must not be able to simplify
+  float one = 1.0f;
 };
 
 struct Launch {

@@ -174,7 +174,7 @@ DI void q8a_block_warp(float v, int l, int nbk, int t, int kb, float* __restrict
     q = max(-127, min(127, r));
   }
   qq[q8a_elem(nbk, t, kb, l)] = (int8_t)q;
-  if (l == 0) qd[q8a_slot(nbk, t, kb)] = d;
+  if (l == 0) qd[q8a_dslot(nbk, t, kb)] = d;
 }
 
 // one warp per block of x (T x K, row-major)
@@ -341,7 +341,7 @@ DI float dot_row(const DevMatrix& m, const DevActs& a, int r, int t) {
           q4k_scale_min(blk + 4, sub, sc, mn);
           const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
           const int kb = b * 8 + sub;
-          const float a_d = a.qa_d[q8a_slot(nbk, t, kb)];
+          const float a_d = a.qa_d[q8a_dslot(nbk, t, kb)];
           const uint8_t* qs = blk + 16 + (sub >> 1) * 32;
           const int8_t* aq = a.qa_q + q8a_slot(nbk, t, kb) * 32;
           const int swz = q8a_swz(t);
