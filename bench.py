@@ -13,8 +13,11 @@ host range coder, through det_encode_symbols.
 * e2e: same tokens / max over ranks of the wall time of the C-ABI calls with
   host buffers (symbols in, payload out; host<->device copies and host range
   coding inside).
-* roofline: per-launch CUDA-event timing of the weight GEMV/GEMM kernels in
-  one profiled step (algorithmic bytes / time) against MEASURED_PEAKS.json.
+* roofline: the decode GEMV (one token per forward, after a 1024-token
+  prefix): algorithmic bytes of every weight GEMV launch / its CUDA-event
+  time, against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+  The chunked encode GEMM is FP32-pipe bound (its exact ordered fold) and
+  is reported separately under chunk_gemm with the per-kernel time shares.
 * cpu_baseline / --impl reference: the C restatement of the reference CPU
   path (oracle/, all host threads) on a bounded prefix of the same stream.
 
@@ -175,6 +178,40 @@ def oracle_sample(spec, gguf, tokens, budget_s=20.0):
     return s, dt, load_s
 
 
+def decode_probe(D, model, tokens, n_prefix=1024, n_steps=48):
+    """Single-token forwards (the decode path) after a 1024-token prefix:
+    device time per token with CUDA graphs, then one profiled pass that times
+    every weight GEMV launch (algorithmic bytes / event time)."""
+    out = {}
+    with model.session(n_ctx=N_CTX, max_chunk=512) as s:
+        for p in range(0, n_prefix, 512):
+            s.forward(tokens[p:p + 512], p)
+        pos = n_prefix
+        for _ in range(4):  # warm-up (graph capture for n = 1)
+            s.forward(tokens[pos:pos + 1], pos)
+            pos += 1
+        s.stats(reset=True)
+        for _ in range(n_steps):
+            s.forward(tokens[pos:pos + 1], pos)
+            pos += 1
+        st = s.stats(reset=True)
+        out["tokens_per_s"] = n_steps / (st.forward_ms / 1000.0)
+        out["ms_per_token"] = st.forward_ms / n_steps
+        D.set_profiling(True)
+        for _ in range(n_steps):
+            s.forward(tokens[pos:pos + 1], pos)
+            pos += 1
+        D.set_profiling(False)
+        pr = s.stats(reset=True)
+    out["gemv_launches"] = int(pr.gemm_launches)
+    out["gemv_ms_per_token"] = pr.gemm_ms / n_steps
+    out["gemv_bytes_per_launch"] = pr.gemm_bytes / max(pr.gemm_launches, 1)
+    out["gemv_ms_per_launch"] = pr.gemm_ms / max(pr.gemm_launches, 1)
+    out["gemv_gbs"] = pr.gemm_bytes / (pr.gemm_ms / 1000.0) / 1e9 if pr.gemm_ms > 0 else None
+    out["positions"] = f"{n_prefix}..{pos - 1}"
+    return out
+
+
 def run_reference(args):
     rank, ws, local = dist_init(args.gpus)
     if rank != 0:
@@ -246,6 +283,7 @@ def run(args):
     D.set_profiling(False)
     prof = model.stats(reset=True)
     kprof = model.profile(reset=True)
+    dec = decode_probe(D, model, tokens)
     if rank != 0:
         return
     total_tokens = N_TOKENS * args.steps * ws
@@ -262,12 +300,17 @@ def run(args):
         "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},
         "gpu_launches": int(st.launches),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak if achieved else None, "traffic": None,
-                     "kernel": "weight GEMV/GEMM (Q8_0 x Q8A)", "peak_kind": peak_kind,
-                     "launches": int(prof.gemm_launches), "ms_per_launch": prof.gemm_ms / max(prof.gemm_launches, 1),
-                     "bytes_per_launch": prof.gemm_bytes / max(prof.gemm_launches, 1),
-                     "share_of_device_time": prof.gemm_ms / max(prof.forward_ms + prof.cdf_ms, 1e-9)},
+        "roofline": {"bound": "hbm", "achieved": dec["gemv_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": dec["gemv_gbs"] / peak if dec["gemv_gbs"] else None, "traffic": None,
+                     "kernel": "decode GEMV (1 token, Q8_0 x Q8A, gemv_decode_kernel)", "peak_kind": peak_kind,
+                     "launches": dec["gemv_launches"], "ms_per_launch": dec["gemv_ms_per_launch"],
+                     "bytes_per_launch": dec["gemv_bytes_per_launch"]},
+        "decode": dec,
+        "chunk_gemm": {"bound": "fp32 pipe (exact ordered fold, 4 fp32 ops per weight per position)",
+                       "weight_stream_gbs": achieved, "launches": int(prof.gemm_launches),
+                       "ms_per_launch": prof.gemm_ms / max(prof.gemm_launches, 1),
+                       "bytes_per_launch": prof.gemm_bytes / max(prof.gemm_launches, 1),
+                       "share_of_device_time": prof.gemm_ms / max(prof.forward_ms + prof.cdf_ms, 1e-9)},
         "kernels": {k: {"launches": n, "ms": round(ms, 3), "share": round(ms / max(sum(v[1] for v in kprof.values()),
                                                                                   1e-9), 4)}
                     for k, (n, ms) in kprof.items() if n},

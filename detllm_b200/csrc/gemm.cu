@@ -38,6 +38,8 @@
 // (globaltimer); on timeout the kernel flags ERRF_TIMEOUT and stops.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "dev_math.cuh"
 #include "internal.h"
 
@@ -468,12 +470,152 @@ cudaError_t launch_chunk(const Launch& L, const DevMatrix& m, const DevActs& a, 
   return launch_chunk_cfg<QT, CkCfg<8, 2>>(L, m, a, T, o);
 }
 
+// ---- decode kernel (T <= 8, e.g. one token): weight stream at HBM rate ----------
+// One CTA per 16-row tile.  Thread 0 moves the tile's records (contiguous)
+// into shared memory with bulk copies on one mbarrier -- in passes of at most
+// DG_PASS_BYTES -- so each CTA has its whole tile in flight and several CTAs
+// per SM overlap.  The per-block products c_b = (d * ad) * isum are
+// independent: the 8 warps split the blocks (isums by MMA; the 8 columns are
+// the positions, zero past T) and leave c_b in shared memory.  Then one
+// thread per (row, position) runs the reference's ordered fold
+// sum = ((0 + c_0) + c_1) + ... with its loads batched ahead of the adds.
+constexpr int DG_WARPS = 8;
+constexpr int DG_THREADS = DG_WARPS * 32;
+constexpr int DG_PASS_BYTES = 112 * 1024;
+constexpr int DG_COPY_BYTES = 32 * 1024;  // one bulk copy
+
+template <int QT>
+struct DecodeSmem {
+  __host__ __device__ static int pass_recs(int nb) {
+    return nb < DG_PASS_BYTES / Rec<QT>::bytes ? nb : DG_PASS_BYTES / Rec<QT>::bytes;
+  }
+  __host__ __device__ static int recs_bytes(int nb) { return pass_recs(nb) * Rec<QT>::bytes; }
+  // products [T * 16][nb + 1] f32, then the staged activations: quants
+  // [nb][T][32 B] (as stored, halves swizzled) and scales [nb][T]
+  __host__ __device__ static int prod_off(int nb) { return recs_bytes(nb) + 16; }
+  __host__ __device__ static int act_off(int T, int nb) { return prod_off(nb) + T * 16 * (nb + 1) * 4; }
+  __host__ __device__ static int ads_off(int T, int nb) { return act_off(T, nb) + nb * T * 32; }
+  __host__ __device__ static int total(int T, int nb) { return ads_off(T, nb) + nb * T * 4; }
+};
+
+template <int QT>
+__global__ void __launch_bounds__(DG_THREADS) gemv_decode_kernel(const uint8_t* __restrict__ W, int nb,
+                                                                 const int8_t* __restrict__ aq,
+                                                                 const float* __restrict__ ad, int T,
+                                                                 const OutSegs o, uint32_t* err) {
+  using S = DecodeSmem<QT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int g = lane >> 2, tg = lane & 3;
+  const int precs = S::pass_recs(nb);
+  const uint32_t bar = smem_u32(smem + S::recs_bytes(nb));
+  float* prod = reinterpret_cast<float*>(smem + S::prod_off(nb));  // [T * 16][nb + 1]
+  uint8_t* act = smem + S::act_off(T, nb);
+  float* ads = reinterpret_cast<float*>(smem + S::ads_off(T, nb));
+  const int ps = nb + 1;
+  const uint8_t* tile = W + (size_t)blockIdx.x * nb * Rec<QT>::bytes;
+  const bool col = g < T;  // B column g = position g
+  const int swz = ((g >> 2) & 1) << 4;
+  const float bias = -12582912.0f;
+
+  // thread 0: bulk copies of the weight records [p0, p0 + nrec) of the tile
+  auto issue = [&](int p0, int nrec) {
+    const uint32_t bytes = (uint32_t)(nrec * Rec<QT>::bytes);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    mbar_expect_tx(bar, bytes);
+    for (uint32_t off = 0; off < bytes; off += DG_COPY_BYTES)
+      bulk_g2s(smem_u32(smem + off), tile + (size_t)p0 * Rec<QT>::bytes + off,
+               min(bytes - off, (uint32_t)DG_COPY_BYTES), bar);
+  };
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    issue(0, precs);
+  }
+  // the T positions' activations (group 0 of the Q8A layout), while the
+  // first weight pass is in flight
+  for (int i = tid; i < nb * T * 8; i += DG_THREADS) {
+    const int w = i & 7, bp = i >> 3, b = bp / T, p = bp - b * T;
+    reinterpret_cast<uint32_t*>(act)[i] = __ldg(reinterpret_cast<const uint32_t*>(aq + ((size_t)b * Q8A_GROUP + p) * 32) + w);
+  }
+  for (int i = tid; i < nb * T; i += DG_THREADS) {
+    const int b = i / T, p = i - b * T;
+    ads[i] = __ldg(ad + (size_t)b * Q8A_GROUP + q8a_sperm(p));
+  }
+  __syncthreads();
+  int pass = 0;
+  for (int p0 = 0; p0 < nb; p0 += precs, pass++) {
+    const int nrec = min(precs, nb - p0);
+    if (pass > 0 && tid == 0) issue(p0, nrec);
+    const bool ok = mbar_wait(bar, (uint32_t)(pass & 1));
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        atomicOr(err, ERRF_TIMEOUT);
+        mbar_wait(bar, (uint32_t)(pass & 1));  // let the copy land before the CTA exits
+      }
+      return;
+    }
+    for (int b = p0 + warp; b < p0 + nrec; b += DG_WARPS) {
+      const uint8_t* r = smem + (size_t)(b - p0) * Rec<QT>::bytes;
+      int a[4];
+      Rec<QT>::frag(r, lane, a);
+      const uint32_t sw = *reinterpret_cast<const uint32_t*>(r + Rec<QT>::qbytes + 4 * g);
+      const uint8_t* abk = act + ((size_t)b * T + g) * 32;
+      const int bv0 = col ? *reinterpret_cast<const int*>(abk + ((4 * tg) ^ swz)) : 0;
+      const int bv1 = col ? *reinterpret_cast<const int*>(abk + ((16 + 4 * tg) ^ swz)) : 0;
+      int c[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
+      mma_s8(c, a, bv0, bv1);
+      const float dl = lo_half(sw), dh = hi_half(sw);
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int p = 2 * tg + e;
+        if (p < T) {
+          const float adp = ads[b * T + p];
+          prod[(p * 16 + g) * ps + b] = fmul(fmul(dl, adp), fadd(__int_as_float(c[e]), bias));
+          prod[(p * 16 + g + 8) * ps + b] = fmul(fmul(dh, adp), fadd(__int_as_float(c[2 + e]), bias));
+        }
+      }
+    }
+    __syncthreads();  // records consumed / products complete
+  }
+  if (tid < 16 * T) {
+    const int p = tid >> 4, rr = tid & 15;
+    const float* pr = prod + (p * 16 + rr) * ps;
+    float sum = 0.0f;
+    int bb = 0;
+    for (; bb + 8 <= nb; bb += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = pr[bb + k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) sum = fadd(sum, v[k]);
+    }
+    for (; bb < nb; bb++) sum = fadd(sum, pr[bb]);
+    const SegView sg = seg_for(o, blockIdx.x * 16);
+    const int lr = blockIdx.x * 16 - sg.row0 + rr;
+    if (lr < sg.rows) store_out(sum, lr, p, sg, err);
+  }
+}
+
+template <int QT>
+cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
+  const int smem = DecodeSmem<QT>::total(T, m.nb);
+  cudaError_t e = cudaFuncSetAttribute(gemv_decode_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  gemv_decode_kernel<QT><<<(m.rows + 15) / 16, DG_THREADS, smem, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q,
+                                                                            a.qa_d, T, o, L.err);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   cudaError_t e;
   if (T > 16) {
     e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, o) : launch_chunk<GT_Q4_0>(L, m, a, T, o);
+  } else if (T <= 8 && (m.type == GT_Q8_0 ? DecodeSmem<GT_Q8_0>::total(T, m.nb)
+                                           : DecodeSmem<GT_Q4_0>::total(T, m.nb)) <= 200 * 1024) {
+    e = m.type == GT_Q8_0 ? launch_decode<GT_Q8_0>(L, m, a, T, o) : launch_decode<GT_Q4_0>(L, m, a, T, o);
   } else {
     const dim3 grid((m.rows + 15) / 16);
     if (m.type == GT_Q8_0)

@@ -97,7 +97,7 @@ def test_fixture_logits_hash(D, goldens, fixtures, name, chunk):
 
 
 @pytest.mark.parametrize("name", list(SPECS))
-@pytest.mark.parametrize("chunk", [1, 7, 24])
+@pytest.mark.parametrize("chunk", [1, 7, 12, 24])  # decode, decode (T <= 8), small-T and chunk GEMM paths
 def test_logits_bit_exact(D, oracle, models, name, chunk):
     spec = SPECS[name]
     toks = S.zipf_tokens(24, spec.vocab, seed=hash(name) % 1000)
