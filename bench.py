@@ -75,14 +75,9 @@ def barrier(ws):
 
 
 def all_max(x, ws):
-    if ws == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from detllm_b200 import segments as G
 
-    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return G.max_over_ranks(x, ws, device="cuda")
 
 
 def model_bytes(rank, ws):
