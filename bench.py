@@ -173,10 +173,13 @@ def oracle_sample(spec, gguf, tokens, budget_s=20.0):
     return s, dt, load_s
 
 
-def decode_probe(D, model, tokens, n_prefix=1024, n_steps=48):
+def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
     """Single-token forwards (the decode path) after a 1024-token prefix:
     device time per token with CUDA graphs, then one profiled pass that times
     every weight GEMV launch (algorithmic bytes / event time)."""
+    from detllm_b200 import synth as S
+
+    tokens = S.zipf_tokens(n_prefix + 2 * n_steps + 8, vocab, seed=11)
     out = {}
     with model.session(n_ctx=N_CTX, max_chunk=512) as s:
         for p in range(0, n_prefix, 512):
@@ -278,7 +281,7 @@ def run(args):
     D.set_profiling(False)
     prof = model.stats(reset=True)
     kprof = model.profile(reset=True)
-    dec = decode_probe(D, model, tokens)
+    dec = decode_probe(D, model, spec.vocab)
     if rank != 0:
         return
     total_tokens = N_TOKENS * args.steps * ws
