@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __
                                                                  int T, int n_head, int gsz, int qb, int n_ctx,
                                                                  int s_ld, float scale, float* __restrict__ S,
                                                                  uint32_t* err) {
+  pdl_enter();
   constexpr int RS = HD + 4;  // padded row stride (floats): conflict-free strided rows
   constexpr int PER = HD / 8; // elements per lane chain
   extern __shared__ float4 qk_smem[];
@@ -219,6 +220,7 @@ constexpr int SM_SMEM_FLOATS = 12288;  // largest staged row set per CTA
 template <bool STAGED>
 __global__ void attn_softmax_kernel(float* __restrict__ S, const int* pos0p, int T, int n_head, int s_ld, int rpc,
                                     uint32_t* err) {
+  pdl_enter();
   extern __shared__ float sm_rows[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * rpc + warp;
@@ -294,6 +296,7 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
                                                                            int gsz, int qb, int n_ctx, int s_ld,
                                                                            float one, float* __restrict__ out,
                                                                            uint32_t* err) {
+  pdl_enter();
   constexpr int NT = (PV_ROWS / 4) * (HD / 4);
   __shared__ __align__(16) float ps[2][PV_ROWS][PV_PS];
   __shared__ __align__(16) float vs[2][PV_KEYS][HD];
@@ -386,6 +389,128 @@ __global__ void __launch_bounds__((PV_ROWS / 4) * (HD / 4)) attn_pv_kernel(const
 // kernel's last tile stays inside the row)
 int score_ld(int n_ctx) { return (n_ctx + 31) & ~31; }
 
+// ---- decode (T <= 8): one CTA per softmax row, one thread per PV chain -----------
+// With a handful of query rows the per-row kernels above leave most of the
+// GPU idle.  The softmax gives each (position, head) row a CTA: exps by all
+// threads into shared memory, the eight ordered Z chains by eight threads,
+// p = e / Z by all.  PV gives each (KV head, 16 dims, position) a CTA with one
+// ordered chain o[d] += p_j v_j[d] per thread, over 32-key tiles of P and V
+// staged with cp.async (double-buffered); as in the chunked path the rows
+// are zero past their length, so whole tiles are summed exactly.
+constexpr int SD_THREADS = 256;
+constexpr int PD_KEYS = 32;
+constexpr int PD_DIMS = 16;
+
+__global__ void __launch_bounds__(SD_THREADS) attn_softmax_row_kernel(float* __restrict__ S, const int* pos0p,
+                                                                     int n_head, int s_ld, uint32_t* err) {
+  pdl_enter();
+  extern __shared__ float sm_row[];  // [s_ld]
+  __shared__ float red[SD_THREADS / 32];
+  __shared__ float lanes[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x;
+  const int t = row / n_head;
+  const int len = *pos0p + t + 1;
+  if (len == 1) return;
+  float* s = S + (size_t)row * s_ld;
+  float mx = -INFINITY;
+  for (int j = tid; j < len; j += SD_THREADS) {
+    const float v = s[j];
+    sm_row[j] = v;
+    mx = fmaxf(mx, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < SD_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+  for (int j = tid; j < len; j += SD_THREADS) {
+    const float d = fsub(sm_row[j], mx);
+    sm_row[j] = expf_det(d > -88.0f ? d : -88.0f);
+  }
+  __syncthreads();
+  if (tid < 8) {  // sum_f32_ref: the ordered chain of lane tid
+    float acc = 0.0f;
+    int j = tid;
+    for (; j + 56 < len; j += 64) {
+      float e[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) e[k] = sm_row[j + 8 * k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+    }
+    for (; j < len; j += 8) acc = fadd(acc, sm_row[j]);
+    lanes[tid] = acc;
+  }
+  __syncthreads();
+  const float z = finish8(lanes);
+  if (!finite(z) || z == 0.0f) {
+    if (tid == 0) atomicOr(err, ERRF_NONFINITE);
+    return;
+  }
+  for (int j = tid; j < len; j += SD_THREADS) {
+    const float p = fdiv(sm_row[j], z);
+    if (!finite(p)) atomicOr(err, ERRF_NONFINITE);
+    s[j] = p;
+  }
+  const int zend = min(s_ld, (len + 31 + 31) & ~31);
+  for (int j = len + tid; j < zend; j += SD_THREADS) s[j] = 0.0f;
+}
+
+template <int HD>
+__global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* __restrict__ vc, const int* pos0p,
+                                      int n_head, int gsz, int n_ctx, int s_ld, float* __restrict__ out,
+                                      uint32_t* err) {
+  pdl_enter();
+  __shared__ __align__(16) float ps[2][32][PD_KEYS];     // gsz <= 32 rows
+  __shared__ __align__(16) float vs[2][PD_KEYS][PD_DIMS];
+  const int kvh = blockIdx.x, d0 = blockIdx.y * PD_DIMS, t = blockIdx.z;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int h = tid / PD_DIMS, dd = tid - h * PD_DIMS;
+  const int len = *pos0p + t + 1;
+  const float* vb = vc + (size_t)kvh * n_ctx * HD;
+  float* ob = out + ((size_t)t * n_head + kvh * gsz + h) * HD + d0 + dd;
+  if (len == 1) {  // score_len == 1 copies v_0 (lib.rs:2319-2322)
+    *ob = vb[d0 + dd];
+    return;
+  }
+  const float* prow0 = P + ((size_t)t * n_head + kvh * gsz) * s_ld;
+  auto load_tile = [&](int k) {
+    const int jc = k * PD_KEYS, bf = k & 1;
+    for (int i = tid; i < gsz * (PD_KEYS / 4); i += nt) {
+      const int r = i / (PD_KEYS / 4), c4 = (i - r * (PD_KEYS / 4)) * 4;
+      cp_async16(&ps[bf][r][c4], prow0 + (size_t)r * s_ld + jc + c4);
+    }
+    for (int i = tid; i < PD_KEYS * (PD_DIMS / 4); i += nt) {
+      const int jj = i / (PD_DIMS / 4), c4 = (i - jj * (PD_DIMS / 4)) * 4;
+      if (jc + jj < len)
+        cp_async16(&vs[bf][jj][c4], vb + (size_t)(jc + jj) * HD + d0 + c4);
+      else
+        *reinterpret_cast<float4*>(&vs[bf][jj][c4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
+  };
+  float acc = 0.0f;
+  const int ntile = (len + PD_KEYS - 1) / PD_KEYS;
+  load_tile(0);
+  for (int k = 0; k < ntile; k++) {
+    if (k + 1 < ntile) {
+      load_tile(k + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int bf = k & 1;
+#pragma unroll 8
+    for (int jj = 0; jj < PD_KEYS; jj++) acc = fadd(acc, fmul(ps[bf][h][jj], vs[bf][jj][dd]));
+    __syncthreads();
+  }
+  if (!finite(acc)) atomicOr(err, ERRF_NONFINITE);
+  *ob = acc;
+}
+
 template <int HD>
 constexpr int qk_smem_bytes() {
   return (QK_ROWS + QK_KEYS) * (HD + 4) * (int)sizeof(float);
@@ -407,24 +532,51 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
   }
   const int s_ld = score_ld(n_ctx);
   dim3 g1((n_ctx + QK_KEYS - 1) / QK_KEYS, (T + qb - 1) / qb, n_head_kv);
-  attn_scores_kernel<HD><<<g1, QK_THREADS, smem, L.stream>>>(q, kc, pos0, T, n_head, gsz, qb, n_ctx, s_ld, scale, S,
-                                                             L.err);
+  {
+    const cudaError_t e_ = launch_k(L, attn_scores_kernel<HD>, g1, QK_THREADS, smem, q, kc, pos0, T, n_head, gsz, qb,
+        n_ctx, s_ld, scale, S, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows = T * n_head;
   const int rpc = std::max(1, std::min(4, SM_SMEM_FLOATS / s_ld));
+  if (T <= 8 && s_ld <= SM_SMEM_FLOATS) {  // decode: a CTA per row, a thread per PV chain
+    {
+      const cudaError_t e_ = launch_k(L, attn_softmax_row_kernel, rows, SD_THREADS, (size_t)s_ld * sizeof(float), S,
+                                      pos0, n_head, s_ld, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
+    {
+      const cudaError_t e_ = launch_k(L, attn_pv_decode_kernel<HD>, dim3(n_head_kv, HD / PD_DIMS, T), gsz * PD_DIMS, 0,
+                                      S, vc, pos0, n_head, gsz, n_ctx, s_ld, out, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
+    if (L.launches) *L.launches += 3;
+    return cudaGetLastError();
+  }
   if (s_ld <= SM_SMEM_FLOATS) {
-    attn_softmax_kernel<true><<<(rows + rpc - 1) / rpc, rpc * 32, (size_t)rpc * s_ld * sizeof(float), L.stream>>>(
-        S, pos0, T, n_head, s_ld, rpc, L.err);
+    {
+      const cudaError_t e_ = launch_k(L, attn_softmax_kernel<true>, (rows + rpc - 1) / rpc, rpc * 32,
+          (size_t)rpc * s_ld * sizeof(float),  S, pos0, T, n_head, s_ld, rpc, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
   } else {
-    attn_softmax_kernel<false><<<(rows + 3) / 4, 4 * 32, 0, L.stream>>>(S, pos0, T, n_head, s_ld, 4, L.err);
+    {
+      const cudaError_t e_ = launch_k(L, attn_softmax_kernel<false>, (rows + 3) / 4, 4 * 32, 0, S, pos0, T, n_head,
+          s_ld, 4, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int qb2 = PV_ROWS / gsz;
   dim3 g3((T + qb2 - 1) / qb2, n_head_kv);
-  attn_pv_kernel<HD><<<g3, (PV_ROWS / 4) * (HD / 4), 0, L.stream>>>(S, vc, pos0, T, n_head, gsz, qb2, n_ctx, s_ld,
-                                                                    1.0f, out, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, attn_pv_kernel<HD>, g3, (PV_ROWS / 4) * (HD / 4), 0, S, vc, pos0, T, n_head,
+        gsz, qb2, n_ctx, s_ld, 1.0f, out, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   if (L.launches) *L.launches += 3;
   return cudaGetLastError();
 }

@@ -370,6 +370,21 @@ DI float finish8(const float a[8]) {
   return fadd(fadd(fadd(a[0], a[1]), fadd(a[2], a[3])), fadd(fadd(a[4], a[5]), fadd(a[6], a[7])));
 }
 
+// ---- programmatic dependent launch -----------------------------------------
+// Kernels are launched with programmatic stream serialization, so a kernel
+// may start while its predecessor in the stream is still running.
+// pdl_wait() blocks until the predecessor grid has completed and its memory
+// writes are visible (it returns at once for a plain launch); every kernel
+// calls it before it reads or writes anything another kernel touches.
+// pdl_trigger() then lets the successor begin launching.  Only reads of
+// constant data (weights) may come before pdl_wait().
+DI void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+DI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+DI void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
 // ---- Q8A activation layout ---------------------------------------------------
 // Quantised activations of T positions x K elements are stored block-major
 // in groups of 64 positions: for group G and block b, 64 consecutive 32-byte

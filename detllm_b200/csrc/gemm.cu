@@ -269,6 +269,7 @@ __global__ void __launch_bounds__(SM_WARPS * 32) gemm_small_kernel(const uint8_t
                                                                    const int8_t* __restrict__ aq,
                                                                    const float* __restrict__ ad, int T,
                                                                    const OutSegs o, uint32_t* err) {
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tg = lane & 3;
   const int pw = warp * 16;  // positions pw .. pw+15 of the first 64-group
@@ -369,6 +370,7 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
                                                                 const int8_t* __restrict__ aq,
                                                                 const float* __restrict__ ad, int T,
                                                                 const OutSegs o, uint32_t* err) {
+  pdl_enter();
   using S = ChunkSmem<QT, C>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -457,8 +459,11 @@ cudaError_t launch_chunk_cfg(const Launch& L, const DevMatrix& m, const DevActs&
   }
   const int tiles = (m.rows + 15) / 16;
   dim3 grid((tiles + CK_TILES - 1) / CK_TILES, (T + Q8A_GROUP - 1) / Q8A_GROUP);
-  gemm_chunk_kernel<QT, C><<<grid, CK_THREADS, smem, L.stream>>>((const uint8_t*)m.q, tiles, m.nb, a.qa_q, a.qa_d, T, o,
-                                                              L.err);
+  {
+    const cudaError_t e_ = launch_k(L, gemm_chunk_kernel<QT, C>, grid, CK_THREADS, smem, (const uint8_t*)m.q, tiles,
+        m.nb, a.qa_q, a.qa_d, T, o, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -530,8 +535,9 @@ __global__ void __launch_bounds__(DG_THREADS) gemv_decode_kernel(const uint8_t* 
   if (tid == 0) {
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    issue(0, precs);
+    issue(0, precs);  // weights are constant: stream them before the predecessor ends
   }
+  pdl_enter();
   // the T positions' activations (group 0 of the Q8A layout), while the
   // first weight pass is in flight
   for (int i = tid; i < nb * T * 8; i += DG_THREADS) {
@@ -602,8 +608,11 @@ cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a,
   const int smem = DecodeSmem<QT>::total(T, m.nb);
   cudaError_t e = cudaFuncSetAttribute(gemv_decode_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  gemv_decode_kernel<QT><<<(m.rows + 15) / 16, DG_THREADS, smem, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q,
-                                                                            a.qa_d, T, o, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, gemv_decode_kernel<QT>, (m.rows + 15) / 16, DG_THREADS, smem,
+        (const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T, o, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -619,11 +628,17 @@ cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs
   } else {
     const dim3 grid((m.rows + 15) / 16);
     if (m.type == GT_Q8_0)
-      gemm_small_kernel<GT_Q8_0><<<grid, SM_WARPS * 32, 0, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T,
-                                                                        o, L.err);
+      {
+        const cudaError_t e_ = launch_k(L, gemm_small_kernel<GT_Q8_0>, grid, SM_WARPS * 32, 0, (const uint8_t*)m.q,
+            m.nb, a.qa_q, a.qa_d, T, o, L.err);
+        if (e_ != cudaSuccess) return e_;
+      }
     else
-      gemm_small_kernel<GT_Q4_0><<<grid, SM_WARPS * 32, 0, L.stream>>>((const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T,
-                                                                        o, L.err);
+      {
+        const cudaError_t e_ = launch_k(L, gemm_small_kernel<GT_Q4_0>, grid, SM_WARPS * 32, 0, (const uint8_t*)m.q,
+            m.nb, a.qa_q, a.qa_d, T, o, L.err);
+        if (e_ != cudaSuccess) return e_;
+      }
     e = cudaGetLastError();
   }
   if (L.launches) ++*L.launches;

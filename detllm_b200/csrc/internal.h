@@ -80,7 +80,30 @@ struct Launch {
   cudaStream_t stream;
   uint32_t* err;        // device error flag
   uint64_t* launches;   // host counter of kernels launched
+  // launch with programmatic stream serialization (see launch_k); used for
+  // short forwards, where launch latency dominates
+  bool pdl = false;
 };
+
+// Launch `kern` on L.stream, with programmatic stream serialization when
+// L.pdl (the kernel may then start before its predecessor finishes; every
+// kernel calls pdl_wait() first, see dev_math.cuh).  DETGPU_NO_PDL=1 turns
+// the attribute off everywhere.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(const Launch& L, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = L.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl && pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 // ---- launchers (kernels.cu) ------------------------------------------------
 cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,

@@ -7,6 +7,8 @@
 // session's device error flag, which the host turns into DET_ERR_NONFINITE.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "dev_math.cuh"
 #include "internal.h"
 
@@ -100,6 +102,7 @@ DI float q6k_value(const uint8_t* body, float d, int index) {
 // ---- RoPE table: RopeTables::llama (det-model lib.rs:813-846) ------------
 __global__ void rope_table_kernel(float* cos_t, float* sin_t, int positions, int half, int rope_dim,
                                   float rope_base) {
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)positions * half) return;
   const int pos = (int)(i / half), j = (int)(i % half);
@@ -113,6 +116,7 @@ __global__ void rope_table_kernel(float* cos_t, float* sin_t, int positions, int
 
 // ---- embedding row: write_row_validated (det-model lib.rs:667-746) --------
 __global__ void embed_kernel(DevMatrix m, const uint32_t* tokens, int T, float* x, uint32_t* err) {
+  pdl_enter();
   const int t = blockIdx.x;
   if (t >= T) return;
   const uint32_t tok = tokens[t];
@@ -180,6 +184,7 @@ DI void q8a_block_warp(float v, int l, int nbk, int t, int kb, float* __restrict
 // one warp per block of x (T x K, row-major)
 __global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, int nbk, float* __restrict__ qd,
                                  int8_t* __restrict__ qq, uint32_t* err) {
+  pdl_enter();
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= nblocks) return;
   const int l = threadIdx.x & 31;
@@ -194,6 +199,7 @@ __global__ void quant_q8a_kernel(const float* __restrict__ x, int nblocks, int n
 __global__ void swiglu_q8a_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
                                   int nblocks, int nbk, float* __restrict__ qd, int8_t* __restrict__ qq,
                                   uint32_t* err) {
+  pdl_enter();
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= nblocks) return;
   const int l = threadIdx.x & 31;
@@ -217,6 +223,7 @@ constexpr int RMS_MAX_SMEM = 16384;  // floats staged per row (larger rows read 
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
                                float* __restrict__ h, float* __restrict__ qd, int8_t* __restrict__ qq,
                                uint32_t* err) {
+  pdl_enter();
   extern __shared__ float xs[];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * n;
@@ -275,6 +282,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // the largest |x| (carried as (|x|, index) through the reduction).
 __global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, float* __restrict__ qd,
                                  int8_t* __restrict__ qq, uint32_t* err) {
+  pdl_enter();
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= nblocks) return;
   const int l = threadIdx.x & 31;
@@ -404,6 +412,7 @@ DI void epilogue_store(float v, int r, int t, float* out, int out_ld, int epi, c
 // grid: x = position-major tiles so consecutive CTAs share rows (L2 reuse)
 __global__ void gemv_generic_kernel(DevMatrix m, DevActs a, int T, float* out, int out_ld, int epi,
                                     const float* bias, uint32_t* err) {
+  pdl_enter();
   const int r = blockIdx.y * blockDim.x + threadIdx.x;
   const int t = blockIdx.x;
   if (r >= m.rows || t >= T) return;
@@ -415,6 +424,7 @@ __global__ void gemv_generic_kernel(DevMatrix m, DevActs a, int T, float* out, i
 __global__ void rope_store_kernel(float* q, float* k, const float* v, const int* pos0p, int n_head, int n_head_kv,
                                   int hd, int half, int pairing, const float* cos_t, const float* sin_t, float* kc,
                                   float* vc, int n_ctx, uint32_t* err) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int pos = *pos0p + t;
   const float* cs = cos_t + (size_t)pos * half;
@@ -463,6 +473,7 @@ __global__ void attention_kernel(const float* __restrict__ q, const float* __res
                                  const float* __restrict__ vc, const int* pos0p, int n_head, int n_head_kv, int hd,
                                  int n_ctx, float scale, float* __restrict__ out, float* __restrict__ scratch,
                                  int smem_scores, uint32_t* err) {
+  pdl_enter();
   extern __shared__ float sm[];
   __shared__ float red[32];
   __shared__ float lanes[8];
@@ -552,6 +563,7 @@ __global__ void __launch_bounds__(ATG_THREADS)
     attention_gqa_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                          const int* pos0p, int n_head, int n_head_kv, int hd, int n_ctx, float scale,
                          float* __restrict__ out, float* __restrict__ scratch, int smem_scores, uint32_t* err) {
+  pdl_enter();
   extern __shared__ __align__(16) float sm[];
   const int t = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
   const int gsz = n_head / n_head_kv, h0 = kvh * gsz;
@@ -674,6 +686,7 @@ __global__ void __launch_bounds__(ATG_THREADS)
 
 // ---- swiglu (det-model lib.rs:2420-2434) ---------------------------------
 __global__ void swiglu_kernel(const float* g, const float* u, float* out, long long n, uint32_t* err) {
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float gv = g[i], uv = u[i];
@@ -689,6 +702,7 @@ constexpr int CDF_CHUNK = 4096;  // floats per shared-memory chunk (multiple of 
 // per row: max, e_i = expf(max(l_i - m, -88)), Z = sum_f32_ref(e)
 __global__ void cdf_prepare_kernel(const float* __restrict__ logits, int V, const uint32_t* rows,
                                    float* __restrict__ e, float* __restrict__ z, uint32_t* err) {
+  pdl_enter();
   __shared__ float red[32];
   __shared__ float lanes[8];
   const uint32_t row = rows[blockIdx.x];
@@ -747,6 +761,7 @@ DI uint32_t freq_of(float e, float z) {  // ((e / Z) * 2^24) as u32 + 1
 // one CTA per query: (cum, freq, total) of symbols[i] under row rows[i]
 __global__ void cdf_ranges_kernel(const float* __restrict__ e, const float* __restrict__ z, int V, int tail,
                                   const uint32_t* rows, const uint32_t* symbols, uint64_t* out3, uint32_t* err) {
+  pdl_enter();
   __shared__ unsigned long long red[32];
   const uint32_t row = rows[blockIdx.x];
   const uint32_t sym = symbols[blockIdx.x];
@@ -781,6 +796,7 @@ __global__ void cdf_ranges_kernel(const float* __restrict__ e, const float* __re
 // (exact integer) frequencies.  out4 = {symbol, cum, freq, total}
 __global__ void decoder_lookup_kernel(const float* __restrict__ e, const float* __restrict__ z, int V, int tail,
                                       uint32_t row, const uint64_t* value_p, uint64_t* out4, uint32_t* err) {
+  pdl_enter();
   __shared__ unsigned long long wsum[32];
   __shared__ unsigned long long base_s;
   __shared__ int found;
@@ -854,6 +870,14 @@ cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n) 
 }
 
 // ---- launchers ---------------------------------------------------------------
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DETGPU_NO_PDL");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
 static inline cudaError_t post(const Launch& L) {
   if (L.launches) ++*L.launches;
   return cudaGetLastError();
@@ -862,13 +886,19 @@ static inline cudaError_t post(const Launch& L) {
 cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,
                               float rope_base) {
   const long long n = (long long)positions * half;
-  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, L.stream>>>(cos_t, sin_t, positions, half, rope_dim,
-                                                                       rope_base);
+  {
+    const cudaError_t e_ = launch_k(L, rope_table_kernel, (unsigned)((n + 255) / 256), 256, 0, cos_t, sin_t,
+        positions, half, rope_dim, rope_base);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* tokens, int T, float* x) {
-  embed_kernel<<<T, 256, 0, L.stream>>>(m, tokens, T, x, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, embed_kernel, T, 256, 0, m, tokens, T, x, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
@@ -880,19 +910,28 @@ cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int 
     if (e != cudaSuccess) return e;
   }
   if (n % 32) qd = nullptr, qq = nullptr;
-  rmsnorm_kernel<<<T, 256, smem, L.stream>>>(x, w, n, eps, h, qd, qq, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, rmsnorm_kernel, T, 256, smem, x, w, n, eps, h, qd, qq, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
   const int nb = T * (K / 32);
-  quant_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, K / 32, qd, qq, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, quant_q8a_kernel, (nb + 7) / 8, 256, 0, x, nb, K / 32, qd, qq, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
   const int nb = T * (K / 256);
-  quant_q8k_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(x, nb, qd, qq, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, quant_q8k_kernel, (nb + 7) / 8, 256, 0, x, nb, qd, qq, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
@@ -905,15 +944,21 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   cudaError_t e = launch_gemv_fast(L, m, a, T, out, out_ld, epi, bias, &handled);
   if (handled || e != cudaSuccess) return e;
   dim3 grid(T, (m.rows + 127) / 128);
-  gemv_generic_kernel<<<grid, 128, 0, L.stream>>>(m, a, T, out, out_ld, epi, bias, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, gemv_generic_kernel, grid, 128, 0, m, a, T, out, out_ld, epi, bias, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* v, int T, const int* pos0, int n_head,
                               int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
                               const float* sin_t, float* kc, float* vc, int n_ctx) {
-  rope_store_kernel<<<T, 256, 0, L.stream>>>(q, k, v, pos0, n_head, n_head_kv, head_dim, rope_dim / 2, pairing,
-                                             cos_t, sin_t, kc, vc, n_ctx, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, rope_store_kernel, T, 256, 0, q, k, v, pos0, n_head, n_head_kv, head_dim,
+        rope_dim / 2, pairing, cos_t, sin_t, kc, vc, n_ctx, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
@@ -955,8 +1000,11 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
       if (e != cudaSuccess) return e;
     }
     dim3 grid(T, n_head_kv);
-    attention_gqa_kernel<<<grid, ATG_THREADS, gsmem, L.stream>>>(q, kc, vc, pos0, n_head, n_head_kv, head_dim, n_ctx,
-                                                                 scale, out, score_scratch, gscores, L.err);
+    {
+      const cudaError_t e_ = launch_k(L, attention_gqa_kernel, grid, ATG_THREADS, gsmem, q, kc, vc, pos0, n_head,
+          n_head_kv, head_dim, n_ctx, scale, out, score_scratch, gscores, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
     return post(L);
   }
   const size_t need = (size_t)(head_dim + n_ctx) * sizeof(float);
@@ -967,8 +1015,11 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
     if (e != cudaSuccess) return e;
   }
   dim3 grid(T, n_head);
-  attention_kernel<<<grid, ATT_THREADS, smem, L.stream>>>(q, kc, vc, pos0, n_head, n_head_kv, head_dim, n_ctx,
-                                                          scale, out, score_scratch, smem_scores, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, attention_kernel, grid, ATT_THREADS, smem, q, kc, vc, pos0, n_head, n_head_kv,
+        head_dim, n_ctx, scale, out, score_scratch, smem_scores, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
@@ -976,29 +1027,44 @@ cudaError_t launch_swiglu(const Launch& L, const float* g, const float* u, float
                           int8_t* qq) {
   if (qq && n % 32 == 0) {
     const int nb = T * (n / 32);
-    swiglu_q8a_kernel<<<(nb + 7) / 8, 256, 0, L.stream>>>(g, u, out, nb, n / 32, qd, qq, L.err);
+    {
+      const cudaError_t e_ = launch_k(L, swiglu_q8a_kernel, (nb + 7) / 8, 256, 0, g, u, out, nb, n / 32, qd, qq, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
     return post(L);
   }
   const long long tot = (long long)n * T;
-  swiglu_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, L.stream>>>(g, u, out, tot, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, swiglu_kernel, (unsigned)((tot + 255) / 256), 256, 0, g, u, out, tot, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, const uint32_t* rows, int nrows,
                                float* e, float* z) {
-  cdf_prepare_kernel<<<nrows, CDF_THREADS, 0, L.stream>>>(logits, V, rows, e, z, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, cdf_prepare_kernel, nrows, CDF_THREADS, 0, logits, V, rows, e, z, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
                               const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3) {
-  cdf_ranges_kernel<<<n, CDF_THREADS, 0, L.stream>>>(e, z, V, tail, rows, symbols, out3, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, cdf_ranges_kernel, n, CDF_THREADS, 0, e, z, V, tail, rows, symbols, out3, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 
 cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
                                   const uint64_t* value, uint64_t* out4) {
-  decoder_lookup_kernel<<<1, 1024, 0, L.stream>>>(e, z, V, tail, row, value, out4, L.err);
+  {
+    const cudaError_t e_ = launch_k(L, decoder_lookup_kernel, 1, 1024, 0, e, z, V, tail, row, value, out4, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
   return post(L);
 }
 

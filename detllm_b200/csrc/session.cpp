@@ -262,6 +262,9 @@ det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
   const ModelCfg& c = m->cfg;
   Launch L = launch_of(s);
   L.launches = launch_counter;
+  // overlapping launches pays off for one-token (decode) forwards; for
+  // chunks it measured slower
+  L.pdl = T <= 16;
   const int* pos0 = s->d_pos;
   const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
   const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
