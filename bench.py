@@ -4,7 +4,7 @@
 Workload: a TinyLlama-1.1B-shaped decoder with
 random-init Q8_0 weights (22 layers, d 2048, 32/4 heads, FFN 5632, vocab
 32000), 4096 Zipf(1.1) token ids encoded as codec symbols at n_ctx 2048
-(overlap 512, one window rollover), forward chunk 512.  One step = one full
+(overlap 512, one window rollover), forward chunk 1024.  One step = one full
 compress of that stream: teacher-forced forward -> logits -> CDF ranges ->
 host range coder, through det_encode_symbols.
 
@@ -293,7 +293,7 @@ def run(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
         "data": "synthetic (seeded random-init weights, Zipf(1.1) tokens)",
         "config": {"workload": f"{CONFIG} encode: {N_TOKENS} Zipf tokens per rank, n_ctx {N_CTX}, overlap {OVERLAP}, "
-                               f"chunk {os.environ.get('DETGPU_CHUNK', '512')}", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
+                               f"chunk {os.environ.get('DETGPU_CHUNK', '1024')}", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
                    "parallelism": f"segments{ws}", "l2": "weights 1.17 GB per step > 126 MB L2 (no flush)"},
         "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},

@@ -31,7 +31,7 @@ uint32_t encode_chunk() {
   static const uint32_t c = [] {
     const char* e = std::getenv("DETGPU_CHUNK");
     const long v = e ? std::strtol(e, nullptr, 10) : 0;
-    return v >= 16 && v <= 1024 ? (uint32_t)v : 512u;
+    return v >= 16 && v <= 1024 ? (uint32_t)v : 1024u;
   }();
   return c;
 }
