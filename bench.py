@@ -42,6 +42,9 @@ CONFIG = "tinyllama-q8_0"
 N_TOKENS = 4096
 N_CTX = 2048
 OVERLAP = N_CTX // 4
+# --config: BASELINE.json configs 2-4 (tokens per rank, n_ctx)
+CONFIG_RUNS = {"tinyllama-q8_0": (4096, 2048), "tinyllama-q4_k_m": (4096, 2048),
+               "qwen2.5-0.5b-q8_0": (8192, 4096), "llama3-8b-q4_k": (4096, 8192)}
 METRIC = "encode tokens/s (logits+CDF+code)"
 
 
@@ -294,13 +297,14 @@ def run(args):
         "data": "synthetic (seeded random-init weights, Zipf(1.1) tokens)",
         "config": {"workload": f"{CONFIG} encode: {N_TOKENS} Zipf tokens per rank, n_ctx {N_CTX}, overlap {OVERLAP}, "
                                f"chunk {os.environ.get('DETGPU_CHUNK', '1024')}", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
-                   "parallelism": f"segments{ws}", "l2": "weights 1.17 GB per step > 126 MB L2 (no flush)"},
+                   "parallelism": f"segments{ws}",
+                   "l2": f"weights {S.weight_bytes_per_token(spec) / 1e9:.2f} GB streamed per chunk > 126 MB L2 (no flush)"},
         "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},
         "gpu_launches": int(st.launches),
         "roofline": {"bound": "hbm", "achieved": dec["gemv_gbs"], "peak": peak, "unit": "GB/s",
                      "frac": dec["gemv_gbs"] / peak if dec["gemv_gbs"] else None, "traffic": None,
-                     "kernel": "decode GEMV (1 token, Q8_0 x Q8A, gemv_decode_kernel)", "peak_kind": peak_kind,
+                     "kernel": f"decode weight GEMVs (1 token per forward, {CONFIG})", "peak_kind": peak_kind,
                      "launches": dec["gemv_launches"], "ms_per_launch": dec["gemv_ms_per_launch"],
                      "bytes_per_launch": dec["gemv_bytes_per_launch"]},
         "decode": dec,
@@ -325,7 +329,7 @@ def run(args):
 
 
 def main():
-    global N_TOKENS
+    global N_TOKENS, CONFIG, N_CTX, OVERLAP
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -333,10 +337,16 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--ref-sample", type=int, default=16, help="tokens per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tokens", type=int, default=N_TOKENS,
-                    help="tokens per rank per step (the benchmark uses 4096; smaller values are for profiling)")
+    ap.add_argument("--config", default=CONFIG, choices=sorted(CONFIG_RUNS),
+                    help="model configuration (default: the headline BASELINE config)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per rank per step (default: the config's; smaller values are for profiling)")
     args = ap.parse_args()
-    N_TOKENS = args.tokens
+    CONFIG = args.config
+    N_TOKENS, N_CTX = CONFIG_RUNS[CONFIG]
+    OVERLAP = N_CTX // 4
+    if args.tokens:
+        N_TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -82,7 +82,7 @@ DI int lm(int d) {
 // and the two rows' lane chains advance together: a packed multiply and a
 // packed fma(p, one, acc) (an exact add) per element pair.
 template <int HD>
-__global__ void __launch_bounds__(QK_THREADS) attn_scores_kernel(const float* __restrict__ q,
+__global__ void __launch_bounds__(QK_THREADS, 3) attn_scores_kernel(const float* __restrict__ q,
                                                                  const float* __restrict__ kc, const int* pos0p,
                                                                  int T, int n_head, int gsz, int qb, int n_ctx,
                                                                  int s_ld, float scale, float* __restrict__ S,
