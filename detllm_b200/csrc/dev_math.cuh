@@ -370,6 +370,36 @@ DI float finish8(const float a[8]) {
   return fadd(fadd(fadd(a[0], a[1]), fadd(a[2], a[3])), fadd(fadd(a[4], a[5]), fadd(a[6], a[7])));
 }
 
+// get_scale_min_k4 of a Q4_K super-block's 12 scale bytes: the 6-bit scale
+// and min of sub-block idx (det-quant lib.rs:506-518)
+DI void q4k_scale_min(const uint8_t* s, int idx, int& sc, int& mn) {
+  if (idx < 4) {
+    sc = s[idx] & 0x3f;
+    mn = s[idx + 4] & 0x3f;
+  } else {
+    sc = (s[idx + 4] & 0x0f) | ((s[idx - 4] >> 6) << 4);
+    mn = (s[idx + 4] >> 4) | ((s[idx] >> 6) << 4);
+  }
+}
+
+// q6_k_quant: the signed 6-bit value of element `index` (0..255) of a Q6_K
+// block body (ql[128] | qh[64] | scales[16]) (det-quant lib.rs:536-556)
+DI int q6k_quant(const uint8_t* body, int index) {
+  const int half = index >> 7, within = index & 127, l = within & 31, part = within >> 5;
+  const uint8_t* ql = body;
+  const uint8_t* qh = body + 128;
+  int v, shift;
+  switch (part) {
+    case 0: v = ql[half * 64 + l] & 0x0f; shift = 0; break;
+    case 1: v = ql[half * 64 + l + 32] & 0x0f; shift = 2; break;
+    case 2: v = ql[half * 64 + l] >> 4; shift = 4; break;
+    default: v = ql[half * 64 + l + 32] >> 4; shift = 6; break;
+  }
+  const int high = ((qh[half * 32 + l] >> shift) & 0x03) << 4;
+  return (v | high) - 32;
+}
+
+
 // ---- programmatic dependent launch -----------------------------------------
 // Kernels are launched with programmatic stream serialization, so a kernel
 // may start while its predecessor in the stream is still running.

@@ -114,6 +114,12 @@ cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int 
                            float* qd = nullptr, int8_t* qq = nullptr);
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
 cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
+// Q4_K matrix, chunk of T > 16 positions (gemm_kq.cu)
+cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                            int epi, const float* bias);
+// Q6_K matrix, chunk of T > 16 positions (gemm_kq.cu)
+cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                            int epi, const float* bias);
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,

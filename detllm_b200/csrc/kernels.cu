@@ -51,15 +51,6 @@ DI unsigned long long block_sum_u64(unsigned long long v, unsigned long long* re
 }
 
 // ---- dequantisation helpers (det-quant lib.rs:506-568) --------------------
-DI void q4k_scale_min(const uint8_t* s, int idx, int& sc, int& mn) {
-  if (idx < 4) {
-    sc = s[idx] & 0x3f;
-    mn = s[idx + 4] & 0x3f;
-  } else {
-    sc = (s[idx + 4] & 0x0f) | ((s[idx - 4] >> 6) << 4);
-    mn = (s[idx + 4] >> 4) | ((s[idx] >> 6) << 4);
-  }
-}
 
 // q4_k_value on a raw 144-byte super-block
 DI float q4k_value(const uint8_t* blk, int index) {
@@ -74,21 +65,6 @@ DI float q4k_value(const uint8_t* blk, int index) {
 }
 
 // q6_k_quant on a 208-byte body (ql[128] | qh[64] | scales[16])
-DI int q6k_quant(const uint8_t* body, int index) {
-  const int half = index >> 7, within = index & 127, l = within & 31, part = within >> 5;
-  const uint8_t* ql = body;
-  const uint8_t* qh = body + 128;
-  int v, shift;
-  switch (part) {
-    case 0: v = ql[half * 64 + l] & 0x0f; shift = 0; break;
-    case 1: v = ql[half * 64 + l + 32] & 0x0f; shift = 2; break;
-    case 2: v = ql[half * 64 + l] >> 4; shift = 4; break;
-    default: v = ql[half * 64 + l + 32] >> 4; shift = 6; break;
-  }
-  const int high = ((qh[half * 32 + l] >> shift) & 0x03) << 4;
-  return (v | high) - 32;
-}
-
 DI int q6k_scale_index(int index) {
   const int half = index >> 7, within = index & 127, l = within & 31, part = within >> 5;
   return half * 8 + (l >> 4) + 2 * part;
@@ -943,6 +919,8 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   bool handled = false;
   cudaError_t e = launch_gemv_fast(L, m, a, T, out, out_ld, epi, bias, &handled);
   if (handled || e != cudaSuccess) return e;
+  if (m.type == GT_Q4_K && T > 16) return launch_gemm_q4k(L, m, a, T, out, out_ld, epi, bias);
+  if (m.type == GT_Q6_K && T > 16) return launch_gemm_q6k(L, m, a, T, out, out_ld, epi, bias);
   dim3 grid(T, (m.rows + 127) / 128);
   {
     const cudaError_t e_ = launch_k(L, gemv_generic_kernel, grid, 128, 0, m, a, T, out, out_ld, epi, bias, L.err);

@@ -41,6 +41,11 @@ LONG_SPECS = {
                                    ctx=320, qkv_bias=True, rope_base=1e6, seed=22),
     "hd128_gqa2": S.ModelSpec(n_layer=1, d=256, d_ff=256, n_head=2, n_head_kv=1, vocab=512, ctx=320,
                               t_attn=S.GT_Q4_0, seed=23),
+    # Q4_K attention / gate / up and embedding, Q6_K down and output: the
+    # K-quant chunk path over several row tiles and position groups
+    "hd64_q4k_m": S.ModelSpec(n_layer=1, d=512, d_ff=768, n_head=8, n_head_kv=2, vocab=300, ctx=320,
+                              t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
+                              t_out=S.GT_Q6_K, seed=24),
 }
 
 
