@@ -275,7 +275,143 @@ __global__ void __launch_bounds__(K6_THREADS) gemm_q6k_kernel(const uint8_t* __r
   }
 }
 
+// ---- one position (decode) ---------------------------------------------------------
+// Q4_K: the reference's chain is sequential over all K elements, so each
+// thread runs one row's chain; the position's dequantised activations
+// (a.d * a.q, the reference's exact value) sit in shared memory, so the chain
+// only waits on its own f32 adds.
+constexpr int D4_THREADS = 128;
+
+__global__ void __launch_bounds__(D4_THREADS) gemv_q4k_decode_kernel(const uint8_t* __restrict__ W, int rows, int nbs,
+                                                                     const int8_t* __restrict__ aq,
+                                                                     const float* __restrict__ ad,
+                                                                     float* __restrict__ out, int epi,
+                                                                     const float* __restrict__ bias, uint32_t* err) {
+  pdl_enter();
+  extern __shared__ float act[];  // [K]
+  const int K = nbs * 256, nbk = nbs * 8;
+  for (int i = threadIdx.x; i < K; i += D4_THREADS) {
+    const int kb = i >> 5, e = i & 31;
+    act[i] = fmul(ad[q8a_dslot(nbk, 0, kb)], (float)aq[q8a_elem(nbk, 0, kb, e)]);
+  }
+  __syncthreads();
+  const int row = blockIdx.x * D4_THREADS + threadIdx.x;
+  if (row >= rows) return;
+  const uint8_t* w = W + (size_t)row * nbs * 144;
+  float sum = 0.0f;
+  for (int b = 0; b < nbs; b++) {
+    const uint8_t* blk = w + (size_t)b * 144;
+    const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+    uint8_t hb[16];
+    *reinterpret_cast<uint4*>(hb) = h;
+    const float d = f16_bits_to_f32((uint16_t)(hb[0] | (hb[1] << 8)));
+    const float dmin = f16_bits_to_f32((uint16_t)(hb[2] | (hb[3] << 8)));
+#pragma unroll 1
+    for (int pair = 0; pair < 4; pair++) {  // sub-blocks 2 pair, 2 pair + 1 share 32 quant bytes
+      uint32_t qw[8];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const uint4 v = *reinterpret_cast<const uint4*>(blk + 16 + pair * 32 + 16 * k);
+        qw[4 * k] = v.x; qw[4 * k + 1] = v.y; qw[4 * k + 2] = v.z; qw[4 * k + 3] = v.w;
+      }
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        const int sub = 2 * pair + half;
+        int sc, mn;
+        q4k_scale_min(hb + 4, sub, sc, mn);
+        const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+        const float* a = act + b * 256 + sub * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const int q = (int)((qw[i >> 2] >> (8 * (i & 3) + 4 * half)) & 0x0fu);
+          sum = fadd(sum, fmul(fsub(fmul(dsc, (float)q), dmn), a[i]));
+        }
+      }
+    }
+  }
+  if (!finite(sum)) atomicOr(err, ERRF_NONFINITE);
+  float v = sum;
+  if (epi == EPI_BIAS) {
+    v = fadd(v, bias[row]);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  } else if (epi == EPI_RESIDUAL) {
+    v = fadd(out[row], v);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  }
+  out[row] = v;
+}
+
+// Q6_K: the integer lane sums are order-free, so a warp takes a row and its
+// lanes split each block (lane l: elements 8 l .. 8 l + 7, one per lane
+// class ln), reduce the 8 class sums exactly with shuffles, and lane 0 keeps
+// the 8 f32 lane sums in block order.
+constexpr int D6_WARPS = 4;
+
+__global__ void __launch_bounds__(D6_WARPS * 32) gemv_q6k_decode_kernel(const uint8_t* __restrict__ W,
+                                                                        const uint16_t* __restrict__ Wd, int rows,
+                                                                        int nb, const int8_t* __restrict__ aq,
+                                                                        const float* __restrict__ ad,
+                                                                        float* __restrict__ out, int epi,
+                                                                        const float* __restrict__ bias,
+                                                                        uint32_t* err) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * D6_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint8_t* w = W + (size_t)row * nb * 208;
+  float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int b = 0; b < nb; b++) {
+    const uint8_t* body = w + (size_t)b * 208;
+    const int8_t* a = aq + (size_t)b * 256;
+    int aux[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int i = 8 * lane + k;  // ln = k
+      aux[k] = (int)(int8_t)body[192 + (i >> 4)] * (int)a[i] * q6k_quant(body, i);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      for (int o = 16; o > 0; o >>= 1) aux[k] += __shfl_xor_sync(0xffffffffu, aux[k], o);
+    const float dd = fmul(f16_bits_to_f32(Wd[(size_t)row * nb + b]), ad[b]);
+#pragma unroll
+    for (int k = 0; k < 8; k++) sums[k] = fadd(sums[k], fmul(dd, __int2float_rn(aux[k])));
+  }
+  if (lane != 0) return;
+  float v = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) v = fadd(v, sums[k]);
+  if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  if (epi == EPI_BIAS) {
+    v = fadd(v, bias[row]);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  } else if (epi == EPI_RESIDUAL) {
+    v = fadd(out[row], v);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  }
+  out[row] = v;
+}
+
 }  // namespace
+
+cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
+                                  const float* bias) {
+  cudaError_t e;
+  if (m.type == GT_Q4_K) {
+    const size_t smem = (size_t)m.nb * 256 * sizeof(float);
+    if (smem > 48 * 1024) {
+      e = cudaFuncSetAttribute(gemv_q4k_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    e = launch_k(L, gemv_q4k_decode_kernel, (m.rows + D4_THREADS - 1) / D4_THREADS, D4_THREADS, smem,
+                 (const uint8_t*)m.q, m.rows, m.nb, a.qa_q, a.qa_d, out, epi, bias, L.err);
+  } else {
+    e = launch_k(L, gemv_q6k_decode_kernel, (m.rows + D6_WARPS - 1) / D6_WARPS, D6_WARPS * 32, 0,
+                 (const uint8_t*)m.q, m.d, m.rows, m.nb, a.qk_q, a.qk_d, out, epi, bias, L.err);
+  }
+  if (e != cudaSuccess) return e;
+  if (L.launches) ++*L.launches;
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias) {

@@ -120,6 +120,9 @@ cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& 
 // Q6_K matrix, chunk of T > 16 positions (gemm_kq.cu)
 cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias);
+// Q4_K / Q6_K matrix, one position (gemm_kq.cu)
+cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
+                                  const float* bias);
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
