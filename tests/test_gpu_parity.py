@@ -165,6 +165,19 @@ def test_codec_bytes_synthetic(D, oracle, models, name, n_ctx):
     assert D.decompress(m, got) == data
 
 
+@pytest.mark.parametrize("name", ["hd64_gqa8", "hd64_q4k_m"])
+def test_codec_bytes_long_stream(D, oracle, long_models, name):
+    # several windows of 320 positions with 80-position replays: chunk GEMMs
+    # over several 64-position groups, tiled attention over several key
+    # tiles, and one-token forwards (decode kernels) in decompress
+    g = long_models[name][0]
+    data = S.markov_text(1500, seed=8)
+    m = D.Model(g)
+    got = D.compress(m, data, 320)
+    assert got == oracle.compress(g, data, 320)
+    assert D.decompress(m, got) == data
+
+
 def test_encode_symbols_streams(D, oracle, models):
     spec = SPECS["q8_0"]
     g = models["q8_0"]
