@@ -101,6 +101,7 @@ def lib():
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
             "det_set_profiling": (I, [I]),
             "det_model_profile": (I, [P, C.c_char_p, SZ, I]),
+            "det_session_gemv_stream": (I, [P, U32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
         }
         for name, (res, args) in sig.items():
@@ -278,6 +279,12 @@ class Session:
         _check(lib().det_decoder_lookup(self._h, row, int(byte_escapes), value, C.byref(sym), C.byref(r)),
                "det_decoder_lookup")
         return sym.value, r.cum, r.freq, r.total
+
+    def gemv_stream(self, reps: int = 20):
+        """(ms, bytes) per pass of the one-token weight GEMVs run back to back."""
+        ms, by = C.c_double(), C.c_double()
+        _check(lib().det_session_gemv_stream(self._h, reps, C.byref(ms), C.byref(by)), "det_session_gemv_stream")
+        return ms.value, by.value
 
     def stats(self, reset: bool = False) -> Stats:
         st = Stats()

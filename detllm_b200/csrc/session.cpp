@@ -664,6 +664,97 @@ det_status det_device_expf(int device, const float* x, float* y, size_t n) {
   return cuda_status(e);
 }
 
+det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per_pass, double* bytes_per_pass) {
+  if (!s || !ms_per_pass || !bytes_per_pass || reps == 0) return DET_ERR_INVALID_ARGUMENT;
+  det_model* m = s->m;
+  const ModelCfg& c = m->cfg;
+  cudaSetDevice(m->device);
+  // the weight GEMVs of one single-token forward, outputs into scratch rows
+  // (the logits and FFN buffers, which this call invalidates)
+  Launch L = launch_of(s);
+  uint64_t count = 0;
+  L.launches = &count;
+  L.pdl = true;
+  DevActs a;
+  a.x = s->h;
+  a.qa_d = s->qa_d;
+  a.qa_q = s->qa_q;
+  a.qk_d = s->qk_d;
+  a.qk_q = s->qk_q;
+  double bytes = 0;
+  auto add_bytes = [&](const DevMatrix& W) {
+    bytes += (double)W.rows * W.cols * bytes_per_weight(W.type) + W.cols * (1.0 + 4.0 / 32.0) + W.rows * 4.0;
+  };
+  auto enqueue = [&]() -> cudaError_t {
+    bytes = 0;
+    for (int l = 0; l < c.L; l++) {
+      const LayerDev& W = m->layers[(size_t)l];
+      cudaError_t e;
+      if (W.wqkv.rows) {
+        OutSegs o;
+        o.n = 1;
+        o.s[0] = OutSeg{W.wqkv.rows, s->logits, W.wqkv.rows, EPI_STORE, nullptr};
+        e = launch_gemm_mma16(L, W.wqkv, a, 1, o);
+        add_bytes(W.wqkv);
+      } else {
+        for (const DevMatrix* Wm : {&W.wq, &W.wk, &W.wv}) {
+          if ((e = launch_gemv(L, *Wm, a, 1, s->logits, Wm->rows, EPI_STORE, nullptr)) != cudaSuccess) return e;
+          add_bytes(*Wm);
+        }
+      }
+      if (e != cudaSuccess) return e;
+      if ((e = launch_gemv(L, W.wo, a, 1, s->gate, W.wo.rows, EPI_STORE, nullptr)) != cudaSuccess) return e;
+      add_bytes(W.wo);
+      if (W.wgu.rows) {
+        OutSegs o;
+        o.n = 1;
+        o.s[0] = OutSeg{W.wgu.rows, s->logits, W.wgu.rows, EPI_STORE, nullptr};
+        e = launch_gemm_mma16(L, W.wgu, a, 1, o);
+        add_bytes(W.wgu);
+      } else {
+        for (const DevMatrix* Wm : {&W.gate, &W.up}) {
+          if ((e = launch_gemv(L, *Wm, a, 1, s->logits, Wm->rows, EPI_STORE, nullptr)) != cudaSuccess) return e;
+          add_bytes(*Wm);
+        }
+      }
+      if (e != cudaSuccess) return e;
+      if ((e = launch_gemv(L, W.down, a, 1, s->gate, W.down.rows, EPI_STORE, nullptr)) != cudaSuccess) return e;
+      add_bytes(W.down);
+    }
+    add_bytes(m->output);
+    return launch_gemv(L, m->output, a, 1, s->logits, m->vocab, EPI_STORE, nullptr);
+  };
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  const cudaError_t eq = enqueue();
+  const cudaError_t ec = cudaStreamEndCapture(s->stream, &graph);
+  if (eq != cudaSuccess || ec != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return cuda_status(eq != cudaSuccess ? eq : ec);
+  }
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(ei);
+  cudaError_t e = cudaGraphLaunch(exec, s->stream);  // warm-up
+  if (e == cudaSuccess) e = cudaEventRecord(s->ev[2], s->stream);
+  for (uint32_t i = 0; i < reps && e == cudaSuccess; i++) e = cudaGraphLaunch(exec, s->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(s->ev[3], s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, s->ev[2], s->ev[3]);
+  cudaGraphExecDestroy(exec);
+  CK(e);
+  s->last_n = 0;  // the logits were overwritten
+  std::fill(s->cdf_ready.begin(), s->cdf_ready.end(), 0);
+  *ms_per_pass = (double)ms / reps;
+  *bytes_per_pass = bytes;
+  // the outputs are discarded: clear any flag their values raised
+  CK(cudaMemsetAsync(s->d_err, 0, 4, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  return DET_OK;
+}
+
 det_status det_session_stats(det_session* s, det_stats* out, int reset) {
   if (!s || !out) return DET_ERR_INVALID_ARGUMENT;
   *out = s->stats;

@@ -193,6 +193,14 @@ det_status det_session_stats(det_session* s, det_stats* out, int reset);
 /* sums of the stats of every session the model has run, including the ones
  * det_encode_symbols / det_compress / det_decompress / det_logits_hash make */
 det_status det_model_stats(det_model* model, det_stats* out, int reset);
+/* Weight-streaming rate of the one-token GEMVs in isolation: the weight
+ * GEMV launches of one single-token forward (every matrix of every layer and
+ * the lm_head, on the session's current activations) captured back to back
+ * in one CUDA graph with programmatic dependent launch, replayed `reps`
+ * times.  Returns the device time per pass and the algorithmic bytes per pass
+ * (weights + quantised activations + outputs).  Overwrites the session's
+ * logits: call det_forward again before det_symbol_ranges. */
+det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per_pass, double* bytes_per_pass);
 /* per-launch device timing of every kernel (adds two event records per
  * launch and turns CUDA graphs off while enabled) */
 det_status det_set_profiling(int enable);
