@@ -81,6 +81,7 @@ def lib():
             "det_status_string": (C.c_char_p, [I]),
             "det_device_count": (I, [C.POINTER(I)]),
             "det_model_load": (I, [P, SZ, I, C.POINTER(P)]),
+            "det_model_load_tp": (I, [P, SZ, P, I, C.POINTER(P)]),
             "det_model_free": (None, [P]),
             "det_model_info": (I, [P, C.POINTER(Config)]),
             "det_model_sha256": (I, [P, P]),
@@ -141,10 +142,21 @@ def _take(p: C.c_void_p, n: int) -> bytes:
 class Model:
     """``F32Llama::from_gguf`` on a B200: weights live in device memory."""
 
-    def __init__(self, gguf: bytes, device: int = 0):
+    def __init__(self, gguf: bytes, device: int = 0, devices=None):
+        """``devices``: a list of CUDA devices for a row-sharded
+        (tensor-parallel) model (``det_model_load_tp``; a device may repeat);
+        ``device`` is then ``devices[0]``."""
         self._keep = np.frombuffer(gguf, np.uint8)
         h = C.c_void_p()
-        _check(lib().det_model_load(_ptr(self._keep), len(gguf), device, C.byref(h)), "det_model_load")
+        if devices is None:
+            _check(lib().det_model_load(_ptr(self._keep), len(gguf), device, C.byref(h)), "det_model_load")
+            self.devices = [device]
+        else:
+            devs = np.ascontiguousarray(np.asarray(devices, dtype=np.int32))
+            _check(lib().det_model_load_tp(_ptr(self._keep), len(gguf), _ptr(devs), int(devs.size), C.byref(h)),
+                   "det_model_load_tp")
+            self.devices = [int(d) for d in devs]
+            device = self.devices[0]
         self._h = h
         del self._keep
         cfg = Config()

@@ -143,6 +143,22 @@ struct ProfEntry {
   int tag;
   double bytes, wbytes;  // algorithmic bytes of a weight GEMM (0 otherwise)
 };
+
+// Row-sharded tensor parallelism (tp.cpp).  Part p of a G-part model owns
+// rows [d0, d1) of wo and down, [f0, f1) of gate and up and [v0, v1) of the
+// lm_head: contiguous slices on 64-row boundaries, so every output row is
+// the same reduction as on one device.  When the KV heads divide evenly
+// (head_count_kv % G == 0) it also owns kv heads [h0, h1) with their query
+// heads, q/k/v rows and KV cache; otherwise every part runs the whole
+// attention block.
+struct TpShard {
+  int part = 0, parts = 1;
+  bool attn_sharded = false;
+  int d0 = 0, d1 = 0, f0 = 0, f1 = 0, v0 = 0, v1 = 0, h0 = 0, h1 = 0;
+  ModelCfg full;  // the unsharded configuration
+};
+struct TpModel;
+struct TpSession;
 }  // namespace det
 
 struct det_model {
@@ -169,11 +185,17 @@ struct det_model {
   // logits hash) so repeated calls skip allocation, RoPE table and graph
   // capture; those entry points are not re-entrant on one model
   det_session* cached = nullptr;
+  // tensor parallelism: `tp` on the model det_model_load_tp returns (its
+  // sessions are tensor-parallel); `shard` on the per-part models that view
+  // the replicas' weights (cfg then holds this part's head and FFN counts)
+  det::TpModel* tp = nullptr;
+  det::TpShard* shard = nullptr;
 };
 
 
 struct det_session {
   det_model* m = nullptr;
+  det_model* owner = nullptr;  // the model whose statistics this session adds to
   int n_ctx = 0, max_chunk = 0;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -207,10 +229,32 @@ struct det_session {
   std::vector<cudaEvent_t> prof_events;
   std::vector<det::ProfEntry> prof_pending;
   det::ProfTags prof;
+  // tensor parallelism: the gathered attention output / SwiGLU output of a
+  // part (full width), and on the session returned to the caller, the parts
+  float *attn_full = nullptr, *ff_full = nullptr;
+  det::TpSession* tp = nullptr;
 };
 
 namespace det {
 extern bool g_profiling;
+det_status cuda_status(cudaError_t e);
+// reads and clears a session's device error flag (synchronises its stream)
+det_status session_take_error(det_session* s, bool cdf);
+// forward stages (session.cpp); `have` carries which quantisations of the
+// FFN activation the SwiGLU launch already wrote
+det_status fwd_embed(det_session* s, const Launch& L, int T);
+det_status fwd_attention(det_session* s, const Launch& L, int l, int T);
+det_status fwd_attn_out(det_session* s, const Launch& L, int l, int T, const float* attn);
+det_status fwd_ffn_in(det_session* s, const Launch& L, int l, int T, int* have);
+det_status fwd_ffn_out(det_session* s, const Launch& L, int l, int T, const float* ff, int have);
+det_status fwd_head(det_session* s, const Launch& L, int T);
+// tensor parallelism (tp.cpp)
+void tp_model_free(det_model* m);
+det_status tp_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out);
+void tp_session_release(det_session* s);  // frees the other parts of a primary session
+det_status tp_run_forward(det_session* s, int T, bool graphs);
+det_status tp_reset(det_session* s);
+det_status tp_take_part_errors(det_session* s);  // error flags of the parts other than the primary
 // model-owned session for the model-level entry points (not re-entrant)
 det_status session_acquire(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out);
 void session_release_cached(det_model* m);

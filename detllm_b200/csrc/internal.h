@@ -149,6 +149,19 @@ cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, cons
 cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
                               const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3);
 cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n);
+// Row-sharded tensor parallelism (exchange.cu): copy column slices of
+// [T][ld] f32 activations that live on other parts (peer memory) into `dst`:
+// dst[p * ld_dst + col0 + c] = src[p * ld + c] for c < n, for every source.
+constexpr int kMaxTpParts = 8;
+struct GatherSrc {
+  const float* src;
+  int ld, col0, n;
+};
+struct GatherPlan {
+  GatherSrc s[kMaxTpParts];
+  int n = 0;
+};
+cudaError_t launch_gather_cols(const Launch& L, const GatherPlan& g, float* dst, int ld_dst, int T);
 cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
                                   const uint64_t* value, uint64_t* out4);
 

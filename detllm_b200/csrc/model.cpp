@@ -461,6 +461,8 @@ void free_model(det_model* m) {
   int cur;
   if (cudaGetDevice(&cur) == cudaSuccess && cur != m->device) cudaSetDevice(m->device);
   session_release_cached(m);
+  tp_model_free(m);  // the other replicas and the per-part views
+  cudaSetDevice(m->device);
   for (void* p : m->allocations) cudaFree(p);
   delete m;
 }

@@ -43,15 +43,14 @@ void session_release_cached(det_model* m) {
     free_session_impl(c);
   }
 }
-}  // namespace det
-
-namespace {
-
 det_status cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return DET_OK;
   if (e == cudaErrorMemoryAllocation) return DET_ERR_DEVICE_OOM;
   return DET_ERR_CUDA;
 }
+}  // namespace det
+
+namespace {
 
 template <typename T>
 det_status dalloc(det_session* s, T** p, size_t count) {
@@ -106,11 +105,16 @@ void free_session(det_session* s) {
   if (!s) return;
   cudaSetDevice(s->m->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
-  add_stats(&s->m->agg, s->stats);
-  add_prof(&s->m->prof_agg, s->prof);
-  for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
+  // a tensor-parallel session's graphs hold the other parts' launches
   for (auto& g : s->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
+  s->graphs.clear();
+  if (s->tp) tp_session_release(s);
+  cudaSetDevice(s->m->device);
+  det_model* owner = s->owner ? s->owner : s->m;
+  add_stats(&owner->agg, s->stats);
+  add_prof(&owner->prof_agg, s->prof);
+  for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   for (void* p : s->allocations) cudaFree(p);
   for (void* p : {(void*)s->h_tokens, (void*)s->h_rows, (void*)s->h_syms, (void*)s->h_err, (void*)s->h_out,
                   (void*)s->h_value, (void*)s->h_pos})
@@ -130,8 +134,11 @@ namespace {
 Launch launch_of(det_session* s) { return Launch{s->stream, s->d_err, &s->stats.launches}; }
 
 // Reads and clears the device error flag (synchronises the stream), and
-// resolves pending profile events.
+// resolves pending profile events.  A tensor-parallel session reads the
+// other parts' flags first.
 det_status take_error(det_session* s, bool cdf) {
+  const det_status part_st = s->tp ? tp_take_part_errors(s) : DET_OK;
+  cudaSetDevice(s->m->device);
   cudaError_t e = cudaMemcpyAsync(s->h_err, s->d_err, 4, cudaMemcpyDeviceToHost, s->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
   if (e != cudaSuccess) return cuda_status(e);
@@ -159,7 +166,7 @@ det_status take_error(det_session* s, bool cdf) {
   if (f & ERRF_DECODE) return DET_ERR_DECODE;
   if (f & ERRF_TIMEOUT) return DET_ERR_TIMEOUT;
   if (f) return DET_ERR_CUDA;
-  return DET_OK;
+  return part_st;
 }
 
 #define CK(expr)                                   \
@@ -167,6 +174,12 @@ det_status take_error(det_session* s, bool cdf) {
     const cudaError_t e_ = (expr);                 \
     if (e_ != cudaSuccess) return cuda_status(e_); \
   } while (0)
+
+}  // namespace
+
+det_status det::session_take_error(det_session* s, bool cdf) { return take_error(s, cdf); }
+
+namespace {
 
 double bytes_per_weight(int type) {
   switch (type) {
@@ -255,87 +268,150 @@ cudaError_t norm(det_session* s, const Launch& L, const float* w, int K, int T, 
   return e;
 }
 
+}  // namespace
+
+// ---- the forward, in the stages a row-sharded (tensor-parallel) forward
+// exchanges slices between (tp.cpp).  A single-device session runs them back
+// to back; a part of a tensor-parallel session computes its own rows of
+// wo / gate / up / down / lm_head (TpShard) and its own KV heads. --------------
+namespace det {
+
+static int shard_d0(const det_session* s) { return s->m->shard ? s->m->shard->d0 : 0; }
+
+det_status fwd_embed(det_session* s, const Launch& L, int T) {
+  CK(timed(s, PT_EMBED, 0, 0, [&] { return launch_embed(L, s->m->tok_embd, s->d_tokens, T, s->x); }));
+  return DET_OK;
+}
+
+// attention block of layer l up to the attention output s->attn
+det_status fwd_attention(det_session* s, const Launch& L, int l, int T) {
+  det_model* m = s->m;
+  const ModelCfg& c = m->cfg;
+  const LayerDev& W = m->layers[(size_t)l];
+  const int* pos0 = s->d_pos;
+  const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
+  const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
+  DevActs a;
+  int have = 0;
+  CK(norm(s, L, W.attn_norm, c.d, T, needs_q8a(W.wq.type) || needs_q8a(W.wk.type) || needs_q8a(W.wv.type), &have));
+  // one Q8A of h shared by q/k/v (:1284-1292); Q8_K recomputed per Q6_K
+  // matrix in the reference gives the same blocks, so it is made once too
+  CK(quantise_for(s, L, W.wq.type, s->h, c.d, T, &a, &have));
+  CK(quantise_for(s, L, W.wk.type, s->h, c.d, T, &a, &have));
+  CK(quantise_for(s, L, W.wv.type, s->h, c.d, T, &a, &have));
+  if (W.wqkv.rows) {
+    OutSegs o;
+    o.n = 3;
+    o.s[0] = OutSeg{W.wq.rows, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq};
+    o.s[1] = OutSeg{W.wk.rows, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk};
+    o.s[2] = OutSeg{W.wv.rows, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv};
+    CK(gemm_fused(s, PT_GEMM_QKV, L, W.wqkv, a, T, o));
+  } else {
+    CK(gemv(s, PT_GEMM_QKV, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
+    CK(gemv(s, PT_GEMM_QKV, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
+    CK(gemv(s, PT_GEMM_QKV, L, W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
+  }
+  float* kc = s->kc + (size_t)l * kv_layer;
+  float* vc = s->vc + (size_t)l * kv_layer;
+  CK(timed(s, PT_ROPE, 0, 0, [&] {
+    return launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
+                             s->rope_sin, kc, vc, s->n_ctx);
+  }));
+  CK(timed(s, PT_ATTENTION, 0, 0, [&] {
+    return launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
+                            s->score_scratch);
+  }));
+  return DET_OK;
+}
+
+// x[:, d0 + r] += (attn . wo^T)[:, r] for this part's rows r of wo
+det_status fwd_attn_out(det_session* s, const Launch& L, int l, int T, const float* attn) {
+  const LayerDev& W = s->m->layers[(size_t)l];
+  if (!W.wo.rows) return DET_OK;
+  DevActs a;
+  int have = 0;
+  CK(quantise_for(s, L, W.wo.type, attn, W.wo.cols, T, &a, &have));
+  CK(gemv(s, PT_GEMM_O, L, W.wo, a, T, s->x + shard_d0(s), s->m->cfg.d, EPI_RESIDUAL, nullptr));
+  return DET_OK;
+}
+
+// RMSNorm, this part's rows of gate / up, SwiGLU -> s->ff; *have: which
+// quantisations of s->ff the launch left in the session buffers
+det_status fwd_ffn_in(det_session* s, const Launch& L, int l, int T, int* have_out) {
+  const ModelCfg& c = s->m->cfg;
+  const LayerDev& W = s->m->layers[(size_t)l];
+  *have_out = 0;
+  if (!W.gate.rows) return DET_OK;
+  DevActs a;
+  int have = 0;
+  CK(norm(s, L, W.ffn_norm, c.d, T, needs_q8a(W.gate.type) || needs_q8a(W.up.type), &have));
+  CK(quantise_for(s, L, W.gate.type, s->h, c.d, T, &a, &have));
+  CK(quantise_for(s, L, W.up.type, s->h, c.d, T, &a, &have));
+  if (W.wgu.rows) {
+    OutSegs o;
+    o.n = 2;
+    o.s[0] = OutSeg{W.gate.rows, s->gate, c.dff, EPI_STORE, nullptr};
+    o.s[1] = OutSeg{W.up.rows, s->up, c.dff, EPI_STORE, nullptr};
+    CK(gemm_fused(s, PT_GEMM_GATE_UP, L, W.wgu, a, T, o));
+  } else {
+    CK(gemv(s, PT_GEMM_GATE_UP, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
+    CK(gemv(s, PT_GEMM_GATE_UP, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
+  }
+  // swiglu also quantises its output to Q8A when the down matrix reads it
+  // (a single device: a tensor-parallel part holds only a slice of the row)
+  const bool ff_q8a = !s->m->shard && needs_q8a(W.down.type) && c.dff % 32 == 0;
+  CK(timed(s, PT_SWIGLU, 0, 0, [&] {
+    return ff_q8a ? launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T, s->qa_d, s->qa_q)
+                  : launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T);
+  }));
+  if (ff_q8a) *have_out |= 1;
+  return DET_OK;
+}
+
+// x[:, d0 + r] += (ff . down^T)[:, r] for this part's rows r of down
+det_status fwd_ffn_out(det_session* s, const Launch& L, int l, int T, const float* ff, int have) {
+  const LayerDev& W = s->m->layers[(size_t)l];
+  if (!W.down.rows) return DET_OK;
+  DevActs a;
+  CK(quantise_for(s, L, W.down.type, ff, W.down.cols, T, &a, &have));
+  CK(gemv(s, PT_GEMM_DOWN, L, W.down, a, T, s->x + shard_d0(s), s->m->cfg.d, EPI_RESIDUAL, nullptr));
+  return DET_OK;
+}
+
+// final RMSNorm and this part's lm_head rows -> s->logits[:, v0 + r]
+det_status fwd_head(det_session* s, const Launch& L, int T) {
+  det_model* m = s->m;
+  if (!m->output.rows) return DET_OK;
+  DevActs a;
+  int have = 0;
+  CK(norm(s, L, m->output_norm, m->cfg.d, T, needs_q8a(m->output.type), &have));
+  CK(quantise_for(s, L, m->output.type, s->h, m->cfg.d, T, &a, &have));
+  const int v0 = m->shard ? m->shard->v0 : 0;
+  CK(gemv(s, PT_GEMM_OUT, L, m->output, a, T, s->logits + v0, m->vocab, EPI_STORE, nullptr));
+  return DET_OK;
+}
+
+}  // namespace det
+
+namespace {
+
 // forward_one_with_workspace for positions pos0 .. pos0+T-1, pos0 = *d_pos
 // (tokens and pos0 already on the device)
 det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
-  det_model* m = s->m;
-  const ModelCfg& c = m->cfg;
   Launch L = launch_of(s);
   L.launches = launch_counter;
   // overlapping launches pays off for one-token (decode) forwards; for
   // chunks it measured slower
   L.pdl = T <= 16;
-  const int* pos0 = s->d_pos;
-  const int qd = c.nh * c.hd, kvd = c.nkv * c.hd;
-  const size_t kv_layer = (size_t)c.nkv * s->n_ctx * c.hd;
-  CK(timed(s, PT_EMBED, 0, 0, [&] { return launch_embed(L, m->tok_embd, s->d_tokens, T, s->x); }));
-  for (int l = 0; l < c.L; l++) {
-    const LayerDev& W = m->layers[(size_t)l];
-    DevActs a;
+  if (det_status st = fwd_embed(s, L, T)) return st;
+  for (int l = 0; l < s->m->cfg.L; l++) {
     int have = 0;
-    CK(norm(s, L, W.attn_norm, c.d, T, needs_q8a(W.wq.type) || needs_q8a(W.wk.type) || needs_q8a(W.wv.type),
-            &have));
-    // one Q8A of h shared by q/k/v (:1284-1292); Q8_K recomputed per Q6_K
-    // matrix in the reference gives the same blocks, so it is made once too
-    CK(quantise_for(s, L, W.wq.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L, W.wk.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L, W.wv.type, s->h, c.d, T, &a, &have));
-    if (W.wqkv.rows) {
-      OutSegs o;
-      o.n = 3;
-      o.s[0] = OutSeg{W.wq.rows, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq};
-      o.s[1] = OutSeg{W.wk.rows, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk};
-      o.s[2] = OutSeg{W.wv.rows, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv};
-      CK(gemm_fused(s, PT_GEMM_QKV, L, W.wqkv, a, T, o));
-    } else {
-      CK(gemv(s, PT_GEMM_QKV, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
-      CK(gemv(s, PT_GEMM_QKV, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
-      CK(gemv(s, PT_GEMM_QKV, L, W.wv, a, T, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv));
-    }
-    float* kc = s->kc + (size_t)l * kv_layer;
-    float* vc = s->vc + (size_t)l * kv_layer;
-    CK(timed(s, PT_ROPE, 0, 0, [&] {
-      return launch_rope_store(L, s->q, s->k, s->v, T, pos0, c.nh, c.nkv, c.hd, c.rope_dim, c.pairing, s->rope_cos,
-                               s->rope_sin, kc, vc, s->n_ctx);
-    }));
-    CK(timed(s, PT_ATTENTION, 0, 0, [&] {
-      return launch_attention(L, s->q, kc, vc, T, pos0, c.nh, c.nkv, c.hd, s->n_ctx, c.attn_scale, s->attn,
-                              s->score_scratch);
-    }));
-    have = 0;
-    CK(quantise_for(s, L, W.wo.type, s->attn, qd, T, &a, &have));
-    CK(gemv(s, PT_GEMM_O, L, W.wo, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
-    have = 0;
-    CK(norm(s, L, W.ffn_norm, c.d, T, needs_q8a(W.gate.type) || needs_q8a(W.up.type), &have));
-    CK(quantise_for(s, L, W.gate.type, s->h, c.d, T, &a, &have));
-    CK(quantise_for(s, L, W.up.type, s->h, c.d, T, &a, &have));
-    if (W.wgu.rows) {
-      OutSegs o;
-      o.n = 2;
-      o.s[0] = OutSeg{W.gate.rows, s->gate, c.dff, EPI_STORE, nullptr};
-      o.s[1] = OutSeg{W.up.rows, s->up, c.dff, EPI_STORE, nullptr};
-      CK(gemm_fused(s, PT_GEMM_GATE_UP, L, W.wgu, a, T, o));
-    } else {
-      CK(gemv(s, PT_GEMM_GATE_UP, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
-      CK(gemv(s, PT_GEMM_GATE_UP, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
-    }
-    have = 0;
-    // swiglu also quantises its output to Q8A when the down matrix reads it
-    const bool ff_q8a = needs_q8a(W.down.type) && c.dff % 32 == 0;
-    CK(timed(s, PT_SWIGLU, 0, 0, [&] {
-      return ff_q8a ? launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T, s->qa_d, s->qa_q)
-                    : launch_swiglu(L, s->gate, s->up, s->ff, c.dff, T);
-    }));
-    if (ff_q8a) have |= 1;
-    CK(quantise_for(s, L, W.down.type, s->ff, c.dff, T, &a, &have));
-    CK(gemv(s, PT_GEMM_DOWN, L, W.down, a, T, s->x, c.d, EPI_RESIDUAL, nullptr));
+    if (det_status st = fwd_attention(s, L, l, T)) return st;
+    if (det_status st = fwd_attn_out(s, L, l, T, s->attn)) return st;
+    if (det_status st = fwd_ffn_in(s, L, l, T, &have)) return st;
+    if (det_status st = fwd_ffn_out(s, L, l, T, s->ff, have)) return st;
   }
-  DevActs a;
-  int have = 0;
-  CK(norm(s, L, m->output_norm, c.d, T, needs_q8a(m->output.type), &have));
-  CK(quantise_for(s, L, m->output.type, s->h, c.d, T, &a, &have));
-  CK(gemv(s, PT_GEMM_OUT, L, m->output, a, T, s->logits, m->vocab, EPI_STORE, nullptr));
-  return DET_OK;
+  return fwd_head(s, L, T);
 }
 
 // H2D copies of the chunk's tokens and first position, then the forward
@@ -356,6 +432,7 @@ bool graphs_enabled() {
 // Runs the chunk forward through a CUDA graph captured once per chunk size
 // (the kernels read pos0 from device memory, so one graph serves every chunk).
 det_status run_forward(det_session* s, int T) {
+  if (s->tp) return tp_run_forward(s, T, graphs_enabled());
   if (!graphs_enabled()) return enqueue_forward(s, T, &s->stats.launches);
   if ((int)s->graphs.size() <= T) s->graphs.resize((size_t)T + 1);
   det_session::Graph& gr = s->graphs[(size_t)T];
@@ -413,7 +490,10 @@ extern "C" {
 det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out) {
   if (!m || !out) return DET_ERR_INVALID_ARGUMENT;
   *out = nullptr;
+  if (m->tp) return tp_session_create(m, n_ctx, max_chunk, out);
   const ModelCfg& c = m->cfg;
+  // a tensor-parallel part also holds full-width inputs of wo and down
+  const ModelCfg& full = m->shard ? m->shard->full : c;
   // RoPE phases pos * omega stay below 2^20 * pi/2 (the range of the
   // restated rem_pio2) for windows up to 2^20 positions.
   if (n_ctx == 0 || (int)n_ctx > c.ctx || n_ctx > (1u << 20) || max_chunk == 0 || max_chunk > 1024)
@@ -422,11 +502,12 @@ det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, 
   det_session* s = new (std::nothrow) det_session();
   if (!s) return DET_ERR_ALLOC;
   s->m = m;
+  s->owner = m;
   s->n_ctx = (int)n_ctx;
   s->max_chunk = (int)std::min<uint32_t>(max_chunk, n_ctx);
   const size_t T = (size_t)s->max_chunk;
   const size_t qd = (size_t)c.nh * c.hd, kvd = (size_t)c.nkv * c.hd;
-  const size_t kmax = std::max({(size_t)c.d, (size_t)c.dff, qd});
+  const size_t kmax = std::max({(size_t)c.d, (size_t)c.dff, qd, (size_t)full.dff, (size_t)full.nh * full.hd});
   const size_t kv = (size_t)c.L * c.nkv * n_ctx * c.hd;
   det_status st = DET_OK;
   if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) st = DET_ERR_CUDA;
@@ -443,6 +524,10 @@ det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, 
   if (!st) st = dalloc(s, &s->up, T * c.dff);
   if (!st) st = dalloc(s, &s->ff, T * c.dff);
   if (!st) st = dalloc(s, &s->logits, T * (size_t)m->vocab);
+  if (!st && m->shard) {
+    st = dalloc(s, &s->ff_full, T * full.dff);
+    if (!st && m->shard->attn_sharded) st = dalloc(s, &s->attn_full, T * (size_t)full.nh * full.hd);
+  }
   // Q8A buffers cover whole 64-position groups; the padding positions stay
   // zero so the chunk GEMM may read (and discard) them.
   const size_t Tg = (T + 63) / 64 * 64;
@@ -497,6 +582,8 @@ void det_session_free(det_session* s) { free_session(s); }
 
 det_status det_session_reset(det_session* s) {
   if (!s) return DET_ERR_INVALID_ARGUMENT;
+  if (s->tp)
+    if (det_status st = tp_reset(s)) return st;
   cudaSetDevice(s->m->device);
   const ModelCfg& c = s->m->cfg;
   const size_t kv = (size_t)c.L * c.nkv * s->n_ctx * c.hd;
@@ -666,6 +753,7 @@ det_status det_device_expf(int device, const float* x, float* y, size_t n) {
 
 det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per_pass, double* bytes_per_pass) {
   if (!s || !ms_per_pass || !bytes_per_pass || reps == 0) return DET_ERR_INVALID_ARGUMENT;
+  if (s->tp) return DET_ERR_UNSUPPORTED_MODEL_FEATURE;
   det_model* m = s->m;
   const ModelCfg& c = m->cfg;
   cudaSetDevice(m->device);

@@ -121,6 +121,25 @@ det_status det_model_info(const det_model* model, det_config* out);
 /* SHA-256 of the GGUF bytes the model was loaded from */
 det_status det_model_sha256(const det_model* model, uint8_t out[32]);
 
+/* ---- tensor parallelism: the row partition of gemv_rows_parallel
+ *      (det-model lib.rs:291-321) spread over devices ----------------------
+ * Loads one replica of the model on each distinct device of
+ * devices[0 .. n) (1 <= n <= 8; a device may repeat, which runs several
+ * parts on one GPU) and returns a model whose sessions run one forward over
+ * all n parts.  Part p computes a contiguous slice (64-row boundaries) of
+ * the output rows of attn_output, ffn_gate, ffn_up, ffn_down and the
+ * lm_head and, when head_count_kv is a multiple of n, its share of the KV
+ * heads (their q/k/v rows, attention and KV cache); otherwise every part
+ * runs the whole attention block.  Before each op that reads a whole row,
+ * the parts exchange their slices (an all-gather: each part reads the
+ * others' device memory over NVLink).  Every output row is the same
+ * reduction as on one device, so logits, logits hashes and DTLZ streams are
+ * identical to those of det_model_load's model.  The returned model and its
+ * sessions take every other call unchanged; logits and CDF work stay on
+ * devices[0].  det_model_free releases all replicas.
+ * DET_ERR_COLLECTIVE: two of the devices cannot reach each other's memory. */
+det_status det_model_load_tp(const uint8_t* gguf, size_t len, const int* devices, int n, det_model** out);
+
 /* ---- session: replaces RopeTables::llama + KvCache::new + ForwardWorkspace
  *      (det-model lib.rs:813, 850, 963) ------------------------------------ */
 /* n_ctx: positions per window (<= context_length); max_chunk: most
