@@ -179,6 +179,71 @@ def oracle_sample(spec, gguf, tokens, budget_s=20.0):
     return s, dt, load_s
 
 
+def decode_tokens_per_s(model, vocab, n_prefix=1024, n_steps=48):
+    """Single-token forwards after an n_prefix-token prefix (CUDA graphs):
+    device time per token (forward events on the session stream)."""
+    from detllm_b200 import synth as S
+
+    tokens = S.zipf_tokens(n_prefix + n_steps + 8, vocab, seed=11)
+    with model.session(n_ctx=N_CTX, max_chunk=512) as s:
+        for p in range(0, n_prefix, 512):
+            s.forward(tokens[p:p + 512], p)
+        pos = n_prefix
+        for _ in range(4):
+            s.forward(tokens[pos:pos + 1], pos)
+            pos += 1
+        s.stats(reset=True)
+        for _ in range(n_steps):
+            s.forward(tokens[pos:pos + 1], pos)
+            pos += 1
+        st = s.stats(reset=True)
+    return n_steps / (st.forward_ms / 1000.0), st.forward_ms / n_steps
+
+
+def run_tp(args):
+    """--tp G1,G2,...: row-sharded tensor parallelism in one process over
+    devices 0..G-1 (det_model_load_tp): single-stream decode tokens/s,
+    chunked encode tokens/s of the config's stream, and the logits hash of
+    the first 256 tokens, which must equal the 1-GPU hash.  One JSON line
+    per part count."""
+    import detllm_b200 as D
+    from detllm_b200 import synth as S
+
+    spec, gguf = model_bytes(0, 1)
+    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7)
+    ndev = D.device_count()
+    ref_hash = None
+    for G in [int(x) for x in args.tp.split(",")]:
+        if G > ndev:
+            log(f"--tp {G}: only {ndev} devices, skipped")
+            continue
+        t = time.time()
+        model = D.Model(gguf, device=0) if G == 1 else D.Model(gguf, devices=list(range(G)))
+        load_s = time.time() - t
+        h = model.logits_hash_for_tokens_chunked(tokens[:256], 64).hex()
+        ref_hash = ref_hash or h
+        dec_tps, dec_ms = decode_tokens_per_s(model, spec.vocab)
+        for _ in range(args.warmup):
+            model.encode_symbols(tokens, N_CTX, OVERLAP)
+        model.stats(reset=True)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            model.encode_symbols(tokens, N_CTX, OVERLAP)
+        wall = time.perf_counter() - t0
+        st = model.stats(reset=True)
+        dev_s = (st.forward_ms + st.cdf_ms) / 1000.0
+        wb = S.weight_bytes_per_token(spec)
+        print(json.dumps({
+            "mode": "tensor-parallel", "config": CONFIG, "parts": G, "devices": list(range(G)),
+            "decode_tokens_per_s": dec_tps, "decode_ms_per_token": dec_ms,
+            "decode_weight_gbs_per_gpu": wb / G / (dec_ms / 1000.0) / 1e9,
+            "encode_tokens_per_s": N_TOKENS * args.steps / dev_s,
+            "encode_e2e_tokens_per_s": N_TOKENS * args.steps / wall,
+            "logits_hash_256": h, "hash_equals_1gpu": h == ref_hash, "load_s": round(load_s, 1),
+        }), flush=True)
+        model.close()
+
+
 def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
     """Single-token forwards (the decode path) after a 1024-token prefix:
     device time per token with CUDA graphs, then one profiled pass that times
@@ -350,6 +415,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default=CONFIG, choices=sorted(CONFIG_RUNS),
                     help="model configuration (default: the headline BASELINE config)")
+    ap.add_argument("--tp", default=None,
+                    help="comma-separated part counts: row-sharded tensor parallelism in one process "
+                         "(single-stream decode / encode), instead of the segment-parallel bench")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per rank per step (default: the config's; smaller values are for profiling)")
     args = ap.parse_args()
@@ -358,7 +426,9 @@ def main():
     OVERLAP = N_CTX // 4
     if args.tokens:
         N_TOKENS = args.tokens
-    if args.impl == "reference":
+    if args.tp:
+        run_tp(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run(args)

@@ -17,6 +17,18 @@
 // orders them with events and captures the whole multi-device forward in one
 // CUDA graph per chunk size.
 //
+// Ordering.  A gather waits for every other part's event recorded after
+// that part wrote its slice (read-after-write).  A part rewrites a slice
+// another part reads only after an exchange that waited for the reader
+// (write-after-read): the attention output and the SwiGLU output are
+// rewritten a layer later, past two exchanges; x's slice is rewritten by
+// down after the SwiGLU exchange and by the next layer's wo after the
+// attention exchange -- or, when the attention is replicated and that
+// exchange does not exist, after a wait on every part's `done` event of the
+// previous layer's last gather.  Eager forwards also wait, on entry, for the
+// other parts' last exchange of the previous forward; a graph forward is one
+// unit on part 0's stream.
+//
 // Weights: one replica per distinct device; each part's model (a "shard")
 // views its replica's matrices through row offsets and owns only the fused
 // q|k|v and gate|up buffers of its slices.
@@ -41,6 +53,8 @@ struct TpSession {
   // per part, recorded at every exchange: [0] eager forwards, [1] inside
   // graph captures (an event recorded in a capture is not waited on outside)
   std::vector<cudaEvent_t> ev[2];
+  // per part, recorded after its last gather of a layer (same [0] / [1] split)
+  std::vector<cudaEvent_t> done[2];
   std::vector<cudaEvent_t> join;     // per part, end of a captured forward
   cudaEvent_t fork = nullptr;        // start of a captured forward (on part 0)
 };
@@ -235,7 +249,8 @@ Launch part_launch(det_session* s, uint64_t* counter) {
 // others' and pulls their slices.  X_RESID / X_LOGITS gather into the buffer
 // the slices live in (a part's own slice is already there); X_ATTN / X_FF
 // gather every part's local output into a separate full-width buffer.
-det_status exchange(TpSession& ts, XKind kind, int T, uint64_t* counter, bool capture) {
+// `mark_done`: each part then records its `done` event after its gather.
+det_status exchange(TpSession& ts, XKind kind, int T, uint64_t* counter, bool capture, bool mark_done = false) {
   const int G = (int)ts.parts.size();
   const std::vector<cudaEvent_t>& ev = ts.ev[capture ? 1 : 0];
   for (int p = 0; p < G; p++) {
@@ -284,6 +299,7 @@ det_status exchange(TpSession& ts, XKind kind, int T, uint64_t* counter, bool ca
       if (src.n > 0) g.s[g.n++] = src;
     }
     CK(launch_gather_cols(part_launch(sp, counter), g, dst, ld, T));
+    if (mark_done) CK(cudaEventRecord(ts.done[capture ? 1 : 0][(size_t)p], sp->stream));
   }
   return DET_OK;
 }
@@ -329,6 +345,13 @@ det_status tp_enqueue(det_session* s0, int T, uint64_t* counter, bool capture) {
     for (int p = 0; p < G; p++) {
       det_session* s = part(p);
       if (det_status st = set_dev(s)) return st;
+      // wo adds into this part's slice of x, which the others read in the
+      // previous layer's last gather.  With sharded heads the attention
+      // exchange already ordered that; with replicated attention nothing
+      // else does.
+      if (!attn_sharded && l > 0)
+        for (int q = 0; q < G; q++)
+          if (q != p) CK(cudaStreamWaitEvent(s->stream, ts.done[capture ? 1 : 0][(size_t)q], 0));
       if (det_status st = fwd_attn_out(s, part_launch(s, counter), l, T, attn_sharded ? s->attn_full : s->attn))
         return st;
     }
@@ -344,7 +367,7 @@ det_status tp_enqueue(det_session* s0, int T, uint64_t* counter, bool capture) {
       if (det_status st = set_dev(s)) return st;
       if (det_status st = fwd_ffn_out(s, part_launch(s, counter), l, T, s->ff_full, 0)) return st;
     }
-    if (det_status st = exchange(ts, X_RESID, T, counter, capture)) return st;
+    if (det_status st = exchange(ts, X_RESID, T, counter, capture, !attn_sharded)) return st;
   }
   for (int p = 0; p < G; p++) {
     if (det_status st = set_dev(part(p))) return st;
@@ -365,8 +388,8 @@ det_status tp_enqueue(det_session* s0, int T, uint64_t* counter, bool capture) {
 void destroy_events(TpSession* ts) {
   for (size_t p = 0; p < ts->parts.size(); p++) {
     if (ts->parts[p]) cudaSetDevice(ts->parts[p]->m->device);
-    for (auto& ev : ts->ev)
-      if (p < ev.size() && ev[p]) cudaEventDestroy(ev[p]);
+    for (auto* set : {&ts->ev[0], &ts->ev[1], &ts->done[0], &ts->done[1]})
+      if (p < set->size() && (*set)[p]) cudaEventDestroy((*set)[p]);
     if (p < ts->join.size() && ts->join[p]) cudaEventDestroy(ts->join[p]);
   }
   if (ts->fork && ts->parts[0]) {
@@ -397,6 +420,8 @@ det_status tp_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, d
   ts->parts.assign((size_t)G, nullptr);
   ts->ev[0].assign((size_t)G, nullptr);
   ts->ev[1].assign((size_t)G, nullptr);
+  ts->done[0].assign((size_t)G, nullptr);
+  ts->done[1].assign((size_t)G, nullptr);
   ts->join.assign((size_t)G, nullptr);
   det_status st = DET_OK;
   for (int p = 0; p < G && !st; p++) st = det_session_create(tm.shards[(size_t)p], n_ctx, max_chunk, &ts->parts[(size_t)p]);
@@ -404,6 +429,8 @@ det_status tp_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, d
     if (cudaSetDevice(tm.devices[(size_t)p]) != cudaSuccess ||
         cudaEventCreateWithFlags(&ts->ev[0][(size_t)p], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ts->ev[1][(size_t)p], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ts->done[0][(size_t)p], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ts->done[1][(size_t)p], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ts->join[(size_t)p], cudaEventDisableTiming) != cudaSuccess)
       st = DET_ERR_CUDA;
   }
