@@ -276,141 +276,406 @@ __global__ void __launch_bounds__(K6_THREADS) gemm_q6k_kernel(const uint8_t* __r
 }
 
 // ---- one position (decode) ---------------------------------------------------------
-// Q4_K: the reference's chain is sequential over all K elements, so each
-// thread runs one row's chain; the position's dequantised activations
-// (a.d * a.q, the reference's exact value) sit in shared memory, so the chain
-// only waits on its own f32 adds.
-constexpr int D4_THREADS = 128;
+// Up to three matrices that read the same activation (q, k, v or gate, up)
+// in one launch: segment i owns CTAs [cta0, next cta0).
+DI KqSeg kq_seg(const KqSegs& S) {
+  const int i = (int)(blockIdx.x >= (unsigned)S.s[1].cta0) + (int)(blockIdx.x >= (unsigned)S.s[2].cta0);
+  return i == 0 ? S.s[0] : (i == 1 ? S.s[1] : S.s[2]);
+}
 
-__global__ void __launch_bounds__(D4_THREADS) gemv_q4k_decode_kernel(const uint8_t* __restrict__ W, int rows, int nbs,
-                                                                     const int8_t* __restrict__ aq,
-                                                                     const float* __restrict__ ad,
-                                                                     float* __restrict__ out, int epi,
-                                                                     const float* __restrict__ bias, uint32_t* err) {
+// byte k (0..11) of a Q4_K block's packed scales (bytes 4..15 of the block)
+DI uint32_t q4k_sbyte(const uint4& h, int k) {
+  const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
+  return (w >> (8 * (k & 3))) & 0xffu;
+}
+
+DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
+  if (!finite(sum)) atomicOr(err, ERRF_NONFINITE);
+  float v = sum;
+  if (g.epi == EPI_BIAS) {
+    v = fadd(v, g.bias[row]);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  } else if (g.epi == EPI_RESIDUAL) {
+    v = fadd(g.out[row], v);
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+  }
+  g.out[row] = v;
+}
+
+// Q4_K: each row is one f32 chain over all K elements (sum += w * act, in
+// order), so its length sets a floor of K dependent adds per launch.  A CTA
+// takes 32 rows: warps 0-7 (producers) dequantise super-block b of the 32
+// rows -- warp w sub-block w, lane r row r -- and write the products
+// w * act into a shared-memory stage, while warp 8 runs the 32 row chains
+// (lane = row) through the previous stage.  Producers load each stage's
+// weights and activation two stages ahead, so HBM latency stays off the
+// chain.  Stage rows are 260 floats apart and both sides move 16-byte
+// vectors (the eight lanes of a quarter-warp hit distinct bank groups); the
+// chain loads 32 values ahead of its adds, so only the add latency is serial.
+constexpr int G4_ROWS = 32;
+constexpr int G4_PWARPS = 8;
+constexpr int G4_THREADS = (G4_PWARPS + 1) * 32;
+constexpr int G4_LD = 260;
+constexpr size_t G4_SMEM = (size_t)(2 * G4_ROWS * G4_LD + 256) * sizeof(float);
+
+struct Q4Stage {
+  uint4 h, v0, v1;  // block header (d, dmin, scales) and the sub-block pair's 32 quant bytes
+  float ad;
+  int aq;
+};
+
+__global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, const int8_t* __restrict__ aq,
+                                                                    const float* __restrict__ ad, uint32_t* err) {
   pdl_enter();
-  extern __shared__ float act[];  // [K]
-  const int K = nbs * 256, nbk = nbs * 8;
-  for (int i = threadIdx.x; i < K; i += D4_THREADS) {
-    const int kb = i >> 5, e = i & 31;
-    act[i] = fmul(ad[q8a_dslot(nbk, 0, kb)], (float)aq[q8a_elem(nbk, 0, kb, e)]);
+  extern __shared__ float g4_smem[];
+  float* prod = g4_smem;                        // [2][G4_ROWS][G4_LD]
+  float* actb = g4_smem + 2 * G4_ROWS * G4_LD;  // [256]: sub-block w at [32 w, 32 w + 32)
+  const KqSeg g = kq_seg(S);
+  const int r0 = ((int)blockIdx.x - g.cta0) * G4_ROWS;
+  const int nbs = S.nb, nbk = nbs * 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = r0 + lane;
+  const bool ok = row < g.rows;
+
+  auto load = [&](int b, Q4Stage& st) {
+    const int kb = b * 8 + warp;
+    st.ad = ad[q8a_dslot(nbk, 0, kb)];
+    st.aq = aq[q8a_elem(nbk, 0, kb, lane)];
+    if (ok) {
+      const uint8_t* blk = g.q + ((size_t)row * nbs + b) * 144;
+      st.h = *reinterpret_cast<const uint4*>(blk);
+      st.v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
+      st.v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
+    }
+  };
+  // products of one stage into buffer `buf` (producer warps only)
+  auto compute = [&](const Q4Stage& st, int buf) {
+    actb[warp * 32 + lane] = fmul(st.ad, (float)st.aq);
+    __syncwarp();
+    float* dst = prod + (buf * G4_ROWS + lane) * G4_LD + warp * 32;
+    if (!ok) {
+#pragma unroll
+      for (int e4 = 0; e4 < 32; e4 += 4) *reinterpret_cast<float4*>(dst + e4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      return;
+    }
+    const uint4 h = st.h;
+    const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
+    const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+    // q4_k_scale_min (det-quant lib.rs:516-529) on the packed bytes
+    int sc, mn;
+    if (warp < 4) {
+      sc = (int)(q4k_sbyte(h, warp) & 63u);
+      mn = (int)(q4k_sbyte(h, warp + 4) & 63u);
+    } else {
+      sc = (int)((q4k_sbyte(h, warp + 4) & 0x0fu) | ((q4k_sbyte(h, warp - 4) >> 6) << 4));
+      mn = (int)((q4k_sbyte(h, warp + 4) >> 4) | ((q4k_sbyte(h, warp) >> 6) << 4));
+    }
+    const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+    const uint32_t qw[8] = {st.v0.x, st.v0.y, st.v0.z, st.v0.w, st.v1.x, st.v1.y, st.v1.z, st.v1.w};
+    const int sh = 4 * (warp & 1);
+    const float* av = actb + warp * 32;
+#pragma unroll
+    for (int e4 = 0; e4 < 32; e4 += 4) {
+      float p[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int e = e4 + j;
+        const uint32_t q = (qw[e >> 2] >> (8 * (e & 3) + sh)) & 0x0fu;
+        const float qf = __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);  // exact
+        p[j] = fmul(fsub(fmul(dsc, qf), dmn), av[e]);
+      }
+      *reinterpret_cast<float4*>(dst + e4) = make_float4(p[0], p[1], p[2], p[3]);
+    }
+  };
+
+  // stage b lives in slot b % 3; the loop is unrolled by three so each slot
+  // keeps its registers (copying a register whose load is in flight would
+  // wait for the load)
+  Q4Stage st0{}, st1{}, st2{};
+  if (warp < G4_PWARPS) {
+    load(0, st0);
+    if (nbs > 1) load(1, st1);
+    if (nbs > 2) load(2, st2);
+    compute(st0, 0);
   }
   __syncthreads();
-  const int row = blockIdx.x * D4_THREADS + threadIdx.x;
-  if (row >= rows) return;
-  const uint8_t* w = W + (size_t)row * nbs * 144;
   float sum = 0.0f;
-  for (int b = 0; b < nbs; b++) {
-    const uint8_t* blk = w + (size_t)b * 144;
-    const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
-    uint8_t hb[16];
-    *reinterpret_cast<uint4*>(hb) = h;
-    const float d = f16_bits_to_f32((uint16_t)(hb[0] | (hb[1] << 8)));
-    const float dmin = f16_bits_to_f32((uint16_t)(hb[2] | (hb[3] << 8)));
+  // step b: load stage b + 3 into the slot stage b used, compute stage b + 1
+  // from its slot, and run the chains through stage b
+  auto step = [&](int b, Q4Stage& ld_slot, const Q4Stage& next) {
+    if (warp < G4_PWARPS) {
+      if (b + 3 < nbs) load(b + 3, ld_slot);
+      if (b + 1 < nbs) compute(next, (b + 1) & 1);
+    } else {
+      const float4* src = reinterpret_cast<const float4*>(prod + ((b & 1) * G4_ROWS + lane) * G4_LD);
 #pragma unroll 1
-    for (int pair = 0; pair < 4; pair++) {  // sub-blocks 2 pair, 2 pair + 1 share 32 quant bytes
-      uint32_t qw[8];
+      for (int e4 = 0; e4 < 64; e4 += 8) {
+        float4 v[8];
 #pragma unroll
-      for (int k = 0; k < 2; k++) {
-        const uint4 v = *reinterpret_cast<const uint4*>(blk + 16 + pair * 32 + 16 * k);
-        qw[4 * k] = v.x; qw[4 * k + 1] = v.y; qw[4 * k + 2] = v.z; qw[4 * k + 3] = v.w;
-      }
+        for (int j = 0; j < 8; j++) v[j] = src[e4 + j];
 #pragma unroll
-      for (int half = 0; half < 2; half++) {
-        const int sub = 2 * pair + half;
-        int sc, mn;
-        q4k_scale_min(hb + 4, sub, sc, mn);
-        const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-        const float* a = act + b * 256 + sub * 32;
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const int q = (int)((qw[i >> 2] >> (8 * (i & 3) + 4 * half)) & 0x0fu);
-          sum = fadd(sum, fmul(fsub(fmul(dsc, (float)q), dmn), a[i]));
+        for (int j = 0; j < 8; j++) {
+          sum = fadd(sum, v[j].x);
+          sum = fadd(sum, v[j].y);
+          sum = fadd(sum, v[j].z);
+          sum = fadd(sum, v[j].w);
         }
       }
     }
+    __syncthreads();
+  };
+  for (int b = 0; b < nbs; b += 3) {
+    step(b, st0, st1);
+    if (b + 1 < nbs) step(b + 1, st1, st2);
+    if (b + 2 < nbs) step(b + 2, st2, st0);
   }
-  if (!finite(sum)) atomicOr(err, ERRF_NONFINITE);
-  float v = sum;
-  if (epi == EPI_BIAS) {
-    v = fadd(v, bias[row]);
-    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  } else if (epi == EPI_RESIDUAL) {
-    v = fadd(out[row], v);
-    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  }
-  out[row] = v;
+  if (warp == G4_PWARPS && ok) kq_store(g, row, sum, err);
 }
 
-// Q6_K: the integer lane sums are order-free, so a warp takes a row and its
-// lanes split each block (lane l: elements 8 l .. 8 l + 7, one per lane
-// class ln), reduce the 8 class sums exactly with shuffles, and lane 0 keeps
-// the 8 f32 lane sums in block order.
-constexpr int D6_WARPS = 4;
+// Q6_K: per block the reference forms eight exact integer lane sums
+// aux[c] = sum over elements i = c (mod 8) of sc[i / 16] * a[i] * (q[i] - 32)
+// and then advances eight f32 chains sums[c] += (d * a.d) * aux[c] in block
+// order.  The integer sums are order-free, so a CTA computes them for all
+// (row, block) items of its R rows in parallel, two items per thread with
+// both items' loads issued first (the lanes of a warp take consecutive rows
+// of one block, so their activation reads are broadcasts): within a
+// 16-element scale group, class c
+// owns elements c and c + 8, whose 6-bit values a byte permute pairs up for
+// dp2a against the activation pairs (a[c], a[c + 8]); the -32 offset is
+// folded in as sc * (a[c] + a[c + 8]) sums, also by dp2a.  Then thread
+// (row, class) runs its f32 chain over the blocks out of shared memory, and
+// the row's eight chains are summed in lane order.
+constexpr int G6_THREADS = 256;
+constexpr int G6_NBC = 32;                 // blocks per pass
+constexpr int G6_AUX_LD = G6_NBC * 8 + 1;  // aux row stride (ints): rows in distinct banks
+constexpr int G6_DD_LD = G6_NBC + 1;
+template <int R>
+constexpr size_t g6_smem() {
+  return (size_t)G6_NBC * (128 + 64) * 4 + (size_t)R * G6_AUX_LD * 4 + (size_t)R * G6_DD_LD * 4;
+}
 
-__global__ void __launch_bounds__(D6_WARPS * 32) gemv_q6k_decode_kernel(const uint8_t* __restrict__ W,
-                                                                        const uint16_t* __restrict__ Wd, int rows,
-                                                                        int nb, const int8_t* __restrict__ aq,
-                                                                        const float* __restrict__ ad,
-                                                                        float* __restrict__ out, int epi,
-                                                                        const float* __restrict__ bias,
-                                                                        uint32_t* err) {
-  pdl_enter();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * D6_WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const uint8_t* w = W + (size_t)row * nb * 208;
-  float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int b = 0; b < nb; b++) {
-    const uint8_t* body = w + (size_t)b * 208;
-    const int8_t* a = aq + (size_t)b * 256;
-    int aux[8];
+DI int dp2a_lo_su(uint32_t a, uint32_t b, int c) {  // a: two s16, b: bytes 0, 1 unsigned
+  int d;
+  asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+DI int dp2a_hi_su(uint32_t a, uint32_t b, int c) {  // bytes 2, 3
+  int d;
+  asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+DI int dp2a_lo_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+DI int dp2a_hi_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+DI uint32_t s16pair(int lo, int hi) { return ((uint32_t)lo & 0xffffu) | ((uint32_t)hi << 16); }
+// prmt.b32 with sign replication (a selector nibble with bit 3 set copies
+// the selected byte's sign bit into the whole target byte)
+DI uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+struct Q6Item {
+  uint32_t w[52];  // ql words 0..31, qh words 32..47, scale words 48..51
+  uint32_t d;      // f16 bits of the block scale
+};
+
+DI void q6_load(const KqSeg& g, int nb, int row, int b, Q6Item& it) {
+  const uint4* src = reinterpret_cast<const uint4*>(g.q + ((size_t)row * nb + b) * 208);
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      const int i = 8 * lane + k;  // ln = k
-      aux[k] = (int)(int8_t)body[192 + (i >> 4)] * (int)a[i] * q6k_quant(body, i);
-    }
-#pragma unroll
-    for (int k = 0; k < 8; k++)
-      for (int o = 16; o > 0; o >>= 1) aux[k] += __shfl_xor_sync(0xffffffffu, aux[k], o);
-    const float dd = fmul(f16_bits_to_f32(Wd[(size_t)row * nb + b]), ad[b]);
-#pragma unroll
-    for (int k = 0; k < 8; k++) sums[k] = fadd(sums[k], fmul(dd, __int2float_rn(aux[k])));
+  for (int k = 0; k < 13; k++) {
+    const uint4 v = src[k];
+    it.w[4 * k] = v.x;
+    it.w[4 * k + 1] = v.y;
+    it.w[4 * k + 2] = v.z;
+    it.w[4 * k + 3] = v.w;
   }
-  if (lane != 0) return;
+  it.d = g.d[(size_t)row * nb + b];
+}
+
+// the eight integer lane sums of one block (A, Sp: its activation pairs)
+DI void q6_aux(const Q6Item& it, const uint32_t* A, const uint32_t* Sp, int* dst) {
+  const uint32_t* w = it.w;
+  int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int half = 0; half < 2; half++)
+#pragma unroll
+    for (int lh = 0; lh < 2; lh++)
+#pragma unroll
+      for (int part = 0; part < 4; part++) {
+        const int gg = half * 8 + part * 2 + lh;  // scale group of these 16 elements
+        uint32_t x[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          uint32_t lw = w[half * 16 + (part & 1) * 8 + lh * 4 + k];
+          if (part >= 2) lw >>= 4;
+          const uint32_t hw = w[32 + half * 8 + lh * 4 + k];
+          const uint32_t hs = part == 0 ? hw << 4 : part == 1 ? hw << 2 : part == 2 ? hw : hw >> 2;
+          x[k] = (lw & 0x0f0f0f0fu) | (hs & 0x30303030u);  // 6-bit values of elements 4k .. 4k + 3
+        }
+        const uint32_t p0 = __byte_perm(x[0], x[2], 0x5140), p1 = __byte_perm(x[0], x[2], 0x7362);
+        const uint32_t p2 = __byte_perm(x[1], x[3], 0x5140), p3 = __byte_perm(x[1], x[3], 0x7362);
+        const uint4 aa = *reinterpret_cast<const uint4*>(A + gg * 8);
+        const uint4 ab = *reinterpret_cast<const uint4*>(A + gg * 8 + 4);
+        const int sc = (int)(int8_t)(w[48 + (gg >> 2)] >> (8 * (gg & 3)));
+        acc[0] += sc * dp2a_lo_su(aa.x, p0, 0);
+        acc[1] += sc * dp2a_hi_su(aa.y, p0, 0);
+        acc[2] += sc * dp2a_lo_su(aa.z, p1, 0);
+        acc[3] += sc * dp2a_hi_su(aa.w, p1, 0);
+        acc[4] += sc * dp2a_lo_su(ab.x, p2, 0);
+        acc[5] += sc * dp2a_hi_su(ab.y, p2, 0);
+        acc[6] += sc * dp2a_lo_su(ab.z, p3, 0);
+        acc[7] += sc * dp2a_hi_su(ab.w, p3, 0);
+      }
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    int corr = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      corr = dp2a_lo_ss(Sp[(2 * k) * 8 + c], w[48 + k], corr);
+      corr = dp2a_hi_ss(Sp[(2 * k + 1) * 8 + c], w[48 + k], corr);
+    }
+    dst[c] = acc[c] - 32 * corr;
+  }
+}
+
+template <int R>
+__global__ void __launch_bounds__(G6_THREADS, 1) gemv_q6k_aux_kernel(KqSegs S, const int8_t* __restrict__ aq,
+                                                                     const float* __restrict__ ad, uint32_t* err) {
+  pdl_enter();
+  extern __shared__ uint32_t g6_smem[];
+  uint32_t* apair = g6_smem;                               // [G6_NBC][16 groups][8 classes]: (a[c], a[c + 8])
+  uint32_t* spair = apair + G6_NBC * 128;                  // [G6_NBC][8 group pairs][8 classes]
+  int* aux = reinterpret_cast<int*>(spair + G6_NBC * 64);  // [R][G6_AUX_LD]
+  float* ddv = reinterpret_cast<float*>(aux + R * G6_AUX_LD);  // [R][G6_DD_LD]: d * a.d
+  const KqSeg g = kq_seg(S);
+  const int r0 = ((int)blockIdx.x - g.cta0) * R;
+  const int nb = S.nb;
+  const int t = threadIdx.x;
+  const int cr = t >> 3, cc = t & 7;  // chain: row, class
+  float sum = 0.0f;
+  for (int b0 = 0; b0 < nb; b0 += G6_NBC) {
+    const int nbc = min(G6_NBC, nb - b0);
+    const int nit = R * nbc;
+    // this thread's two (row, block) items: loads first
+    Q6Item i0, i1;
+    const int it0 = t, it1 = t + G6_THREADS;  // item it: row it % R, block it / R
+    const int rw0 = r0 + it0 % R, rw1 = r0 + it1 % R;
+    const bool h0 = it0 < nit && rw0 < g.rows, h1 = it1 < nit && rw1 < g.rows;
+    if (h0) q6_load(g, nb, rw0, b0 + it0 / R, i0);
+    if (h1) q6_load(g, nb, rw1, b0 + it1 / R, i1);
+    // activation pairs of the pass: one (block, group pair) per thread
+    for (int i = t; i < nbc * 8; i += G6_THREADS) {
+      const int bb = i >> 3, j = i & 7;
+      const uint4 v0 = *reinterpret_cast<const uint4*>(aq + (size_t)(b0 + bb) * 256 + j * 32);
+      const uint4 v1 = *reinterpret_cast<const uint4*>(aq + (size_t)(b0 + bb) * 256 + j * 32 + 16);
+      uint32_t* A = apair + bb * 128 + (2 * j) * 8;
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        const uint32_t k = (uint32_t)(c & 3);
+        // bytes c and c + 8 of the group, each sign-extended to 16 bits
+        const uint32_t sel = k | ((k | 8u) << 4) | ((4u + k) << 8) | (((4u + k) | 8u) << 12);
+        const uint32_t a0 = prmt_sx(c < 4 ? v0.x : v0.y, c < 4 ? v0.z : v0.w, sel);
+        const uint32_t a1 = prmt_sx(c < 4 ? v1.x : v1.y, c < 4 ? v1.z : v1.w, sel);
+        A[c] = a0;
+        A[8 + c] = a1;
+        const int s0 = (int)(int16_t)(a0 & 0xffffu) + ((int)a0 >> 16);
+        const int s1 = (int)(int16_t)(a1 & 0xffffu) + ((int)a1 >> 16);
+        spair[bb * 64 + j * 8 + c] = s16pair(s0, s1);
+      }
+    }
+    __syncthreads();
+    if (h0) {
+      const int r = it0 % R, bb = it0 / R;
+      q6_aux(i0, apair + bb * 128, spair + bb * 64, aux + r * G6_AUX_LD + bb * 8);
+      ddv[r * G6_DD_LD + bb] = fmul(f16_bits_to_f32((uint16_t)i0.d), ad[b0 + bb]);
+    }
+    if (h1) {
+      const int r = it1 % R, bb = it1 / R;
+      q6_aux(i1, apair + bb * 128, spair + bb * 64, aux + r * G6_AUX_LD + bb * 8);
+      ddv[r * G6_DD_LD + bb] = fmul(f16_bits_to_f32((uint16_t)i1.d), ad[b0 + bb]);
+    }
+    __syncthreads();
+    if (cr < R && r0 + cr < g.rows) {
+      const int* src = aux + cr * G6_AUX_LD + cc;
+      const float* dd = ddv + cr * G6_DD_LD;
+      for (int bb = 0; bb < nbc; bb++) sum = fadd(sum, fmul(dd[bb], __int2float_rn(src[bb * 8])));
+    }
+    __syncthreads();
+  }
+  // ((((0 + s0) + s1) + ...) + s7) within each group of eight lanes
   float v = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 8; k++) v = fadd(v, sums[k]);
-  if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  if (epi == EPI_BIAS) {
-    v = fadd(v, bias[row]);
-    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  } else if (epi == EPI_RESIDUAL) {
-    v = fadd(out[row], v);
-    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-  }
-  out[row] = v;
+  for (int k = 0; k < 8; k++) v = fadd(v, __shfl_sync(0xffffffffu, sum, (t & 31 & ~7) + k));
+  const int row = r0 + cr;
+  if (cr < R && cc == 0 && row < g.rows) kq_store(g, row, v, err);
 }
 
 }  // namespace
 
-cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
-                                  const float* bias) {
-  cudaError_t e;
-  if (m.type == GT_Q4_K) {
-    const size_t smem = (size_t)m.nb * 256 * sizeof(float);
-    if (smem > 48 * 1024) {
-      e = cudaFuncSetAttribute(gemv_q4k_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
+cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
+                                       float* const* out, const int* epi, const float* const* bias) {
+  if (n < 1 || n > 3) return cudaErrorInvalidValue;
+  const bool q4 = m[0]->type == GT_Q4_K;
+  // Q6_K rows per CTA: two (row, block) items per thread per pass of up to
+  // 32 blocks (16 rows for wide matrices, 32 when a row has 16 blocks or fewer)
+  const bool r32 = !q4 && m[0]->nb <= 16;
+  const int per = q4 ? G4_ROWS : (r32 ? 32 : 16);
+  KqSegs S;
+  S.nb = m[0]->nb;
+  int ctas = 0;
+  for (int i = 0; i < 3; i++) {
+    KqSeg& g = S.s[i];
+    if (i < n) {
+      if (m[i]->type != m[0]->type || m[i]->nb != S.nb) return cudaErrorInvalidValue;
+      g = KqSeg{(const uint8_t*)m[i]->q, m[i]->d, m[i]->rows, ctas, out[i], epi[i], bias[i]};
+      ctas += (m[i]->rows + per - 1) / per;
+    } else {
+      g = KqSeg{nullptr, nullptr, 0, 0x7fffffff, nullptr, EPI_STORE, nullptr};
     }
-    e = launch_k(L, gemv_q4k_decode_kernel, (m.rows + D4_THREADS - 1) / D4_THREADS, D4_THREADS, smem,
-                 (const uint8_t*)m.q, m.rows, m.nb, a.qa_q, a.qa_d, out, epi, bias, L.err);
-  } else {
-    e = launch_k(L, gemv_q6k_decode_kernel, (m.rows + D6_WARPS - 1) / D6_WARPS, D6_WARPS * 32, 0,
-                 (const uint8_t*)m.q, m.d, m.rows, m.nb, a.qk_q, a.qk_d, out, epi, bias, L.err);
   }
+  if (ctas == 0) return cudaSuccess;
+  static unsigned long long attr_set = 0;  // one bit per device and kernel
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int kid = q4 ? 0 : (r32 ? 1 : 2);
+  const unsigned long long bit = 1ull << ((dev & 15) * 4 + kid);
+  cudaError_t e = cudaSuccess;
+  if (dev >= 16 || !(attr_set & bit)) {
+    e = q4 ? cudaFuncSetAttribute(gemv_q4k_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G4_SMEM)
+        : r32 ? cudaFuncSetAttribute(gemv_q6k_aux_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)g6_smem<32>())
+              : cudaFuncSetAttribute(gemv_q6k_aux_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)g6_smem<16>());
+    if (e != cudaSuccess) return e;
+    if (dev < 16) attr_set |= bit;
+  }
+  if (q4)
+    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_THREADS, G4_SMEM, S, a.qa_q, a.qa_d, L.err);
+  else if (r32)
+    e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
+  else
+    e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);
   if (e != cudaSuccess) return e;
   if (L.launches) ++*L.launches;
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
+                                  const float* bias) {
+  const DevMatrix* mm[1] = {&m};
+  float* oo[1] = {out};
+  const int ee[1] = {epi};
+  const float* bb[1] = {bias};
+  return launch_gemv_kq_decode_segs(L, mm, 1, a, oo, ee, bb);
 }
 
 cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,

@@ -123,6 +123,22 @@ cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& 
 // Q4_K / Q6_K matrix, one position (gemm_kq.cu)
 cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
                                   const float* bias);
+// up to three Q4_K (or three Q6_K) matrices of equal width that read the same
+// activation (q / k / v, gate / up), one position, one launch
+struct KqSeg {
+  const uint8_t* q;
+  const uint16_t* d;
+  int rows, cta0;
+  float* out;
+  int epi;
+  const float* bias;
+};
+struct KqSegs {
+  KqSeg s[3];
+  int nb;
+};
+cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
+                                       float* const* out, const int* epi, const float* const* bias);
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,

@@ -234,6 +234,28 @@ cudaError_t gemm_fused(det_session* s, int tag, const Launch& L, const DevMatrix
   return timed_gemm(s, tag, W, T, ob, [&] { return launch_gemm_mma16(L, W, a, T, o); });
 }
 
+// Matrices that read the same activation (q / k / v, gate / up) and can run
+// as one one-position launch: Q4_K or Q6_K, all of one type and width.
+bool kq_fusable(const DevMatrix* const* m, int n) {
+  for (int i = 0; i < n; i++)
+    if ((m[i]->type != GT_Q4_K && m[i]->type != GT_Q6_K) || m[i]->type != m[0]->type || m[i]->nb != m[0]->nb ||
+        m[i]->rows == 0)
+      return false;
+  return true;
+}
+
+// one launch over kq_fusable matrices, one position
+cudaError_t gemv_segs(det_session* s, int tag, const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
+                      float* const* out, const int* epi, const float* const* bias) {
+  double wb = 0, ob = 0;
+  for (int i = 0; i < n; i++) {
+    wb += (double)m[i]->rows * m[i]->cols * bytes_per_weight(m[i]->type);
+    ob += m[i]->rows * (epi[i] == EPI_RESIDUAL ? 8.0 : 4.0);
+  }
+  const double ab = (double)m[0]->cols * (m[0]->type == GT_Q6_K ? 1.0 + 4.0 / 256.0 : 1.0 + 4.0 / 32.0);
+  return timed(s, tag, wb + ab + ob, wb, [&] { return launch_gemv_kq_decode_segs(L, m, n, a, out, epi, bias); });
+}
+
 // quantise `x` (T x K) for a matrix of type `type` into the session buffers
 cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float* x, int K, int T, DevActs* a,
                          int* have) {
@@ -306,6 +328,11 @@ det_status fwd_attention(det_session* s, const Launch& L, int l, int T) {
     o.s[1] = OutSeg{W.wk.rows, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk};
     o.s[2] = OutSeg{W.wv.rows, s->v, kvd, W.bv ? EPI_BIAS : EPI_STORE, W.bv};
     CK(gemm_fused(s, PT_GEMM_QKV, L, W.wqkv, a, T, o));
+  } else if (const DevMatrix* mq[3] = {&W.wq, &W.wk, &W.wv}; T == 1 && kq_fusable(mq, 3)) {
+    float* const oo[3] = {s->q, s->k, s->v};
+    const int ee[3] = {W.bq ? EPI_BIAS : EPI_STORE, W.bk ? EPI_BIAS : EPI_STORE, W.bv ? EPI_BIAS : EPI_STORE};
+    const float* const bb[3] = {W.bq, W.bk, W.bv};
+    CK(gemv_segs(s, PT_GEMM_QKV, L, mq, 3, a, oo, ee, bb));
   } else {
     CK(gemv(s, PT_GEMM_QKV, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
     CK(gemv(s, PT_GEMM_QKV, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
@@ -353,6 +380,11 @@ det_status fwd_ffn_in(det_session* s, const Launch& L, int l, int T, int* have_o
     o.s[0] = OutSeg{W.gate.rows, s->gate, c.dff, EPI_STORE, nullptr};
     o.s[1] = OutSeg{W.up.rows, s->up, c.dff, EPI_STORE, nullptr};
     CK(gemm_fused(s, PT_GEMM_GATE_UP, L, W.wgu, a, T, o));
+  } else if (const DevMatrix* mg[2] = {&W.gate, &W.up}; T == 1 && kq_fusable(mg, 2)) {
+    float* const oo[2] = {s->gate, s->up};
+    const int ee[2] = {EPI_STORE, EPI_STORE};
+    const float* const bb[2] = {nullptr, nullptr};
+    CK(gemv_segs(s, PT_GEMM_GATE_UP, L, mg, 2, a, oo, ee, bb));
   } else {
     CK(gemv(s, PT_GEMM_GATE_UP, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
     CK(gemv(s, PT_GEMM_GATE_UP, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
@@ -784,6 +816,12 @@ det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per
         o.s[0] = OutSeg{W.wqkv.rows, s->logits, W.wqkv.rows, EPI_STORE, nullptr};
         e = launch_gemm_mma16(L, W.wqkv, a, 1, o);
         add_bytes(W.wqkv);
+      } else if (const DevMatrix* mq[3] = {&W.wq, &W.wk, &W.wv}; kq_fusable(mq, 3)) {
+        float* const oo[3] = {s->logits, s->logits + W.wq.rows, s->logits + W.wq.rows + W.wk.rows};
+        const int ee[3] = {EPI_STORE, EPI_STORE, EPI_STORE};
+        const float* const bb[3] = {nullptr, nullptr, nullptr};
+        e = launch_gemv_kq_decode_segs(L, mq, 3, a, oo, ee, bb);
+        for (const DevMatrix* Wm : mq) add_bytes(*Wm);
       } else {
         for (const DevMatrix* Wm : {&W.wq, &W.wk, &W.wv}) {
           if ((e = launch_gemv(L, *Wm, a, 1, s->logits, Wm->rows, EPI_STORE, nullptr)) != cudaSuccess) return e;
@@ -799,6 +837,12 @@ det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per
         o.s[0] = OutSeg{W.wgu.rows, s->logits, W.wgu.rows, EPI_STORE, nullptr};
         e = launch_gemm_mma16(L, W.wgu, a, 1, o);
         add_bytes(W.wgu);
+      } else if (const DevMatrix* mg[2] = {&W.gate, &W.up}; kq_fusable(mg, 2)) {
+        float* const oo[2] = {s->logits, s->logits + W.gate.rows};
+        const int ee[2] = {EPI_STORE, EPI_STORE};
+        const float* const bb[2] = {nullptr, nullptr};
+        e = launch_gemv_kq_decode_segs(L, mg, 2, a, oo, ee, bb);
+        for (const DevMatrix* Wm : mg) add_bytes(*Wm);
       } else {
         for (const DevMatrix* Wm : {&W.gate, &W.up}) {
           if ((e = launch_gemv(L, *Wm, a, 1, s->logits, Wm->rows, EPI_STORE, nullptr)) != cudaSuccess) return e;

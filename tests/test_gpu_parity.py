@@ -27,6 +27,11 @@ SPECS = {
                            t_out=S.GT_Q6_K, seed=5),
     "qwen2_bias_tied_q4_0": S.ModelSpec(arch="qwen2", n_layer=2, d=128, d_ff=256, n_head=2, n_head_kv=1, vocab=600,
                                         ctx=64, tied=True, qkv_bias=True, rope_base=1e6, t_attn=S.GT_Q4_0, seed=9),
+    # one-position K-quant kernels: a Q6_K ffn_down 8448 wide (two passes of
+    # 32 blocks) and 1000 output rows (a ragged 32-row tile)
+    "q4k_q6k_wide_ffn": S.ModelSpec(n_layer=1, d=256, d_ff=8448, n_head=4, n_head_kv=2, vocab=1000, ctx=64,
+                                    t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
+                                    t_out=S.GT_Q6_K, seed=6),
     "f16_f32_escapes": S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=2, vocab=300, ctx=32,
                                    t_embd=S.GT_F16, t_attn=S.GT_F32, t_gate_up=S.GT_F16, t_down=S.GT_Q8_0,
                                    t_out=S.GT_F32, escape_bytes=(10, 32, 65), seed=3),
