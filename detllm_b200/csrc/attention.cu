@@ -395,11 +395,15 @@ int score_ld(int n_ctx) { return (n_ctx + 31) & ~31; }
 // threads into shared memory, the eight ordered Z chains by eight threads,
 // p = e / Z by all.  PV gives each (KV head, 16 dims, position) a CTA with one
 // ordered chain o[d] += p_j v_j[d] per thread, over 32-key tiles of P and V
-// staged with cp.async (double-buffered); as in the chunked path the rows
-// are zero past their length, so whole tiles are summed exactly.
+// staged with cp.async, PD_STAGES tiles in flight (a tile's 32 adds are far
+// shorter than a load from HBM); as in the chunked path the rows are zero
+// past their length, so whole tiles are summed exactly.
 constexpr int SD_THREADS = 256;
 constexpr int PD_KEYS = 32;
 constexpr int PD_DIMS = 16;
+constexpr int PD_STAGES = 8;
+DI int pd_ps_floats(int gsz) { return PD_STAGES * gsz * PD_KEYS; }
+inline size_t pd_smem_bytes(int gsz) { return (size_t)PD_STAGES * (gsz * PD_KEYS + PD_KEYS * PD_DIMS) * sizeof(float); }
 
 __global__ void __launch_bounds__(SD_THREADS) attn_softmax_row_kernel(float* __restrict__ S, const int* pos0p,
                                                                      int n_head, int s_ld, uint32_t* err) {
@@ -463,8 +467,9 @@ __global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* 
                                       int n_head, int gsz, int n_ctx, int s_ld, float* __restrict__ out,
                                       uint32_t* err) {
   pdl_enter();
-  __shared__ __align__(16) float ps[2][32][PD_KEYS];     // gsz <= 32 rows
-  __shared__ __align__(16) float vs[2][PD_KEYS][PD_DIMS];
+  extern __shared__ __align__(16) float pd_smem[];
+  float* ps = pd_smem;                     // [PD_STAGES][gsz][PD_KEYS]
+  float* vs = pd_smem + pd_ps_floats(gsz);  // [PD_STAGES][PD_KEYS][PD_DIMS]
   const int kvh = blockIdx.x, d0 = blockIdx.y * PD_DIMS, t = blockIdx.z;
   const int tid = threadIdx.x, nt = blockDim.x;
   const int h = tid / PD_DIMS, dd = tid - h * PD_DIMS;
@@ -476,36 +481,40 @@ __global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* 
     return;
   }
   const float* prow0 = P + ((size_t)t * n_head + kvh * gsz) * s_ld;
+  const int ntile = (len + PD_KEYS - 1) / PD_KEYS;
+  // tile k into stage k % PD_STAGES; an empty commit group past the last
+  // tile keeps the wait count uniform
   auto load_tile = [&](int k) {
-    const int jc = k * PD_KEYS, bf = k & 1;
-    for (int i = tid; i < gsz * (PD_KEYS / 4); i += nt) {
-      const int r = i / (PD_KEYS / 4), c4 = (i - r * (PD_KEYS / 4)) * 4;
-      cp_async16(&ps[bf][r][c4], prow0 + (size_t)r * s_ld + jc + c4);
-    }
-    for (int i = tid; i < PD_KEYS * (PD_DIMS / 4); i += nt) {
-      const int jj = i / (PD_DIMS / 4), c4 = (i - jj * (PD_DIMS / 4)) * 4;
-      if (jc + jj < len)
-        cp_async16(&vs[bf][jj][c4], vb + (size_t)(jc + jj) * HD + d0 + c4);
-      else
-        *reinterpret_cast<float4*>(&vs[bf][jj][c4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < ntile) {
+      const int jc = k * PD_KEYS, bf = k % PD_STAGES;
+      float* pb = ps + bf * gsz * PD_KEYS;
+      float* vbuf = vs + bf * PD_KEYS * PD_DIMS;
+      for (int i = tid; i < gsz * (PD_KEYS / 4); i += nt) {
+        const int r = i / (PD_KEYS / 4), c4 = (i - r * (PD_KEYS / 4)) * 4;
+        cp_async16(pb + r * PD_KEYS + c4, prow0 + (size_t)r * s_ld + jc + c4);
+      }
+      for (int i = tid; i < PD_KEYS * (PD_DIMS / 4); i += nt) {
+        const int jj = i / (PD_DIMS / 4), c4 = (i - jj * (PD_DIMS / 4)) * 4;
+        if (jc + jj < len)
+          cp_async16(vbuf + jj * PD_DIMS + c4, vb + (size_t)(jc + jj) * HD + d0 + c4);
+        else
+          *reinterpret_cast<float4*>(vbuf + jj * PD_DIMS + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
     cp_async_commit();
   };
   float acc = 0.0f;
-  const int ntile = (len + PD_KEYS - 1) / PD_KEYS;
-  load_tile(0);
+  for (int k = 0; k < PD_STAGES - 1; k++) load_tile(k);
   for (int k = 0; k < ntile; k++) {
-    if (k + 1 < ntile) {
-      load_tile(k + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    load_tile(k + PD_STAGES - 1);
+    cp_async_wait<PD_STAGES - 1>();  // tile k has landed
     __syncthreads();
-    const int bf = k & 1;
+    const int bf = k % PD_STAGES;
+    const float* pr = ps + (bf * gsz + h) * PD_KEYS;
+    const float* vr = vs + bf * PD_KEYS * PD_DIMS + dd;
 #pragma unroll 8
-    for (int jj = 0; jj < PD_KEYS; jj++) acc = fadd(acc, fmul(ps[bf][h][jj], vs[bf][jj][dd]));
-    __syncthreads();
+    for (int jj = 0; jj < PD_KEYS; jj++) acc = fadd(acc, fmul(pr[jj], vr[jj * PD_DIMS]));
+    __syncthreads();  // stage bf is refilled by the next iteration's load
   }
   if (!finite(acc)) atomicOr(err, ERRF_NONFINITE);
   *ob = acc;
@@ -548,8 +557,8 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
       if (e_ != cudaSuccess) return e_;
     }
     {
-      const cudaError_t e_ = launch_k(L, attn_pv_decode_kernel<HD>, dim3(n_head_kv, HD / PD_DIMS, T), gsz * PD_DIMS, 0,
-                                      S, vc, pos0, n_head, gsz, n_ctx, s_ld, out, L.err);
+      const cudaError_t e_ = launch_k(L, attn_pv_decode_kernel<HD>, dim3(n_head_kv, HD / PD_DIMS, T), gsz * PD_DIMS,
+                                      pd_smem_bytes(gsz), S, vc, pos0, n_head, gsz, n_ctx, s_ld, out, L.err);
       if (e_ != cudaSuccess) return e_;
     }
     if (L.launches) *L.launches += 3;

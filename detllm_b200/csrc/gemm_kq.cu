@@ -304,19 +304,63 @@ DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
 
 // Q4_K: each row is one f32 chain over all K elements (sum += w * act, in
 // order), so its length sets a floor of K dependent adds per launch.  A CTA
-// takes 32 rows: warps 0-7 (producers) dequantise super-block b of the 32
+// takes 32 rows: warps 0-7 (producers) dequantise super-block s of the 32
 // rows -- warp w sub-block w, lane r row r -- and write the products
-// w * act into a shared-memory stage, while warp 8 runs the 32 row chains
-// (lane = row) through the previous stage.  Producers load each stage's
-// weights and activation two stages ahead, so HBM latency stays off the
-// chain.  Stage rows are 260 floats apart and both sides move 16-byte
-// vectors (the eight lanes of a quarter-warp hit distinct bank groups); the
-// chain loads 32 values ahead of its adds, so only the add latency is serial.
+// w * act into stage buffer s % 3, while warp 8 runs the 32 row chains
+// (lane = row) through the stages in order.  Producers and chain meet only
+// at named hardware barriers: FULL[i] (producers arrive after writing buffer
+// i, the chain waits) and EMPTY[i] (the chain arrives after reading it, the
+// producers wait before writing it again), so producers run up to two
+// stages ahead.  Producers load each stage's weights and activation two
+// stages before they use them, and do their arithmetic as f32x2 pairs.
+// Stage rows are 260 floats apart and both sides move 16-byte vectors (the
+// eight lanes of a quarter-warp hit distinct bank groups).
 constexpr int G4_ROWS = 32;
 constexpr int G4_PWARPS = 8;
 constexpr int G4_THREADS = (G4_PWARPS + 1) * 32;
 constexpr int G4_LD = 260;
-constexpr size_t G4_SMEM = (size_t)(2 * G4_ROWS * G4_LD + 256) * sizeof(float);
+constexpr int G4_NBUF = 3;
+constexpr size_t G4_SMEM = (size_t)(G4_NBUF * G4_ROWS * G4_LD + 256) * sizeof(float);
+constexpr int G4_BAR_FULL = 1, G4_BAR_EMPTY = 1 + G4_NBUF;  // named barriers 1..6 (0 is __syncthreads)
+static_assert(G4_NBUF == 3, "nbar_*_buf dispatch three buffers");
+
+// barrier ids are immediates (a register id makes the CTA reserve all 16)
+template <int ID>
+DI void nbar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(G4_THREADS) : "memory");
+}
+template <int ID>
+DI void nbar_arrive() {
+  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(G4_THREADS) : "memory");
+}
+template <int BASE>
+DI void nbar_sync_buf(int buf) {
+  if (buf == 0) nbar_sync<BASE>();
+  else if (buf == 1) nbar_sync<BASE + 1>();
+  else nbar_sync<BASE + 2>();
+}
+template <int BASE>
+DI void nbar_arrive_buf(int buf) {
+  if (buf == 0) nbar_arrive<BASE>();
+  else if (buf == 1) nbar_arrive<BASE + 1>();
+  else nbar_arrive<BASE + 2>();
+}
+
+DI unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+DI unsigned long long mul2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+DI unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 
 struct Q4Stage {
   uint4 h, v0, v1;  // block header (d, dmin, scales) and the sub-block pair's 32 quant bytes
@@ -328,8 +372,8 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
                                                                     const float* __restrict__ ad, uint32_t* err) {
   pdl_enter();
   extern __shared__ float g4_smem[];
-  float* prod = g4_smem;                        // [2][G4_ROWS][G4_LD]
-  float* actb = g4_smem + 2 * G4_ROWS * G4_LD;  // [256]: sub-block w at [32 w, 32 w + 32)
+  float* prod = g4_smem;                               // [G4_NBUF][G4_ROWS][G4_LD]
+  float* actb = g4_smem + G4_NBUF * G4_ROWS * G4_LD;  // [256]: sub-block w at [32 w, 32 w + 32)
   const KqSeg g = kq_seg(S);
   const int r0 = ((int)blockIdx.x - g.cta0) * G4_ROWS;
   const int nbs = S.nb, nbk = nbs * 8;
@@ -337,77 +381,83 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
   const int row = r0 + lane;
   const bool ok = row < g.rows;
 
-  auto load = [&](int b, Q4Stage& st) {
-    const int kb = b * 8 + warp;
-    st.ad = ad[q8a_dslot(nbk, 0, kb)];
-    st.aq = aq[q8a_elem(nbk, 0, kb, lane)];
-    if (ok) {
-      const uint8_t* blk = g.q + ((size_t)row * nbs + b) * 144;
-      st.h = *reinterpret_cast<const uint4*>(blk);
-      st.v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
-      st.v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
-    }
-  };
-  // products of one stage into buffer `buf` (producer warps only)
-  auto compute = [&](const Q4Stage& st, int buf) {
-    actb[warp * 32 + lane] = fmul(st.ad, (float)st.aq);
-    __syncwarp();
-    float* dst = prod + (buf * G4_ROWS + lane) * G4_LD + warp * 32;
-    if (!ok) {
-#pragma unroll
-      for (int e4 = 0; e4 < 32; e4 += 4) *reinterpret_cast<float4*>(dst + e4) = make_float4(0.f, 0.f, 0.f, 0.f);
-      return;
-    }
-    const uint4 h = st.h;
-    const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
-    const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
-    // q4_k_scale_min (det-quant lib.rs:516-529) on the packed bytes
-    int sc, mn;
-    if (warp < 4) {
-      sc = (int)(q4k_sbyte(h, warp) & 63u);
-      mn = (int)(q4k_sbyte(h, warp + 4) & 63u);
-    } else {
-      sc = (int)((q4k_sbyte(h, warp + 4) & 0x0fu) | ((q4k_sbyte(h, warp - 4) >> 6) << 4));
-      mn = (int)((q4k_sbyte(h, warp + 4) >> 4) | ((q4k_sbyte(h, warp) >> 6) << 4));
-    }
-    const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-    const uint32_t qw[8] = {st.v0.x, st.v0.y, st.v0.z, st.v0.w, st.v1.x, st.v1.y, st.v1.z, st.v1.w};
-    const int sh = 4 * (warp & 1);
-    const float* av = actb + warp * 32;
-#pragma unroll
-    for (int e4 = 0; e4 < 32; e4 += 4) {
-      float p[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int e = e4 + j;
-        const uint32_t q = (qw[e >> 2] >> (8 * (e & 3) + sh)) & 0x0fu;
-        const float qf = __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);  // exact
-        p[j] = fmul(fsub(fmul(dsc, qf), dmn), av[e]);
-      }
-      *reinterpret_cast<float4*>(dst + e4) = make_float4(p[0], p[1], p[2], p[3]);
-    }
-  };
-
-  // stage b lives in slot b % 3; the loop is unrolled by three so each slot
-  // keeps its registers (copying a register whose load is in flight would
-  // wait for the load)
-  Q4Stage st0{}, st1{}, st2{};
   if (warp < G4_PWARPS) {
+    // a row past the matrix keeps zero weights, so its products are 0
+    auto load = [&](int s, Q4Stage& st) {
+      const int kb = s * 8 + warp;
+      st.ad = ad[q8a_dslot(nbk, 0, kb)];
+      st.aq = aq[q8a_elem(nbk, 0, kb, lane)];
+      if (ok) {
+        const uint8_t* blk = g.q + ((size_t)row * nbs + s) * 144;
+        st.h = *reinterpret_cast<const uint4*>(blk);
+        st.v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
+        st.v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
+      }
+    };
+    const unsigned long long one2 = pk2(S.one, S.one), nmag2 = pk2(-8388608.0f, -8388608.0f);
+    // w * act for this warp's sub-block of stage `st` into buffer `buf`
+    auto compute = [&](const Q4Stage& st, int buf) {
+      actb[warp * 32 + lane] = fmul(st.ad, (float)st.aq);
+      __syncwarp();
+      const uint4 h = st.h;
+      const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
+      const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+      // q4_k_scale_min (det-quant lib.rs:516-529) on the packed bytes
+      int sc, mn;
+      if (warp < 4) {
+        sc = (int)(q4k_sbyte(h, warp) & 63u);
+        mn = (int)(q4k_sbyte(h, warp + 4) & 63u);
+      } else {
+        sc = (int)((q4k_sbyte(h, warp + 4) & 0x0fu) | ((q4k_sbyte(h, warp - 4) >> 6) << 4));
+        mn = (int)((q4k_sbyte(h, warp + 4) >> 4) | ((q4k_sbyte(h, warp) >> 6) << 4));
+      }
+      const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+      const unsigned long long dsc2 = pk2(dsc, dsc), ndmn2 = pk2(-dmn, -dmn);
+      const uint32_t qw[8] = {st.v0.x, st.v0.y, st.v0.z, st.v0.w, st.v1.x, st.v1.y, st.v1.z, st.v1.w};
+      const int sh = 4 * (warp & 1);
+      const float4* av = reinterpret_cast<const float4*>(actb + warp * 32);
+      float* dst = prod + (buf * G4_ROWS + lane) * G4_LD + warp * 32;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {  // elements 4k .. 4k + 3
+        const uint32_t nib = (qw[k] >> sh) & 0x0f0f0f0fu;
+        // 2^23 + q as f32 bits, minus 2^23: q exactly
+        const float m0 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540));
+        const float m1 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7541));
+        const float m2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542));
+        const float m3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543));
+        const float4 a = av[k];
+        // w = (d*sc)*q - (dmin*m) as fma(p, one, -dmn) (one == 1.0 at run
+        // time: exact, and not contractible with the multiply), then w * act
+        const unsigned long long w01 = fma2(mul2(dsc2, add2(pk2(m0, m1), nmag2)), one2, ndmn2);
+        const unsigned long long w23 = fma2(mul2(dsc2, add2(pk2(m2, m3), nmag2)), one2, ndmn2);
+        const float2 r01 = up2(mul2(w01, pk2(a.x, a.y)));
+        const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
+        *reinterpret_cast<float4*>(dst + 4 * k) = make_float4(r01.x, r01.y, r23.x, r23.y);
+      }
+      __syncwarp();  // actb is rewritten by this warp's next stage
+    };
+    // stage s: load stage s + 2 into `ld_slot` (stage s - 1's), wait until
+    // the chain has released buffer `buf`, write it, signal it full
+    auto pstep = [&](int s, int buf, Q4Stage& ld_slot, const Q4Stage& cur) {
+      if (s + 2 < nbs) load(s + 2, ld_slot);
+      if (s >= G4_NBUF) nbar_sync_buf<G4_BAR_EMPTY>(buf);
+      compute(cur, buf);
+      nbar_arrive_buf<G4_BAR_FULL>(buf);
+    };
+    Q4Stage st0{}, st1{}, st2{};  // stage s lives in slot s % 3
     load(0, st0);
     if (nbs > 1) load(1, st1);
-    if (nbs > 2) load(2, st2);
-    compute(st0, 0);
-  }
-  __syncthreads();
-  float sum = 0.0f;
-  // step b: load stage b + 3 into the slot stage b used, compute stage b + 1
-  // from its slot, and run the chains through stage b
-  auto step = [&](int b, Q4Stage& ld_slot, const Q4Stage& next) {
-    if (warp < G4_PWARPS) {
-      if (b + 3 < nbs) load(b + 3, ld_slot);
-      if (b + 1 < nbs) compute(next, (b + 1) & 1);
-    } else {
-      const float4* src = reinterpret_cast<const float4*>(prod + ((b & 1) * G4_ROWS + lane) * G4_LD);
+    for (int s = 0; s < nbs; s += 3) {
+      pstep(s, 0, st2, st0);
+      if (s + 1 < nbs) pstep(s + 1, 1, st0, st1);
+      if (s + 2 < nbs) pstep(s + 2, 2, st1, st2);
+    }
+  } else {
+    float sum = 0.0f;
+    for (int s = 0; s < nbs; s++) {
+      const int buf = s % G4_NBUF;
+      nbar_sync_buf<G4_BAR_FULL>(buf);
+      const float4* src = reinterpret_cast<const float4*>(prod + (buf * G4_ROWS + lane) * G4_LD);
 #pragma unroll 1
       for (int e4 = 0; e4 < 64; e4 += 8) {
         float4 v[8];
@@ -421,15 +471,10 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
           sum = fadd(sum, v[j].w);
         }
       }
+      if (s + G4_NBUF < nbs) nbar_arrive_buf<G4_BAR_EMPTY>(buf);
     }
-    __syncthreads();
-  };
-  for (int b = 0; b < nbs; b += 3) {
-    step(b, st0, st1);
-    if (b + 1 < nbs) step(b + 1, st1, st2);
-    if (b + 2 < nbs) step(b + 2, st2, st0);
+    if (ok) kq_store(g, row, sum, err);
   }
-  if (warp == G4_PWARPS && ok) kq_store(g, row, sum, err);
 }
 
 // Q6_K: per block the reference forms eight exact integer lane sums

@@ -136,6 +136,7 @@ struct KqSeg {
 struct KqSegs {
   KqSeg s[3];
   int nb;
+  float one = 1.0f;  // passed at run time (see OutSegs::one)
 };
 cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
                                        float* const* out, const int* epi, const float* const* bias);

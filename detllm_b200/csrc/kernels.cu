@@ -190,8 +190,9 @@ __global__ void swiglu_q8a_kernel(const float* __restrict__ g, const float* __re
 
 // ---- rmsnorm (det-model lib.rs:2053-2073) ----------------------------------
 // sum_squares_f32_ref: lane l accumulates x[i]^2 for i = l (mod 8) in order.
-// The row is staged in shared memory by all threads (coalesced), then eight
-// threads run the eight ordered lane chains out of shared memory.
+// The row and the norm weights are staged in shared memory by all threads
+// (coalesced, one load latency), then eight threads run the eight ordered
+// lane chains out of shared memory.
 constexpr int RMS_MAX_SMEM = 16384;  // floats staged per row (larger rows read global)
 
 // When qd / qq are given (n a multiple of 32), the normalised row is also
@@ -200,16 +201,20 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
                                float* __restrict__ h, float* __restrict__ qd, int8_t* __restrict__ qq,
                                uint32_t* err) {
   pdl_enter();
-  extern __shared__ float xs[];
+  extern __shared__ float xs[];  // [n] x, then [n] w
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * n;
   __shared__ float lanes[8];
   __shared__ float r_s;
   const bool staged = n <= RMS_MAX_SMEM;
   if (staged)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      xs[i] = xr[i];
+      xs[n + i] = w[i];
+    }
   __syncthreads();
   const float* src = staged ? xs : xr;
+  const float* wv = staged ? xs + n : w;
   if (threadIdx.x < 8) {
     float acc = 0.0f;
     int i = threadIdx.x;
@@ -238,7 +243,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     for (int kb = threadIdx.x >> 5; kb < nbk; kb += blockDim.x >> 5) {
       const int i = kb * 32 + l;
       const float xi = src[i];
-      const float v = fmul(fmul(xi, r), w[i]);
+      const float v = fmul(fmul(xi, r), wv[i]);
       if (!finite(v) || !finite(xi)) flag(err, ERRF_NONFINITE);
       h[(size_t)t * n + i] = v;
       q8a_block_warp(v, l, nbk, t, kb, qd, qq);
@@ -247,7 +252,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   }
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float xi = src[i];
-    const float v = fmul(fmul(xi, r), w[i]);
+    const float v = fmul(fmul(xi, r), wv[i]);
     if (!finite(v) || !finite(xi)) flag(err, ERRF_NONFINITE);
     h[(size_t)t * n + i] = v;
   }
@@ -880,14 +885,16 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
 
 cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h,
                            float* qd, int8_t* qq) {
-  const size_t smem = n <= RMS_MAX_SMEM ? (size_t)n * sizeof(float) : 0;
+  const size_t smem = n <= RMS_MAX_SMEM ? 2 * (size_t)n * sizeof(float) : 0;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   if (n % 32) qd = nullptr, qq = nullptr;
+  // a short chunk is one or a few CTAs: more warps share the quantisation
+  const int threads = T <= 16 ? 1024 : 256;
   {
-    const cudaError_t e_ = launch_k(L, rmsnorm_kernel, T, 256, smem, x, w, n, eps, h, qd, qq, L.err);
+    const cudaError_t e_ = launch_k(L, rmsnorm_kernel, T, threads, smem, x, w, n, eps, h, qd, qq, L.err);
     if (e_ != cudaSuccess) return e_;
   }
   return post(L);
