@@ -179,6 +179,20 @@ struct GatherPlan {
   int n = 0;
 };
 cudaError_t launch_gather_cols(const Launch& L, const GatherPlan& g, float* dst, int ld_dst, int T);
+// Parts on distinct GPUs order their exchanges themselves (exchange.cu):
+// `peer[q]` is this part's counter slot in part q's flag array (null for
+// q == self), `mine` this part's own array, one slot per part.
+struct TpFlags {
+  unsigned long long* peer[kMaxTpParts];
+  const unsigned long long* mine;
+  int parts;
+};
+// signal exchange k of the current forward (counter *epoch * nx + k + 1),
+// wait (bounded) for the parts in wait_mask, then pull `g` into dst
+cudaError_t launch_tp_exchange(const Launch& L, const TpFlags& f, const unsigned long long* epoch, int k, int nx,
+                               unsigned wait_mask, const GatherPlan& g, float* dst, int ld_dst, int T);
+// *epoch += 1 (the start of a forward)
+cudaError_t launch_tp_epoch(const Launch& L, unsigned long long* epoch);
 cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
                                   const uint64_t* value, uint64_t* out4);
 

@@ -13,9 +13,17 @@
 //   SwiGLU output, before ffn_down
 //   residual x, after ffn_down
 // and after the lm_head the primary part (devices[0], which runs the CDF)
-// gathers the logits.  exchange.cu does the copies; this file plans them,
-// orders them with events and captures the whole multi-device forward in one
-// CUDA graph per chunk size.
+// gathers the logits.  exchange.cu does the copies; this file plans them and
+// orders them one of two ways:
+//  * parts on distinct GPUs: each part runs its own stream (one CUDA graph
+//    per part and chunk size), and each exchange is one kernel that signals
+//    the peers through counters in their memory, waits for theirs (bounded)
+//    and pulls; with replicated attention a data-free exchange stands in for
+//    the attention exchange;
+//  * parts sharing a GPU (kernels that wait on one another must never share
+//    one): host events order the pulls, and the whole multi-device forward is
+//    captured in one CUDA graph per chunk size.  DETGPU_TP_EVENTS=1 selects
+//    this form for distinct GPUs too.
 //
 // Ordering.  A gather waits for every other part's event recorded after
 // that part wrote its slice (read-after-write).  A part rewrites a slice
@@ -27,12 +35,16 @@
 // exchange does not exist, after a wait on every part's `done` event of the
 // previous layer's last gather.  Eager forwards also wait, on entry, for the
 // other parts' last exchange of the previous forward; a graph forward is one
-// unit on part 0's stream.
+// unit on part 0's stream.  The device-side form keeps the same order: each
+// exchange kernel is an all-to-all barrier (it signals, then waits for every
+// peer), the replicated-attention barrier takes the place of the `done` wait,
+// and det_forward synchronises every part before it returns.
 //
 // Weights: one replica per distinct device; each part's model (a "shard")
 // views its replica's matrices through row offsets and owns only the fused
 // q|k|v and gate|up buffers of its slices.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -50,6 +62,10 @@ struct TpModel {
 
 struct TpSession {
   std::vector<det_session*> parts;   // [0] is the session the caller holds
+  // distinct GPUs: device-side ordering (flag[p]: part p's counters, one per
+  // part; epoch[p]: forwards started on part p)
+  bool device_sync = false;
+  std::vector<unsigned long long*> flag, epoch;
   // per part, recorded at every exchange: [0] eager forwards, [1] inside
   // graph captures (an event recorded in a capture is not waited on outside)
   std::vector<cudaEvent_t> ev[2];
@@ -235,7 +251,8 @@ det_status make_shard(det_model* R, int p, int G, bool attn_sharded, det_model**
 }
 
 // ---- the forward ------------------------------------------------------------
-enum XKind { X_ATTN, X_RESID, X_FF, X_LOGITS };
+// X_BARRIER: no data, every part waits for every other (device-side form)
+enum XKind { X_ATTN, X_RESID, X_FF, X_LOGITS, X_BARRIER };
 
 det_status set_dev(const det_session* s) { return cuda_status(cudaSetDevice(s->m->device)); }
 
@@ -243,6 +260,50 @@ Launch part_launch(det_session* s, uint64_t* counter) {
   Launch L{s->stream, s->d_err, counter};
   L.pdl = false;
   return L;
+}
+
+// The slices part p pulls for an exchange of `kind` into *dst (row stride *ld).
+GatherPlan plan_for(TpSession& ts, XKind kind, int p, float** dst, int* ld) {
+  const int G = (int)ts.parts.size();
+  det_session* sp = ts.parts[(size_t)p];
+  GatherPlan g;
+  *dst = nullptr;
+  *ld = 0;
+  for (int q = 0; q < G && kind != X_BARRIER; q++) {
+    if ((kind == X_RESID || kind == X_LOGITS) && q == p) continue;
+    det_session* sq = ts.parts[(size_t)q];
+    const TpShard& sh = *sq->m->shard;
+    const ModelCfg& full = sh.full;
+    GatherSrc src{nullptr, 0, 0, 0};
+    switch (kind) {
+      case X_ATTN: {
+        const int qd = sq->m->cfg.nh * full.hd;
+        src = GatherSrc{sq->attn, qd, sh.h0 * (full.nh / full.nkv) * full.hd, qd};
+        *dst = sp->attn_full;
+        *ld = full.nh * full.hd;
+        break;
+      }
+      case X_RESID:
+        src = GatherSrc{sq->x + sh.d0, full.d, sh.d0, sh.d1 - sh.d0};
+        *dst = sp->x;
+        *ld = full.d;
+        break;
+      case X_FF:
+        src = GatherSrc{sq->ff, sh.f1 - sh.f0, sh.f0, sh.f1 - sh.f0};
+        *dst = sp->ff_full;
+        *ld = full.dff;
+        break;
+      case X_LOGITS:
+        src = GatherSrc{sq->logits + sh.v0, sq->m->vocab, sh.v0, sh.v1 - sh.v0};
+        *dst = sp->logits;
+        *ld = sq->m->vocab;
+        break;
+      case X_BARRIER:
+        break;
+    }
+    if (src.n > 0) g.s[g.n++] = src;
+  }
+  return g;
 }
 
 // Every part records its event; each part that gathers waits for the
@@ -263,41 +324,9 @@ det_status exchange(TpSession& ts, XKind kind, int T, uint64_t* counter, bool ca
     if (det_status st = set_dev(sp)) return st;
     for (int q = 0; q < G; q++)
       if (q != p) CK(cudaStreamWaitEvent(sp->stream, ev[(size_t)q], 0));
-    GatherPlan g;
     float* dst = nullptr;
     int ld = 0;
-    for (int q = 0; q < G; q++) {
-      if ((kind == X_RESID || kind == X_LOGITS) && q == p) continue;
-      det_session* sq = ts.parts[(size_t)q];
-      const TpShard& sh = *sq->m->shard;
-      const ModelCfg& full = sh.full;
-      GatherSrc src{nullptr, 0, 0, 0};
-      switch (kind) {
-        case X_ATTN: {
-          const int qd = sq->m->cfg.nh * full.hd;
-          src = GatherSrc{sq->attn, qd, sh.h0 * (full.nh / full.nkv) * full.hd, qd};
-          dst = sp->attn_full;
-          ld = full.nh * full.hd;
-          break;
-        }
-        case X_RESID:
-          src = GatherSrc{sq->x + sh.d0, full.d, sh.d0, sh.d1 - sh.d0};
-          dst = sp->x;
-          ld = full.d;
-          break;
-        case X_FF:
-          src = GatherSrc{sq->ff, sh.f1 - sh.f0, sh.f0, sh.f1 - sh.f0};
-          dst = sp->ff_full;
-          ld = full.dff;
-          break;
-        case X_LOGITS:
-          src = GatherSrc{sq->logits + sh.v0, sq->m->vocab, sh.v0, sh.v1 - sh.v0};
-          dst = sp->logits;
-          ld = sq->m->vocab;
-          break;
-      }
-      if (src.n > 0) g.s[g.n++] = src;
-    }
+    const GatherPlan g = plan_for(ts, kind, p, &dst, &ld);
     CK(launch_gather_cols(part_launch(sp, counter), g, dst, ld, T));
     if (mark_done) CK(cudaEventRecord(ts.done[capture ? 1 : 0][(size_t)p], sp->stream));
   }
@@ -385,6 +414,105 @@ det_status tp_enqueue(det_session* s0, int T, uint64_t* counter, bool capture) {
   return set_dev(s0);
 }
 
+// ---- distinct GPUs: one stream per part, device-side exchanges ---------------
+// exchange k (0-based, nx per forward) of part p
+det_status exchange_device(TpSession& ts, int p, XKind kind, int k, int nx, int T, const Launch& L) {
+  const int G = (int)ts.parts.size();
+  TpFlags f{};
+  f.parts = G;
+  f.mine = ts.flag[(size_t)p];
+  unsigned wait = 0;
+  for (int q = 0; q < G; q++) {
+    f.peer[q] = q == p ? nullptr : ts.flag[(size_t)q] + p;
+    if (q != p) wait |= 1u << q;
+  }
+  // logits: the other parts only signal; part 0 waits and pulls
+  if (kind == X_LOGITS && p != 0) wait = 0;
+  float* dst = nullptr;
+  int ld = 0;
+  GatherPlan g;
+  if (!(kind == X_LOGITS && p != 0)) g = plan_for(ts, kind, p, &dst, &ld);
+  CK(launch_tp_exchange(L, f, ts.epoch[(size_t)p], k, nx, wait, g, dst, ld, T));
+  return DET_OK;
+}
+
+// one chunk forward of part p on its own stream
+det_status tp_enqueue_part(TpSession& ts, int p, int T, uint64_t* counter) {
+  det_session* s = ts.parts[(size_t)p];
+  if (det_status st = set_dev(s)) return st;
+  Launch L{s->stream, s->d_err, counter};
+  L.pdl = T <= 16;  // as on one device
+  CK(cudaMemcpyAsync(s->d_tokens, s->h_tokens, (size_t)T * 4, cudaMemcpyHostToDevice, s->stream));
+  CK(cudaMemcpyAsync(s->d_pos, s->h_pos, 4, cudaMemcpyHostToDevice, s->stream));
+  CK(launch_tp_epoch(L, ts.epoch[(size_t)p]));
+  if (det_status st = fwd_embed(s, L, T)) return st;
+  const bool attn_sharded = s->m->shard->attn_sharded;
+  const int nl = s->m->cfg.L, nx = 4 * nl + 1;
+  int k = 0;
+  for (int l = 0; l < nl; l++) {
+    if (det_status st = fwd_attention(s, L, l, T)) return st;
+    // replicated attention: a barrier in its place keeps wo from rewriting
+    // this part's slice of x before the others have pulled it
+    if (det_status st = exchange_device(ts, p, attn_sharded ? X_ATTN : X_BARRIER, k++, nx, T, L)) return st;
+    if (det_status st = fwd_attn_out(s, L, l, T, attn_sharded ? s->attn_full : s->attn)) return st;
+    if (det_status st = exchange_device(ts, p, X_RESID, k++, nx, T, L)) return st;
+    int have = 0;
+    if (det_status st = fwd_ffn_in(s, L, l, T, &have)) return st;
+    if (det_status st = exchange_device(ts, p, X_FF, k++, nx, T, L)) return st;
+    if (det_status st = fwd_ffn_out(s, L, l, T, s->ff_full, 0)) return st;
+    if (det_status st = exchange_device(ts, p, X_RESID, k++, nx, T, L)) return st;
+  }
+  if (det_status st = fwd_head(s, L, T)) return st;
+  return exchange_device(ts, p, X_LOGITS, k++, nx, T, L);
+}
+
+det_status tp_run_device(det_session* s0, int T, bool graphs) {
+  TpSession& ts = *s0->tp;
+  const int G = (int)ts.parts.size();
+  if (!graphs) {
+    for (int p = 0; p < G; p++)
+      if (det_status st = tp_enqueue_part(ts, p, T, &s0->stats.launches)) return st;
+    return set_dev(s0);
+  }
+  for (int p = 0; p < G; p++) {
+    det_session* s = ts.parts[(size_t)p];
+    if ((int)s->graphs.size() <= T) s->graphs.resize((size_t)T + 1);
+    det_session::Graph& gr = s->graphs[(size_t)T];
+    if (gr.exec) continue;
+    if (det_status st = set_dev(s)) return st;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    uint64_t count = 0;
+    const det_status st = tp_enqueue_part(ts, p, T, &count);
+    cudaSetDevice(s->m->device);
+    const cudaError_t ec = cudaStreamEndCapture(s->stream, &graph);
+    if (st) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    CK(ec);
+    const cudaError_t ei = cudaGraphInstantiate(&gr.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(ei);
+    gr.kernels = count;
+  }
+  for (int p = 0; p < G; p++) {
+    det_session* s = ts.parts[(size_t)p];
+    if (det_status st = set_dev(s)) return st;
+    CK(cudaGraphLaunch(s->graphs[(size_t)T].exec, s->stream));
+    s0->stats.launches += s->graphs[(size_t)T].kernels;
+  }
+  return set_dev(s0);
+}
+
+bool tp_force_events() {
+  static const int on = [] {
+    const char* e = std::getenv("DETGPU_TP_EVENTS");
+    return e && *e && *e != '0' ? 1 : 0;
+  }();
+  return on != 0;
+}
+
 void destroy_events(TpSession* ts) {
   for (size_t p = 0; p < ts->parts.size(); p++) {
     if (ts->parts[p]) cudaSetDevice(ts->parts[p]->m->device);
@@ -437,8 +565,36 @@ det_status tp_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, d
   if (!st && (cudaSetDevice(tm.devices[0]) != cudaSuccess ||
               cudaEventCreateWithFlags(&ts->fork, cudaEventDisableTiming) != cudaSuccess))
     st = DET_ERR_CUDA;
+  // one part per GPU: exchanges ordered on the devices
+  bool distinct = G > 1 && !tp_force_events();
+  for (int p = 0; p < G && distinct; p++)
+    for (int q = 0; q < p; q++)
+      if (tm.devices[(size_t)p] == tm.devices[(size_t)q]) distinct = false;
+  if (!st && distinct) {
+    ts->device_sync = true;
+    ts->flag.assign((size_t)G, nullptr);
+    ts->epoch.assign((size_t)G, nullptr);
+    for (int p = 0; p < G && !st; p++) {
+      void *f = nullptr, *e = nullptr;
+      if (cudaSetDevice(tm.devices[(size_t)p]) != cudaSuccess || cudaMalloc(&f, (size_t)G * 8) != cudaSuccess ||
+          cudaMalloc(&e, 8) != cudaSuccess || cudaMemset(f, 0, (size_t)G * 8) != cudaSuccess ||
+          cudaMemset(e, 0, 8) != cudaSuccess) {
+        st = DET_ERR_DEVICE_OOM;
+        if (f) cudaFree(f);
+        if (e) cudaFree(e);
+        break;
+      }
+      ts->flag[(size_t)p] = static_cast<unsigned long long*>(f);
+      ts->epoch[(size_t)p] = static_cast<unsigned long long*>(e);
+    }
+  }
   if (st) {
     destroy_events(ts);
+    for (size_t p = 0; p < ts->flag.size(); p++) {
+      cudaSetDevice(tm.devices[p]);
+      if (ts->flag[p]) cudaFree(ts->flag[p]);
+      if (ts->epoch[p]) cudaFree(ts->epoch[p]);
+    }
     for (det_session* s : ts->parts)
       if (s) det_session_free(s);
     delete ts;
@@ -460,6 +616,11 @@ void tp_session_release(det_session* s) {
     cudaStreamSynchronize(ts->parts[p]->stream);
   }
   destroy_events(ts);
+  for (size_t p = 0; p < ts->flag.size(); p++) {
+    cudaSetDevice(ts->parts[p]->m->device);
+    if (ts->flag[p]) cudaFree(ts->flag[p]);
+    if (ts->epoch[p]) cudaFree(ts->epoch[p]);
+  }
   for (size_t p = 1; p < ts->parts.size(); p++) det_session_free(ts->parts[p]);
   delete ts;
 }
@@ -487,6 +648,7 @@ det_status tp_run_forward(det_session* s0, int T, bool graphs) {
     std::memcpy(ts.parts[p]->h_tokens, s0->h_tokens, (size_t)T * 4);
     *ts.parts[p]->h_pos = *s0->h_pos;
   }
+  if (ts.device_sync) return tp_run_device(s0, T, graphs);
   if (!graphs) return tp_enqueue(s0, T, &s0->stats.launches, false);
   if ((int)s0->graphs.size() <= T) s0->graphs.resize((size_t)T + 1);
   det_session::Graph& gr = s0->graphs[(size_t)T];
