@@ -23,6 +23,7 @@
 // rewritten by its owner between layers.
 #include <algorithm>
 
+#include "../../include/detgpu.h"
 #include "dev_math.cuh"
 #include "internal.h"
 
@@ -150,3 +151,29 @@ cudaError_t launch_tp_epoch(const Launch& L, unsigned long long* epoch) {
 }
 
 }  // namespace det
+
+extern "C" det_status det_tp_exchange_timeout_selftest(int device) {
+  using namespace det;
+  int cnt = 0;
+  if (cudaGetDeviceCount(&cnt) != cudaSuccess || cnt == 0) return DET_ERR_NO_DEVICE;
+  if (device < 0 || device >= cnt) return DET_ERR_INVALID_ARGUMENT;
+  if (cudaSetDevice(device) != cudaSuccess) return DET_ERR_CUDA;
+  // [0, 2): this part's counters (slot 1 is the absent peer's), [2]: epoch,
+  // [3]: error word
+  unsigned long long* mem = nullptr;
+  if (cudaMalloc(&mem, 4 * sizeof(unsigned long long)) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  cudaError_t e = cudaMemset(mem, 0, 4 * sizeof(unsigned long long));
+  TpFlags f{};
+  f.parts = 2;
+  f.mine = mem;  // peer[0], peer[1] stay null: nobody is signalled
+  uint32_t* err = reinterpret_cast<uint32_t*>(mem + 3);
+  Launch L{nullptr, err, nullptr};
+  GatherPlan g;  // no data
+  if (e == cudaSuccess) e = launch_tp_exchange(L, f, mem + 2, 0, 1, 1u << 1, g, nullptr, 0, 1);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  uint32_t flag = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&flag, err, 4, cudaMemcpyDeviceToHost);
+  cudaFree(mem);
+  if (e != cudaSuccess) return DET_ERR_CUDA;
+  return (flag & ERRF_TIMEOUT) ? DET_ERR_TIMEOUT : DET_OK;
+}

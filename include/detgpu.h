@@ -193,6 +193,12 @@ void det_free(void* p);
  * y[i] = det-num exp_f32(x[i]) (vendored_libm/expf.rs:33-106) computed on
  * `device`; n may be large (the exhaustive sweep uses 2^32 / k). */
 det_status det_device_expf(int device, const float* x, float* y, size_t n);
+/* Self-test of the tensor-parallel exchange's bounded wait (no counterpart
+ * in the reference): on `device`, runs the exchange kernel waiting for a
+ * peer counter that nothing sets.  The wait gives up after 2 s and the kernel
+ * reports it through the error word, so the expected result is
+ * DET_ERR_TIMEOUT, with the device still usable afterwards. */
+det_status det_tp_exchange_timeout_selftest(int device);
 
 /* ---- timing hooks for benchmarks (device time of the last call) -------- */
 typedef struct {

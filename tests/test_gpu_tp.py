@@ -132,3 +132,19 @@ def test_tp_rejects_bad_devices(D):
         D.Model(g, devices=[0, D.device_count()])
     with pytest.raises(D.DetError):
         D.Model(g, devices=[0] * 9)
+
+
+def test_tp_exchange_wait_times_out(D):
+    # the exchange kernel waits for a peer counter that nothing sets: after
+    # its 2 s bound it reports a timeout instead of hanging, and the device
+    # keeps working
+    import time
+
+    t = time.time()
+    code = D.lib().det_tp_exchange_timeout_selftest(0)
+    assert code == 67, D.lib().det_status_string(code)  # DET_ERR_TIMEOUT
+    assert 1.5 < time.time() - t < 30
+    spec = SPECS["q8_0"]
+    g = S.build_gguf(spec)
+    toks = S.zipf_tokens(8, spec.vocab, seed=1)
+    assert D.Model(g).logits_for_tokens(toks, chunk=8).shape == (8, spec.vocab)
