@@ -244,6 +244,31 @@ def run_tp(args):
         model.close()
 
 
+def tp_probe(D, gguf, vocab, devices, dec_1gpu):
+    """Row-sharded tensor parallelism over `devices` from this one process
+    (run by rank 0 after the timed region while the other ranks wait):
+    single-stream decode tokens/s, and the logits hash of 256 tokens against
+    the single-device model's."""
+    from detllm_b200 import synth as S
+
+    toks = S.zipf_tokens(256, vocab, seed=5)
+    try:
+        t = time.time()
+        tp = D.Model(gguf, devices=devices)
+        load_s = time.time() - t
+        h_tp = tp.logits_hash_for_tokens_chunked(toks, 64).hex()
+        tps, ms = decode_tokens_per_s(tp, vocab)
+        tp.close()
+        one = D.Model(gguf, device=devices[0])
+        h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
+        one.close()
+    except Exception as e:  # reported, never fatal to the bench line
+        return {"parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
+    return {"parts": len(devices), "devices": devices, "decode_tokens_per_s": tps, "decode_ms_per_token": ms,
+            "decode_tokens_per_s_1gpu": dec_1gpu, "speedup": tps / dec_1gpu if dec_1gpu else None,
+            "logits_hash_equal": h_tp == h_one, "load_s": round(load_s, 1)}
+
+
 def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
     """Single-token forwards (the decode path) after a 1024-token prefix:
     device time per token with CUDA graphs, then one profiled pass that times
@@ -358,6 +383,20 @@ def run(args):
     prof = model.stats(reset=True)
     kprof = model.profile(reset=True)
     dec = decode_probe(D, model, spec.vocab)
+    # tensor parallelism over all the job's GPUs, from rank 0 alone; the
+    # other ranks wait on a CPU (gloo) group, since an NCCL barrier kernel
+    # spinning on their GPU would time-slice with rank 0's parts there
+    tpj = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+        dist.barrier(group=cpu)
+        if rank == 0:
+            tpj = tp_probe(D, gguf, spec.vocab, list(range(ws)), dec["tokens_per_s"])
+        dist.barrier(group=cpu)
     if rank != 0:
         return
     total_tokens = N_TOKENS * args.steps * ws
@@ -393,6 +432,7 @@ def run(args):
                                                                                   1e-9), 4)}
                     for k, (n, ms) in kprof.items() if n},
         "clocks": clk.summary(),
+        "tensor_parallel": tpj,
         "payload_bytes": len(payload),
         "weight_bytes_per_token": S.weight_bytes_per_token(spec),
     }

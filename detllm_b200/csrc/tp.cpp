@@ -47,6 +47,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <thread>
 
 #include "host_common.h"
 
@@ -701,12 +702,19 @@ extern "C" det_status det_model_load_tp(const uint8_t* gguf, size_t len, const i
     }
   TpModel* tm = new (std::nothrow) TpModel();
   if (!tm) return DET_ERR_ALLOC;
+  // one host thread per device uploads its replica
+  std::vector<det_model*> reps(uniq.size(), nullptr);
+  std::vector<det_status> rst(uniq.size(), DET_OK);
+  {
+    std::vector<std::thread> th;
+    for (size_t i = 0; i < uniq.size(); i++)
+      th.emplace_back([&, i] { rst[i] = det_model_load(gguf, len, uniq[i], &reps[i]); });
+    for (auto& t : th) t.join();
+  }
   det_status st = DET_OK;
-  for (int d : uniq) {
-    det_model* r = nullptr;
-    st = det_model_load(gguf, len, d, &r);
-    if (st) break;
-    tm->replicas.push_back(r);
+  for (size_t i = 0; i < uniq.size(); i++) {
+    if (reps[i]) tm->replicas.push_back(reps[i]);
+    if (rst[i] && !st) st = rst[i];
   }
   if (!st) {
     const ModelCfg& c = tm->replicas[0]->cfg;
