@@ -306,44 +306,58 @@ DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
 // order), so its length sets a floor of K dependent adds per launch.  A CTA
 // takes 32 rows: warps 0-7 (producers) dequantise super-block s of the 32
 // rows -- warp w sub-block w, lane r row r -- and write the products
-// w * act into stage buffer s % 3, while warp 8 runs the 32 row chains
+// w * act into stage buffer s % 2, while warp 8 runs the 32 row chains
 // (lane = row) through the stages in order.  Producers and chain meet only
 // at named hardware barriers: FULL[i] (producers arrive after writing buffer
 // i, the chain waits) and EMPTY[i] (the chain arrives after reading it, the
-// producers wait before writing it again), so producers run up to two
-// stages ahead.  Producers load each stage's weights and activation two
-// stages before they use them, and do their arithmetic as f32x2 pairs.
-// Stage rows are 260 floats apart and both sides move 16-byte vectors (the
-// eight lanes of a quarter-warp hit distinct bank groups).
+// producers wait before writing it again).  The super-blocks' bytes arrive
+// by cp.async G4_PREF stages ahead into a ring of raw slots (a producer-only
+// barrier publishes each slot), the activations are dequantised into shared
+// memory once, and the producers' arithmetic runs as f32x2 pairs.  Stage
+// rows are 260 floats apart and both sides move 16-byte vectors (the eight
+// lanes of a quarter-warp hit distinct bank groups).
 constexpr int G4_ROWS = 32;
 constexpr int G4_PWARPS = 8;
-constexpr int G4_THREADS = (G4_PWARPS + 1) * 32;
+constexpr int G4_PTHREADS = G4_PWARPS * 32;
+constexpr int G4_THREADS = G4_PTHREADS + 32;
 constexpr int G4_LD = 260;
-constexpr int G4_NBUF = 3;
-constexpr size_t G4_SMEM = (size_t)(G4_NBUF * G4_ROWS * G4_LD + 256) * sizeof(float);
-constexpr int G4_BAR_FULL = 1, G4_BAR_EMPTY = 1 + G4_NBUF;  // named barriers 1..6 (0 is __syncthreads)
-static_assert(G4_NBUF == 3, "nbar_*_buf dispatch three buffers");
+constexpr int G4_NBUF = 2;
+constexpr int G4_PREF = 4;                   // super-blocks in flight ahead of the producers
+constexpr int G4_RAWN = G4_PREF + 2;         // raw slots: the ring never overwrites a slot in use
+constexpr int G4_RAW_STAGE = G4_ROWS * 144;  // bytes of one super-block of 32 rows
+constexpr int G4_BAR_FULL = 1, G4_BAR_EMPTY = 1 + G4_NBUF, G4_BAR_PROD = 1 + 2 * G4_NBUF;  // 0 is __syncthreads
+static_assert(G4_NBUF == 2, "nbar_*_buf dispatch two buffers");
+constexpr int G4_MAX_NB = 64;  // K <= 16384 (activations staged in shared memory)
+constexpr size_t G4_FIXED_SMEM = (size_t)G4_NBUF * G4_ROWS * G4_LD * 4 + (size_t)G4_RAWN * G4_RAW_STAGE;
+inline size_t g4_smem_bytes(int nbs) { return G4_FIXED_SMEM + (size_t)nbs * 256 * 4; }
 
 // barrier ids are immediates (a register id makes the CTA reserve all 16)
-template <int ID>
+template <int ID, int N>
 DI void nbar_sync() {
-  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(G4_THREADS) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(N) : "memory");
 }
-template <int ID>
+template <int ID, int N>
 DI void nbar_arrive() {
-  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(G4_THREADS) : "memory");
+  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(N) : "memory");
 }
 template <int BASE>
 DI void nbar_sync_buf(int buf) {
-  if (buf == 0) nbar_sync<BASE>();
-  else if (buf == 1) nbar_sync<BASE + 1>();
-  else nbar_sync<BASE + 2>();
+  if (buf == 0) nbar_sync<BASE, G4_THREADS>();
+  else nbar_sync<BASE + 1, G4_THREADS>();
 }
 template <int BASE>
 DI void nbar_arrive_buf(int buf) {
-  if (buf == 0) nbar_arrive<BASE>();
-  else if (buf == 1) nbar_arrive<BASE + 1>();
-  else nbar_arrive<BASE + 2>();
+  if (buf == 0) nbar_arrive<BASE, G4_THREADS>();
+  else nbar_arrive<BASE + 1, G4_THREADS>();
+}
+
+DI void g4_cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)), "l"(gsrc) : "memory");
+}
+DI void g4_cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+DI void g4_cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 DI unsigned long long add2(unsigned long long a, unsigned long long b) {
@@ -362,44 +376,59 @@ DI unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned 
   return r;
 }
 
-struct Q4Stage {
-  uint4 h, v0, v1;  // block header (d, dmin, scales) and the sub-block pair's 32 quant bytes
-  float ad;
-  int aq;
-};
-
 __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, const int8_t* __restrict__ aq,
                                                                     const float* __restrict__ ad, uint32_t* err) {
-  pdl_enter();
-  extern __shared__ float g4_smem[];
-  float* prod = g4_smem;                               // [G4_NBUF][G4_ROWS][G4_LD]
-  float* actb = g4_smem + G4_NBUF * G4_ROWS * G4_LD;  // [256]: sub-block w at [32 w, 32 w + 32)
+  extern __shared__ __align__(16) uint8_t g4_smem[];
+  float* prod = reinterpret_cast<float*>(g4_smem);                     // [G4_NBUF][G4_ROWS][G4_LD]
+  uint8_t* raw = g4_smem + (size_t)G4_NBUF * G4_ROWS * G4_LD * 4;      // [G4_RAWN][G4_ROWS][144]
+  float* act = reinterpret_cast<float*>(raw + (size_t)G4_RAWN * G4_RAW_STAGE);  // [K]
   const KqSeg g = kq_seg(S);
   const int r0 = ((int)blockIdx.x - g.cta0) * G4_ROWS;
   const int nbs = S.nb, nbk = nbs * 8;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = r0 + lane;
   const bool ok = row < g.rows;
 
-  if (warp < G4_PWARPS) {
-    // a row past the matrix keeps zero weights, so its products are 0
-    auto load = [&](int s, Q4Stage& st) {
-      const int kb = s * 8 + warp;
-      st.ad = ad[q8a_dslot(nbk, 0, kb)];
-      st.aq = aq[q8a_elem(nbk, 0, kb, lane)];
-      if (ok) {
-        const uint8_t* blk = g.q + ((size_t)row * nbs + s) * 144;
-        st.h = *reinterpret_cast<const uint4*>(blk);
-        st.v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
-        st.v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
+  // raw bytes of super-block s (32 rows x 144 B) into slot s % G4_RAWN (by
+  // the producer threads); rows past the matrix are zeros (zero weights,
+  // zero products).  Every producer thread commits one group per call, so
+  // the wait counts stay uniform.
+  auto issue = [&](int s) {
+      if (s < nbs) {
+        uint8_t* dst0 = raw + (size_t)(s % G4_RAWN) * G4_RAW_STAGE;
+        for (int c = tid; c < G4_ROWS * 9; c += G4_PTHREADS) {
+          const int r = c / 9, part = c - 9 * r;
+          uint8_t* dst = dst0 + r * 144 + part * 16;
+          if (r0 + r < g.rows)
+            g4_cp_async16(dst, g.q + ((size_t)(r0 + r) * nbs + s) * 144 + part * 16);
+          else
+            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        }
       }
-    };
+      g4_cp_commit();
+  };
+  if (warp < G4_PWARPS)  // weights are constant: stream them before the predecessor ends
+    for (int s = 0; s < G4_PREF; s++) issue(s);
+  pdl_enter();
+  // the activation, dequantised once: act[i] = a.d * a.q (the reference's value)
+  for (int i = tid; i < nbk * 32; i += G4_THREADS) {
+    const int kb = i >> 5;
+    act[i] = fmul(ad[q8a_dslot(nbk, 0, kb)], (float)aq[q8a_elem(nbk, 0, kb, i & 31)]);
+  }
+  __syncthreads();
+
+  if (warp < G4_PWARPS) {
     const unsigned long long one2 = pk2(S.one, S.one), nmag2 = pk2(-8388608.0f, -8388608.0f);
-    // w * act for this warp's sub-block of stage `st` into buffer `buf`
-    auto compute = [&](const Q4Stage& st, int buf) {
-      actb[warp * 32 + lane] = fmul(st.ad, (float)st.aq);
-      __syncwarp();
-      const uint4 h = st.h;
+    for (int s = 0; s < nbs; s++) {
+      issue(s + G4_PREF);
+      g4_cp_wait<G4_PREF>();  // this thread's copies of stage s have landed
+      nbar_sync<G4_BAR_PROD, G4_PTHREADS>();  // ... and every producer's
+      const int buf = s & 1;
+      if (s >= G4_NBUF) nbar_sync_buf<G4_BAR_EMPTY>(buf);
+      const uint8_t* blk = raw + (size_t)(s % G4_RAWN) * G4_RAW_STAGE + lane * 144;
+      const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+      const uint4 v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
+      const uint4 v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
       const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
       const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
       // q4_k_scale_min (det-quant lib.rs:516-529) on the packed bytes
@@ -413,9 +442,9 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
       }
       const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
       const unsigned long long dsc2 = pk2(dsc, dsc), ndmn2 = pk2(-dmn, -dmn);
-      const uint32_t qw[8] = {st.v0.x, st.v0.y, st.v0.z, st.v0.w, st.v1.x, st.v1.y, st.v1.z, st.v1.w};
+      const uint32_t qw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       const int sh = 4 * (warp & 1);
-      const float4* av = reinterpret_cast<const float4*>(actb + warp * 32);
+      const float4* av = reinterpret_cast<const float4*>(act + s * 256 + warp * 32);
       float* dst = prod + (buf * G4_ROWS + lane) * G4_LD + warp * 32;
 #pragma unroll
       for (int k = 0; k < 8; k++) {  // elements 4k .. 4k + 3
@@ -434,28 +463,12 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
         const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
         *reinterpret_cast<float4*>(dst + 4 * k) = make_float4(r01.x, r01.y, r23.x, r23.y);
       }
-      __syncwarp();  // actb is rewritten by this warp's next stage
-    };
-    // stage s: load stage s + 2 into `ld_slot` (stage s - 1's), wait until
-    // the chain has released buffer `buf`, write it, signal it full
-    auto pstep = [&](int s, int buf, Q4Stage& ld_slot, const Q4Stage& cur) {
-      if (s + 2 < nbs) load(s + 2, ld_slot);
-      if (s >= G4_NBUF) nbar_sync_buf<G4_BAR_EMPTY>(buf);
-      compute(cur, buf);
       nbar_arrive_buf<G4_BAR_FULL>(buf);
-    };
-    Q4Stage st0{}, st1{}, st2{};  // stage s lives in slot s % 3
-    load(0, st0);
-    if (nbs > 1) load(1, st1);
-    for (int s = 0; s < nbs; s += 3) {
-      pstep(s, 0, st2, st0);
-      if (s + 1 < nbs) pstep(s + 1, 1, st0, st1);
-      if (s + 2 < nbs) pstep(s + 2, 2, st1, st2);
     }
   } else {
     float sum = 0.0f;
     for (int s = 0; s < nbs; s++) {
-      const int buf = s % G4_NBUF;
+      const int buf = s & 1;
       nbar_sync_buf<G4_BAR_FULL>(buf);
       const float4* src = reinterpret_cast<const float4*>(prod + (buf * G4_ROWS + lane) * G4_LD);
 #pragma unroll 1
@@ -666,9 +679,15 @@ __global__ void __launch_bounds__(G6_THREADS, 1) gemv_q6k_aux_kernel(KqSegs S, c
 
 }  // namespace
 
+bool kq_decode_supported(const DevMatrix& m) {
+  return m.type == GT_Q6_K || (m.type == GT_Q4_K && m.nb <= G4_MAX_NB);
+}
+
 cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
                                        float* const* out, const int* epi, const float* const* bias) {
   if (n < 1 || n > 3) return cudaErrorInvalidValue;
+  for (int i = 0; i < n; i++)
+    if (!kq_decode_supported(*m[i])) return cudaErrorInvalidValue;
   const bool q4 = m[0]->type == GT_Q4_K;
   // Q6_K rows per CTA: two (row, block) items per thread per pass of up to
   // 32 blocks (16 rows for wide matrices, 32 when a row has 16 blocks or fewer)
@@ -695,7 +714,8 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   const unsigned long long bit = 1ull << ((dev & 15) * 4 + kid);
   cudaError_t e = cudaSuccess;
   if (dev >= 16 || !(attr_set & bit)) {
-    e = q4 ? cudaFuncSetAttribute(gemv_q4k_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G4_SMEM)
+    e = q4 ? cudaFuncSetAttribute(gemv_q4k_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)g4_smem_bytes(G4_MAX_NB))
         : r32 ? cudaFuncSetAttribute(gemv_q6k_aux_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)g6_smem<32>())
               : cudaFuncSetAttribute(gemv_q6k_aux_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -704,7 +724,7 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     if (dev < 16) attr_set |= bit;
   }
   if (q4)
-    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_THREADS, G4_SMEM, S, a.qa_q, a.qa_d, L.err);
+    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_THREADS, g4_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
   else if (r32)
     e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
   else

@@ -120,7 +120,9 @@ cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& 
 // Q6_K matrix, chunk of T > 16 positions (gemm_kq.cu)
 cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias);
-// Q4_K / Q6_K matrix, one position (gemm_kq.cu)
+// Q4_K / Q6_K matrix, one position (gemm_kq.cu); supported: every Q6_K, and
+// Q4_K rows of up to 64 super-blocks (K <= 16384)
+bool kq_decode_supported(const DevMatrix& m);
 cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const DevActs& a, float* out, int epi,
                                   const float* bias);
 // up to three Q4_K (or three Q6_K) matrices of equal width that read the same

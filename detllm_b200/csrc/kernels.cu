@@ -928,7 +928,7 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   if (handled || e != cudaSuccess) return e;
   if (m.type == GT_Q4_K && T > 16) return launch_gemm_q4k(L, m, a, T, out, out_ld, epi, bias);
   if (m.type == GT_Q6_K && T > 16) return launch_gemm_q6k(L, m, a, T, out, out_ld, epi, bias);
-  if ((m.type == GT_Q4_K || m.type == GT_Q6_K) && T == 1 && (size_t)m.nb * 256 * sizeof(float) <= 200 * 1024)
+  if ((m.type == GT_Q4_K || m.type == GT_Q6_K) && T == 1 && kq_decode_supported(m))
     return launch_gemv_kq_decode(L, m, a, out, epi, bias);
   dim3 grid(T, (m.rows + 127) / 128);
   {

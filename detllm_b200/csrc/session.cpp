@@ -238,8 +238,7 @@ cudaError_t gemm_fused(det_session* s, int tag, const Launch& L, const DevMatrix
 // as one one-position launch: Q4_K or Q6_K, all of one type and width.
 bool kq_fusable(const DevMatrix* const* m, int n) {
   for (int i = 0; i < n; i++)
-    if ((m[i]->type != GT_Q4_K && m[i]->type != GT_Q6_K) || m[i]->type != m[0]->type || m[i]->nb != m[0]->nb ||
-        m[i]->rows == 0)
+    if (!kq_decode_supported(*m[i]) || m[i]->type != m[0]->type || m[i]->nb != m[0]->nb || m[i]->rows == 0)
       return false;
   return true;
 }
