@@ -471,8 +471,8 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
       const int buf = s & 1;
       nbar_sync_buf<G4_BAR_FULL>(buf);
       const float4* src = reinterpret_cast<const float4*>(prod + (buf * G4_ROWS + lane) * G4_LD);
-#pragma unroll 1
-      for (int e4 = 0; e4 < 64; e4 += 8) {
+#pragma unroll
+      for (int e4 = 0; e4 < 64; e4 += 8) {  // unrolled: the next group's loads issue during these adds
         float4 v[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) v[j] = src[e4 + j];
