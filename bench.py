@@ -49,6 +49,10 @@ OVERLAP = N_CTX // 4
 CONFIG_RUNS = {"tinyllama-q8_0": (4096, 2048), "tinyllama-q4_k_m": (4096, 2048),
                "qwen2.5-0.5b-q8_0": (8192, 4096), "llama3-8b-q4_k": (4096, 8192)}
 METRIC = "encode tokens/s (logits+CDF+code)"
+# DRAM bytes (read + write) per launch of one token's 89 weight GEMVs of the
+# headline config, from one ncu capture
+# (profiles/gemv_decode_stream_tinyllama_q8_0_1token_traffic.md)
+DECODE_GEMV_TRAFFIC_PER_LAUNCH = 12.400e6
 
 
 def log(*a):
@@ -415,7 +419,9 @@ def run(args):
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},
         "gpu_launches": int(st.launches),
         "roofline": {"bound": "hbm", "achieved": dec["gemv_stream_gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": dec["gemv_stream_gbs"] / peak if dec["gemv_stream_gbs"] else None, "traffic": None,
+                     "frac": dec["gemv_stream_gbs"] / peak if dec["gemv_stream_gbs"] else None,
+                     "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH if CONFIG == "tinyllama-q8_0" else None,
+                     "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
                      "kernel": f"decode weight GEMVs, one token's {dec['gemv_launches'] // 48} launches back to back "
                                f"({CONFIG})", "peak_kind": peak_kind,
                      "launches": dec["gemv_launches"] // 48,
