@@ -248,29 +248,40 @@ def run_tp(args):
         model.close()
 
 
-def tp_probe(D, gguf, vocab, devices, dec_1gpu):
+TP_CONFIG = "llama3-8b-q4_k"  # the configuration BASELINE.json runs row-sharded
+
+
+def tp_probe(D, devices):
     """Row-sharded tensor parallelism over `devices` from this one process
-    (run by rank 0 after the timed region while the other ranks wait):
-    single-stream decode tokens/s, and the logits hash of 256 tokens against
-    the single-device model's."""
+    (run by rank 0 after the timed region while the other ranks wait), on the
+    Llama-3-8B-shaped Q4_K/Q6_K model BASELINE.json names for it:
+    single-stream decode tokens/s on one GPU and on all of `devices`, and
+    whether the logits hashes of 256 tokens are equal."""
     from detllm_b200 import synth as S
 
-    toks = S.zipf_tokens(256, vocab, seed=5)
+    spec = S.CONFIGS[TP_CONFIG]
     try:
+        t = time.time()
+        gguf = S.build_gguf(spec)
+        build_s = time.time() - t
+        toks = S.zipf_tokens(256, spec.vocab, seed=5)
+        one = D.Model(gguf, device=devices[0])
+        h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
+        tps1, ms1 = decode_tokens_per_s(one, spec.vocab)
+        one.close()
         t = time.time()
         tp = D.Model(gguf, devices=devices)
         load_s = time.time() - t
         h_tp = tp.logits_hash_for_tokens_chunked(toks, 64).hex()
-        tps, ms = decode_tokens_per_s(tp, vocab)
+        tps, ms = decode_tokens_per_s(tp, spec.vocab)
         tp.close()
-        one = D.Model(gguf, device=devices[0])
-        h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
-        one.close()
     except Exception as e:  # reported, never fatal to the bench line
-        return {"parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
-    return {"parts": len(devices), "devices": devices, "decode_tokens_per_s": tps, "decode_ms_per_token": ms,
-            "decode_tokens_per_s_1gpu": dec_1gpu, "speedup": tps / dec_1gpu if dec_1gpu else None,
-            "logits_hash_equal": h_tp == h_one, "load_s": round(load_s, 1)}
+        return {"config": TP_CONFIG, "parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
+    return {"config": TP_CONFIG, "parts": len(devices), "devices": devices, "decode_tokens_per_s": tps,
+            "decode_ms_per_token": ms, "decode_tokens_per_s_1gpu": tps1, "decode_ms_per_token_1gpu": ms1,
+            "speedup": tps / tps1, "logits_hash_equal": h_tp == h_one,
+            "weight_bytes_per_token": S.weight_bytes_per_token(spec), "load_s": round(load_s, 1),
+            "build_s": round(build_s, 1)}
 
 
 def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
@@ -399,7 +410,7 @@ def run(args):
         cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
         dist.barrier(group=cpu)
         if rank == 0:
-            tpj = tp_probe(D, gguf, spec.vocab, list(range(ws)), dec["tokens_per_s"])
+            tpj = tp_probe(D, list(range(ws)))
         dist.barrier(group=cpu)
     if rank != 0:
         return
