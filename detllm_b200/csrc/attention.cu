@@ -393,15 +393,15 @@ int score_ld(int n_ctx) { return (n_ctx + 31) & ~31; }
 // With a handful of query rows the per-row kernels above leave most of the
 // GPU idle.  The softmax gives each (position, head) row a CTA: exps by all
 // threads into shared memory, the eight ordered Z chains by eight threads,
-// p = e / Z by all.  PV gives each (KV head, 16 dims, position) a CTA with one
-// ordered chain o[d] += p_j v_j[d] per thread, over 32-key tiles of P and V
-// staged with cp.async, PD_STAGES tiles in flight (a tile's 32 adds are far
+// p = e / Z by all.  PV gives each (KV head, 8 dims, position) a CTA with one
+// ordered chain o[d] += p_j v_j[d] per thread, over 64-key tiles of P and V
+// staged with cp.async, PD_STAGES tiles in flight (a tile's 64 adds are far
 // shorter than a load from HBM); as in the chunked path the rows are zero
 // past their length, so whole tiles are summed exactly.
 constexpr int SD_THREADS = 256;
-constexpr int PD_KEYS = 32;
-constexpr int PD_DIMS = 16;
-constexpr int PD_STAGES = 8;
+constexpr int PD_KEYS = 64;
+constexpr int PD_DIMS = 8;
+constexpr int PD_STAGES = 4;
 DI int pd_ps_floats(int gsz) { return PD_STAGES * gsz * PD_KEYS; }
 inline size_t pd_smem_bytes(int gsz) { return (size_t)PD_STAGES * (gsz * PD_KEYS + PD_KEYS * PD_DIMS) * sizeof(float); }
 
@@ -491,7 +491,12 @@ __global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* 
       float* vbuf = vs + bf * PD_KEYS * PD_DIMS;
       for (int i = tid; i < gsz * (PD_KEYS / 4); i += nt) {
         const int r = i / (PD_KEYS / 4), c4 = (i - r * (PD_KEYS / 4)) * 4;
-        cp_async16(pb + r * PD_KEYS + c4, prow0 + (size_t)r * s_ld + jc + c4);
+        // a chunk that starts at or past the score length is zero (never
+        // read: it may lie past the row's zeroed tail)
+        if (jc + c4 < len)
+          cp_async16(pb + r * PD_KEYS + c4, prow0 + (size_t)r * s_ld + jc + c4);
+        else
+          *reinterpret_cast<float4*>(pb + r * PD_KEYS + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
       for (int i = tid; i < PD_KEYS * (PD_DIMS / 4); i += nt) {
         const int jj = i / (PD_DIMS / 4), c4 = (i - jj * (PD_DIMS / 4)) * 4;
