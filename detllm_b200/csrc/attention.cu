@@ -28,6 +28,7 @@
 // Rows of different queries in one CTA have different score lengths; the
 // PV chains of shorter rows see p = 0 for the extra keys, and adding
 // 0 * v (v finite, the chain never -0) leaves an f32 sum unchanged.
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -536,13 +537,13 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
   const int gsz = n_head / n_head_kv;
   const int qb = QK_ROWS / gsz;
   constexpr int smem = qk_smem_bytes<HD>();
-  static unsigned long long attr_set = 0;  // one bit per device
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device (sessions may run on several host threads)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && (dev >= 64 || !(attr_set >> dev & 1ull))) {
+  if (smem > 48 * 1024 && (dev >= 64 || !(attr_set.load() >> dev & 1ull))) {
     cudaError_t e = cudaFuncSetAttribute(attn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) attr_set |= 1ull << dev;
+    if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   const int s_ld = score_ld(n_ctx);
   dim3 g1((n_ctx + QK_KEYS - 1) / QK_KEYS, (T + qb - 1) / qb, n_head_kv);

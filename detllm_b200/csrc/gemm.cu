@@ -36,6 +36,7 @@
 // warp issues, completing on a "full" mbarrier; compute warps release a slot
 // through an "empty" mbarrier.  Every mbarrier wait is bounded
 // (globaltimer); on timeout the kernel flags ERRF_TIMEOUT and stops.
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -449,13 +450,13 @@ __global__ void __launch_bounds__(CK_THREADS) gemm_chunk_kernel(const uint8_t* _
 template <int QT, class C>
 cudaError_t launch_chunk_cfg(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   constexpr int smem = ChunkSmem<QT, C>::total;
-  static unsigned long long attr_set = 0;  // one bit per device
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device (sessions may run on several host threads)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(attr_set >> dev & 1ull)) {
+  if (dev >= 64 || !(attr_set.load() >> dev & 1ull)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_chunk_kernel<QT, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) attr_set |= 1ull << dev;
+    if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   const int tiles = (m.rows + 15) / 16;
   dim3 grid((tiles + CK_TILES - 1) / CK_TILES, (T + Q8A_GROUP - 1) / Q8A_GROUP);

@@ -14,6 +14,7 @@
 // `one` == 1.0 a kernel argument -- exact, and not contractible with the
 // multiply (a packed add fed by a packed multiply is contracted by the code
 // generator).
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include "dev_math.cuh"
@@ -707,13 +708,13 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     }
   }
   if (ctas == 0) return cudaSuccess;
-  static unsigned long long attr_set = 0;  // one bit per device and kernel
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device and kernel (several host threads)
   int dev = 0;
   cudaGetDevice(&dev);
   const int kid = q4 ? 0 : (r32 ? 1 : 2);
   const unsigned long long bit = 1ull << ((dev & 15) * 4 + kid);
   cudaError_t e = cudaSuccess;
-  if (dev >= 16 || !(attr_set & bit)) {
+  if (dev >= 16 || !(attr_set.load() & bit)) {
     e = q4 ? cudaFuncSetAttribute(gemv_q4k_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)g4_smem_bytes(G4_MAX_NB))
         : r32 ? cudaFuncSetAttribute(gemv_q6k_aux_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -721,7 +722,7 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
               : cudaFuncSetAttribute(gemv_q6k_aux_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)g6_smem<16>());
     if (e != cudaSuccess) return e;
-    if (dev < 16) attr_set |= bit;
+    if (dev < 16) attr_set.fetch_or(bit);
   }
   if (q4)
     e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_THREADS, g4_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
