@@ -18,7 +18,8 @@
 //    peer's flag array, then waits until every peer's slot in its own array
 //    has reached that value (acquire, system scope) and pulls.  The wait is
 //    bounded by the global timer: on timeout the kernel sets ERRF_TIMEOUT and
-//    skips the pull, so a missing peer ends in an error status, not a hang.
+//    skips the pull, so a missing peer ends in an error status, not a hang;
+//    later exchanges of the same forward see the flag and do not wait again.
 // The loads are ld.global.cv (fetch again, never a cached copy): a slice is
 // rewritten by its owner between layers.
 #include <algorithm>
@@ -85,7 +86,9 @@ __global__ void __launch_bounds__(GX_THREADS)
   __shared__ int timed_out;
   const unsigned long long target = *epoch * (unsigned long long)nx + (unsigned long long)k + 1ull;
   if (threadIdx.x == 0) {
-    timed_out = 0;
+    // an earlier exchange of this forward already gave up: fail fast, so a
+    // missing peer costs one bounded wait per forward, not one per exchange
+    timed_out = (*reinterpret_cast<volatile uint32_t*>(err) & ERRF_TIMEOUT) ? 1 : 0;
     if (blockIdx.x == 0 && blockIdx.y == 0)
       for (int q = 0; q < f.parts; q++)
         if (f.peer[q]) st_release_sys(f.peer[q], target);
