@@ -19,6 +19,9 @@ host range coder, through det_encode_symbols.
   activations + outputs) / CUDA-event time, against the measured HBM copy
   bandwidth in MEASURED_PEAKS.json.  decode.gemv_gbs_in_forward is the same
   ratio for the launches inside real forwards, each bracketed by events.
+  With DETGPU_FUSED_DECODE=1 the one-position forward is one persistent
+  kernel (decode_fused_kernel) and the roofline is that launch: all weight
+  bytes of one token + the KV rows its attention reads, / its event time.
   The chunked encode GEMM is FP32-pipe bound (its exact ordered fold) and
   is reported separately under chunk_gemm with the per-kernel time shares.
 * cpu_baseline / --impl reference: the C restatement of the reference CPU
@@ -313,6 +316,8 @@ def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
         D.set_profiling(False)
         pr = s.stats(reset=True)
         gms, gbytes = s.gemv_stream(20)
+    # one GEMM-accounted launch per token: the fused one-position kernel ran
+    out["fused"] = int(pr.gemm_launches) == n_steps
     out["gemv_launches"] = int(pr.gemm_launches)
     out["gemv_ms_per_token"] = pr.gemm_ms / n_steps
     out["gemv_bytes_per_launch"] = pr.gemm_bytes / max(pr.gemm_launches, 1)
@@ -324,6 +329,29 @@ def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
     out["gemv_stream_bytes_per_token"] = gbytes
     out["gemv_stream_gbs"] = gbytes / (gms / 1000.0) / 1e9 if gms > 0 else None
     return out
+
+
+def roofline(dec, peak, peak_kind):
+    """The decode roofline object: the fused one-position kernel when it ran,
+    else the per-op weight GEMVs back to back (see the module docstring)."""
+    if dec.get("fused"):
+        gbs = dec["gemv_gbs_in_forward"]
+        return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                "frac": gbs / peak if gbs else None, "traffic": None,
+                "traffic_unit": "bytes per launch (no ncu capture of this kernel's DRAM bytes yet)",
+                "kernel": f"decode_fused_kernel: one token's forward (all layers + lm_head) in one launch ({CONFIG})",
+                "peak_kind": peak_kind, "launches": 1, "ms_per_launch": dec["gemv_ms_per_launch"],
+                "bytes_per_launch": dec["gemv_bytes_per_launch"],
+                "bytes": "weights of every matrix + K and V rows read by the attention",
+                "per_op_gemv_stream_gbs": dec["gemv_stream_gbs"]}
+    n = max(dec["gemv_launches"] // 48, 1)
+    return {"bound": "hbm", "achieved": dec["gemv_stream_gbs"], "peak": peak, "unit": "GB/s",
+            "frac": dec["gemv_stream_gbs"] / peak if dec["gemv_stream_gbs"] else None,
+            "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH if CONFIG == "tinyllama-q8_0" else None,
+            "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
+            "kernel": f"decode weight GEMVs, one token's {n} launches back to back ({CONFIG})",
+            "peak_kind": peak_kind, "launches": n, "ms_per_launch": dec["gemv_stream_ms_per_token"] / n,
+            "bytes_per_launch": dec["gemv_stream_bytes_per_token"] / n, "in_forward_gbs": dec["gemv_gbs_in_forward"]}
 
 
 def run_reference(args):
@@ -429,16 +457,7 @@ def run(args):
         "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
                 "d2h_bytes_per_step": st.d2h_bytes // args.steps},
         "gpu_launches": int(st.launches),
-        "roofline": {"bound": "hbm", "achieved": dec["gemv_stream_gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": dec["gemv_stream_gbs"] / peak if dec["gemv_stream_gbs"] else None,
-                     "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH if CONFIG == "tinyllama-q8_0" else None,
-                     "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
-                     "kernel": f"decode weight GEMVs, one token's {dec['gemv_launches'] // 48} launches back to back "
-                               f"({CONFIG})", "peak_kind": peak_kind,
-                     "launches": dec["gemv_launches"] // 48,
-                     "ms_per_launch": dec["gemv_stream_ms_per_token"] / max(dec["gemv_launches"] // 48, 1),
-                     "bytes_per_launch": dec["gemv_stream_bytes_per_token"] / max(dec["gemv_launches"] // 48, 1),
-                     "in_forward_gbs": dec["gemv_gbs_in_forward"]},
+        "roofline": roofline(dec, peak, peak_kind),
         "decode": dec,
         "chunk_gemm": {"bound": "fp32 pipe (exact ordered fold, 4 fp32 ops per weight per position)",
                        "weight_stream_gbs": achieved, "launches": int(prof.gemm_launches),

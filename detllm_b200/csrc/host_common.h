@@ -133,6 +133,7 @@ enum ProfTag : int {
   PT_GEMM_DOWN,
   PT_GEMM_OUT,
   PT_CDF,
+  PT_FUSED,  // the one-position forward as one persistent kernel (decode_fused.cu)
   PT_COUNT
 };
 struct ProfTags {
@@ -233,6 +234,12 @@ struct det_session {
   // part (full width), and on the session returned to the caller, the parts
   float *attn_full = nullptr, *ff_full = nullptr;
   det::TpSession* tp = nullptr;
+  // one-position forward as one persistent kernel (decode_fused.cu):
+  // fd_state 0 = not yet checked, 1 = in use, -1 = the per-op kernels run
+  int fd_state = 0;
+  det::FdParams fd;
+  int fd_grid = 0;
+  double fd_wbytes = 0;  // weight bytes one fused forward streams
 };
 
 namespace det {

@@ -198,4 +198,41 @@ cudaError_t launch_tp_epoch(const Launch& L, unsigned long long* epoch);
 cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
                                   const uint64_t* value, uint64_t* out4);
 
+// ---- one-position forward as one persistent kernel (decode_fused.cu) -------
+// A LAYOUT_MMA16 matrix (Q8_0 or Q4_0) as the fused kernel reads it.
+struct FdMat {
+  const uint8_t* q = nullptr;
+  int type = 0, rows = 0, nb = 0;
+};
+// one layer's weights (device array of L entries)
+struct FdLayer {
+  FdMat qkv, o, gu, down;
+  const float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+};
+struct FdParams {
+  const FdLayer* layers = nullptr;
+  int L = 0;
+  FdMat out;
+  const float* out_norm = nullptr;
+  int d = 0, dff = 0, nh = 0, nkv = 0, hd = 0, half = 0, pairing = 0, n_ctx = 0, s_ld = 0, vocab = 0;
+  float eps = 0.0f, scale = 0.0f;
+  const int* pos = nullptr;
+  const float *cos_t = nullptr, *sin_t = nullptr;
+  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *S = nullptr, *attn = nullptr;
+  float *gate = nullptr, *up = nullptr, *logits = nullptr, *kc = nullptr, *vc = nullptr;
+  uint32_t* err = nullptr;
+  unsigned* sync = nullptr;  // [0] grid-barrier arrivals, [1] abort; zeroed before each launch
+  // shared-memory plan (fused_decode_plan): ring slots, largest K / 32, scratch floats
+  int ns = 0, nbmax = 0, scratch = 0;
+};
+// fills p->ns / nbmax / scratch for these shapes on the current device;
+// false when the fused kernel does not apply (the per-op kernels run instead)
+bool fused_decode_plan(int d, int dff, int nh, int nkv, int hd, int s_ld, FdParams* p);
+int fused_decode_smem(const FdParams& p);
+// sets the kernel's shared-memory limit on the current device and returns
+// the grid (one CTA per SM); once per session, before its first launch
+cudaError_t fused_decode_prepare(const FdParams& p, int* grid);
+// cooperative launch (every CTA resident: the kernel has grid barriers)
+cudaError_t launch_decode_fused(const Launch& L, const FdParams& p, int grid);
+
 }  // namespace det

@@ -92,14 +92,16 @@ void add_prof(ProfTags* a, const ProfTags& b) {
   }
 }
 
+// launches whose time and algorithmic bytes go into the GEMM statistics (the
+// fused one-position forward counts as one: it streams every weight matrix)
 bool is_gemm_tag(int tag) {
   return tag == PT_GEMM_QKV || tag == PT_GEMM_O || tag == PT_GEMM_GATE_UP || tag == PT_GEMM_DOWN ||
-         tag == PT_GEMM_OUT;
+         tag == PT_GEMM_OUT || tag == PT_FUSED;
 }
 
 const char* const kProfTagNames[PT_COUNT] = {"embed",  "rmsnorm",       "quantise", "gemm_qkv", "rope_store",
                                              "attention", "gemm_o",     "gemm_gate_up", "swiglu", "gemm_down",
-                                             "gemm_output", "cdf"};
+                                             "gemm_output", "cdf",      "decode_fused"};
 
 void free_session(det_session* s) {
   if (!s) return;
@@ -426,11 +428,127 @@ det_status fwd_head(det_session* s, const Launch& L, int T) {
 
 namespace {
 
+// DETGPU_FUSED_DECODE=1 runs one-position forwards through decode_fused.cu
+// where it applies; unset or 0 keeps the per-op kernels
+bool fused_decode_enabled() {
+  static const int on = [] {
+    const char* e = std::getenv("DETGPU_FUSED_DECODE");
+    return e && *e && *e != '0' ? 1 : 0;
+  }();
+  return on != 0;
+}
+
+FdMat fd_mat(const DevMatrix& m) {
+  FdMat f;
+  f.q = static_cast<const uint8_t*>(m.q);
+  f.type = m.type;
+  f.rows = m.rows;
+  f.nb = m.nb;
+  return f;
+}
+
+// Whether this session's one-position forwards run as one persistent kernel
+// (decode_fused.cu).  It applies to a single-device model whose q|k|v and
+// gate|up are fused and whose every weight matrix, lm_head included, is
+// Q8_0 / Q4_0 in the MMA16 tile layout, with head_dim 64 or 128.  The first
+// call builds the kernel's layer table; it runs outside any graph capture
+// (run_forward checks it before capturing).
+bool fused_decode_ready(det_session* s) {
+  if (s->fd_state) return s->fd_state > 0;
+  s->fd_state = -1;
+  det_model* m = s->m;
+  const ModelCfg& c = m->cfg;
+  if (!fused_decode_enabled() || s->tp || m->shard || m->tp) return false;
+  if (!attention_tiled_supported(c.nh, c.nkv, c.hd) || !s->score_scratch) return false;
+  if (m->output.layout != LAYOUT_MMA16 || !m->output_norm || m->output.cols != c.d) return false;
+  std::vector<FdLayer> ly((size_t)c.L);
+  double wb = (double)m->output.rows * m->output.cols * bytes_per_weight(m->output.type);
+  for (int l = 0; l < c.L; l++) {
+    const LayerDev& W = m->layers[(size_t)l];
+    if (!W.wqkv.rows || !W.wgu.rows || W.wo.layout != LAYOUT_MMA16 || W.down.layout != LAYOUT_MMA16) return false;
+    FdLayer& f = ly[(size_t)l];
+    f.qkv = fd_mat(W.wqkv);
+    f.o = fd_mat(W.wo);
+    f.gu = fd_mat(W.wgu);
+    f.down = fd_mat(W.down);
+    f.attn_norm = W.attn_norm;
+    f.ffn_norm = W.ffn_norm;
+    f.bq = W.bq;
+    f.bk = W.bk;
+    f.bv = W.bv;
+    for (const DevMatrix* d : {&W.wqkv, &W.wo, &W.wgu, &W.down})
+      wb += (double)d->rows * d->cols * bytes_per_weight(d->type);
+  }
+  FdParams p;
+  const int s_ld = (s->n_ctx + 31) & ~31;
+  if (!fused_decode_plan(c.d, c.dff, c.nh, c.nkv, c.hd, s_ld, &p)) return false;
+  FdLayer* dl = nullptr;
+  unsigned* sync = nullptr;
+  if (dalloc(s, &dl, ly.size()) || dalloc(s, &sync, 2)) return false;
+  if (cudaMemcpy(dl, ly.data(), ly.size() * sizeof(FdLayer), cudaMemcpyHostToDevice) != cudaSuccess) return false;
+  int grid = 0;
+  if (fused_decode_prepare(p, &grid) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  p.layers = dl;
+  p.L = c.L;
+  p.out = fd_mat(m->output);
+  p.out_norm = m->output_norm;
+  p.d = c.d;
+  p.dff = c.dff;
+  p.nh = c.nh;
+  p.nkv = c.nkv;
+  p.hd = c.hd;
+  p.half = c.rope_dim / 2;
+  p.pairing = c.pairing;
+  p.n_ctx = s->n_ctx;
+  p.s_ld = s_ld;
+  p.vocab = m->vocab;
+  p.eps = c.eps;
+  p.scale = c.attn_scale;
+  p.pos = s->d_pos;
+  p.cos_t = s->rope_cos;
+  p.sin_t = s->rope_sin;
+  p.x = s->x;
+  p.q = s->q;
+  p.k = s->k;
+  p.v = s->v;
+  p.S = s->score_scratch;
+  p.attn = s->attn;
+  p.gate = s->gate;
+  p.up = s->up;
+  p.logits = s->logits;
+  p.kc = s->kc;
+  p.vc = s->vc;
+  p.err = s->d_err;
+  p.sync = sync;
+  s->fd = p;
+  s->fd_grid = grid;
+  s->fd_wbytes = wb;
+  s->fd_state = 1;
+  return true;
+}
+
+// The one-position forward through decode_fused.cu: the embedding row, then
+// one launch for every layer and the lm_head.  Algorithmic bytes: the
+// weights plus the KV rows the attention reads (K and V of positions
+// 0..pos in every layer).
+det_status forward_fused(det_session* s, const Launch& L) {
+  if (det_status st = fwd_embed(s, L, 1)) return st;
+  const ModelCfg& c = s->m->cfg;
+  CK(cudaMemsetAsync(s->fd.sync, 0, 2 * sizeof(unsigned), s->stream));
+  const double kv = 2.0 * c.L * c.nkv * c.hd * 4.0 * (double)(*s->h_pos + 1);
+  CK(timed(s, PT_FUSED, s->fd_wbytes + kv, s->fd_wbytes, [&] { return launch_decode_fused(L, s->fd, s->fd_grid); }));
+  return DET_OK;
+}
+
 // forward_one_with_workspace for positions pos0 .. pos0+T-1, pos0 = *d_pos
 // (tokens and pos0 already on the device)
 det_status forward_chunk(det_session* s, int T, uint64_t* launch_counter) {
   Launch L = launch_of(s);
   L.launches = launch_counter;
+  if (T == 1 && s->fd_state > 0) return forward_fused(s, L);
   // overlapping launches pays off for one-token (decode) forwards; for
   // chunks it measured slower
   L.pdl = T <= 16;
@@ -464,7 +582,10 @@ bool graphs_enabled() {
 // (the kernels read pos0 from device memory, so one graph serves every chunk).
 det_status run_forward(det_session* s, int T) {
   if (s->tp) return tp_run_forward(s, T, graphs_enabled());
-  if (!graphs_enabled()) return enqueue_forward(s, T, &s->stats.launches);
+  // the fused one-position forward is two launches and a memset: no graph
+  // (its kernel is a cooperative launch)
+  const bool fused = T == 1 && fused_decode_ready(s);
+  if (!graphs_enabled() || fused) return enqueue_forward(s, T, &s->stats.launches);
   if ((int)s->graphs.size() <= T) s->graphs.resize((size_t)T + 1);
   det_session::Graph& gr = s->graphs[(size_t)T];
   if (!gr.exec) {

@@ -4,6 +4,12 @@ Integer / byte / index results must be bit-exact, and so must every float:
 the reference's numerics are normative (fixed reduction order, explicit
 rounding), so the tolerance for logits is zero ULP.
 """
+import dataclasses
+import json
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -70,7 +76,7 @@ def long_models(oracle):
 
 
 @pytest.mark.parametrize("name", list(LONG_SPECS))
-@pytest.mark.parametrize("chunk", [37, 128, 300])
+@pytest.mark.parametrize("chunk", [1, 37, 128, 300])  # 1: one-position forwards
 def test_long_window_logits_bit_exact(D, long_models, name, chunk):
     g, toks, want = long_models[name]
     got = D.Model(g).logits_for_tokens(toks, chunk=chunk)
@@ -80,6 +86,48 @@ def test_long_window_logits_bit_exact(D, long_models, name, chunk):
 
 def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+# The child process of test_fused_one_position_forward: DETGPU_FUSED_DECODE is
+# read once per process, so the fused path runs in a process of its own.
+_FUSED_CHILD = """
+import json, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+import detllm_b200 as D
+from detllm_b200 import synth as S
+spec = S.ModelSpec(**json.loads(sys.argv[2]))
+toks = np.array(json.loads(sys.argv[3]), np.uint32)
+m = D.Model(S.build_gguf(spec))
+D.set_profiling(True)
+got = m.logits_for_tokens(toks, chunk=1)
+D.set_profiling(False)
+np.save(sys.argv[4], got)
+print(json.dumps(m.profile(reset=True)))
+"""
+
+
+@pytest.mark.parametrize("name", ["hd64_gqa8", "hd64_gqa7_qwen2", "hd128_gqa2"])
+def test_fused_one_position_forward(D, long_models, name, tmp_path):
+    """DETGPU_FUSED_DECODE=1: models whose weights are all Q8_0 / Q4_0 run
+    each one-position forward as one persistent kernel (decode_fused.cu), one
+    launch per token, with logits bit-exact against the oracle over score
+    lengths 1..120 (two 64-key tiles; GQA groups of 8 and 7, split-half RoPE
+    with q/k/v biases, head_dim 128 with Q4_0 attention)."""
+    g, toks, want = long_models[name]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = tmp_path / "logits.npy"
+    env = dict(os.environ, DETGPU_FUSED_DECODE="1")
+    r = subprocess.run([sys.executable, "-c", _FUSED_CHILD, root, json.dumps(dataclasses.asdict(LONG_SPECS[name])),
+                        json.dumps([int(t) for t in toks[:120]]), str(out)],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    prof = json.loads(r.stdout.strip().splitlines()[-1])
+    assert prof["decode_fused"][0] == 120, prof
+    assert prof["gemm_qkv"][0] == 0 and prof["attention"][0] == 0, prof
+    got = np.load(out)
+    diff = np.nonzero(bits(got) != bits(want[:120]))
+    assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
 
 
 def test_device_expf_matches_vendored_expf(D, oracle):
