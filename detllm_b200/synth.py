@@ -148,3 +148,202 @@ def markov_text(n: int, seed: int = 11) -> bytes:
         out[i] = alphabet[c]
         a, b = b, c
     return out.tobytes()
+
+
+# ---- GGUF metadata (tokenizer vocabularies) ---------------------------------
+# GGUF v3 value types (det-gguf lib.rs:58-96)
+GV_U32, GV_I32, GV_F32, GV_STRING, GV_ARRAY = 4, 5, 6, 8, 9
+
+
+def _gguf_str(s) -> bytes:
+    b = s.encode() if isinstance(s, str) else bytes(s)
+    return len(b).to_bytes(8, "little") + b
+
+
+def _gguf_value(ty: int, v) -> bytes:
+    import struct
+
+    if ty == GV_STRING:
+        return _gguf_str(v)
+    if ty == GV_U32:
+        return struct.pack("<I", v)
+    if ty == GV_I32:
+        return struct.pack("<i", v)
+    if ty == GV_F32:
+        return struct.pack("<f", v)
+    elem, items = v
+    body = b"".join(_gguf_value(elem, x) for x in items)
+    return struct.pack("<IQ", elem, len(items)) + body
+
+
+def gguf_metadata(kvs) -> bytes:
+    """A GGUF v3 file with metadata only (no tensors): kvs is a list of
+    (key, type, value); an array value is (element type, items)."""
+    out = b"GGUF" + (3).to_bytes(4, "little") + (0).to_bytes(8, "little") + len(kvs).to_bytes(8, "little")
+    for key, ty, v in kvs:
+        out += _gguf_str(key) + ty.to_bytes(4, "little") + _gguf_value(ty, v)
+    return out + b"\0" * (-len(out) % 32)
+
+
+def byte_tokens() -> list:
+    """The 256 canonical byte-fallback tokens <0x00>..<0xFF>."""
+    return [f"<0x{b:02X}>" for b in range(256)]
+
+
+def tokenizer_kvs(tokens, model=None, merges=None, scores=None, token_type=None) -> list:
+    """tokenizer.ggml.* metadata entries for gguf_metadata / with_tokenizer."""
+    kv = [("tokenizer.ggml.tokens", GV_ARRAY, (GV_STRING, list(tokens)))]
+    if model is not None:
+        kv.append(("tokenizer.ggml.model", GV_STRING, model))
+    if merges is not None:
+        kv.append(("tokenizer.ggml.merges", GV_ARRAY, (GV_STRING, list(merges))))
+    if scores is not None:
+        kv.append(("tokenizer.ggml.scores", GV_ARRAY, (GV_F32, list(scores))))
+    if token_type is not None:
+        kv.append(("tokenizer.ggml.token_type", GV_ARRAY, (GV_I32, list(token_type))))
+    return kv
+
+
+def _gpt2_chars() -> list:
+    """GPT-2's byte-to-unicode table: printable bytes stand for themselves,
+    the other 68 bytes map to code points 256, 257, ... in byte order (the
+    decoding det-token applies to BPE token strings, lib.rs:813-839)."""
+    def printable(c):
+        return 33 <= c <= 126 or 161 <= c <= 172 or 174 <= c <= 255
+    out, n = [], 0
+    for b in range(256):
+        if printable(b):
+            out.append(chr(b))
+        else:
+            out.append(chr(256 + n))
+            n += 1
+    return out
+
+
+def _spm_vocab(vocab: int, sample: bytes) -> tuple:
+    """SentencePiece-style vocabulary: the 256 byte tokens, then the most
+    frequent 2..8-byte pieces of `sample` (a leading space written as U+2581),
+    scored by descending frequency x length."""
+    counts = {}
+    for n in range(2, 9):
+        for i in range(len(sample) - n + 1):
+            p = sample[i:i + n]
+            if b"\n" in p[1:]:
+                continue
+            counts[p] = counts.get(p, 0) + 1
+    ranked = sorted(counts, key=lambda p: (-counts[p] * len(p), p))[: vocab - 256]
+    tokens = byte_tokens()
+    scores = [0.0] * 256
+    for r, p in enumerate(ranked):
+        s = p.decode()
+        tokens.append("▁" + s[1:] if s.startswith(" ") else s)
+        scores.append(-float(r + 1))
+    return tokens, scores
+
+
+def _bpe_vocab(vocab: int, sample: bytes) -> tuple:
+    """Byte-level BPE vocabulary: GPT-2 byte tokens, then merges learned on
+    `sample` (most frequent adjacent pair first, ties by first occurrence)."""
+    chars = _gpt2_chars()
+    tokens = list(chars)
+    pieces = [bytes([b]) for b in range(256)]
+    seq = [pieces[b] for b in sample]
+    merges = []
+    known = set(pieces)
+    while len(tokens) < vocab and len(seq) > 1:
+        counts, first = {}, {}
+        for i in range(len(seq) - 1):
+            pr = (seq[i], seq[i + 1])
+            counts[pr] = counts.get(pr, 0) + 1
+            first.setdefault(pr, i)
+        best = None
+        for pr, c in counts.items():
+            if pr[0] + pr[1] in known:
+                continue
+            if best is None or c > counts[best] or (c == counts[best] and first[pr] < first[best]):
+                best = pr
+        if best is None or counts[best] < 2:
+            break
+        merged = best[0] + best[1]
+        known.add(merged)
+        tokens.append("".join(chars[b] for b in merged))
+        merges.append("".join(chars[b] for b in best[0]) + " " + "".join(chars[b] for b in best[1]))
+        out, i = [], 0
+        while i < len(seq):
+            if i + 1 < len(seq) and (seq[i], seq[i + 1]) == best:
+                out.append(merged)
+                i += 2
+            else:
+                out.append(seq[i])
+                i += 1
+        seq = out
+    while len(tokens) < vocab:  # filler pieces that the merges never produce
+        tokens.append(f"<unused{len(tokens)}>")
+    return tokens, merges
+
+
+_VOCABS = {}
+
+
+def synthetic_tokenizer_kvs(kind: str, vocab: int, seed: int = 5) -> list:
+    """tokenizer.ggml.* metadata of a seeded `kind` ("spm" or "bpe")
+    vocabulary of exactly `vocab` tokens learned on Markov text."""
+    key = (kind, vocab, seed)
+    if key not in _VOCABS:
+        sample = markov_text(3000, seed=seed)
+        if kind == "spm":
+            tokens, scores = _spm_vocab(vocab, sample)
+            _VOCABS[key] = tokenizer_kvs(tokens, model="llama", scores=scores)
+        else:
+            tokens, merges = _bpe_vocab(vocab, sample)
+            _VOCABS[key] = tokenizer_kvs(tokens, model="gpt2", merges=merges)
+    return _VOCABS[key]
+
+
+def _skip_value(b: bytes, o: int, ty: int) -> int:
+    fixed = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+    if ty in fixed:
+        return o + fixed[ty]
+    if ty == GV_STRING:
+        return o + 8 + int.from_bytes(b[o:o + 8], "little")
+    if ty == GV_ARRAY:
+        et, n = int.from_bytes(b[o:o + 4], "little"), int.from_bytes(b[o + 4:o + 12], "little")
+        o += 12
+        if et in fixed:
+            return o + fixed[et] * n
+        for _ in range(n):
+            o = _skip_value(b, o, et)
+        return o
+    raise ValueError(f"GGUF value type {ty}")
+
+
+def with_tokenizer(gguf: bytes, kvs) -> bytes:
+    """`gguf` (v3) with its tokenizer.ggml.* metadata replaced by `kvs`;
+    tensor infos and data are kept (tensor offsets are relative to the
+    data section, which stays aligned to 32 bytes)."""
+    assert gguf[:4] == b"GGUF"
+    n_t = int.from_bytes(gguf[8:16], "little")
+    n_kv = int.from_bytes(gguf[16:24], "little")
+    o, keep = 24, []
+    for _ in range(n_kv):
+        start = o
+        klen = int.from_bytes(gguf[o:o + 8], "little")
+        key = gguf[o + 8:o + 8 + klen].decode()
+        ty = int.from_bytes(gguf[o + 8 + klen:o + 12 + klen], "little")
+        o = _skip_value(gguf, o + 12 + klen, ty)
+        if not key.startswith("tokenizer.ggml."):
+            keep.append(gguf[start:o])
+        if key == "general.alignment":
+            raise ValueError("custom alignment is not handled")
+    infos_start = o
+    for _ in range(n_t):
+        nlen = int.from_bytes(gguf[o:o + 8], "little")
+        o += 8 + nlen
+        nd = int.from_bytes(gguf[o:o + 4], "little")
+        o += 4 + 8 * nd + 4 + 8
+    infos = gguf[infos_start:o]
+    data = gguf[o + (-o % 32):]
+    new_kv = b"".join(_gguf_str(k) + t.to_bytes(4, "little") + _gguf_value(t, v) for k, t, v in kvs)
+    head = gguf[:8] + n_t.to_bytes(8, "little") + (len(keep) + len(kvs)).to_bytes(8, "little")
+    body = head + b"".join(keep) + new_kv + infos
+    return body + b"\0" * (-len(body) % 32) + data

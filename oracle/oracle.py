@@ -85,6 +85,9 @@ def lib():
             "ref_quantize_q8a_flat": (I, [P, SZ, P, P]),
             "ref_quantize_q8k_flat": (I, [P, SZ, P, P, P]),
             "ref_free": (None, [P]),
+            "ref_tokenizer_kind": (I, [P, SZ, C.POINTER(C.c_int)]),
+            "ref_tokenize": (I, [P, SZ, P, SZ, I, C.POINTER(P), C.POINTER(SZ)]),
+            "ref_detokenize": (I, [P, SZ, P, SZ, I, C.POINTER(P), C.POINTER(SZ)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -223,6 +226,39 @@ def decompress(model: bytes, dtlz: bytes) -> bytes:
     db = np.frombuffer(dtlz, np.uint8) if dtlz else np.zeros(1, np.uint8)
     out, n = C.c_void_p(), C.c_size_t()
     _check(lib().ref_decompress(_ptr(mb), len(model), _ptr(db), len(dtlz), C.byref(out), C.byref(n)), "decompress")
+    return _take_bytes(out, n.value)
+
+
+TOKENIZER_KINDS = ("byte_fallback", "byte_bpe", "sentencepiece")
+
+
+def tokenizer_kind(gguf: bytes) -> str:
+    """Tokenizer::from_gguf's selection (det-token lib.rs:86-132)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    k = C.c_int()
+    _check(lib().ref_tokenizer_kind(_ptr(gb), len(gguf), C.byref(k)), "tokenizer")
+    return TOKENIZER_KINDS[k.value]
+
+
+def tokenize(gguf: bytes, data: bytes, codec: bool = False) -> np.ndarray:
+    """tokenize_bytes of the GGUF's tokenizer, or with codec=True the codec
+    symbols (tokens, and vocab + byte for byte escapes)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    ib = np.frombuffer(data, np.uint8) if data else np.zeros(1, np.uint8)
+    out, n = C.c_void_p(), C.c_size_t()
+    _check(lib().ref_tokenize(_ptr(gb), len(gguf), _ptr(ib), len(data), int(codec), C.byref(out), C.byref(n)),
+           "tokenize")
+    return np.frombuffer(_take_bytes(out, 4 * n.value), np.uint32).copy()
+
+
+def detokenize(gguf: bytes, symbols, escapes: bool = True) -> bytes:
+    """The bytes of a token / codec symbol sequence (decode_codec_symbol)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    s = np.ascontiguousarray(symbols, np.uint32)
+    sb = s if s.size else np.zeros(1, np.uint32)
+    out, n = C.c_void_p(), C.c_size_t()
+    _check(lib().ref_detokenize(_ptr(gb), len(gguf), _ptr(sb), s.size, int(escapes), C.byref(out), C.byref(n)),
+           "detokenize")
     return _take_bytes(out, n.value)
 
 

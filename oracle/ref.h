@@ -134,6 +134,17 @@ typedef struct {
 } ref_model_info;
 
 void ref_set_threads(int threads);
+
+/* Tokenizers (ref_token.c; det-token lib.rs:85-850) on a GGUF's metadata:
+ * the selected kind (0 byte fallback, 1 byte-BPE, 2 SentencePiece),
+ * tokenize_bytes (codec = 0) or codec_symbols with byte escapes (codec = 1),
+ * and the bytes of a symbol sequence (decode_codec_symbol).  *out is
+ * malloc'd (ref_free). */
+int ref_tokenizer_kind(const uint8_t* gguf, size_t len, int* kind);
+int ref_tokenize(const uint8_t* gguf, size_t len, const uint8_t* in, size_t n, int codec, uint32_t** out,
+                 size_t* out_n);
+int ref_detokenize(const uint8_t* gguf, size_t len, const uint32_t* syms, size_t n, int escapes, uint8_t** out,
+                   size_t* out_n);
 int ref_model_load(const uint8_t* gguf, size_t len, ref_model** out);
 void ref_model_free(ref_model* m);
 int ref_model_get_info(const ref_model* m, ref_model_info* info);

@@ -3,11 +3,8 @@
  * (TEST INFRASTRUCTURE, see ref.h).
  *
  * Follows crates/det-cli/src/main.rs:433-855 (LoadedModel, windowed model
- * state, encode/decode loops, canonical re-encode), crates/det-token/src/
- * lib.rs:85-326, 619-850 (tokenizer selection, byte-fallback tokenizer,
- * codec symbols) and crates/det-coder/src/file.rs:1-90 (DTLZ header).
- * Only the byte-fallback tokenizer is restated; GGUFs that select the
- * byte-BPE or SentencePiece tokenizers are rejected with REF_ERR_TOKENIZER.
+ * state, encode/decode loops, canonical re-encode) and crates/det-coder/src/
+ * file.rs:1-90 (DTLZ header); the tokenizers are ref_token.c.
  */
 #include <stdlib.h>
 
@@ -15,108 +12,10 @@
 #include "ref_coder.h"
 #include "ref_internal.h"
 #include "ref_model.h"
+#include "ref_token.h"
 
 #define BYTE_ESCAPES 256u
 #define MAX_SYMBOLS (1u << 18)
-
-/* ---- byte-fallback tokenizer ------------------------------------------------ */
-typedef struct {
-    int32_t byte_to_token[256]; /* -1 if absent or not emittable */
-    int16_t* token_to_byte;      /* -1 if the token is not a byte-fallback token */
-    size_t vocab;
-} ref_tokenizer;
-
-/* canonical_byte_fallback_token (det-token lib.rs:841-848): "<0xHH>" where
- * HH parses like u8::from_str_radix(_, 16) (an optional leading '+'). */
-static int byte_fallback_of(const gg_str* s) {
-    if (s->len != 6) return -1;
-    const uint8_t* p = s->ptr;
-    if (p[0] != '<' || p[1] != '0' || p[2] != 'x' || p[5] != '>') return -1;
-    int v = 0;
-    int start = 3;
-    if (p[3] == '+') start = 4;
-    if (start == 4 && p[4] == '+') return -1;
-    for (int i = start; i < 5; i++) {
-        int c = p[i], d;
-        if (c >= '0' && c <= '9') d = c - '0';
-        else if (c >= 'a' && c <= 'f') d = c - 'a' + 10;
-        else if (c >= 'A' && c <= 'F') d = c - 'A' + 10;
-        else return -1;
-        v = v * 16 + d;
-    }
-    return v;
-}
-
-/* token_type_is_emittable (det-token lib.rs:704-710) */
-static int token_type_emittable(int64_t t, int* ok) {
-    *ok = 1;
-    if (t == 1 || t == 4 || t == 6) return 1;
-    if (t == 2 || t == 3 || t == 5) return 0;
-    *ok = 0;
-    return 0;
-}
-
-/* Tokenizer::from_gguf (det-token lib.rs:86-132) restricted to the
- * byte-fallback branch, and ByteFallbackTokenizer::from_tokens_and_emit_mask
- * (:256-296). */
-static int tokenizer_from_gguf(const gg_file* g, ref_tokenizer* t) {
-    memset(t, 0, sizeof *t);
-    const gg_kv* toks = gg_find(g, "tokenizer.ggml.tokens");
-    if (!toks || toks->type != GV_ARRAY || toks->elem_type != GV_STRING) return REF_ERR_TOKENIZER;
-    size_t V = (size_t)toks->count;
-    const gg_kv* tt = gg_find(g, "tokenizer.ggml.token_type");
-    if (tt) {
-        if (tt->type != GV_ARRAY || (tt->elem_type != GV_I32 && tt->elem_type != GV_U32)) return REF_ERR_TOKENIZER;
-        if (tt->count != V) return REF_ERR_TOKENIZER;
-    }
-    const gg_kv* merges = gg_find(g, "tokenizer.ggml.merges");
-    if (merges && (merges->type != GV_ARRAY || merges->elem_type != GV_STRING)) return REF_ERR_TOKENIZER;
-    const gg_kv* model = gg_find(g, "tokenizer.ggml.model");
-    if (model && model->type != GV_STRING) return REF_ERR_TOKENIZER;
-    const gg_kv* scores = gg_find(g, "tokenizer.ggml.scores");
-    if (scores && (scores->type != GV_ARRAY || scores->elem_type != GV_F32)) return REF_ERR_TOKENIZER;
-    /* byte-BPE / SentencePiece selection: not restated (out of scope) */
-    if (model || (merges && merges->count > 0) || scores) return REF_ERR_TOKENIZER;
-    int* emit = NULL;
-    if (tt) {
-        emit = (int*)malloc(sizeof(int) * (V ? V : 1));
-        if (!emit) return REF_ERR_ALLOC;
-        for (size_t i = 0; i < V; i++) {
-            uint32_t raw = (uint32_t)tt->arr[4 * i] | ((uint32_t)tt->arr[4 * i + 1] << 8) |
-                           ((uint32_t)tt->arr[4 * i + 2] << 16) | ((uint32_t)tt->arr[4 * i + 3] << 24);
-            int64_t v = tt->elem_type == GV_I32 ? (int64_t)(int32_t)raw : (int64_t)raw;
-            int ok;
-            emit[i] = token_type_emittable(v, &ok);
-            if (!ok) { free(emit); return REF_ERR_TOKENIZER; }
-        }
-    }
-    int seen[256];
-    for (int b = 0; b < 256; b++) { seen[b] = 0; t->byte_to_token[b] = -1; }
-    t->vocab = V;
-    t->token_to_byte = (int16_t*)malloc(sizeof(int16_t) * (V ? V : 1));
-    if (!t->token_to_byte) { free(emit); return REF_ERR_ALLOC; }
-    for (size_t i = 0; i < V; i++) t->token_to_byte[i] = -1;
-    for (size_t i = 0; i < V; i++) {
-        int b = byte_fallback_of(&toks->strs[i]);
-        if (b < 0) continue;
-        if (seen[b]) { free(emit); free(t->token_to_byte); t->token_to_byte = NULL; return REF_ERR_TOKENIZER; }
-        seen[b] = 1;
-        t->token_to_byte[i] = (int16_t)b;
-        if (!emit || emit[i]) t->byte_to_token[b] = (int32_t)i;
-    }
-    free(emit);
-    for (int b = 0; b < 256; b++)
-        if (!seen[b]) { free(t->token_to_byte); t->token_to_byte = NULL; return REF_ERR_TOKENIZER; }
-    return REF_OK;
-}
-
-/* Tokenizer::codec_symbols (det-token lib.rs:150-180) for byte fallback */
-static void codec_symbols(const ref_tokenizer* t, const uint8_t* in, size_t n, size_t V, uint32_t* out) {
-    for (size_t i = 0; i < n; i++) {
-        int32_t tok = t->byte_to_token[in[i]];
-        out[i] = tok >= 0 ? (uint32_t)tok : (uint32_t)(V + in[i]);
-    }
-}
 
 /* ---- windowed model state: det-cli main.rs:632-778 ---------------------------- */
 typedef struct {
@@ -252,7 +151,7 @@ int ref_symbol_ranges_stream(const ref_model* m, const uint32_t* symbols, size_t
 typedef struct {
     uint8_t sha[32];
     ref_model* model;
-    ref_tokenizer tok;
+    ref_tok tok;
 } loaded_t;
 
 static int load(const uint8_t* bytes, size_t len, loaded_t* L) {
@@ -260,22 +159,22 @@ static int load(const uint8_t* bytes, size_t len, loaded_t* L) {
     ref_sha256(bytes, len, L->sha);
     gg_file g;
     if (gg_parse(bytes, len, &g)) return REF_ERR_GGUF;
-    int st = tokenizer_from_gguf(&g, &L->tok);
+    int st = ref_tok_from_gguf(&g, &L->tok);
     if (!st) st = ref_model_load_gguf(&g, bytes, &L->model);
     gg_free(&g);
-    if (st) { free(L->tok.token_to_byte); return st; }
+    if (st) { ref_tok_free(&L->tok); return st; }
     if (L->tok.vocab != L->model->vocab) st = REF_ERR_VOCAB_MISMATCH;
     else if (L->model->vocab + BYTE_ESCAPES > MAX_SYMBOLS) st = REF_ERR_CDF_TOO_MANY_SYMBOLS;
     if (st) {
         ref_model_free(L->model);
-        free(L->tok.token_to_byte);
+        ref_tok_free(&L->tok);
     }
     return st;
 }
 
 static void unload(loaded_t* L) {
     ref_model_free(L->model);
-    free(L->tok.token_to_byte);
+    ref_tok_free(&L->tok);
 }
 
 static void put_le(uint8_t* p, uint64_t v, int n) {
@@ -293,15 +192,14 @@ int ref_compress(const uint8_t* model_bytes, size_t model_len, const uint8_t* in
     loaded_t L;
     int st = load(model_bytes, model_len, &L);
     if (st) return st;
-    size_t V = L.model->vocab;
-    uint32_t* sym = (uint32_t*)malloc(sizeof(uint32_t) * (in_len ? in_len : 1));
-    if (!sym) { unload(&L); return REF_ERR_ALLOC; }
-    codec_symbols(&L.tok, input, in_len, V, sym);
+    uint32_t* sym = NULL;
+    size_t nsym = 0;
+    if ((st = ref_tok_codec_symbols(&L.tok, input, in_len, &sym, &nsym))) { unload(&L); return st; }
     size_t n_ctx = n_ctx_opt ? n_ctx_opt : L.model->cfg.ctx;
     size_t overlap = n_ctx / 4;
     rc_enc e;
     rc_enc_init(&e);
-    st = encode_symbols(L.model, sym, in_len, n_ctx, overlap, 1, &e, NULL);
+    st = encode_symbols(L.model, sym, nsym, n_ctx, overlap, 1, &e, NULL);
     if (!st) st = rc_enc_finish(&e);
     free(sym);
     if (st) { free(e.out); unload(&L); return st; }
@@ -344,12 +242,15 @@ int ref_decompress(const uint8_t* model_bytes, size_t model_len, const uint8_t* 
     if (memcmp(L.sha, dtlz + 8, 32) != 0) { unload(&L); return REF_ERR_MODEL_HASH_MISMATCH; }
     if ((st = validate_window(n_ctx, overlap, L.model->cfg.ctx))) { unload(&L); return st; }
     int escapes = (flags & 1) != 0;
-    size_t V = L.model->vocab;
     rc_dec d;
     if ((st = rc_dec_init(&d, payload, plen))) { unload(&L); return st; }
     wstate w;
     if ((st = ws_init(&w, L.model, n_ctx, escapes))) { unload(&L); return st; }
-    size_t cap = (size_t)orig_len + 16;
+    /* the last symbol may run past orig_len by up to one token's bytes */
+    size_t maxtok = 1;
+    for (size_t i = 0; i < L.tok.vocab; i++)
+        if (L.tok.tok_len[i] > (int64_t)maxtok) maxtok = (size_t)L.tok.tok_len[i];
+    size_t cap = (size_t)orig_len + maxtok + 16;
     uint8_t* bytes = (uint8_t*)malloc(cap);
     uint32_t* ctx = (uint32_t*)malloc(sizeof(uint32_t) * (cap));
     uint32_t* syms = (uint32_t*)malloc(sizeof(uint32_t) * (cap));
@@ -359,20 +260,17 @@ int ref_decompress(const uint8_t* model_bytes, size_t model_len, const uint8_t* 
         if ((st = ws_sync(&w, ctx, clen, overlap))) break;
         uint32_t s;
         if ((st = ws_decode_symbol(&w, &d, &s))) break;
-        /* decode_codec_symbol (det-token lib.rs:182-199) / detokenize_bytes */
-        int byte;
-        if (s < V) {
-            byte = L.tok.token_to_byte[s];
-            if (byte < 0) { st = REF_ERR_TOKENIZER; break; }
-        } else if (escapes && s < V + BYTE_ESCAPES) {
-            byte = (int)(s - V);
-        } else {
-            st = REF_ERR_TOKENIZER;
-            break;
-        }
-        bytes[nb++] = (uint8_t)byte;
+        /* decode_codec_symbol (det-token lib.rs:182-196) / detokenize_bytes;
+         * a symbol that yields no bytes is an error (main.rs:614-616) */
+        uint8_t one;
+        const uint8_t* piece;
+        size_t plen_sym;
+        if ((st = ref_tok_symbol_bytes(&L.tok, s, escapes, &one, &piece, &plen_sym))) break;
+        if (plen_sym == 0) { st = REF_ERR_TOKENIZER; break; }
+        memcpy(bytes + nb, piece, plen_sym);
+        nb += plen_sym;
         syms[ns++] = s;
-        if (escapes && s >= V) continue;
+        if (escapes && s >= L.tok.vocab) continue;
         ctx[clen++] = s;
         st = ws_advance(&w, s);
     }
@@ -391,5 +289,64 @@ int ref_decompress(const uint8_t* model_bytes, size_t model_len, const uint8_t* 
     if (st) { free(bytes); return st; }
     *out = bytes;
     *out_len = (size_t)orig_len;
+    return REF_OK;
+}
+
+/* ---- tokenizer entry points for the tests: Tokenizer::from_gguf on the GGUF
+ * metadata, then tokenize_bytes / codec_symbols / decode_codec_symbol ---- */
+static int tok_load(const uint8_t* gguf, size_t len, ref_tok* t) {
+    gg_file g;
+    if (gg_parse(gguf, len, &g)) return REF_ERR_GGUF;
+    const int st = ref_tok_from_gguf(&g, t);
+    gg_free(&g);
+    return st;
+}
+
+int ref_tokenizer_kind(const uint8_t* gguf, size_t len, int* kind) {
+    ref_tok t;
+    const int st = tok_load(gguf, len, &t);
+    if (st) return st;
+    *kind = t.kind;
+    ref_tok_free(&t);
+    return REF_OK;
+}
+
+int ref_tokenize(const uint8_t* gguf, size_t len, const uint8_t* in, size_t n, int codec, uint32_t** out,
+                 size_t* out_n) {
+    ref_tok t;
+    int st = tok_load(gguf, len, &t);
+    if (st) return st;
+    st = codec ? ref_tok_codec_symbols(&t, in, n, out, out_n) : ref_tok_tokenize(&t, in, n, out, out_n);
+    ref_tok_free(&t);
+    return st;
+}
+
+int ref_detokenize(const uint8_t* gguf, size_t len, const uint32_t* syms, size_t n, int escapes, uint8_t** out,
+                   size_t* out_n) {
+    ref_tok t;
+    int st = tok_load(gguf, len, &t);
+    if (st) return st;
+    size_t total = 0, cap = 64;
+    uint8_t* o = (uint8_t*)malloc(cap);
+    if (!o) st = REF_ERR_ALLOC;
+    for (size_t i = 0; !st && i < n; i++) {
+        uint8_t one;
+        const uint8_t* p;
+        size_t pl;
+        if ((st = ref_tok_symbol_bytes(&t, syms[i], escapes, &one, &p, &pl))) break;
+        while (total + pl > cap) {
+            uint8_t* q = (uint8_t*)realloc(o, cap * 2);
+            if (!q) { st = REF_ERR_ALLOC; break; }
+            o = q;
+            cap *= 2;
+        }
+        if (st) break;
+        memcpy(o + total, p, pl);
+        total += pl;
+    }
+    ref_tok_free(&t);
+    if (st) { free(o); return st; }
+    *out = o;
+    *out_n = total;
     return REF_OK;
 }
