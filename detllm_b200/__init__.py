@@ -97,6 +97,9 @@ def lib():
             "det_decompress": (I, [P, P, SZ, C.POINTER(P), C.POINTER(SZ)]),
             "det_encode_symbols": (I, [P, P, SZ, U32, U32, I, C.POINTER(P), C.POINTER(SZ)]),
             "det_free": (None, [P]),
+            "det_tokenizer_kind": (I, [P, SZ, C.POINTER(C.c_int)]),
+            "det_tokenize": (I, [P, SZ, P, SZ, I, C.POINTER(P), C.POINTER(SZ)]),
+            "det_detokenize": (I, [P, SZ, P, SZ, I, C.POINTER(P), C.POINTER(SZ)]),
             "det_session_stats": (I, [P, C.POINTER(Stats), I]),
             "det_device_expf": (I, [I, P, P, SZ]),
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
@@ -316,6 +319,40 @@ def device_expf(x: np.ndarray, device: int = 0) -> np.ndarray:
     y = np.empty_like(x)
     _check(lib().det_device_expf(device, _ptr(x), _ptr(y), x.size), "det_device_expf")
     return y
+
+
+TOKENIZER_KINDS = ("byte_fallback", "byte_bpe", "sentencepiece")
+
+
+def tokenizer_kind(gguf: bytes) -> str:
+    """``Tokenizer::from_gguf``'s selection for a GGUF's tokenizer metadata
+    (host only, no device)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    k = C.c_int()
+    _check(lib().det_tokenizer_kind(_ptr(gb), len(gguf), C.byref(k)), "det_tokenizer_kind")
+    return TOKENIZER_KINDS[k.value]
+
+
+def tokenize(gguf: bytes, data: bytes, codec: bool = False) -> np.ndarray:
+    """``tokenize_bytes``, or with codec=True the codec symbols (tokens, and
+    vocab + byte for byte escapes), of the GGUF's tokenizer (host only)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    ib = np.frombuffer(data, np.uint8) if data else np.zeros(1, np.uint8)
+    out, n = C.c_void_p(), C.c_size_t()
+    _check(lib().det_tokenize(_ptr(gb), len(gguf), _ptr(ib), len(data), int(codec), C.byref(out), C.byref(n)),
+           "det_tokenize")
+    return np.frombuffer(_take(out, 4 * n.value), np.uint32).copy()
+
+
+def detokenize(gguf: bytes, symbols, byte_escapes: bool = True) -> bytes:
+    """The bytes of a token / codec symbol sequence (host only)."""
+    gb = np.frombuffer(gguf, np.uint8)
+    s = np.ascontiguousarray(symbols, np.uint32)
+    sb = s if s.size else np.zeros(1, np.uint32)
+    out, n = C.c_void_p(), C.c_size_t()
+    _check(lib().det_detokenize(_ptr(gb), len(gguf), _ptr(sb), s.size, int(byte_escapes), C.byref(out),
+                                C.byref(n)), "det_detokenize")
+    return _take(out, n.value)
 
 
 def compress(model: Model, data: bytes, n_ctx: int = 0) -> bytes:

@@ -166,7 +166,7 @@ det_status copy_out(const std::vector<uint8_t>& v, uint8_t** out, size_t* out_le
 // LoadedModel checks (det-cli main.rs:954-1008)
 det_status codec_model_checks(det_model* m) {
   if (m->tok_status) return m->tok_status;
-  if (m->tok_vocab != (size_t)m->vocab) return DET_ERR_VOCAB_MISMATCH;
+  if (m->tok.vocab != (size_t)m->vocab) return DET_ERR_VOCAB_MISMATCH;
   if ((uint64_t)m->vocab + kEscapes > (1u << 18)) return DET_ERR_CDF_TOO_MANY_SYMBOLS;
   return DET_OK;
 }
@@ -197,16 +197,13 @@ det_status det_compress(det_model* m, const uint8_t* input, size_t len, uint32_t
                         size_t* out_len) {
   if (!m || (!input && len) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
   if (det_status st = codec_model_checks(m)) return st;
-  const uint32_t V = (uint32_t)m->vocab;
-  std::vector<uint32_t> sym(len);
-  for (size_t i = 0; i < len; i++) {  // codec_symbols (det-token lib.rs:150-180)
-    const int32_t t = m->byte_to_token[input[i]];
-    sym[i] = t >= 0 ? (uint32_t)t : V + input[i];
-  }
+  std::vector<uint32_t> sym;  // codec_symbols (det-token lib.rs:150-180)
+  sym.reserve(len);
+  if (det_status st = m->tok.codec_symbols(input, len, &sym)) return st;
   const uint32_t ctx = n_ctx ? n_ctx : (uint32_t)m->cfg.ctx;
   const uint32_t overlap = ctx / 4;
   std::vector<uint8_t> payload;
-  if (det_status st = encode_impl(m, sym.data(), len, ctx, overlap, 1, &payload)) return st;
+  if (det_status st = encode_impl(m, sym.data(), sym.size(), ctx, overlap, 1, &payload)) return st;
   std::vector<uint8_t> file(56 + payload.size());
   std::memcpy(file.data(), "DTLZ", 4);  // DtlzHeader::encode (file.rs:28-38)
   put_le(&file[4], 1, 2);
@@ -249,6 +246,7 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
   if (det_status st = det_session_reset(s)) return st;
   std::vector<uint8_t> bytes;
   std::vector<uint32_t> ctx, syms;
+  std::string piece;
   size_t ws = 0, clen = 0;
   uint32_t last_row = 0;
   det_status st = DET_OK;
@@ -281,18 +279,11 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
       if ((st = det_decoder_lookup(s, last_row, escapes, value, &symbol, &r))) break;
       if ((st = dec.advance(r.cum, r.freq, r.total))) break;
     }
-    // decode_codec_symbol / detokenize_bytes (det-token lib.rs:182-199, 310-322)
-    int byte;
-    if (symbol < V) {
-      byte = symbol < m->token_to_byte.size() ? m->token_to_byte[symbol] : -1;
-      if (byte < 0) { st = DET_ERR_TOKENIZER; break; }
-    } else if (escapes && symbol < V + kEscapes) {
-      byte = (int)(symbol - V);
-    } else {
-      st = DET_ERR_TOKENIZER;
-      break;
-    }
-    bytes.push_back((uint8_t)byte);
+    // decode_codec_symbol / detokenize_bytes (det-token lib.rs:182-196); a
+    // symbol without bytes is an error (det-cli main.rs:614-616)
+    if ((st = m->tok.symbol_bytes(symbol, escapes != 0, &piece))) break;
+    if (piece.empty()) { st = DET_ERR_TOKENIZER; break; }
+    bytes.insert(bytes.end(), piece.begin(), piece.end());
     syms.push_back(symbol);
     if (escapes && symbol >= V) continue;
     ctx.push_back(symbol);

@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cstring>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/detgpu.h"
@@ -102,6 +103,24 @@ class Gguf {
   size_t len_ = 0;
 };
 
+// ---- tokenizers (tokenizer.cpp; det-token lib.rs:85-850) -------------------
+struct Tokenizer {
+  enum Kind : int { BYTE_FALLBACK = 0, BPE = 1, SPM = 2 };
+  Kind kind = BYTE_FALLBACK;
+  size_t vocab = 0;
+  int32_t byte_to_token[256];       // the single-byte token of each byte, -1 if none emittable
+  std::vector<std::string> bytes;   // token_to_bytes
+  std::vector<char> has_bytes;      // byte fallback: only the "<0xHH>" tokens have bytes
+  std::unordered_map<uint64_t, std::pair<uint64_t, uint32_t>> merges;  // (left, right) -> (rank, merged)
+  std::unordered_map<std::string, uint32_t> pieces;  // SentencePiece multi-byte pieces -> token
+  size_t max_piece_len = 1;
+
+  det_status from_gguf(const Gguf& g);
+  det_status tokenize(const uint8_t* in, size_t n, std::vector<uint32_t>* out) const;
+  det_status codec_symbols(const uint8_t* in, size_t n, std::vector<uint32_t>* out) const;
+  det_status symbol_bytes(uint32_t symbol, bool escapes, std::string* piece) const;
+};
+
 // ---- model ------------------------------------------------------------------
 struct LayerDev {
   DevMatrix wq, wk, wv, wo, gate, up, down;
@@ -167,11 +186,9 @@ struct det_model {
   det::ModelCfg cfg;
   int vocab = 0;
   uint8_t sha[32];
-  // byte-fallback tokenizer (det-token lib.rs:228-326)
+  // the codec's tokenizer (tokenizer.cpp); tok_status: its construction error
   det_status tok_status = DET_OK;
-  int32_t byte_to_token[256];
-  std::vector<int16_t> token_to_byte;
-  size_t tok_vocab = 0;
+  det::Tokenizer tok;
   det::DevMatrix tok_embd, output;
   bool tied = false;
   std::vector<det::LayerDev> layers;

@@ -397,65 +397,6 @@ det_status vocab_size(const Gguf& g, size_t* out) {
 }
 
 // canonical_byte_fallback_token (det-token lib.rs:841-848)
-int byte_fallback_of(const std::string& s) {
-  if (s.size() != 6 || s[0] != '<' || s[1] != '0' || s[2] != 'x' || s[5] != '>') return -1;
-  const char* h = s.c_str() + 3;
-  int start = h[0] == '+' ? 1 : 0;
-  if (start == 1 && h[1] == '+') return -1;
-  int v = 0;
-  for (int i = start; i < 2; i++) {
-    const char c = h[i];
-    int dgt;
-    if (c >= '0' && c <= '9') dgt = c - '0';
-    else if (c >= 'a' && c <= 'f') dgt = c - 'a' + 10;
-    else if (c >= 'A' && c <= 'F') dgt = c - 'A' + 10;
-    else return -1;
-    v = v * 16 + dgt;
-  }
-  return v;
-}
-
-det_status tokenizer_from_gguf(const Gguf& g, det_model* m) {
-  for (int b = 0; b < 256; b++) m->byte_to_token[b] = -1;
-  const GgufValue* toks = g.find("tokenizer.ggml.tokens");
-  if (!toks || toks->type != GV_ARRAY || toks->elem_type != GV_STRING) return DET_ERR_TOKENIZER;
-  const size_t V = toks->strs.size();
-  const GgufValue* tt = g.find("tokenizer.ggml.token_type");
-  if (tt && (tt->type != GV_ARRAY || (tt->elem_type != GV_I32 && tt->elem_type != GV_U32) || tt->count != V))
-    return DET_ERR_TOKENIZER;
-  const GgufValue* merges = g.find("tokenizer.ggml.merges");
-  if (merges && (merges->type != GV_ARRAY || merges->elem_type != GV_STRING)) return DET_ERR_TOKENIZER;
-  const GgufValue* model = g.find("tokenizer.ggml.model");
-  if (model && model->type != GV_STRING) return DET_ERR_TOKENIZER;
-  const GgufValue* scores = g.find("tokenizer.ggml.scores");
-  if (scores && (scores->type != GV_ARRAY || scores->elem_type != GV_F32)) return DET_ERR_TOKENIZER;
-  if (model || (merges && !merges->strs.empty()) || scores) return DET_ERR_TOKENIZER;  // BPE / SPM: out of scope
-  std::vector<int> emit(V, 1);
-  if (tt)
-    for (size_t i = 0; i < V; i++) {
-      uint32_t raw;
-      std::memcpy(&raw, tt->raw + 4 * i, 4);
-      const int64_t ty = tt->elem_type == GV_I32 ? (int64_t)(int32_t)raw : (int64_t)raw;
-      if (ty == 1 || ty == 4 || ty == 6) emit[i] = 1;
-      else if (ty == 2 || ty == 3 || ty == 5) emit[i] = 0;
-      else return DET_ERR_TOKENIZER;
-    }
-  bool seen[256] = {false};
-  m->token_to_byte.assign(V, -1);
-  for (size_t i = 0; i < V; i++) {
-    const int b = byte_fallback_of(toks->strs[i]);
-    if (b < 0) continue;
-    if (seen[b]) return DET_ERR_TOKENIZER;
-    seen[b] = true;
-    m->token_to_byte[i] = (int16_t)b;
-    if (emit[i]) m->byte_to_token[b] = (int32_t)i;
-  }
-  for (bool s : seen)
-    if (!s) return DET_ERR_TOKENIZER;
-  m->tok_vocab = V;
-  return DET_OK;
-}
-
 void free_model(det_model* m) {
   if (!m) return;
   int cur;
@@ -473,7 +414,7 @@ det_status load_impl(const uint8_t* bytes, size_t len, det_model* m) {
   h.finish(m->sha);
   Gguf g;
   if (g.parse(bytes, len)) return DET_ERR_GGUF;
-  m->tok_status = tokenizer_from_gguf(g, m);
+  m->tok_status = m->tok.from_gguf(g);
   ModelCfg& c = m->cfg;
   if (det_status st = config_from_gguf(g, &c)) return st;
   size_t V;

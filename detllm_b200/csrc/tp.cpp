@@ -182,9 +182,7 @@ det_status make_shard(det_model* R, int p, int G, bool attn_sharded, det_model**
   S->vocab = R->vocab;
   std::memcpy(S->sha, R->sha, 32);
   S->tok_status = R->tok_status;
-  std::memcpy(S->byte_to_token, R->byte_to_token, sizeof S->byte_to_token);
-  S->token_to_byte = R->token_to_byte;
-  S->tok_vocab = R->tok_vocab;
+  S->tok = R->tok;
   S->tok_embd = R->tok_embd;
   S->tied = R->tied;
   S->output_norm = R->output_norm;

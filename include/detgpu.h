@@ -188,6 +188,23 @@ det_status det_encode_symbols(det_model* model, const uint32_t* symbols, size_t 
                               int byte_escapes, uint8_t** out, size_t* out_len);
 void det_free(void* p);
 
+/* ---- tokenizers: replace Tokenizer::from_gguf, tokenize_bytes,
+ *      codec_symbols and decode_codec_symbol (det-token lib.rs:86-196,
+ *      306-617).  Host only: they read the GGUF's tokenizer.ggml.* metadata
+ *      and need no device.  kind: 0 byte fallback, 1 byte-level BPE
+ *      (tokenizer.ggml.model "gpt2", or merges), 2 SentencePiece ("llama",
+ *      "spm", "sentencepiece", or scores).  codec != 0 returns codec symbols
+ *      (vocab + byte for a byte without a single-byte token); byte_escapes
+ *      != 0 lets det_detokenize take those symbols.  *out is allocated by
+ *      the library; release it with det_free.  Malformed tokenizer metadata
+ *      and bytes or tokens the tokenizer cannot map return
+ *      DET_ERR_TOKENIZER. */
+det_status det_tokenizer_kind(const uint8_t* gguf, size_t len, int* kind);
+det_status det_tokenize(const uint8_t* gguf, size_t len, const uint8_t* input, size_t n, int codec, uint32_t** out,
+                        size_t* out_n);
+det_status det_detokenize(const uint8_t* gguf, size_t len, const uint32_t* symbols, size_t n, int byte_escapes,
+                          uint8_t** out, size_t* out_n);
+
 /* ---- device numerics self-test: replaces `detllm selftest`'s canaries
  *      (det-cli main.rs:126-144) with a direct check of the device expf.
  * y[i] = det-num exp_f32(x[i]) (vendored_libm/expf.rs:33-106) computed on

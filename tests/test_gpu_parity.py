@@ -272,3 +272,19 @@ def test_nonfinite_is_an_error_like_the_reference(D, oracle):
     with pytest.raises(D.DetError) as eg:
         D.Model(g).logits_for_tokens([1, 2])
     assert eo.value.code == eg.value.code == 2
+
+
+@pytest.mark.parametrize("kind", ["spm", "bpe"])
+def test_codec_bytes_sentencepiece_and_bpe(D, oracle, kind):
+    """compress / decompress through a SentencePiece and a byte-level BPE
+    vocabulary (multi-byte tokens, det-token lib.rs:328-617) at n_ctx 48 (many
+    window rollovers): DTLZ bytes equal to the oracle's, and decompress
+    restores the input."""
+    spec = S.ModelSpec(n_layer=1, d=128, d_ff=256, n_head=2, n_head_kv=1, vocab=700, ctx=64, seed=41)
+    g = S.with_tokenizer(S.build_gguf(spec), S.synthetic_tokenizer_kvs(kind, 700, seed=5))
+    data = S.markov_text(600, seed=5) + bytes([0, 255, 10])
+    want = oracle.compress(g, data, 48)
+    m = D.Model(g)
+    got = D.compress(m, data, 48)
+    assert got == want
+    assert D.decompress(m, got) == data

@@ -47,7 +47,7 @@ class Impl:
         return [int(t) for t in self.tok(g, data, codec=True)]
 
 
-@pytest.fixture(scope="module", params=["oracle"])
+@pytest.fixture(scope="module", params=["oracle", "product"])
 def impl(request):
     return Impl(request.param)
 
