@@ -320,7 +320,19 @@ DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
 constexpr int G4_ROWS = 32;
 constexpr int G4_PWARPS = 8;
 constexpr int G4_PTHREADS = G4_PWARPS * 32;
-constexpr int G4_THREADS = G4_PTHREADS + 32;
+constexpr int G4_THREADS = G4_PTHREADS + 32;   // producers + chain warp (named-barrier count)
+// The CTA has 12 warps: producers are warps {0,1,2,4,5,6,8,9}, the chain
+// warp is warp 3, and warps 7, 10, 11 only help stage the activation.  An
+// SM sub-partition issues the warps whose ids agree mod 4, so the chain
+// warp (K dependent adds per row) has its scheduler to itself instead of
+// sharing it with two producer warps; 12 warps keep the mapping the same
+// for every CTA on the SM.
+constexpr int G4_BLOCK = 12 * 32;
+constexpr int G4_CHAIN_WARP = 3;
+// producer index of warp w (-1: not a producer)
+__host__ __device__ constexpr int g4_producer(int w) {
+  return w < 3 ? w : w == 3 || w == 7 || w > 9 ? -1 : w < 7 ? w - 1 : w - 2;
+}
 constexpr int G4_LD = 260;
 constexpr int G4_NBUF = 2;
 constexpr int G4_PREF = 4;                   // super-blocks in flight ahead of the producers
@@ -377,7 +389,7 @@ DI unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned 
   return r;
 }
 
-__global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, const int8_t* __restrict__ aq,
+__global__ void __launch_bounds__(G4_BLOCK) gemv_q4k_chain_kernel(KqSegs S, const int8_t* __restrict__ aq,
                                                                     const float* __restrict__ ad, uint32_t* err) {
   extern __shared__ __align__(16) uint8_t g4_smem[];
   float* prod = reinterpret_cast<float*>(g4_smem);                     // [G4_NBUF][G4_ROWS][G4_LD]
@@ -386,7 +398,10 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
   const KqSeg g = kq_seg(S);
   const int r0 = ((int)blockIdx.x - g.cta0) * G4_ROWS;
   const int nbs = S.nb, nbk = nbs * 8;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = g4_producer(tid >> 5);  // producer index 0..7, or -1
+  const int ptid = warp * 32 + lane;       // producer thread index
+  const bool chain = (tid >> 5) == G4_CHAIN_WARP;
   const int row = r0 + lane;
   const bool ok = row < g.rows;
 
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
   auto issue = [&](int s) {
       if (s < nbs) {
         uint8_t* dst0 = raw + (size_t)(s % G4_RAWN) * G4_RAW_STAGE;
-        for (int c = tid; c < G4_ROWS * 9; c += G4_PTHREADS) {
+        for (int c = ptid; c < G4_ROWS * 9; c += G4_PTHREADS) {
           const int r = c / 9, part = c - 9 * r;
           uint8_t* dst = dst0 + r * 144 + part * 16;
           if (r0 + r < g.rows)
@@ -408,17 +423,18 @@ __global__ void __launch_bounds__(G4_THREADS) gemv_q4k_chain_kernel(KqSegs S, co
       }
       g4_cp_commit();
   };
-  if (warp < G4_PWARPS)  // weights are constant: stream them before the predecessor ends
+  if (warp >= 0)  // weights are constant: stream them before the predecessor ends
     for (int s = 0; s < G4_PREF; s++) issue(s);
   pdl_enter();
   // the activation, dequantised once: act[i] = a.d * a.q (the reference's value)
-  for (int i = tid; i < nbk * 32; i += G4_THREADS) {
+  for (int i = tid; i < nbk * 32; i += G4_BLOCK) {
     const int kb = i >> 5;
     act[i] = fmul(ad[q8a_dslot(nbk, 0, kb)], (float)aq[q8a_elem(nbk, 0, kb, i & 31)]);
   }
   __syncthreads();
+  if (warp < 0 && !chain) return;  // staging warps: done
 
-  if (warp < G4_PWARPS) {
+  if (warp >= 0) {
     const unsigned long long one2 = pk2(S.one, S.one), nmag2 = pk2(-8388608.0f, -8388608.0f);
     for (int s = 0; s < nbs; s++) {
       issue(s + G4_PREF);
@@ -725,7 +741,7 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     if (dev < 16) attr_set.fetch_or(bit);
   }
   if (q4)
-    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_THREADS, g4_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
+    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_BLOCK, g4_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
   else if (r32)
     e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
   else
