@@ -56,6 +56,9 @@ METRIC = "encode tokens/s (logits+CDF+code)"
 # headline config, from one ncu capture
 # (profiles/gemv_decode_stream_tinyllama_q8_0_1token_traffic.md)
 DECODE_GEMV_TRAFFIC_PER_LAUNCH = 12.400e6
+# DRAM bytes (read + write) per launch of the fused one-position kernel, per
+# config, from one ncu capture (profiles/decode_fused_tinyllama_q8_0_1token.md)
+DECODE_FUSED_TRAFFIC_PER_LAUNCH = {"tinyllama-q8_0": 1146.713e6 + 25.272e6}
 
 
 def log(*a):
@@ -337,8 +340,8 @@ def roofline(dec, peak, peak_kind):
     if dec.get("fused"):
         gbs = dec["gemv_gbs_in_forward"]
         return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                "frac": gbs / peak if gbs else None, "traffic": None,
-                "traffic_unit": "bytes per launch (no ncu capture of this kernel's DRAM bytes yet)",
+                "frac": gbs / peak if gbs else None, "traffic": DECODE_FUSED_TRAFFIC_PER_LAUNCH.get(CONFIG),
+                "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
                 "kernel": f"decode_fused_kernel: one token's forward (all layers + lm_head) in one launch ({CONFIG})",
                 "peak_kind": peak_kind, "launches": 1, "ms_per_launch": dec["gemv_ms_per_launch"],
                 "bytes_per_launch": dec["gemv_bytes_per_launch"],
