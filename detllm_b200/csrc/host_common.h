@@ -21,6 +21,7 @@ class Sha256 {
 
  private:
   void block(const uint8_t* p);
+  void blocks(const uint8_t* p, size_t n);  // SHA extensions where the CPU has them
   uint32_t st_[8];
   uint64_t len_ = 0;
   uint8_t buf_[64];

@@ -1,6 +1,12 @@
 // host_util.cpp -- SHA-256, the range coder and the GGUF reader of
 // libdetgpu.so (host side).
 #include <algorithm>
+#include <cstdlib>
+
+#if defined(__x86_64__)
+#include <cpuid.h>
+#include <immintrin.h>
+#endif
 
 #include "host_common.h"
 
@@ -42,14 +48,71 @@ void Sha256::block(const uint8_t* p) {
   st_[0] += a; st_[1] += b; st_[2] += c; st_[3] += d; st_[4] += e; st_[5] += f; st_[6] += g; st_[7] += h;
 }
 
+#if defined(__x86_64__)
+// n 64-byte blocks with the x86 SHA extensions (Intel's SHA-256 instruction
+// set: sha256rnds2 runs two rounds on the state packed as ABEF / CDGH,
+// sha256msg1 / sha256msg2 extend the message schedule four words at a time)
+__attribute__((target("sha,sse4.1,ssse3"))) static void sha256_blocks_ni(uint32_t st[8], const uint8_t* p,
+                                                                          size_t n) {
+  const __m128i bswap = _mm_set_epi64x(0x0c0d0e0f08090a0bLL, 0x0405060700010203LL);
+  __m128i t = _mm_shuffle_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(st)), 0xB1);  // b a d c
+  __m128i s1 = _mm_shuffle_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(st + 4)), 0x1B);  // h g f e
+  __m128i s0 = _mm_alignr_epi8(t, s1, 8);  // f e b a (ABEF)
+  s1 = _mm_blend_epi16(s1, t, 0xF0);       // h g d c (CDGH)
+  for (; n; n--, p += 64) {
+    const __m128i save0 = s0, save1 = s1;
+    __m128i m[16];
+    for (int g = 0; g < 4; g++)
+      m[g] = _mm_shuffle_epi8(_mm_loadu_si128(reinterpret_cast<const __m128i*>(p + 16 * g)), bswap);
+    for (int g = 4; g < 16; g++)  // W[t..t+3] from W[t-16..t-1]
+      m[g] = _mm_sha256msg2_epu32(
+          _mm_add_epi32(_mm_sha256msg1_epu32(m[g - 4], m[g - 3]), _mm_alignr_epi8(m[g - 1], m[g - 2], 4)), m[g - 1]);
+    for (int g = 0; g < 16; g++) {
+      __m128i k = _mm_add_epi32(m[g], _mm_loadu_si128(reinterpret_cast<const __m128i*>(kSha + 4 * g)));
+      s1 = _mm_sha256rnds2_epu32(s1, s0, k);
+      k = _mm_shuffle_epi32(k, 0x0E);
+      s0 = _mm_sha256rnds2_epu32(s0, s1, k);
+    }
+    s0 = _mm_add_epi32(s0, save0);
+    s1 = _mm_add_epi32(s1, save1);
+  }
+  t = _mm_shuffle_epi32(s0, 0x1B);    // a b e f
+  s1 = _mm_shuffle_epi32(s1, 0xB1);   // g h c d
+  s0 = _mm_blend_epi16(t, s1, 0xF0);  // a b c d
+  s1 = _mm_alignr_epi8(s1, t, 8);     // e f g h
+  _mm_storeu_si128(reinterpret_cast<__m128i*>(st), s0);
+  _mm_storeu_si128(reinterpret_cast<__m128i*>(st + 4), s1);
+}
+
+static bool cpu_has_sha() {
+  static const bool has = [] {
+    unsigned a, b, c, d;
+    if (!__get_cpuid_count(7, 0, &a, &b, &c, &d)) return false;
+    return ((b >> 29) & 1u) != 0;  // CPUID.(EAX=7, ECX=0):EBX.SHA
+  }();
+  return has;
+}
+#endif
+
+void Sha256::blocks(const uint8_t* p, size_t n) {
+#if defined(__x86_64__)
+  if (cpu_has_sha()) {
+    sha256_blocks_ni(st_, p, n);
+    return;
+  }
+#endif
+  for (; n; n--, p += 64) block(p);
+}
+
 void Sha256::update(const void* data, size_t len) {
   const uint8_t* p = static_cast<const uint8_t*>(data);
   len_ += len;
   while (len) {
     if (n_ == 0 && len >= 64) {
-      block(p);
-      p += 64;
-      len -= 64;
+      const size_t nb = len / 64;
+      blocks(p, nb);
+      p += 64 * nb;
+      len -= 64 * nb;
       continue;
     }
     const size_t k = std::min(len, 64 - n_);

@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstdlib>
 
+#include <thread>
+
 #include "host_common.h"
 
 using namespace det;
@@ -409,9 +411,19 @@ void free_model(det_model* m) {
 }
 
 det_status load_impl(const uint8_t* bytes, size_t len, det_model* m) {
-  Sha256 h;
-  h.update(bytes, len);
-  h.finish(m->sha);
+  // the file hash (the DTLZ header's model SHA-256) on a second thread, while
+  // this one parses, repacks and uploads; joined on every return path
+  struct Hasher {
+    std::thread t;
+    ~Hasher() {
+      if (t.joinable()) t.join();
+    }
+  } hasher;
+  hasher.t = std::thread([bytes, len, m] {
+    Sha256 h;
+    h.update(bytes, len);
+    h.finish(m->sha);
+  });
   Gguf g;
   if (g.parse(bytes, len)) return DET_ERR_GGUF;
   m->tok_status = m->tok.from_gguf(g);
