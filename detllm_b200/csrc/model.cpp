@@ -202,7 +202,9 @@ struct Loader {
       const size_t qb = q8 ? 512 : 256, rb = qb + 32, per_row = q8 ? 32 : 16;
       const size_t tiles = (rows + 15) / 16;
       std::vector<uint8_t> recs(tiles * nb * rb, 0);
-      for (size_t tl = 0; tl < tiles; tl++)
+      // tiles are independent: split them over host threads
+      auto repack = [&](size_t t0, size_t t1) {
+      for (size_t tl = t0; tl < t1; tl++)
         for (size_t b = 0; b < nb; b++) {
           uint8_t* r = &recs[(tl * nb + b) * rb];
           for (int lane = 0; lane < 32; lane++) {
@@ -226,6 +228,15 @@ struct Loader {
             std::memcpy(r + qb + 4 * g, &w, 4);
           }
         }
+      };
+      const size_t nt = std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), 16);
+      if (nt <= 1 || tiles < 64) {
+        repack(0, tiles);
+      } else {
+        std::vector<std::thread> pool;
+        for (size_t k = 0; k < nt; k++) pool.emplace_back(repack, tiles * k / nt, tiles * (k + 1) / nt);
+        for (auto& th : pool) th.join();
+      }
       if (det_status st = upload(recs.data(), recs.size(), &p)) return st;
       out->q = p;
       out->layout = LAYOUT_MMA16;
