@@ -75,13 +75,13 @@ DI int lm(int d) {
   return (d & 7) * (HD / 8) + (d >> 3);
 }
 
-// Shared-memory operands, both lane-major (element d of a row at lm(d)):
-//   Q: 32 pair-rows; pair-row P holds query-head rows (P & 15) + 32 (P >> 4)
-//      and that + 16 interleaved, element e at [2e] and [2e + 1];
-//   K: 64 key rows, every element stored twice ([2e] and [2e + 1]).
-// One 16-byte load of each then gives two elements for two rows x one key,
-// and the two rows' lane chains advance together: a packed multiply and a
-// packed fma(p, one, acc) (an exact add) per element pair.
+// Shared-memory operands: QK_ROWS query-head rows and QK_KEYS key rows of
+// HD + 4 floats (padded stride), each row lane-major (element d at lm(d)),
+// so the HD / 8 elements of one lane chain are contiguous.  A thread owns
+// the dots of rows mt + 16r and keys jt + 16c (r, c < 4) and runs their
+// eight lane chains one lane at a time: a 16-byte load of a row and of a key
+// gives four consecutive elements of the same chain, a packed multiply
+// forms two products at a time, and the chain adds them in order one by one.
 template <int HD>
 __global__ void __launch_bounds__(QK_THREADS, 3) attn_scores_kernel(const float* __restrict__ q,
                                                                  const float* __restrict__ kc, const int* pos0p,
