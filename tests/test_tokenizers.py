@@ -279,3 +279,83 @@ def test_synthetic_vocab_round_trip_and_oracle_agreement(impl, kind):
     assert got == [int(t) for t in want]
     assert impl.detok(g, got) == data
     assert len(got) < len(data)  # multi-byte pieces are used
+
+
+def _random_tokenizer(rng, kind):
+    """A random tokenizer GGUF over a small alphabet (so pieces overlap and
+    compete).  SentencePiece: canonical byte tokens (sometimes one missing),
+    random pieces, some with the space marker, scores with ties and
+    duplicates.  BPE: GPT-2 byte tokens and merges that join two existing
+    pieces (sometimes an invalid or duplicate merge).  Random token types.
+    Invalid vocabularies are allowed: both sides must then refuse them."""
+    def enc(bs):
+        return "".join(GPT2_BYTES[b] for b in bs)
+    alphabet = b"ab c\n"
+    if kind == "spm":
+        toks = S.byte_tokens()
+        if rng.random() < 0.15:
+            del toks[int(rng.integers(256))]
+        for _ in range(int(rng.integers(5, 60))):
+            n = int(rng.integers(2, 6))
+            p = "".join(chr(alphabet[int(rng.integers(len(alphabet)))]) for _ in range(n))
+            toks.append(SPACE + p[1:] if rng.random() < 0.3 else p)
+        kw = {"model": "llama" if rng.random() < 0.7 else None}
+        if kw["model"] is None or rng.random() < 0.8:
+            kw["scores"] = [float(rng.integers(-3, 3)) for _ in toks]
+    else:
+        toks = list(GPT2_BYTES)
+        known = [bytes([c]) for c in alphabet]
+        merges = []
+        for _ in range(int(rng.integers(5, 60))):
+            a = known[int(rng.integers(len(known)))]
+            b = known[int(rng.integers(len(known)))]
+            m = a + b
+            if m in known or len(m) > 8:
+                continue
+            known.append(m)
+            toks.append(enc(m))
+            merges.append(enc(a) + " " + enc(b))
+        if rng.random() < 0.1:
+            merges.append("a zz")  # a piece that is not a token
+        if rng.random() < 0.1 and merges:
+            merges.append(merges[0])  # duplicate merge
+        if rng.random() < 0.2:
+            rng.shuffle(merges)
+        kw = {"merges": merges, "model": "gpt2" if rng.random() < 0.5 else None}
+    if rng.random() < 0.3:
+        kw["token_type"] = [int(rng.choice([1, 1, 1, 6, 3])) for _ in toks]
+    return gguf(toks, **kw)
+
+
+@pytest.mark.parametrize("kind", ["spm", "bpe"])
+def test_random_tokenizers_product_matches_oracle(kind):
+    """Differential test: the library's tokenizer (C++) against the oracle's
+    (C) on random vocabularies and inputs: the same tokenizer kind or the
+    same refusal, the same tokens, codec symbols and bytes."""
+    import detllm_b200 as D
+    from oracle import oracle as O
+
+    O.build()
+    rng = np.random.default_rng(17 if kind == "spm" else 18)
+    for _ in range(60):
+        g = _random_tokenizer(rng, kind)
+        try:
+            want_kind = O.tokenizer_kind(g)
+        except O.OracleError:
+            with pytest.raises(D.DetError):
+                D.tokenizer_kind(g)
+            continue
+        assert D.tokenizer_kind(g) == want_kind
+        for _ in range(4):
+            n = int(rng.integers(0, 200))
+            data = bytes(rng.choice(list(b"ab c\n\xff\x00"), size=n).astype(np.uint8)) if n else b""
+            for codec in (False, True):
+                try:
+                    want = O.tokenize(g, data, codec=codec)
+                except O.OracleError:
+                    with pytest.raises(D.DetError):
+                        D.tokenize(g, data, codec=codec)
+                    continue
+                got = D.tokenize(g, data, codec=codec)
+                assert got.tolist() == want.tolist()
+                assert D.detokenize(g, got, byte_escapes=codec) == O.detokenize(g, want, escapes=codec)
