@@ -113,7 +113,8 @@ det_status det_device_count(int* count);
 /* ---- model: replaces F32Llama::from_gguf (det-model lib.rs:1035) --------- */
 /* Parses the GGUF bytes (det-gguf lib.rs:156), validates the model exactly as
  * the reference does, uploads the weights to `device` in the library's
- * layout and keeps the byte-fallback tokenizer and the SHA-256 of the file
+ * layout and keeps the GGUF's tokenizer (byte fallback, byte-level BPE or
+ * SentencePiece, as det_tokenizer_kind reports) and the SHA-256 of the file
  * (det-cli main.rs:933-1008).  The bytes are not retained. */
 det_status det_model_load(const uint8_t* gguf, size_t len, int device, det_model** out);
 void det_model_free(det_model* model);
