@@ -3,10 +3,11 @@
 // Mirrors F32Llama::from_gguf (crates/det-model/src/lib.rs:1035-1140),
 // LlamaConfig::from_gguf (:1498-1596) and the per-type tensor readers
 // (:1650-1953), including their error order, then repacks each weight matrix
-// into the device layout documented in internal.h.  The tokenizer follows
-// Tokenizer::from_gguf (crates/det-token/src/lib.rs:86-132) for the
-// byte-fallback vocabulary; byte-BPE and SentencePiece vocabularies are
-// reported as DET_ERR_TOKENIZER when compress/decompress need them.
+// into the device layout documented in internal.h.  The tokenizer
+// (byte fallback, byte-level BPE or SentencePiece) is read by
+// det::Tokenizer::from_gguf in tokenizer.cpp, following Tokenizer::from_gguf
+// (crates/det-token/src/lib.rs:86-132); its status is kept and reported
+// when compress/decompress need the tokenizer.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -409,7 +410,6 @@ det_status vocab_size(const Gguf& g, size_t* out) {
   return DET_ERR_MISSING_METADATA;
 }
 
-// canonical_byte_fallback_token (det-token lib.rs:841-848)
 void free_model(det_model* m) {
   if (!m) return;
   int cur;
