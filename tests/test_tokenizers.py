@@ -348,7 +348,9 @@ def test_random_tokenizers_product_matches_oracle(kind):
         assert D.tokenizer_kind(g) == want_kind
         for _ in range(4):
             n = int(rng.integers(0, 200))
-            data = bytes(rng.choice(list(b"ab c\n\xff\x00"), size=n).astype(np.uint8)) if n else b""
+            # the alphabet includes the UTF-8 bytes of the space marker U+2581,
+            # so literal marker bytes in the input meet the "▁" pieces
+            data = bytes(rng.choice(list(b"ab c\n\xff\x00\xe2\x96\x81"), size=n).astype(np.uint8)) if n else b""
             for codec in (False, True):
                 try:
                     want = O.tokenize(g, data, codec=codec)
