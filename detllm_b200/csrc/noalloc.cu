@@ -1,13 +1,17 @@
 // noalloc.cu -- det_symbol_ranges_noalloc: symbol ranges for logits that are
 // already in device memory, computed without allocating anything.
 //
-// Some callers cannot allocate device memory inside a call: code that runs
-// while a CUDA graph is being captured, a host engine that owns a fixed
-// memory budget and forbids allocation after start-up, or a runtime whose
-// allocator is not cudaMalloc.  For them this entry point keeps its working
+// Some callers cannot allocate device memory inside a call: a host engine
+// that owns a fixed memory budget and forbids allocation after start-up, or
+// a runtime whose allocator is not cudaMalloc and that must account for
+// every byte it hands out.  For them this entry point keeps its working
 // memory (the exp values, the per-row normalisers, row ids and an error
 // word) in one file-scope device array of fixed size.  Every GPU that loads
 // this library holds the array until the process exits.
+//
+// Each call ends by copying the error word to the host and synchronising
+// `stream`, so it returns only after its kernels have finished, on the
+// error paths too.
 //
 // The array is shared by every call on a device and keeps what the last call
 // left there: the error word is cleared at the start of each call and the
@@ -91,16 +95,22 @@ extern "C" det_status det_symbol_ranges_noalloc(const float* logits, uint32_t n,
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const Launch L{s, err, nullptr};
   if (cudaMemsetAsync(err, 0, sizeof(uint32_t), s) != cudaSuccess) return DET_ERR_CUDA;
+  // once work is enqueued, a failure still waits for the stream, so that no
+  // kernel of this call writes the array or `out` after the status returns
+  auto fail = [s]() {
+    cudaStreamSynchronize(s);
+    return DET_ERR_CUDA;
+  };
   noalloc_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(symbols, (int)n, vocab + tail, rows, err);
-  if (cudaGetLastError() != cudaSuccess) return DET_ERR_CUDA;
-  if (launch_cdf_prepare(L, logits, (int)vocab, rows, (int)n, e, z) != cudaSuccess) return DET_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return fail();
+  if (launch_cdf_prepare(L, logits, (int)vocab, rows, (int)n, e, z) != cudaSuccess) return fail();
   // (cum, freq, total) as three u64 per row is the det_symbol_range layout:
   // freq < 2^32 leaves the `reserved` word zero
   if (launch_cdf_ranges(L, e, z, (int)vocab, (int)tail, rows, symbols, (int)n, reinterpret_cast<uint64_t*>(out)) !=
       cudaSuccess)
-    return DET_ERR_CUDA;
+    return fail();
   uint32_t f = 0;
-  if (cudaMemcpyAsync(&f, err, sizeof(f), cudaMemcpyDeviceToHost, s) != cudaSuccess) return DET_ERR_CUDA;
+  if (cudaMemcpyAsync(&f, err, sizeof(f), cudaMemcpyDeviceToHost, s) != cudaSuccess) return fail();
   if (cudaStreamSynchronize(s) != cudaSuccess) return DET_ERR_CUDA;
   if (f & ERRF_SYMBOL) return DET_ERR_CDF_SYMBOL_OUT_OF_RANGE;
   if (f & ERRF_CDF_NONFINITE) return DET_ERR_CDF_NONFINITE_LOGIT;

@@ -253,17 +253,19 @@ det_status det_set_profiling(int enable);
 det_status det_model_profile(det_model* model, char* out, size_t cap, int reset);
 
 /* ---- symbol ranges without allocation (no counterpart in the reference) --
- * For callers that cannot allocate device memory inside a call: code running
- * while a CUDA graph is captured, engines that fix their memory budget at
- * start-up, runtimes whose allocator is not cudaMalloc.  Same result as
- * det_symbol_ranges with rows == NULL, but every buffer is the caller's
- * device memory: logits (n x vocab f32, row-major), symbols (n u32) and out
- * (n det_symbol_range).  Runs on the calling thread's current device, on
- * `stream` (a cudaStream_t; NULL = the legacy default stream), and waits for
- * that stream before it returns the status.
+ * For callers that cannot allocate device memory inside a call: engines that
+ * fix their memory budget at start-up, runtimes whose allocator is not
+ * cudaMalloc.  Same result as det_symbol_ranges with rows == NULL, but every
+ * buffer is the caller's device memory: logits (n x vocab f32, row-major),
+ * symbols (n u32) and out (n det_symbol_range).  Runs on the calling
+ * thread's current device, on `stream` (a cudaStream_t; NULL = the legacy
+ * default stream).  Every call ends by copying its error word to the host
+ * and synchronising `stream`, on the error paths too, so it returns only
+ * after its kernels have finished.
  * Working memory is one fixed array in device memory that every GPU loading
  * this library holds until exit: DET_NOALLOC_MAX_FLOATS floats of exp values
- * plus per-row words, about 8 MiB.  Requests with n > DET_NOALLOC_MAX_ROWS or
+ * plus 2 * DET_NOALLOC_MAX_ROWS + 64 words, about 8 MiB.  Requests with
+ * n > DET_NOALLOC_MAX_ROWS or
  * n * vocab > DET_NOALLOC_MAX_FLOATS return DET_ERR_SCRATCH_LIMIT.  The first
  * call on a device looks up the array's device address; make that first call
  * before any stream capture.  All calls on a device share the array: calls

@@ -62,4 +62,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_goldens.py <path of the detllm reference checkout>")
+    main(sys.argv[1])

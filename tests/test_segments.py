@@ -6,6 +6,7 @@ model replica, whose output does not depend on the rank."""
 import hashlib
 import os
 import socket
+import time
 
 import pytest
 import torch.multiprocessing as mp
@@ -83,3 +84,87 @@ def test_two_rank_gather_matches_one_rank():
     assert res[0][0] == want  # rank 0 holds every file, in segment order
     assert res[1][0] is None
     assert res[0][1] == res[1][1] == 2.0  # the slowest rank's time
+
+
+def _failing_stand_in(seg: bytes) -> bytes:
+    if seg[:1] == b"\xff":
+        raise ValueError("corrupt segment")
+    return _stand_in(seg)
+
+
+def _failing_worker(rank, ws, port, data, n, q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        segs = G.split_stream(data, n)
+        local = G.run_local(segs, rank, ws, _failing_stand_in)
+        try:
+            G.gather(local, n, ws)
+            q.put((rank, None))
+        except G.SegmentError as e:
+            q.put((rank, e.failures))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_failing_segment_is_reported_on_every_rank():
+    """A segment whose compress raises on rank 1 is reported by gather on
+    both ranks (segment index, rank and error text), after the same
+    collective steps, instead of leaving rank 0 blocked in the gather."""
+    n = 4
+    segs = [b"a" * 10, b"\xff" * 10, b"c" * 10, b"d" * 10]  # segment 1 -> rank 1 of 2
+    data = b"".join(segs)
+    with pytest.raises(G.SegmentError) as e:
+        G.gather(G.run_local(segs, 0, 1, _failing_stand_in), n, 1)
+    assert e.value.failures == [(1, 0, "ValueError: corrupt segment")]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, data, n, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=100) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    assert res[0] == res[1] == [(1, 1, "ValueError: corrupt segment")]
+
+
+def _leaving_worker(rank, ws, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # leaves between steps, without joining the gather
+    t = time.time()
+    try:
+        G.gather({0: b"x"}, 2, ws)
+        q.put(("returned", time.time() - t))
+    except Exception as e:  # the missing peer surfaces as an error on rank 0
+        q.put((type(e).__name__, time.time() - t))
+    os._exit(0)
+
+
+@pytest.mark.timeout(120)
+def test_rank_that_leaves_ends_the_gather_with_an_error():
+    """A rank that exits without joining the gather: rank 0's gather ends
+    with an error within the process group's short timeout, not a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    what, waited = q.get(timeout=100)
+    for p in procs:
+        p.join(timeout=30)
+    assert what != "returned"
+    assert waited < 60
