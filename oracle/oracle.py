@@ -67,6 +67,7 @@ def lib():
             "ref_quant_kernel_hash": (I, [P]),
             "ref_fixture_gguf": (SZ, [I, P, SZ]),
             "ref_set_threads": (None, [I]),
+            "ref_set_rowwise_gemv": (None, [I]),
             "ref_model_load": (I, [P, SZ, C.POINTER(P)]),
             "ref_model_free": (None, [P]),
             "ref_model_get_info": (I, [P, C.POINTER(ModelInfo)]),
@@ -114,6 +115,12 @@ def _check(code: int, what: str):
 
 def set_threads(n: int) -> None:
     lib().ref_set_threads(int(n))
+
+
+def set_rowwise_gemv(on: bool) -> None:
+    """True: every GEMV row goes through the one-row K-quant dot functions
+    (ref_dot_q4_k_q8a / ref_dot_q6_k_q8k) instead of the row-group ones."""
+    lib().ref_set_rowwise_gemv(int(bool(on)))
 
 
 def sha256(data: bytes) -> bytes:

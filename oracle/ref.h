@@ -101,6 +101,14 @@ float ref_dot_q8_0_q8a_block(const ref_q8a_block* w, const ref_q8a_block* a);
 float ref_dot_q4_0_q8a_block(const ref_q4_0_block* w, const ref_q8a_block* a);
 int ref_dot_q8_0_q8a(const ref_q8a_block* w, const ref_q8a_block* a, size_t nb, float* out);
 int ref_dot_q4_0_q8a(const ref_q4_0_block* w, const ref_q8a_block* a, size_t nb, float* out);
+/* the same per-row results as ref_dot_q4_k_q8a / ref_dot_q6_k_q8k for n <=
+ * REF_ROW_GROUP consecutive rows (ref_quant.c explains the equivalence) */
+#define REF_ROW_GROUP 32
+void ref_q8a_dequant(const ref_q8a_block* a, size_t nblocks, float* act);
+int ref_dot_q4_k_rows(const ref_q4k_block* w, size_t nb, size_t n, const float* act, float* out);
+int ref_dot_q6_k_rows(const ref_q6k_block* w, size_t nb, size_t n, const ref_q8k_block* a, float* out);
+/* 1: the GEMV takes the one-row functions for every row (tests compare the two) */
+void ref_set_rowwise_gemv(int on);
 int ref_dot_q4_k_q8a(const ref_q4k_block* w, const ref_q8a_block* a, size_t nb, float* out);
 int ref_dot_q6_k_q8a(const ref_q6k_block* w, const ref_q8a_block* a, size_t nb, float* out);
 int ref_dot_q6_k_q8k(const ref_q6k_block* w, const ref_q8k_block* a, size_t nb, float* out);

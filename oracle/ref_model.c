@@ -176,13 +176,33 @@ typedef struct {
     const float* x;
     const ref_q8a_block* qa;
     const ref_q8k_block* qk;
+    const float* act; /* Q4_K: a.d * a.q per element (row-independent) */
     float* out;
     volatile int err;
 } gemv_ctx;
 
+static int g_rowwise = 0;
+void ref_set_rowwise_gemv(int on) { g_rowwise = on; }
+
 static void gemv_range(void* p, size_t b, size_t e) {
     gemv_ctx* c = (gemv_ctx*)p;
     const ref_matrix* m = c->m;
+    if (!g_rowwise && (m->type == GT_Q4_K || m->type == GT_Q6_K)) {
+        /* REF_ROW_GROUP rows at a time, same per-row results (ref_quant.c) */
+        for (size_t r = b; r < e && !c->err; r += REF_ROW_GROUP) {
+            size_t n = e - r < REF_ROW_GROUP ? e - r : REF_ROW_GROUP;
+            int st = m->type == GT_Q4_K
+                         ? ref_dot_q4_k_rows((const ref_q4k_block*)m->data + r * m->blocks_per_row,
+                                             m->blocks_per_row, n, c->act, c->out + r)
+                         : ref_dot_q6_k_rows((const ref_q6k_block*)m->data + r * m->blocks_per_row,
+                                             m->blocks_per_row, n, c->qk, c->out + r);
+            if (st != REF_OK) {
+                c->err = st;
+                return;
+            }
+        }
+        return;
+    }
     for (size_t r = b; r < e && !c->err; r++) {
         float v = 0.0f;
         int st = REF_OK;
@@ -222,7 +242,8 @@ static int needs_q8a(const ref_matrix* m) {
 static int gemv(const ref_matrix* m, const float* x, const ref_q8a_block* shared_qa, ref_q8a_block* qa_scratch,
                 ref_q8k_block* qk_scratch, float* out) {
     if (!finite_slice(x, m->cols)) return REF_ERR_NONFINITE;
-    gemv_ctx c = {m, x, NULL, NULL, out, 0};
+    gemv_ctx c = {m, x, NULL, NULL, NULL, out, 0};
+    float* act = NULL;
     if (needs_q8a(m)) {
         if (shared_qa) {
             c.qa = shared_qa;
@@ -231,12 +252,19 @@ static int gemv(const ref_matrix* m, const float* x, const ref_q8a_block* shared
             if (st) return st;
             c.qa = qa_scratch;
         }
+        if (m->type == GT_Q4_K && !g_rowwise) {
+            act = (float*)malloc(m->cols * sizeof(float));
+            if (!act) return REF_ERR_SHAPE;
+            ref_q8a_dequant(c.qa, m->cols / 32, act);
+            c.act = act;
+        }
     } else if (m->type == GT_Q6_K) {
         int st = ref_quantize_q8k(x, m->cols, qk_scratch);
         if (st) return st;
         c.qk = qk_scratch;
     }
     ref_parallel_for(m->rows, gemv_range, &c);
+    free(act);
     return c.err;
 }
 

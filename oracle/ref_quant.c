@@ -313,6 +313,99 @@ int ref_dot_q6_k_q8k(const ref_q6k_block* w, const ref_q8k_block* a, size_t nb, 
     return REF_OK;
 }
 
+/* ---- row groups: the same per-row arithmetic, several rows side by side --
+ * These compute exactly what ref_dot_q4_k_q8a / ref_dot_q6_k_q8k compute for
+ * each row (same operations on the same values, in the same order within a
+ * row); they only hoist row-independent values out of the element loop and
+ * interleave up to REF_ROW_GROUP rows so the compiler can run their
+ * independent chains in vector lanes.  A non-finite product or partial sum
+ * makes the row's final sum non-finite (inf and NaN absorb later finite
+ * adds), so testing the final sum reports the same NonFinite error. */
+
+/* act[k] = a.d * (float)a.q[k] for the nb * 256 elements of a Q8A vector:
+ * the reference's per-element `act`, which does not depend on the row */
+void ref_q8a_dequant(const ref_q8a_block* a, size_t nblocks, float* act) {
+    for (size_t b = 0; b < nblocks; b++)
+        for (int i = 0; i < 32; i++) act[b * 32 + i] = a[b].d * (float)a[b].q[i];
+}
+
+/* det-quant lib.rs:281-315 for rows w[0..n) (row stride nb blocks) */
+int ref_dot_q4_k_rows(const ref_q4k_block* w, size_t nb, size_t n, const float* act, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    float sum[REF_ROW_GROUP] = {0};
+    float wt[256][REF_ROW_GROUP];
+    for (size_t b = 0; b < nb; b++) {
+        for (size_t r = 0; r < REF_ROW_GROUP; r++) {
+            if (r >= n) {
+                for (int i = 0; i < 256; i++) wt[i][r] = 0.0f;
+                continue;
+            }
+            const ref_q4k_block* blk = &w[r * nb + b];
+            if (!isfinite_f(blk->d) || !isfinite_f(blk->dmin)) return REF_ERR_NONFINITE;
+            for (int sub = 0; sub < 8; sub++) {
+                uint8_t sc, mn;
+                q4_k_scale_min(blk->scales, sub, &sc, &mn);
+                const float dsc = blk->d * (float)sc, dmn = blk->dmin * (float)mn;
+                for (int k = 0; k < 32; k++) {
+                    uint8_t byte = blk->qs[(sub / 2) * 32 + k];
+                    uint8_t q = (sub % 2 == 0) ? (byte & 0x0f) : (byte >> 4);
+                    wt[sub * 32 + k][r] = dsc * (float)q - dmn;
+                }
+            }
+        }
+        const float* ab = act + b * 256;
+        for (int i = 0; i < 256; i++)
+            for (size_t r = 0; r < REF_ROW_GROUP; r++) sum[r] += wt[i][r] * ab[i];
+    }
+    for (size_t r = 0; r < n; r++) {
+        if (!isfinite_f(sum[r])) return REF_ERR_NONFINITE;
+        out[r] = sum[r];
+    }
+    return REF_OK;
+}
+
+/* det-quant lib.rs:353-397 for rows w[0..n) (row stride nb blocks) */
+int ref_dot_q6_k_rows(const ref_q6k_block* w, size_t nb, size_t n, const ref_q8k_block* a, float* out) {
+    if (nb == 0) return REF_ERR_SHAPE;
+    for (size_t r = 0; r < n; r++) {
+        float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (size_t b = 0; b < nb; b++) {
+            const ref_q6k_block* blk = &w[r * nb + b];
+            if (!isfinite_f(blk->d) || !isfinite_f(a[b].d)) return REF_ERR_NONFINITE;
+            /* q6_k_quant(blk, i) * scales[i / 16] (the scale of element i,
+             * q6_k_scale_index) for all 256 elements: the same bit fields,
+             * walked as (half, part, l) loops */
+            int32_t q6[256];
+            for (int half = 0; half < 2; half++)
+                for (int part = 0; part < 4; part++) {
+                    const uint8_t* qlp = blk->ql + half * 64 + (part & 1) * 32;
+                    const uint8_t* qhp = blk->qh + half * 32;
+                    const int nib = part < 2 ? 0 : 4, sh = 2 * part;
+                    for (int l16 = 0; l16 < 32; l16 += 16) {
+                        const int i0 = half * 128 + part * 32 + l16;
+                        const int32_t scale = blk->scales[i0 / 16];
+                        for (int l = l16; l < l16 + 16; l++) {
+                            const uint8_t ql = (uint8_t)((qlp[l] >> nib) & 0x0f);
+                            const uint8_t high = (uint8_t)(((qhp[l] >> sh) & 0x03) << 4);
+                            q6[i0 + l - l16] = ((int32_t)(ql | high) - 32) * scale;
+                        }
+                    }
+                }
+            int32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int off = 0; off < 256; off += 8)
+                for (int lane = 0; lane < 8; lane++) aux[lane] += (int32_t)a[b].q[off + lane] * q6[off + lane];
+            float d = blk->d * a[b].d;
+            if (!isfinite_f(d)) return REF_ERR_NONFINITE;
+            for (int lane = 0; lane < 8; lane++) sums[lane] += d * (float)aux[lane];
+        }
+        float sum = 0.0f;
+        for (int lane = 0; lane < 8; lane++) sum += sums[lane];
+        if (!isfinite_f(sum)) return REF_ERR_NONFINITE;
+        out[r] = sum;
+    }
+    return REF_OK;
+}
+
 /* ---- deterministic block generators: det-cli main.rs:273-388 ------------- */
 static ref_q8a_block gen_q8_block(uint32_t seed) {
     ref_q8a_block b;

@@ -263,3 +263,29 @@ def test_range_coder_million_symbols(oracle):
             pos += 1
             low = (low << 8) & M
             rng_ = (rng_ << 8) & M
+
+
+@pytest.mark.parametrize("threads", [1, 3])
+def test_kquant_row_groups_equal_row_by_row(oracle, threads):
+    """The oracle's row-group Q4_K / Q6_K GEMV (several rows side by side,
+    row-independent values hoisted) gives the same logits bit for bit as the
+    one-row functions that restate dot_q4_k_q8a / dot_q6_k_q8k
+    (det-quant lib.rs:281-315, :353-397); 1,000 output rows leave a ragged
+    last group, d_ff 768 three Q6_K blocks per down row."""
+    from detllm_b200 import synth as S
+
+    spec = S.ModelSpec(n_layer=2, d=512, d_ff=768, n_head=8, n_head_kv=2, vocab=1000, ctx=64,
+                       t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
+                       t_out=S.GT_Q6_K, seed=31)
+    g = S.build_gguf(spec)
+    toks = S.zipf_tokens(12, spec.vocab, seed=2)
+    oracle.set_threads(threads)
+    try:
+        m = oracle.Model(g)
+        fast = m.logits(toks)
+        oracle.set_rowwise_gemv(True)
+        slow = m.logits(toks)
+    finally:
+        oracle.set_rowwise_gemv(False)
+        oracle.set_threads(0)
+    assert (fast.view(np.uint32) == slow.view(np.uint32)).all()
