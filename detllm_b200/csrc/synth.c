@@ -388,3 +388,55 @@ size_t synth_gguf(const synth_spec* s, uint8_t* out, size_t cap, int threads) {
     free(ts);
     return total;
 }
+
+/* ---- synthetic order-2 Markov byte stream (benchmark input) ----------------
+ * n bytes over printable ASCII 0x20..0x7E plus '\n', each byte drawn from a
+ * seeded transition table indexed by the two previous bytes.  Row weights are
+ * u^12 for u uniform (a few likely successors per context, like text), and
+ * the markup bytes '<' and '>' get extra mass in every context.  Sampling is
+ * a binary search in the row's cumulative table, driven by splitmix64. */
+#define MK_K 96
+static uint8_t mk_sym(int i) { return i < 95 ? (uint8_t)(0x20 + i) : (uint8_t)'\n'; }
+
+size_t synth_markov(uint8_t* out, size_t n, uint64_t seed) {
+    uint32_t* cdf = (uint32_t*)malloc(sizeof(uint32_t) * MK_K * MK_K * MK_K);
+    if (!cdf) return 0;
+    const int lt = '<' - 0x20, gt = '>' - 0x20;
+    for (int ctx = 0; ctx < MK_K * MK_K; ctx++) {
+        double w[MK_K], tot = 0.0;
+        for (int c = 0; c < MK_K; c++) {
+            const double u = (double)(mix64(seed ^ ((uint64_t)ctx << 8) ^ (uint64_t)c) >> 11) * (1.0 / 9007199254740992.0);
+            const double u2 = u * u, u4 = u2 * u2;
+            w[c] = u4 * u4 * u4;
+            tot += w[c];
+        }
+        w[lt] += 2.0 * tot / MK_K;
+        w[gt] += 2.0 * tot / MK_K;
+        tot = 0.0;
+        for (int c = 0; c < MK_K; c++) tot += w[c];
+        double acc = 0.0;
+        for (int c = 0; c < MK_K; c++) {
+            acc += w[c];
+            double v = acc / tot * 4294967295.0;
+            cdf[(size_t)ctx * MK_K + c] = c == MK_K - 1 ? 0xffffffffu : (uint32_t)v;
+        }
+    }
+    int a = 0, b = 1;
+    uint64_t st = mix64(seed ^ 0x6d61726b6f76ull);
+    for (size_t i = 0; i < n; i++) {
+        st = mix64(st);
+        const uint32_t u = (uint32_t)(st >> 32);
+        const uint32_t* row = cdf + ((size_t)a * MK_K + b) * MK_K;
+        int lo = 0, hi = MK_K - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (row[mid] >= u) hi = mid;
+            else lo = mid + 1;
+        }
+        out[i] = mk_sym(lo);
+        a = b;
+        b = lo;
+    }
+    free(cdf);
+    return n;
+}

@@ -84,6 +84,8 @@ def _synth_lib():
         L = C.CDLL(_LIB)
         L.synth_gguf.restype = C.c_size_t
         L.synth_gguf.argtypes = [C.POINTER(_Spec), C.c_void_p, C.c_size_t, C.c_int]
+        L.synth_markov.restype = C.c_size_t
+        L.synth_markov.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]
         _lib = L
     return _lib
 
@@ -148,6 +150,17 @@ def markov_text(n: int, seed: int = 11) -> bytes:
         out[i] = alphabet[c]
         a, b = b, c
     return out.tobytes()
+
+
+def markov_stream(n: int, seed: int = 16) -> bytes:
+    """n bytes of seeded order-2 Markov text (printable ASCII, newline, extra
+    '<' / '>' markup mass) from libdetsynth.so: the benchmark's multi-MiB
+    input streams, generated in well under a second."""
+    buf = np.empty(max(n, 1), np.uint8)
+    got = _synth_lib().synth_markov(buf.ctypes.data, n, seed)
+    if got != n:
+        raise MemoryError("synth_markov failed")
+    return buf[:n].tobytes()
 
 
 # ---- GGUF metadata (tokenizer vocabularies) ---------------------------------
