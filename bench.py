@@ -1,34 +1,46 @@
 #!/usr/bin/env python3
 """Benchmark: encode tokens/s of the detllm token loop on B200.
 
-Workload: a TinyLlama-1.1B-shaped decoder with
-random-init Q8_0 weights (22 layers, d 2048, 32/4 heads, FFN 5632, vocab
-32000), 4096 Zipf(1.1) token ids encoded as codec symbols at n_ctx 2048
-(overlap 512, one window rollover), forward chunk 1024.  One step = one full
-compress of that stream: teacher-forced forward -> logits -> CDF ranges ->
-host range coder, through det_encode_symbols.
+Headline workload (the configuration it names for
+1/2/4/8 GPUs): a Llama-3-8B-shaped decoder with random-init Q4_K / Q6_K
+weights (32 layers, d 4096, 32/8 heads, head_dim 128, FFN 14336, vocab
+128256, RoPE theta 5e5), n_ctx 8192, over a seeded 16 MiB order-2 Markov
+byte stream cut into 8 independent segments (2 MiB each) that run
+segment-parallel: one model replica per GPU, segments dealt round-robin, no
+data-path collective.  The byte-fallback tokenizer makes one token per byte.
 
-* value: tokens of all ranks / max over ranks of the device time of the
-  timed steps (CUDA events on the session stream: forward + CDF kernels).
-* e2e: same tokens / max over ranks of the wall time of the C-ABI calls with
-  host buffers (symbols in, payload out; host<->device copies and host range
-  coding inside).
-* roofline: the decode GEMVs (one token per forward, after a 1024-token
-  prefix): one token's weight GEMV launches replayed back to back in a CUDA
-  graph (programmatic dependent launch), algorithmic bytes (weights +
+One step = every rank compresses one segment's first 8,192 bytes (one full
+n_ctx window: positions 0..8191, overlap n_ctx / 4) through det_compress:
+tokenize -> teacher-forced forward in 1,024-position chunks -> logits ->
+CDF ranges -> host range coder -> DTLZ file.  Rank r takes segment
+(step * N + r) mod 8, so per-GPU work per step is fixed (weak scaling) and
+the 8 segments are covered in turn.
+
+* value: bytes (= tokens) of all ranks / max over ranks of the device time
+  of the timed steps (CUDA events on the session stream around the forward
+  and CDF kernels).
+* e2e: the same tokens / max over ranks of the wall time of the det_compress
+  calls, with host bytes in and the DTLZ file out (tokenisation, the token
+  upload, the range download and host range coding inside).
+* full_stream: the whole 16 MiB stream extrapolated from the measured window
+  (every later window forwards the same 8,192 positions: 2,048 replayed,
+  6,144 coded), as the reference's bench-file estimate scales a prefix
+  (xtask/src/main.rs:2295-2325).
+* roofline: the headline model's decode weight GEMVs (one token per forward):
+  one token's weight GEMV launches back to back in a CUDA graph
+  (programmatic dependent launch), algorithmic bytes (weights + quantised
   activations + outputs) / CUDA-event time, against the measured HBM copy
-  bandwidth in MEASURED_PEAKS.json.  decode.gemv_gbs_in_forward is the same
-  ratio for the launches inside real forwards, each bracketed by events.
-  With DETGPU_FUSED_DECODE=1 the one-position forward is one persistent
-  kernel (decode_fused_kernel) and the roofline is that launch: all weight
-  bytes of one token + the KV rows its attention reads, / its event time.
-  The chunked encode GEMM is FP32-pipe bound (its exact ordered fold) and
-  is reported separately under chunk_gemm with the per-kernel time shares.
+  bandwidth in MEASURED_PEAKS.json.
+* roofline_encode: the encode step's dominant kernel (the Q4_K chunk GEMM),
+  against the FP32 pipe it is bound by (the reference's one ordered f32
+  chain per row: 2 rounded ops per weight per position).
+* configs: BASELINE configs 2-4 at N = 1 (TinyLlama Q8_0 at chunk 1024 and at
+  the configuration's literal chunk 64; TinyLlama Q4_K_M compress and
+  decompress of Markov bytes; Qwen2.5-0.5B with V 151,936).
 * cpu_baseline / --impl reference: the C restatement of the reference CPU
-  path (oracle/, all host threads) on a bounded prefix of the same stream.
-
-Multi-GPU (torchrun, one rank per GPU): independent compression segments,
-one model replica per GPU, no data-path collective (weak scaling).
+  path (oracle/, all host threads) on a bounded prefix of the same segment;
+  the GPU's payload for that prefix is compared with the oracle's
+  (parity.payload_equal).
 """
 from __future__ import annotations
 
@@ -44,21 +56,18 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIG = "tinyllama-q8_0"
-N_TOKENS = 4096
-N_CTX = 2048
-OVERLAP = N_CTX // 4
-# --config: BASELINE.json configs 2-4 (tokens per rank, n_ctx)
-CONFIG_RUNS = {"tinyllama-q8_0": (4096, 2048), "tinyllama-q4_k_m": (4096, 2048),
-               "qwen2.5-0.5b-q8_0": (8192, 4096), "llama3-8b-q4_k": (4096, 8192)}
+HEADLINE = "llama3-8b-q4_k"
+STREAM_BYTES = 16 << 20
+N_SEGMENTS = 8
+PREFIX = 8192          # bytes (= tokens) of each segment per step: one n_ctx window
+HEAD_CTX = 8192
+STREAM_SEED = 16
 METRIC = "encode tokens/s (logits+CDF+code)"
-# DRAM bytes (read + write) per launch of one token's 89 weight GEMVs of the
-# headline config, from one ncu capture
+# DRAM bytes (read + write) per launch of one token's weight GEMVs of
+# TinyLlama Q8_0, from one ncu capture
 # (profiles/gemv_decode_stream_tinyllama_q8_0_1token_traffic.md)
-DECODE_GEMV_TRAFFIC_PER_LAUNCH = 12.400e6
-# DRAM bytes (read + write) per launch of the fused one-position kernel, per
-# config, from one ncu capture (profiles/decode_fused_tinyllama_q8_0_1token.md)
-DECODE_FUSED_TRAFFIC_PER_LAUNCH = {"tinyllama-q8_0": 1146.713e6 + 25.272e6}
+DECODE_GEMV_TRAFFIC_PER_LAUNCH = {"tinyllama-q8_0": 12.400e6}
+FP32_LANES_PER_SM = 128
 
 
 def log(*a):
@@ -96,12 +105,12 @@ def all_max(x, ws):
     return G.max_over_ranks(x, ws, device="cuda")
 
 
-def model_bytes(rank, ws):
-    """Build the seeded GGUF once per box (rank 0), shared through /tmp."""
+def model_bytes(config, rank=0, ws=1):
+    """The seeded GGUF of `config`, built once per box (rank 0) into /tmp."""
     from detllm_b200 import synth as S
 
-    spec = S.CONFIGS[CONFIG]
-    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{CONFIG}_s{spec.seed}.gguf")
+    spec = S.CONFIGS[config]
+    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{config}_s{spec.seed}.gguf")
     if rank == 0 and not os.path.exists(path):
         t = time.time()
         data = S.build_gguf(spec)
@@ -112,6 +121,14 @@ def model_bytes(rank, ws):
     barrier(ws)
     with open(path, "rb") as f:
         return spec, f.read()
+
+
+def segment_prefixes():
+    from detllm_b200 import segments as G
+    from detllm_b200 import synth as S
+
+    segs = G.split_stream(S.markov_stream(STREAM_BYTES, seed=STREAM_SEED), N_SEGMENTS)
+    return segs, [s[:PREFIX] for s in segs]
 
 
 class Clocks:
@@ -170,135 +187,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def oracle_sample(spec, gguf, tokens, budget_s=20.0):
-    """Time the CPU oracle on a bounded prefix (encode of the first S symbols)."""
-    from oracle import oracle as O
-
-    O.build()
-    t = time.time()
-    om = O.Model(gguf)
-    load_s = time.time() - t
-    t = time.time()
-    om.encode_symbols(tokens[:2], N_CTX, OVERLAP)
-    per_tok = max((time.time() - t) / 2, 1e-4)
-    s = int(max(4, min(len(tokens), budget_s / per_tok)))
-    t = time.time()
-    om.encode_symbols(tokens[:s], N_CTX, OVERLAP)
-    dt = time.time() - t
-    om.close()
-    return s, dt, load_s
-
-
-def decode_tokens_per_s(model, vocab, n_prefix=1024, n_steps=48):
-    """Single-token forwards after an n_prefix-token prefix (CUDA graphs):
-    device time per token (forward events on the session stream)."""
-    from detllm_b200 import synth as S
-
-    tokens = S.zipf_tokens(n_prefix + n_steps + 8, vocab, seed=11)
-    with model.session(n_ctx=N_CTX, max_chunk=512) as s:
-        for p in range(0, n_prefix, 512):
-            s.forward(tokens[p:p + 512], p)
-        pos = n_prefix
-        for _ in range(4):
-            s.forward(tokens[pos:pos + 1], pos)
-            pos += 1
-        s.stats(reset=True)
-        for _ in range(n_steps):
-            s.forward(tokens[pos:pos + 1], pos)
-            pos += 1
-        st = s.stats(reset=True)
-    return n_steps / (st.forward_ms / 1000.0), st.forward_ms / n_steps
-
-
-def run_tp(args):
-    """--tp G1,G2,...: row-sharded tensor parallelism in one process over
-    devices 0..G-1 (det_model_load_tp): single-stream decode tokens/s,
-    chunked encode tokens/s of the config's stream, and the logits hash of
-    the first 256 tokens, which must equal the 1-GPU hash.  One JSON line
-    per part count."""
+def decode_probe(model, vocab, n_ctx, n_prefix=1024, n_steps=48):
+    """Single-token forwards (the decode path) after an n_prefix-token
+    prefix: device time per token with CUDA graphs, then one profiled pass
+    that times every weight GEMV launch, then the same GEMV launches back to
+    back in one graph (det_session_gemv_stream)."""
     import detllm_b200 as D
-    from detllm_b200 import synth as S
-
-    spec, gguf = model_bytes(0, 1)
-    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7)
-    ndev = D.device_count()
-    ref_hash = None
-    for G in [int(x) for x in args.tp.split(",")]:
-        if G > ndev:
-            log(f"--tp {G}: only {ndev} devices, skipped")
-            continue
-        t = time.time()
-        model = D.Model(gguf, device=0) if G == 1 else D.Model(gguf, devices=list(range(G)))
-        load_s = time.time() - t
-        h = model.logits_hash_for_tokens_chunked(tokens[:256], 64).hex()
-        ref_hash = ref_hash or h
-        dec_tps, dec_ms = decode_tokens_per_s(model, spec.vocab)
-        for _ in range(args.warmup):
-            model.encode_symbols(tokens, N_CTX, OVERLAP)
-        model.stats(reset=True)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            model.encode_symbols(tokens, N_CTX, OVERLAP)
-        wall = time.perf_counter() - t0
-        st = model.stats(reset=True)
-        dev_s = (st.forward_ms + st.cdf_ms) / 1000.0
-        wb = S.weight_bytes_per_token(spec)
-        print(json.dumps({
-            "mode": "tensor-parallel", "config": CONFIG, "parts": G, "devices": list(range(G)),
-            "decode_tokens_per_s": dec_tps, "decode_ms_per_token": dec_ms,
-            "decode_weight_gbs_per_gpu": wb / G / (dec_ms / 1000.0) / 1e9,
-            "encode_tokens_per_s": N_TOKENS * args.steps / dev_s,
-            "encode_e2e_tokens_per_s": N_TOKENS * args.steps / wall,
-            "logits_hash_256": h, "hash_equals_1gpu": h == ref_hash, "load_s": round(load_s, 1),
-        }), flush=True)
-        model.close()
-
-
-TP_CONFIG = "llama3-8b-q4_k"  # the configuration BASELINE.json runs row-sharded
-
-
-def tp_probe(D, devices):
-    """Row-sharded tensor parallelism over `devices` from this one process
-    (run by rank 0 after the timed region while the other ranks wait), on the
-    Llama-3-8B-shaped Q4_K/Q6_K model BASELINE.json names for it:
-    single-stream decode tokens/s on one GPU and on all of `devices`, and
-    whether the logits hashes of 256 tokens are equal."""
-    from detllm_b200 import synth as S
-
-    spec = S.CONFIGS[TP_CONFIG]
-    try:
-        t = time.time()
-        gguf = S.build_gguf(spec)
-        build_s = time.time() - t
-        toks = S.zipf_tokens(256, spec.vocab, seed=5)
-        one = D.Model(gguf, device=devices[0])
-        h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
-        tps1, ms1 = decode_tokens_per_s(one, spec.vocab)
-        one.close()
-        t = time.time()
-        tp = D.Model(gguf, devices=devices)
-        load_s = time.time() - t
-        h_tp = tp.logits_hash_for_tokens_chunked(toks, 64).hex()
-        tps, ms = decode_tokens_per_s(tp, spec.vocab)
-        tp.close()
-    except Exception as e:  # reported, never fatal to the bench line
-        return {"config": TP_CONFIG, "parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
-    return {"config": TP_CONFIG, "parts": len(devices), "devices": devices, "decode_tokens_per_s": tps,
-            "decode_ms_per_token": ms, "decode_tokens_per_s_1gpu": tps1, "decode_ms_per_token_1gpu": ms1,
-            "speedup": tps / tps1, "logits_hash_equal": h_tp == h_one,
-            "weight_bytes_per_token": S.weight_bytes_per_token(spec), "load_s": round(load_s, 1),
-            "build_s": round(build_s, 1)}
-
-
-def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
-    """Single-token forwards (the decode path) after a 1024-token prefix:
-    device time per token with CUDA graphs, then one profiled pass that times
-    every weight GEMV launch (algorithmic bytes / event time)."""
     from detllm_b200 import synth as S
 
     tokens = S.zipf_tokens(n_prefix + 2 * n_steps + 8, vocab, seed=11)
     out = {}
-    with model.session(n_ctx=N_CTX, max_chunk=512) as s:
+    with model.session(n_ctx=n_ctx, max_chunk=512) as s:
         for p in range(0, n_prefix, 512):
             s.forward(tokens[p:p + 512], p)
         pos = n_prefix
@@ -319,61 +218,217 @@ def decode_probe(D, model, vocab, n_prefix=1024, n_steps=48):
         D.set_profiling(False)
         pr = s.stats(reset=True)
         gms, gbytes = s.gemv_stream(20)
-    # one GEMM-accounted launch per token: the fused one-position kernel ran
-    out["fused"] = int(pr.gemm_launches) == n_steps
-    out["gemv_launches"] = int(pr.gemm_launches)
+    out["fused"] = int(pr.gemm_launches) == n_steps  # one GEMM-accounted launch per token
+    out["gemv_launches_per_token"] = int(pr.gemm_launches) // n_steps
     out["gemv_ms_per_token"] = pr.gemm_ms / n_steps
-    out["gemv_bytes_per_launch"] = pr.gemm_bytes / max(pr.gemm_launches, 1)
-    out["gemv_ms_per_launch"] = pr.gemm_ms / max(pr.gemm_launches, 1)
     out["gemv_gbs_in_forward"] = pr.gemm_bytes / (pr.gemm_ms / 1000.0) / 1e9 if pr.gemm_ms > 0 else None
     out["positions"] = f"{n_prefix}..{pos - 1}"
-    # the same launches back to back (one graph, programmatic dependent launch)
     out["gemv_stream_ms_per_token"] = gms
     out["gemv_stream_bytes_per_token"] = gbytes
     out["gemv_stream_gbs"] = gbytes / (gms / 1000.0) / 1e9 if gms > 0 else None
     return out
 
 
-def roofline(dec, peak, peak_kind):
-    """The decode roofline object: the fused one-position kernel when it ran,
-    else the per-op weight GEMVs back to back (see the module docstring)."""
-    if dec.get("fused"):
-        gbs = dec["gemv_gbs_in_forward"]
-        return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                "frac": gbs / peak if gbs else None, "traffic": DECODE_FUSED_TRAFFIC_PER_LAUNCH.get(CONFIG),
-                "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
-                "kernel": f"decode_fused_kernel: one token's forward (all layers + lm_head) in one launch ({CONFIG})",
-                "peak_kind": peak_kind, "launches": 1, "ms_per_launch": dec["gemv_ms_per_launch"],
-                "bytes_per_launch": dec["gemv_bytes_per_launch"],
-                "bytes": "weights of every matrix + K and V rows read by the attention",
-                "per_op_gemv_stream_gbs": dec["gemv_stream_gbs"]}
-    n = max(dec["gemv_launches"] // 48, 1)
-    return {"bound": "hbm", "achieved": dec["gemv_stream_gbs"], "peak": peak, "unit": "GB/s",
-            "frac": dec["gemv_stream_gbs"] / peak if dec["gemv_stream_gbs"] else None,
-            "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH if CONFIG == "tinyllama-q8_0" else None,
+def decode_roofline(dec, config, peak, peak_kind):
+    n = max(dec["gemv_launches_per_token"], 1)
+    gbs = dec["gemv_stream_gbs"]
+    return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak if gbs else None,
+            "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH.get(config),
             "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
-            "kernel": f"decode weight GEMVs, one token's {n} launches back to back ({CONFIG})",
+            "kernel": f"decode weight GEMVs, one token's {n} launches back to back ({config})",
             "peak_kind": peak_kind, "launches": n, "ms_per_launch": dec["gemv_stream_ms_per_token"] / n,
             "bytes_per_launch": dec["gemv_stream_bytes_per_token"] / n, "in_forward_gbs": dec["gemv_gbs_in_forward"]}
 
 
-def run_reference(args):
-    rank, ws, local = dist_init(args.gpus)
-    if rank != 0:
-        return
+def encode_roofline(kprof, ops, sm_mhz, n_sms):
+    """The Q4_K chunk GEMMs (q|k|v, o, gate|up of the headline model) against
+    the FP32 pipe: 2 rounded ops per weight per position (the reference's
+    product and chain add), over their kernel time in one profiled step."""
+    groups = ("gemm_qkv", "gemm_o", "gemm_gate_up")
+    n = sum(kprof.get(g, (0, 0.0))[0] for g in groups)
+    ms = sum(kprof.get(g, (0, 0.0))[1] for g in groups)
+    if not n or not sm_mhz or ms <= 0:
+        return None
+    peak = n_sms * FP32_LANES_PER_SM * sm_mhz * 1e6 / 1e12
+    achieved = ops / (ms / 1000.0) / 1e12
+    return {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "T lane-ops/s", "frac": achieved / peak,
+            "traffic": None, "kernel": "gemm_q4k_kernel (Q4_K x Q8A chunk GEMMs: q|k|v, o, gate|up of one step)",
+            "peak_kind": f"nominal: {n_sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x measured {sm_mhz:.0f} MHz",
+            "launches": n, "ms": ms, "ops": ops}
+
+
+def q4k_weight_positions(spec, positions):
+    """Q4_K weight x position products of one step's chunk GEMMs (the
+    lm_head of the last window position is skipped by the codec, which this
+    count ignores)."""
     from detllm_b200 import synth as S
 
-    spec, gguf = model_bytes(0, 1)
-    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7)
+    hd = spec.head_dim
+    per_tok = 0
+    if spec.t_attn == S.GT_Q4_K:
+        per_tok += spec.d * (spec.n_head * hd * 2 + spec.n_head_kv * hd * 2)
+    if spec.t_gate_up == S.GT_Q4_K:
+        per_tok += 2 * spec.d_ff * spec.d
+    return per_tok * spec.n_layer * positions
+
+
+def full_stream_estimate(seg_len, n_ctx, t_window, ws):
+    """Windows of one segment: the first codes n_ctx symbols, every later one
+    replays n_ctx / 4 and codes the rest (det-cli next_window_start,
+    main.rs:772-778) and forwards the same n_ctx positions."""
+    adv = n_ctx - n_ctx // 4
+    windows = 1 + max(0, -(-(seg_len - n_ctx) // adv))
+    segs_per_rank = -(-N_SEGMENTS // ws)
+    est = segs_per_rank * windows * t_window
+    return {"bytes": STREAM_BYTES, "segments": N_SEGMENTS, "windows_per_segment": windows,
+            "est_s": est, "est_tokens_per_s": STREAM_BYTES / est,
+            "method": "measured one-window step time x windows per segment x segments per GPU"}
+
+
+def oracle_prefix(gguf, prefix_bytes, n_ctx, budget_s=20.0):
+    """The CPU oracle on a bounded prefix: (symbols, payload, seconds)."""
     from oracle import oracle as O
 
     O.build()
     om = O.Model(gguf)
-    per = []
+    syms = O.tokenize(gguf, prefix_bytes, codec=True)
+    t = time.time()
+    om.encode_symbols(syms[:2], n_ctx, n_ctx // 4)
+    per = max((time.time() - t) / 2, 1e-4)
+    s = int(max(4, min(len(syms), budget_s / per)))
+    t = time.time()
+    payload = om.encode_symbols(syms[:s], n_ctx, n_ctx // 4)
+    dt = time.time() - t
+    om.close()
+    return syms[:s], payload, dt
+
+
+def timed(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    t = time.perf_counter()
+    for _ in range(steps):
+        out = fn()
+    return time.perf_counter() - t, out
+
+
+def sub_configs(D, S, peak, peak_kind):
+    """BASELINE configs 2-4 on this GPU (N = 1): each model built, loaded,
+    measured and freed in turn."""
+    out = {}
+    # config 2: TinyLlama-1.1B Q8_0, 4,096 Zipf tokens, n_ctx 2048
+    spec, g = model_bytes("tinyllama-q8_0")
+    m = D.Model(g)
+    toks = S.zipf_tokens(4096, spec.vocab, seed=7)
+    r = {"workload": "tinyllama-q8_0 encode of 4,096 Zipf(1.1) tokens, n_ctx 2048, overlap 512"}
+    for chunk in (1024, 64):
+        D.set_encode_chunk(chunk)
+        m.stats(reset=True)
+        wall, _ = timed(lambda: m.encode_symbols(toks, 2048, 512), 3, 1)
+        st = m.stats(reset=True)
+        r[f"chunk{chunk}"] = {"tokens_per_s": 3 * 4096 / ((st.forward_ms + st.cdf_ms) / 1000.0),
+                              "e2e_tokens_per_s": 3 * 4096 / wall}
+    D.set_encode_chunk(0)
+    dec = decode_probe(m, spec.vocab, 2048)
+    r["decode"] = dec
+    r["roofline"] = decode_roofline(dec, "tinyllama-q8_0", peak, peak_kind)
+    m.close()
+    out["tinyllama-q8_0"] = r
+    # config 3: TinyLlama Q4_K_M, compress and decompress of Markov bytes
+    spec, g = model_bytes("tinyllama-q4_k_m")
+    m = D.Model(g)
+    data = S.markov_stream(16384, seed=3)
+    m.stats(reset=True)
+    wall_c, f = timed(lambda: D.compress(m, data, 2048), 2, 1)
+    st = m.stats(reset=True)
+    enc_tps = 2 * len(data) / ((st.forward_ms + st.cdf_ms) / 1000.0)
+    small = D.compress(m, data[:1024], 2048)
+    t = time.perf_counter()
+    back = D.decompress(m, small)
+    wall_d = time.perf_counter() - t
+    assert back == data[:1024], "config 3 round trip failed"
+    dec_tps = 1024 / wall_d
+    out["tinyllama-q4_k_m"] = {
+        "workload": "tinyllama-q4_k_m: compress of 16 KiB of order-2 Markov bytes (byte-fallback tokens), "
+                    "decompress of a 1 KiB prefix, n_ctx 2048",
+        "compress_tokens_per_s": enc_tps, "compress_e2e_tokens_per_s": 2 * len(data) / wall_c,
+        "decompress_e2e_tokens_per_s": dec_tps, "round_trip_ok": True,
+        "est_1mib_round_trip_s": (1 << 20) / enc_tps + (1 << 20) / dec_tps,
+        "decode": decode_probe(m, spec.vocab, 2048)}
+    m.close()
+    # config 4: Qwen2.5-0.5B Q8_0, V 151,936, 8,192 Zipf tokens at n_ctx 4096
+    spec, g = model_bytes("qwen2.5-0.5b-q8_0")
+    m = D.Model(g)
+    toks = S.zipf_tokens(8192, spec.vocab, seed=7)
+    m.stats(reset=True)
+    wall, _ = timed(lambda: m.encode_symbols(toks, 4096, 1024), 3, 1)
+    st = m.stats(reset=True)
+    out["qwen2.5-0.5b-q8_0"] = {"workload": "qwen2.5-0.5b-q8_0 encode of 8,192 Zipf(1.1) tokens, n_ctx 4096",
+                                "tokens_per_s": 3 * 8192 / ((st.forward_ms + st.cdf_ms) / 1000.0),
+                                "e2e_tokens_per_s": 3 * 8192 / wall,
+                                "decode": decode_probe(m, spec.vocab, 4096)}
+    m.close()
+    return out
+
+
+TP_CONFIG = HEADLINE  # the configuration BASELINE.json runs row-sharded
+
+
+def tp_probe(D, gguf, spec, devices):
+    """Row-sharded tensor parallelism over `devices` from this one process
+    (rank 0, after the timed region, while the other ranks wait): single-
+    stream decode tokens/s on one GPU and on all of `devices`, and whether
+    the logits hashes of 256 tokens are equal."""
+    from detllm_b200 import synth as S
+
+    try:
+        toks = S.zipf_tokens(256, spec.vocab, seed=5)
+        one = D.Model(gguf, device=devices[0])
+        h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
+        d1 = decode_probe(one, spec.vocab, HEAD_CTX)
+        one.close()
+        t = time.time()
+        tp = D.Model(gguf, devices=devices)
+        load_s = time.time() - t
+        h_tp = tp.logits_hash_for_tokens_chunked(toks, 64).hex()
+        with tp.session(n_ctx=HEAD_CTX, max_chunk=512) as s:
+            tk = S.zipf_tokens(1024 + 60, spec.vocab, seed=11)
+            for p in range(0, 1024, 512):
+                s.forward(tk[p:p + 512], p)
+            for p in range(1024, 1028):
+                s.forward(tk[p:p + 1], p)
+            s.stats(reset=True)
+            for p in range(1028, 1076):
+                s.forward(tk[p:p + 1], p)
+            st = s.stats(reset=True)
+        tps = 48 / (st.forward_ms / 1000.0)
+        tp.close()
+    except Exception as e:  # reported, never fatal to the bench line
+        return {"config": TP_CONFIG, "parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
+    return {"config": TP_CONFIG, "parts": len(devices), "devices": devices, "decode_tokens_per_s": tps,
+            "decode_tokens_per_s_1gpu": d1["tokens_per_s"], "speedup": tps / d1["tokens_per_s"],
+            "logits_hash_equal": h_tp == h_one, "load_s": round(load_s, 1)}
+
+
+def run_reference(args):
+    """The reference arm: the C restatement of the reference CPU path
+    (oracle/, all host threads) on the headline configuration, each step a
+    bounded prefix of segment 0 (rank 0 only)."""
+    rank, ws, local = dist_init(args.gpus)
+    if rank != 0:
+        return
+    spec, gguf = model_bytes(HEADLINE)
+    from oracle import oracle as O
+
+    O.build()
+    _, prefixes = segment_prefixes()
+    syms = O.tokenize(gguf, prefixes[0], codec=True)
+    om = O.Model(gguf)
     sample = args.ref_sample
+    per = []
     for i in range(args.warmup + args.steps):
         t = time.time()
-        om.encode_symbols(tokens[:sample], N_CTX, OVERLAP)
+        om.encode_symbols(syms[:sample], HEAD_CTX, HEAD_CTX // 4)
         if i >= args.warmup:
             per.append(time.time() - t)
     tps = sample * len(per) / sum(per)
@@ -381,57 +436,66 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(per) / len(per),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
-        "data": "synthetic (seeded random-init weights, Zipf tokens)",
-        "config": {"workload": f"{CONFIG} encode, first {sample} of {N_TOKENS} Zipf tokens per step, n_ctx {N_CTX}",
-                   "global_batch": sample, "seq_len": N_CTX, "parallelism": "cpu"},
+        "data": "synthetic (seeded random-init weights, order-2 Markov bytes)",
+        "config": {"workload": f"{HEADLINE} encode, first {sample} bytes of segment 0 of the 16 MiB stream per step, "
+                               f"n_ctx {HEAD_CTX}", "global_batch": sample, "seq_len": HEAD_CTX, "parallelism": "cpu"},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"first {sample} tokens of the {N_TOKENS}-token stream per step"},
+                         "sample": f"encode of the first {sample} byte tokens of segment 0 per step"},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def run(args):
-    import numpy as np
-
     rank, ws, local = dist_init(args.gpus)
     import detllm_b200 as D
     from detllm_b200 import synth as S
 
-    spec, gguf = model_bytes(rank, ws)
-    tokens = S.zipf_tokens(N_TOKENS, spec.vocab, seed=7 + rank)  # one segment per rank
+    spec, gguf = model_bytes(HEADLINE, rank, ws)
+    segs, prefixes = segment_prefixes()
     t = time.time()
     model = D.Model(gguf, device=local)
     log(f"rank {rank}: model on cuda:{local} in {time.time() - t:.1f}s")
     import torch
 
     torch.cuda.set_device(local)
+    step_i = [0]
+
+    def step():
+        seg = (step_i[0] * ws + rank) % N_SEGMENTS
+        step_i[0] += 1
+        return seg, D.compress(model, prefixes[seg], HEAD_CTX)
+
     for _ in range(args.warmup):
-        model.encode_symbols(tokens, N_CTX, OVERLAP)
+        step()
     model.stats(reset=True)
+    files = {}
     barrier(ws)
     torch.cuda.synchronize()
     with Clocks(local) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            payload = model.encode_symbols(tokens, N_CTX, OVERLAP)
+            seg, f = step()
+            files[seg] = f
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     barrier(ws)
     st = model.stats(reset=True)
     dev_s = (st.forward_ms + st.cdf_ms) / 1000.0
     dev_max, wall_max = all_max(dev_s, ws), all_max(wall, ws)
-    # one profiled step for the per-launch GEMV/GEMM roofline
+    clocks = clk.summary()
+    # one profiled step: per-kernel-group device time
     D.set_profiling(True)
     model.profile(reset=True)
-    model.encode_symbols(tokens, N_CTX, OVERLAP)
+    D.compress(model, prefixes[rank % N_SEGMENTS], HEAD_CTX)
     D.set_profiling(False)
-    prof = model.stats(reset=True)
+    model.stats(reset=True)
     kprof = model.profile(reset=True)
-    dec = decode_probe(D, model, spec.vocab)
-    # tensor parallelism over all the job's GPUs, from rank 0 alone; the
-    # other ranks wait on a CPU (gloo) group, since an NCCL barrier kernel
-    # spinning on their GPU would time-slice with rank 0's parts there
+    # decode path: a short round trip of this rank's first segment, then the
+    # one-token probe and the weight-GEMV stream
+    small = D.compress(model, prefixes[rank % N_SEGMENTS][:256], HEAD_CTX)
+    round_trip_ok = D.decompress(model, small) == prefixes[rank % N_SEGMENTS][:256]
+    dec = decode_probe(model, spec.vocab, HEAD_CTX)
     tpj = None
     if ws > 1:
         import datetime
@@ -441,73 +505,70 @@ def run(args):
         cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
         dist.barrier(group=cpu)
         if rank == 0:
-            tpj = tp_probe(D, list(range(ws)))
+            model.close()
+            tpj = tp_probe(D, gguf, spec, list(range(ws)))
         dist.barrier(group=cpu)
     if rank != 0:
+        model.close()
         return
-    total_tokens = N_TOKENS * args.steps * ws
+    total = PREFIX * args.steps * ws
     peak, peak_kind = peaks()
-    achieved = prof.gemm_bytes / (prof.gemm_ms / 1000.0) / 1e9 if prof.gemm_ms > 0 else None
+    props = torch.cuda.get_device_properties(local)
     line = {
-        "metric": METRIC, "value": total_tokens / dev_max, "unit": "tokens/s", "n_gpus": ws,
+        "metric": METRIC, "value": total / dev_max, "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+int8",
-        "data": "synthetic (seeded random-init weights, Zipf(1.1) tokens)",
-        "config": {"workload": f"{CONFIG} encode: {N_TOKENS} Zipf tokens per rank, n_ctx {N_CTX}, overlap {OVERLAP}, "
-                               f"chunk {os.environ.get('DETGPU_CHUNK', '1024')}", "global_batch": N_TOKENS * ws, "seq_len": N_CTX,
-                   "parallelism": f"segments{ws}",
-                   "l2": f"weights {S.weight_bytes_per_token(spec) / 1e9:.2f} GB streamed per chunk > 126 MB L2 (no flush)"},
-        "e2e": {"value": total_tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // args.steps,
-                "d2h_bytes_per_step": st.d2h_bytes // args.steps},
+        "data": "synthetic (seeded random-init weights, order-2 Markov byte stream)",
+        "config": {"workload": f"{HEADLINE} segment-parallel compress: 16 MiB Markov stream in {N_SEGMENTS} segments, "
+                               f"each step one segment's first {PREFIX} bytes per GPU (one n_ctx {HEAD_CTX} window, "
+                               f"overlap {HEAD_CTX // 4}), chunk 1024",
+                   "global_batch": PREFIX * ws, "seq_len": HEAD_CTX, "parallelism": f"segments{ws}",
+                   "l2": f"weights {S.weight_bytes_per_token(spec) / 1e9:.2f} GB streamed per chunk > 126 MB L2 "
+                         "(no flush)"},
+        "e2e": {"value": total / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // max(args.steps, 1),
+                "d2h_bytes_per_step": st.d2h_bytes // max(args.steps, 1)},
         "gpu_launches": int(st.launches),
-        "roofline": roofline(dec, peak, peak_kind),
+        "roofline": decode_roofline(dec, HEADLINE, peak, peak_kind),
+        "roofline_encode": encode_roofline(kprof, 2.0 * q4k_weight_positions(spec, PREFIX), clocks.get("sm_mhz"),
+                                           props.multi_processor_count),
+        "full_stream": full_stream_estimate(len(segs[0]), HEAD_CTX, dev_max / args.steps, ws),
         "decode": dec,
-        "chunk_gemm": {"bound": "fp32 pipe (exact ordered fold, 4 fp32 ops per weight per position)",
-                       "weight_stream_gbs": achieved, "launches": int(prof.gemm_launches),
-                       "ms_per_launch": prof.gemm_ms / max(prof.gemm_launches, 1),
-                       "bytes_per_launch": prof.gemm_bytes / max(prof.gemm_launches, 1),
-                       "share_of_device_time": prof.gemm_ms / max(prof.forward_ms + prof.cdf_ms, 1e-9)},
-        "kernels": {k: {"launches": n, "ms": round(ms, 3), "share": round(ms / max(sum(v[1] for v in kprof.values()),
-                                                                                  1e-9), 4)}
+        "round_trip_ok": round_trip_ok,
+        "kernels": {k: {"launches": n, "ms": round(ms, 3),
+                        "share": round(ms / max(sum(v[1] for v in kprof.values()), 1e-9), 4)}
                     for k, (n, ms) in kprof.items() if n},
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "tensor_parallel": tpj,
-        "payload_bytes": len(payload),
+        "payload_bytes": {str(k): len(v) for k, v in sorted(files.items())},
         "weight_bytes_per_token": S.weight_bytes_per_token(spec),
     }
     if ws == 1 and not args.no_cpu_baseline:
-        s, dt, load_s = oracle_sample(spec, gguf, tokens)
-        line["cpu_baseline"] = {"value": s / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                                "sample": f"encode of the first {s} tokens of the stream (~{dt:.0f}s)"}
-    print(json.dumps(line), flush=True)
+        syms, want, dt = oracle_prefix(gguf, prefixes[0], HEAD_CTX)
+        got = model.encode_symbols(syms, HEAD_CTX, HEAD_CTX // 4)
+        line["cpu_baseline"] = {"value": len(syms) / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"encode of the first {len(syms)} byte tokens of segment 0 (~{dt:.0f}s)"}
+        line["parity"] = {"prefix_tokens": len(syms), "payload_equal": got == want, "payload_bytes": len(got)}
     model.close()
+    if ws == 1 and not args.no_configs:
+        line["configs"] = sub_configs(D, S, peak, peak_kind)
+    print(json.dumps(line), flush=True)
 
 
 def main():
-    global N_TOKENS, CONFIG, N_CTX, OVERLAP
+    global PREFIX
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--ref-sample", type=int, default=16, help="tokens per reference step")
+    ap.add_argument("--ref-sample", type=int, default=4, help="byte tokens per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default=CONFIG, choices=sorted(CONFIG_RUNS),
-                    help="model configuration (default: the headline BASELINE config)")
-    ap.add_argument("--tp", default=None,
-                    help="comma-separated part counts: row-sharded tensor parallelism in one process "
-                         "(single-stream decode / encode), instead of the segment-parallel bench")
-    ap.add_argument("--tokens", type=int, default=None,
-                    help="tokens per rank per step (default: the config's; smaller values are for profiling)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE configs 2-4 sub-benchmarks")
+    ap.add_argument("--prefix", type=int, default=PREFIX,
+                    help="bytes of each segment per step (default one n_ctx window; smaller is for profiling)")
     args = ap.parse_args()
-    CONFIG = args.config
-    N_TOKENS, N_CTX = CONFIG_RUNS[CONFIG]
-    OVERLAP = N_CTX // 4
-    if args.tokens:
-        N_TOKENS = args.tokens
-    if args.tp:
-        run_tp(args)
-    elif args.impl == "reference":
+    PREFIX = args.prefix
+    if args.impl == "reference":
         run_reference(args)
     else:
         run(args)

@@ -104,6 +104,7 @@ def lib():
             "det_device_expf": (I, [I, P, P, SZ]),
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
             "det_set_profiling": (I, [I]),
+            "det_set_encode_chunk": (I, [U32, C.POINTER(U32)]),
             "det_model_profile": (I, [P, C.c_char_p, SZ, I]),
             "det_session_gemv_stream": (I, [P, U32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
@@ -306,6 +307,14 @@ class Session:
         st = Stats()
         _check(lib().det_session_stats(self._h, C.byref(st), int(reset)), "det_session_stats")
         return st
+
+
+def set_encode_chunk(chunk: int) -> int:
+    """Positions per forward chunk of the codec (16..1024, 0 = default);
+    returns the previous value.  The output bytes do not depend on it."""
+    prev = C.c_uint32()
+    _check(lib().det_set_encode_chunk(int(chunk), C.byref(prev)), "det_set_encode_chunk")
+    return prev.value
 
 
 def set_profiling(enable: bool) -> None:

@@ -18,6 +18,8 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include <atomic>
+
 #include "host_common.h"
 
 using namespace det;
@@ -25,14 +27,22 @@ using namespace det;
 namespace {
 
 // Positions per forward launch sequence: larger chunks give the GEMMs and
-// attention more parallel work per weight pass.  DETGPU_CHUNK overrides the
-// default (16 .. 1024); the output bytes do not depend on it.
+// attention more parallel work per weight pass.  DETGPU_CHUNK, or
+// det_set_encode_chunk, overrides the default (16 .. 1024); the output bytes
+// do not depend on it.
+uint32_t env_chunk() {
+  const char* e = std::getenv("DETGPU_CHUNK");
+  const long v = e ? std::strtol(e, nullptr, 10) : 0;
+  return v >= 16 && v <= 1024 ? (uint32_t)v : 1024u;
+}
+std::atomic<uint32_t> g_chunk{0};  // 0: not read yet
 uint32_t encode_chunk() {
-  static const uint32_t c = [] {
-    const char* e = std::getenv("DETGPU_CHUNK");
-    const long v = e ? std::strtol(e, nullptr, 10) : 0;
-    return v >= 16 && v <= 1024 ? (uint32_t)v : 1024u;
-  }();
+  uint32_t c = g_chunk.load(std::memory_order_relaxed);
+  if (!c) {
+    uint32_t want = env_chunk(), zero = 0;
+    g_chunk.compare_exchange_strong(zero, want);
+    c = g_chunk.load(std::memory_order_relaxed);
+  }
   return c;
 }
 constexpr uint32_t kEscapes = 256;
@@ -183,6 +193,14 @@ uint64_t get_le(const uint8_t* p, int n) {
 }  // namespace
 
 extern "C" {
+
+det_status det_set_encode_chunk(uint32_t chunk, uint32_t* previous) {
+  if (chunk != 0 && (chunk < 16 || chunk > 1024)) return DET_ERR_INVALID_ARGUMENT;
+  const uint32_t prev = encode_chunk();
+  g_chunk.store(chunk ? chunk : env_chunk(), std::memory_order_relaxed);
+  if (previous) *previous = prev;
+  return DET_OK;
+}
 
 det_status det_encode_symbols(det_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx, uint32_t overlap,
                               int byte_escapes, uint8_t** out, size_t* out_len) {

@@ -244,6 +244,13 @@ det_status det_model_stats(det_model* model, det_stats* out, int reset);
  * (weights + quantised activations + outputs).  Overwrites the session's
  * logits: call det_forward again before det_symbol_ranges. */
 det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per_pass, double* bytes_per_pass);
+/* Positions per forward chunk of det_encode_symbols / det_compress /
+ * det_decompress's re-encode (16..1024; 0 restores the default, 1024 or
+ * DETGPU_CHUNK).  The output bytes do not depend on it; it trades launch
+ * count against parallel work per weight pass.  Process-wide; the previous
+ * value goes to *previous when non-NULL.  A tuning hook with no counterpart
+ * in the reference. */
+det_status det_set_encode_chunk(uint32_t chunk, uint32_t* previous);
 /* per-launch device timing of every kernel (adds two event records per
  * launch and turns CUDA graphs off while enabled) */
 det_status det_set_profiling(int enable);
