@@ -303,9 +303,13 @@ def oracle_prefix(gguf, prefix_bytes, n_ctx, budget_s=20.0):
     return syms[:s], payload, dt
 
 
-def timed(fn, steps, warmup):
+def timed(fn, steps, warmup, model=None):
+    """Wall time of `steps` calls after `warmup` untimed ones; the model's
+    device-time counters are reset after the warm-up."""
     for _ in range(warmup):
         fn()
+    if model is not None:
+        model.stats(reset=True)
     t = time.perf_counter()
     for _ in range(steps):
         out = fn()
@@ -323,8 +327,7 @@ def sub_configs(D, S, peak, peak_kind):
     r = {"workload": "tinyllama-q8_0 encode of 4,096 Zipf(1.1) tokens, n_ctx 2048, overlap 512"}
     for chunk in (1024, 64):
         D.set_encode_chunk(chunk)
-        m.stats(reset=True)
-        wall, _ = timed(lambda: m.encode_symbols(toks, 2048, 512), 3, 1)
+        wall, _ = timed(lambda: m.encode_symbols(toks, 2048, 512), 3, 1, m)
         st = m.stats(reset=True)
         r[f"chunk{chunk}"] = {"tokens_per_s": 3 * 4096 / ((st.forward_ms + st.cdf_ms) / 1000.0),
                               "e2e_tokens_per_s": 3 * 4096 / wall}
@@ -338,8 +341,7 @@ def sub_configs(D, S, peak, peak_kind):
     spec, g = model_bytes("tinyllama-q4_k_m")
     m = D.Model(g)
     data = S.markov_stream(16384, seed=3)
-    m.stats(reset=True)
-    wall_c, f = timed(lambda: D.compress(m, data, 2048), 2, 1)
+    wall_c, f = timed(lambda: D.compress(m, data, 2048), 2, 1, m)
     st = m.stats(reset=True)
     enc_tps = 2 * len(data) / ((st.forward_ms + st.cdf_ms) / 1000.0)
     small = D.compress(m, data[:1024], 2048)
@@ -360,8 +362,7 @@ def sub_configs(D, S, peak, peak_kind):
     spec, g = model_bytes("qwen2.5-0.5b-q8_0")
     m = D.Model(g)
     toks = S.zipf_tokens(8192, spec.vocab, seed=7)
-    m.stats(reset=True)
-    wall, _ = timed(lambda: m.encode_symbols(toks, 4096, 1024), 3, 1)
+    wall, _ = timed(lambda: m.encode_symbols(toks, 4096, 1024), 3, 1, m)
     st = m.stats(reset=True)
     out["qwen2.5-0.5b-q8_0"] = {"workload": "qwen2.5-0.5b-q8_0 encode of 8,192 Zipf(1.1) tokens, n_ctx 4096",
                                 "tokens_per_s": 3 * 8192 / ((st.forward_ms + st.cdf_ms) / 1000.0),

@@ -54,8 +54,10 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const uint8_t* __r
                                                               const float* __restrict__ bias, float one,
                                                               uint32_t* err) {
   pdl_enter();
-  __shared__ __align__(16) float ws[KQ_E][KQ_WS];  // dequantised weights [element][row]
-  __shared__ __align__(16) float as[KQ_E][KQ_WS];  // dequantised activations [element][position]
+  // two stage buffers: stage s + 1 is dequantised into one while the chains
+  // run over the other, from raw bytes loaded into registers before stage s
+  __shared__ __align__(16) float ws[2][KQ_E][KQ_WS];  // dequantised weights [element][row]
+  __shared__ __align__(16) float as[2][KQ_E][KQ_WS];  // dequantised activations [element][position]
   const int tid = threadIdx.x;
   const int r0 = blockIdx.x * KQ_ROWS, p0 = blockIdx.y * KQ_POS;
   const int nbk = nbs * 8;  // Q8A blocks per position
@@ -71,56 +73,87 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const uint8_t* __r
 #pragma unroll
   for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
 
-  for (int b = 0; b < nbs; b++) {
-    const uint8_t* blk = wrow + (size_t)b * 144;
-    const float d = row_ok ? f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8))) : 0.0f;
-    const float dmin = row_ok ? f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8))) : 0.0f;
-    for (int sub = 0; sub < 8; sub++) {
-      __syncthreads();  // previous stage consumed
-      // weights: w = (d * sc) * q - dmin * m
-      if (row_ok) {
-        int sc, mn;
-        q4k_scale_min(blk + 4, sub, sc, mn);
-        const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-        const uint2 qv = *reinterpret_cast<const uint2*>(blk + 16 + (sub >> 1) * 32 + se);
-        const int sh = (sub & 1) * 4;
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-          const uint32_t word = k < 4 ? qv.x : qv.y;
-          const int q = (int)((word >> (8 * (k & 3) + sh)) & 0x0fu);
-          ws[se + k][sr] = fsub(fmul(dsc, (float)q), dmn);
-        }
+  // raw bytes of stage st (super-block st >> 3, sub-block st & 7)
+  uint4 hdr = make_uint4(0, 0, 0, 0);  // the current super-block's d, dmin and scales
+  uint2 qv = make_uint2(0, 0), qa = make_uint2(0, 0);
+  float a_d = 0.0f;
+  auto load = [&](int st) {
+    const int b = st >> 3, sub = st & 7;
+    if (row_ok) {
+      const uint8_t* blk = wrow + (size_t)b * 144;
+      if (sub == 0) hdr = *reinterpret_cast<const uint4*>(blk);
+      qv = *reinterpret_cast<const uint2*>(blk + 16 + (sub >> 1) * 32 + se);
+    }
+    if (pos_ok) {
+      const int kb = b * 8 + sub;
+      a_d = ad[q8a_dslot(nbk, t_st, kb)];
+      qa = *reinterpret_cast<const uint2*>(aq + q8a_slot(nbk, t_st, kb) * 32 + (se ^ q8a_swz(t_st)));
+    }
+  };
+  // w = (d * sc) * q - dmin * m and a.d * a.q, with the reference's rounding
+  auto dequant = [&](int st, int buf) {
+    const int sub = st & 7;
+    if (row_ok) {
+      const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffffu));
+      const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+      // get_scale_min_k4 (det-quant lib.rs:506-518) on the scale bytes
+      // held in hdr.y .. hdr.w (bytes 4..15 of the block)
+      auto sbyte = [&](int k) -> int {
+        const uint32_t w = k < 4 ? hdr.y : (k < 8 ? hdr.z : hdr.w);
+        return (int)((w >> (8 * (k & 3))) & 0xffu);
+      };
+      int sc, mn;
+      if (sub < 4) {
+        sc = sbyte(sub) & 0x3f;
+        mn = sbyte(sub + 4) & 0x3f;
       } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) ws[se + k][sr] = 0.0f;
+        sc = (sbyte(sub + 4) & 0x0f) | ((sbyte(sub - 4) >> 6) << 4);
+        mn = (sbyte(sub + 4) >> 4) | ((sbyte(sub) >> 6) << 4);
       }
-      // activations: a.d * a.q (Q8A block b * 8 + sub of position t_st)
-      if (pos_ok) {
-        const int kb = b * 8 + sub;
-        const float a_d = ad[q8a_dslot(nbk, t_st, kb)];
-        const uint2 qa = *reinterpret_cast<const uint2*>(aq + q8a_slot(nbk, t_st, kb) * 32 + (se ^ q8a_swz(t_st)));
+      const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+      const int sh = (sub & 1) * 4;
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-          const uint32_t word = k < 4 ? qa.x : qa.y;
-          as[se + k][sr] = fmul(a_d, (float)(int8_t)(word >> (8 * (k & 3))));
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) as[se + k][sr] = 0.0f;
+      for (int k = 0; k < 8; k++) {
+        const uint32_t word = k < 4 ? qv.x : qv.y;
+        const int q = (int)((word >> (8 * (k & 3) + sh)) & 0x0fu);
+        ws[buf][se + k][sr] = fsub(fmul(dsc, (float)q), dmn);
       }
-      __syncthreads();
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) ws[buf][se + k][sr] = 0.0f;
+    }
+    if (pos_ok) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const uint32_t word = k < 4 ? qa.x : qa.y;
+        as[buf][se + k][sr] = fmul(a_d, (float)(int8_t)(word >> (8 * (k & 3))));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) as[buf][se + k][sr] = 0.0f;
+    }
+  };
+
+  const int nst = nbs * 8;
+  load(0);
+  dequant(0, 0);
+  __syncthreads();
+  for (int st = 0; st < nst; st++) {
+    const int buf = st & 1;
+    if (st + 1 < nst) load(st + 1);  // in flight while the chains run
 #pragma unroll 8
-      for (int e = 0; e < KQ_E; e++) {
-        const float4 w4 = *reinterpret_cast<const float4*>(&ws[e][rt * 4]);
-        const float4 a4 = *reinterpret_cast<const float4*>(&as[e][pt * 4]);
-        const float wr[4] = {w4.x, w4.y, w4.z, w4.w};
+    for (int e = 0; e < KQ_E; e++) {
+      const float4 w4 = *reinterpret_cast<const float4*>(&ws[buf][e][rt * 4]);
+      const float4 a4 = *reinterpret_cast<const float4*>(&as[buf][e][pt * 4]);
+      const float wr[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-          acc[r][0] = madd2(wr[r], a4.x, a4.y, one, acc[r][0]);
-          acc[r][1] = madd2(wr[r], a4.z, a4.w, one, acc[r][1]);
-        }
+      for (int r = 0; r < 4; r++) {
+        acc[r][0] = madd2(wr[r], a4.x, a4.y, one, acc[r][0]);
+        acc[r][1] = madd2(wr[r], a4.z, a4.w, one, acc[r][1]);
       }
     }
+    if (st + 1 < nst) dequant(st + 1, buf ^ 1);
+    __syncthreads();
   }
 #pragma unroll
   for (int r = 0; r < 4; r++) {

@@ -225,6 +225,7 @@ struct det_session {
   int8_t* qa_q = nullptr;
   float* qk_d = nullptr;
   int8_t* qk_q = nullptr;
+  uint8_t* qk_p = nullptr;  // Q8_K records of the tensor-core Q6_K chunk GEMM (chunks > 16)
   float *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *score_scratch = nullptr;
   float *cdf_e = nullptr, *cdf_z = nullptr;
   uint32_t *d_tokens = nullptr, *d_rows = nullptr, *d_syms = nullptr, *d_err = nullptr;

@@ -42,6 +42,8 @@ struct DevMatrix {
   const void* q = nullptr;
   const uint16_t* d = nullptr;
   const float* f = nullptr;
+  // Q6_K: the tensor-core records of the chunk GEMM (gemm_q6k_tc.cu), or null
+  const uint8_t* tc = nullptr;
 };
 
 // Quantised activations for `T` positions of length K (row stride K).
@@ -51,6 +53,7 @@ struct DevActs {
   const int8_t* qa_q = nullptr;// Q8A quants, q8a_elem order, 64-position groups
   const float* qk_d = nullptr; // Q8_K scales [T][K/256]
   const int8_t* qk_q = nullptr;// Q8_K quants [T][K]
+  const uint8_t* qk_p = nullptr;// Q8_K in the class-permuted records of gemm_q6k_tc.cu, or null
 };
 
 // epilogue modes of a GEMV/GEMM
@@ -113,10 +116,20 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
 cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h,
                            float* qd = nullptr, int8_t* qq = nullptr);
 cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
-cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq);
+// qp non-null: also writes the class-permuted records gemm_q6k_tc.cu reads
+cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq,
+                             uint8_t* qp = nullptr);
 // Q4_K matrix, chunk of T > 16 positions (gemm_kq.cu)
 cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias);
+// Q6_K matrix, chunk of T > 16 positions, on int8 tensor cores
+// (gemm_q6k_tc.cu): needs m.tc (q6k_tc_repack at load) and a.qk_p
+size_t q6k_tc_bytes(int rows, int nb);
+size_t q6k_tc_act_bytes(int T, int K);
+size_t q6k_tc_row_offset(int r0, int nb);  // r0 a multiple of 64
+cudaError_t launch_q6k_tc_repack(cudaStream_t st, const DevMatrix& m, uint8_t* out);
+cudaError_t launch_gemm_q6k_tc(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                               int epi, const float* bias);
 // Q6_K matrix, chunk of T > 16 positions (gemm_kq.cu)
 cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias);

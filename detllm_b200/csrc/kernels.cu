@@ -261,13 +261,24 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // ---- Q8_K quantiser: try_quantize_q8k_block (det-quant lib.rs:139-172) ----
 // one warp per 256-element block; the signed max is x at the FIRST index with
 // the largest |x| (carried as (|x|, index) through the reduction).
-__global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, float* __restrict__ qd,
-                                 int8_t* __restrict__ qq, uint32_t* err) {
+// qp non-null: also the class-permuted record of gemm_q6k_tc.cu per
+// (64-position group, block): byte (c, p, j) = q[8 j + c] of position p,
+// 16-byte halves swapped for positions with bit 2 set, then a.d per position
+__global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, int nbk, float* __restrict__ qd,
+                                 int8_t* __restrict__ qq, uint8_t* __restrict__ qp, uint32_t* err) {
   pdl_enter();
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= nblocks) return;
   const int l = threadIdx.x & 31;
   const float* xb = x + (size_t)b * 256;
+  // this lane's elements 8 l .. 8 l + 7 are column l of classes 0..7
+  uint8_t* prec = nullptr;
+  int pcol = 0;
+  if (qp) {
+    const int t = b / nbk, kb = b - t * nbk, p = t & 63;
+    prec = qp + ((size_t)(t >> 6) * nbk + kb) * (8 * 64 * 32 + 64 * 4);
+    pcol = p * 32 + (l ^ (((p >> 2) & 1) << 4));
+  }
   float v[8];
   float amax = 0.0f;
   int idx = 0x7fffffff;
@@ -292,6 +303,10 @@ __global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, float
   if (amax == 0.0f) {
     for (int k = 0; k < 8; k++) qq[(size_t)b * 256 + l * 8 + k] = 0;
     if (l == 0) qd[b] = 0.0f;
+    if (prec) {
+      for (int k = 0; k < 8; k++) prec[k * 2048 + pcol] = 0;
+      if (l == 0) reinterpret_cast<float*>(prec + 16384)[(b / nbk) & 63] = 0.0f;
+    }
     return;
   }
   const float mx = xb[idx];
@@ -299,9 +314,15 @@ __global__ void quant_q8k_kernel(const float* __restrict__ x, int nblocks, float
   for (int k = 0; k < 8; k++) {
     const float val = fadd(fmul(iscale, v[k]), 12582912.0f);
     int r = (int)(__float_as_uint(val) & 0x007fffffu) - 0x00400000;
-    qq[(size_t)b * 256 + l * 8 + k] = (int8_t)min(127, r);
+    const int8_t q = (int8_t)min(127, r);
+    qq[(size_t)b * 256 + l * 8 + k] = q;
+    if (prec) prec[k * 2048 + pcol] = (uint8_t)q;
   }
-  if (l == 0) qd[b] = fdiv(1.0f, iscale);
+  if (l == 0) {
+    const float dv = fdiv(1.0f, iscale);
+    qd[b] = dv;
+    if (prec) reinterpret_cast<float*>(prec + 16384)[(b / nbk) & 63] = dv;
+  }
 }
 
 // ---- generic GEMV: one thread per (row, position) running the reference's
@@ -909,10 +930,10 @@ cudaError_t launch_quant_q8a(const Launch& L, const float* x, int K, int T, floa
   return post(L);
 }
 
-cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq) {
+cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, float* qd, int8_t* qq, uint8_t* qp) {
   const int nb = T * (K / 256);
   {
-    const cudaError_t e_ = launch_k(L, quant_q8k_kernel, (nb + 7) / 8, 256, 0, x, nb, qd, qq, L.err);
+    const cudaError_t e_ = launch_k(L, quant_q8k_kernel, (nb + 7) / 8, 256, 0, x, nb, K / 256, qd, qq, qp, L.err);
     if (e_ != cudaSuccess) return e_;
   }
   return post(L);
@@ -927,6 +948,7 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   cudaError_t e = launch_gemv_fast(L, m, a, T, out, out_ld, epi, bias, &handled);
   if (handled || e != cudaSuccess) return e;
   if (m.type == GT_Q4_K && T > 16) return launch_gemm_q4k(L, m, a, T, out, out_ld, epi, bias);
+  if (m.type == GT_Q6_K && T > 16 && m.tc && a.qk_p) return launch_gemm_q6k_tc(L, m, a, T, out, out_ld, epi, bias);
   if (m.type == GT_Q6_K && T > 16) return launch_gemm_q6k(L, m, a, T, out, out_ld, epi, bias);
   if ((m.type == GT_Q4_K || m.type == GT_Q6_K) && T == 1 && kq_decode_supported(m))
     return launch_gemv_kq_decode(L, m, a, out, epi, bias);

@@ -252,6 +252,19 @@ struct Loader {
       out->d = static_cast<const uint16_t*>(p);
       m->weight_bytes += d.size() * 2;
     }
+    if (t->type == GT_Q6_K) {
+      // the tensor-core chunk GEMM's records, built on the device from the
+      // uploaded blocks (gemm_q6k_tc.cu)
+      const size_t tb_bytes = q6k_tc_bytes((int)rows, (int)nb);
+      void* tcp = nullptr;
+      if (cudaMalloc(&tcp, tb_bytes) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+      m->allocations.push_back(tcp);
+      if (launch_q6k_tc_repack(nullptr, *out, static_cast<uint8_t*>(tcp)) != cudaSuccess ||
+          cudaDeviceSynchronize() != cudaSuccess)
+        return DET_ERR_CUDA;
+      out->tc = static_cast<const uint8_t*>(tcp);
+      m->weight_bytes += tb_bytes;
+    }
     return DET_OK;
   }
 };

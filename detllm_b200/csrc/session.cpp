@@ -267,7 +267,8 @@ cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float*
     *have |= 1;
   }
   if (type == GT_Q6_K && !(*have & 2)) {
-    cudaError_t e = timed(s, PT_QUANT, 0, 0, [&] { return launch_quant_q8k(L, x, K, T, s->qk_d, s->qk_q); });
+    uint8_t* qp = T > 16 ? s->qk_p : nullptr;
+    cudaError_t e = timed(s, PT_QUANT, 0, 0, [&] { return launch_quant_q8k(L, x, K, T, s->qk_d, s->qk_q, qp); });
     if (e != cudaSuccess) return e;
     *have |= 2;
   }
@@ -275,6 +276,7 @@ cudaError_t quantise_for(det_session* s, const Launch& L, int type, const float*
   a->qa_q = s->qa_q;
   a->qk_d = s->qk_d;
   a->qk_q = s->qk_q;
+  a->qk_p = T > 16 ? s->qk_p : nullptr;
   return cudaSuccess;
 }
 
@@ -635,6 +637,16 @@ det_status check_symbols(det_session* s, int tail) {
   return DET_OK;
 }
 
+// any Q6_K matrix with tensor-core chunk records (then chunks > 16 quantise
+// into the permuted Q8_K records too)
+bool model_has_q6k_tc(const det_model* m) {
+  if (m->output.tc || m->tok_embd.tc) return true;
+  for (const LayerDev& L : m->layers)
+    for (const DevMatrix* W : {&L.wq, &L.wk, &L.wv, &L.wo, &L.gate, &L.up, &L.down})
+      if (W->tc) return true;
+  return false;
+}
+
 }  // namespace
 
 extern "C" {
@@ -690,6 +702,7 @@ det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, 
     st = DET_ERR_CUDA;
   if (!st) st = dalloc(s, &s->qk_d, T * (kmax / 256 + 1));
   if (!st) st = dalloc(s, &s->qk_q, T * kmax + 64);
+  if (!st && T > 16 && model_has_q6k_tc(m)) st = dalloc(s, &s->qk_p, q6k_tc_act_bytes((int)T, (int)kmax));
   if (!st) st = dalloc(s, &s->kc, kv);
   if (!st) st = dalloc(s, &s->vc, kv);
   if (!st) st = dalloc(s, &s->rope_cos, (size_t)n_ctx * (c.rope_dim / 2));

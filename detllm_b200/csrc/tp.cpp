@@ -122,6 +122,7 @@ DevMatrix row_view(const DevMatrix& M, int r0, int r1) {
     default:  // GT_Q6_K
       v.q = q + r * (size_t)M.nb * 208;
       v.d = M.d + r * (size_t)M.nb;
+      if (M.tc) v.tc = M.tc + q6k_tc_row_offset(r0, M.nb);  // r0: a multiple of 64 (kRowGrain)
       break;
   }
   return v;
