@@ -209,6 +209,10 @@ struct det_model {
   // the replicas' weights (cfg then holds this part's head and FFN counts)
   det::TpModel* tp = nullptr;
   det::TpShard* shard = nullptr;
+  // bytes of every codec symbol (tokens, then the 256 byte escapes) for the
+  // decompress loop on the device; built on first use
+  uint16_t* piece_len = nullptr;
+  size_t max_piece = 1;
 };
 
 
@@ -259,6 +263,13 @@ struct det_session {
   det::FdParams fd;
   int fd_grid = 0;
   double fd_wbytes = 0;  // weight bytes one fused forward streams
+  // the decompress loop on the device (codec.cpp): its state, a pinned copy,
+  // row id 0 for the CDF of the one-position logits, and the one-position
+  // forward that reads its token and position from device memory
+  det::RcState* d_rc = nullptr;
+  det::RcState* h_rc = nullptr;
+  uint32_t* d_row0 = nullptr;
+  Graph graph_dev1;
 };
 
 namespace det {
@@ -266,6 +277,11 @@ extern bool g_profiling;
 det_status cuda_status(cudaError_t e);
 // reads and clears a session's device error flag (synchronises its stream)
 det_status session_take_error(det_session* s, bool cdf);
+// the decompress loop on the device: allocates the session's RcState (once)
+det_status rc_loop_init(det_session* s);
+// a one-position forward whose token and position are already in device
+// memory (s->d_tokens[0], s->d_pos[0]), e.g. written by rc_step_kernel
+det_status forward_device_inputs(det_session* s);
 // forward stages (session.cpp); `have` carries which quantisations of the
 // FFN activation the SwiGLU launch already wrote
 det_status fwd_embed(det_session* s, const Launch& L, int T);

@@ -208,6 +208,25 @@ cudaError_t launch_tp_exchange(const Launch& L, const TpFlags& f, const unsigned
                                unsigned wait_mask, const GatherPlan& g, float* dst, int ld_dst, int T);
 // *epoch += 1 (the start of a forward)
 cudaError_t launch_tp_epoch(const Launch& L, unsigned long long* epoch);
+// The decompress loop's device state (one per session in device memory): the
+// range decoder (det-coder range.rs:88-178), the window's token count, the
+// bytes produced so far, and the symbols one batch of steps decoded.
+constexpr int kRcMaxBatch = 64;
+enum : uint32_t { RC_RUNNING = 0, RC_DONE = 1, RC_WINDOW_FULL = 2, RC_FAILED = 3 };
+struct RcState {
+  unsigned long long low, code, range;  // RangeDecoder
+  unsigned long long pos, len;          // payload cursor and length
+  unsigned long long bytes, orig_len;   // output bytes so far / in the file
+  uint32_t status, error;               // RC_*, and the det_status of RC_FAILED
+  uint32_t count, max_count;            // symbols this batch / steps allowed this batch
+  uint32_t clen, n_ctx, tail, pad;      // tokens in the window, window size, escapes (256 or 0)
+  uint32_t syms[kRcMaxBatch];
+};
+// one decode step (rc_step_kernel): next symbol under logits row 0's CDF
+// (cdf_prepare of row 0 must precede it), range decoder advance, and the
+// token / position of the next one-position forward
+cudaError_t launch_rc_step(const Launch& L, RcState* S, const float* e, const float* z, int V, const uint8_t* payload,
+                           const uint16_t* piece_len, uint32_t* tok, int* pos);
 cudaError_t launch_decoder_lookup(const Launch& L, const float* e, const float* z, int V, int tail, uint32_t row,
                                   const uint64_t* value, uint64_t* out4);
 

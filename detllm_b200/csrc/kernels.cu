@@ -10,6 +10,7 @@
 #include <cstdlib>
 
 #include "dev_math.cuh"
+#include "../../include/detgpu.h"
 #include "internal.h"
 
 namespace det {
@@ -859,6 +860,192 @@ __global__ void decoder_lookup_kernel(const float* __restrict__ e, const float* 
   }
 }
 
+// ---- the decompress loop on the device -------------------------------------
+// One decoded symbol per launch (one CTA of RC_THREADS): the symbol range of
+// the next symbol under logits row 0 (or the uniform CDF while the window is
+// empty), the range decoder's decode_freq / advance with its renormalisation
+// (det-coder range.rs:110-178), the symbol's byte count, and the next
+// one-position forward's token and position in device memory.  A launch
+// after the loop has stopped (done, window full, error, batch full) changes
+// nothing, and neither does the forward that follows it: that forward then
+// recomputes the previous one (same token, same position) bit for bit.
+constexpr int RC_THREADS = 1024;
+constexpr unsigned long long RC_TOP = 1ull << 56, RC_BOTTOM = 1ull << 48;
+
+// normalize_step (range.rs:169-178)
+DI bool rc_normalize_step(unsigned long long low, unsigned long long& range) {
+  if ((low ^ (low + range)) < RC_TOP) return true;
+  if (range < RC_BOTTOM) {
+    range = (0ull - low) & (RC_BOTTOM - 1);
+    return true;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(RC_THREADS) rc_step_kernel(RcState* __restrict__ S, const float* __restrict__ e,
+                                                             const float* __restrict__ z, int V,
+                                                             const uint8_t* __restrict__ payload,
+                                                             const uint16_t* __restrict__ piece_len,
+                                                             uint32_t* __restrict__ tok, int* __restrict__ posp,
+                                                             uint32_t* err) {
+  pdl_enter();
+  __shared__ unsigned long long wsum[32];
+  __shared__ unsigned long long sh_total, sh_value, sh_r, sh_base, sh_sym, sh_cum, sh_freq;
+  __shared__ int sh_run, sh_uniform, sh_found, sh_fail;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int tail = (int)S->tail;
+  if (tid == 0) {
+    sh_run = S->status == RC_RUNNING && S->count < S->max_count;
+    sh_uniform = S->clen == 0;
+    sh_found = 0;
+    sh_fail = 0;
+    sh_base = 0;
+  }
+  __syncthreads();
+  if (!sh_run) return;
+  const float zz = sh_uniform ? 1.0f : z[0];
+  // total of the distribution (symbols_total for the uniform CDF)
+  unsigned long long tot = 0;
+  if (!sh_uniform)
+    for (int i = tid; i < V; i += RC_THREADS) tot += freq_of(e[i], zz);
+  tot = block_sum_u64<RC_THREADS>(tot, wsum);
+  if (tid == 0) {
+    const unsigned long long total = (unsigned long long)V + (unsigned long long)tail;
+    sh_total = sh_uniform ? total : tot + (unsigned long long)tail;
+    // decode_freq (range.rs:110-128)
+    const unsigned long long t = sh_total;
+    unsigned long long r = 0, value = 0;
+    int bad = 0;
+    if (!sh_uniform && t >= (1ull << 31)) {
+      bad = DET_ERR_CDF_TOTAL_TOO_LARGE;
+    } else if (t == 0 || t >= (1ull << 31)) {
+      bad = DET_ERR_RANGE_INVALID_FREQUENCY;
+    } else {
+      r = S->range / t;
+      if (r == 0) bad = DET_ERR_RANGE_INVALID_FREQUENCY;
+      else {
+        value = (S->code - S->low) / r;
+        if (value >= t) bad = DET_ERR_RANGE_INVALID_FREQUENCY;
+      }
+    }
+    if (bad) {
+      S->status = RC_FAILED;
+      S->error = (uint32_t)bad;
+      sh_fail = 1;
+    }
+    sh_value = value;
+    sh_r = r;
+    if (sh_uniform) {  // uniform_symbol_range (cdf.rs:247-253)
+      sh_sym = value;
+      sh_cum = value;
+      sh_freq = 1;
+      sh_found = 1;
+    }
+  }
+  __syncthreads();
+  if (sh_fail) return;
+  const unsigned long long value = sh_value;
+  if (!sh_uniform) {
+    // DecoderDistribution::symbol_range (cdf.rs:392-425): exclusive scans of
+    // the exact integer frequencies
+    for (int start = 0; start < V; start += RC_THREADS) {
+      const int i = start + tid;
+      const unsigned long long f = i < V ? freq_of(e[i], zz) : 0ull;
+      unsigned long long inc = f;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (l >= o) inc += n;
+      }
+      __syncthreads();
+      if (l == 31) wsum[w] = inc;
+      __syncthreads();
+      if (w == 0) {
+        unsigned long long s = wsum[l];
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned long long n = __shfl_up_sync(0xffffffffu, s, o);
+          if (l >= o) s += n;
+        }
+        wsum[l] = s;
+      }
+      __syncthreads();
+      const unsigned long long base = sh_base;
+      const unsigned long long excl = base + (w ? wsum[w - 1] : 0ull) + inc - f;
+      if (i < V && excl <= value && value < excl + f) {
+        sh_sym = (unsigned long long)i;
+        sh_cum = excl;
+        sh_freq = f;
+        sh_found = 1;
+      }
+      __syncthreads();
+      if (tid == 0) sh_base = base + wsum[31];
+      __syncthreads();
+    }
+  }
+  if (tid != 0) return;
+  unsigned long long sym = sh_sym, cum = sh_cum, freq = sh_freq;
+  const unsigned long long total = sh_total;
+  if (!sh_found) {  // the byte-escape tail
+    const unsigned long long tot_f = sh_base;
+    if (value >= tot_f && value - tot_f < (unsigned long long)tail) {
+      sym = (unsigned long long)V + (value - tot_f);
+      cum = value;
+      freq = 1;
+    } else {
+      flag(err, ERRF_DECODE);
+      S->status = RC_FAILED;
+      S->error = DET_ERR_DECODE;
+      return;
+    }
+  }
+  // advance (range.rs:130-148) with validate (:180-186) and renorm
+  const unsigned long long end = cum + freq;
+  if (end < cum || freq == 0 || total == 0 || total >= (1ull << 31) || end > total) {
+    S->status = RC_FAILED;
+    S->error = DET_ERR_RANGE_INVALID_FREQUENCY;
+    return;
+  }
+  unsigned long long low = S->low, code = S->code, range = sh_r, pos = S->pos;
+  low += range * cum;
+  range *= freq;
+  while (rc_normalize_step(low, range)) {
+    if (pos >= S->len) {
+      S->status = RC_FAILED;
+      S->error = DET_ERR_RANGE_UNEXPECTED_EOF;
+      return;
+    }
+    code = (code << 8) | (unsigned long long)payload[pos++];
+    low <<= 8;
+    range <<= 8;
+  }
+  S->low = low;
+  S->code = code;
+  S->range = range;
+  S->pos = pos;
+  // the symbol's bytes; a symbol without bytes is an error (det-cli
+  // main.rs:614-616)
+  const unsigned plen = piece_len[sym];
+  S->syms[S->count++] = (uint32_t)sym;
+  if (plen == 0) {
+    S->status = RC_FAILED;
+    S->error = DET_ERR_TOKENIZER;
+    return;
+  }
+  S->bytes += plen;
+  const bool token = !(tail && sym >= (unsigned long long)V);
+  if (token) {
+    if (S->clen >= S->n_ctx) {
+      S->status = RC_FAILED;
+      S->error = DET_ERR_WINDOW;
+      return;
+    }
+    tok[0] = (uint32_t)sym;
+    *posp = (int)S->clen;
+    S->clen++;
+  }
+  if (S->bytes >= S->orig_len) S->status = RC_DONE;
+  else if (token && S->clen >= S->n_ctx) S->status = RC_WINDOW_FULL;
+}
+
 __global__ void expf_kernel(const float* x, float* y, long long n) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = expf_det(x[i]);
@@ -1063,6 +1250,16 @@ cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, i
                               const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3) {
   {
     const cudaError_t e_ = launch_k(L, cdf_ranges_kernel, n, CDF_THREADS, 0, e, z, V, tail, rows, symbols, out3, L.err);
+    if (e_ != cudaSuccess) return e_;
+  }
+  return post(L);
+}
+
+cudaError_t launch_rc_step(const Launch& L, RcState* S, const float* e, const float* z, int V, const uint8_t* payload,
+                           const uint16_t* piece_len, uint32_t* tok, int* pos) {
+  {
+    const cudaError_t e_ =
+        launch_k(L, rc_step_kernel, 1, RC_THREADS, 0, S, e, z, V, payload, piece_len, tok, pos, L.err);
     if (e_ != cudaSuccess) return e_;
   }
   return post(L);

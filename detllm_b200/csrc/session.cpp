@@ -118,8 +118,9 @@ void free_session(det_session* s) {
   add_prof(&owner->prof_agg, s->prof);
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   for (void* p : s->allocations) cudaFree(p);
+  if (s->graph_dev1.exec) cudaGraphExecDestroy(s->graph_dev1.exec);
   for (void* p : {(void*)s->h_tokens, (void*)s->h_rows, (void*)s->h_syms, (void*)s->h_err, (void*)s->h_out,
-                  (void*)s->h_value, (void*)s->h_pos})
+                  (void*)s->h_value, (void*)s->h_pos, (void*)s->h_rc})
     if (p) cudaFreeHost(p);
   for (auto& e : s->ev)
     if (e) cudaEventDestroy(e);
@@ -610,6 +611,55 @@ det_status run_forward(det_session* s, int T) {
   s->stats.launches += gr.kernels;
   return DET_OK;
 }
+
+}  // namespace
+
+det_status det::rc_loop_init(det_session* s) {
+  if (s->d_rc) return DET_OK;
+  cudaSetDevice(s->m->device);
+  det_status st = dalloc(s, &s->d_rc, 1);
+  if (!st) st = dalloc(s, &s->d_row0, 1);
+  if (!st) st = halloc(s, &s->h_rc, 1);
+  if (!st && cudaMemset(s->d_row0, 0, sizeof(uint32_t)) != cudaSuccess) st = DET_ERR_CUDA;
+  if (st) s->d_rc = nullptr;
+  return st;
+}
+
+// forward_one_with_workspace for the one position whose token and position
+// a kernel left in s->d_tokens[0] / s->d_pos[0]: the same launches as
+// run_forward(s, 1) without the host-to-device copies, in a graph of its own
+det_status det::forward_device_inputs(det_session* s) {
+  if (s->tp) return DET_ERR_UNSUPPORTED_MODEL_FEATURE;
+  const bool fused = fused_decode_ready(s);
+  if (!graphs_enabled() || fused) {
+    const det_status st = forward_chunk(s, 1, &s->stats.launches);
+    s->last_n = 1;
+    return st;
+  }
+  det_session::Graph& gr = s->graph_dev1;
+  if (!gr.exec) {
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    uint64_t count = 0;
+    const det_status st = forward_chunk(s, 1, &count);
+    const cudaError_t ec = cudaStreamEndCapture(s->stream, &graph);
+    if (st) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    CK(ec);
+    const cudaError_t ei = cudaGraphInstantiate(&gr.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(ei);
+    gr.kernels = count;
+  }
+  CK(cudaGraphLaunch(gr.exec, s->stream));
+  s->stats.launches += gr.kernels;
+  s->last_n = 1;
+  return DET_OK;
+}
+
+namespace {
 
 // e/z for the listed rows of the last forward (once per row per forward)
 det_status prepare_rows(det_session* s, const uint32_t* rows, uint32_t n) {
