@@ -190,6 +190,140 @@ uint64_t get_le(const uint8_t* p, int n) {
   return v;
 }
 
+// bytes of every codec symbol on the device, for the decompress loop (once
+// per model): token pieces, then 1 for each byte escape; 0 marks a symbol
+// without bytes (det-token lib.rs:182-196)
+det_status ensure_piece_len(det_model* m) {
+  if (m->piece_len) return DET_OK;
+  const size_t n = (size_t)m->vocab + kEscapes;
+  std::vector<uint16_t> len(n);
+  std::string piece;
+  size_t mx = 1;
+  for (size_t i = 0; i < n; i++) {
+    const bool ok = m->tok.symbol_bytes((uint32_t)i, true, &piece) == DET_OK;
+    len[i] = ok ? (uint16_t)std::min<size_t>(piece.size(), 65535) : 0;
+    if (ok) mx = std::max(mx, piece.size());
+  }
+  void* p = nullptr;
+  cudaSetDevice(m->device);
+  if (cudaMalloc(&p, n * sizeof(uint16_t)) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  m->allocations.push_back(p);
+  if (cudaMemcpy(p, len.data(), n * sizeof(uint16_t), cudaMemcpyHostToDevice) != cudaSuccess) return DET_ERR_CUDA;
+  m->piece_len = static_cast<uint16_t*>(p);
+  m->max_piece = mx;
+  return DET_OK;
+}
+
+// decode_bytes_with_model (det-cli main.rs:585-630) with the symbol loop on
+// the device: per step, the CDF of the last logits row, the range decoder's
+// decode_freq / symbol search / advance (rc_step_kernel) and the next
+// one-position forward, whose token and position the step kernel writes.
+// The host enqueues a batch of steps and synchronises once per batch, not
+// per symbol; it maps the batch's symbols to bytes and replays the overlap
+// when a window is full, as the host loop does.  Symbols and bytes are those
+// of the host loop: every step computes the same ranges on the same logits.
+det_status decode_on_device(det_model* m, det_session* s, const uint8_t* payload, size_t plen, uint64_t orig_len,
+                            uint32_t n_ctx, uint32_t overlap, int escapes, std::vector<uint8_t>* bytes,
+                            std::vector<uint32_t>* syms) {
+  if (plen < 8) return DET_ERR_RANGE_UNEXPECTED_EOF;  // RangeDecoder::new reads 8 bytes
+  if (det_status st = ensure_piece_len(m)) return st;
+  if (det_status st = rc_loop_init(s)) return st;
+  cudaSetDevice(m->device);
+  const uint32_t V = (uint32_t)m->vocab;
+  struct DevBuf {
+    uint8_t* p = nullptr;
+    ~DevBuf() {
+      if (p) cudaFree(p);
+    }
+  } pay;
+  if (cudaMalloc(&pay.p, plen) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  RcState& H = *s->h_rc;
+  std::memset(&H, 0, sizeof(H));
+  H.low = 0;
+  H.range = ~0ull;
+  for (int i = 0; i < 8; i++) H.code = (H.code << 8) | payload[i];
+  H.pos = 8;
+  H.len = plen;
+  H.orig_len = orig_len;
+  H.n_ctx = n_ctx;
+  H.tail = escapes ? kEscapes : 0;
+  // before any forward: finite logits for the (unused) CDF of an empty
+  // window, and token 0 at position 0 for the recomputing forwards
+  if (cudaMemcpyAsync(pay.p, payload, plen, cudaMemcpyHostToDevice, s->stream) != cudaSuccess ||
+      cudaMemsetAsync(s->logits, 0, (size_t)V * sizeof(float), s->stream) != cudaSuccess ||
+      cudaMemsetAsync(s->d_tokens, 0, sizeof(uint32_t), s->stream) != cudaSuccess ||
+      cudaMemsetAsync(s->d_pos, 0, sizeof(int), s->stream) != cudaSuccess)
+    return DET_ERR_CUDA;
+  s->stats.h2d_bytes += plen;
+  const Launch L{s->stream, s->d_err, &s->stats.launches};
+  std::vector<uint32_t> ctx;
+  std::string piece;
+  size_t ws = 0;
+  uint32_t clen = 0;
+  while (bytes->size() < orig_len) {
+    // steps this batch: no more symbols than the remaining bytes can hold,
+    // no more tokens than the window has room for
+    const uint64_t remaining = orig_len - bytes->size();
+    uint32_t B = (uint32_t)std::min<uint64_t>(kRcMaxBatch, std::max<uint64_t>(1, remaining / m->max_piece));
+    B = std::min<uint32_t>(B, std::max<uint32_t>(1, n_ctx - clen));
+    H.count = 0;
+    H.max_count = B;
+    H.status = RC_RUNNING;
+    H.clen = clen;
+    if (cudaMemcpyAsync(s->d_rc, &H, sizeof(RcState), cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+      return DET_ERR_CUDA;
+    if (cudaEventRecord(s->ev[0], s->stream) != cudaSuccess) return DET_ERR_CUDA;
+    for (uint32_t b = 0; b < B; b++) {
+      if (launch_cdf_prepare(L, s->logits, (int)V, s->d_row0, 1, s->cdf_e, s->cdf_z) != cudaSuccess ||
+          launch_rc_step(L, s->d_rc, s->cdf_e, s->cdf_z, (int)V, pay.p, m->piece_len, s->d_tokens, s->d_pos) !=
+              cudaSuccess)
+        return DET_ERR_CUDA;
+      if (det_status st = forward_device_inputs(s)) return st;
+    }
+    if (cudaEventRecord(s->ev[1], s->stream) != cudaSuccess ||
+        cudaMemcpyAsync(&H, s->d_rc, sizeof(RcState), cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+      return DET_ERR_CUDA;
+    s->stats.h2d_bytes += sizeof(RcState);
+    s->stats.d2h_bytes += sizeof(RcState);
+    if (det_status st = session_take_error(s, true)) return st;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, s->ev[0], s->ev[1]) == cudaSuccess) s->stats.forward_ms += ms;
+    for (uint32_t i = 0; i < H.count; i++) {
+      const uint32_t symbol = H.syms[i];
+      if (det_status st = m->tok.symbol_bytes(symbol, escapes != 0, &piece)) return st;
+      bytes->insert(bytes->end(), piece.begin(), piece.end());
+      syms->push_back(symbol);
+      if (escapes && symbol >= V) continue;
+      ctx.push_back(symbol);
+      s->stats.tokens++;
+    }
+    clen = H.clen;
+    if (H.status == RC_FAILED) return (det_status)H.error;
+    if (H.status == RC_DONE) break;
+    if (H.status == RC_WINDOW_FULL) {  // replay the overlap as chunked prefill
+      const size_t pos = ctx.size();
+      ws = next_window_start(pos, ws, n_ctx, overlap);
+      clen = 0;
+      if (det_status st = det_session_reset(s)) return st;
+      for (size_t p = ws; p < pos; p += (size_t)s->max_chunk) {
+        const uint32_t cnt = (uint32_t)std::min<size_t>((size_t)s->max_chunk, pos - p);
+        if (det_status st = det_forward(s, ctx.data() + p, cnt, clen, nullptr)) return st;
+        clen += cnt;
+      }
+      // the last replayed position once more as a one-position forward: its
+      // logits go to row 0 and its token and position to the buffers the
+      // steps' forwards read (bit-identical to the chunk's last row)
+      if (clen) {
+        if (det_status st = det_forward(s, &ctx.back(), 1, clen - 1, nullptr)) return st;
+      } else if (cudaMemsetAsync(s->d_tokens, 0, sizeof(uint32_t), s->stream) != cudaSuccess ||
+                 cudaMemsetAsync(s->d_pos, 0, sizeof(int), s->stream) != cudaSuccess) {
+        return DET_ERR_CUDA;
+      }
+    }
+  }
+  return DET_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -268,7 +402,10 @@ det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t
   size_t ws = 0, clen = 0;
   uint32_t last_row = 0;
   det_status st = DET_OK;
-  while (!st && bytes.size() < orig_len) {
+  // one session on one device: the symbol loop runs on the device; a
+  // tensor-parallel session (parts on several devices) keeps the host loop
+  if (!s->tp) st = decode_on_device(m, s, payload, plen, orig_len, n_ctx, overlap, escapes, &bytes, &syms);
+  while (s->tp && !st && bytes.size() < orig_len) {
     const size_t pos = ctx.size();
     const size_t nws = next_window_start(pos, ws, n_ctx, overlap);
     if (nws != ws) {  // replay the overlap as chunked prefill

@@ -207,7 +207,7 @@ def test_fixture_codec_bytes(D, oracle, goldens, fixtures, name):
 
 
 @pytest.mark.parametrize("name", list(SPECS))
-@pytest.mark.parametrize("n_ctx", [9, 64])
+@pytest.mark.parametrize("n_ctx", [2, 3, 9, 64])  # 2, 3: overlap 0, every window starts empty
 def test_codec_bytes_synthetic(D, oracle, models, name, n_ctx):
     spec = SPECS[name]
     n_ctx = min(n_ctx, spec.ctx)
