@@ -105,12 +105,19 @@ def all_max(x, ws):
     return G.max_over_ranks(x, ws, device="cuda")
 
 
+LAYERS = 0  # --layers: cut the headline model's layer count (profiling captures only)
+
+
 def model_bytes(config, rank=0, ws=1):
     """The seeded GGUF of `config`, built once per box (rank 0) into /tmp."""
+    import dataclasses
+
     from detllm_b200 import synth as S
 
     spec = S.CONFIGS[config]
-    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{config}_s{spec.seed}.gguf")
+    if LAYERS and config == HEADLINE:
+        spec = dataclasses.replace(spec, n_layer=LAYERS)
+    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{config}_L{spec.n_layer}_s{spec.seed}.gguf")
     if rank == 0 and not os.path.exists(path):
         t = time.time()
         data = S.build_gguf(spec)
@@ -556,7 +563,7 @@ def run(args):
 
 
 def main():
-    global PREFIX
+    global PREFIX, LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -567,8 +574,11 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE configs 2-4 sub-benchmarks")
     ap.add_argument("--prefix", type=int, default=PREFIX,
                     help="bytes of each segment per step (default one n_ctx window; smaller is for profiling)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="layers of the headline model (default all; fewer only for profiling captures)")
     args = ap.parse_args()
     PREFIX = args.prefix
+    LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:
