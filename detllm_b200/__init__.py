@@ -109,6 +109,7 @@ def lib():
             "det_session_gemv_stream": (I, [P, U32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
             "det_tp_exchange_timeout_selftest": (I, [I]),
+            "det_q6k_pipeline_timeout_selftest": (I, [I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

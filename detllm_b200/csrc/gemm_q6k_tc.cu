@@ -38,6 +38,7 @@
 #include <atomic>
 #include <cuda_runtime.h>
 
+#include "../../include/detgpu.h"
 #include "dev_math.cuh"
 #include "internal.h"
 
@@ -57,6 +58,7 @@ constexpr int TC_RED_LD = TC_ROWS + 4;  // reduction rows (floats): conflict-fre
 constexpr int TC_SMEM = TC_STAGE * TC_STAGES + 2 * TC_STAGES * 8;
 static_assert(8 * TC_POS * TC_RED_LD * 4 <= TC_STAGE * TC_STAGES, "reduction fits the ring");
 constexpr unsigned long long kTcWaitNs = 2000000000ull;  // mbarrier wait bound (2 s)
+constexpr unsigned long long kTcSelftestWaitNs = 20000000ull;  // the self-test's bound (20 ms)
 
 DI uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 DI void tc_mbar_init(uint32_t bar, uint32_t count) {
@@ -76,8 +78,8 @@ DI unsigned long long tc_now() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// bounded wait for phase `parity`; false on timeout
-DI bool tc_wait(uint32_t bar, uint32_t parity) {
+// bounded wait for phase `parity`; false after `bound_ns`
+DI bool tc_wait(uint32_t bar, uint32_t parity, unsigned long long bound_ns) {
   unsigned long long t0 = 0;
   for (unsigned it = 0;; it++) {
     uint32_t ok;
@@ -88,7 +90,7 @@ DI bool tc_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     if (ok) return true;
     if (it == 0) t0 = tc_now();
-    else if ((it & 63) == 0 && tc_now() - t0 > kTcWaitNs) return false;
+    else if ((it & 63) == 0 && tc_now() - t0 > bound_ns) return false;
   }
 }
 
@@ -143,7 +145,9 @@ DI void ldsm_b(const uint8_t* cls, int p0, int lane, int (&b)[4]) {
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_q6k_tc_kernel(const uint8_t* __restrict__ W, int rows, int nb, const uint8_t* __restrict__ A, int T,
                        float* __restrict__ out, int out_ld, int epi, const float* __restrict__ bias, float one,
-                       uint32_t* err) {
+                       uint32_t* err, int withhold, unsigned long long wait_ns) {
+  // withhold >= 0 (det_q6k_pipeline_timeout_selftest only): that stage is
+  // never copied, so every wait on it runs out after wait_ns
   pdl_enter();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -163,6 +167,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint8_t* wrec = W + (size_t)rg * nb * TC_A_REC;
   const uint8_t* arec = A + (size_t)grp * nb * TC_B_REC;
   auto issue = [&](int b) {
+    if (b == withhold) return;
     const int slot = b % TC_STAGES;
     uint8_t* sb = smem + slot * TC_STAGE;
     tc_expect_tx(full0 + 8 * slot, TC_STAGE);
@@ -188,7 +193,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   bool ok = true;
   for (int b = 0; b < nb; b++) {
     const int slot = b % TC_STAGES;
-    if (ok && !tc_wait(full0 + 8 * slot, (uint32_t)((b / TC_STAGES) & 1))) {
+    if (ok && !tc_wait(full0 + 8 * slot, (uint32_t)((b / TC_STAGES) & 1), wait_ns)) {
       if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
       ok = false;
     }
@@ -234,7 +239,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
     if (lane == 0) tc_arrive(empty0 + 8 * slot);
     if (producer && issued < nb) {
-      if (!tc_wait(empty0 + 8 * slot, (uint32_t)((b / TC_STAGES) & 1))) {
+      if (!tc_wait(empty0 + 8 * slot, (uint32_t)((b / TC_STAGES) & 1), wait_ns)) {
         atomicOr(err, ERRF_TIMEOUT);
         ok = false;
       } else {
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // the stages a failed warp left unread (bounded), then agree on the outcome
   if (producer)
     for (int s2 = max(0, issued - TC_STAGES); s2 < issued; s2++)
-      tc_wait(full0 + 8 * (s2 % TC_STAGES), (uint32_t)((s2 / TC_STAGES) & 1));
+      if (s2 != withhold) tc_wait(full0 + 8 * (s2 % TC_STAGES), (uint32_t)((s2 / TC_STAGES) & 1), wait_ns);
   if (!__syncthreads_and(ok)) return;
   float* red = reinterpret_cast<float*>(smem);  // [class][position][row]
 #pragma unroll
@@ -345,9 +350,46 @@ cudaError_t launch_gemm_q6k_tc(const Launch& L, const DevMatrix& m, const DevAct
   }
   dim3 grid((T + TC_POS - 1) / TC_POS, (m.rows + TC_ROWS - 1) / TC_ROWS);
   const cudaError_t e = launch_k(L, gemm_q6k_tc_kernel, grid, TC_THREADS, TC_SMEM, m.tc, m.rows, m.nb, a.qk_p, T,
-                                 out, out_ld, epi, bias, 1.0f, L.err);
+                                 out, out_ld, epi, bias, 1.0f, L.err, -1, kTcWaitNs);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 }  // namespace det
+
+// The pipeline's bounded waits, exercised: one CTA over zero-filled records
+// of 64 rows x 4 blocks and 64 positions, first with stage 1 never copied
+// (every wait on it gives up after 20 ms and the kernel reports
+// ERRF_TIMEOUT without writing its outputs), then complete (outputs 0, no
+// error), on the same device and stream.
+extern "C" det_status det_q6k_pipeline_timeout_selftest(int device) {
+  using namespace det;
+  int cnt = 0;
+  if (cudaGetDeviceCount(&cnt) != cudaSuccess || cnt == 0) return DET_ERR_NO_DEVICE;
+  if (device < 0 || device >= cnt) return DET_ERR_INVALID_ARGUMENT;
+  if (cudaSetDevice(device) != cudaSuccess) return DET_ERR_CUDA;
+  constexpr int nb = 4;
+  const size_t wbytes = (size_t)nb * TC_A_REC, abytes = (size_t)nb * TC_B_REC, obytes = (size_t)TC_ROWS * TC_POS * 4;
+  uint8_t* mem = nullptr;
+  if (cudaMalloc(&mem, wbytes + abytes + obytes + 256) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  uint8_t* w = mem;
+  uint8_t* a = mem + wbytes;
+  float* out = reinterpret_cast<float*>(mem + wbytes + abytes);
+  uint32_t* err = reinterpret_cast<uint32_t*>(mem + wbytes + abytes + obytes);
+  cudaError_t e = cudaMemset(mem, 0, wbytes + abytes + obytes + 256);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_q6k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+  uint32_t flag[2] = {0, 0};
+  for (int run = 0; run < 2 && e == cudaSuccess; run++) {
+    gemm_q6k_tc_kernel<<<dim3(1, 1), TC_THREADS, TC_SMEM>>>(w, TC_ROWS, nb, a, TC_POS, out, TC_ROWS, EPI_STORE,
+                                                           nullptr, 1.0f, err, run == 0 ? 1 : -1,
+                                                           kTcSelftestWaitNs);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&flag[run], err, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(err, 0, 4);
+  }
+  cudaFree(mem);
+  if (e != cudaSuccess) return DET_ERR_CUDA;
+  if (flag[1] != 0) return DET_ERR_CUDA;  // the complete run must not flag anything
+  return (flag[0] & ERRF_TIMEOUT) ? DET_ERR_TIMEOUT : DET_OK;
+}

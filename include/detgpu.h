@@ -217,6 +217,13 @@ det_status det_device_expf(int device, const float* x, float* y, size_t n);
  * reports it through the error word, so the expected result is
  * DET_ERR_TIMEOUT, with the device still usable afterwards. */
 det_status det_tp_exchange_timeout_selftest(int device);
+/* Self-test of the bounded mbarrier waits of the bulk-copy pipelines (no
+ * counterpart in the reference): on `device`, runs the tensor-core Q6_K
+ * chunk GEMM on zero-filled records with one stage never copied.  Its waits
+ * give up after 20 ms and the kernel reports it through the error word
+ * (expected result DET_ERR_TIMEOUT), then the same launch with every stage
+ * copied must finish without an error (else DET_ERR_CUDA). */
+det_status det_q6k_pipeline_timeout_selftest(int device);
 
 /* ---- timing hooks for benchmarks (device time of the last call) -------- */
 typedef struct {

@@ -288,3 +288,19 @@ def test_codec_bytes_sentencepiece_and_bpe(D, oracle, kind):
     got = D.compress(m, data, 48)
     assert got == want
     assert D.decompress(m, got) == data
+
+
+def test_pipeline_wait_times_out_and_device_recovers(D):
+    """The bulk-copy pipeline's bounded mbarrier waits: the tensor-core Q6_K
+    chunk GEMM runs with one stage never copied, gives up after its (20 ms)
+    bound and reports DET_ERR_TIMEOUT without hanging; the complete launch
+    after it, and a K-quant forward through the model, still work."""
+    import time
+
+    t = time.time()
+    code = D.lib().det_q6k_pipeline_timeout_selftest(0)
+    assert code == 67, D.lib().det_status_string(code)  # DET_ERR_TIMEOUT
+    assert time.time() - t < 20
+    spec = SPECS["q4k_q6k"]
+    toks = S.zipf_tokens(24, spec.vocab, seed=2)
+    assert D.Model(S.build_gguf(spec)).logits_for_tokens(toks, chunk=24).shape == (24, spec.vocab)
