@@ -178,137 +178,6 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const uint8_t* __r
   }
 }
 
-// ---- Q6_K x Q8_K chunk GEMM -------------------------------------------------------
-// Reference: dot_q6_k_q8k (crates/det-quant/src/lib.rs:353-397).  Per
-// 256-element block, lane ln (elements i = 16 s + 8 rep + ln) accumulates the
-// exact integer aux[ln] = sum over s, rep of scale_s * a.q[i] * q6[i]; then
-// sums[ln] += (w.d * a.d) * (f32)aux[ln] block by block, and the result is
-// ((((0 + sums[0]) + sums[1]) + ...) + sums[7]).  A CTA stages one block of
-// 32 rows and 64 positions: per (row, ln, s) the int16 pair
-// (scale_s * q6[16s + ln], scale_s * q6[16s + 8 + ln]) and per (position,
-// ln, s, s + 1) the four matching int8 activations, so one dp2a adds both
-// products of a (lane, sub-block) pair.  A thread owns 2 rows x 4 positions
-// and runs lane by lane: integer aux (exact in any order), then the f32
-// lane sums in block order.
-constexpr int K6_ROWS = 32;
-constexpr int K6_POS = 64;
-constexpr int K6_THREADS = 256;
-
-__global__ void __launch_bounds__(K6_THREADS) gemm_q6k_kernel(const uint8_t* __restrict__ W,
-                                                              const uint16_t* __restrict__ Wd, int rows, int nb,
-                                                              const int8_t* __restrict__ aq,
-                                                              const float* __restrict__ ad, int T,
-                                                              float* __restrict__ out, int out_ld, int epi,
-                                                              const float* __restrict__ bias, uint32_t* err) {
-  pdl_enter();
-  __shared__ __align__(16) int wp[8][16][K6_ROWS];      // [ln][s][row]: int16 pair
-  __shared__ __align__(16) int ap[8][8][K6_POS];        // [ln][s / 2][pos]: 4 x int8
-  __shared__ float sdw[K6_ROWS], sad[K6_POS];
-  const int tid = threadIdx.x;
-  const int r0 = blockIdx.x * K6_ROWS, p0 = blockIdx.y * K6_POS;
-  const int K = nb * 256;
-  const int rt = tid >> 4, pt = tid & 15;  // rows 2 rt .. + 1, positions 4 pt .. + 3
-  float sums[2][4][8];
-#pragma unroll
-  for (int r = 0; r < 2; r++)
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-#pragma unroll
-      for (int l = 0; l < 8; l++) sums[r][c][l] = 0.0f;
-
-  for (int b = 0; b < nb; b++) {
-    __syncthreads();  // previous block consumed
-    // weights: 32 rows x 128 (ln, s) pairs; thread: row tid >> 3, pairs (tid & 7) * 16 .. + 16
-    {
-      const int r = tid >> 3, pr0 = (tid & 7) * 16;
-      const bool ok = r0 + r < rows;
-      const uint8_t* body = W + ((size_t)(ok ? r0 + r : 0) * nb + b) * 208;
-#pragma unroll 4
-      for (int k = 0; k < 16; k++) {
-        const int pr = pr0 + k, ln = pr >> 4, sb = pr & 15;
-        int v = 0;
-        if (ok) {
-          const int scale = (int8_t)body[192 + sb];
-          const int lo = scale * q6k_quant(body, sb * 16 + ln), hi = scale * q6k_quant(body, sb * 16 + 8 + ln);
-          v = (int)(((uint32_t)lo & 0xffffu) | ((uint32_t)hi << 16));
-        }
-        wp[ln][sb][r] = v;
-      }
-      if (tid < K6_ROWS) sdw[tid] = r0 + tid < rows ? f16_bits_to_f32(Wd[(size_t)(r0 + tid) * nb + b]) : 0.0f;
-    }
-    // activations: 64 positions x 64 (ln, s-pair) words; thread: position tid >> 2, 16 words
-    {
-      const int p = tid >> 2, w0 = (tid & 3) * 16;
-      const int t = p0 + p;
-      const bool ok = t < T;
-      const int8_t* qa = aq + (size_t)(ok ? t : 0) * K + (size_t)b * 256;
-#pragma unroll 4
-      for (int k = 0; k < 16; k++) {
-        const int wi = w0 + k, ln = wi >> 3, s2 = wi & 7, s = 2 * s2;
-        uint32_t v = 0;
-        if (ok)
-          v = (uint32_t)(uint8_t)qa[s * 16 + ln] | ((uint32_t)(uint8_t)qa[s * 16 + 8 + ln] << 8) |
-              ((uint32_t)(uint8_t)qa[(s + 1) * 16 + ln] << 16) | ((uint32_t)(uint8_t)qa[(s + 1) * 16 + 8 + ln] << 24);
-        ap[ln][s2][p] = (int)v;
-      }
-      if (tid < K6_POS) sad[tid] = p0 + tid < T ? ad[(size_t)(p0 + tid) * nb + b] : 0.0f;
-    }
-    __syncthreads();
-    float dd[2][4];
-#pragma unroll
-    for (int r = 0; r < 2; r++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) dd[r][c] = fmul(sdw[2 * rt + r], sad[4 * pt + c]);
-#pragma unroll
-    for (int ln = 0; ln < 8; ln++) {
-      int aux[2][4];
-#pragma unroll
-      for (int r = 0; r < 2; r++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) aux[r][c] = 0;
-#pragma unroll
-      for (int s2 = 0; s2 < 8; s2++) {
-        const int2 w0 = *reinterpret_cast<const int2*>(&wp[ln][2 * s2][2 * rt]);
-        const int2 w1 = *reinterpret_cast<const int2*>(&wp[ln][2 * s2 + 1][2 * rt]);
-        const int4 a4 = *reinterpret_cast<const int4*>(&ap[ln][s2][4 * pt]);
-        const int av[4] = {a4.x, a4.y, a4.z, a4.w};
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          aux[0][c] = __dp2a_hi(w1.x, av[c], __dp2a_lo(w0.x, av[c], aux[0][c]));
-          aux[1][c] = __dp2a_hi(w1.y, av[c], __dp2a_lo(w0.y, av[c], aux[1][c]));
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < 2; r++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) sums[r][c][ln] = fadd(sums[r][c][ln], fmul(dd[r][c], __int2float_rn(aux[r][c])));
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    const int row = r0 + 2 * rt + r;
-    if (row >= rows) continue;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const int t = p0 + 4 * pt + c;
-      if (t >= T) continue;
-      float v = 0.0f;
-#pragma unroll
-      for (int l = 0; l < 8; l++) v = fadd(v, sums[r][c][l]);
-      if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-      float* dst = out + (size_t)t * out_ld + row;
-      if (epi == EPI_BIAS) {
-        v = fadd(v, bias[row]);
-        if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-      } else if (epi == EPI_RESIDUAL) {
-        v = fadd(*dst, v);
-        if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
-      }
-      *dst = v;
-    }
-  }
-}
-
 // ---- one position (decode) ---------------------------------------------------------
 // Up to three matrices that read the same activation (q, k, v or gate, up)
 // in one launch: segment i owns CTAs [cta0, next cta0).
@@ -793,15 +662,6 @@ cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const Dev
   return launch_gemv_kq_decode_segs(L, mm, 1, a, oo, ee, bb);
 }
 
-cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
-                            int epi, const float* bias) {
-  const dim3 grid((m.rows + K6_ROWS - 1) / K6_ROWS, (T + K6_POS - 1) / K6_POS);
-  const cudaError_t e = launch_k(L, gemm_q6k_kernel, grid, K6_THREADS, 0, (const uint8_t*)m.q, m.d, m.rows, m.nb,
-                                 a.qk_q, a.qk_d, T, out, out_ld, epi, bias, L.err);
-  if (e != cudaSuccess) return e;
-  if (L.launches) ++*L.launches;
-  return cudaGetLastError();
-}
 
 cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias) {

@@ -130,9 +130,6 @@ size_t q6k_tc_row_offset(int r0, int nb);  // r0 a multiple of 64
 cudaError_t launch_q6k_tc_repack(cudaStream_t st, const DevMatrix& m, uint8_t* out);
 cudaError_t launch_gemm_q6k_tc(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                                int epi, const float* bias);
-// Q6_K matrix, chunk of T > 16 positions (gemm_kq.cu)
-cudaError_t launch_gemm_q6k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
-                            int epi, const float* bias);
 // Q4_K / Q6_K matrix, one position (gemm_kq.cu); supported: every Q6_K, and
 // Q4_K rows of up to 64 super-blocks (K <= 16384)
 bool kq_decode_supported(const DevMatrix& m);

@@ -1135,8 +1135,7 @@ cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, i
   cudaError_t e = launch_gemv_fast(L, m, a, T, out, out_ld, epi, bias, &handled);
   if (handled || e != cudaSuccess) return e;
   if (m.type == GT_Q4_K && T > 16) return launch_gemm_q4k(L, m, a, T, out, out_ld, epi, bias);
-  if (m.type == GT_Q6_K && T > 16 && m.tc && a.qk_p) return launch_gemm_q6k_tc(L, m, a, T, out, out_ld, epi, bias);
-  if (m.type == GT_Q6_K && T > 16) return launch_gemm_q6k(L, m, a, T, out, out_ld, epi, bias);
+  if (m.type == GT_Q6_K && T > 16) return launch_gemm_q6k_tc(L, m, a, T, out, out_ld, epi, bias);
   if ((m.type == GT_Q4_K || m.type == GT_Q6_K) && T == 1 && kq_decode_supported(m))
     return launch_gemv_kq_decode(L, m, a, out, epi, bias);
   dim3 grid(T, (m.rows + 127) / 128);
