@@ -47,19 +47,32 @@ constexpr int KQ_E = 32;    // elements per stage: one Q4_K sub-block = one Q8A 
 constexpr int KQ_THREADS = 256;
 constexpr int KQ_WS = KQ_ROWS + 4;  // padded tile rows (floats)
 
-__global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const uint8_t* __restrict__ W, int rows, int nbs,
+// Up to three matrices that read the same activation (q / k / v, gate / up)
+// in one launch: segment i owns the row tiles from cta0[i] on (blockIdx.x).
+struct Q4Segs {
+  const uint8_t* W[3];
+  int rows[3], cta0[3], out_ld[3], epi[3];
+  float* out[3];
+  const float* bias[3];
+};
+
+__global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, int nbs,
                                                               const int8_t* __restrict__ aq,
-                                                              const float* __restrict__ ad, int T,
-                                                              float* __restrict__ out, int out_ld, int epi,
-                                                              const float* __restrict__ bias, float one,
+                                                              const float* __restrict__ ad, int T, float one,
                                                               uint32_t* err) {
   pdl_enter();
+  const int seg = (int)(blockIdx.x >= (unsigned)G.cta0[1]) + (int)(blockIdx.x >= (unsigned)G.cta0[2]);
+  const uint8_t* __restrict__ W = G.W[seg];
+  const int rows = G.rows[seg], out_ld = G.out_ld[seg], epi = G.epi[seg];
+  float* __restrict__ out = G.out[seg];
+  const float* __restrict__ bias = G.bias[seg];
+  const int tile = (int)blockIdx.x - G.cta0[seg];
   // two stage buffers: stage s + 1 is dequantised into one while the chains
   // run over the other, from raw bytes loaded into registers before stage s
   __shared__ __align__(16) float ws[2][KQ_E][KQ_WS];  // dequantised weights [element][row]
   __shared__ __align__(16) float as[2][KQ_E][KQ_WS];  // dequantised activations [element][position]
   const int tid = threadIdx.x;
-  const int r0 = blockIdx.x * KQ_ROWS, p0 = blockIdx.y * KQ_POS;
+  const int r0 = tile * KQ_ROWS, p0 = blockIdx.y * KQ_POS;
   const int nbk = nbs * 8;  // Q8A blocks per position
   // staging: row / position tid >> 2, elements 8 * (tid & 3) .. + 8
   const int sr = tid >> 2, se = 8 * (tid & 3);
@@ -663,14 +676,38 @@ cudaError_t launch_gemv_kq_decode(const Launch& L, const DevMatrix& m, const Dev
 }
 
 
-cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
-                            int epi, const float* bias) {
-  const dim3 grid((m.rows + KQ_ROWS - 1) / KQ_ROWS, (T + KQ_POS - 1) / KQ_POS);
-  const cudaError_t e = launch_k(L, gemm_q4k_kernel, grid, KQ_THREADS, 0, (const uint8_t*)m.q, m.rows, m.nb, a.qa_q,
-                                 a.qa_d, T, out, out_ld, epi, bias, 1.0f, L.err);
+cudaError_t launch_gemm_q4k_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a, int T,
+                                 float* const* out, const int* out_ld, const int* epi, const float* const* bias) {
+  if (n < 1 || n > 3) return cudaErrorInvalidValue;
+  Q4Segs G{};
+  int ctas = 0;
+  for (int i = 0; i < 3; i++) {
+    const int k = i < n ? i : n - 1;  // unused segments repeat the last one and own no tiles
+    if (m[k]->type != GT_Q4_K || m[k]->nb != m[0]->nb) return cudaErrorInvalidValue;
+    G.W[i] = static_cast<const uint8_t*>(m[k]->q);
+    G.rows[i] = m[k]->rows;
+    G.out[i] = out[k];
+    G.out_ld[i] = out_ld[k];
+    G.epi[i] = epi[k];
+    G.bias[i] = bias[k];
+    G.cta0[i] = i < n ? ctas : 1 << 30;
+    if (i < n) ctas += (m[k]->rows + KQ_ROWS - 1) / KQ_ROWS;
+  }
+  const dim3 grid(ctas, (T + KQ_POS - 1) / KQ_POS);
+  const cudaError_t e =
+      launch_k(L, gemm_q4k_kernel, grid, KQ_THREADS, 0, G, m[0]->nb, a.qa_q, a.qa_d, T, 1.0f, L.err);
   if (e != cudaSuccess) return e;
   if (L.launches) ++*L.launches;
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
+                            int epi, const float* bias) {
+  const DevMatrix* mm[1] = {&m};
+  float* const oo[1] = {out};
+  const int ll[1] = {out_ld}, ee[1] = {epi};
+  const float* const bb[1] = {bias};
+  return launch_gemm_q4k_segs(L, mm, 1, a, T, oo, ll, ee, bb);
 }
 
 }  // namespace det

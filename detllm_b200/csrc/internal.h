@@ -122,6 +122,10 @@ cudaError_t launch_quant_q8k(const Launch& L, const float* x, int K, int T, floa
 // Q4_K matrix, chunk of T > 16 positions (gemm_kq.cu)
 cudaError_t launch_gemm_q4k(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,
                             int epi, const float* bias);
+// up to three Q4_K matrices of equal width that read the same activation
+// (q / k / v, gate / up), chunk of T > 16 positions, one launch
+cudaError_t launch_gemm_q4k_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a, int T,
+                                 float* const* out, const int* out_ld, const int* epi, const float* const* bias);
 // Q6_K matrix, chunk of T > 16 positions, on int8 tensor cores
 // (gemm_q6k_tc.cu): needs m.tc (q6k_tc_repack at load) and a.qk_p
 size_t q6k_tc_bytes(int rows, int nb);

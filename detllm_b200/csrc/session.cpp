@@ -237,6 +237,26 @@ cudaError_t gemm_fused(det_session* s, int tag, const Launch& L, const DevMatrix
   return timed_gemm(s, tag, W, T, ob, [&] { return launch_gemm_mma16(L, W, a, T, o); });
 }
 
+// Q4_K matrices of one width that read the same activation, as one chunk
+// launch (T > 16)
+bool q4k_chunk_fusable(const DevMatrix* const* m, int n) {
+  for (int i = 0; i < n; i++)
+    if (m[i]->type != GT_Q4_K || m[i]->nb != m[0]->nb || m[i]->rows == 0) return false;
+  return true;
+}
+
+// one chunk launch over q4k_chunk_fusable matrices
+cudaError_t gemm_q4k_segs(det_session* s, int tag, const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
+                          int T, float* const* out, const int* ld, const int* epi, const float* const* bias) {
+  double wb = 0, ob = 0;
+  for (int i = 0; i < n; i++) {
+    wb += (double)m[i]->rows * m[i]->cols * bytes_per_weight(m[i]->type);
+    ob += (double)T * m[i]->rows * (epi[i] == EPI_RESIDUAL ? 8.0 : 4.0);
+  }
+  const double ab = (double)T * m[0]->cols * (1.0 + 4.0 / 32.0);
+  return timed(s, tag, wb + ab + ob, wb, [&] { return launch_gemm_q4k_segs(L, m, n, a, T, out, ld, epi, bias); });
+}
+
 // Matrices that read the same activation (q / k / v, gate / up) and can run
 // as one one-position launch: Q4_K or Q6_K, all of one type and width.
 bool kq_fusable(const DevMatrix* const* m, int n) {
@@ -337,6 +357,12 @@ det_status fwd_attention(det_session* s, const Launch& L, int l, int T) {
     const int ee[3] = {W.bq ? EPI_BIAS : EPI_STORE, W.bk ? EPI_BIAS : EPI_STORE, W.bv ? EPI_BIAS : EPI_STORE};
     const float* const bb[3] = {W.bq, W.bk, W.bv};
     CK(gemv_segs(s, PT_GEMM_QKV, L, mq, 3, a, oo, ee, bb));
+  } else if (T > 16 && q4k_chunk_fusable(mq, 3)) {
+    float* const oo[3] = {s->q, s->k, s->v};
+    const int ll[3] = {qd, kvd, kvd};
+    const int ee[3] = {W.bq ? EPI_BIAS : EPI_STORE, W.bk ? EPI_BIAS : EPI_STORE, W.bv ? EPI_BIAS : EPI_STORE};
+    const float* const bb[3] = {W.bq, W.bk, W.bv};
+    CK(gemm_q4k_segs(s, PT_GEMM_QKV, L, mq, 3, a, T, oo, ll, ee, bb));
   } else {
     CK(gemv(s, PT_GEMM_QKV, L, W.wq, a, T, s->q, qd, W.bq ? EPI_BIAS : EPI_STORE, W.bq));
     CK(gemv(s, PT_GEMM_QKV, L, W.wk, a, T, s->k, kvd, W.bk ? EPI_BIAS : EPI_STORE, W.bk));
@@ -389,6 +415,11 @@ det_status fwd_ffn_in(det_session* s, const Launch& L, int l, int T, int* have_o
     const int ee[2] = {EPI_STORE, EPI_STORE};
     const float* const bb[2] = {nullptr, nullptr};
     CK(gemv_segs(s, PT_GEMM_GATE_UP, L, mg, 2, a, oo, ee, bb));
+  } else if (T > 16 && q4k_chunk_fusable(mg, 2)) {
+    float* const oo[2] = {s->gate, s->up};
+    const int ll[2] = {c.dff, c.dff}, ee[2] = {EPI_STORE, EPI_STORE};
+    const float* const bb[2] = {nullptr, nullptr};
+    CK(gemm_q4k_segs(s, PT_GEMM_GATE_UP, L, mg, 2, a, T, oo, ll, ee, bb));
   } else {
     CK(gemv(s, PT_GEMM_GATE_UP, L, W.gate, a, T, s->gate, c.dff, EPI_STORE, nullptr));
     CK(gemv(s, PT_GEMM_GATE_UP, L, W.up, a, T, s->up, c.dff, EPI_STORE, nullptr));
