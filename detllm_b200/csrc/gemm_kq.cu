@@ -62,11 +62,14 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, in
                                                               uint32_t* err) {
   pdl_enter();
   const int seg = (int)(blockIdx.x >= (unsigned)G.cta0[1]) + (int)(blockIdx.x >= (unsigned)G.cta0[2]);
-  const uint8_t* __restrict__ W = G.W[seg];
-  const int rows = G.rows[seg], out_ld = G.out_ld[seg], epi = G.epi[seg];
-  float* __restrict__ out = G.out[seg];
-  const float* __restrict__ bias = G.bias[seg];
-  const int tile = (int)blockIdx.x - G.cta0[seg];
+  // constant indices only (a runtime index would copy G to local memory)
+#define KQ_PICK(f) (seg == 0 ? G.f[0] : (seg == 1 ? G.f[1] : G.f[2]))
+  const uint8_t* __restrict__ W = KQ_PICK(W);
+  const int rows = KQ_PICK(rows), out_ld = KQ_PICK(out_ld), epi = KQ_PICK(epi);
+  float* __restrict__ out = KQ_PICK(out);
+  const float* __restrict__ bias = KQ_PICK(bias);
+  const int tile = (int)blockIdx.x - KQ_PICK(cta0);
+#undef KQ_PICK
   // two stage buffers: stage s + 1 is dequantised into one while the chains
   // run over the other, from raw bytes loaded into registers before stage s
   __shared__ __align__(16) float ws[2][KQ_E][KQ_WS];  // dequantised weights [element][row]
