@@ -26,14 +26,16 @@ the 8 segments are covered in turn.
   (every later window forwards the same 8,192 positions: 2,048 replayed,
   6,144 coded), as the reference's bench-file estimate scales a prefix
   (xtask/src/main.rs:2295-2325).
-* roofline: the headline model's decode weight GEMVs (one token per forward):
-  one token's weight GEMV launches back to back in a CUDA graph
-  (programmatic dependent launch), algorithmic bytes (weights + quantised
-  activations + outputs) / CUDA-event time, against the measured HBM copy
-  bandwidth in MEASURED_PEAKS.json.
-* roofline_encode: the encode step's dominant kernel (the Q4_K chunk GEMM),
-  against the FP32 pipe it is bound by (the reference's one ordered f32
-  chain per row: 2 rounded ops per weight per position).
+* roofline: the encode step's dominant kernel, the Q4_K chunk GEMM (q|k|v,
+  o, gate|up: two thirds of the step), against the FP32 pipe that bounds it
+  (the reference's one ordered f32 chain per row: 2 rounded ops per weight
+  per position; peak = 148 SMs x 128 lanes x the SM clock measured during
+  the timed region, since no FP32 peak is measured by the driver).
+* roofline_decode: the headline model's decode weight GEMVs (one token per
+  forward), the north-star HBM target: one token's weight GEMV launches back
+  to back in a CUDA graph (programmatic dependent launch), algorithmic bytes
+  (weights + quantised activations + outputs) / CUDA-event time, against
+  the measured HBM copy bandwidth in MEASURED_PEAKS.json.
 * configs: BASELINE configs 2-4 at N = 1 (TinyLlama Q8_0 at chunk 1024 and at
   the configuration's literal chunk 64; TinyLlama Q4_K_M compress and
   decompress of Markov bytes; Qwen2.5-0.5B with V 151,936).
@@ -536,9 +538,9 @@ def run(args):
         "e2e": {"value": total / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": st.h2d_bytes // max(args.steps, 1),
                 "d2h_bytes_per_step": st.d2h_bytes // max(args.steps, 1)},
         "gpu_launches": int(st.launches),
-        "roofline": decode_roofline(dec, HEADLINE, peak, peak_kind),
-        "roofline_encode": encode_roofline(kprof, 2.0 * q4k_weight_positions(spec, PREFIX), clocks.get("sm_mhz"),
-                                           props.multi_processor_count),
+        "roofline": encode_roofline(kprof, 2.0 * q4k_weight_positions(spec, PREFIX), clocks.get("sm_mhz"),
+                                    props.multi_processor_count),
+        "roofline_decode": decode_roofline(dec, HEADLINE, peak, peak_kind),
         "full_stream": full_stream_estimate(len(segs[0]), HEAD_CTX, dev_max / args.steps, ws),
         "decode": dec,
         "round_trip_ok": round_trip_ok,
