@@ -132,7 +132,9 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, in
       for (int k = 0; k < 8; k++) {
         const uint32_t word = k < 4 ? qv.x : qv.y;
         const int q = (int)((word >> (8 * (k & 3) + sh)) & 0x0fu);
-        ws[buf][se + k][sr] = fsub(fmul(dsc, (float)q), dmn);
+        // (d*sc)*q is exact (17 + 4 significant bits), so the fused form
+        // rounds once, exactly where the reference's subtraction does
+        ws[buf][se + k][sr] = __fmaf_rn(dsc, (float)q, -dmn);
       }
     } else {
 #pragma unroll
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(G4_BLOCK) gemv_q4k_chain_kernel(KqSegs S, cons
   if (warp < 0 && !chain) return;  // staging warps: done
 
   if (warp >= 0) {
-    const unsigned long long one2 = pk2(S.one, S.one), nmag2 = pk2(-8388608.0f, -8388608.0f);
+    const unsigned long long nmag2 = pk2(-8388608.0f, -8388608.0f);
     for (int s = 0; s < nbs; s++) {
       issue(s + G4_PREF);
       g4_cp_wait<G4_PREF>();  // this thread's copies of stage s have landed
@@ -390,10 +392,12 @@ __global__ void __launch_bounds__(G4_BLOCK) gemv_q4k_chain_kernel(KqSegs S, cons
         const float m2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542));
         const float m3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543));
         const float4 a = av[k];
-        // w = (d*sc)*q - (dmin*m) as fma(p, one, -dmn) (one == 1.0 at run
-        // time: exact, and not contractible with the multiply), then w * act
-        const unsigned long long w01 = fma2(mul2(dsc2, add2(pk2(m0, m1), nmag2)), one2, ndmn2);
-        const unsigned long long w23 = fma2(mul2(dsc2, add2(pk2(m2, m3), nmag2)), one2, ndmn2);
+        // w = (d*sc)*q - (dmin*m): d*sc and q have at most 17 and 4
+        // significant bits, so the product is exact and one fused
+        // multiply-add rounds exactly where the reference's subtraction
+        // does; then w * act
+        const unsigned long long w01 = fma2(dsc2, add2(pk2(m0, m1), nmag2), ndmn2);
+        const unsigned long long w23 = fma2(dsc2, add2(pk2(m2, m3), nmag2), ndmn2);
         const float2 r01 = up2(mul2(w01, pk2(a.x, a.y)));
         const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
         *reinterpret_cast<float4*>(dst + 4 * k) = make_float4(r01.x, r01.y, r23.x, r23.y);
