@@ -221,12 +221,16 @@ def decode_probe(model, vocab, n_ctx, n_prefix=1024, n_steps=48):
         out["tokens_per_s"] = n_steps / (st.forward_ms / 1000.0)
         out["ms_per_token"] = st.forward_ms / n_steps
         D.set_profiling(True)
+        model.profile(reset=True)
         for _ in range(n_steps):
             s.forward(tokens[pos:pos + 1], pos)
             pos += 1
         D.set_profiling(False)
         pr = s.stats(reset=True)
         gms, gbytes = s.gemv_stream(20)
+    # per-kernel-group device time of one token (the profiled pass)
+    out["kernels_us_per_token"] = {k: round(1000.0 * ms / n_steps, 2)
+                                   for k, (n, ms) in model.profile(reset=True).items() if n}
     out["fused"] = int(pr.gemm_launches) == n_steps  # one GEMM-accounted launch per token
     out["gemv_launches_per_token"] = int(pr.gemm_launches) // n_steps
     out["gemv_ms_per_token"] = pr.gemm_ms / n_steps
