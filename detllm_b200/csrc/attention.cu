@@ -273,6 +273,81 @@ __global__ void attn_softmax_kernel(float* __restrict__ S, const int* pos0p, int
   for (int j = len + lane; j < zend; j += 32) s[j] = 0.0f;
 }
 
+// Long rows (a window of thousands of keys): the staged kernel would hold a
+// whole row in shared memory per warp and keep the SM nearly empty.  Here a
+// warp owns a row in global memory (L2): a max pass, then blocks of 256
+// elements in which lane l computes e_j for j = base + 32k + 8(l >> 3) +
+// (l & 7), k < 8, and writes it back in place; lane c < 8 runs the ordered
+// z chain of class c (j = c, c + 8, ...) by taking the class's values from
+// lanes c + 8, c + 16, c + 24 with shuffles, in increasing j; then
+// p_j = e_j / z in place and zeros to the end of the PV tile.  Elements past
+// the row add +0 to a chain, which leaves it unchanged.
+constexpr int SL_WARPS = 8;
+
+__global__ void __launch_bounds__(SL_WARPS * 32) attn_softmax_long_kernel(float* __restrict__ S, const int* pos0p,
+                                                                          int T, int n_head, int s_ld, uint32_t* err) {
+  pdl_enter();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * SL_WARPS + warp;
+  if (row >= T * n_head) return;
+  const int t = row / n_head;
+  const int len = *pos0p + t + 1;
+  if (len == 1) return;
+  float* s = S + (size_t)row * s_ld;
+  // max (order-free); rows start 128-byte aligned (s_ld is a multiple of 32)
+  float mx = -INFINITY;
+  const int n4 = len >> 2;
+  const float4* s4 = reinterpret_cast<const float4*>(s);
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = s4[i];
+    mx = fmaxf(fmaxf(mx, v.x), fmaxf(fmaxf(v.y, v.z), v.w));
+  }
+  for (int j = 4 * n4 + lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  // e_j in place, and the eight ordered z chains (sum_f32_ref)
+  float acc = 0.0f;
+  const int jl = 8 * (lane >> 3) + (lane & 7);  // this lane's offset within each 32-element slice
+  for (int base = 0; base < len; base += 256) {
+    float e[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int j = base + 32 * k + jl;
+      e[k] = 0.0f;
+      if (j < len) {
+        const float d = fsub(s[j], mx);
+        e[k] = expf_det(d > -88.0f ? d : -88.0f);
+        s[j] = e[k];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const float e1 = __shfl_down_sync(0xffffffffu, e[k], 8);
+      const float e2 = __shfl_down_sync(0xffffffffu, e[k], 16);
+      const float e3 = __shfl_down_sync(0xffffffffu, e[k], 24);
+      acc = fadd(acc, e[k]);
+      acc = fadd(acc, e1);
+      acc = fadd(acc, e2);
+      acc = fadd(acc, e3);
+    }
+  }
+  float l8[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) l8[k] = __shfl_sync(0xffffffffu, acc, k);
+  const float z = finish8(l8);
+  if (!finite(z) || z == 0.0f) {
+    if (lane == 0) atomicOr(err, ERRF_NONFINITE);
+    return;
+  }
+  __syncwarp();  // every lane's e_j stores precede the reads below
+  for (int j = lane; j < len; j += 32) {
+    const float p = fdiv(s[j], z);
+    if (!finite(p)) atomicOr(err, ERRF_NONFINITE);
+    s[j] = p;
+  }
+  const int zend = min(s_ld, (len + 31 + 31) & ~31);
+  for (int j = len + lane; j < zend; j += 32) s[j] = 0.0f;
+}
+
 // ---- P x V ----------------------------------------------------------------------
 // P and V tiles of PV_KEYS keys are double-buffered in shared memory with
 // cp.async; P stays row-major, so one 16-byte load gives 4 keys of a row.
@@ -570,7 +645,7 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
     if (L.launches) *L.launches += 3;
     return cudaGetLastError();
   }
-  if (s_ld <= SM_SMEM_FLOATS) {
+  if (rpc >= 4) {  // rows short enough to stage four per CTA in shared memory
     {
       const cudaError_t e_ = launch_k(L, attn_softmax_kernel<true>, (rows + rpc - 1) / rpc, rpc * 32,
           (size_t)rpc * s_ld * sizeof(float),  S, pos0, T, n_head, s_ld, rpc, L.err);
@@ -578,8 +653,8 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
     }
   } else {
     {
-      const cudaError_t e_ = launch_k(L, attn_softmax_kernel<false>, (rows + 3) / 4, 4 * 32, 0, S, pos0, T, n_head,
-          s_ld, 4, L.err);
+      const cudaError_t e_ = launch_k(L, attn_softmax_long_kernel, (rows + SL_WARPS - 1) / SL_WARPS, SL_WARPS * 32, 0,
+                                      S, pos0, T, n_head, s_ld, L.err);
       if (e_ != cudaSuccess) return e_;
     }
   }

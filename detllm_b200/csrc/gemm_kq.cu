@@ -56,7 +56,7 @@ struct Q4Segs {
   const float* bias[3];
 };
 
-__global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, int nbs,
+__global__ void __launch_bounds__(KQ_THREADS, 5) gemm_q4k_kernel(const Q4Segs G, int nbs,
                                                               const int8_t* __restrict__ aq,
                                                               const float* __restrict__ ad, int T, float one,
                                                               uint32_t* err) {
@@ -134,21 +134,21 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, in
         const int q = (int)((word >> (8 * (k & 3) + sh)) & 0x0fu);
         // (d*sc)*q is exact (17 + 4 significant bits), so the fused form
         // rounds once, exactly where the reference's subtraction does
-        ws[buf][se + k][sr] = __fmaf_rn(dsc, (float)q, -dmn);
+        ws[buf][se + k][sr ^ se] = __fmaf_rn(dsc, (float)q, -dmn);
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; k++) ws[buf][se + k][sr] = 0.0f;
+      for (int k = 0; k < 8; k++) ws[buf][se + k][sr ^ se] = 0.0f;
     }
     if (pos_ok) {
 #pragma unroll
       for (int k = 0; k < 8; k++) {
         const uint32_t word = k < 4 ? qa.x : qa.y;
-        as[buf][se + k][sr] = fmul(a_d, (float)(int8_t)(word >> (8 * (k & 3))));
+        as[buf][se + k][sr ^ se] = fmul(a_d, (float)(int8_t)(word >> (8 * (k & 3))));
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; k++) as[buf][se + k][sr] = 0.0f;
+      for (int k = 0; k < 8; k++) as[buf][se + k][sr ^ se] = 0.0f;
     }
   };
 
@@ -161,8 +161,11 @@ __global__ void __launch_bounds__(KQ_THREADS) gemm_q4k_kernel(const Q4Segs G, in
     if (st + 1 < nst) load(st + 1);  // in flight while the chains run
 #pragma unroll 8
     for (int e = 0; e < KQ_E; e++) {
-      const float4 w4 = *reinterpret_cast<const float4*>(&ws[buf][e][rt * 4]);
-      const float4 a4 = *reinterpret_cast<const float4*>(&as[buf][e][pt * 4]);
+      // rows / positions of element e are stored XOR 8 * (e / 8) (bank
+      // spread for the staging stores; 4-row groups stay contiguous)
+      const int sw = (e >> 3) << 3;
+      const float4 w4 = *reinterpret_cast<const float4*>(&ws[buf][e][(rt * 4) ^ sw]);
+      const float4 a4 = *reinterpret_cast<const float4*>(&as[buf][e][(pt * 4) ^ sw]);
       const float wr[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
       for (int r = 0; r < 4; r++) {
