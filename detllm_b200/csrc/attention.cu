@@ -298,6 +298,7 @@ __global__ void __launch_bounds__(SL_WARPS * 32) attn_softmax_long_kernel(float*
   float mx = -INFINITY;
   const int n4 = len >> 2;
   const float4* s4 = reinterpret_cast<const float4*>(s);
+#pragma unroll 4
   for (int i = lane; i < n4; i += 32) {
     const float4 v = s4[i];
     mx = fmaxf(fmaxf(mx, v.x), fmaxf(fmaxf(v.y, v.z), v.w));
@@ -305,19 +306,28 @@ __global__ void __launch_bounds__(SL_WARPS * 32) attn_softmax_long_kernel(float*
   for (int j = 4 * n4 + lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   // e_j in place, and the eight ordered z chains (sum_f32_ref)
+  // (lane = 8 (lane >> 3) + (lane & 7): element base + 32 k + lane is of
+  // class lane & 7; the loads of a block are issued before any store)
   float acc = 0.0f;
-  const int jl = 8 * (lane >> 3) + (lane & 7);  // this lane's offset within each 32-element slice
   for (int base = 0; base < len; base += 256) {
     float e[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      const int j = base + 32 * k + jl;
-      e[k] = 0.0f;
+      const int j = base + 32 * k + lane;
+      e[k] = j < len ? s[j] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int j = base + 32 * k + lane;
       if (j < len) {
-        const float d = fsub(s[j], mx);
+        const float d = fsub(e[k], mx);
         e[k] = expf_det(d > -88.0f ? d : -88.0f);
-        s[j] = e[k];
       }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int j = base + 32 * k + lane;
+      if (j < len) s[j] = e[k];
     }
 #pragma unroll
     for (int k = 0; k < 8; k++) {
@@ -339,11 +349,25 @@ __global__ void __launch_bounds__(SL_WARPS * 32) attn_softmax_long_kernel(float*
     return;
   }
   __syncwarp();  // every lane's e_j stores precede the reads below
-  for (int j = lane; j < len; j += 32) {
-    const float p = fdiv(s[j], z);
-    if (!finite(p)) atomicOr(err, ERRF_NONFINITE);
-    s[j] = p;
+  bool bad = false;
+  for (int base = 0; base < len; base += 256) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int j = base + 32 * k + lane;
+      v[k] = j < len ? s[j] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int j = base + 32 * k + lane;
+      if (j < len) {
+        const float p = fdiv(v[k], z);
+        bad |= !finite(p);
+        s[j] = p;
+      }
+    }
   }
+  if (bad) atomicOr(err, ERRF_NONFINITE);
   const int zend = min(s_ld, (len + 31 + 31) & ~31);
   for (int j = len + lane; j < zend; j += 32) s[j] = 0.0f;
 }
