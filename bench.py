@@ -70,6 +70,11 @@ METRIC = "encode tokens/s (logits+CDF+code)"
 # (profiles/gemv_decode_stream_tinyllama_q8_0_1token_traffic.md)
 DECODE_GEMV_TRAFFIC_PER_LAUNCH = {"tinyllama-q8_0": 12.400e6}
 FP32_LANES_PER_SM = 128
+# DRAM bytes (read + write) of one fused gate|up Q4_K chunk launch of the
+# headline model (28,672 rows x K 4,096 x 1,024 positions), from one ncu
+# capture (profiles/gemm_q4k_llama3_8b_q4_k_gate_up_T1024.md); the
+# algorithmic bytes of that launch are 188.2 MB
+ENCODE_Q4K_TRAFFIC_PER_LAUNCH = 102.500e6 + 85.558e6
 
 
 def log(*a):
@@ -265,7 +270,10 @@ def encode_roofline(kprof, ops, sm_mhz, n_sms):
     peak = n_sms * FP32_LANES_PER_SM * sm_mhz * 1e6 / 1e12
     achieved = ops / (ms / 1000.0) / 1e12
     return {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "T lane-ops/s", "frac": achieved / peak,
-            "traffic": None, "kernel": "gemm_q4k_kernel (Q4_K x Q8A chunk GEMMs: q|k|v, o, gate|up of one step)",
+            "traffic": ENCODE_Q4K_TRAFFIC_PER_LAUNCH,
+            "traffic_unit": "DRAM bytes of one fused gate|up launch (ncu capture, see profiles/); "
+                            "its algorithmic bytes are 188.2 MB",
+            "kernel": "gemm_q4k_kernel (Q4_K x Q8A chunk GEMMs: q|k|v, o, gate|up of one step)",
             "peak_kind": f"nominal: {n_sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x measured {sm_mhz:.0f} MHz",
             "launches": n, "ms": ms, "ops": ops}
 
