@@ -42,7 +42,9 @@ DI float2 madd2(float w, float a0, float a1, float one, float2 acc) {
 }
 
 constexpr int KQ_ROWS = 64;
+constexpr int KQ_POS = 64;  // one Q8A group
 constexpr int KQ_E = 32;    // elements per stage: one Q4_K sub-block = one Q8A block
+constexpr int KQ_THREADS = 256;
 constexpr int KQ_WS = KQ_ROWS + 4;  // padded tile rows (floats)
 
 // Up to three matrices that read the same activation (q / k / v, gate / up)
@@ -54,21 +56,10 @@ struct Q4Segs {
   const float* bias[3];
 };
 
-// A CTA owns 64 rows x POS positions (POS = 64: 256 threads; POS = 32: 128
-// threads, for matrices whose 64-position tiles would leave a mostly empty
-// last wave).  Each thread runs 4 rows x 4 positions = 16 chains.
-template <int POS>
-struct KqShape {
-  static constexpr int THREADS = POS * 4;
-  static constexpr int RSLOTS = KQ_ROWS * 4 / THREADS;  // weight staging slots per thread
-  static constexpr int MIN_CTAS = POS == 64 ? 5 : 8;    // resident CTAs per SM (registers, shared memory)
-};
-
-template <int POS>
-__global__ void __launch_bounds__(KqShape<POS>::THREADS, KqShape<POS>::MIN_CTAS)
-    gemm_q4k_kernel(const Q4Segs G, int nbs, const int8_t* __restrict__ aq, const float* __restrict__ ad, int T,
-                    float one, uint32_t* err) {
-  using Sh = KqShape<POS>;
+__global__ void __launch_bounds__(KQ_THREADS, 5) gemm_q4k_kernel(const Q4Segs G, int nbs,
+                                                              const int8_t* __restrict__ aq,
+                                                              const float* __restrict__ ad, int T, float one,
+                                                              uint32_t* err) {
   pdl_enter();
   const int seg = (int)(blockIdx.x >= (unsigned)G.cta0[1]) + (int)(blockIdx.x >= (unsigned)G.cta0[2]);
   // constant indices only (a runtime index would copy G to local memory)
@@ -81,106 +72,83 @@ __global__ void __launch_bounds__(KqShape<POS>::THREADS, KqShape<POS>::MIN_CTAS)
 #undef KQ_PICK
   // two stage buffers: stage s + 1 is dequantised into one while the chains
   // run over the other, from raw bytes loaded into registers before stage s
-  __shared__ __align__(16) float ws[2][KQ_E][KQ_WS];    // dequantised weights [element][row]
-  __shared__ __align__(16) float as[2][KQ_E][POS + 4];  // dequantised activations [element][position]
+  __shared__ __align__(16) float ws[2][KQ_E][KQ_WS];  // dequantised weights [element][row]
+  __shared__ __align__(16) float as[2][KQ_E][KQ_WS];  // dequantised activations [element][position]
   const int tid = threadIdx.x;
-  const int r0 = tile * KQ_ROWS, p0 = blockIdx.y * POS;
+  const int r0 = tile * KQ_ROWS, p0 = blockIdx.y * KQ_POS;
   const int nbk = nbs * 8;  // Q8A blocks per position
-  // staging: elements 8 * (tid & 3) .. + 8 of rows (tid >> 2) + k * THREADS / 4
-  // and of position tid >> 2
-  const int se = 8 * (tid & 3);
-  int srow[Sh::RSLOTS];
-  bool row_ok[Sh::RSLOTS];
-  const uint8_t* wrow[Sh::RSLOTS];
-#pragma unroll
-  for (int k = 0; k < Sh::RSLOTS; k++) {
-    srow[k] = (tid >> 2) + k * (Sh::THREADS / 4);
-    row_ok[k] = r0 + srow[k] < rows;
-    wrow[k] = W + (size_t)(row_ok[k] ? r0 + srow[k] : 0) * nbs * 144;
-  }
-  const int sp = tid >> 2;
-  const int t_st = p0 + sp;
+  // staging: row / position tid >> 2, elements 8 * (tid & 3) .. + 8
+  const int sr = tid >> 2, se = 8 * (tid & 3);
+  const bool row_ok = r0 + sr < rows;
+  const int t_st = p0 + sr;
   const bool pos_ok = t_st < T;
+  const uint8_t* wrow = W + (size_t)(row_ok ? r0 + sr : 0) * nbs * 144;
   // compute: rows rt * 4 .. + 3, positions pt * 4 .. + 3
-  const int rt = tid / (POS / 4), pt = tid % (POS / 4);
+  const int rt = tid >> 4, pt = tid & 15;
   float2 acc[4][2];
 #pragma unroll
   for (int r = 0; r < 4; r++) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
 
   // raw bytes of stage st (super-block st >> 3, sub-block st & 7)
-  uint4 hdr[Sh::RSLOTS];  // the current super-block's d, dmin and scales
-  uint2 qv[Sh::RSLOTS], qa = make_uint2(0, 0);
+  uint4 hdr = make_uint4(0, 0, 0, 0);  // the current super-block's d, dmin and scales
+  uint2 qv = make_uint2(0, 0), qa = make_uint2(0, 0);
   float a_d = 0.0f;
-#pragma unroll
-  for (int k = 0; k < Sh::RSLOTS; k++) {
-    hdr[k] = make_uint4(0, 0, 0, 0);
-    qv[k] = make_uint2(0, 0);
-  }
   auto load = [&](int st) {
     const int b = st >> 3, sub = st & 7;
-#pragma unroll
-    for (int k = 0; k < Sh::RSLOTS; k++)
-      if (row_ok[k]) {
-        const uint8_t* blk = wrow[k] + (size_t)b * 144;
-        if (sub == 0) hdr[k] = *reinterpret_cast<const uint4*>(blk);
-        qv[k] = *reinterpret_cast<const uint2*>(blk + 16 + (sub >> 1) * 32 + se);
-      }
+    if (row_ok) {
+      const uint8_t* blk = wrow + (size_t)b * 144;
+      if (sub == 0) hdr = *reinterpret_cast<const uint4*>(blk);
+      qv = *reinterpret_cast<const uint2*>(blk + 16 + (sub >> 1) * 32 + se);
+    }
     if (pos_ok) {
       const int kb = b * 8 + sub;
       a_d = ad[q8a_dslot(nbk, t_st, kb)];
       qa = *reinterpret_cast<const uint2*>(aq + q8a_slot(nbk, t_st, kb) * 32 + (se ^ q8a_swz(t_st)));
     }
   };
-  // w = (d * sc) * q - dmin * m and a.d * a.q, with the reference's rounding;
-  // the rows / positions of element e are stored XOR 8 * (e / 8) (bank
-  // spread for these stores; 4-row groups stay contiguous)
+  // w = (d * sc) * q - dmin * m and a.d * a.q, with the reference's rounding
   auto dequant = [&](int st, int buf) {
     const int sub = st & 7;
-#pragma unroll
-    for (int k = 0; k < Sh::RSLOTS; k++) {
-      const int sr = srow[k];
-      if (row_ok[k]) {
-        const uint4 h = hdr[k];
-        const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
-        const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
-        // get_scale_min_k4 (det-quant lib.rs:506-518) on the scale bytes
-        // held in h.y .. h.w (bytes 4..15 of the block)
-        auto sbyte = [&](int i) -> int {
-          const uint32_t w = i < 4 ? h.y : (i < 8 ? h.z : h.w);
-          return (int)((w >> (8 * (i & 3))) & 0xffu);
-        };
-        int sc, mn;
-        if (sub < 4) {
-          sc = sbyte(sub) & 0x3f;
-          mn = sbyte(sub + 4) & 0x3f;
-        } else {
-          sc = (sbyte(sub + 4) & 0x0f) | ((sbyte(sub - 4) >> 6) << 4);
-          mn = (sbyte(sub + 4) >> 4) | ((sbyte(sub) >> 6) << 4);
-        }
-        const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-        const int sh = (sub & 1) * 4;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const uint32_t word = i < 4 ? qv[k].x : qv[k].y;
-          const int q = (int)((word >> (8 * (i & 3) + sh)) & 0x0fu);
-          // (d*sc)*q is exact (17 + 4 significant bits), so the fused form
-          // rounds once, exactly where the reference's subtraction does
-          ws[buf][se + i][sr ^ se] = __fmaf_rn(dsc, (float)q, -dmn);
-        }
+    if (row_ok) {
+      const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffffu));
+      const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+      // get_scale_min_k4 (det-quant lib.rs:506-518) on the scale bytes
+      // held in hdr.y .. hdr.w (bytes 4..15 of the block)
+      auto sbyte = [&](int k) -> int {
+        const uint32_t w = k < 4 ? hdr.y : (k < 8 ? hdr.z : hdr.w);
+        return (int)((w >> (8 * (k & 3))) & 0xffu);
+      };
+      int sc, mn;
+      if (sub < 4) {
+        sc = sbyte(sub) & 0x3f;
+        mn = sbyte(sub + 4) & 0x3f;
       } else {
-#pragma unroll
-        for (int i = 0; i < 8; i++) ws[buf][se + i][sr ^ se] = 0.0f;
+        sc = (sbyte(sub + 4) & 0x0f) | ((sbyte(sub - 4) >> 6) << 4);
+        mn = (sbyte(sub + 4) >> 4) | ((sbyte(sub) >> 6) << 4);
       }
-    }
-    if (pos_ok) {
+      const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+      const int sh = (sub & 1) * 4;
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t word = i < 4 ? qa.x : qa.y;
-        as[buf][se + i][sp ^ se] = fmul(a_d, (float)(int8_t)(word >> (8 * (i & 3))));
+      for (int k = 0; k < 8; k++) {
+        const uint32_t word = k < 4 ? qv.x : qv.y;
+        const int q = (int)((word >> (8 * (k & 3) + sh)) & 0x0fu);
+        // (d*sc)*q is exact (17 + 4 significant bits), so the fused form
+        // rounds once, exactly where the reference's subtraction does
+        ws[buf][se + k][sr ^ se] = __fmaf_rn(dsc, (float)q, -dmn);
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; i++) as[buf][se + i][sp ^ se] = 0.0f;
+      for (int k = 0; k < 8; k++) ws[buf][se + k][sr ^ se] = 0.0f;
+    }
+    if (pos_ok) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const uint32_t word = k < 4 ? qa.x : qa.y;
+        as[buf][se + k][sr ^ se] = fmul(a_d, (float)(int8_t)(word >> (8 * (k & 3))));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) as[buf][se + k][sr ^ se] = 0.0f;
     }
   };
 
@@ -193,6 +161,8 @@ __global__ void __launch_bounds__(KqShape<POS>::THREADS, KqShape<POS>::MIN_CTAS)
     if (st + 1 < nst) load(st + 1);  // in flight while the chains run
 #pragma unroll 8
     for (int e = 0; e < KQ_E; e++) {
+      // rows / positions of element e are stored XOR 8 * (e / 8) (bank
+      // spread for the staging stores; 4-row groups stay contiguous)
       const int sw = (e >> 3) << 3;
       const float4 w4 = *reinterpret_cast<const float4*>(&ws[buf][e][(rt * 4) ^ sw]);
       const float4 a4 = *reinterpret_cast<const float4*>(&as[buf][e][(pt * 4) ^ sw]);
@@ -733,27 +703,9 @@ cudaError_t launch_gemm_q4k_segs(const Launch& L, const DevMatrix* const* m, int
     G.cta0[i] = i < n ? ctas : 1 << 30;
     if (i < n) ctas += (m[k]->rows + KQ_ROWS - 1) / KQ_ROWS;
   }
-  // the tile width that finishes first: waves (rounded up) x the work one
-  // wave of resident CTAs does per SM (CTAs x positions)
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  auto cost = [&](int pos, int per_sm) {
-    const long long c = (long long)ctas * ((T + pos - 1) / pos), wave = (long long)sms * per_sm;
-    return ((c + wave - 1) / wave) * per_sm * pos;
-  };
-  const bool narrow = cost(32, KqShape<32>::MIN_CTAS) < cost(64, KqShape<64>::MIN_CTAS);
-  cudaError_t e;
-  if (narrow)
-    e = launch_k(L, gemm_q4k_kernel<32>, dim3(ctas, (T + 31) / 32), KqShape<32>::THREADS, 0, G, m[0]->nb, a.qa_q,
-                 a.qa_d, T, 1.0f, L.err);
-  else
-    e = launch_k(L, gemm_q4k_kernel<64>, dim3(ctas, (T + 63) / 64), KqShape<64>::THREADS, 0, G, m[0]->nb, a.qa_q,
-                 a.qa_d, T, 1.0f, L.err);
+  const dim3 grid(ctas, (T + KQ_POS - 1) / KQ_POS);
+  const cudaError_t e =
+      launch_k(L, gemm_q4k_kernel, grid, KQ_THREADS, 0, G, m[0]->nb, a.qa_q, a.qa_d, T, 1.0f, L.err);
   if (e != cudaSuccess) return e;
   if (L.launches) ++*L.launches;
   return cudaGetLastError();
