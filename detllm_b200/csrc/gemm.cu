@@ -621,7 +621,9 @@ cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a,
 
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   cudaError_t e;
-  if (T > 16) {
+  if (T > 16 && m.tc) {
+    e = launch_gemm_q8_tc(L, m, a, T, o);
+  } else if (T > 16) {
     e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, o) : launch_chunk<GT_Q4_0>(L, m, a, T, o);
   } else if (T <= 8 && (m.type == GT_Q8_0 ? DecodeSmem<GT_Q8_0>::total(T, m.nb)
                                            : DecodeSmem<GT_Q4_0>::total(T, m.nb)) <= 200 * 1024) {

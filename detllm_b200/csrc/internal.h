@@ -42,7 +42,8 @@ struct DevMatrix {
   const void* q = nullptr;
   const uint16_t* d = nullptr;
   const float* f = nullptr;
-  // Q6_K: the tensor-core records of the chunk GEMM (gemm_q6k_tc.cu), or null
+  // tensor-core records of the chunk GEMM, or null: Q6_K (gemm_q6k_tc.cu),
+  // Q8_0 / Q4_0 in LAYOUT_MMA16 (gemm_q8_tc.cu)
   const uint8_t* tc = nullptr;
 };
 
@@ -156,6 +157,11 @@ struct KqSegs {
 };
 cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* m, int n, const DevActs& a,
                                        float* const* out, const int* epi, const float* const* bias);
+// Q8_0 / Q4_0 chunk GEMM on tcgen05 tensor cores (gemm_q8_tc.cu): needs the
+// matrix's tensor-core copy in m.tc (q8_tc_repack at load)
+size_t q8_tc_bytes(int rows, int nb);
+cudaError_t launch_q8_tc_repack(cudaStream_t st, const DevMatrix& m, uint8_t* out);
+cudaError_t launch_gemm_q8_tc(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,

@@ -308,6 +308,22 @@ det_status fuse_matrices(det_model* m, DevMatrix* const* parts, int n, DevMatrix
   return DET_OK;
 }
 
+// the tensor-core copy (gemm_q8_tc.cu) of a LAYOUT_MMA16 matrix that chunk
+// GEMMs read, built on the device from its records
+det_status build_q8_tc(det_model* m, DevMatrix* M) {
+  if (!M->rows || M->layout != LAYOUT_MMA16 || M->tc) return DET_OK;
+  const size_t bytes = q8_tc_bytes(M->rows, M->nb);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+  m->allocations.push_back(p);
+  if (launch_q8_tc_repack(nullptr, *M, static_cast<uint8_t*>(p)) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess)
+    return DET_ERR_CUDA;
+  M->tc = static_cast<const uint8_t*>(p);
+  m->weight_bytes += bytes;
+  return DET_OK;
+}
+
 // optional metadata helpers (det-model lib.rs:1566-1645)
 det_status opt_u32(const Gguf& g, const std::string& k, uint32_t* v, bool* present) {
   const int e = g.get_u32(k, v);
@@ -498,6 +514,26 @@ det_status load_impl(const uint8_t* bytes, size_t len, det_model* m) {
     return DET_ERR_GGUF;
   }
   m->vocab = (int)V;
+  // tensor-core copies of the Q8_0 / Q4_0 matrices the chunk GEMMs read (the
+  // fused q|k|v and gate|up where they exist, else their parts)
+  for (LayerDev& L : m->layers) {
+    det_status st;
+    if (L.wqkv.rows) {
+      if ((st = build_q8_tc(m, &L.wqkv))) return st;
+    } else {
+      for (DevMatrix* W : {&L.wq, &L.wk, &L.wv})
+        if ((st = build_q8_tc(m, W))) return st;
+    }
+    if (L.wgu.rows) {
+      if ((st = build_q8_tc(m, &L.wgu))) return st;
+    } else {
+      for (DevMatrix* W : {&L.gate, &L.up})
+        if ((st = build_q8_tc(m, W))) return st;
+    }
+    for (DevMatrix* W : {&L.wo, &L.down})
+      if ((st = build_q8_tc(m, W))) return st;
+  }
+  if (det_status st = build_q8_tc(m, &m->output)) return st;
   return DET_OK;
 }
 

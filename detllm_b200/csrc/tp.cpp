@@ -111,6 +111,7 @@ DevMatrix row_view(const DevMatrix& M, int r0, int r1) {
     case GT_Q4_0:
       if (M.layout == LAYOUT_MMA16) {
         v.q = q + (r / 16) * (size_t)M.nb * (M.type == GT_Q8_0 ? 544 : 288);
+        v.tc = nullptr;  // parts run the mma.sync chunk GEMM (the tensor-core copy has 128-row tiles)
       } else {
         v.q = q + r * (size_t)(M.type == GT_Q8_0 ? M.cols : M.cols / 2);
         v.d = M.d + r * (size_t)M.nb;
