@@ -295,7 +295,10 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
     unsigned long long acc[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) acc[j] = 0ull;
-    const unsigned long long NEG_M = qp2(-12582912.0f, -12582912.0f), ONE = qp2(1.0f, 1.0f);
+    // `one` comes from the host (OutSegs::one == 1.0): with a literal 1.0 the
+    // compiler may turn fma(c, 1, acc) into c + acc and contract it with the
+    // product before it, which would skip the product's rounding
+    const unsigned long long NEG_M = qp2(-12582912.0f, -12582912.0f), ONE = qp2(o.one, o.one);
     int b = 0;
     for (int st = 0; st < nst && ok; st++) {
       const int slot = st % QT_STAGES, b0 = st * QT_SB, nblk = min(QT_SB, nb - b0);
