@@ -105,6 +105,7 @@ def lib():
             "det_model_stats": (I, [P, C.POINTER(Stats), I]),
             "det_set_profiling": (I, [I]),
             "det_set_encode_chunk": (I, [U32, C.POINTER(U32)]),
+            "det_set_q8_tensor_cores": (I, [I, C.POINTER(I)]),
             "det_model_profile": (I, [P, C.c_char_p, SZ, I]),
             "det_session_gemv_stream": (I, [P, U32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
@@ -316,6 +317,14 @@ def set_encode_chunk(chunk: int) -> int:
     prev = C.c_uint32()
     _check(lib().det_set_encode_chunk(int(chunk), C.byref(prev)), "det_set_encode_chunk")
     return prev.value
+
+
+def set_q8_tensor_cores(enable: bool) -> bool:
+    """Chunk GEMM for Q8_0 / Q4_0 weights: True the tcgen05 kernel (default),
+    False the mma.sync kernel; returns the previous choice.  Same bits."""
+    prev = C.c_int()
+    _check(lib().det_set_q8_tensor_cores(int(bool(enable)), C.byref(prev)), "det_set_q8_tensor_cores")
+    return bool(prev.value)
 
 
 def set_profiling(enable: bool) -> None:

@@ -42,6 +42,7 @@
 #include <algorithm>
 
 #include "dev_math.cuh"
+#include "../../include/detgpu.h"
 #include "internal.h"
 
 namespace det {
@@ -617,11 +618,16 @@ cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a,
   return cudaGetLastError();
 }
 
+// Which chunk GEMM runs for Q8_0 / Q4_0 matrices that have tensor-core
+// records: 1 the tcgen05 kernel (gemm_q8_tc.cu), 0 the mma.sync kernel
+// above.  Both give the same bits.
+std::atomic<int> g_q8_tc{1};
+
 }  // namespace
 
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   cudaError_t e;
-  if (T > 16 && m.tc) {
+  if (T > 16 && m.tc && g_q8_tc.load(std::memory_order_relaxed)) {
     e = launch_gemm_q8_tc(L, m, a, T, o);
   } else if (T > 16) {
     e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, o) : launch_chunk<GT_Q4_0>(L, m, a, T, o);
@@ -660,3 +666,9 @@ cudaError_t launch_gemv_fast(const Launch& L, const DevMatrix& m, const DevActs&
 }
 
 }  // namespace det
+
+extern "C" det_status det_set_q8_tensor_cores(int enable, int* previous) {
+  const int prev = det::g_q8_tc.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+  if (previous) *previous = prev;
+  return DET_OK;
+}

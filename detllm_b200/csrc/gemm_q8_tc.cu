@@ -292,13 +292,13 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
     const int q = warp & 3, cg = warp >> 2;  // TMEM lane quarter (rows), column group (positions)
     const int row_l = 32 * q + lane;
     const bool cols_live = cg < 2 * ngroups;  // columns of an absent group are never written
-    unsigned long long acc[16];
+    float acc[32];
 #pragma unroll
-    for (int j = 0; j < 16; j++) acc[j] = 0ull;
+    for (int j = 0; j < 32; j++) acc[j] = 0.0f;
     // `one` comes from the host (OutSegs::one == 1.0): with a literal 1.0 the
     // compiler may turn fma(c, 1, acc) into c + acc and contract it with the
     // product before it, which would skip the product's rounding
-    const unsigned long long NEG_M = qp2(-12582912.0f, -12582912.0f), ONE = qp2(o.one, o.one);
+    const float one = o.one;
     int b = 0;
     for (int st = 0; st < nst && ok; st++) {
       const int slot = st % QT_STAGES, b0 = st * QT_SB, nblk = min(QT_SB, nb - b0);
@@ -323,20 +323,28 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
         __syncwarp();
         if (lane == 0) q_arrive(tempty0 + 8 * buf);
         if (!cols_live) continue;
-        // c = (w.d * a.d) * isum, sum += c, two positions at a time
+        // c = (w.d * a.d) * isum, sum += c.  The 32 activation scales of this
+        // warp's positions are the 32 slots of one half of the group's
+        // (permuted) scale slab: load them as 8 vectors, pick each by its
+        // slot (position 8j + 2u + e sits at 8u + 2j + e, q8a_sperm)
         const float wd = reinterpret_cast<const float*>(sb + QT_OFF_WS)[k * QT_ROWS + row_l];
-        const float* as = reinterpret_cast<const float*>(sb + QT_OFF_AS) + (cg >> 1) * QT_SB * 64 + k * 64;
-        const unsigned long long wd2 = qp2(wd, wd);
-        const int p_base = 32 * (cg & 1);  // position within the group
+        const float4* as4 = reinterpret_cast<const float4*>(
+            reinterpret_cast<const float*>(sb + QT_OFF_AS) + (cg >> 1) * QT_SB * 64 + k * 64 + 32 * (cg & 1));
+        float adv[32];
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int p0 = p_base + 2 * j;
-          const unsigned long long ad2 = qp2(as[q8a_sperm(p0)], as[q8a_sperm(p0 + 1)]);
-          unsigned long long bits;
-          asm("mov.b64 %0, {%1, %2};" : "=l"(bits) : "r"(v[2 * j] + 0x4B400000u), "r"(v[2 * j + 1] + 0x4B400000u));
-          const unsigned long long isum = q_add2(bits, NEG_M);  // exact
-          const unsigned long long c = q_mul2(q_mul2(wd2, ad2), isum);
-          acc[j] = q_fma2(c, ONE, acc[j]);  // acc + c, rounded once
+        for (int i = 0; i < 8; i++) {
+          const float4 f = as4[i];
+          adv[4 * i] = f.x;
+          adv[4 * i + 1] = f.y;
+          adv[4 * i + 2] = f.z;
+          adv[4 * i + 3] = f.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int slot = (((j >> 1) & 3) << 3) | (((j >> 3) & 3) << 1) | (j & 1);
+          const float isum = __fsub_rn(__uint_as_float(v[j] + 0x4B400000u), 12582912.0f);  // exact
+          const float c = __fmul_rn(__fmul_rn(wd, adv[slot]), isum);
+          acc[j] = __fmaf_rn(c, one, acc[j]);  // acc + c, rounded once
         }
       }
       if (!ok) break;
@@ -349,14 +357,12 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
       if (row < rows) {
         const QtSeg sg = qt_seg(o, row);
         const int lr = row - sg.row0;
-        for (int j = 0; j < 16; j++) {
-          const float2 v2 = q_un2(acc[j]);
-          const int pos = grp0 * 64 + 32 * cg + 2 * j;
 #pragma unroll
-          for (int e = 0; e < 2; e++) {
-            const int p = pos + e;
+        for (int j = 0; j < 32; j++) {
+          {
+            const int p = grp0 * 64 + 32 * cg + j;
             if (p >= T) continue;
-            float v = e ? v2.y : v2.x;
+            float v = acc[j];
             if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
             float* dst = sg.out + (size_t)p * sg.ld + lr;
             if (sg.epi == EPI_BIAS) {

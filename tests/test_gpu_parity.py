@@ -84,6 +84,21 @@ def test_long_window_logits_bit_exact(D, long_models, name, chunk):
     assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
 
 
+@pytest.mark.parametrize("name", ["hd64_gqa8", "hd128_gqa2"])  # Q8_0 everywhere; Q4_0 attention
+@pytest.mark.parametrize("chunk", [37, 300])
+def test_q8_chunk_gemm_mma_sync_kernel(D, long_models, name, chunk):
+    """The mma.sync chunk GEMM (the alternative to the tcgen05 one) gives the
+    same bits."""
+    g, toks, want = long_models[name]
+    prev = D.set_q8_tensor_cores(False)
+    try:
+        got = D.Model(g).logits_for_tokens(toks, chunk=chunk)
+    finally:
+        D.set_q8_tensor_cores(prev)
+    diff = np.nonzero(bits(got) != bits(want))
+    assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
+
+
 def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
