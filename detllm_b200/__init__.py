@@ -320,8 +320,8 @@ def set_encode_chunk(chunk: int) -> int:
 
 
 def set_q8_tensor_cores(enable: bool) -> bool:
-    """Chunk GEMM for Q8_0 / Q4_0 weights: True the tcgen05 kernel (default),
-    False the mma.sync kernel; returns the previous choice.  Same bits."""
+    """Chunk GEMM for Q8_0 / Q4_0 weights: True the tcgen05 kernel, False the
+    mma.sync kernel (default); returns the previous choice.  Same bits."""
     prev = C.c_int()
     _check(lib().det_set_q8_tensor_cores(int(bool(enable)), C.byref(prev)), "det_set_q8_tensor_cores")
     return bool(prev.value)

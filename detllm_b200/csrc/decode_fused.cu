@@ -958,7 +958,7 @@ bool fused_decode_plan(int d, int dff, int nh, int nkv, int hd, int s_ld, FdPara
 
 cudaError_t fused_decode_prepare(const FdParams& p, int* grid) {
   const int smem = fused_decode_smem(p);
-  cudaError_t e = cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = raise_smem_cap((const void*)decode_fused_kernel, smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0, occ = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;

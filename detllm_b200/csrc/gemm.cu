@@ -608,8 +608,7 @@ __global__ void __launch_bounds__(DG_THREADS) gemv_decode_kernel(const uint8_t* 
 template <int QT>
 cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   const int smem = DecodeSmem<QT>::total(T, m.nb);
-  cudaError_t e = cudaFuncSetAttribute(gemv_decode_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  if (cudaError_t e = raise_smem_cap((const void*)gemv_decode_kernel<QT>, smem)) return e;
   {
     const cudaError_t e_ = launch_k(L, gemv_decode_kernel<QT>, (m.rows + 15) / 16, DG_THREADS, smem,
         (const uint8_t*)m.q, m.nb, a.qa_q, a.qa_d, T, o, L.err);
@@ -620,14 +619,20 @@ cudaError_t launch_decode(const Launch& L, const DevMatrix& m, const DevActs& a,
 
 // Which chunk GEMM runs for Q8_0 / Q4_0 matrices that have tensor-core
 // records: 1 the tcgen05 kernel (gemm_q8_tc.cu), 0 the mma.sync kernel
-// above.  Both give the same bits.
-std::atomic<int> g_q8_tc{1};
+// above.  Both give the same bits.  Both are bound by the per-block f32 folds
+// (four rounded operations per row, position and block), not by the integer
+// dots, and the mma.sync kernel, with four CTAs of 8 warps per SM, hides
+// their latency better: at TinyLlama shape and 1,024 positions its gate|up
+// launch takes 157 us against 233 us, so it is the default.
+std::atomic<int> g_q8_tc{0};
 
 }  // namespace
 
+bool q8_tensor_cores() { return g_q8_tc.load(std::memory_order_relaxed) != 0; }
+
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o) {
   cudaError_t e;
-  if (T > 16 && m.tc && g_q8_tc.load(std::memory_order_relaxed)) {
+  if (T > 16 && m.tc && q8_tensor_cores()) {
     e = launch_gemm_q8_tc(L, m, a, T, o);
   } else if (T > 16) {
     e = m.type == GT_Q8_0 ? launch_chunk<GT_Q8_0>(L, m, a, T, o) : launch_chunk<GT_Q4_0>(L, m, a, T, o);

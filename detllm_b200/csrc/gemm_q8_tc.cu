@@ -140,6 +140,27 @@ DI void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// 32 lanes x 16 columns, without the wait: the registers are not valid until
+// tc_wait16 on the same array
+DI void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+// waits for every tcgen05.ld of the thread; v is an in/out operand so the
+// compiler cannot read it before the wait
+DI void tc_wait16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                 "+r"(v[15])
+               :
+               : "memory");
+}
+
 // packed f32 pairs (each half one IEEE round-to-nearest operation)
 DI unsigned long long qp2(float a, float b) {
   unsigned long long r;
@@ -299,57 +320,104 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
     // compiler may turn fma(c, 1, acc) into c + acc and contract it with the
     // product before it, which would skip the product's rounding
     const float one = o.one;
-    int b = 0;
-    for (int st = 0; st < nst && ok; st++) {
-      const int slot = st % QT_STAGES, b0 = st * QT_SB, nblk = min(QT_SB, nb - b0);
-      // the stage's scales (same copies as the MMA operands)
-      if (!q_wait(full0 + 8 * slot, (uint32_t)((st / QT_STAGES) & 1))) {
-        if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
-        ok = false;
-        break;
+    // One block b at a time, in order.  The block's 32 columns are read in
+    // two 16-column halves, and each read is issued before the arithmetic
+    // on the previous half, so its latency hides behind that arithmetic:
+    //   ld A(b) ... wait, ld B(b), fold A(b), wait, release buffer,
+    //   ld A(b + 1), fold B(b).
+    // A stage's scales are released after the fold of its last block.
+    // Column j of the warp's 32 is position 32 (cg & 1) + j of the group;
+    // its activation scale sits at slot 8 ((j >> 1) & 3) + 2 (j >> 3) +
+    // (j & 1) of the group's permuted half (q8a_sperm): half A (j < 16)
+    // reads float4s 0, 2, 4, 6 of the half, half B float4s 1, 3, 5, 7.
+    const uint32_t tlane = (uint32_t)(32 * q) << 16;
+    auto full_wait = [&](int st) {
+      if (q_wait(full0 + 8 * (st % QT_STAGES), (uint32_t)((st / QT_STAGES) & 1))) return true;
+      if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
+      return false;
+    };
+    auto tfull_wait = [&](int b) {
+      if (q_wait(tfull0 + 8 * (b % QT_BUFS), (uint32_t)((b / QT_BUFS) & 1))) return true;
+      if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
+      return false;
+    };
+    auto fold = [&](const uint32_t (&v)[16], int b, int half) {
+      const int st = b / QT_SB, k = b - st * QT_SB;
+      const uint8_t* sb = smem + (st % QT_STAGES) * QT_STAGE;
+      const float wd = reinterpret_cast<const float*>(sb + QT_OFF_WS)[k * QT_ROWS + row_l];
+      const float4* as4 = reinterpret_cast<const float4*>(
+          reinterpret_cast<const float*>(sb + QT_OFF_AS) + (cg >> 1) * QT_SB * 64 + k * 64 + 32 * (cg & 1));
+      float adv[16];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 f = as4[2 * i + half];
+        adv[4 * i] = f.x;
+        adv[4 * i + 1] = f.y;
+        adv[4 * i + 2] = f.z;
+        adv[4 * i + 3] = f.w;
       }
-      const uint8_t* sb = smem + slot * QT_STAGE;
-      for (int k = 0; k < nblk; k++, b++) {
-        const int buf = b % QT_BUFS;
-        if (!q_wait(tfull0 + 8 * buf, (uint32_t)((b / QT_BUFS) & 1))) {
-          if (lane == 0) atomicOr(err, ERRF_TIMEOUT);
-          ok = false;
-          break;
-        }
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        const int j = 16 * half + jj;
+        // slot within this half's four float4s: 8u + 2a + e -> 4 (u) + (2a + e) % 4
+        const int u = (j >> 1) & 3, ae = ((j >> 3) & 1) * 2 + (j & 1);
+        const float isum = __fsub_rn(__uint_as_float(v[jj] + 0x4B400000u), 12582912.0f);  // exact
+        const float c = __fmul_rn(__fmul_rn(wd, adv[4 * u + ae]), isum);
+        acc[j] = __fmaf_rn(c, one, acc[j]);  // acc + c, rounded once
+      }
+    };
+    if (cols_live) {
+      uint32_t va[16], vb[16];
+      if (nb > 0 && (ok = full_wait(0) && tfull_wait(0))) {
         tc_fence_after();
-        uint32_t v[32];
-        if (cols_live) tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 128 + 32 * cg), v);
+        tc_ld16(tmem + tlane + (uint32_t)(32 * cg), va);
+      }
+      for (int b = 0; b < nb && ok; b++) {
+        const int buf = b % QT_BUFS;
+        tc_wait16(va);
+        tc_ld16(tmem + tlane + (uint32_t)(buf * 128 + 32 * cg + 16), vb);
+        fold(va, b, 0);
+        tc_wait16(vb);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) q_arrive(tempty0 + 8 * buf);
-        if (!cols_live) continue;
-        // c = (w.d * a.d) * isum, sum += c.  The 32 activation scales of this
-        // warp's positions are the 32 slots of one half of the group's
-        // (permuted) scale slab: load them as 8 vectors, pick each by its
-        // slot (position 8j + 2u + e sits at 8u + 2j + e, q8a_sperm)
-        const float wd = reinterpret_cast<const float*>(sb + QT_OFF_WS)[k * QT_ROWS + row_l];
-        const float4* as4 = reinterpret_cast<const float4*>(
-            reinterpret_cast<const float*>(sb + QT_OFF_AS) + (cg >> 1) * QT_SB * 64 + k * 64 + 32 * (cg & 1));
-        float adv[32];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const float4 f = as4[i];
-          adv[4 * i] = f.x;
-          adv[4 * i + 1] = f.y;
-          adv[4 * i + 2] = f.z;
-          adv[4 * i + 3] = f.w;
+        if (b + 1 < nb) {
+          if ((b + 1) % QT_SB == 0 && !full_wait((b + 1) / QT_SB)) ok = false;
+          if (ok && !tfull_wait(b + 1)) ok = false;
+          if (ok) {
+            tc_fence_after();
+            tc_ld16(tmem + tlane + (uint32_t)(((b + 1) % QT_BUFS) * 128 + 32 * cg), va);
+          }
         }
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int slot = (((j >> 1) & 3) << 3) | (((j >> 3) & 3) << 1) | (j & 1);
-          const float isum = __fsub_rn(__uint_as_float(v[j] + 0x4B400000u), 12582912.0f);  // exact
-          const float c = __fmul_rn(__fmul_rn(wd, adv[slot]), isum);
-          acc[j] = __fmaf_rn(c, one, acc[j]);  // acc + c, rounded once
+        fold(vb, b, 1);
+        if (b + 1 == nb || (b + 1) % QT_SB == 0) {
+          __syncwarp();
+          if (lane == 0) q_arrive(empty0 + 8 * ((b / QT_SB) % QT_STAGES));  // done with the stage's scales
         }
       }
-      if (!ok) break;
-      __syncwarp();
-      if (lane == 0) q_arrive(empty0 + 8 * slot);  // this warp is done with the stage's scales
+      // no read of the tensor memory may be in flight past this point
+      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+    } else {
+      // columns of an absent group: keep the barrier counts
+      int b = 0;
+      for (int st = 0; st < nst && ok; st++) {
+        const int nblk = min(QT_SB, nb - st * QT_SB);
+        if (!full_wait(st)) {
+          ok = false;
+          break;
+        }
+        for (int k = 0; k < nblk; k++, b++) {
+          if (!tfull_wait(b)) {
+            ok = false;
+            break;
+          }
+          __syncwarp();
+          if (lane == 0) q_arrive(tempty0 + 8 * (b % QT_BUFS));
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) q_arrive(empty0 + 8 * (st % QT_STAGES));
+      }
     }
     // outputs of row (tile * 128 + row_l), positions grp0 * 64 + 32 cg + j
     if (__all_sync(0xffffffffu, ok) && cols_live) {

@@ -109,6 +109,13 @@ cudaError_t launch_k(const Launch& L, void (*kern)(KArgs...), dim3 grid, dim3 bl
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// Raises the dynamic shared-memory cap of `kern` on the current device to at
+// least `bytes` (a no-op at 48 KiB or less) and never lowers it: a CUDA graph
+// captured earlier may hold a launch of the same kernel that needs more than
+// the launch at hand, and whatever replays that launch on its own (a
+// profiler's node-by-node replay) checks it against the current cap.
+cudaError_t raise_smem_cap(const void* kern, size_t bytes);
+
 // ---- launchers (kernels.cu) ------------------------------------------------
 cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,
                               float rope_base);
@@ -162,6 +169,9 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
 size_t q8_tc_bytes(int rows, int nb);
 cudaError_t launch_q8_tc_repack(cudaStream_t st, const DevMatrix& m, uint8_t* out);
 cudaError_t launch_gemm_q8_tc(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
+// the process-wide choice of det_set_q8_tensor_cores (gemm.cu): models loaded
+// while it is on get tensor-core copies, and chunk GEMMs use them while it is
+bool q8_tensor_cores();
 // LAYOUT_MMA16 Q8_0 / Q4_0 matrix with per-segment outputs (gemm.cu)
 cudaError_t launch_gemm_mma16(const Launch& L, const DevMatrix& m, const DevActs& a, int T, const OutSegs& o);
 cudaError_t launch_gemv(const Launch& L, const DevMatrix& m, const DevActs& a, int T, float* out, int out_ld,

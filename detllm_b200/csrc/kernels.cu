@@ -8,6 +8,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "dev_math.cuh"
 #include "../../include/detgpu.h"
@@ -1091,13 +1094,25 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
   return post(L);
 }
 
+cudaError_t raise_smem_cap(const void* kern, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> caps;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& cap = caps[{kern, dev}];
+  if (cap >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) cap = bytes;
+  return e;
+}
+
 cudaError_t launch_rmsnorm(const Launch& L, const float* x, const float* w, int n, float eps, int T, float* h,
                            float* qd, int8_t* qq) {
   const size_t smem = n <= RMS_MAX_SMEM ? 2 * (size_t)n * sizeof(float) : 0;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  if (cudaError_t e = raise_smem_cap((const void*)rmsnorm_kernel, smem)) return e;
   if (n % 32) qd = nullptr, qq = nullptr;
   // a short chunk is one or a few CTAs: more warps share the quantisation
   const int threads = T <= 16 ? 1024 : 256;
@@ -1189,11 +1204,7 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
   size_t gsmem;
   int gscores;
   if (gqa_plan(n_head, n_head_kv, head_dim, n_ctx, &gsmem, &gscores)) {
-    if (gsmem > 48 * 1024) {
-      cudaError_t e =
-          cudaFuncSetAttribute(attention_gqa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem);
-      if (e != cudaSuccess) return e;
-    }
+    if (cudaError_t e = raise_smem_cap((const void*)attention_gqa_kernel, gsmem)) return e;
     dim3 grid(T, n_head_kv);
     {
       const cudaError_t e_ = launch_k(L, attention_gqa_kernel, grid, ATG_THREADS, gsmem, q, kc, vc, pos0, n_head,
@@ -1205,10 +1216,7 @@ cudaError_t launch_attention(const Launch& L, const float* q, const float* kc, c
   const size_t need = (size_t)(head_dim + n_ctx) * sizeof(float);
   const int smem_scores = need <= 160 * 1024 ? 1 : 0;
   const size_t smem = smem_scores ? need : head_dim * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  if (cudaError_t e = raise_smem_cap((const void*)attention_kernel, smem)) return e;
   dim3 grid(T, n_head);
   {
     const cudaError_t e_ = launch_k(L, attention_kernel, grid, ATT_THREADS, smem, q, kc, vc, pos0, n_head, n_head_kv,

@@ -311,7 +311,8 @@ det_status fuse_matrices(det_model* m, DevMatrix* const* parts, int n, DevMatrix
 // the tensor-core copy (gemm_q8_tc.cu) of a LAYOUT_MMA16 matrix that chunk
 // GEMMs read, built on the device from its records
 det_status build_q8_tc(det_model* m, DevMatrix* M) {
-  if (!M->rows || M->layout != LAYOUT_MMA16 || M->tc) return DET_OK;
+  // the copy doubles the matrix's footprint: only when the tcgen05 kernel is chosen
+  if (!M->rows || M->layout != LAYOUT_MMA16 || M->tc || !q8_tensor_cores()) return DET_OK;
   const size_t bytes = q8_tc_bytes(M->rows, M->nb);
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return DET_ERR_DEVICE_OOM;

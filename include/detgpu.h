@@ -259,10 +259,13 @@ det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per
  * in the reference. */
 det_status det_set_encode_chunk(uint32_t chunk, uint32_t* previous);
 /* Chunk GEMM (more than 16 positions) for Q8_0 / Q4_0 weights: enable != 0
- * selects the tcgen05 tensor-core kernel (the default), 0 the mma.sync
- * kernel.  Both give identical bits; process-wide, for forwards launched
- * after the call.  The previous setting goes to *previous when non-NULL.  A
- * tuning hook with no counterpart in the reference. */
+ * selects the tcgen05 tensor-core kernel, 0 the mma.sync kernel (the
+ * default: faster at the shapes measured).  Both give identical bits.
+ * Process-wide: models loaded while it is on get the kernel's weight copies
+ * (as much device memory again as their Q8_0 / Q4_0 matrices), and their
+ * forwards launched while it is on use them.  The previous setting goes to
+ * *previous when non-NULL.  A tuning hook with no counterpart in the
+ * reference. */
 det_status det_set_q8_tensor_cores(int enable, int* previous);
 /* per-launch device timing of every kernel (adds two event records per
  * launch and turns CUDA graphs off while enabled) */

@@ -86,11 +86,12 @@ def test_long_window_logits_bit_exact(D, long_models, name, chunk):
 
 @pytest.mark.parametrize("name", ["hd64_gqa8", "hd128_gqa2"])  # Q8_0 everywhere; Q4_0 attention
 @pytest.mark.parametrize("chunk", [37, 300])
-def test_q8_chunk_gemm_mma_sync_kernel(D, long_models, name, chunk):
-    """The mma.sync chunk GEMM (the alternative to the tcgen05 one) gives the
-    same bits."""
+def test_q8_chunk_gemm_tcgen05_kernel(D, long_models, name, chunk):
+    """The tcgen05 chunk GEMM (the alternative to the default mma.sync one)
+    gives the same bits; 37 positions leave the second 64-position group of
+    the CTA absent."""
     g, toks, want = long_models[name]
-    prev = D.set_q8_tensor_cores(False)
+    prev = D.set_q8_tensor_cores(True)
     try:
         got = D.Model(g).logits_for_tokens(toks, chunk=chunk)
     finally:
