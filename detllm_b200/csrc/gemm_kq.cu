@@ -226,66 +226,27 @@ DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
   g.out[row] = v;
 }
 
-// Q4_K: each row is one f32 chain over all K elements (sum += w * act, in
-// order), so its length sets a floor of K dependent adds per launch.  A CTA
-// takes 32 rows: warps 0-7 (producers) dequantise super-block s of the 32
-// rows -- warp w sub-block w, lane r row r -- and write the products
-// w * act into stage buffer s % 2, while warp 8 runs the 32 row chains
-// (lane = row) through the stages in order.  Producers and chain meet only
-// at named hardware barriers: FULL[i] (producers arrive after writing buffer
-// i, the chain waits) and EMPTY[i] (the chain arrives after reading it, the
-// producers wait before writing it again).  The super-blocks' bytes arrive
-// by cp.async G4_PREF stages ahead into a ring of raw slots (a producer-only
-// barrier publishes each slot), the activations are dequantised into shared
-// memory once, and the producers' arithmetic runs as f32x2 pairs.  Stage
-// rows are 260 floats apart and both sides move 16-byte vectors (the eight
-// lanes of a quarter-warp hit distinct bank groups).
-constexpr int G4_ROWS = 32;
-constexpr int G4_PWARPS = 8;
-constexpr int G4_PTHREADS = G4_PWARPS * 32;
-constexpr int G4_THREADS = G4_PTHREADS + 32;   // producers + chain warp (named-barrier count)
-// The CTA has 12 warps: producers are warps {0,1,2,4,5,6,8,9}, the chain
-// warp is warp 3, and warps 7, 10, 11 only help stage the activation.  An
-// SM sub-partition issues the warps whose ids agree mod 4, so the chain
-// warp (K dependent adds per row) has its scheduler to itself instead of
-// sharing it with two producer warps; 12 warps keep the mapping the same
-// for every CTA on the SM.
-constexpr int G4_BLOCK = 12 * 32;
-constexpr int G4_CHAIN_WARP = 3;
-// producer index of warp w (-1: not a producer)
-__host__ __device__ constexpr int g4_producer(int w) {
-  return w < 3 ? w : w == 3 || w == 7 || w > 9 ? -1 : w < 7 ? w - 1 : w - 2;
-}
-constexpr int G4_LD = 260;
-constexpr int G4_NBUF = 2;
-constexpr int G4_PREF = 4;                   // super-blocks in flight ahead of the producers
-constexpr int G4_RAWN = G4_PREF + 2;         // raw slots: the ring never overwrites a slot in use
-constexpr int G4_RAW_STAGE = G4_ROWS * 144;  // bytes of one super-block of 32 rows
-constexpr int G4_BAR_FULL = 1, G4_BAR_EMPTY = 1 + G4_NBUF, G4_BAR_PROD = 1 + 2 * G4_NBUF;  // 0 is __syncthreads
-static_assert(G4_NBUF == 2, "nbar_*_buf dispatch two buffers");
-constexpr int G4_MAX_NB = 64;  // K <= 16384 (activations staged in shared memory)
-constexpr size_t G4_FIXED_SMEM = (size_t)G4_NBUF * G4_ROWS * G4_LD * 4 + (size_t)G4_RAWN * G4_RAW_STAGE;
-inline size_t g4_smem_bytes(int nbs) { return G4_FIXED_SMEM + (size_t)nbs * 256 * 4; }
-
-// barrier ids are immediates (a register id makes the CTA reserve all 16)
-template <int ID, int N>
-DI void nbar_sync() {
-  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(N) : "memory");
-}
-template <int ID, int N>
-DI void nbar_arrive() {
-  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(N) : "memory");
-}
-template <int BASE>
-DI void nbar_sync_buf(int buf) {
-  if (buf == 0) nbar_sync<BASE, G4_THREADS>();
-  else nbar_sync<BASE + 1, G4_THREADS>();
-}
-template <int BASE>
-DI void nbar_arrive_buf(int buf) {
-  if (buf == 0) nbar_arrive<BASE, G4_THREADS>();
-  else nbar_arrive<BASE + 1, G4_THREADS>();
-}
+// Q4_K, one position.  Each row is one f32 chain over all K elements
+// (sum += w * act, in order; det-quant lib.rs:281-315), so a row costs K
+// dependent adds however it is split.  Every lane therefore owns one row and
+// runs its whole chain in registers: it dequantises its row's weights out of
+// shared memory, multiplies them by the activation and adds the products in
+// element order.  A CTA is one warp (32 rows), so the scheduler spreads the
+// warps of a wide matrix over every SM and sub-partition at once; each warp
+// streams its rows' super-blocks (32 rows x 144 B) through a G4R_STAGES-slot
+// ring with cp.async, G4R_STAGES - 1 super-blocks ahead, and holds the
+// activation, dequantised once (act[i] = a.d * a.q, the reference's value),
+// in shared memory, where every lane reads the same float4 (a broadcast).
+// A wide matrix (more CTAs than two per SM) gets 3 ring slots, which keep
+// the CTA at 30 KB so that seven fit per SM and the matrix runs in one wave;
+// a narrow one gets 8, so that its few warps keep 7 super-blocks in flight.
+// Lane l reads its row's bytes at 144 l: a quarter-warp's eight 16-byte
+// reads fall in distinct bank groups.  The dequantisation and the products
+// run as f32x2 pairs; the chain adds one element at a time.
+constexpr int G4R_ROWS = 32;
+constexpr int G4R_STAGE = G4R_ROWS * 144;  // bytes of one super-block of 32 rows
+constexpr int G4_MAX_NB = 64;              // K <= 16384 (activation staged in shared memory)
+inline size_t g4r_smem_bytes(int stages, int nbs) { return (size_t)stages * G4R_STAGE + (size_t)nbs * 256 * 4; }
 
 DI void g4_cp_async16(void* sdst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)), "l"(gsrc) : "memory");
@@ -312,124 +273,160 @@ DI unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned 
   return r;
 }
 
-__global__ void __launch_bounds__(G4_BLOCK) gemv_q4k_chain_kernel(KqSegs S, const int8_t* __restrict__ aq,
-                                                                    const float* __restrict__ ad, uint32_t* err) {
-  extern __shared__ __align__(16) uint8_t g4_smem[];
-  float* prod = reinterpret_cast<float*>(g4_smem);                     // [G4_NBUF][G4_ROWS][G4_LD]
-  uint8_t* raw = g4_smem + (size_t)G4_NBUF * G4_ROWS * G4_LD * 4;      // [G4_RAWN][G4_ROWS][144]
-  float* act = reinterpret_cast<float*>(raw + (size_t)G4_RAWN * G4_RAW_STAGE);  // [K]
-  const KqSeg g = kq_seg(S);
-  const int r0 = ((int)blockIdx.x - g.cta0) * G4_ROWS;
-  const int nbs = S.nb, nbk = nbs * 8;
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int warp = g4_producer(tid >> 5);  // producer index 0..7, or -1
-  const int ptid = warp * 32 + lane;       // producer thread index
-  const bool chain = (tid >> 5) == G4_CHAIN_WARP;
-  const int row = r0 + lane;
-  const bool ok = row < g.rows;
-
-  // raw bytes of super-block s (32 rows x 144 B) into slot s % G4_RAWN (by
-  // the producer threads); rows past the matrix are zeros (zero weights,
-  // zero products).  Every producer thread commits one group per call, so
-  // the wait counts stay uniform.
-  auto issue = [&](int s) {
-      if (s < nbs) {
-        uint8_t* dst0 = raw + (size_t)(s % G4_RAWN) * G4_RAW_STAGE;
-        for (int c = ptid; c < G4_ROWS * 9; c += G4_PTHREADS) {
-          const int r = c / 9, part = c - 9 * r;
-          uint8_t* dst = dst0 + r * 144 + part * 16;
-          if (r0 + r < g.rows)
-            g4_cp_async16(dst, g.q + ((size_t)(r0 + r) * nbs + s) * 144 + part * 16);
-          else
-            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+// The activation of position 0, dequantised: act[i] = a.d * a.q (the
+// reference's value), by threads tid = 0 .. nthreads - 1 with each thread's
+// loads in flight together (a block's 32 quants of position 0 are
+// contiguous and unswizzled).
+DI void q4k_stage_act(float* act, const int8_t* __restrict__ aq, const float* __restrict__ ad, int nbk, int tid,
+                      int nthreads) {
+  for (int kb0 = 0; kb0 < nbk; kb0 += 4 * nthreads) {
+    uint4 qv[4][2];
+    float dv[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int kb = kb0 + nthreads * u + tid;
+      if (kb < nbk) {
+        const uint4* src = reinterpret_cast<const uint4*>(aq + q8a_elem(nbk, 0, kb, 0));
+        qv[u][0] = src[0];
+        qv[u][1] = src[1];
+        dv[u] = ad[q8a_dslot(nbk, 0, kb)];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int kb = kb0 + nthreads * u + tid;
+      if (kb < nbk) {
+        const uint32_t w[8] = {qv[u][0].x, qv[u][0].y, qv[u][0].z, qv[u][0].w,
+                               qv[u][1].x, qv[u][1].y, qv[u][1].z, qv[u][1].w};
+        float4* dst = reinterpret_cast<float4*>(act + kb * 32);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const int x = (int)w[k];
+          dst[k] = make_float4(fmul(dv[u], (float)((x << 24) >> 24)), fmul(dv[u], (float)((x << 16) >> 24)),
+                               fmul(dv[u], (float)((x << 8) >> 24)), fmul(dv[u], (float)(x >> 24)));
         }
       }
-      g4_cp_commit();
-  };
-  if (warp >= 0)  // weights are constant: stream them before the predecessor ends
-    for (int s = 0; s < G4_PREF; s++) issue(s);
-  pdl_enter();
-  // the activation, dequantised once: act[i] = a.d * a.q (the reference's value)
-  for (int i = tid; i < nbk * 32; i += G4_BLOCK) {
-    const int kb = i >> 5;
-    act[i] = fmul(ad[q8a_dslot(nbk, 0, kb)], (float)aq[q8a_elem(nbk, 0, kb, i & 31)]);
-  }
-  __syncthreads();
-  if (warp < 0 && !chain) return;  // staging warps: done
-
-  if (warp >= 0) {
-    const unsigned long long nmag2 = pk2(-8388608.0f, -8388608.0f);
-    for (int s = 0; s < nbs; s++) {
-      issue(s + G4_PREF);
-      g4_cp_wait<G4_PREF>();  // this thread's copies of stage s have landed
-      nbar_sync<G4_BAR_PROD, G4_PTHREADS>();  // ... and every producer's
-      const int buf = s & 1;
-      if (s >= G4_NBUF) nbar_sync_buf<G4_BAR_EMPTY>(buf);
-      const uint8_t* blk = raw + (size_t)(s % G4_RAWN) * G4_RAW_STAGE + lane * 144;
-      const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
-      const uint4 v0 = *reinterpret_cast<const uint4*>(blk + 16 + (warp >> 1) * 32);
-      const uint4 v1 = *reinterpret_cast<const uint4*>(blk + 32 + (warp >> 1) * 32);
-      const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
-      const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
-      // q4_k_scale_min (det-quant lib.rs:516-529) on the packed bytes
-      int sc, mn;
-      if (warp < 4) {
-        sc = (int)(q4k_sbyte(h, warp) & 63u);
-        mn = (int)(q4k_sbyte(h, warp + 4) & 63u);
-      } else {
-        sc = (int)((q4k_sbyte(h, warp + 4) & 0x0fu) | ((q4k_sbyte(h, warp - 4) >> 6) << 4));
-        mn = (int)((q4k_sbyte(h, warp + 4) >> 4) | ((q4k_sbyte(h, warp) >> 6) << 4));
-      }
-      const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
-      const unsigned long long dsc2 = pk2(dsc, dsc), ndmn2 = pk2(-dmn, -dmn);
-      const uint32_t qw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const int sh = 4 * (warp & 1);
-      const float4* av = reinterpret_cast<const float4*>(act + s * 256 + warp * 32);
-      float* dst = prod + (buf * G4_ROWS + lane) * G4_LD + warp * 32;
-#pragma unroll
-      for (int k = 0; k < 8; k++) {  // elements 4k .. 4k + 3
-        const uint32_t nib = (qw[k] >> sh) & 0x0f0f0f0fu;
-        // 2^23 + q as f32 bits, minus 2^23: q exactly
-        const float m0 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540));
-        const float m1 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7541));
-        const float m2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542));
-        const float m3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543));
-        const float4 a = av[k];
-        // w = (d*sc)*q - (dmin*m): d*sc and q have at most 17 and 4
-        // significant bits, so the product is exact and one fused
-        // multiply-add rounds exactly where the reference's subtraction
-        // does; then w * act
-        const unsigned long long w01 = fma2(dsc2, add2(pk2(m0, m1), nmag2), ndmn2);
-        const unsigned long long w23 = fma2(dsc2, add2(pk2(m2, m3), nmag2), ndmn2);
-        const float2 r01 = up2(mul2(w01, pk2(a.x, a.y)));
-        const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
-        *reinterpret_cast<float4*>(dst + 4 * k) = make_float4(r01.x, r01.y, r23.x, r23.y);
-      }
-      nbar_arrive_buf<G4_BAR_FULL>(buf);
     }
+  }
+}
+
+// (d * sc, -(dmin * m)) of sub-block j (q4_k_scale_min, det-quant
+// lib.rs:516-529, on the packed scale bytes of header h), as f32x2 pairs
+DI void q4k_sub_scales(const uint4& h, float d, float dmin, int j, unsigned long long& dsc2,
+                       unsigned long long& ndmn2) {
+  int sc, mn;
+  if (j < 4) {
+    sc = (int)(q4k_sbyte(h, j) & 63u);
+    mn = (int)(q4k_sbyte(h, j + 4) & 63u);
   } else {
-    float sum = 0.0f;
-    for (int s = 0; s < nbs; s++) {
-      const int buf = s & 1;
-      nbar_sync_buf<G4_BAR_FULL>(buf);
-      const float4* src = reinterpret_cast<const float4*>(prod + (buf * G4_ROWS + lane) * G4_LD);
-#pragma unroll
-      for (int e4 = 0; e4 < 64; e4 += 8) {  // unrolled: the next group's loads issue during these adds
-        float4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = src[e4 + j];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          sum = fadd(sum, v[j].x);
-          sum = fadd(sum, v[j].y);
-          sum = fadd(sum, v[j].z);
-          sum = fadd(sum, v[j].w);
-        }
-      }
-      if (s + G4_NBUF < nbs) nbar_arrive_buf<G4_BAR_EMPTY>(buf);
-    }
-    if (ok) kq_store(g, row, sum, err);
+    sc = (int)((q4k_sbyte(h, j + 4) & 0x0fu) | ((q4k_sbyte(h, j - 4) >> 6) << 4));
+    mn = (int)((q4k_sbyte(h, j + 4) >> 4) | ((q4k_sbyte(h, j) >> 6) << 4));
   }
+  const float dsc = fmul(d, (float)sc), dmn = fmul(dmin, (float)mn);
+  dsc2 = pk2(dsc, dsc);
+  ndmn2 = pk2(-dmn, -dmn);
+}
+
+// products w * act of the four elements whose nibbles are the low nibbles
+// of the bytes of `nib` (already shifted and masked).  w = (d*sc)*q -
+// (dmin*m): d*sc and q have at most 17 and 4 significant bits, so the
+// product is exact and one fused multiply-add rounds exactly where the
+// reference's subtraction does; then w * act, rounded.
+DI float4 q4k_prod4(uint32_t nib, unsigned long long dsc2, unsigned long long ndmn2, float4 a) {
+  const unsigned long long nmag2 = pk2(-8388608.0f, -8388608.0f);
+  // 2^23 + q as f32 bits, minus 2^23: q exactly
+  const float m0 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540));
+  const float m1 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7541));
+  const float m2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542));
+  const float m3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543));
+  const unsigned long long w01 = fma2(dsc2, add2(pk2(m0, m1), nmag2), ndmn2);
+  const unsigned long long w23 = fma2(dsc2, add2(pk2(m2, m3), nmag2), ndmn2);
+  const float2 r01 = up2(mul2(w01, pk2(a.x, a.y)));
+  const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
+  return make_float4(r01.x, r01.y, r23.x, r23.y);
+}
+
+template <int G4R_STAGES>
+__global__ void __launch_bounds__(32) gemv_q4k_rows_kernel(KqSegs S, const int8_t* __restrict__ aq,
+                                                           const float* __restrict__ ad, uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t g4r_smem[];
+  uint8_t* ring = g4r_smem;                                                      // [stage][32 rows][144]
+  float* act = reinterpret_cast<float*>(g4r_smem + (size_t)G4R_STAGES * G4R_STAGE);  // [K]
+  const KqSeg g = kq_seg(S);
+  const int r0 = ((int)blockIdx.x - g.cta0) * G4R_ROWS;
+  const int nbs = S.nb, nbk = nbs * 8;
+  const int lane = threadIdx.x;
+
+  // raw bytes of super-block s of the 32 rows into slot s % G4R_STAGES;
+  // rows past the matrix are zeros (zero weights, zero products).  Every
+  // lane commits one group per call, so the wait counts stay uniform.
+  auto issue = [&](int s) {
+    if (s < nbs) {
+      uint8_t* dst0 = ring + (size_t)(s % G4R_STAGES) * G4R_STAGE;
+#pragma unroll
+      for (int i = 0; i < 9; i++) {
+        const int c = lane + 32 * i, r = c / 9, part = c - 9 * r;
+        uint8_t* dst = dst0 + r * 144 + part * 16;
+        if (r0 + r < g.rows)
+          g4_cp_async16(dst, g.q + ((size_t)(r0 + r) * nbs + s) * 144 + part * 16);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    g4_cp_commit();
+  };
+  for (int s = 0; s < G4R_STAGES - 1; s++) issue(s);  // weights are constant: before the predecessor ends
+  pdl_enter();
+  q4k_stage_act(act, aq, ad, nbk, lane, 32);
+  __syncwarp();
+
+  float sum = 0.0f;
+  for (int s = 0; s < nbs; s++) {
+    issue(s + G4R_STAGES - 1);             // into the slot read in iteration s - 1
+    g4_cp_wait<G4R_STAGES - 1>();          // this lane's copies of super-block s have landed
+    __syncwarp();                          // ... and every lane's
+    const uint8_t* blk = ring + (size_t)(s % G4R_STAGES) * G4R_STAGE + lane * 144;
+    const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+    const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
+    const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+    const float4* av = reinterpret_cast<const float4*>(act + s * 256);
+    // the super-block's 128 quant bytes at once, and the activation one
+    // sub-block ahead of the arithmetic, so no shared-memory load latency
+    // sits on the chain
+    uint4 qv[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) qv[i] = reinterpret_cast<const uint4*>(blk + 16)[i];
+    float4 acur[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) acur[k] = av[k];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {  // sub-block j: bytes 32 (j / 2) .., low nibbles for even j
+      float4 anext[8];
+      if (j < 7) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) anext[k] = av[(j + 1) * 8 + k];
+      }
+      unsigned long long dsc2, ndmn2;
+      q4k_sub_scales(h, d, dmin, j, dsc2, ndmn2);
+      const uint4 v0 = qv[(j >> 1) * 2], v1 = qv[(j >> 1) * 2 + 1];
+      const uint32_t qw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int k = 0; k < 8; k++) {  // elements 4k .. 4k + 3 of sub-block j, then the chain
+        const float4 r = q4k_prod4((qw[k] >> (4 * (j & 1))) & 0x0f0f0f0fu, dsc2, ndmn2, acur[k]);
+        sum = fadd(sum, r.x);
+        sum = fadd(sum, r.y);
+        sum = fadd(sum, r.z);
+        sum = fadd(sum, r.w);
+      }
+      if (j < 7) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) acur[k] = anext[k];
+      }
+    }
+    __syncwarp();  // every lane is done with the slot before it is refilled
+  }
+  const int row = r0 + lane;
+  if (row < g.rows) kq_store(g, row, sum, err);
 }
 
 // Q6_K: per block the reference forms eight exact integer lane sums
@@ -634,7 +631,7 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   // Q6_K rows per CTA: two (row, block) items per thread per pass of up to
   // 32 blocks (16 rows for wide matrices, 32 when a row has 16 blocks or fewer)
   const bool r32 = !q4 && m[0]->nb <= 16;
-  const int per = q4 ? G4_ROWS : (r32 ? 32 : 16);
+  const int per = q4 ? G4R_ROWS : (r32 ? 32 : 16);
   KqSegs S;
   S.nb = m[0]->nb;
   int ctas = 0;
@@ -656,8 +653,7 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   const unsigned long long bit = 1ull << ((dev & 15) * 4 + kid);
   cudaError_t e = cudaSuccess;
   if (dev >= 16 || !(attr_set.load() & bit)) {
-    e = q4 ? cudaFuncSetAttribute(gemv_q4k_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)g4_smem_bytes(G4_MAX_NB))
+    e = q4 ? raise_smem_cap((const void*)gemv_q4k_rows_kernel<3>, g4r_smem_bytes(3, G4_MAX_NB))
         : r32 ? cudaFuncSetAttribute(gemv_q6k_aux_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)g6_smem<32>())
               : cudaFuncSetAttribute(gemv_q6k_aux_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -665,12 +661,20 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     if (e != cudaSuccess) return e;
     if (dev < 16) attr_set.fetch_or(bit);
   }
-  if (q4)
-    e = launch_k(L, gemv_q4k_chain_kernel, ctas, G4_BLOCK, g4_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
-  else if (r32)
+  if (q4) {
+    static const int sms = [dev] {  // the same part on every device of a node
+      int n = 0;
+      return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+    }();
+    if (ctas > 2 * sms)
+      e = launch_k(L, gemv_q4k_rows_kernel<3>, ctas, G4R_ROWS, g4r_smem_bytes(3, S.nb), S, a.qa_q, a.qa_d, L.err);
+    else if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<8>, g4r_smem_bytes(8, G4_MAX_NB))) == cudaSuccess)
+      e = launch_k(L, gemv_q4k_rows_kernel<8>, ctas, G4R_ROWS, g4r_smem_bytes(8, S.nb), S, a.qa_q, a.qa_d, L.err);
+  } else if (r32) {
     e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
-  else
+  } else {
     e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);
+  }
   if (e != cudaSuccess) return e;
   if (L.launches) ++*L.launches;
   return cudaGetLastError();
