@@ -625,6 +625,181 @@ __global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* 
   *ob = acc;
 }
 
+// ---- one position, fused ------------------------------------------------------
+// For a chunk of one position (decode) the three steps run in one kernel,
+// one CTA per query head, with the score row in shared memory:
+//   scores  the K rows stream through an AD_STAGES-slot cp.async ring of
+//           64-key tiles; four threads share a key, thread quarter r owning
+//           the lane chains 2r and 2r + 1 of the dot (elements 8i + 2r,
+//           8i + 2r + 1, i ascending), so ((l0 + l1) + (l2 + l3)) +
+//           ((l4 + l5) + (l6 + l7)) is two in-thread adds and two shuffles;
+//   softmax max, e_j, the eight ordered z chains (eight threads), p = e / z;
+//   PV      the V tiles stream through the same ring (the first ones are in
+//           flight during the softmax) and thread d runs the chain o[d].
+// Tile rows are HD + 8 floats apart, so the 8-byte reads of a half-warp (four
+// keys x four quarters) and the 4-byte reads of consecutive d fall in
+// distinct banks.
+constexpr int AD_THREADS = 256;
+constexpr int AD_KEYS = 64;
+constexpr int AD_STAGES = 3;
+constexpr int AD_MAX_CTX = 16384;  // score row in shared memory
+template <int HD>
+__host__ __device__ constexpr int ad_tile_floats() {
+  return AD_KEYS * (HD + 8);
+}
+template <int HD>
+size_t ad_smem_bytes(int n_ctx) {
+  return ((size_t)AD_STAGES * ad_tile_floats<HD>() + HD + (size_t)score_ld(n_ctx)) * sizeof(float);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const float* __restrict__ q,
+                                                                 const float* __restrict__ kc,
+                                                                 const float* __restrict__ vc, const int* pos0p,
+                                                                 int gsz, int n_ctx, float scale,
+                                                                 float* __restrict__ out, uint32_t* err) {
+  constexpr int LD = HD + 8;
+  pdl_enter();
+  extern __shared__ __align__(16) float ad_smem[];
+  float* ring = ad_smem;                             // [AD_STAGES][AD_KEYS][LD]
+  float* qs = ring + AD_STAGES * ad_tile_floats<HD>();  // [HD]
+  float* sc = qs + HD;                               // [len]: scores, then e, then p
+  __shared__ float red[AD_THREADS / 32];
+  __shared__ float l8[8];
+  const int h = blockIdx.x, kvh = h / gsz;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int len = *pos0p + 1;
+  const float* kb = kc + (size_t)kvh * n_ctx * HD;
+  const float* vb = vc + (size_t)kvh * n_ctx * HD;
+  float* ob = out + (size_t)h * HD;
+  if (len == 1) {  // score_len == 1 copies v_0 (lib.rs:2319-2322)
+    for (int d = tid; d < HD; d += AD_THREADS) ob[d] = vb[d];
+    return;
+  }
+  const int ntile = (len + AD_KEYS - 1) / AD_KEYS;
+  // tile k of `base` (keys 64k ..) into slot k % AD_STAGES, rows past the
+  // score length zero; an empty group past the last tile keeps the wait
+  // counts uniform
+  auto load_tile = [&](const float* base, int k) {
+    if (k < ntile) {
+      float* dst = ring + (k % AD_STAGES) * ad_tile_floats<HD>();
+      for (int i = tid; i < AD_KEYS * (HD / 4); i += AD_THREADS) {
+        const int jj = i / (HD / 4), c4 = (i - jj * (HD / 4)) * 4;
+        if (k * AD_KEYS + jj < len)
+          cp_async16(dst + jj * LD + c4, base + (size_t)(k * AD_KEYS + jj) * HD + c4);
+        else
+          *reinterpret_cast<float4*>(dst + jj * LD + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int k = 0; k < AD_STAGES - 1; k++) load_tile(kb, k);
+  for (int d = tid; d < HD; d += AD_THREADS) {
+    const float v = q[(size_t)h * HD + d];
+    if (!finite(v)) atomicOr(err, ERRF_NONFINITE);
+    qs[d] = v;
+  }
+
+  // scores: s_j = dot_f32_ref(q, k_j) * scale
+  const int jj = tid >> 2, qr = tid & 3;
+  for (int k = 0; k < ntile; k++) {
+    load_tile(kb, k + AD_STAGES - 1);
+    cp_async_wait<AD_STAGES - 1>();  // tile k has landed
+    __syncthreads();
+    const float* kr = ring + (k % AD_STAGES) * ad_tile_floats<HD>() + jj * LD + 2 * qr;
+    float a0 = 0.0f, a1 = 0.0f;  // lane chains 2 qr and 2 qr + 1
+#pragma unroll
+    for (int i = 0; i < HD / 8; i++) {
+      const float2 kv = *reinterpret_cast<const float2*>(kr + 8 * i);
+      const float2 qv = *reinterpret_cast<const float2*>(qs + 8 * i + 2 * qr);
+      const float2 pr = mul2(qv.x, qv.y, kv.x, kv.y);
+      a0 = fadd(a0, pr.x);
+      a1 = fadd(a1, pr.y);
+    }
+    const float pair = fadd(a0, a1);                                        // l(2qr) + l(2qr + 1)
+    const float quad = fadd(pair, __shfl_xor_sync(0xffffffffu, pair, 1));  // (l0 + l1) + (l2 + l3), ...
+    const float dot = fadd(quad, __shfl_xor_sync(0xffffffffu, quad, 2));
+    const int j = k * AD_KEYS + jj;
+    if (qr == 0 && j < len) {
+      const float sv = fmul(dot, scale);
+      if (!finite(sv)) atomicOr(err, ERRF_NONFINITE);
+      sc[j] = sv;
+    }
+    __syncthreads();  // slot k % AD_STAGES is refilled by the next iteration
+  }
+  for (int k = 0; k < AD_STAGES - 1; k++) load_tile(vb, k);  // V, during the softmax
+
+  // softmax (attention_one_head: e_j = exp(max(s_j - max, -88)), z = sum_f32_ref(e))
+  float mx = -INFINITY;
+  for (int j = tid; j < len; j += AD_THREADS) mx = fmaxf(mx, sc[j]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < AD_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+  for (int j = tid; j < len; j += AD_THREADS) {
+    const float d = fsub(sc[j], mx);
+    sc[j] = expf_det(d > -88.0f ? d : -88.0f);
+  }
+  __syncthreads();
+  if (tid < 8) {  // sum_f32_ref: the ordered chain of lane tid
+    float acc = 0.0f;
+    int j = tid;
+    for (; j + 56 < len; j += 64) {
+      float e[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) e[k] = sc[j + 8 * k];
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+    }
+    for (; j < len; j += 8) acc = fadd(acc, sc[j]);
+    l8[tid] = acc;
+  }
+  __syncthreads();
+  const float z = finish8(l8);
+  if (!finite(z) || z == 0.0f) {
+    if (tid == 0) atomicOr(err, ERRF_NONFINITE);
+    cp_async_wait<0>();  // no copy into this CTA's shared memory outlives it
+    return;
+  }
+  for (int j = tid; j < len; j += AD_THREADS) {
+    const float pj = fdiv(sc[j], z);
+    if (!finite(pj)) atomicOr(err, ERRF_NONFINITE);
+    sc[j] = pj;
+  }
+
+  // o[d] = sum over j of p_j * v_j[d], in order
+  float acc = 0.0f;
+  for (int k = 0; k < ntile; k++) {
+    load_tile(vb, k + AD_STAGES - 1);
+    cp_async_wait<AD_STAGES - 1>();
+    __syncthreads();  // tile k (and, at k = 0, every p_j) visible
+    if (tid < HD) {
+      const float* vr = ring + (k % AD_STAGES) * ad_tile_floats<HD>() + tid;
+      const float* pr = sc + k * AD_KEYS;
+      const int n = min(AD_KEYS, len - k * AD_KEYS);
+      int i = 0;
+      for (; i + 8 <= n; i += 8) {
+        float pv[8], vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          pv[u] = pr[i + u];
+          vv[u] = vr[(i + u) * LD];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc = fadd(acc, fmul(pv[u], vv[u]));
+      }
+      for (; i < n; i++) acc = fadd(acc, fmul(pr[i], vr[i * LD]));
+    }
+    __syncthreads();
+  }
+  if (tid < HD) {
+    if (!finite(acc)) atomicOr(err, ERRF_NONFINITE);
+    ob[tid] = acc;
+  }
+}
+
 template <int HD>
 constexpr int qk_smem_bytes() {
   return (QK_ROWS + QK_KEYS) * (HD + 4) * (int)sizeof(float);
@@ -645,6 +820,16 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
     if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   const int s_ld = score_ld(n_ctx);
+  if (T == 1 && n_ctx <= AD_MAX_CTX) {  // one position: the fused kernel
+    if (cudaError_t e = raise_smem_cap((const void*)attn_decode_kernel<HD>, ad_smem_bytes<HD>(AD_MAX_CTX))) return e;
+    {
+      const cudaError_t e_ = launch_k(L, attn_decode_kernel<HD>, n_head, AD_THREADS, ad_smem_bytes<HD>(n_ctx), q, kc,
+                                      vc, pos0, gsz, n_ctx, scale, out, L.err);
+      if (e_ != cudaSuccess) return e_;
+    }
+    if (L.launches) *L.launches += 1;
+    return cudaGetLastError();
+  }
   dim3 g1((n_ctx + QK_KEYS - 1) / QK_KEYS, (T + qb - 1) / qb, n_head_kv);
   {
     const cudaError_t e_ = launch_k(L, attn_scores_kernel<HD>, g1, QK_THREADS, smem, q, kc, pos0, T, n_head, gsz, qb,

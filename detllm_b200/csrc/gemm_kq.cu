@@ -14,6 +14,7 @@
 // `one` == 1.0 a kernel argument -- exact, and not contractible with the
 // multiply (a packed add fed by a packed multiply is contracted by the code
 // generator).
+#include <algorithm>
 #include <atomic>
 #include <cuda_runtime.h>
 
@@ -544,6 +545,139 @@ DI void q6_aux(const Q6Item& it, const uint32_t* A, const uint32_t* Sp, int* dst
   }
 }
 
+// Activation pairs of Q8_K block b, group pair j (elements 32 j .. 32 j + 31):
+// A[c] and A[8 + c] hold (a[c], a[c + 8]) of the pair's two 16-element
+// groups as sign-extended 16-bit halves, Sp[c] their two sums.
+DI void q6_pairs(const int8_t* __restrict__ aq, int b, int j, uint32_t* A, uint32_t* Sp) {
+  const uint4 v0 = *reinterpret_cast<const uint4*>(aq + (size_t)b * 256 + j * 32);
+  const uint4 v1 = *reinterpret_cast<const uint4*>(aq + (size_t)b * 256 + j * 32 + 16);
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const uint32_t k = (uint32_t)(c & 3);
+    // bytes c and c + 8 of the group, each sign-extended to 16 bits
+    const uint32_t sel = k | ((k | 8u) << 4) | ((4u + k) << 8) | (((4u + k) | 8u) << 12);
+    const uint32_t a0 = prmt_sx(c < 4 ? v0.x : v0.y, c < 4 ? v0.z : v0.w, sel);
+    const uint32_t a1 = prmt_sx(c < 4 ? v1.x : v1.y, c < 4 ? v1.z : v1.w, sel);
+    A[c] = a0;
+    A[8 + c] = a1;
+    const int s0 = (int)(int16_t)(a0 & 0xffffu) + ((int)a0 >> 16);
+    const int s1 = (int)(int16_t)(a1 & 0xffffu) + ((int)a1 >> 16);
+    Sp[c] = s16pair(s0, s1);
+  }
+}
+
+// Q6_K, one position, streamed: the same integer lane sums and chains as
+// gemv_q6k_aux_kernel, laid out so that the weight stream runs at HBM rate.
+// A persistent CTA (one per SM) walks 32-row tiles; each tile is read in
+// passes of 8 blocks, one (row, block) item of 208 bytes per thread, and
+// every thread copies the item it will use in the NEXT pass into its own
+// slot of a two-pass shared-memory buffer with cp.async while it works on
+// the current one (the passes run on across tile boundaries), so about
+// 53 KB per SM are always in flight.  The activation's pairs for all blocks
+// are staged once per CTA.  After a pass, thread (row, class) advances its
+// f32 chain over the pass's blocks in order; after a tile's last pass the
+// row's eight chains are summed in lane order.
+constexpr int Q6S_ROWS = 32;
+constexpr int Q6S_NBP = 8;  // blocks per pass
+constexpr int Q6S_THREADS = Q6S_ROWS * Q6S_NBP;
+constexpr int Q6S_AUX_LD = Q6S_NBP * 8 + 1;  // aux row stride (ints)
+constexpr int Q6S_MAX_NB = 64;               // K <= 16384 (activation pairs staged in shared memory)
+inline size_t q6s_smem_bytes(int nb) {
+  return (size_t)2 * Q6S_THREADS * 208 + (size_t)nb * (128 + 64) * 4 + (size_t)Q6S_ROWS * Q6S_AUX_LD * 4 +
+         (size_t)Q6S_ROWS * (Q6S_NBP + 1) * 4;
+}
+
+// the segment that holds tile `tile` (its first tile is its cta0)
+DI KqSeg kq_seg_at(const KqSegs& S, int tile) {
+  const int i = (int)(tile >= S.s[1].cta0) + (int)(tile >= S.s[2].cta0);
+  return i == 0 ? S.s[0] : (i == 1 ? S.s[1] : S.s[2]);
+}
+
+__global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs S, int tiles,
+                                                                        const int8_t* __restrict__ aq,
+                                                                        const float* __restrict__ ad,
+                                                                        uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t q6s_smem[];
+  uint8_t* items = q6s_smem;                                                      // [2][256][208]
+  uint32_t* apair = reinterpret_cast<uint32_t*>(items + (size_t)2 * Q6S_THREADS * 208);  // [nb][16][8]
+  const int nb = S.nb;
+  uint32_t* spair = apair + (size_t)nb * 128;                                     // [nb][8][8]
+  int* aux = reinterpret_cast<int*>(spair + (size_t)nb * 64);                     // [32][Q6S_AUX_LD]
+  float* ddv = reinterpret_cast<float*>(aux + Q6S_ROWS * Q6S_AUX_LD);             // [32][Q6S_NBP + 1]
+  const int t = threadIdx.x;
+  const int ir = t & 31, ib = t >> 5;  // this thread's item: row ir, block ib of each pass
+  const int cr = t >> 3, cc = t & 7;   // chain: row, class
+  const int npass = (nb + Q6S_NBP - 1) / Q6S_NBP;
+  // the passes of this CTA, in order: tile blockIdx.x + k gridDim.x, pass p
+  const int my_tiles = tiles > (int)blockIdx.x ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nq = my_tiles * npass;
+
+  // issue the copy of pass q's item into buffer q & 1 (and load its scale)
+  auto issue = [&](int q, uint32_t& dbits) {
+    if (q < nq) {
+      const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, b = (q % npass) * Q6S_NBP + ib;
+      const KqSeg g = kq_seg_at(S, tile);
+      const int row = (tile - g.cta0) * Q6S_ROWS + ir;
+      if (b < nb && row < g.rows) {
+        const uint8_t* src = g.q + ((size_t)row * nb + b) * 208;
+        uint8_t* dst = items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208;
+#pragma unroll
+        for (int k = 0; k < 13; k++) g4_cp_async16(dst + 16 * k, src + 16 * k);
+        dbits = g.d[(size_t)row * nb + b];
+      }
+    }
+    g4_cp_commit();
+  };
+  uint32_t dnext = 0;
+  issue(0, dnext);  // weights are constant: before the predecessor ends
+  pdl_enter();
+  for (int i = t; i < nb * 8; i += Q6S_THREADS)
+    q6_pairs(aq, i >> 3, i & 7, apair + (i >> 3) * 128 + (2 * (i & 7)) * 8, spair + (i >> 3) * 64 + (i & 7) * 8);
+  __syncthreads();
+
+  float sum = 0.0f;
+  for (int q = 0; q < nq; q++) {
+    const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, p = q % npass;
+    const KqSeg g = kq_seg_at(S, tile);
+    const int r0 = (tile - g.cta0) * Q6S_ROWS, b0 = p * Q6S_NBP;
+    const uint32_t dcur = dnext;
+    issue(q + 1, dnext);
+    g4_cp_wait<1>();  // this thread's item of pass q has landed (only this thread reads it)
+    const int b = b0 + ib;
+    if (b < nb && r0 + ir < g.rows) {
+      Q6Item it;
+      const uint4* src = reinterpret_cast<const uint4*>(items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208);
+#pragma unroll
+      for (int k = 0; k < 13; k++) {
+        const uint4 v = src[k];
+        it.w[4 * k] = v.x;
+        it.w[4 * k + 1] = v.y;
+        it.w[4 * k + 2] = v.z;
+        it.w[4 * k + 3] = v.w;
+      }
+      q6_aux(it, apair + b * 128, spair + b * 64, aux + ir * Q6S_AUX_LD + ib * 8);
+      ddv[ir * (Q6S_NBP + 1) + ib] = fmul(f16_bits_to_f32((uint16_t)dcur), ad[b]);
+    }
+    __syncthreads();  // aux / ddv of the pass complete
+    if (r0 + cr < g.rows) {
+      const int nbp = min(Q6S_NBP, nb - b0);
+      const int* src = aux + cr * Q6S_AUX_LD + cc;
+      const float* dd = ddv + cr * (Q6S_NBP + 1);
+      for (int bb = 0; bb < nbp; bb++) sum = fadd(sum, fmul(dd[bb], __int2float_rn(src[bb * 8])));
+    }
+    if (p == npass - 1) {
+      // ((((0 + s0) + s1) + ...) + s7) within each group of eight lanes
+      float v = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) v = fadd(v, __shfl_sync(0xffffffffu, sum, (t & 31 & ~7) + k));
+      const int row = r0 + cr;
+      if (cc == 0 && row < g.rows) kq_store(g, row, v, err);
+      sum = 0.0f;
+    }
+    __syncthreads();  // aux / ddv free for the next pass
+  }
+}
+
 template <int R>
 __global__ void __launch_bounds__(G6_THREADS, 1) gemv_q6k_aux_kernel(KqSegs S, const int8_t* __restrict__ aq,
                                                                      const float* __restrict__ ad, uint32_t* err) {
@@ -628,13 +762,15 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   for (int i = 0; i < n; i++)
     if (!kq_decode_supported(*m[i])) return cudaErrorInvalidValue;
   const bool q4 = m[0]->type == GT_Q4_K;
-  // Q6_K rows per CTA: two (row, block) items per thread per pass of up to
-  // 32 blocks (16 rows for wide matrices, 32 when a row has 16 blocks or fewer)
-  const bool r32 = !q4 && m[0]->nb <= 16;
-  const int per = q4 ? G4R_ROWS : (r32 ? 32 : 16);
+  // Q6_K: the streamed kernel when the activation pairs fit in shared memory;
+  // else two (row, block) items per thread per pass of up to 32 blocks (16
+  // rows per CTA for wide matrices, 32 when a row has 16 blocks or fewer)
+  const bool q6s = !q4 && m[0]->nb <= Q6S_MAX_NB;
+  const bool r32 = !q4 && !q6s && m[0]->nb <= 16;
+  const int per = q4 ? G4R_ROWS : (q6s ? Q6S_ROWS : (r32 ? 32 : 16));
   KqSegs S;
   S.nb = m[0]->nb;
-  int ctas = 0;
+  int ctas = 0;  // CTAs of the per-tile kernels, tiles of the streamed one
   for (int i = 0; i < 3; i++) {
     KqSeg& g = S.s[i];
     if (i < n) {
@@ -646,34 +782,32 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     }
   }
   if (ctas == 0) return cudaSuccess;
-  static std::atomic<unsigned long long> attr_set{0};  // one bit per device and kernel (several host threads)
   int dev = 0;
-  cudaGetDevice(&dev);
-  const int kid = q4 ? 0 : (r32 ? 1 : 2);
-  const unsigned long long bit = 1ull << ((dev & 15) * 4 + kid);
-  cudaError_t e = cudaSuccess;
-  if (dev >= 16 || !(attr_set.load() & bit)) {
-    e = q4 ? raise_smem_cap((const void*)gemv_q4k_rows_kernel<3>, g4r_smem_bytes(3, G4_MAX_NB))
-        : r32 ? cudaFuncSetAttribute(gemv_q6k_aux_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)g6_smem<32>())
-              : cudaFuncSetAttribute(gemv_q6k_aux_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)g6_smem<16>());
-    if (e != cudaSuccess) return e;
-    if (dev < 16) attr_set.fetch_or(bit);
-  }
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static const int sms = [dev] {  // the same part on every device of a node
+    int c = 0;
+    return cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && c > 0 ? c : 148;
+  }();
   if (q4) {
-    static const int sms = [dev] {  // the same part on every device of a node
-      int n = 0;
-      return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
-    }();
-    if (ctas > 2 * sms)
-      e = launch_k(L, gemv_q4k_rows_kernel<3>, ctas, G4R_ROWS, g4r_smem_bytes(3, S.nb), S, a.qa_q, a.qa_d, L.err);
-    else if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<8>, g4r_smem_bytes(8, G4_MAX_NB))) == cudaSuccess)
+    if (ctas > 2 * sms) {
+      if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<3>, g4r_smem_bytes(3, G4_MAX_NB))) == cudaSuccess)
+        e = launch_k(L, gemv_q4k_rows_kernel<3>, ctas, G4R_ROWS, g4r_smem_bytes(3, S.nb), S, a.qa_q, a.qa_d,
+                     L.err);
+    } else if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<8>, g4r_smem_bytes(8, G4_MAX_NB))) ==
+               cudaSuccess) {
       e = launch_k(L, gemv_q4k_rows_kernel<8>, ctas, G4R_ROWS, g4r_smem_bytes(8, S.nb), S, a.qa_q, a.qa_d, L.err);
+    }
+  } else if (q6s) {
+    if ((e = raise_smem_cap((const void*)gemv_q6k_stream_kernel, q6s_smem_bytes(Q6S_MAX_NB))) == cudaSuccess)
+      e = launch_k(L, gemv_q6k_stream_kernel, std::min(ctas, sms), Q6S_THREADS, q6s_smem_bytes(S.nb), S, ctas,
+                   a.qk_q, a.qk_d, L.err);
   } else if (r32) {
-    e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
+    if ((e = raise_smem_cap((const void*)gemv_q6k_aux_kernel<32>, g6_smem<32>())) == cudaSuccess)
+      e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
   } else {
-    e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);
+    if ((e = raise_smem_cap((const void*)gemv_q6k_aux_kernel<16>, g6_smem<16>())) == cudaSuccess)
+      e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);
   }
   if (e != cudaSuccess) return e;
   if (L.launches) ++*L.launches;
