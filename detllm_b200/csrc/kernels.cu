@@ -211,23 +211,35 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   __shared__ float lanes[8];
   __shared__ float r_s;
   const bool staged = n <= RMS_MAX_SMEM;
-  if (staged)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      xs[i] = xr[i];
-      xs[n + i] = w[i];
+  if (staged) {
+    if ((n & 3) == 0 && (((uintptr_t)xr | (uintptr_t)w) & 15) == 0) {  // float4 copies, two per thread in flight
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      const float4* w4 = reinterpret_cast<const float4*>(w);
+      for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+        const float4 a = x4[i], b = w4[i];
+        reinterpret_cast<float4*>(xs)[i] = a;
+        reinterpret_cast<float4*>(xs + n)[i] = b;
+      }
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        xs[i] = xr[i];
+        xs[n + i] = w[i];
+      }
     }
+  }
   __syncthreads();
   const float* src = staged ? xs : xr;
   const float* wv = staged ? xs + n : w;
-  if (threadIdx.x < 8) {
+  if (threadIdx.x < 8) {  // sum_squares_f32_ref: the ordered chain of lane threadIdx.x
     float acc = 0.0f;
     int i = threadIdx.x;
-    for (; i + 56 < n; i += 64) {
-      float a[8];
+    // two groups of eight loads in flight ahead of the adds
+    for (; i + 120 < n; i += 128) {
+      float a[16];
 #pragma unroll
-      for (int k = 0; k < 8; k++) a[k] = src[i + 8 * k];
+      for (int k = 0; k < 16; k++) a[k] = src[i + 8 * k];
 #pragma unroll
-      for (int k = 0; k < 8; k++) acc = fadd(acc, fmul(a[k], a[k]));
+      for (int k = 0; k < 16; k++) acc = fadd(acc, fmul(a[k], a[k]));
     }
     for (; i < n; i += 8) acc = fadd(acc, fmul(src[i], src[i]));
     lanes[threadIdx.x] = acc;
@@ -427,22 +439,26 @@ __global__ void gemv_generic_kernel(DevMatrix m, DevActs a, int T, float* out, i
 
 // ---- RoPE + KV store: apply_rope (det-model lib.rs:2011-2051) and
 // KvCache::store (:883-913) ------------------------------------------------
+// One thread per item, all items of a position in flight at once: a (q or k)
+// rotation pair, or a K/V element past the rotated dims.  A k pair also
+// stores its two rotated values and the V values at the same two dims in
+// the cache, so no second pass (and no barrier) is needed.
 __global__ void rope_store_kernel(float* q, float* k, const float* v, const int* pos0p, int n_head, int n_head_kv,
                                   int hd, int half, int pairing, const float* cos_t, const float* sin_t, float* kc,
                                   float* vc, int n_ctx, uint32_t* err) {
   pdl_enter();
   const int t = blockIdx.x;
   const int pos = *pos0p + t;
-  const float* cs = cos_t + (size_t)pos * half;
-  const float* sn = sin_t + (size_t)pos * half;
   float* qt = q + (size_t)t * n_head * hd;
   float* kt = k + (size_t)t * n_head_kv * hd;
   const float* vt = v + (size_t)t * n_head_kv * hd;
-  const int nq = n_head * half, nk = n_head_kv * half;
-  for (int i = threadIdx.x; i < nq + nk; i += blockDim.x) {
-    float* base = i < nq ? qt : kt;
-    const int ii = i < nq ? i : i - nq;
-    const int head = ii / half, j = ii % half;
+  const int nq = n_head * half, nk = n_head_kv * half, rest = hd - 2 * half;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;
+  if (i < nq + nk) {
+    const bool isk = i >= nq;
+    float* base = isk ? kt : qt;
+    const int ii = isk ? i - nq : i;
+    const int head = ii / half, j = ii - head * half;
     int a, b;
     if (pairing == 0) {
       a = head * hd + 2 * j;
@@ -452,20 +468,27 @@ __global__ void rope_store_kernel(float* q, float* k, const float* v, const int*
       b = a + half;
     }
     const float x0 = base[a], x1 = base[b];
-    const float c = cs[j], s = sn[j];
-    const float y0 = fsub(fmul(x0, c), fmul(x1, s));
-    const float y1 = fadd(fmul(x0, s), fmul(x1, c));
+    const float c = cos_t[(size_t)pos * half + j], sv = sin_t[(size_t)pos * half + j];
+    const float y0 = fsub(fmul(x0, c), fmul(x1, sv));
+    const float y1 = fadd(fmul(x0, sv), fmul(x1, c));
     if (!finite(y0) || !finite(y1) || !finite(x0) || !finite(x1)) flag(err, ERRF_NONFINITE);
     base[a] = y0;
     base[b] = y1;
-  }
-  __syncthreads();
-  // KV store for every kv head (K after RoPE)
-  for (int i = threadIdx.x; i < n_head_kv * hd; i += blockDim.x) {
-    const int kh = i / hd, dd = i % hd;
-    const size_t off = ((size_t)kh * n_ctx + pos) * hd + dd;
-    const float kv = kt[i], vv = vt[i];
+    if (isk) {  // the KV store of these two dims (K after RoPE)
+      const float va = vt[a], vb = vt[b];
+      if (!finite(va) || !finite(vb)) flag(err, ERRF_NONFINITE);
+      const size_t row = ((size_t)head * n_ctx + pos) * hd;
+      kc[row + (a - head * hd)] = y0;
+      kc[row + (b - head * hd)] = y1;
+      vc[row + (a - head * hd)] = va;
+      vc[row + (b - head * hd)] = vb;
+    }
+  } else if (i < nq + nk + n_head_kv * rest) {  // K / V dims past the rotated ones: stored as they are
+    const int ii = i - nq - nk;
+    const int kh = ii / rest, dd = 2 * half + (ii - kh * rest);
+    const float kv = kt[kh * hd + dd], vv = vt[kh * hd + dd];
     if (!finite(kv) || !finite(vv)) flag(err, ERRF_NONFINITE);
+    const size_t off = ((size_t)kh * n_ctx + pos) * hd + dd;
     kc[off] = kv;
     vc[off] = vv;
   }
@@ -1165,8 +1188,10 @@ cudaError_t launch_rope_store(const Launch& L, float* q, float* k, const float* 
                               int n_head_kv, int head_dim, int rope_dim, int pairing, const float* cos_t,
                               const float* sin_t, float* kc, float* vc, int n_ctx) {
   {
-    const cudaError_t e_ = launch_k(L, rope_store_kernel, T, 256, 0, q, k, v, pos0, n_head, n_head_kv, head_dim,
-        rope_dim / 2, pairing, cos_t, sin_t, kc, vc, n_ctx, L.err);
+    const int items = (n_head + n_head_kv) * (rope_dim / 2) + n_head_kv * (head_dim - rope_dim);
+    const cudaError_t e_ = launch_k(L, rope_store_kernel, dim3(T, (items + 255) / 256), 256, 0, q, k, v, pos0,
+                                    n_head, n_head_kv, head_dim, rope_dim / 2, pairing, cos_t, sin_t, kc, vc, n_ctx,
+                                    L.err);
     if (e_ != cudaSuccess) return e_;
   }
   return post(L);
