@@ -113,6 +113,7 @@ def all_max(x, ws):
 
 
 LAYERS = 0  # --layers: cut the headline model's layer count (profiling captures only)
+PROFILE_ANY_LAYERS = False  # --decode-profile: --layers applies to the profiled configuration
 
 
 def model_bytes(config, rank=0, ws=1):
@@ -122,7 +123,7 @@ def model_bytes(config, rank=0, ws=1):
     from detllm_b200 import synth as S
 
     spec = S.CONFIGS[config]
-    if LAYERS and config == HEADLINE:
+    if LAYERS and (config == HEADLINE or PROFILE_ANY_LAYERS):
         spec = dataclasses.replace(spec, n_layer=LAYERS)
     path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{config}_L{spec.n_layer}_s{spec.seed}.gguf")
     if rank == 0 and not os.path.exists(path):
@@ -247,10 +248,48 @@ def decode_probe(model, vocab, n_ctx, n_prefix=1024, n_steps=48):
     return out
 
 
-def decode_roofline(dec, config, peak, peak_kind):
+# bytes per weight of the GEMV matrix types (ggml block sizes)
+TYPE_BYTES_PER_WEIGHT = {"Q8_0": 34 / 32, "Q4_0": 18 / 32, "Q4_K": 144 / 256, "Q6_K": 210 / 256}
+
+
+def decode_chain_floor(spec, add_cycles, sm_mhz, hbm_gbs):
+    """The floor of one token's weight GEMVs: each launch takes at least its
+    bytes at HBM rate and, for a Q4_K matrix, its row chain of K dependent
+    adds (det-quant lib.rs:281-315) at the measured latency of one add.
+    Q8_0 / Q4_0 / Q6_K rows are chains of K / 32 or K / 256 adds per lane,
+    far below their bytes."""
+    from detllm_b200 import synth as S
+
+    names = {S.GT_Q8_0: "Q8_0", S.GT_Q4_0: "Q4_0", S.GT_Q4_K: "Q4_K", S.GT_Q6_K: "Q6_K"}
+    hd, d = spec.head_dim, spec.d
+    qkv_rows = (spec.n_head + 2 * spec.n_head_kv) * hd
+    launches = [(spec.t_attn, qkv_rows, d), (spec.t_attn, d, spec.n_head * hd), (spec.t_gate_up, 2 * spec.d_ff, d),
+                (spec.t_down, d, spec.d_ff)]
+    us = 0.0
+    parts = {}
+    for t, rows, k in launches:
+        name = names.get(t)
+        if name is None:
+            return None
+        mem = rows * k * TYPE_BYTES_PER_WEIGHT[name] / (hbm_gbs * 1e3)  # us
+        chain = k * add_cycles / sm_mhz if name == "Q4_K" else 0.0
+        parts[f"{name} {rows}x{k}"] = {"us": round(max(mem, chain), 2), "bound": "chain" if chain > mem else "hbm"}
+        us += max(mem, chain) * spec.n_layer
+    out_t = names.get(spec.t_embd if spec.tied else spec.t_out)
+    if out_t is None:
+        return None
+    us += spec.vocab * d * TYPE_BYTES_PER_WEIGHT[out_t] / (hbm_gbs * 1e3)
+    return {"ms_per_token": us / 1000.0, "add_cycles": add_cycles, "sm_mhz": sm_mhz, "per_layer_launch": parts}
+
+
+def decode_roofline(dec, config, peak, peak_kind, floor=None):
     n = max(dec["gemv_launches_per_token"], 1)
     gbs = dec["gemv_stream_gbs"]
-    return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak if gbs else None,
+    extra = {}
+    if floor:
+        extra = {"chain_floor": floor,
+                 "frac_of_chain_floor": floor["ms_per_token"] / dec["gemv_stream_ms_per_token"]}
+    return {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak if gbs else None, **extra,
             "traffic": DECODE_GEMV_TRAFFIC_PER_LAUNCH.get(config),
             "traffic_unit": "bytes per launch (ncu capture, see profiles/)",
             "kernel": f"decode weight GEMVs, one token's {n} launches back to back ({config})",
@@ -337,7 +376,7 @@ def timed(fn, steps, warmup, model=None):
     return time.perf_counter() - t, out
 
 
-def sub_configs(D, S, peak, peak_kind):
+def sub_configs(D, S, peak, peak_kind, add_cycles=None, sm_mhz=None):
     """BASELINE configs 2-4 on this GPU (N = 1): each model built, loaded,
     measured and freed in turn."""
     out = {}
@@ -355,7 +394,9 @@ def sub_configs(D, S, peak, peak_kind):
     D.set_encode_chunk(0)
     dec = decode_probe(m, spec.vocab, 2048)
     r["decode"] = dec
-    r["roofline"] = decode_roofline(dec, "tinyllama-q8_0", peak, peak_kind)
+    r["roofline"] = decode_roofline(dec, "tinyllama-q8_0", peak, peak_kind,
+                                    decode_chain_floor(spec, add_cycles, sm_mhz, peak) if add_cycles and sm_mhz
+                                    else None)
     m.close()
     out["tinyllama-q8_0"] = r
     # config 3: TinyLlama Q4_K_M, compress and decompress of Markov bytes
@@ -536,6 +577,7 @@ def run(args):
     total = PREFIX * args.steps * ws
     peak, peak_kind = peaks()
     props = torch.cuda.get_device_properties(local)
+    add_cycles = D.add_latency_cycles(local)  # measured: the floor of every ordered chain
     line = {
         "metric": METRIC, "value": total / dev_max, "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_max / args.steps,
@@ -552,7 +594,9 @@ def run(args):
         "gpu_launches": int(st.launches),
         "roofline": encode_roofline(kprof, 2.0 * q4k_weight_positions(spec, PREFIX), clocks.get("sm_mhz"),
                                     props.multi_processor_count),
-        "roofline_decode": decode_roofline(dec, HEADLINE, peak, peak_kind),
+        "roofline_decode": decode_roofline(dec, HEADLINE, peak, peak_kind,
+                                           decode_chain_floor(spec, add_cycles, clocks.get("sm_mhz"), peak)
+                                           if add_cycles and clocks.get("sm_mhz") else None),
         "full_stream": full_stream_estimate(len(segs[0]), HEAD_CTX, dev_max / args.steps, ws),
         "decode": dec,
         "round_trip_ok": round_trip_ok,
@@ -572,12 +616,47 @@ def run(args):
         line["parity"] = {"prefix_tokens": len(syms), "payload_equal": got == want, "payload_bytes": len(got)}
     model.close()
     if ws == 1 and not args.no_configs:
-        line["configs"] = sub_configs(D, S, peak, peak_kind)
+        line["configs"] = sub_configs(D, S, peak, peak_kind, add_cycles, clocks.get("sm_mhz"))
     print(json.dumps(line), flush=True)
 
 
+def run_decode_profile(args):
+    """One configuration's one-position forwards for a profiler: a 512-token
+    prefill, 6 warm-up tokens, 20 timed tokens (device time printed), then
+    `--profile-tokens` more between cudaProfilerStart and cudaProfilerStop, so
+    that `ncu --profile-from-start off` sees exactly those launches."""
+    import torch
+
+    import detllm_b200 as D
+    from detllm_b200 import synth as S
+
+    spec, gguf = model_bytes(args.decode_profile)
+    m = D.Model(gguf)
+    toks = S.zipf_tokens(600 + args.profile_tokens, spec.vocab, seed=3)
+    with m.session(n_ctx=2048, max_chunk=512) as s:
+        s.forward(toks[:512], 0)
+        pos = 512
+        for _ in range(6):
+            s.forward(toks[pos:pos + 1], pos)
+            pos += 1
+        s.stats(reset=True)
+        for _ in range(20):
+            s.forward(toks[pos:pos + 1], pos)
+            pos += 1
+        st = s.stats(reset=True)
+        torch.cuda.profiler.start()
+        for _ in range(args.profile_tokens):
+            s.forward(toks[pos:pos + 1], pos)
+            pos += 1
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    m.close()
+    print(json.dumps({"decode_profile": args.decode_profile, "layers": spec.n_layer, "position": 512,
+                      "ms_per_token": st.forward_ms / 20}), flush=True)
+
+
 def main():
-    global PREFIX, LAYERS
+    global PREFIX, LAYERS, PROFILE_ANY_LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -590,9 +669,16 @@ def main():
                     help="bytes of each segment per step (default one n_ctx window; smaller is for profiling)")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers of the headline model (default all; fewer only for profiling captures)")
+    ap.add_argument("--decode-profile", default=None, metavar="CONFIG",
+                    help="only one-position forwards of CONFIG, for a profiler (see run_decode_profile)")
+    ap.add_argument("--profile-tokens", type=int, default=1)
     args = ap.parse_args()
     PREFIX = args.prefix
     LAYERS = args.layers
+    if args.decode_profile:
+        PROFILE_ANY_LAYERS = True
+        run_decode_profile(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

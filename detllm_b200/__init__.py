@@ -111,6 +111,7 @@ def lib():
             "det_symbol_ranges_noalloc": (I, [P, U32, U32, P, I, P, P]),
             "det_tp_exchange_timeout_selftest": (I, [I]),
             "det_q6k_pipeline_timeout_selftest": (I, [I]),
+            "det_add_latency_cycles": (I, [I, C.POINTER(C.c_double)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -325,6 +326,14 @@ def set_q8_tensor_cores(enable: bool) -> bool:
     prev = C.c_int()
     _check(lib().det_set_q8_tensor_cores(int(bool(enable)), C.byref(prev)), "det_set_q8_tensor_cores")
     return bool(prev.value)
+
+
+def add_latency_cycles(device: int = 0) -> float:
+    """Measured cycles of one dependent f32 add on `device` (the floor of
+    every ordered chain)."""
+    v = C.c_double()
+    _check(lib().det_add_latency_cycles(int(device), C.byref(v)), "det_add_latency_cycles")
+    return v.value
 
 
 def set_profiling(enable: bool) -> None:

@@ -567,7 +567,7 @@ DI void q6_pairs(const int8_t* __restrict__ aq, int b, int j, uint32_t* A, uint3
 }
 
 // Q6_K, one position, streamed: the same integer lane sums and chains as
-// gemv_q6k_aux_kernel, laid out so that the weight stream runs at HBM rate.
+// gemv_q6k_aux_kernel, with the weight stream overlapping the integer work.
 // A persistent CTA (one per SM) walks 32-row tiles; each tile is read in
 // passes of 8 blocks, one (row, block) item of 208 bytes per thread, and
 // every thread copies the item it will use in the NEXT pass into its own
@@ -762,12 +762,11 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   for (int i = 0; i < n; i++)
     if (!kq_decode_supported(*m[i])) return cudaErrorInvalidValue;
   const bool q4 = m[0]->type == GT_Q4_K;
-  // Q6_K: the streamed kernel when the activation pairs fit in shared memory;
-  // else two (row, block) items per thread per pass of up to 32 blocks (16
-  // rows per CTA for wide matrices, 32 when a row has 16 blocks or fewer)
+  // Q6_K: the streamed kernel when the activation pairs fit in shared memory,
+  // else two (row, block) items per thread per pass of up to 32 blocks, 16
+  // rows per CTA
   const bool q6s = !q4 && m[0]->nb <= Q6S_MAX_NB;
-  const bool r32 = !q4 && !q6s && m[0]->nb <= 16;
-  const int per = q4 ? G4R_ROWS : (q6s ? Q6S_ROWS : (r32 ? 32 : 16));
+  const int per = q4 ? G4R_ROWS : (q6s ? Q6S_ROWS : 16);
   KqSegs S;
   S.nb = m[0]->nb;
   int ctas = 0;  // CTAs of the per-tile kernels, tiles of the streamed one
@@ -802,9 +801,6 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     if ((e = raise_smem_cap((const void*)gemv_q6k_stream_kernel, q6s_smem_bytes(Q6S_MAX_NB))) == cudaSuccess)
       e = launch_k(L, gemv_q6k_stream_kernel, std::min(ctas, sms), Q6S_THREADS, q6s_smem_bytes(S.nb), S, ctas,
                    a.qk_q, a.qk_d, L.err);
-  } else if (r32) {
-    if ((e = raise_smem_cap((const void*)gemv_q6k_aux_kernel<32>, g6_smem<32>())) == cudaSuccess)
-      e = launch_k(L, gemv_q6k_aux_kernel<32>, ctas, G6_THREADS, g6_smem<32>(), S, a.qk_q, a.qk_d, L.err);
   } else {
     if ((e = raise_smem_cap((const void*)gemv_q6k_aux_kernel<16>, g6_smem<16>())) == cudaSuccess)
       e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);

@@ -198,6 +198,8 @@ cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, cons
 cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
                               const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3);
 cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n);
+// one warp, n pairs of dependent f32 adds, clock cycles into *cycles
+cudaError_t launch_add_chain(const float* x, float* out, long long* cycles, int n);
 // Row-sharded tensor parallelism (exchange.cu): copy column slices of
 // [T][ld] f32 activations that live on other parts (peer memory) into `dst`:
 // dst[p * ld_dst + col0 + c] = src[p * ld + c] for c < n, for every source.

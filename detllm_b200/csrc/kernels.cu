@@ -1079,6 +1079,27 @@ __global__ void expf_kernel(const float* x, float* y, long long n) {
 
 }  // namespace
 
+// One warp runs n pairs of dependent rounded adds between two clock reads:
+// the cycles per add are the latency floor of every ordered f32 chain.
+__global__ void add_chain_kernel(const float* __restrict__ x, float* __restrict__ out, long long* cycles, int n) {
+  float s = 0.0f;
+  const float a = x[threadIdx.x], b = x[threadIdx.x + 32];
+  const long long t0 = clock64();
+#pragma unroll 16
+  for (int i = 0; i < n; i++) {
+    s = fadd(s, a);
+    s = fadd(s, b);
+  }
+  const long long t1 = clock64();
+  out[threadIdx.x] = s;
+  if (threadIdx.x == 0) *cycles = t1 - t0;
+}
+
+cudaError_t launch_add_chain(const float* x, float* out, long long* cycles, int n) {
+  add_chain_kernel<<<1, 32>>>(x, out, cycles, n);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n) {
   expf_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n);
   return cudaGetLastError();

@@ -997,6 +997,32 @@ det_status det_device_expf(int device, const float* x, float* y, size_t n) {
   return cuda_status(e);
 }
 
+det_status det_add_latency_cycles(int device, double* cycles_per_add) {
+  if (!cycles_per_add) return DET_ERR_INVALID_ARGUMENT;
+  int cnt = 0;
+  if (cudaGetDeviceCount(&cnt) != cudaSuccess || cnt == 0) return DET_ERR_NO_DEVICE;
+  if (device < 0 || device >= cnt) return DET_ERR_INVALID_ARGUMENT;
+  CK(cudaSetDevice(device));
+  void* mem = nullptr;
+  CK(cudaMalloc(&mem, 1024));  // 64 inputs (zeros), 32 outputs, the cycle count
+  float* x = static_cast<float*>(mem);
+  long long* cyc = reinterpret_cast<long long*>(static_cast<char*>(mem) + 768);
+  const int n = 4096;
+  cudaError_t e = cudaMemset(mem, 0, 1024);
+  double best = 0.0;
+  for (int rep = 0; rep < 3 && e == cudaSuccess; rep++) {  // the first run also loads the code
+    long long c = 0;
+    e = launch_add_chain(x, x + 64, cyc, n);
+    if (e == cudaSuccess) e = cudaMemcpy(&c, cyc, sizeof c, cudaMemcpyDeviceToHost);
+    const double v = (double)c / (2.0 * n);
+    if (e == cudaSuccess && (best == 0.0 || v < best)) best = v;
+  }
+  cudaFree(mem);
+  if (e != cudaSuccess) return cuda_status(e);
+  *cycles_per_add = best;
+  return DET_OK;
+}
+
 det_status det_session_gemv_stream(det_session* s, uint32_t reps, double* ms_per_pass, double* bytes_per_pass) {
   if (!s || !ms_per_pass || !bytes_per_pass || reps == 0) return DET_ERR_INVALID_ARGUMENT;
   if (s->tp) return DET_ERR_UNSUPPORTED_MODEL_FEATURE;

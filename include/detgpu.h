@@ -224,6 +224,11 @@ det_status det_tp_exchange_timeout_selftest(int device);
  * (expected result DET_ERR_TIMEOUT), then the same launch with every stage
  * copied must finish without an error (else DET_ERR_CUDA). */
 det_status det_q6k_pipeline_timeout_selftest(int device);
+/* Measured latency of one dependent rounded f32 add on `device`, in SM
+ * clock cycles (one warp, 8,192 adds between two clock reads, best of
+ * three): the floor of every ordered chain, e.g. the K adds of a Q4_K row.
+ * A benchmark hook with no counterpart in the reference. */
+det_status det_add_latency_cycles(int device, double* cycles_per_add);
 
 /* ---- timing hooks for benchmarks (device time of the last call) -------- */
 typedef struct {

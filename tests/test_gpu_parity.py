@@ -38,6 +38,11 @@ SPECS = {
     "q4k_q6k_wide_ffn": S.ModelSpec(n_layer=1, d=256, d_ff=8448, n_head=4, n_head_kv=2, vocab=1000, ctx=64,
                                     t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
                                     t_out=S.GT_Q6_K, seed=6),
+    # a Q6_K ffn_down wider than 16,384 (65 blocks): the one-position Q6_K
+    # kernel that stages no activation pairs
+    "q6k_down_65_blocks": S.ModelSpec(n_layer=1, d=256, d_ff=16640, n_head=4, n_head_kv=2, vocab=300, ctx=64,
+                                      t_embd=S.GT_Q4_K, t_attn=S.GT_Q4_K, t_gate_up=S.GT_Q4_K, t_down=S.GT_Q6_K,
+                                      t_out=S.GT_Q6_K, seed=8),
     "f16_f32_escapes": S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=2, vocab=300, ctx=32,
                                    t_embd=S.GT_F16, t_attn=S.GT_F32, t_gate_up=S.GT_F16, t_down=S.GT_Q8_0,
                                    t_out=S.GT_F32, escape_bytes=(10, 32, 65), seed=3),
