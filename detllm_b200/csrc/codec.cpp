@@ -124,39 +124,66 @@ det_status encode_impl(det_model* m, const uint32_t* sym, size_t n, uint32_t n_c
     if (w.needed) need_device = true;
   if (need_device)
     if (det_status st = session_acquire(m, n_ctx, encode_chunk(), &s)) return st;
+  // the forwards as one list of chunks: window, first position, length
+  struct Chunk {
+    size_t wi, p0;
+    uint32_t cnt;
+  };
+  std::vector<Chunk> chunks;
+  if (s)
+    for (size_t wi = 0; wi < windows.size(); wi++)
+      for (size_t p0 = 0; p0 < windows[wi].needed; p0 += (size_t)s->max_chunk)
+        chunks.push_back({wi, p0, (uint32_t)std::min<size_t>((size_t)s->max_chunk, windows[wi].needed - p0)});
+  // Chunk k + 1 is enqueued as soon as chunk k's ranges are on the host, so
+  // the host range-codes chunk k while the device runs chunk k + 1 (the
+  // ranges call is the synchronisation point, and a forward's errors surface
+  // there).  A window after the first starts from a cleared KV cache.
+  // Tensor-parallel sessions forward synchronously (their forward spans
+  // several devices).
+  auto enqueue = [&](size_t k) -> det_status {
+    const Chunk& c = chunks[k];
+    if (c.p0 == 0 && c.wi > 0)
+      if (det_status st = det_session_reset(s)) return st;
+    const uint32_t* tk = tokens.data() + windows[c.wi].start + c.p0;
+    return s->tp ? det_forward(s, tk, c.cnt, (uint32_t)c.p0, nullptr) : forward_enqueue(s, tk, c.cnt, (uint32_t)c.p0);
+  };
   std::vector<uint32_t> rows, qsym;
   std::vector<det_symbol_range> ranges;
-  det_status st = DET_OK;
-  for (size_t wi = 0; wi < windows.size() && !st; wi++) {
-    const WindowPlan& w = windows[wi];
-    if (w.needed == 0) continue;
-    if (wi > 0) st = det_session_reset(s);
-    const uint32_t chunk = (uint32_t)s->max_chunk;
-    for (size_t p0 = 0; p0 < w.needed && !st; p0 += chunk) {
-      const uint32_t cnt = (uint32_t)std::min<size_t>(chunk, w.needed - p0);
-      st = det_forward(s, tokens.data() + w.start + p0, cnt, (uint32_t)p0, nullptr);
-      if (st) break;
-      rows.clear();
-      qsym.clear();
-      size_t j = next;
-      for (; j < n; j++) {
-        const SymbolPlan& sp = plan[j];
-        if (sp.window < 0) {
-          // a uniform symbol after a device window can only follow a window
-          // with no tokens, which cannot happen mid-stream
-          break;
-        }
-        if ((size_t)sp.window != wi || (size_t)sp.pos >= p0 + cnt) break;
-        rows.push_back((uint32_t)(sp.pos - p0));
-        qsym.push_back(sym[j]);
+  det_status st = chunks.empty() ? DET_OK : enqueue(0);
+  for (size_t k = 0; k < chunks.size() && !st; k++) {
+    const Chunk& c = chunks[k];
+    rows.clear();
+    qsym.clear();
+    size_t j = next;
+    for (; j < n; j++) {
+      const SymbolPlan& sp = plan[j];
+      if (sp.window < 0) {
+        // a uniform symbol after a device window can only follow a window
+        // with no tokens, which cannot happen mid-stream
+        break;
       }
-      ranges.resize(rows.size());
-      if (!rows.empty()) st = det_symbol_ranges(s, rows.data(), qsym.data(), (uint32_t)rows.size(), escapes,
-                                                ranges.data());
-      for (size_t k = 0; k < rows.size() && !st; k++) st = enc.encode(ranges[k].cum, ranges[k].freq, ranges[k].total);
-      next = j;
-      if (!st) st = drain_uniform();
+      if ((size_t)sp.window != c.wi || (size_t)sp.pos >= c.p0 + c.cnt) break;
+      rows.push_back((uint32_t)(sp.pos - c.p0));
+      qsym.push_back(sym[j]);
     }
+    ranges.resize(rows.size());
+    if (!rows.empty()) {
+      st = det_symbol_ranges(s, rows.data(), qsym.data(), (uint32_t)rows.size(), escapes, ranges.data());
+    } else {  // no symbol reads this chunk's logits: still check its forward
+      st = session_take_error(s, false);
+      forward_collect(s);
+    }
+    if (!st && k + 1 < chunks.size()) st = enqueue(k + 1);
+    for (size_t q = 0; q < rows.size() && !st; q++) st = enc.encode(ranges[q].cum, ranges[q].freq, ranges[q].total);
+    next = j;
+    if (!st) st = drain_uniform();
+  }
+  if (st && s) {  // leave the session idle for its next user
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(s->stream);
+    session_take_error(s, false);
+    forward_collect(s);
+    s->last_n = 0;
   }
   if (st) return st;
   if (next != n) return DET_ERR_WINDOW;

@@ -246,6 +246,7 @@ struct det_session {
   };
   std::vector<Graph> graphs;  // indexed by chunk size
   int last_n = 0;
+  bool fwd_timed = false;  // a forward whose device time forward_collect has not added yet
   std::vector<uint8_t> cdf_ready;
   det_stats stats{};
   std::vector<void*> allocations;
@@ -279,6 +280,11 @@ det_status cuda_status(cudaError_t e);
 det_status session_take_error(det_session* s, bool cdf);
 // the decompress loop on the device: allocates the session's RcState (once)
 det_status rc_loop_init(det_session* s);
+// det_forward split in two for the codec's pipeline: the forward enqueued
+// without a synchronisation (its errors surface at the next take_error), and
+// its device time added once the stream has passed it
+det_status forward_enqueue(det_session* s, const uint32_t* tokens, uint32_t n, uint32_t pos0);
+void forward_collect(det_session* s);
 // a one-position forward whose token and position are already in device
 // memory (s->d_tokens[0], s->d_pos[0]), e.g. written by rc_step_kernel
 det_status forward_device_inputs(det_session* s);

@@ -198,6 +198,12 @@ cudaError_t launch_cdf_prepare(const Launch& L, const float* logits, int V, cons
 cudaError_t launch_cdf_ranges(const Launch& L, const float* e, const float* z, int V, int tail,
                               const uint32_t* rows, const uint32_t* symbols, int n, uint64_t* out3);
 cudaError_t launch_expf(cudaStream_t st, const float* x, float* y, long long n);
+// GGUF tensor bytes (in device memory) -> device layouts (repack.cu); a
+// non-finite scale or value sets ERRF_NONFINITE in *err
+cudaError_t launch_repack_mma16(const uint8_t* raw, int q8, int rows, int nb, uint8_t* recs, uint32_t* err);
+cudaError_t launch_check_q4k(const uint8_t* blocks, long long nblk, uint32_t* err);
+cudaError_t launch_split_q6k(const uint8_t* raw, long long nblk, uint8_t* q, uint16_t* d, uint32_t* err);
+cudaError_t launch_dense_f32(const uint8_t* raw, int f16, long long n, float* out, uint32_t* err);
 // one warp, n pairs of dependent f32 adds, clock cycles into *cycles
 cudaError_t launch_add_chain(const float* x, float* out, long long* cycles, int n);
 // Row-sharded tensor parallelism (exchange.cu): copy column slices of

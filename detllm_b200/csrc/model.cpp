@@ -3,7 +3,9 @@
 // Mirrors F32Llama::from_gguf (crates/det-model/src/lib.rs:1035-1140),
 // LlamaConfig::from_gguf (:1498-1596) and the per-type tensor readers
 // (:1650-1953), including their error order, then repacks each weight matrix
-// into the device layout documented in internal.h.  The tokenizer
+// into the device layout documented in internal.h: a tensor's bytes go to the
+// device as stored in the file and repack.cu's kernels write the layout (and
+// check the scales) there.  The tokenizer
 // (byte fallback, byte-level BPE or SentencePiece) is read by
 // det::Tokenizer::from_gguf in tokenizer.cpp, following Tokenizer::from_gguf
 // (crates/det-token/src/lib.rs:86-132); its status is kept and reported
@@ -64,6 +66,53 @@ float f16_to_f32(uint16_t bits) {
 struct Loader {
   det_model* m;
   const Gguf& g;
+  // device staging of one tensor's GGUF bytes (grown as needed) and the
+  // repack kernels' error word
+  uint8_t* stage = nullptr;
+  size_t stage_cap = 0;
+  uint32_t* d_err = nullptr;
+
+  Loader(det_model* m_, const Gguf& g_) : m(m_), g(g_) {}
+  Loader(const Loader&) = delete;
+  Loader& operator=(const Loader&) = delete;
+  ~Loader() {
+    if (stage) cudaFree(stage);
+    if (d_err) cudaFree(d_err);
+  }
+
+  det_status ensure_err() {
+    if (d_err) return DET_OK;
+    if (cudaMalloc(&d_err, 4) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+    return cudaMemset(d_err, 0, 4) == cudaSuccess ? DET_OK : DET_ERR_CUDA;
+  }
+  // the tensor's bytes, as stored in the file, in device memory
+  det_status staged(const uint8_t* data, size_t len, const uint8_t** dev) {
+    if (det_status st = ensure_err()) return st;
+    if (len > stage_cap) {
+      if (stage) cudaFree(stage);
+      stage = nullptr;
+      stage_cap = 0;
+      if (cudaMalloc(&stage, len) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+      stage_cap = len;
+    }
+    if (len && cudaMemcpy(stage, data, len, cudaMemcpyHostToDevice) != cudaSuccess) return DET_ERR_CUDA;
+    *dev = stage;
+    return DET_OK;
+  }
+  // waits for the repack kernels; a non-finite scale or value fails the load
+  det_status repack_status() {
+    uint32_t f = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&f, d_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+      return DET_ERR_CUDA;
+    if (f & ERRF_NONFINITE) return DET_ERR_NONFINITE;
+    return f ? DET_ERR_CUDA : DET_OK;
+  }
+  det_status alloc(size_t bytes, void** p) {
+    *p = nullptr;
+    if (cudaMalloc(p, bytes ? bytes : 16) != cudaSuccess) return DET_ERR_DEVICE_OOM;
+    m->allocations.push_back(*p);
+    return DET_OK;
+  }
 
   det_status upload(const void* host, size_t bytes, void** dev) {
     void* p = nullptr;
@@ -127,14 +176,24 @@ struct Loader {
     out->rows = (int)rows;
     out->cols = (int)cols;
     if (t->type == GT_F32 || t->type == GT_F16) {
-      std::vector<float> v;
-      if (det_status st = dense_f32(*t, &v)) return st;
+      const uint8_t* data;
+      size_t len;
+      uint64_t n;
+      if (g.tensor_bytes(t->name, &data, &len)) return DET_ERR_GGUF;
+      if (Gguf::element_count(*t, &n)) return DET_ERR_SHAPE;
+      const bool f16 = t->type == GT_F16;
+      if (len != n * (f16 ? 2 : 4)) return DET_ERR_SHAPE;
       if (rows == 0 || cols == 0) return DET_ERR_SHAPE;
+      const uint8_t* raw;
+      if (det_status st = staged(data, len, &raw)) return st;
       void* p;
-      if (det_status st = upload(v.data(), v.size() * 4, &p)) return st;
+      if (det_status st = alloc((size_t)n * 4, &p)) return st;
+      if (launch_dense_f32(raw, f16 ? 1 : 0, (long long)n, static_cast<float*>(p), d_err) != cudaSuccess)
+        return DET_ERR_CUDA;
+      if (det_status st = repack_status()) return st;
       out->type = GT_F32;
       out->f = static_cast<float*>(p);
-      m->weight_bytes += v.size() * 4;
+      m->weight_bytes += (size_t)n * 4;
       return DET_OK;
     }
     size_t bk, tb;
@@ -153,118 +212,55 @@ struct Loader {
     if (len != nblk * tb) return DET_ERR_SHAPE;
     out->type = t->type;
     out->nb = (int)nb;
-    std::vector<uint8_t> q;
-    std::vector<uint16_t> d;
-    switch (t->type) {
-      case GT_Q8_0:
-        q.resize(nblk * 32);
-        d.resize(nblk);
-        for (size_t i = 0; i < nblk; i++) {
-          const uint8_t* b = data + i * tb;
-          d[i] = rd16(b);
-          if (!f16_finite(d[i])) return DET_ERR_NONFINITE;
-          std::memcpy(&q[i * 32], b + 2, 32);
-        }
-        break;
-      case GT_Q4_0:
-        q.resize(nblk * 16);
-        d.resize(nblk);
-        for (size_t i = 0; i < nblk; i++) {
-          const uint8_t* b = data + i * tb;
-          d[i] = rd16(b);
-          if (!f16_finite(d[i])) return DET_ERR_NONFINITE;
-          std::memcpy(&q[i * 16], b + 2, 16);
-        }
-        break;
-      case GT_Q4_K:
-        q.resize(nblk * 144);
-        for (size_t i = 0; i < nblk; i++) {
-          const uint8_t* b = data + i * tb;
-          if (!f16_finite(rd16(b)) || !f16_finite(rd16(b + 2))) return DET_ERR_NONFINITE;
-        }
-        std::memcpy(q.data(), data, nblk * 144);
-        break;
-      default:  // Q6_K: ql | qh | scales kept together (208 B), d split out
-        q.resize(nblk * 208);
-        d.resize(nblk);
-        for (size_t i = 0; i < nblk; i++) {
-          const uint8_t* b = data + i * tb;
-          std::memcpy(&q[i * 208], b, 208);
-          d[i] = rd16(b + 208);
-          if (!f16_finite(d[i])) return DET_ERR_NONFINITE;
-        }
-        break;
-    }
     if (rows == 0 || cols == 0) return DET_ERR_SHAPE;
     void* p;
+    if (t->type == GT_Q4_K) {  // the blocks as stored: copied straight into place, then checked
+      if (det_status st = alloc(len, &p)) return st;
+      if (cudaMemcpy(p, data, len, cudaMemcpyHostToDevice) != cudaSuccess) return DET_ERR_CUDA;
+      if (det_status st = ensure_err()) return st;
+      if (launch_check_q4k(static_cast<const uint8_t*>(p), (long long)nblk, d_err) != cudaSuccess)
+        return DET_ERR_CUDA;
+      if (det_status st = repack_status()) return st;
+      out->q = p;
+      m->weight_bytes += len;
+      return DET_OK;
+    }
+    const uint8_t* raw;
+    if (det_status st = staged(data, len, &raw)) return st;
     if (t->type == GT_Q8_0 || t->type == GT_Q4_0) {
       // tensor-core tile records (gemm.cu): one record per (16-row tile, block)
       const bool q8 = t->type == GT_Q8_0;
-      const size_t qb = q8 ? 512 : 256, rb = qb + 32, per_row = q8 ? 32 : 16;
-      const size_t tiles = (rows + 15) / 16;
-      std::vector<uint8_t> recs(tiles * nb * rb, 0);
-      // tiles are independent: split them over host threads
-      auto repack = [&](size_t t0, size_t t1) {
-      for (size_t tl = t0; tl < t1; tl++)
-        for (size_t b = 0; b < nb; b++) {
-          uint8_t* r = &recs[(tl * nb + b) * rb];
-          for (int lane = 0; lane < 32; lane++) {
-            const size_t g = (size_t)lane / 4, tg = (size_t)lane % 4;
-            for (int hi = 0; hi < 2; hi++) {
-              const size_t row = tl * 16 + g + 8 * hi;
-              if (row >= rows) continue;
-              const uint8_t* src = &q[(row * nb + b) * per_row];
-              if (q8) {
-                std::memcpy(r + lane * 16 + hi * 4, src + tg * 4, 4);
-                std::memcpy(r + lane * 16 + 8 + hi * 4, src + 16 + tg * 4, 4);
-              } else {
-                std::memcpy(r + lane * 8 + hi * 4, src + tg * 4, 4);
-              }
-            }
-          }
-          for (size_t g = 0; g < 8; g++) {
-            const size_t r0 = tl * 16 + g, r1 = r0 + 8;
-            const uint16_t d0 = r0 < rows ? d[r0 * nb + b] : 0, d1 = r1 < rows ? d[r1 * nb + b] : 0;
-            const uint32_t w = (uint32_t)d0 | ((uint32_t)d1 << 16);
-            std::memcpy(r + qb + 4 * g, &w, 4);
-          }
-        }
-      };
-      const size_t nt = std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), 16);
-      if (nt <= 1 || tiles < 64) {
-        repack(0, tiles);
-      } else {
-        std::vector<std::thread> pool;
-        for (size_t k = 0; k < nt; k++) pool.emplace_back(repack, tiles * k / nt, tiles * (k + 1) / nt);
-        for (auto& th : pool) th.join();
-      }
-      if (det_status st = upload(recs.data(), recs.size(), &p)) return st;
+      const size_t rb = q8 ? 544 : 288, tiles = (rows + 15) / 16;
+      if (det_status st = alloc(tiles * nb * rb, &p)) return st;
+      if (launch_repack_mma16(raw, q8 ? 1 : 0, (int)rows, (int)nb, static_cast<uint8_t*>(p), d_err) != cudaSuccess)
+        return DET_ERR_CUDA;
+      if (det_status st = repack_status()) return st;
       out->q = p;
       out->layout = LAYOUT_MMA16;
-      m->weight_bytes += recs.size();
+      m->weight_bytes += tiles * nb * rb;
       return DET_OK;
     }
-    if (det_status st = upload(q.data(), q.size(), &p)) return st;
+    // Q6_K: ql | qh | scales kept together (208 B), d split out
+    void* pd;
+    if (det_status st = alloc(nblk * 208, &p)) return st;
+    if (det_status st = alloc(nblk * 2, &pd)) return st;
+    if (launch_split_q6k(raw, (long long)nblk, static_cast<uint8_t*>(p), static_cast<uint16_t*>(pd), d_err) !=
+        cudaSuccess)
+      return DET_ERR_CUDA;
+    if (det_status st = repack_status()) return st;
     out->q = p;
-    m->weight_bytes += q.size();
-    if (!d.empty()) {
-      if (det_status st = upload(d.data(), d.size() * 2, &p)) return st;
-      out->d = static_cast<const uint16_t*>(p);
-      m->weight_bytes += d.size() * 2;
-    }
-    if (t->type == GT_Q6_K) {
-      // the tensor-core chunk GEMM's records, built on the device from the
-      // uploaded blocks (gemm_q6k_tc.cu)
-      const size_t tb_bytes = q6k_tc_bytes((int)rows, (int)nb);
-      void* tcp = nullptr;
-      if (cudaMalloc(&tcp, tb_bytes) != cudaSuccess) return DET_ERR_DEVICE_OOM;
-      m->allocations.push_back(tcp);
-      if (launch_q6k_tc_repack(nullptr, *out, static_cast<uint8_t*>(tcp)) != cudaSuccess ||
-          cudaDeviceSynchronize() != cudaSuccess)
-        return DET_ERR_CUDA;
-      out->tc = static_cast<const uint8_t*>(tcp);
-      m->weight_bytes += tb_bytes;
-    }
+    out->d = static_cast<const uint16_t*>(pd);
+    m->weight_bytes += nblk * 210;
+    // the tensor-core chunk GEMM's records, built on the device from the
+    // split blocks (gemm_q6k_tc.cu)
+    const size_t tb_bytes = q6k_tc_bytes((int)rows, (int)nb);
+    void* tcp;
+    if (det_status st = alloc(tb_bytes, &tcp)) return st;
+    if (launch_q6k_tc_repack(nullptr, *out, static_cast<uint8_t*>(tcp)) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+      return DET_ERR_CUDA;
+    out->tc = static_cast<const uint8_t*>(tcp);
+    m->weight_bytes += tb_bytes;
     return DET_OK;
   }
 };
@@ -472,7 +468,7 @@ det_status load_impl(const uint8_t* bytes, size_t len, det_model* m) {
   if (det_status st = config_from_gguf(g, &c)) return st;
   size_t V;
   if (det_status st = vocab_size(g, &V)) return st;
-  Loader ld{m, g};
+  Loader ld(m, g);
   const size_t hd = (size_t)c.hd;
   if (det_status st = ld.matrix("token_embd.weight", V, c.d, &m->tok_embd, &m->weight_types[0])) return st;
   m->layers.resize((size_t)c.L);

@@ -730,6 +730,34 @@ bool model_has_q6k_tc(const det_model* m) {
 
 }  // namespace
 
+det_status det::forward_enqueue(det_session* s, const uint32_t* tokens, uint32_t n, uint32_t pos0) {
+  if (!s || !tokens) return DET_ERR_INVALID_ARGUMENT;
+  if (n == 0 || (int)n > s->max_chunk || (uint64_t)pos0 + n > (uint64_t)s->n_ctx) return DET_ERR_SHAPE;
+  det_model* m = s->m;
+  for (uint32_t i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)m->vocab || tokens[i] >= (uint32_t)m->tok_embd.rows) return DET_ERR_SHAPE;
+  cudaSetDevice(m->device);
+  std::memcpy(s->h_tokens, tokens, n * 4);
+  *s->h_pos = (int)pos0;
+  s->stats.h2d_bytes += n * 4 + 4;
+  CK(cudaEventRecord(s->ev[0], s->stream));
+  det_status st = run_forward(s, (int)n);
+  if (st) return st;
+  CK(cudaEventRecord(s->ev[1], s->stream));
+  s->last_n = (int)n;
+  s->stats.tokens += n;
+  s->fwd_timed = true;
+  std::fill(s->cdf_ready.begin(), s->cdf_ready.end(), 0);
+  return DET_OK;
+}
+
+void det::forward_collect(det_session* s) {
+  if (!s->fwd_timed) return;
+  float ms = 0.0f;
+  if (cudaEventElapsedTime(&ms, s->ev[0], s->ev[1]) == cudaSuccess) s->stats.forward_ms += ms;
+  s->fwd_timed = false;
+}
+
 extern "C" {
 
 det_status det_session_create(det_model* m, uint32_t n_ctx, uint32_t max_chunk, det_session** out) {
@@ -842,30 +870,16 @@ det_status det_session_reset(det_session* s) {
 }
 
 det_status det_forward(det_session* s, const uint32_t* tokens, uint32_t n, uint32_t pos0, float* logits_out) {
-  if (!s || !tokens) return DET_ERR_INVALID_ARGUMENT;
-  if (n == 0 || (int)n > s->max_chunk || (uint64_t)pos0 + n > (uint64_t)s->n_ctx) return DET_ERR_SHAPE;
+  if (det_status st = forward_enqueue(s, tokens, n, pos0)) return st;
   det_model* m = s->m;
-  for (uint32_t i = 0; i < n; i++)
-    if (tokens[i] >= (uint32_t)m->vocab || tokens[i] >= (uint32_t)m->tok_embd.rows) return DET_ERR_SHAPE;
-  cudaSetDevice(m->device);
-  std::memcpy(s->h_tokens, tokens, n * 4);
-  *s->h_pos = (int)pos0;
-  s->stats.h2d_bytes += n * 4 + 4;
-  CK(cudaEventRecord(s->ev[0], s->stream));
-  det_status st = run_forward(s, (int)n);
-  if (st) return st;
-  CK(cudaEventRecord(s->ev[1], s->stream));
-  s->last_n = (int)n;
-  s->stats.tokens += n;
-  std::fill(s->cdf_ready.begin(), s->cdf_ready.end(), 0);
+  det_status st = DET_OK;
   if (logits_out) {
     const size_t bytes = (size_t)n * m->vocab * 4;
     CK(cudaMemcpyAsync(logits_out, s->logits, bytes, cudaMemcpyDeviceToHost, s->stream));
     s->stats.d2h_bytes += bytes;
   }
   st = take_error(s, false);
-  float ms = 0.0f;
-  if (cudaEventElapsedTime(&ms, s->ev[0], s->ev[1]) == cudaSuccess) s->stats.forward_ms += ms;
+  forward_collect(s);
   if (st) s->last_n = 0;
   return st;
 }
@@ -901,6 +915,7 @@ det_status det_symbol_ranges(det_session* s, const uint32_t* rows, const uint32_
     CK(cudaMemcpyAsync(s->h_out, s->d_out, cnt * 24, cudaMemcpyDeviceToHost, s->stream));
     s->stats.d2h_bytes += cnt * 24;
     if (det_status st = take_error(s, true)) return st;
+    forward_collect(s);  // a forward enqueued without a synchronisation has run
     float ms = 0.0f;
     if (cudaEventElapsedTime(&ms, s->ev[2], s->ev[3]) == cudaSuccess) s->stats.cdf_ms += ms;
     for (uint32_t i = 0; i < cnt; i++) {

@@ -295,6 +295,28 @@ def test_nonfinite_is_an_error_like_the_reference(D, oracle):
     assert eo.value.code == eg.value.code == 2
 
 
+# (block bytes, offset of the f16 scale in the block) of the lm_head types
+_SCALE_AT = {S.GT_Q8_0: (34, 0), S.GT_Q4_0: (18, 0), S.GT_Q4_K: (144, 0), S.GT_Q6_K: (210, 208), S.GT_F16: (2, 0)}
+
+
+@pytest.mark.parametrize("t_out", list(_SCALE_AT))
+def test_load_rejects_a_nonfinite_scale(D, oracle, t_out):
+    """The device repack checks every block scale as the reference's readers
+    do: an infinite f16 scale in the last block of output.weight (the last
+    tensor of the file) fails the load with the oracle's status."""
+    spec = S.ModelSpec(n_layer=1, d=256, d_ff=256, n_head=2, n_head_kv=2, vocab=300, ctx=16, t_out=t_out, seed=4)
+    g = bytearray(S.build_gguf(spec))
+    block, at = _SCALE_AT[t_out]
+    p = len(g) - block + at
+    g[p:p + 2] = b"\x00\x7c"  # +inf
+    g = bytes(g)
+    with pytest.raises(oracle.OracleError) as eo:
+        oracle.Model(g).logits([1, 2])
+    with pytest.raises(D.DetError) as eg:
+        D.Model(g)
+    assert eo.value.code == eg.value.code == 2
+
+
 @pytest.mark.parametrize("kind", ["spm", "bpe"])
 def test_codec_bytes_sentencepiece_and_bpe(D, oracle, kind):
     """compress / decompress through a SentencePiece and a byte-level BPE
