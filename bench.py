@@ -437,11 +437,26 @@ def sub_configs(D, S, peak, peak_kind, add_cycles=None, sm_mhz=None):
 TP_CONFIG = HEADLINE  # the configuration BASELINE.json runs row-sharded
 
 
+def chunk_probe(model, vocab):
+    """Single-stream chunked forwards (the encode path): positions 0..1023
+    as warm-up, then 1024..3071 in two 1,024-position chunks, device time."""
+    from detllm_b200 import synth as S
+
+    tk = S.zipf_tokens(3072, vocab, seed=13)
+    with model.session(n_ctx=HEAD_CTX, max_chunk=1024) as s:
+        s.forward(tk[:1024], 0)
+        s.stats(reset=True)
+        s.forward(tk[1024:2048], 1024)
+        s.forward(tk[2048:3072], 2048)
+        st = s.stats(reset=True)
+    return 2048 / (st.forward_ms / 1000.0)
+
+
 def tp_probe(D, gguf, spec, devices):
     """Row-sharded tensor parallelism over `devices` from this one process
     (rank 0, after the timed region, while the other ranks wait): single-
-    stream decode tokens/s on one GPU and on all of `devices`, and whether
-    the logits hashes of 256 tokens are equal."""
+    stream decode and chunked-forward tokens/s on one GPU and on all of
+    `devices`, and whether the logits hashes of 256 tokens are equal."""
     from detllm_b200 import synth as S
 
     try:
@@ -449,6 +464,7 @@ def tp_probe(D, gguf, spec, devices):
         one = D.Model(gguf, device=devices[0])
         h_one = one.logits_hash_for_tokens_chunked(toks, 64).hex()
         d1 = decode_probe(one, spec.vocab, HEAD_CTX)
+        c1 = chunk_probe(one, spec.vocab)
         one.close()
         t = time.time()
         tp = D.Model(gguf, devices=devices)
@@ -465,11 +481,13 @@ def tp_probe(D, gguf, spec, devices):
                 s.forward(tk[p:p + 1], p)
             st = s.stats(reset=True)
         tps = 48 / (st.forward_ms / 1000.0)
+        ctp = chunk_probe(tp, spec.vocab)
         tp.close()
     except Exception as e:  # reported, never fatal to the bench line
         return {"config": TP_CONFIG, "parts": len(devices), "unavailable": f"{type(e).__name__}: {e}"}
     return {"config": TP_CONFIG, "parts": len(devices), "devices": devices, "decode_tokens_per_s": tps,
             "decode_tokens_per_s_1gpu": d1["tokens_per_s"], "speedup": tps / d1["tokens_per_s"],
+            "chunk_tokens_per_s": ctp, "chunk_tokens_per_s_1gpu": c1, "chunk_speedup": ctp / c1,
             "logits_hash_equal": h_tp == h_one, "load_s": round(load_s, 1)}
 
 
