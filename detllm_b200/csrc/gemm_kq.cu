@@ -570,13 +570,14 @@ DI void q6_pairs(const int8_t* __restrict__ aq, int b, int j, uint32_t* A, uint3
 // gemv_q6k_aux_kernel, with the weight stream overlapping the integer work.
 // A persistent CTA (one per SM) walks 32-row tiles; each tile is read in
 // passes of 8 blocks, one (row, block) item of 208 bytes per thread, and
-// every thread copies the item it will use in the NEXT pass into its own
-// slot of a two-pass shared-memory buffer with cp.async while it works on
-// the current one (the passes run on across tile boundaries), so about
-// 53 KB per SM are always in flight.  The activation's pairs for all blocks
-// are staged once per CTA.  After a pass, thread (row, class) advances its
-// f32 chain over the pass's blocks in order; after a tile's last pass the
-// row's eight chains are summed in lane order.
+// every thread moves the item it will use in the NEXT pass into its own
+// slot of a two-pass shared-memory buffer with one cp.async.bulk while it
+// works on the current one (the passes run on across tile boundaries); a
+// buffer's mbarrier counts the pass's bytes (thread 0 arrives with the
+// expected total).  The activation's pairs for all blocks are staged once
+// per CTA.  After a pass, thread (row, class) advances its f32 chain over
+// the pass's blocks in order; after a tile's last pass the row's eight
+// chains are summed in lane order.  Waits are bounded by %globaltimer.
 constexpr int Q6S_ROWS = 32;
 constexpr int Q6S_NBP = 8;  // blocks per pass
 constexpr int Q6S_THREADS = Q6S_ROWS * Q6S_NBP;
@@ -584,13 +585,30 @@ constexpr int Q6S_AUX_LD = Q6S_NBP * 8 + 1;  // aux row stride (ints)
 constexpr int Q6S_MAX_NB = 64;               // K <= 16384 (activation pairs staged in shared memory)
 inline size_t q6s_smem_bytes(int nb) {
   return (size_t)2 * Q6S_THREADS * 208 + (size_t)nb * (128 + 64) * 4 + (size_t)Q6S_ROWS * Q6S_AUX_LD * 4 +
-         (size_t)Q6S_ROWS * (Q6S_NBP + 1) * 4;
+         (size_t)Q6S_ROWS * (Q6S_NBP + 1) * 4 + 16;
 }
 
 // the segment that holds tile `tile` (its first tile is its cta0)
 DI KqSeg kq_seg_at(const KqSegs& S, int tile) {
   const int i = (int)(tile >= S.s[1].cta0) + (int)(tile >= S.s[2].cta0);
   return i == 0 ? S.s[0] : (i == 1 ? S.s[1] : S.s[2]);
+}
+
+DI bool q6s_wait(uint32_t bar, uint32_t parity) {
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; it++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    if (it == 0) t0 = t;
+    else if (t - t0 > 2000000000ull) return false;
+  }
 }
 
 __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs S, int tiles,
@@ -604,6 +622,7 @@ __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs 
   uint32_t* spair = apair + (size_t)nb * 128;                                     // [nb][8][8]
   int* aux = reinterpret_cast<int*>(spair + (size_t)nb * 64);                     // [32][Q6S_AUX_LD]
   float* ddv = reinterpret_cast<float*>(aux + Q6S_ROWS * Q6S_AUX_LD);             // [32][Q6S_NBP + 1]
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(ddv + Q6S_ROWS * (Q6S_NBP + 1));  // [2] mbarriers
   const int t = threadIdx.x;
   const int ir = t & 31, ib = t >> 5;  // this thread's item: row ir, block ib of each pass
   const int cr = t >> 3, cc = t & 7;   // chain: row, class
@@ -611,22 +630,37 @@ __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs 
   // the passes of this CTA, in order: tile blockIdx.x + k gridDim.x, pass p
   const int my_tiles = tiles > (int)blockIdx.x ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int nq = my_tiles * npass;
+  if (t == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar0) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar0 + 8) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
 
-  // issue the copy of pass q's item into buffer q & 1 (and load its scale)
+  // pass q's item of this thread into buffer q & 1 (one bulk copy), and its
+  // block scale; thread 0 arrives on the buffer's barrier with the pass's
+  // byte count (complete_tx may come first: the count then runs negative)
   auto issue = [&](int q, uint32_t& dbits) {
-    if (q < nq) {
-      const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, b = (q % npass) * Q6S_NBP + ib;
-      const KqSeg g = kq_seg_at(S, tile);
-      const int row = (tile - g.cta0) * Q6S_ROWS + ir;
-      if (b < nb && row < g.rows) {
-        const uint8_t* src = g.q + ((size_t)row * nb + b) * 208;
-        uint8_t* dst = items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208;
-#pragma unroll
-        for (int k = 0; k < 13; k++) g4_cp_async16(dst + 16 * k, src + 16 * k);
-        dbits = g.d[(size_t)row * nb + b];
-      }
+    if (q >= nq) return;
+    const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, p = q % npass, b = p * Q6S_NBP + ib;
+    const KqSeg g = kq_seg_at(S, tile);
+    const int r0 = (tile - g.cta0) * Q6S_ROWS, row = r0 + ir;
+    const uint32_t bar = bar0 + 8 * (q & 1);
+    if (t == 0) {
+      const uint32_t nrow = (uint32_t)min(Q6S_ROWS, g.rows - r0), nblk = (uint32_t)min(Q6S_NBP, nb - p * Q6S_NBP);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(nrow * nblk * 208u)
+                   : "memory");
     }
-    g4_cp_commit();
+    if (b < nb && row < g.rows) {
+      const uint8_t* src = g.q + ((size_t)row * nb + b) * 208;
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208);
+      // the slot was last read with ordinary loads (pass q - 2)
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], 208, [%2];\n" ::"r"(dst),
+                   "l"(src), "r"(bar)
+                   : "memory");
+      dbits = g.d[(size_t)row * nb + b];
+    }
   };
   uint32_t dnext = 0;
   issue(0, dnext);  // weights are constant: before the predecessor ends
@@ -636,15 +670,24 @@ __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs 
   __syncthreads();
 
   float sum = 0.0f;
+  bool ok = true;
+  int issued = nq > 0 ? 0 : -1;  // the last pass whose copies were issued
   for (int q = 0; q < nq; q++) {
     const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, p = q % npass;
     const KqSeg g = kq_seg_at(S, tile);
     const int r0 = (tile - g.cta0) * Q6S_ROWS, b0 = p * Q6S_NBP;
     const uint32_t dcur = dnext;
     issue(q + 1, dnext);
-    g4_cp_wait<1>();  // this thread's item of pass q has landed (only this thread reads it)
+    if (q + 1 < nq) issued = q + 1;
     const int b = b0 + ib;
-    if (b < nb && r0 + ir < g.rows) {
+    const bool has = b < nb && r0 + ir < g.rows;
+    const float adb = has ? ad[b] : 0.0f;
+    if (!q6s_wait(bar0 + 8 * (q & 1), (uint32_t)((q >> 1) & 1))) {  // pass q's items have landed
+      atomicOr(err, ERRF_TIMEOUT);
+      ok = false;
+    }
+    if (!__syncthreads_and(ok)) break;
+    if (has) {
       Q6Item it;
       const uint4* src = reinterpret_cast<const uint4*>(items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208);
 #pragma unroll
@@ -656,7 +699,7 @@ __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs 
         it.w[4 * k + 3] = v.w;
       }
       q6_aux(it, apair + b * 128, spair + b * 64, aux + ir * Q6S_AUX_LD + ib * 8);
-      ddv[ir * (Q6S_NBP + 1) + ib] = fmul(f16_bits_to_f32((uint16_t)dcur), ad[b]);
+      ddv[ir * (Q6S_NBP + 1) + ib] = fmul(f16_bits_to_f32((uint16_t)dcur), adb);
     }
     __syncthreads();  // aux / ddv of the pass complete
     if (r0 + cr < g.rows) {
@@ -676,6 +719,8 @@ __global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs 
     }
     __syncthreads();  // aux / ddv free for the next pass
   }
+  if (!ok)  // every copy issued has landed before the CTA's shared memory goes away (bounded)
+    for (int q = max(0, issued - 1); q <= issued; q++) q6s_wait(bar0 + 8 * (q & 1), (uint32_t)((q >> 1) & 1));
 }
 
 template <int R>
