@@ -626,30 +626,58 @@ __global__ void attn_pv_decode_kernel(const float* __restrict__ P, const float* 
 }
 
 // ---- one position, fused ------------------------------------------------------
-// For a chunk of one position (decode) the three steps run in one kernel,
-// one CTA per query head, with the score row in shared memory:
-//   scores  the K rows stream through an AD_STAGES-slot cp.async ring of
-//           64-key tiles; four threads share a key, thread quarter r owning
-//           the lane chains 2r and 2r + 1 of the dot (elements 8i + 2r,
-//           8i + 2r + 1, i ascending), so ((l0 + l1) + (l2 + l3)) +
-//           ((l4 + l5) + (l6 + l7)) is two in-thread adds and two shuffles;
-//   softmax max, e_j, the eight ordered z chains (eight threads), p = e / z;
-//   PV      the V tiles stream through the same ring (the first ones are in
-//           flight during the softmax) and thread d runs the chain o[d].
-// Tile rows are HD + 8 floats apart, so the 8-byte reads of a half-warp (four
-// keys x four quarters) and the 4-byte reads of consecutive d fall in
-// distinct banks.
+// For a chunk of one position (decode) the three steps run in one kernel: a
+// cluster of AD_CS CTAs per query head, each CTA owning a contiguous quarter
+// of the keys (whole 64-key tiles, in order), so each SM streams a quarter
+// of the head's K and V rows:
+//   scores  the CTA's K tiles stream through an AD_STAGES-slot cp.async ring;
+//           four threads share a key, thread quarter r owning the lane
+//           chains 2r and 2r + 1 of the dot (elements 8i + 2r, 8i + 2r + 1,
+//           i ascending), so ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 +
+//           l7)) is two in-thread adds and two shuffles;
+//   softmax the max over the cluster (each CTA's max read through
+//           distributed shared memory), e_j, then the eight ordered z lane
+//           chains relayed CTA to CTA in key order (CTA c starts its lanes
+//           from CTA c - 1's partial sums), z = finish8 of the last, p = e/z;
+//   PV      the CTA's V tiles stream in during the softmax; the chain o[d]
+//           is relayed the same way: CTA c continues CTA c - 1's sums over
+//           its own keys, and the last CTA stores them.
+// Each relay step is one cluster barrier, taken by every thread of every
+// CTA, so the chains keep the reference's order exactly.  Tile rows are
+// HD + 8 floats apart, so the 8-byte reads of a half-warp (four keys x four
+// quarters) and the 4-byte reads of consecutive d fall in distinct banks.
 constexpr int AD_THREADS = 256;
 constexpr int AD_KEYS = 64;
 constexpr int AD_STAGES = 3;
-constexpr int AD_MAX_CTX = 16384;  // score row in shared memory
+constexpr int AD_CS = 4;           // CTAs per head (cluster size)
+constexpr int AD_MAX_CTX = 16384;  // each CTA's score slice in shared memory
 template <int HD>
 __host__ __device__ constexpr int ad_tile_floats() {
   return AD_KEYS * (HD + 8);
 }
+// the most keys one CTA owns: whole tiles, ceil(tiles / AD_CS) of them
+inline int ad_slice_keys(int n_ctx) { return ((n_ctx + AD_KEYS - 1) / AD_KEYS + AD_CS - 1) / AD_CS * AD_KEYS; }
 template <int HD>
 size_t ad_smem_bytes(int n_ctx) {
-  return ((size_t)AD_STAGES * ad_tile_floats<HD>() + HD + (size_t)score_ld(n_ctx)) * sizeof(float);
+  // ring, q row, score slice, relay buffer (HD PV sums)
+  return ((size_t)AD_STAGES * ad_tile_floats<HD>() + 2 * HD + (size_t)ad_slice_keys(n_ctx)) * sizeof(float);
+}
+
+DI void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+DI uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// a float of CTA `rank`'s shared memory at the address of `local` in this CTA
+DI float ld_dsmem(const float* local, uint32_t rank) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
 }
 
 template <int HD>
@@ -661,32 +689,40 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const float* __
   constexpr int LD = HD + 8;
   pdl_enter();
   extern __shared__ __align__(16) float ad_smem[];
-  float* ring = ad_smem;                             // [AD_STAGES][AD_KEYS][LD]
+  float* ring = ad_smem;                                 // [AD_STAGES][AD_KEYS][LD]
   float* qs = ring + AD_STAGES * ad_tile_floats<HD>();  // [HD]
-  float* sc = qs + HD;                               // [len]: scores, then e, then p
+  float* relay = qs + HD;                                // [HD]: PV sums handed to the next CTA
+  float* sc = relay + HD;                                // [slice]: scores, then e, then p
   __shared__ float red[AD_THREADS / 32];
-  __shared__ float l8[8];
-  const int h = blockIdx.x, kvh = h / gsz;
+  __shared__ float cmax;
+  __shared__ float l8[8];  // z lane sums handed to the next CTA
+  const uint32_t rank = cluster_rank();
+  const int h = (int)blockIdx.x / AD_CS, kvh = h / gsz;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int len = *pos0p + 1;
   const float* kb = kc + (size_t)kvh * n_ctx * HD;
   const float* vb = vc + (size_t)kvh * n_ctx * HD;
   float* ob = out + (size_t)h * HD;
-  if (len == 1) {  // score_len == 1 copies v_0 (lib.rs:2319-2322)
-    for (int d = tid; d < HD; d += AD_THREADS) ob[d] = vb[d];
+  if (len == 1) {  // score_len == 1 copies v_0 (lib.rs:2319-2322); the same in every CTA of the cluster
+    if (rank == 0)
+      for (int d = tid; d < HD; d += AD_THREADS) ob[d] = vb[d];
     return;
   }
-  const int ntile = (len + AD_KEYS - 1) / AD_KEYS;
-  // tile k of `base` (keys 64k ..) into slot k % AD_STAGES, rows past the
-  // score length zero; an empty group past the last tile keeps the wait
-  // counts uniform
+  // this CTA's tiles [t0, t1) of the score row
+  const int ntile_all = (len + AD_KEYS - 1) / AD_KEYS;
+  const int t0 = (int)(((long long)ntile_all * rank) / AD_CS), t1 = (int)(((long long)ntile_all * (rank + 1)) / AD_CS);
+  const int ntile = t1 - t0, j0 = t0 * AD_KEYS, jn = min(len, t1 * AD_KEYS) - j0;  // local keys [0, jn)
+  // local tile k of `base` into slot k % AD_STAGES, rows past the score
+  // length zero; an empty group past the last tile keeps the wait counts
+  // uniform
   auto load_tile = [&](const float* base, int k) {
     if (k < ntile) {
       float* dst = ring + (k % AD_STAGES) * ad_tile_floats<HD>();
       for (int i = tid; i < AD_KEYS * (HD / 4); i += AD_THREADS) {
         const int jj = i / (HD / 4), c4 = (i - jj * (HD / 4)) * 4;
-        if (k * AD_KEYS + jj < len)
-          cp_async16(dst + jj * LD + c4, base + (size_t)(k * AD_KEYS + jj) * HD + c4);
+        const int j = j0 + k * AD_KEYS + jj;
+        if (j < len)
+          cp_async16(dst + jj * LD + c4, base + (size_t)j * HD + c4);
         else
           *reinterpret_cast<float4*>(dst + jj * LD + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
@@ -719,11 +755,11 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const float* __
     const float pair = fadd(a0, a1);                                        // l(2qr) + l(2qr + 1)
     const float quad = fadd(pair, __shfl_xor_sync(0xffffffffu, pair, 1));  // (l0 + l1) + (l2 + l3), ...
     const float dot = fadd(quad, __shfl_xor_sync(0xffffffffu, quad, 2));
-    const int j = k * AD_KEYS + jj;
-    if (qr == 0 && j < len) {
+    const int jl = k * AD_KEYS + jj;
+    if (qr == 0 && jl < jn) {
       const float sv = fmul(dot, scale);
       if (!finite(sv)) atomicOr(err, ERRF_NONFINITE);
-      sc[j] = sv;
+      sc[jl] = sv;
     }
     __syncthreads();  // slot k % AD_STAGES is refilled by the next iteration
   }
@@ -731,73 +767,101 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const float* __
 
   // softmax (attention_one_head: e_j = exp(max(s_j - max, -88)), z = sum_f32_ref(e))
   float mx = -INFINITY;
-  for (int j = tid; j < len; j += AD_THREADS) mx = fmaxf(mx, sc[j]);
+  for (int j = tid; j < jn; j += AD_THREADS) mx = fmaxf(mx, sc[j]);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red[warp] = mx;
   __syncthreads();
-  mx = red[0];
+  if (tid == 0) {
+    float m = red[0];
 #pragma unroll
-  for (int w = 1; w < AD_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
-  for (int j = tid; j < len; j += AD_THREADS) {
+    for (int w = 1; w < AD_THREADS / 32; w++) m = fmaxf(m, red[w]);
+    cmax = m;
+  }
+  cluster_sync();  // every CTA's max is published
+  mx = ld_dsmem(&cmax, 0);
+#pragma unroll
+  for (int r = 1; r < AD_CS; r++) mx = fmaxf(mx, ld_dsmem(&cmax, (uint32_t)r));
+  for (int j = tid; j < jn; j += AD_THREADS) {
     const float d = fsub(sc[j], mx);
     sc[j] = expf_det(d > -88.0f ? d : -88.0f);
   }
   __syncthreads();
-  if (tid < 8) {  // sum_f32_ref: the ordered chain of lane tid
-    float acc = 0.0f;
-    int j = tid;
-    for (; j + 56 < len; j += 64) {
-      float e[8];
+  // sum_f32_ref: lane l sums e_j over j = l (mod 8) in key order, CTA after CTA
+  for (int c = 0; c < AD_CS; c++) {
+    if ((int)rank == c && tid < 8) {
+      float acc = c == 0 ? 0.0f : ld_dsmem(&l8[tid], (uint32_t)(c - 1));
+      // local key jl has global index j0 + jl; j0 is a multiple of 8, so the
+      // lane of local key jl is jl mod 8
+      int j = tid;
+      for (; j + 56 < jn; j += 64) {
+        float e[8];
 #pragma unroll
-      for (int k = 0; k < 8; k++) e[k] = sc[j + 8 * k];
+        for (int k = 0; k < 8; k++) e[k] = sc[j + 8 * k];
 #pragma unroll
-      for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+        for (int k = 0; k < 8; k++) acc = fadd(acc, e[k]);
+      }
+      for (; j < jn; j += 8) acc = fadd(acc, sc[j]);
+      l8[tid] = acc;
     }
-    for (; j < len; j += 8) acc = fadd(acc, sc[j]);
-    l8[tid] = acc;
+    cluster_sync();
   }
-  __syncthreads();
-  const float z = finish8(l8);
-  if (!finite(z) || z == 0.0f) {
-    if (tid == 0) atomicOr(err, ERRF_NONFINITE);
+  float lz[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) lz[k] = ld_dsmem(&l8[k], AD_CS - 1);
+  const float z = finish8(lz);
+  if (!finite(z) || z == 0.0f) {  // the same z in every CTA: the whole cluster stops here
+    if (tid == 0 && rank == 0) atomicOr(err, ERRF_NONFINITE);
     cp_async_wait<0>();  // no copy into this CTA's shared memory outlives it
+    cluster_sync();      // no CTA leaves while another may still read its shared memory
     return;
   }
-  for (int j = tid; j < len; j += AD_THREADS) {
+  for (int j = tid; j < jn; j += AD_THREADS) {
     const float pj = fdiv(sc[j], z);
     if (!finite(pj)) atomicOr(err, ERRF_NONFINITE);
     sc[j] = pj;
   }
+  __syncthreads();
 
-  // o[d] = sum over j of p_j * v_j[d], in order
-  float acc = 0.0f;
-  for (int k = 0; k < ntile; k++) {
-    load_tile(vb, k + AD_STAGES - 1);
-    cp_async_wait<AD_STAGES - 1>();
-    __syncthreads();  // tile k (and, at k = 0, every p_j) visible
-    if (tid < HD) {
-      const float* vr = ring + (k % AD_STAGES) * ad_tile_floats<HD>() + tid;
-      const float* pr = sc + k * AD_KEYS;
-      const int n = min(AD_KEYS, len - k * AD_KEYS);
-      int i = 0;
-      for (; i + 8 <= n; i += 8) {
-        float pv[8], vv[8];
+  // o[d] = sum over j of p_j * v_j[d], in key order, CTA after CTA
+  for (int c = 0; c < AD_CS; c++) {
+    if ((int)rank == c) {
+      float acc = 0.0f;
+      if (c > 0 && tid < HD) acc = ld_dsmem(&relay[tid], (uint32_t)(c - 1));
+      for (int k = 0; k < ntile; k++) {
+        load_tile(vb, k + AD_STAGES - 1);
+        cp_async_wait<AD_STAGES - 1>();
+        __syncthreads();  // tile k visible
+        if (tid < HD) {
+          const float* vr = ring + (k % AD_STAGES) * ad_tile_floats<HD>() + tid;
+          const float* pr = sc + k * AD_KEYS;
+          const int n = min(AD_KEYS, jn - k * AD_KEYS);
+          int i = 0;
+          for (; i + 8 <= n; i += 8) {
+            float pv[8], vv[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          pv[u] = pr[i + u];
-          vv[u] = vr[(i + u) * LD];
+            for (int u = 0; u < 8; u++) {
+              pv[u] = pr[i + u];
+              vv[u] = vr[(i + u) * LD];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = fadd(acc, fmul(pv[u], vv[u]));
+          }
+          for (; i < n; i++) acc = fadd(acc, fmul(pr[i], vr[i * LD]));
         }
-#pragma unroll
-        for (int u = 0; u < 8; u++) acc = fadd(acc, fmul(pv[u], vv[u]));
+        __syncthreads();
       }
-      for (; i < n; i++) acc = fadd(acc, fmul(pr[i], vr[i * LD]));
+      if (tid < HD) {
+        if (c == AD_CS - 1) {
+          if (!finite(acc)) atomicOr(err, ERRF_NONFINITE);
+          ob[tid] = acc;
+        } else {
+          relay[tid] = acc;
+        }
+      }
     }
-    __syncthreads();
+    cluster_sync();
   }
-  if (tid < HD) {
-    if (!finite(acc)) atomicOr(err, ERRF_NONFINITE);
-    ob[tid] = acc;
-  }
+  cp_async_wait<0>();
 }
 
 template <int HD>
@@ -820,13 +884,25 @@ cudaError_t launch_tiled(const Launch& L, const float* q, const float* kc, const
     if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   const int s_ld = score_ld(n_ctx);
-  if (T == 1 && n_ctx <= AD_MAX_CTX) {  // one position: the fused kernel
+  if (T == 1 && n_ctx <= AD_MAX_CTX) {  // one position: the fused kernel, a cluster of AD_CS CTAs per head
     if (cudaError_t e = raise_smem_cap((const void*)attn_decode_kernel<HD>, ad_smem_bytes<HD>(AD_MAX_CTX))) return e;
-    {
-      const cudaError_t e_ = launch_k(L, attn_decode_kernel<HD>, n_head, AD_THREADS, ad_smem_bytes<HD>(n_ctx), q, kc,
-                                      vc, pos0, gsz, n_ctx, scale, out, L.err);
-      if (e_ != cudaSuccess) return e_;
-    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_head * AD_CS);
+    cfg.blockDim = dim3(AD_THREADS);
+    cfg.dynamicSmemBytes = ad_smem_bytes<HD>(n_ctx);
+    cfg.stream = L.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = AD_CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = L.pdl && pdl_enabled() ? 2 : 1;
+    const cudaError_t e_ = cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD>, q, kc, vc, pos0, gsz, n_ctx, scale, out,
+                                              L.err);
+    if (e_ != cudaSuccess) return e_;
     if (L.launches) *L.launches += 1;
     return cudaGetLastError();
   }
