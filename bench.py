@@ -673,6 +673,39 @@ def run_decode_profile(args):
                       "ms_per_token": st.forward_ms / 20}), flush=True)
 
 
+def run_chunk_profile(args):
+    """One configuration's chunked forwards for a profiler: positions 0..1023
+    in chunks of `--chunk` as warm-up, the same positions again timed (device
+    time printed), then the last chunk once more between cudaProfilerStart
+    and cudaProfilerStop."""
+    import torch
+
+    import detllm_b200 as D
+    from detllm_b200 import synth as S
+
+    if args.q8_tensor_cores:
+        D.set_q8_tensor_cores(True)
+    spec, gguf = model_bytes(args.chunk_profile)
+    m = D.Model(gguf)
+    c = min(args.chunk, 1024)
+    toks = S.zipf_tokens(1024, spec.vocab, seed=3)
+    with m.session(n_ctx=1024, max_chunk=c) as s:
+        for p in range(0, 1024, c):
+            s.forward(toks[p:p + c], p)
+        s.stats(reset=True)
+        for p in range(0, 1024, c):
+            s.forward(toks[p:p + c], p)
+        st = s.stats(reset=True)
+        torch.cuda.profiler.start()
+        s.forward(toks[1024 - c:], 1024 - c)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    m.close()
+    print(json.dumps({"chunk_profile": args.chunk_profile, "layers": spec.n_layer, "chunk": c,
+                      "q8_tensor_cores": bool(args.q8_tensor_cores),
+                      "tokens_per_s": 1024 / (st.forward_ms / 1000.0)}), flush=True)
+
+
 def main():
     global PREFIX, LAYERS, PROFILE_ANY_LAYERS
     ap = argparse.ArgumentParser()
@@ -690,12 +723,21 @@ def main():
     ap.add_argument("--decode-profile", default=None, metavar="CONFIG",
                     help="only one-position forwards of CONFIG, for a profiler (see run_decode_profile)")
     ap.add_argument("--profile-tokens", type=int, default=1)
+    ap.add_argument("--chunk-profile", default=None, metavar="CONFIG",
+                    help="only chunked forwards of CONFIG, for a profiler (see run_chunk_profile)")
+    ap.add_argument("--chunk", type=int, default=1024)
+    ap.add_argument("--q8-tensor-cores", action="store_true",
+                    help="with --chunk-profile: the tcgen05 Q8_0 / Q4_0 chunk GEMM instead of the mma.sync one")
     args = ap.parse_args()
     PREFIX = args.prefix
     LAYERS = args.layers
     if args.decode_profile:
         PROFILE_ANY_LAYERS = True
         run_decode_profile(args)
+        return
+    if args.chunk_profile:
+        PROFILE_ANY_LAYERS = True
+        run_chunk_profile(args)
         return
     if args.impl == "reference":
         run_reference(args)
