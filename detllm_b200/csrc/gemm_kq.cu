@@ -826,13 +826,8 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
     }
   }
   if (ctas == 0) return cudaSuccess;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  static const int sms = [dev] {  // the same part on every device of a node
-    int c = 0;
-    return cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && c > 0 ? c : 148;
-  }();
+  cudaError_t e = cudaSuccess;
+  const int sms = device_sms();
   if (q4) {
     if (ctas > 2 * sms) {
       if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<3>, g4r_smem_bytes(3, G4_MAX_NB))) == cudaSuccess)

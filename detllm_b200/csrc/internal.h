@@ -115,6 +115,8 @@ cudaError_t launch_k(const Launch& L, void (*kern)(KArgs...), dim3 grid, dim3 bl
 // the launch at hand, and whatever replays that launch on its own (a
 // profiler's node-by-node replay) checks it against the current cap.
 cudaError_t raise_smem_cap(const void* kern, size_t bytes);
+// SMs of the current device (read once: one part per node)
+int device_sms();
 
 // ---- launchers (kernels.cu) ------------------------------------------------
 cudaError_t launch_rope_table(const Launch& L, float* cos_t, float* sin_t, int positions, int half, int rope_dim,

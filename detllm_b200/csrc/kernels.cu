@@ -1138,6 +1138,17 @@ cudaError_t launch_embed(const Launch& L, const DevMatrix& m, const uint32_t* to
   return post(L);
 }
 
+int device_sms() {
+  static const int sms = [] {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        n <= 0)
+      return 148;
+    return n;
+  }();
+  return sms;
+}
+
 cudaError_t raise_smem_cap(const void* kern, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
   int dev = 0;
