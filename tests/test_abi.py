@@ -51,3 +51,28 @@ def test_no_silent_cpu_path_without_gpu(lib):
     with pytest.raises(D.DetError) as e:
         D.Model(O.fixture_gguf("tiny-f32"))
     assert e.value.code == D.ERR_NO_DEVICE
+
+
+def test_q8_kernel_choice_round_trips(lib):
+    import detllm_b200 as D
+
+    prev = D.set_q8_tensor_cores(True)
+    try:
+        assert D.set_q8_tensor_cores(False) is True
+        assert D.set_q8_tensor_cores(False) is False
+    finally:
+        D.set_q8_tensor_cores(prev)
+
+
+def test_add_latency_needs_a_gpu(lib):
+    import ctypes as C
+
+    import detllm_b200 as D
+
+    n = C.c_int(-1)
+    assert lib.det_device_count(C.byref(n)) == 0
+    if n.value > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(D.DetError) as e:
+        D.add_latency_cycles(0)
+    assert e.value.code == D.ERR_NO_DEVICE

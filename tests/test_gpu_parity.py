@@ -151,6 +151,13 @@ def test_fused_one_position_forward(D, long_models, name, tmp_path):
     assert diff[0].size == 0, f"{diff[0].size} logits differ, first at {diff[0][0]},{diff[1][0]}"
 
 
+def test_add_latency_probe(D):
+    """det_add_latency_cycles: one dependent f32 add takes a few cycles (the
+    chain floor bench.py reports decode against)."""
+    c = D.add_latency_cycles(0)
+    assert 1.0 < c < 64.0, c
+
+
 def test_device_expf_matches_vendored_expf(D, oracle):
     # every 251st bit pattern of the f32 space plus dense sweeps where the
     # algorithm changes branch (expf.rs:47-80) and the softmax/CDF range
