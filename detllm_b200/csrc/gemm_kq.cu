@@ -430,6 +430,158 @@ __global__ void __launch_bounds__(32) gemv_q4k_rows_kernel(KqSegs S, const int8_
   if (row < g.rows) kq_store(g, row, sum, err);
 }
 
+// Q4_K, one position, for narrow matrices (at most two CTAs per SM): the
+// same per-row chain, with the products made by other warps.  A lane of the
+// kernel above both forms its row's products and adds them, so with one
+// warp per SM sub-partition the row runs at the warp's issue rate, about
+// twice the chain's own latency of one dependent add per element.  Here a
+// CTA of 32 rows has four producer warps and one chain warp: producer thread
+// (row r, sub-block s of a half block) dequantises its 32 weights and forms
+// the exact products w * act (q4k_prod4), written to a three-slot ring of
+// half-block product tiles [32 rows][128 elements]; the chain warp's lane r
+// then only loads row r's products and adds them in element order.  The
+// raw blocks come in by cp.async, issued by the producers seven blocks ahead;
+// the product slots hand over on mbarriers (full: 128 producer arrivals,
+// empty: the chain warp), every wait bounded by %globaltimer and abandoned
+// at once after any timeout.
+constexpr int G4S_PROD_WARPS = 4;
+constexpr int G4S_THREADS = (G4S_PROD_WARPS + 1) * 32;
+constexpr int G4S_RAW = 8;                      // raw block slots: 7 blocks in flight
+constexpr int G4S_PS = 3;                       // product slots (half blocks)
+constexpr int G4S_PLD = 128 + 4;                // product row stride (floats): rows 4 banks apart
+constexpr int G4S_PSLOT = G4R_ROWS * G4S_PLD;   // floats per product slot
+// raw ring | product ring | activation [K] | full[PS], empty[PS] | abort flag
+inline size_t g4s_smem_bytes(int nbs) {
+  return (size_t)G4S_RAW * G4R_STAGE + (size_t)G4S_PS * G4S_PSLOT * 4 + (size_t)nbs * 256 * 4 + 2 * G4S_PS * 8 + 16;
+}
+
+// bounded wait for phase `parity`; returns at once once the CTA has given up
+DI void g4s_wait(uint32_t bar, uint32_t parity, volatile int* gave_up, uint32_t* err) {
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; it++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok || *gave_up) return;
+    if ((it & 63) == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      if (it == 0) {
+        t0 = t;
+      } else if (t - t0 > 2000000000ull) {
+        atomicOr(err, ERRF_TIMEOUT);
+        *gave_up = 1;
+        return;
+      }
+    }
+  }
+}
+DI void g4s_arrive(uint32_t bar) { asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory"); }
+
+__global__ void __launch_bounds__(G4S_THREADS) gemv_q4k_split_kernel(KqSegs S, const int8_t* __restrict__ aq,
+                                                                     const float* __restrict__ ad, uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t g4s_smem[];
+  const int nbs = S.nb, nbk = nbs * 8;
+  uint8_t* raw = g4s_smem;                                                          // [RAW][32 rows][144]
+  float* prod = reinterpret_cast<float*>(raw + (size_t)G4S_RAW * G4R_STAGE);        // [PS][32][PLD]
+  float* act = prod + (size_t)G4S_PS * G4S_PSLOT;                                   // [K]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(act + (size_t)nbs * 256);
+  volatile int* gave_up = reinterpret_cast<volatile int*>(bars + 2 * G4S_PS);
+  const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(bars), empty0 = full0 + 8 * G4S_PS;
+  const KqSeg g = kq_seg(S);
+  const int r0 = ((int)blockIdx.x - g.cta0) * G4R_ROWS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool producer = warp < G4S_PROD_WARPS;
+  if (tid == 0) {
+    for (int i = 0; i < G4S_PS; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(full0 + 8 * i), "r"(G4S_PROD_WARPS * 32) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(empty0 + 8 * i) : "memory");
+    }
+    *gave_up = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  // raw bytes of block b of the 32 rows into slot b % G4S_RAW (producers;
+  // rows past the matrix are zeros); one commit group per call
+  auto issue = [&](int b) {
+    if (b < nbs) {
+      uint8_t* dst0 = raw + (size_t)(b % G4S_RAW) * G4R_STAGE;
+      for (int c = tid; c < G4R_ROWS * 9; c += G4S_PROD_WARPS * 32) {
+        const int r = c / 9, part = c - 9 * r;
+        uint8_t* dst = dst0 + r * 144 + part * 16;
+        if (r0 + r < g.rows)
+          g4_cp_async16(dst, g.q + ((size_t)(r0 + r) * nbs + b) * 144 + part * 16);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    g4_cp_commit();
+  };
+  if (producer)
+    for (int b = 0; b < G4S_RAW - 1; b++) issue(b);  // weights are constant: before the predecessor ends
+  pdl_enter();
+  q4k_stage_act(act, aq, ad, nbk, tid, G4S_THREADS);
+  __syncthreads();  // activation and barrier initialisation visible
+
+  if (producer) {
+    const int pr = tid & 31, ps = tid >> 5;  // row, sub-block of the half block
+    for (int b = 0; b < nbs; b++) {
+      asm volatile("bar.sync 1, %0;\n" ::"n"(G4S_PROD_WARPS * 32) : "memory");  // slot (b - 1) % RAW is read
+      issue(b + G4S_RAW - 1);
+      g4_cp_wait<G4S_RAW - 1>();  // this thread's copies of block b have landed
+      asm volatile("bar.sync 1, %0;\n" ::"n"(G4S_PROD_WARPS * 32) : "memory");  // ... and every producer's
+      const uint8_t* blk = raw + (size_t)(b % G4S_RAW) * G4R_STAGE + pr * 144;
+      const uint4 h = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+      const float d = f16_bits_to_f32((uint16_t)(h.x & 0xffffu));
+      const float dmin = f16_bits_to_f32((uint16_t)(h.x >> 16));
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        const int hh = 2 * b + hf, slot = hh % G4S_PS;
+        g4s_wait(empty0 + 8 * slot, (uint32_t)(((hh / G4S_PS) & 1) ^ 1), gave_up, err);
+        const int j = 4 * hf + ps;  // sub-block: bytes 32 (j / 2) .., low nibbles for even j
+        unsigned long long dsc2, ndmn2;
+        q4k_sub_scales(h, d, dmin, j, dsc2, ndmn2);
+        const uint4 v0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (j >> 1));
+        const uint4 v1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * (j >> 1));
+        const uint32_t qw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const float4* av = reinterpret_cast<const float4*>(act + (size_t)b * 256 + 32 * j);
+        float4* dst = reinterpret_cast<float4*>(prod + (size_t)slot * G4S_PSLOT + pr * G4S_PLD + 32 * ps);
+#pragma unroll
+        for (int k = 0; k < 8; k++) dst[k] = q4k_prod4((qw[k] >> (4 * (j & 1))) & 0x0f0f0f0fu, dsc2, ndmn2, av[k]);
+        g4s_arrive(full0 + 8 * slot);
+      }
+    }
+    g4_cp_wait<0>();
+  } else {
+    // lane = row: the chain over the half blocks' products in element order
+    float sum = 0.0f;
+    for (int hh = 0; hh < 2 * nbs; hh++) {
+      const int slot = hh % G4S_PS;
+      g4s_wait(full0 + 8 * slot, (uint32_t)((hh / G4S_PS) & 1), gave_up, err);
+      const float4* src = reinterpret_cast<const float4*>(prod + (size_t)slot * G4S_PSLOT + lane * G4S_PLD);
+#pragma unroll
+      for (int k0 = 0; k0 < 32; k0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = src[k0 + u];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          sum = fadd(sum, v[u].x);
+          sum = fadd(sum, v[u].y);
+          sum = fadd(sum, v[u].z);
+          sum = fadd(sum, v[u].w);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) g4s_arrive(empty0 + 8 * slot);  // the slot's products are read
+    }
+    const int row = r0 + lane;
+    if (row < g.rows) kq_store(g, row, sum, err);
+  }
+}
+
 // Q6_K: per block the reference forms eight exact integer lane sums
 // aux[c] = sum over elements i = c (mod 8) of sc[i / 16] * a[i] * (q[i] - 32)
 // and then advances eight f32 chains sums[c] += (d * a.d) * aux[c] in block
@@ -545,56 +697,52 @@ DI void q6_aux(const Q6Item& it, const uint32_t* A, const uint32_t* Sp, int* dst
   }
 }
 
-// Activation pairs of Q8_K block b, group pair j (elements 32 j .. 32 j + 31):
-// A[c] and A[8 + c] hold (a[c], a[c + 8]) of the pair's two 16-element
-// groups as sign-extended 16-bit halves, Sp[c] their two sums.
-DI void q6_pairs(const int8_t* __restrict__ aq, int b, int j, uint32_t* A, uint32_t* Sp) {
-  const uint4 v0 = *reinterpret_cast<const uint4*>(aq + (size_t)b * 256 + j * 32);
-  const uint4 v1 = *reinterpret_cast<const uint4*>(aq + (size_t)b * 256 + j * 32 + 16);
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const uint32_t k = (uint32_t)(c & 3);
-    // bytes c and c + 8 of the group, each sign-extended to 16 bits
-    const uint32_t sel = k | ((k | 8u) << 4) | ((4u + k) << 8) | (((4u + k) | 8u) << 12);
-    const uint32_t a0 = prmt_sx(c < 4 ? v0.x : v0.y, c < 4 ? v0.z : v0.w, sel);
-    const uint32_t a1 = prmt_sx(c < 4 ? v1.x : v1.y, c < 4 ? v1.z : v1.w, sel);
-    A[c] = a0;
-    A[8 + c] = a1;
-    const int s0 = (int)(int16_t)(a0 & 0xffffu) + ((int)a0 >> 16);
-    const int s1 = (int)(int16_t)(a1 & 0xffffu) + ((int)a1 >> 16);
-    Sp[c] = s16pair(s0, s1);
-  }
+// Q6_K, one position, on int8 tensor cores (mma.sync m16n8k16).  Per block
+// the reference's lane sums (dot_q6_k_q8k, det-quant lib.rs:353-397) are
+//   aux[r][l] = sum over the 16 scale groups j of scale[r][j] * C_j[r][l],
+//   C_j[r][l] = sum over e in {16 j + l, 16 j + 8 + l} of (q6[r][e] - 32) * a[e],
+// so one group of 16 rows is one m16n8k16 MMA: A = the rows' 6-bit codes of
+// the group as unsigned bytes (MMA column k = element 16 j + k), B = the
+// activation placed so that output column l sees only the group's two
+// elements of lane l (B[k][l] = a[16 j + k] when k % 8 == l, else 0).  Every
+// C_j' = sum of q6 * a fits 16 bits (|C| <= 16,128), so the scale step takes
+// a group pair at once: dp2a of the packed (C'_2Q, C'_2Q+1) with scale bytes
+// 2Q and 2Q + 1.  The -32 offset is one more product per tile,
+//   sum over j of scale[r][j] * (a[16 j + l] + a[16 j + 8 + l]),
+// two m16n8k16 MMAs of the rows' 16 scales (as A, k = group) by the
+// activation's two elements of each (group, lane) (as B), taken 32 times
+// off the integer sums.  The float work is the reference's: d = w.d *
+// a.d, p = d * (f32)aux, each (row, lane) chain adds p in block order, and
+// the row's result sums its eight chains in lane order.
+//
+// A CTA owns ceil(rows / SMs) contiguous rows, so the weight stream is
+// spread evenly over every SM.  It walks them in groups of 32 rows, each
+// group's blocks in chunks of 8; one stage is one (group, chunk), whose
+// rows are contiguous 1,664-byte runs (one cp.async.bulk per row) moved into
+// a Q6M_STAGES-slot ring on per-slot mbarriers.  Each of the 16 warps takes
+// one (16-row tile, block) unit per stage and leaves its 16 x 8 products in
+// shared memory; after the stage's barrier, threads (row, lane) add them to
+// their chains while the warps go on to the next stage.  The activation is
+// staged once per CTA: the B bytes of every (block, thread slot) and the
+// offset operands of every (block, thread).  Waits are bounded by
+// %globaltimer.
+constexpr int Q6M_THREADS = 512;
+constexpr int Q6M_GROUP = 32;                          // rows per group (two MMA tiles)
+constexpr int Q6M_CHUNK = 8;                           // blocks per stage
+constexpr int Q6M_STAGES = 3;
+constexpr int Q6M_ROW = Q6M_CHUNK * 208;               // one row of a stage: 1,664 B
+constexpr int Q6M_ROW_LD = Q6M_ROW + 16;               // its slot: 420 words, so rows g = 0..7 start 4 banks apart
+constexpr int Q6M_STAGE = Q6M_GROUP * Q6M_ROW_LD;      // 53,760 B
+constexpr int Q6M_MAX_NB = 64;                         // K <= 16384 (activation tables in shared memory)
+constexpr int Q6M_PLD = Q6M_CHUNK * 8 + 8;             // product row stride (floats): conflict-free chain reads
+constexpr int Q6M_PBUF = 2 * Q6M_GROUP * Q6M_PLD * 4;  // two stages of products
+// ring | mbarriers (32 B) | B bytes [nb][16][16] | offset B words [nb][32][2] | products | a.d [nb]
+inline size_t q6m_smem_bytes(int nb) {
+  return (size_t)Q6M_STAGES * Q6M_STAGE + 32 + (size_t)nb * 256 + (size_t)nb * 256 + Q6M_PBUF + (size_t)nb * 4;
 }
+static_assert(Q6M_PBUF >= Q6M_MAX_NB * 256, "the activation is staged in the product buffers");
 
-// Q6_K, one position, streamed: the same integer lane sums and chains as
-// gemv_q6k_aux_kernel, with the weight stream overlapping the integer work.
-// A persistent CTA (one per SM) walks 32-row tiles; each tile is read in
-// passes of 8 blocks, one (row, block) item of 208 bytes per thread, and
-// every thread moves the item it will use in the NEXT pass into its own
-// slot of a two-pass shared-memory buffer with one cp.async.bulk while it
-// works on the current one (the passes run on across tile boundaries); a
-// buffer's mbarrier counts the pass's bytes (thread 0 arrives with the
-// expected total).  The activation's pairs for all blocks are staged once
-// per CTA.  After a pass, thread (row, class) advances its f32 chain over
-// the pass's blocks in order; after a tile's last pass the row's eight
-// chains are summed in lane order.  Waits are bounded by %globaltimer.
-constexpr int Q6S_ROWS = 32;
-constexpr int Q6S_NBP = 8;  // blocks per pass
-constexpr int Q6S_THREADS = Q6S_ROWS * Q6S_NBP;
-constexpr int Q6S_AUX_LD = Q6S_NBP * 8 + 1;  // aux row stride (ints)
-constexpr int Q6S_MAX_NB = 64;               // K <= 16384 (activation pairs staged in shared memory)
-inline size_t q6s_smem_bytes(int nb) {
-  return (size_t)2 * Q6S_THREADS * 208 + (size_t)nb * (128 + 64) * 4 + (size_t)Q6S_ROWS * Q6S_AUX_LD * 4 +
-         (size_t)Q6S_ROWS * (Q6S_NBP + 1) * 4 + 16;
-}
-
-// the segment that holds tile `tile` (its first tile is its cta0)
-DI KqSeg kq_seg_at(const KqSegs& S, int tile) {
-  const int i = (int)(tile >= S.s[1].cta0) + (int)(tile >= S.s[2].cta0);
-  return i == 0 ? S.s[0] : (i == 1 ? S.s[1] : S.s[2]);
-}
-
-DI bool q6s_wait(uint32_t bar, uint32_t parity) {
+DI bool q6m_wait(uint32_t bar, uint32_t parity) {
   unsigned long long t0 = 0;
   for (unsigned it = 0;; it++) {
     uint32_t ok;
@@ -604,123 +752,329 @@ DI bool q6s_wait(uint32_t bar, uint32_t parity) {
         : "r"(bar), "r"(parity)
         : "memory");
     if (ok) return true;
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    if (it == 0) t0 = t;
-    else if (t - t0 > 2000000000ull) return false;
+    if ((it & 63) == 0) {  // the clock every 64 polls
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) return false;
+    }
   }
 }
 
-__global__ void __launch_bounds__(Q6S_THREADS, 1) gemv_q6k_stream_kernel(KqSegs S, int tiles,
-                                                                        const int8_t* __restrict__ aq,
-                                                                        const float* __restrict__ ad,
-                                                                        uint32_t* err) {
-  extern __shared__ __align__(16) uint8_t q6s_smem[];
-  uint8_t* items = q6s_smem;                                                      // [2][256][208]
-  uint32_t* apair = reinterpret_cast<uint32_t*>(items + (size_t)2 * Q6S_THREADS * 208);  // [nb][16][8]
+// the segment of concatenated row r and r's index in it
+DI KqSeg q6m_seg(const KqSegs& S, int r, int& rr) {
+  const int p1 = S.s[0].rows, p2 = p1 + S.s[1].rows;
+  if (r < p1) {
+    rr = r;
+    return S.s[0];
+  }
+  if (r < p2) {
+    rr = r - p1;
+    return S.s[1];
+  }
+  rr = r - p2;
+  return S.s[2];
+}
+
+// the unsigned 6-bit codes of quarter qd (nibble nib of the ql word, bits
+// 2 qd, 2 qd + 1 of the qh word) for four consecutive elements
+template <int NIB, int QD>
+DI uint32_t q6m_code(uint32_t ql, uint32_t qh) {
+  const uint32_t lo = NIB ? ql >> 4 : ql;
+  const uint32_t hi = QD == 0 ? qh << 4 : (QD == 1 ? qh << 2 : (QD == 2 ? qh : qh >> 2));
+  return (lo & 0x0f0f0f0fu) | (hi & 0x30303030u);
+}
+
+// four 8 x 16-byte matrices: lane 8 m + r gives row r of matrix m; lane
+// (g, t) receives word t of row g of each
+DI void q6m_ldsm(const uint8_t* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(p))
+               : "memory");
+}
+
+// c = A B with unsigned A (the codes), signed B
+DI void q6m_mma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(b), "r"(0));
+}
+// c += A B, both signed (the offset product)
+DI void q6m_mma_ss(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(b));
+}
+
+__global__ void __launch_bounds__(Q6M_THREADS, 1) gemv_q6k_mma_kernel(KqSegs S, int total, int per_cta,
+                                                                      const int8_t* __restrict__ aq,
+                                                                      const float* __restrict__ ad, uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t q6m_smem[];
   const int nb = S.nb;
-  uint32_t* spair = apair + (size_t)nb * 128;                                     // [nb][8][8]
-  int* aux = reinterpret_cast<int*>(spair + (size_t)nb * 64);                     // [32][Q6S_AUX_LD]
-  float* ddv = reinterpret_cast<float*>(aux + Q6S_ROWS * Q6S_AUX_LD);             // [32][Q6S_NBP + 1]
-  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(ddv + Q6S_ROWS * (Q6S_NBP + 1));  // [2] mbarriers
-  const int t = threadIdx.x;
-  const int ir = t & 31, ib = t >> 5;  // this thread's item: row ir, block ib of each pass
-  const int cr = t >> 3, cc = t & 7;   // chain: row, class
-  const int npass = (nb + Q6S_NBP - 1) / Q6S_NBP;
-  // the passes of this CTA, in order: tile blockIdx.x + k gridDim.x, pass p
-  const int my_tiles = tiles > (int)blockIdx.x ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int nq = my_tiles * npass;
-  if (t == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar0) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar0 + 8) : "memory");
+  uint8_t* ring = q6m_smem;                                                      // [stages][32 rows][1680]
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(ring + (size_t)Q6M_STAGES * Q6M_STAGE);
+  uint8_t* bact = ring + (size_t)Q6M_STAGES * Q6M_STAGE + 32;                   // [nb][16 slots][16 groups]
+  // offset B words: lane (g, t) holds bytes a[16 (4t + i) + g] and
+  // a[16 (4t + i) + 8 + g], i = 0..3, of each block
+  uint2* offb = reinterpret_cast<uint2*>(bact + (size_t)nb * 256);
+  float* pbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(offb) + (size_t)nb * 256);  // [2][32][PLD]
+  float* adv = pbuf + 2 * Q6M_GROUP * Q6M_PLD;                                  // [nb]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;     // MMA fragment coordinates
+  const int mt = warp >> 3, bb = warp & 7;   // this warp's unit: 16-row tile, block of the chunk
+  const int row0 = (int)blockIdx.x * per_cta, rows = min(per_cta, total - row0);
+  const int nch = (nb + Q6M_CHUNK - 1) / Q6M_CHUNK;
+  const int nst = (rows + Q6M_GROUP - 1) / Q6M_GROUP * nch;
+  if (tid == 0) {
+    for (int s = 0; s < Q6M_STAGES; s++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar0 + 8 * s) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
 
-  // pass q's item of this thread into buffer q & 1 (one bulk copy), and its
-  // block scale; thread 0 arrives on the buffer's barrier with the pass's
-  // byte count (complete_tx may come first: the count then runs negative)
-  auto issue = [&](int q, uint32_t& dbits) {
-    if (q >= nq) return;
-    const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, p = q % npass, b = p * Q6S_NBP + ib;
-    const KqSeg g = kq_seg_at(S, tile);
-    const int r0 = (tile - g.cta0) * Q6S_ROWS, row = r0 + ir;
-    const uint32_t bar = bar0 + 8 * (q & 1);
-    if (t == 0) {
-      const uint32_t nrow = (uint32_t)min(Q6S_ROWS, g.rows - r0), nblk = (uint32_t)min(Q6S_NBP, nb - p * Q6S_NBP);
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(nrow * nblk * 208u)
-                   : "memory");
-    }
-    if (b < nb && row < g.rows) {
-      const uint8_t* src = g.q + ((size_t)row * nb + b) * 208;
-      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208);
-      // the slot was last read with ordinary loads (pass q - 2)
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], 208, [%2];\n" ::"r"(dst),
-                   "l"(src), "r"(bar)
-                   : "memory");
-      dbits = g.d[(size_t)row * nb + b];
+  // stage coordinates (row group, chunk), advanced one stage at a time
+  struct At {
+    int grp, ch;
+  };
+  auto next = [&](At& a) {
+    if (++a.ch == nch) {
+      a.ch = 0;
+      a.grp++;
     }
   };
-  uint32_t dnext = 0;
-  issue(0, dnext);  // weights are constant: before the predecessor ends
-  pdl_enter();
-  for (int i = t; i < nb * 8; i += Q6S_THREADS)
-    q6_pairs(aq, i >> 3, i & 7, apair + (i >> 3) * 128 + (2 * (i & 7)) * 8, spair + (i >> 3) * 64 + (i & 7) * 8);
-  __syncthreads();
-
-  float sum = 0.0f;
-  bool ok = true;
-  int issued = nq > 0 ? 0 : -1;  // the last pass whose copies were issued
-  for (int q = 0; q < nq; q++) {
-    const int tile = (int)blockIdx.x + (q / npass) * (int)gridDim.x, p = q % npass;
-    const KqSeg g = kq_seg_at(S, tile);
-    const int r0 = (tile - g.cta0) * Q6S_ROWS, b0 = p * Q6S_NBP;
-    const uint32_t dcur = dnext;
-    issue(q + 1, dnext);
-    if (q + 1 < nq) issued = q + 1;
-    const int b = b0 + ib;
-    const bool has = b < nb && r0 + ir < g.rows;
-    const float adb = has ? ad[b] : 0.0f;
-    if (!q6s_wait(bar0 + 8 * (q & 1), (uint32_t)((q >> 1) & 1))) {  // pass q's items have landed
-      atomicOr(err, ERRF_TIMEOUT);
-      ok = false;
+  // stage s (at a) into slot s % Q6M_STAGES: one bulk copy per row; thread
+  // 0 arrives with the stage's byte count (complete_tx may come first)
+  auto issue = [&](int s, const At& a) {
+    const int r0 = a.grp * Q6M_GROUP, nr = min(Q6M_GROUP, rows - r0);
+    const int b0 = a.ch * Q6M_CHUNK, nbk = min(Q6M_CHUNK, nb - b0);
+    const uint32_t bar = bar0 + 8 * (s % Q6M_STAGES);
+    if (tid == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"((uint32_t)(nr * nbk * 208))
+                   : "memory");
+    if (tid < nr) {
+      int rr;
+      const KqSeg sg = q6m_seg(S, row0 + r0 + tid, rr);
+      const uint8_t* src = sg.q + ((size_t)rr * nb + b0) * 208;
+      const uint32_t dst =
+          (uint32_t)__cvta_generic_to_shared(ring + (size_t)(s % Q6M_STAGES) * Q6M_STAGE + (size_t)tid * Q6M_ROW_LD);
+      // the slot was last read with ordinary loads (stage s - Q6M_STAGES)
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                   "l"(src), "r"((uint32_t)(nbk * 208)), "r"(bar)
+                   : "memory");
     }
-    if (!__syncthreads_and(ok)) break;
-    if (has) {
-      Q6Item it;
-      const uint4* src = reinterpret_cast<const uint4*>(items + ((size_t)(q & 1) * Q6S_THREADS + t) * 208);
-#pragma unroll
-      for (int k = 0; k < 13; k++) {
-        const uint4 v = src[k];
-        it.w[4 * k] = v.x;
-        it.w[4 * k + 1] = v.y;
-        it.w[4 * k + 2] = v.z;
-        it.w[4 * k + 3] = v.w;
+  };
+  // the f16 block scales of this thread's rows g and g + 8 in the unit of
+  // the stage at a (row pointers cached per group; 0 past the rows)
+  int dgrp = -1;
+  const uint16_t *dpa = nullptr, *dpb = nullptr;
+  auto load_d = [&](const At& a, uint32_t& da, uint32_t& db) {
+    da = db = 0u;
+    if (a.grp != dgrp) {
+      dgrp = a.grp;
+      const int la = a.grp * Q6M_GROUP + mt * 16 + g;
+      int rr;
+      dpa = dpb = nullptr;
+      if (la < rows) {
+        const KqSeg sg = q6m_seg(S, row0 + la, rr);
+        dpa = sg.d + (size_t)rr * nb;
       }
-      q6_aux(it, apair + b * 128, spair + b * 64, aux + ir * Q6S_AUX_LD + ib * 8);
-      ddv[ir * (Q6S_NBP + 1) + ib] = fmul(f16_bits_to_f32((uint16_t)dcur), adb);
+      if (la + 8 < rows) {
+        const KqSeg sg = q6m_seg(S, row0 + la + 8, rr);
+        dpb = sg.d + (size_t)rr * nb;
+      }
     }
-    __syncthreads();  // aux / ddv of the pass complete
-    if (r0 + cr < g.rows) {
-      const int nbp = min(Q6S_NBP, nb - b0);
-      const int* src = aux + cr * Q6S_AUX_LD + cc;
-      const float* dd = ddv + cr * (Q6S_NBP + 1);
-      for (int bb = 0; bb < nbp; bb++) sum = fadd(sum, fmul(dd[bb], __int2float_rn(src[bb * 8])));
+    const int b = a.ch * Q6M_CHUNK + bb;
+    if (b < nb) {
+      if (dpa) da = dpa[b];
+      if (dpb) db = dpb[b];
     }
-    if (p == npass - 1) {
+  };
+  int issued = 0;
+  At ia{0, 0};  // the next stage to issue
+  for (; issued < nst && issued < Q6M_STAGES; issued++, next(ia)) issue(issued, ia);  // weights are constant: before the predecessor ends
+  uint32_t da, db;
+  load_d(At{0, 0}, da, db);
+  pdl_enter();
+
+  // activation tables: the raw bytes staged in the product buffers first
+  {
+    int8_t* raw = reinterpret_cast<int8_t*>(pbuf);
+    for (int i = tid; i < nb * 16; i += Q6M_THREADS)
+      reinterpret_cast<uint4*>(raw)[i] = reinterpret_cast<const uint4*>(aq)[i];
+    for (int b = tid; b < nb; b += Q6M_THREADS) adv[b] = ad[b];
+    __syncthreads();
+    // B bytes: slot sl = 4 t + (g & 3) holds a[16 j + sl] for j = 0..15
+    for (int i = tid; i < nb * 16; i += Q6M_THREADS) {
+      const int b = i >> 4, sl = i & 15;
+      const int8_t* a = raw + b * 256 + sl;
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++)
+        w[k] = (uint32_t)(uint8_t)a[64 * k] | ((uint32_t)(uint8_t)a[64 * k + 16] << 8) |
+               ((uint32_t)(uint8_t)a[64 * k + 32] << 16) | ((uint32_t)(uint8_t)a[64 * k + 48] << 24);
+      reinterpret_cast<uint4*>(bact)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (int i = tid; i < nb * 32; i += Q6M_THREADS) {
+      const int b = i >> 5, lg = (i & 31) >> 2, lt = i & 3;
+      const int8_t* a = raw + b * 256 + 64 * lt + lg;
+      uint32_t w0 = 0u, w1 = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        w0 |= (uint32_t)(uint8_t)a[16 * k] << (8 * k);
+        w1 |= (uint32_t)(uint8_t)a[16 * k + 8] << (8 * k);
+      }
+      offb[i] = make_uint2(w0, w1);
+    }
+    __syncthreads();  // the product buffers are free again
+  }
+
+  // B placement: byte x of an activation word to byte g & 3 when this
+  // thread's k rows (4 t .. 4 t + 3) hold lane g's elements, else zero
+  const bool bl = (g >> 2) == (t & 1);
+  uint32_t bsel[4];
+#pragma unroll
+  for (int x = 0; x < 4; x++)
+    bsel[x] = bl ? ((0x4444u & ~(0xfu << (4 * (g & 3)))) | ((uint32_t)x << (4 * (g & 3)))) : 0x4444u;
+
+  // threads (row tid >> 3, lane tid & 7) < 256 add the products of the
+  // stage at a (buffer sp & 1) to their chains in block order; after a
+  // group's last chunk each row sums its eight chains in lane order and is
+  // stored.  A stage's products stay in place until the barrier of the next.
+  float csum = 0.0f;
+  auto chain = [&](int sp, const At& a) {
+    if (tid >= 256) return;
+    const int crow = tid >> 3;
+    const int nbk = min(Q6M_CHUNK, nb - a.ch * Q6M_CHUNK);
+    const float* pr = pbuf + (size_t)(sp & 1) * Q6M_GROUP * Q6M_PLD + (size_t)crow * Q6M_PLD + (tid & 7);
+    float pv[Q6M_CHUNK];
+#pragma unroll
+    for (int k = 0; k < Q6M_CHUNK; k++) pv[k] = pr[k * 8];  // in the buffer for every k; used below nbk
+#pragma unroll
+    for (int k = 0; k < Q6M_CHUNK; k++)
+      if (k < nbk) csum = fadd(csum, pv[k]);
+    if (a.ch == nch - 1) {
       // ((((0 + s0) + s1) + ...) + s7) within each group of eight lanes
       float v = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 8; k++) v = fadd(v, __shfl_sync(0xffffffffu, sum, (t & 31 & ~7) + k));
-      const int row = r0 + cr;
-      if (cc == 0 && row < g.rows) kq_store(g, row, v, err);
-      sum = 0.0f;
+      for (int k = 0; k < 8; k++) v = fadd(v, __shfl_sync(0xffffffffu, csum, (lane & ~7) + k));
+      const int r = a.grp * Q6M_GROUP + crow;
+      if ((tid & 7) == 0 && r < rows) {
+        int rr;
+        const KqSeg sg = q6m_seg(S, row0 + r, rr);
+        kq_store(sg, rr, v, err);
+      }
+      csum = 0.0f;
     }
-    __syncthreads();  // aux / ddv free for the next pass
+  };
+  bool ok = true;
+  int s = 0;
+  At at{0, 0}, prev{0, 0};  // stage s, stage s - 1
+  for (; s < nst; s++) {
+    const int slot = s % Q6M_STAGES, buf = s & 1;
+    At nx = at;
+    next(nx);
+    uint32_t dna = 0u, dnb = 0u;
+    if (s + 1 < nst) load_d(nx, dna, dnb);
+    if (!q6m_wait(bar0 + 8 * slot, (uint32_t)((s / Q6M_STAGES) & 1))) {
+      atomicOr(err, ERRF_TIMEOUT);
+      ok = false;
+    }
+    const int b = at.ch * Q6M_CHUNK + bb;
+    if (ok && b < nb && at.grp * Q6M_GROUP + mt * 16 < rows) {
+      const uint8_t* wa = ring + (size_t)slot * Q6M_STAGE + (size_t)(mt * 16 + g) * Q6M_ROW_LD + bb * 208;
+      const uint8_t* wb = wa + 8 * Q6M_ROW_LD;
+      const uint4 sca = *reinterpret_cast<const uint4*>(wa + 192);
+      const uint4 scb = *reinterpret_cast<const uint4*>(wb + 192);
+      const uint4 av = *reinterpret_cast<const uint4*>(bact + ((size_t)b * 16 + 4 * t + (g & 3)) * 16);
+      const uint32_t avw[4] = {av.x, av.y, av.z, av.w};
+      const uint32_t scwa[4] = {sca.x, sca.y, sca.z, sca.w}, scwb[4] = {scb.x, scb.y, scb.z, scb.w};
+      // ldmatrix rows: lanes 8m .. 8m + 7 give matrix m = (rows 0-7 | 8-15 of the tile, bytes 0-15 | 16-31 of a run)
+      const uint8_t* lrow = ring + (size_t)slot * Q6M_STAGE +
+                            (size_t)(mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * Q6M_ROW_LD + bb * 208 +
+                            16 * (lane >> 4);
+      int xa0 = 0, xa1 = 0, xb0 = 0, xb1 = 0;  // aux of (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t hE_a, hE_b, hO_a, hO_b;  // qh words t (group E) and 4 + t (group O) of rows g, g + 8
+        q6m_ldsm(lrow + 128 + 32 * h, hE_a, hE_b, hO_a, hO_b);
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+          uint32_t lE_a, lE_b, lO_a, lO_b;  // ql words of run (h, p), likewise
+          q6m_ldsm(lrow + 64 * h + 32 * p, lE_a, lE_b, lO_a, lO_b);
+#pragma unroll
+          for (int nib = 0; nib < 2; nib++) {
+            const int qd = p + 2 * nib, Q = 4 * h + qd;  // groups 2Q, 2Q + 1
+            uint32_t aE0, aE1, aO0, aO1;
+            if (nib == 0 && p == 0) {
+              aE0 = q6m_code<0, 0>(lE_a, hE_a), aE1 = q6m_code<0, 0>(lE_b, hE_b);
+              aO0 = q6m_code<0, 0>(lO_a, hO_a), aO1 = q6m_code<0, 0>(lO_b, hO_b);
+            } else if (nib == 0) {
+              aE0 = q6m_code<0, 1>(lE_a, hE_a), aE1 = q6m_code<0, 1>(lE_b, hE_b);
+              aO0 = q6m_code<0, 1>(lO_a, hO_a), aO1 = q6m_code<0, 1>(lO_b, hO_b);
+            } else if (p == 0) {
+              aE0 = q6m_code<1, 2>(lE_a, hE_a), aE1 = q6m_code<1, 2>(lE_b, hE_b);
+              aO0 = q6m_code<1, 2>(lO_a, hO_a), aO1 = q6m_code<1, 2>(lO_b, hO_b);
+            } else {
+              aE0 = q6m_code<1, 3>(lE_a, hE_a), aE1 = q6m_code<1, 3>(lE_b, hE_b);
+              aO0 = q6m_code<1, 3>(lO_a, hO_a), aO1 = q6m_code<1, 3>(lO_b, hO_b);
+            }
+            int cE[4], cO[4];
+            q6m_mma(cE, aE0, aE1, __byte_perm(avw[Q >> 1], 0u, bsel[(2 * Q) & 3]));
+            q6m_mma(cO, aO0, aO1, __byte_perm(avw[Q >> 1], 0u, bsel[(2 * Q + 1) & 3]));
+            const uint32_t pa0 = __byte_perm((uint32_t)cE[0], (uint32_t)cO[0], 0x5410u);
+            const uint32_t pa1 = __byte_perm((uint32_t)cE[1], (uint32_t)cO[1], 0x5410u);
+            const uint32_t pb0 = __byte_perm((uint32_t)cE[2], (uint32_t)cO[2], 0x5410u);
+            const uint32_t pb1 = __byte_perm((uint32_t)cE[3], (uint32_t)cO[3], 0x5410u);
+            if (Q & 1) {  // scale bytes 2, 3 of word Q >> 1
+              xa0 = dp2a_hi_ss(pa0, scwa[Q >> 1], xa0);
+              xa1 = dp2a_hi_ss(pa1, scwa[Q >> 1], xa1);
+              xb0 = dp2a_hi_ss(pb0, scwb[Q >> 1], xb0);
+              xb1 = dp2a_hi_ss(pb1, scwb[Q >> 1], xb1);
+            } else {  // bytes 0, 1
+              xa0 = dp2a_lo_ss(pa0, scwa[Q >> 1], xa0);
+              xa1 = dp2a_lo_ss(pa1, scwa[Q >> 1], xa1);
+              xb0 = dp2a_lo_ss(pb0, scwb[Q >> 1], xb0);
+              xb1 = dp2a_lo_ss(pb1, scwb[Q >> 1], xb1);
+            }
+          }
+        }
+      }
+      {  // the -32 offset: 32 * sum over j of scale[r][j] * (a[16 j + l] + a[16 j + 8 + l])
+        const uint2 ow = offb[(size_t)b * 32 + lane];
+        const uint32_t swa = *reinterpret_cast<const uint32_t*>(wa + 192 + 4 * t);
+        const uint32_t swb = *reinterpret_cast<const uint32_t*>(wb + 192 + 4 * t);
+        int co[4] = {0, 0, 0, 0};
+        q6m_mma_ss(co, swa, swb, ow.x);
+        q6m_mma_ss(co, swa, swb, ow.y);
+        xa0 -= 32 * co[0];
+        xa1 -= 32 * co[1];
+        xb0 -= 32 * co[2];
+        xb1 -= 32 * co[3];
+      }
+      const float adb = adv[b];
+      const float dda = fmul(f16_bits_to_f32((uint16_t)da), adb), ddb = fmul(f16_bits_to_f32((uint16_t)db), adb);
+      float* pr = pbuf + (size_t)buf * Q6M_GROUP * Q6M_PLD + (size_t)(mt * 16 + g) * Q6M_PLD + bb * 8 + 2 * t;
+      *reinterpret_cast<float2*>(pr) = make_float2(fmul(dda, __int2float_rn(xa0)), fmul(dda, __int2float_rn(xa1)));
+      *reinterpret_cast<float2*>(pr + 8 * Q6M_PLD) =
+          make_float2(fmul(ddb, __int2float_rn(xb0)), fmul(ddb, __int2float_rn(xb1)));
+    }
+    if (s > 0) chain(s - 1, prev);  // overlaps the other warps' units of stage s
+    da = dna;
+    db = dnb;
+    prev = at;
+    at = nx;
+    if (!__syncthreads_and(ok)) break;  // the stage's products are complete and its slot is free
+    if (issued < nst) {
+      issue(issued, ia);
+      issued++;
+      next(ia);
+    }
   }
+  if (ok && nst > 0) chain(nst - 1, prev);
   if (!ok)  // every copy issued has landed before the CTA's shared memory goes away (bounded)
-    for (int q = max(0, issued - 1); q <= issued; q++) q6s_wait(bar0 + 8 * (q & 1), (uint32_t)((q >> 1) & 1));
+    for (int q = s; q < issued; q++) q6m_wait(bar0 + 8 * (q % Q6M_STAGES), (uint32_t)((q / Q6M_STAGES) & 1));
 }
 
 template <int R>
@@ -807,20 +1161,21 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
   for (int i = 0; i < n; i++)
     if (!kq_decode_supported(*m[i])) return cudaErrorInvalidValue;
   const bool q4 = m[0]->type == GT_Q4_K;
-  // Q6_K: the streamed kernel when the activation pairs fit in shared memory,
-  // else two (row, block) items per thread per pass of up to 32 blocks, 16
-  // rows per CTA
-  const bool q6s = !q4 && m[0]->nb <= Q6S_MAX_NB;
-  const int per = q4 ? G4R_ROWS : (q6s ? Q6S_ROWS : 16);
+  // Q6_K: the tensor-core kernel when the activation tables fit in shared
+  // memory, else two (row, block) items per thread per pass of up to 32
+  // blocks, 16 rows per CTA
+  const bool q6m = !q4 && m[0]->nb <= Q6M_MAX_NB;
+  const int per = q4 ? G4R_ROWS : 16;
   KqSegs S;
   S.nb = m[0]->nb;
-  int ctas = 0;  // CTAs of the per-tile kernels, tiles of the streamed one
+  int ctas = 0, total = 0;  // CTAs of the per-tile kernels; rows
   for (int i = 0; i < 3; i++) {
     KqSeg& g = S.s[i];
     if (i < n) {
       if (m[i]->type != m[0]->type || m[i]->nb != S.nb) return cudaErrorInvalidValue;
       g = KqSeg{(const uint8_t*)m[i]->q, m[i]->d, m[i]->rows, ctas, out[i], epi[i], bias[i]};
       ctas += (m[i]->rows + per - 1) / per;
+      total += m[i]->rows;
     } else {
       g = KqSeg{nullptr, nullptr, 0, 0x7fffffff, nullptr, EPI_STORE, nullptr};
     }
@@ -833,14 +1188,15 @@ cudaError_t launch_gemv_kq_decode_segs(const Launch& L, const DevMatrix* const* 
       if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<3>, g4r_smem_bytes(3, G4_MAX_NB))) == cudaSuccess)
         e = launch_k(L, gemv_q4k_rows_kernel<3>, ctas, G4R_ROWS, g4r_smem_bytes(3, S.nb), S, a.qa_q, a.qa_d,
                      L.err);
-    } else if ((e = raise_smem_cap((const void*)gemv_q4k_rows_kernel<8>, g4r_smem_bytes(8, G4_MAX_NB))) ==
-               cudaSuccess) {
-      e = launch_k(L, gemv_q4k_rows_kernel<8>, ctas, G4R_ROWS, g4r_smem_bytes(8, S.nb), S, a.qa_q, a.qa_d, L.err);
+    } else if ((e = raise_smem_cap((const void*)gemv_q4k_split_kernel, g4s_smem_bytes(G4_MAX_NB))) == cudaSuccess) {
+      e = launch_k(L, gemv_q4k_split_kernel, ctas, G4S_THREADS, g4s_smem_bytes(S.nb), S, a.qa_q, a.qa_d, L.err);
     }
-  } else if (q6s) {
-    if ((e = raise_smem_cap((const void*)gemv_q6k_stream_kernel, q6s_smem_bytes(Q6S_MAX_NB))) == cudaSuccess)
-      e = launch_k(L, gemv_q6k_stream_kernel, std::min(ctas, sms), Q6S_THREADS, q6s_smem_bytes(S.nb), S, ctas,
-                   a.qk_q, a.qk_d, L.err);
+  } else if (q6m) {
+    // ceil(rows / SMs) contiguous rows per CTA
+    const int per_cta = (total + sms - 1) / sms, grid = (total + per_cta - 1) / per_cta;
+    if ((e = raise_smem_cap((const void*)gemv_q6k_mma_kernel, q6m_smem_bytes(Q6M_MAX_NB))) == cudaSuccess)
+      e = launch_k(L, gemv_q6k_mma_kernel, grid, Q6M_THREADS, q6m_smem_bytes(S.nb), S, total, per_cta, a.qk_q,
+                   a.qk_d, L.err);
   } else {
     if ((e = raise_smem_cap((const void*)gemv_q6k_aux_kernel<16>, g6_smem<16>())) == cudaSuccess)
       e = launch_k(L, gemv_q6k_aux_kernel<16>, ctas, G6_THREADS, g6_smem<16>(), S, a.qk_q, a.qk_d, L.err);
