@@ -238,9 +238,9 @@ DI void kq_store(const KqSeg& g, int row, float sum, uint32_t* err) {
 // ring with cp.async, G4R_STAGES - 1 super-blocks ahead, and holds the
 // activation, dequantised once (act[i] = a.d * a.q, the reference's value),
 // in shared memory, where every lane reads the same float4 (a broadcast).
-// A wide matrix (more CTAs than two per SM) gets 3 ring slots, which keep
-// the CTA at 30 KB so that seven fit per SM and the matrix runs in one wave;
-// a narrow one gets 8, so that its few warps keep 7 super-blocks in flight.
+// It serves wide matrices (more CTAs than two per SM; gemv_q4k_split_kernel
+// below takes the narrow ones): 3 ring slots keep the CTA at 30 KB, so that
+// seven fit per SM and the matrix runs in one wave.
 // Lane l reads its row's bytes at 144 l: a quarter-warp's eight 16-byte
 // reads fall in distinct bank groups.  The dequantisation and the products
 // run as f32x2 pairs; the chain adds one element at a time.
