@@ -1,11 +1,11 @@
 """det_symbol_ranges_noalloc against det_symbol_ranges.
 
 The no-allocation entry point serves callers that cannot allocate device
-memory inside a call (graph capture, fixed memory budgets, foreign
-allocators): they hand it device buffers and it works in a fixed device
-array.  Its results are integers, so they must equal the session entry
-point's exactly, call after call, although every call reuses the same
-array.  This file is collected last so that a stop at the first failure has
+memory inside a call (engines whose memory budget is fixed at start-up,
+runtimes whose allocator is not cudaMalloc): they hand it device buffers and
+it works in a fixed device array.  Its results are integers, so they must
+equal the session entry point's exactly, call after call, although every
+call reuses the same array.  This file is collected last so that a stop at the first failure has
 already run every other test.
 """
 import numpy as np
