@@ -609,7 +609,6 @@ __global__ void __launch_bounds__(ATG_THREADS)
   float* qs = sm;                         // [gsz][hd]
   float* kvs = qs + gsz * hd;             // [ATG_J][ks]  (K chunk, then V chunk)
   float* sc = smem_scores ? kvs + ATG_J * ks : scratch + ((size_t)t * n_head + h0) * n_ctx;  // [gsz][n_ctx]
-  __shared__ float zs[32];
   const float* qg = q + ((size_t)t * n_head + h0) * hd;
   for (int i = tid; i < gsz * hd; i += ATG_THREADS) {
     const float v = qg[i];

@@ -120,11 +120,11 @@ static int read_value(rd* r, gg_kv* kv) {
     if (st) return st;
     kv->type = ty;
     switch (ty) {
-        case GV_U8: case GV_I8: { uint8_t v; st = rd_u8(r, &v); kv->u = v; return st; }
-        case GV_U16: case GV_I16: { uint16_t v; st = rd_u16(r, &v); kv->u = v; return st; }
-        case GV_U32: case GV_I32: { uint32_t v; st = rd_u32(r, &v); kv->u = v; return st; }
+        case GV_U8: case GV_I8: { uint8_t v = 0; st = rd_u8(r, &v); kv->u = v; return st; }
+        case GV_U16: case GV_I16: { uint16_t v = 0; st = rd_u16(r, &v); kv->u = v; return st; }
+        case GV_U32: case GV_I32: { uint32_t v = 0; st = rd_u32(r, &v); kv->u = v; return st; }
         case GV_F32: {
-            uint32_t v;
+            uint32_t v = 0;
             st = rd_u32(r, &v);
             float f;
             memcpy(&f, &v, 4);
@@ -133,7 +133,7 @@ static int read_value(rd* r, gg_kv* kv) {
             return st;
         }
         case GV_BOOL: {
-            uint8_t v;
+            uint8_t v = 0;
             st = rd_u8(r, &v);
             if (st) return st;
             if (v > 1) return GG_INVALID_BOOL;

@@ -738,8 +738,8 @@ static int config_from_gguf(const gg_file* g, ref_config* c) {
     else return REF_ERR_UNSUPPORTED_ARCH;
     char key[128];
 #define KEY(s) (snprintf(key, sizeof key, "%s.%s", prefix, s), key)
-    uint32_t v;
-    int st, present, gs;
+    uint32_t v = 0;
+    int st, present = 0, gs;
     if ((gs = gg_u32(g, KEY("attention.head_count"), &v))) return map_gguf_error(gs);
     c->n_head = v;
     if ((st = opt_u32(g, KEY("attention.head_count_kv"), &v, &present))) return st;
@@ -851,7 +851,7 @@ int ref_model_load_gguf(const gg_file* g, const uint8_t* bytes, ref_model** out)
     int st = config_from_gguf(g, &m->cfg);
     if (st) { free(m); return st; }
     ref_config* c = &m->cfg;
-    size_t V;
+    size_t V = 0;
     if ((st = vocab_size(g, &V))) { free(m); return st; }
     m->layers = (ref_layer*)calloc(c->block_count, sizeof(ref_layer));
     if (!m->layers) { free(m); return REF_ERR_ALLOC; }
