@@ -674,10 +674,13 @@ def run_decode_profile(args):
 
 
 def run_chunk_profile(args):
-    """One configuration's chunked forwards for a profiler: positions 0..1023
-    in chunks of `--chunk` as warm-up, the same positions again timed (device
-    time printed), then the last chunk once more between cudaProfilerStart
-    and cudaProfilerStop."""
+    """One configuration's chunked forwards for a profiler: positions
+    0..ctx-1 (`--ctx`, default 1024) in chunks of `--chunk` as warm-up, the
+    same positions again timed (device time printed), then between
+    cudaProfilerStart and cudaProfilerStop the last chunk once more or, when
+    ctx > 1024, the first and the last chunk (attention time grows linearly
+    with the chunk's position, so the two together weigh the kernels as a
+    whole window does)."""
     import torch
 
     import detllm_b200 as D
@@ -687,23 +690,26 @@ def run_chunk_profile(args):
         D.set_q8_tensor_cores(True)
     spec, gguf = model_bytes(args.chunk_profile)
     m = D.Model(gguf)
-    c = min(args.chunk, 1024)
-    toks = S.zipf_tokens(1024, spec.vocab, seed=3)
-    with m.session(n_ctx=1024, max_chunk=c) as s:
-        for p in range(0, 1024, c):
+    ctx = max(args.ctx, 16)
+    c = min(args.chunk, 1024, ctx)
+    toks = S.zipf_tokens(ctx, spec.vocab, seed=3)
+    starts = list(range(0, ctx, c))
+    with m.session(n_ctx=ctx, max_chunk=c) as s:
+        for p in starts:
             s.forward(toks[p:p + c], p)
         s.stats(reset=True)
-        for p in range(0, 1024, c):
+        for p in starts:
             s.forward(toks[p:p + c], p)
         st = s.stats(reset=True)
         torch.cuda.profiler.start()
-        s.forward(toks[1024 - c:], 1024 - c)
+        for p in ([0] if ctx > 1024 else []) + [starts[-1]]:
+            s.forward(toks[p:p + c], p)
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
     m.close()
-    print(json.dumps({"chunk_profile": args.chunk_profile, "layers": spec.n_layer, "chunk": c,
+    print(json.dumps({"chunk_profile": args.chunk_profile, "layers": spec.n_layer, "chunk": c, "ctx": ctx,
                       "q8_tensor_cores": bool(args.q8_tensor_cores),
-                      "tokens_per_s": 1024 / (st.forward_ms / 1000.0)}), flush=True)
+                      "tokens_per_s": ctx / (st.forward_ms / 1000.0)}), flush=True)
 
 
 def main():
@@ -726,6 +732,9 @@ def main():
     ap.add_argument("--chunk-profile", default=None, metavar="CONFIG",
                     help="only chunked forwards of CONFIG, for a profiler (see run_chunk_profile)")
     ap.add_argument("--chunk", type=int, default=1024)
+    ap.add_argument("--ctx", type=int, default=1024,
+                    help="with --chunk-profile: positions forwarded (the window); above 1,024 the first and last "
+                         "chunks are profiled")
     ap.add_argument("--q8-tensor-cores", action="store_true",
                     help="with --chunk-profile: the tcgen05 Q8_0 / Q4_0 chunk GEMM instead of the mma.sync one")
     args = ap.parse_args()
