@@ -83,6 +83,7 @@ def lib():
             "ref_decompress": (I, [P, SZ, P, SZ, C.POINTER(P), C.POINTER(SZ)]),
             "ref_encode_symbols": (I, [P, P, SZ, U32, U32, I, C.POINTER(P), C.POINTER(SZ)]),
             "ref_symbol_ranges_stream": (I, [P, P, SZ, U32, U32, I, P]),
+            "ref_next_window_start": (SZ, [SZ, SZ, SZ, SZ]),
             "ref_quantize_q8a_flat": (I, [P, SZ, P, P]),
             "ref_quantize_q8k_flat": (I, [P, SZ, P, P, P]),
             "ref_free": (None, [P]),
@@ -111,6 +112,11 @@ class OracleError(RuntimeError):
 def _check(code: int, what: str):
     if code != 0:
         raise OracleError(code, what)
+
+
+def next_window_start(pos: int, start: int, n_ctx: int, overlap: int) -> int:
+    """det-cli next_window_start (main.rs:772-778)."""
+    return int(lib().ref_next_window_start(pos, start, n_ctx, overlap))
 
 
 def set_threads(n: int) -> None:

@@ -187,6 +187,9 @@ int ref_decompress(const uint8_t* model_bytes, size_t model_len, const uint8_t* 
  * return the range-coder payload (no header). */
 int ref_encode_symbols(const ref_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx,
                        uint32_t overlap, int byte_escapes, uint8_t** out, size_t* out_len);
+/* det-cli next_window_start (main.rs:772-778): the window's first token
+ * index after the token at `pos` is appended to a window starting at `ws`. */
+size_t ref_next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t overlap);
 /* Per-symbol ranges of that stream (what the device boundary returns). */
 int ref_symbol_ranges_stream(const ref_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx,
                              uint32_t overlap, int byte_escapes, ref_symbol_range* out);

@@ -30,6 +30,11 @@ static size_t next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t over
     return ws;
 }
 
+/* exported for the rollover known-answer test (det-cli main.rs:1289-1304) */
+size_t ref_next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t overlap) {
+    return next_window_start(pos, ws, n_ctx, overlap);
+}
+
 static int ws_init(wstate* w, const ref_model* m, size_t n_ctx, int escapes) {
     memset(w, 0, sizeof *w);
     int st = ref_state_init(&w->st, m, n_ctx);

@@ -285,6 +285,20 @@ def test_decompress_rejections(D, oracle, fixtures):
     assert e.value.code == 48
 
 
+def test_encode_rejects_invalid_windows(D, oracle, fixtures):
+    # det-cli main.rs:1264-1287: n_ctx 0, overlap == n_ctx and n_ctx above
+    # the model's context length fail with the window error, as the oracle does
+    m = D.Model(fixtures["tiny-f32"])
+    om = oracle.Model(fixtures["tiny-f32"])
+    assert m.encode_symbols([0, 1], 3, 1) == om.encode_symbols([0, 1], 3, 1)
+    for n_ctx, overlap in [(0, 0), (3, 3), (m.config.context_length + 1, 0)]:
+        with pytest.raises(D.DetError) as e:
+            m.encode_symbols([0, 1], n_ctx, overlap)
+        assert e.value.code == 57, (n_ctx, overlap)
+    assert m.encode_symbols([0, 1], 3, 1) == om.encode_symbols([0, 1], 3, 1)  # the model is still usable
+    m.close()
+
+
 def test_nonfinite_is_an_error_like_the_reference(D, oracle):
     # DET-4: an overflowing activation is rejected, not propagated
     spec = S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=2, vocab=300, ctx=16, t_embd=S.GT_F32,

@@ -199,6 +199,30 @@ def test_codec_round_trips(oracle, fixtures, name):
         assert oracle.decompress(fixtures[name], d) == data
 
 
+def test_window_rolls_over_when_context_reaches_n_ctx(oracle):
+    # det-cli main.rs:1289-1304: n_ctx 8, overlap 2
+    start, seen = 0, []
+    for pos in range(18):
+        start = oracle.next_window_start(pos, start, 8, 2)
+        seen.append((pos, start, pos - start))
+    assert seen[7] == (7, 0, 7)
+    assert seen[8] == (8, 6, 2)
+    assert seen[13] == (13, 6, 7)
+    assert seen[14] == (14, 12, 2)
+
+
+def test_codec_rejects_invalid_windows(oracle, fixtures):
+    # det-cli main.rs:1264-1287: n_ctx 0, overlap == n_ctx, n_ctx above the
+    # model's context length all fail with the window error (status 57)
+    m = oracle.Model(fixtures["tiny-f32"])
+    assert m.encode_symbols([0, 1], 3, 1)
+    for n_ctx, overlap in [(0, 0), (3, 3), (m.info.context_length + 1, 0)]:
+        with pytest.raises(oracle.OracleError) as e:
+            m.encode_symbols([0, 1], n_ctx, overlap)
+        assert e.value.code == 57, (n_ctx, overlap)
+    m.close()
+
+
 def test_codec_rejects_noncanonical_and_bad_header(oracle, fixtures):
     # testdata_cli.rs:312-371, file.rs:45-56
     m = fixtures["tiny-f32"]
