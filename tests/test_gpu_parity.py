@@ -182,6 +182,28 @@ def test_fixture_logits_hash(D, goldens, fixtures, name, chunk):
     assert h.hex() == goldens[name.replace("-", "_") + "_logits_sha256"]
 
 
+@pytest.mark.parametrize("name", ["tiny-f32", "tiny-qmix", "q4k_q6k"])
+def test_position_invariance_under_replay(D, goldens, fixtures, models, name):
+    # det-model lib.rs:3681-3724, 3761-3796: the logits of position p from
+    # continuous one-position forwards equal those of a fresh cache that
+    # replays positions 0..p, bit for bit; here the replay also runs as one
+    # teacher-forced chunk, whose last row must be the same logits
+    g = fixtures[name] if name in fixtures else models[name]
+    toks = goldens["tokens"] if name in fixtures else [int(t) for t in S.zipf_tokens(12, SPECS[name].vocab, seed=2)]
+    m = D.Model(g)
+    with m.session(n_ctx=len(toks), max_chunk=len(toks)) as s:
+        cont = [bits(s.forward([t], p, want_logits=True)[0]) for p, t in enumerate(toks)]
+        for end in range(len(toks)):
+            s.reset()
+            for p in range(end + 1):
+                lg = s.forward([toks[p]], p, want_logits=True)[0]
+            assert (bits(lg) == cont[end]).all(), f"one-position replay differs at {end}"
+            s.reset()
+            lg = s.forward(toks[:end + 1], 0, want_logits=True)[-1]
+            assert (bits(lg) == cont[end]).all(), f"chunked replay differs at {end}"
+    m.close()
+
+
 @pytest.mark.parametrize("name", list(SPECS))
 @pytest.mark.parametrize("chunk", [1, 7, 12, 24])  # decode, decode (T <= 8), small-T and chunk GEMM paths
 def test_logits_bit_exact(D, oracle, models, name, chunk):
