@@ -165,7 +165,7 @@ def markov_stream(n: int, seed: int = 16) -> bytes:
 
 # ---- GGUF metadata (tokenizer vocabularies) ---------------------------------
 # GGUF v3 value types (det-gguf lib.rs:58-96)
-GV_U32, GV_I32, GV_F32, GV_STRING, GV_ARRAY = 4, 5, 6, 8, 9
+GV_U32, GV_I32, GV_F32, GV_BOOL, GV_STRING, GV_ARRAY, GV_F64 = 4, 5, 6, 7, 8, 9, 12
 
 
 def _gguf_str(s) -> bytes:
@@ -184,6 +184,10 @@ def _gguf_value(ty: int, v) -> bytes:
         return struct.pack("<i", v)
     if ty == GV_F32:
         return struct.pack("<f", v)
+    if ty == GV_BOOL:
+        return struct.pack("<B", int(v))
+    if ty == GV_F64:
+        return struct.pack("<d", v)
     elem, items = v
     body = b"".join(_gguf_value(elem, x) for x in items)
     return struct.pack("<IQ", elem, len(items)) + body
@@ -334,7 +338,15 @@ def with_tokenizer(gguf: bytes, kvs) -> bytes:
     """`gguf` (v3) with its tokenizer.ggml.* metadata replaced by `kvs`;
     tensor infos and data are kept (tensor offsets are relative to the
     data section, which stays aligned to 32 bytes)."""
+    return with_metadata(gguf, kvs, drop=lambda key: key.startswith("tokenizer.ggml."))
+
+
+def with_metadata(gguf: bytes, kvs, drop=None) -> bytes:
+    """`gguf` (v3) with the (key, type, value) entries of `kvs` set (an
+    existing entry of the same key is replaced) and the keys for which
+    `drop(key)` is true removed; tensor infos and data are kept."""
     assert gguf[:4] == b"GGUF"
+    new_keys = {k for k, _, _ in kvs}
     n_t = int.from_bytes(gguf[8:16], "little")
     n_kv = int.from_bytes(gguf[16:24], "little")
     o, keep = 24, []
@@ -344,7 +356,7 @@ def with_tokenizer(gguf: bytes, kvs) -> bytes:
         key = gguf[o + 8:o + 8 + klen].decode()
         ty = int.from_bytes(gguf[o + 8 + klen:o + 12 + klen], "little")
         o = _skip_value(gguf, o + 12 + klen, ty)
-        if not key.startswith("tokenizer.ggml."):
+        if key not in new_keys and not (drop and drop(key)):
             keep.append(gguf[start:o])
         if key == "general.alignment":
             raise ValueError("custom alignment is not handled")
