@@ -15,7 +15,8 @@ import pytest
 
 from detllm_b200 import synth as S
 
-SHAPE, HEAD_LENGTH, FEATURE, ROPE_SCALING = 1, 4, 5, 6  # ModelError order (det-model :48-59)
+# ModelError order (det-model :48-59)
+SHAPE, ARCH, HEAD_LENGTH, FEATURE, ROPE_SCALING, MISSING, GGUF = 1, 3, 4, 5, 6, 7, 8
 
 SPEC = S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=1, vocab=300, ctx=32, seed=71)
 HD = SPEC.d // SPEC.n_head
@@ -52,7 +53,21 @@ CASES = [
     ("rope base 0", [("llama.rope.freq_base", S.GV_F32, 0.0)], SHAPE),
     ("rope base inf", [("llama.rope.freq_base", S.GV_F32, math.inf)], SHAPE),
     ("rope dims 3", [("llama.rope.dimension_count", S.GV_U32, 3)], SHAPE),
+    # metadata of the wrong kind: map_metadata_error and vocab_size (:1668-1692, :2158-2163, :3087-3116)
+    ("architecture", [("general.architecture", S.GV_STRING, "gpt2")], ARCH),
+    ("head_count as a string", [("llama.attention.head_count", S.GV_STRING, "2")], GGUF),
+    ("vocab_size as a string", [("llama.vocab_size", S.GV_STRING, "3")], GGUF),
 ] + [(k.split(".")[-1], [(k, S.GV_F32, 1.0)], FEATURE) for k in F32_FEATURE_KEYS]
+
+# (name, entries set, keys removed, expected status)
+DROPPED = [
+    ("no head_count", [], {"llama.attention.head_count"}, MISSING),
+    ("no block_count", [], {"llama.block_count"}, MISSING),
+    # without a vocab_size key the vocabulary comes from the token list,
+    # which must be strings (vocab_size, :1679-1684)
+    ("tokens as integers", [("tokenizer.ggml.tokens", S.GV_ARRAY, (S.GV_U32, [0, 1, 2]))],
+     {"llama.vocab_size"}, GGUF),
+]
 
 
 @pytest.fixture(scope="module")
@@ -63,6 +78,8 @@ def base():
 def variants(base):
     for name, kvs, want in CASES:
         yield name, S.with_metadata(base, kvs), want
+    for name, kvs, keys, want in DROPPED:
+        yield name, S.with_metadata(base, kvs, drop=lambda k, keys=keys: k in keys), want
 
 
 def test_oracle_refuses_metadata_like_the_reference(oracle, base):
@@ -73,6 +90,18 @@ def test_oracle_refuses_metadata_like_the_reference(oracle, base):
         with pytest.raises(oracle.OracleError) as e:
             oracle.Model(g)
         assert e.value.code == want, name
+
+
+def test_oracle_refuses_token_ids_outside_the_vocabulary(oracle, base):
+    # det-model :3153-3175
+    m = oracle.Model(base)
+    with pytest.raises(oracle.OracleError) as e:
+        m.logits_hash([SPEC.vocab], 1)
+    assert e.value.code == SHAPE
+    with pytest.raises(oracle.OracleError) as e:
+        m.logits_hash([0, SPEC.vocab], 1)
+    assert e.value.code == SHAPE
+    m.close()
 
 
 @pytest.mark.gpu
@@ -90,3 +119,11 @@ def test_library_refuses_metadata_like_the_reference(oracle, base):
         with pytest.raises(D.DetError) as e:
             D.Model(g)
         assert e.value.code == want, name
+    # token ids outside the vocabulary (det-model :3153-3175), then the model still works
+    m = D.Model(base)
+    for bad in ([SPEC.vocab], [0, SPEC.vocab]):
+        with pytest.raises(D.DetError) as e:
+            m.logits_hash_for_tokens(bad)
+        assert e.value.code == SHAPE, bad
+    assert m.logits_hash_for_tokens(toks) == oracle.Model(base).logits_hash(toks, 1)
+    m.close()
