@@ -84,6 +84,7 @@ def lib():
             "ref_encode_symbols": (I, [P, P, SZ, U32, U32, I, C.POINTER(P), C.POINTER(SZ)]),
             "ref_symbol_ranges_stream": (I, [P, P, SZ, U32, U32, I, P]),
             "ref_next_window_start": (SZ, [SZ, SZ, SZ, SZ]),
+            "ref_gguf_parse_status": (I, [C.c_char_p, SZ]),
             "ref_quantize_q8a_flat": (I, [P, SZ, P, P]),
             "ref_quantize_q8k_flat": (I, [P, SZ, P, P, P]),
             "ref_free": (None, [P]),
@@ -112,6 +113,18 @@ class OracleError(RuntimeError):
 def _check(code: int, what: str):
     if code != 0:
         raise OracleError(code, what)
+
+
+GGUF_ERRORS = ["ok", "bad magic", "unsupported version", "truncated", "unsupported value type", "invalid utf-8",
+               "invalid tensor offset", "invalid tensor shape", "tensor not found", "metadata not found",
+               "duplicate metadata key", "duplicate tensor name", "invalid bool", "metadata type mismatch",
+               "unsupported tensor type", "alloc"]
+
+
+def gguf_parse_error(data: bytes) -> str:
+    """The det-gguf parse result of a whole file: "ok" or the GgufError
+    (restated in oracle/ref_gguf.c)."""
+    return GGUF_ERRORS[lib().ref_gguf_parse_status(data, len(data))]
 
 
 def next_window_start(pos: int, start: int, n_ctx: int, overlap: int) -> int:

@@ -372,3 +372,12 @@ int gg_tensor_data(const gg_file* f, const uint8_t* bytes, const char* name, con
     *len = (size_t)el;
     return GG_OK;
 }
+
+/* gg_parse's status for a whole file (exported for the parser tests that
+ * restate det-gguf lib.rs:586-730) */
+int ref_gguf_parse_status(const uint8_t* bytes, size_t len) {
+    gg_file f;
+    int st = gg_parse(bytes, len, &f);
+    if (!st) gg_free(&f);
+    return st;
+}

@@ -59,6 +59,7 @@ typedef struct {
 } gg_file;
 
 int gg_parse(const uint8_t* bytes, size_t len, gg_file* out);
+int ref_gguf_parse_status(const uint8_t* bytes, size_t len);
 void gg_free(gg_file* f);
 const gg_kv* gg_find(const gg_file* f, const char* key);
 int gg_u32(const gg_file* f, const char* key, uint32_t* out);
