@@ -2,8 +2,9 @@
 
 crates/det-gguf/src/lib.rs:586-845 builds small GGUF byte strings and
 checks which `GgufError` each one raises.  The same byte strings go through
-the oracle's reader (oracle/ref_gguf.c), which the library's loader
-restates in C++ (detllm_b200/csrc/model.cpp).
+the oracle's reader (oracle/ref_gguf.c) on the CPU and, on a GPU, through
+the library's loader (det_model_load, detllm_b200/csrc/model.cpp), which
+reports every parse error as the reference's ModelError::Gguf.
 """
 import struct
 
@@ -100,3 +101,32 @@ def test_parses_all_supported_metadata_array_types(parse):
 def test_rejects_unsupported_version_and_value_type(parse):
     assert parse(pad(b"GGUF" + struct.pack("<IQQ", 4, 0, 0))) == "unsupported version"
     assert parse(pad(header(0, 1) + string("x") + struct.pack("<I", 13))) == "unsupported value type"
+
+
+@pytest.mark.gpu
+def test_library_loader_refuses_the_same_files():
+    """det_model_load on each malformed file returns DET_ERR_GGUF (8), as
+    F32Llama::from_gguf maps every GgufError (det-model :2158-2163); a
+    well-formed file without metadata lacks general.architecture (7)."""
+    import detllm_b200 as D
+
+    assert D.device_count() > 0, "gpu tests need a CUDA device"
+    bad = [
+        b"nope",
+        header(0, 0),
+        header(1, 1) + u32_kv("answer", 42) + tensor_info("weight"),
+        b"GGUF" + struct.pack("<IQQ", 3, 2**64 - 1, 0),
+        header(0, 2) + u32_kv("dup", 1) + u32_kv("dup", 2),
+        header(2, 0) + tensor_info("dup") + tensor_info("dup"),
+        pad(header(2, 0) + tensor_info("a", 0) + tensor_info("b", 2)) + b"\0" * 6,
+        pad(header(1, 0) + tensor_info("a", 4)) + b"\0" * 4,
+        header(0, 1) + string("flag") + struct.pack("<IB", 7, 2),
+        pad(b"GGUF" + struct.pack("<IQQ", 4, 0, 0)),
+    ]
+    for i, b in enumerate(bad):
+        with pytest.raises(D.DetError) as e:
+            D.Model(b)
+        assert e.value.code == 8, i
+    with pytest.raises(D.DetError) as e:
+        D.Model(pad(header(0, 0)))
+    assert e.value.code == 7
