@@ -240,6 +240,49 @@ def test_codec_rejects_noncanonical_and_bad_header(oracle, fixtures):
     assert e.value.code == 58
 
 
+def test_dtlz_header_rejections(oracle, fixtures):
+    # det-coder file.rs:111-207 through decompress: each header field is
+    # checked before the model hash and the payload
+    m = fixtures["tiny-f32"]
+    d = oracle.compress(m, b"detllm header", 8)
+
+    def patched(off, fmt, value):
+        b = bytearray(d)
+        struct.pack_into(fmt, b, off, value)
+        return bytes(b)
+
+    cases = [
+        (b"", 48), (d[:55], 48),                      # TooShort
+        (b"NOPE" + d[4:], 49),                        # BadMagic
+        (patched(4, "<H", 2), 50),                    # UnsupportedVersion(VERSION + 1)
+        (patched(6, "<H", 1 << 1), 51),               # UnsupportedFlags(FLAG_BYTE_ESCAPES << 1)
+        (patched(40, "<I", 0), 52),                   # InvalidContext: n_ctx 0
+        (patched(44, "<I", 8), 53),                   # InvalidOverlap: overlap == n_ctx
+    ]
+    for data, want in cases:
+        with pytest.raises(oracle.OracleError) as e:
+            oracle.decompress(m, data)
+        assert e.value.code == want, (data[:8], want)
+    assert oracle.decompress(m, d) == b"detllm header"
+
+
+def test_range_encoder_rejects_invalid_frequency_ranges(oracle):
+    # det-coder range.rs:270-282: cum + freq beyond total (without
+    # overflowing), a zero frequency, and a total above 2^31 - 1
+    import ctypes as C
+
+    out = np.zeros(64, np.uint8)
+    n = C.c_size_t()
+    for cum, freq, total in [(2**64 - 1, 1, 8), (0, 0, 8), (8, 1, 8), (0, 1, 1 << 31)]:
+        cs, fs, ts = (np.array([v], np.uint64) for v in (cum, freq, total))
+        st = oracle.lib().ref_range_encode(cs.ctypes.data, fs.ctypes.data, ts.ctypes.data, 1, out.ctypes.data,
+                                           out.size, C.byref(n))
+        assert st == 40, (cum, freq, total)
+    cs, fs, ts = (np.array([v], np.uint64) for v in (7, 1, 8))
+    assert oracle.lib().ref_range_encode(cs.ctypes.data, fs.ctypes.data, ts.ctypes.data, 1, out.ctypes.data,
+                                         out.size, C.byref(n)) == 0
+
+
 def test_range_coder_million_symbols(oracle):
     # det-coder range.rs:327-357 (LCG stream) -- encode through the oracle,
     # decode with a Python restatement of RangeDecoder
