@@ -85,6 +85,9 @@ def lib():
             "ref_symbol_ranges_stream": (I, [P, P, SZ, U32, U32, I, P]),
             "ref_next_window_start": (SZ, [SZ, SZ, SZ, SZ]),
             "ref_gguf_parse_status": (I, [C.c_char_p, SZ]),
+            "ref_rope_rotate": (I, [P, SZ, SZ, SZ, I, P, P]),
+            "ref_softmax": (I, [P, SZ]),
+            "ref_rmsnorm": (I, [P, P, SZ, F, P]),
             "ref_quantize_q8a_flat": (I, [P, SZ, P, P]),
             "ref_quantize_q8k_flat": (I, [P, SZ, P, P, P]),
             "ref_free": (None, [P]),
@@ -113,6 +116,32 @@ class OracleError(RuntimeError):
 def _check(code: int, what: str):
     if code != 0:
         raise OracleError(code, what)
+
+
+def rmsnorm(x, w, eps: float) -> np.ndarray:
+    """det-model rmsnorm (lib.rs:2053-2073)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    _check(lib().ref_rmsnorm(_ptr(x), _ptr(w), x.size, eps, _ptr(out)), "rmsnorm")
+    return out
+
+
+def softmax(x) -> np.ndarray:
+    """det-model softmax_in_place (lib.rs:2361-2388)."""
+    x = np.array(x, np.float32)
+    _check(lib().ref_softmax(_ptr(x), x.size), "softmax")
+    return x
+
+
+def rope_rotate(x, heads: int, head_dim: int, cos_row, sin_row, split_half: bool) -> np.ndarray:
+    """det-model apply_rope (lib.rs:2011-2051) for one position, with the
+    given table row (len(cos_row) rotation pairs per head)."""
+    x = np.array(x, np.float32)
+    c = np.ascontiguousarray(cos_row, np.float32)
+    s = np.ascontiguousarray(sin_row, np.float32)
+    _check(lib().ref_rope_rotate(_ptr(x), heads, head_dim, c.size, int(split_half), _ptr(c), _ptr(s)), "rope")
+    return x
 
 
 GGUF_ERRORS = ["ok", "bad magic", "unsupported version", "truncated", "unsupported value type", "invalid utf-8",

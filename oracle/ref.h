@@ -187,6 +187,14 @@ int ref_decompress(const uint8_t* model_bytes, size_t model_len, const uint8_t* 
  * return the range-coder payload (no header). */
 int ref_encode_symbols(const ref_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx,
                        uint32_t overlap, int byte_escapes, uint8_t** out, size_t* out_len);
+/* RoPE rotation of one position's `heads` x hd values with a table row of
+ * `half` cos / sin entries (pairing 0 adjacent, 1 split-half), and
+ * softmax_in_place; exported for the det-model op-order tests. */
+int ref_rope_rotate(float* x, size_t heads, size_t hd, size_t half, int pairing, const float* cs_row,
+                    const float* sn_row);
+int ref_softmax(float* x, size_t n);
+/* rmsnorm (det-model :2053-2073) */
+int ref_rmsnorm(const float* x, const float* w, size_t n, float eps, float* out);
 /* det-cli next_window_start (main.rs:772-778): the window's first token
  * index after the token at `pos` is appended to a window starting at `ws`. */
 size_t ref_next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t overlap);

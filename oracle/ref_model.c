@@ -324,16 +324,18 @@ static int add_into(float* x, const float* b, size_t n) {
     return REF_OK;
 }
 
-/* apply_rope (:2011-2051) */
-static int apply_rope(float* x, size_t heads, size_t hd, const ref_state* s, size_t pos) {
-    const ref_config* c = &s->m->cfg;
-    size_t half = c->rope_dim / 2;
+/* apply_rope (:2011-2051): the `half` rotation pairs of each of `heads`
+ * heads of hd values (adjacent (2j, 2j+1) for pairing 0, split-half
+ * (j, j+half) for pairing 1) with one position's table row; values past
+ * the rotary pairs are left as they are */
+static int rope_rotate(float* x, size_t heads, size_t hd, size_t half, int pairing, const float* cs_row,
+                       const float* sn_row) {
     if (!finite_slice(x, heads * hd)) return REF_ERR_NONFINITE;
     for (size_t h = 0; h < heads; h++) {
         size_t base = h * hd;
         for (size_t j = 0; j < half; j++) {
             size_t a, b;
-            if (c->pairing == 0) {
+            if (pairing == 0) {
                 a = base + 2 * j;
                 b = a + 1;
             } else {
@@ -341,13 +343,26 @@ static int apply_rope(float* x, size_t heads, size_t hd, const ref_state* s, siz
                 b = base + j + half;
             }
             float x0 = x[a], x1 = x[b];
-            float cs = s->rope_cos[pos * half + j], sn = s->rope_sin[pos * half + j];
+            float cs = cs_row[j], sn = sn_row[j];
             x[a] = x0 * cs - x1 * sn;
             x[b] = x0 * sn + x1 * cs;
             if (!isfinite_f(x[a]) || !isfinite_f(x[b])) return REF_ERR_NONFINITE;
         }
     }
     return REF_OK;
+}
+
+static int apply_rope(float* x, size_t heads, size_t hd, const ref_state* s, size_t pos) {
+    const ref_config* c = &s->m->cfg;
+    size_t half = c->rope_dim / 2;
+    return rope_rotate(x, heads, hd, half, c->pairing, s->rope_cos + pos * half, s->rope_sin + pos * half);
+}
+
+/* exported for the op-order known answers (det-model :2752-2821) */
+int ref_rope_rotate(float* x, size_t heads, size_t hd, size_t half, int pairing, const float* cs_row,
+                    const float* sn_row) {
+    if (hd == 0 || 2 * half > hd) return REF_ERR_SHAPE;
+    return rope_rotate(x, heads, hd, half, pairing, cs_row, sn_row);
 }
 
 static inline float max_f(float a, float b) { return a > b ? a : (b != b ? a : b); }
@@ -372,6 +387,9 @@ static int softmax(float* x, size_t n) {
     }
     return REF_OK;
 }
+
+/* exported for the op-order known answers (det-model :2462-2469) */
+int ref_softmax(float* x, size_t n) { return softmax(x, n); }
 
 /* attention_one_head (:2300-2333) with scores (:2335-2359) and weighted
  * value (:2390-2418) */

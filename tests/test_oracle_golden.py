@@ -19,6 +19,10 @@ def bits(x):
     return struct.unpack("<I", struct.pack("<f", np.float32(x)))[0]
 
 
+def abits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
 def test_num_canary(oracle, goldens):
     # crates/det-num/src/canary.rs:3-6
     assert oracle.canary_hash().hex() == goldens["num_canary_sha256"]
@@ -108,6 +112,47 @@ def test_dot_lane_order(oracle):
                       np.float32(np.float32(acc[4] + acc[5]) + np.float32(acc[6] + acc[7])))
     got = oracle.lib().ref_dot_f32(x.ctypes.data, y.ctypes.data, 17)
     assert bits(got) == bits(want)
+
+
+def test_rmsnorm_runs_in_specified_order(oracle):
+    # det-model lib.rs:2443-2459: ss by the 8-lane sum of squares, then
+    # r = 1 / sqrt(ss / n + eps), out = (x * r) * w, each op rounded to f32
+    f = np.float32
+    x = np.array([1.0, -2.0, 3.0, -4.0], f)
+    w = np.array([0.5, 1.0, 1.5, 2.0], f)
+    out = oracle.rmsnorm(x, w, 1e-5)
+    sq = x * x
+    ss = f(f(sq[0] + sq[1]) + f(sq[2] + sq[3]))  # lanes 4..7 are zero
+    r = f(1.0) / np.sqrt(f(f(ss / f(4.0)) + f(1e-5)))
+    assert (abits(out) == abits((x * r).astype(f) * w)).all()
+
+
+def test_softmax_uses_det_exp_and_8lane_sum(oracle):
+    # det-model lib.rs:2462-2469
+    x = oracle.softmax([1.0, 0.0, -2.0, 3.0, -88.0, 3.0, -1.0, 2.0, 0.5])
+    z = np.float32(0.0)
+    lanes = [np.float32(0.0)] * 8
+    for i, v in enumerate(x):
+        lanes[i % 8] = np.float32(lanes[i % 8] + v)
+    z = np.float32(np.float32(np.float32(lanes[0] + lanes[1]) + np.float32(lanes[2] + lanes[3])) +
+                   np.float32(np.float32(lanes[4] + lanes[5]) + np.float32(lanes[6] + lanes[7])))
+    assert abs(float(z) - 1.0) < 1e-6
+    assert bits(x[3]) == bits(x[5])
+
+
+def test_rope_pairs_in_specified_order(oracle):
+    # det-model lib.rs:2752-2821: position 1 of a 2-position table with
+    # cos (0, 0.5) and sin (1, -0.25)
+    c, s = [0.0, 0.5], [1.0, -0.25]
+    adj = oracle.rope_rotate([1, 2, 3, 4, 5, 6, 7, 8], 2, 4, c, s, split_half=False)
+    assert (abits(adj) == abits(np.array([-2.0, 1.0, 2.5, 1.25, -6.0, 5.0, 5.5, 2.25], np.float32))).all()
+    split = oracle.rope_rotate([1, 2, 3, 4], 1, 4, c, s, split_half=True)
+    assert (abits(split) == abits(np.array([-3.0, 2.0, 1.0, 1.5], np.float32))).all()
+    # a head longer than the rotary pairs keeps its tail
+    tail = oracle.rope_rotate([1, 2, 3, 4, 9, -9], 1, 6, c, s, split_half=False)
+    assert (abits(tail) == abits(np.array([-2.0, 1.0, 2.5, 1.25, 9.0, -9.0], np.float32))).all()
+    tail = oracle.rope_rotate([1, 2, 3, 4, 9, -9], 1, 6, c, s, split_half=True)
+    assert (abits(tail) == abits(np.array([-3.0, 2.0, 1.0, 1.5, 9.0, -9.0], np.float32))).all()
 
 
 def test_q8a_quantize_kat(oracle):
