@@ -57,7 +57,7 @@ DI float2 mul2(float a0, float a1, float b0, float b1) {
 // multiply is contracted into a fused multiply-add by the code generator
 DI float2 add_by_fma2(float2 p, float one, float2 acc) {
   unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(p.x, p.y)), "l"(pk2(one, one)), "l"(pk2(acc.x, acc.y)));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(p.x, p.y)), "l"(pk2(one, one)), "l"(pk2(acc.x, acc.y)));  // exact: p * 1
   float2 o;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
   return o;

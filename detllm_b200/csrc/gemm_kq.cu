@@ -340,8 +340,8 @@ DI float4 q4k_prod4(uint32_t nib, unsigned long long dsc2, unsigned long long nd
   const float m1 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7541));
   const float m2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7542));
   const float m3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7543));
-  const unsigned long long w01 = fma2(dsc2, add2(pk2(m0, m1), nmag2), ndmn2);
-  const unsigned long long w23 = fma2(dsc2, add2(pk2(m2, m3), nmag2), ndmn2);
+  const unsigned long long w01 = fma2(dsc2, add2(pk2(m0, m1), nmag2), ndmn2);  // exact product, one rounding
+  const unsigned long long w23 = fma2(dsc2, add2(pk2(m2, m3), nmag2), ndmn2);  // exact product, one rounding
   const float2 r01 = up2(mul2(w01, pk2(a.x, a.y)));
   const float2 r23 = up2(mul2(w23, pk2(a.z, a.w)));
   return make_float4(r01.x, r01.y, r23.x, r23.y);
