@@ -366,6 +366,7 @@ det_status det_set_encode_chunk(uint32_t chunk, uint32_t* previous) {
 det_status det_encode_symbols(det_model* m, const uint32_t* symbols, size_t n, uint32_t n_ctx, uint32_t overlap,
                               int byte_escapes, uint8_t** out, size_t* out_len) {
   if (!m || (!symbols && n) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(m->mu);  // the model's cached session
   std::vector<uint8_t> payload;
   if (det_status st = encode_impl(m, symbols, n, n_ctx, overlap, byte_escapes, &payload)) return st;
   return copy_out(payload, out, out_len);
@@ -375,6 +376,7 @@ det_status det_encode_symbols(det_model* m, const uint32_t* symbols, size_t n, u
 det_status det_compress(det_model* m, const uint8_t* input, size_t len, uint32_t n_ctx, uint8_t** out,
                         size_t* out_len) {
   if (!m || (!input && len) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(m->mu);  // the model's cached session
   if (det_status st = codec_model_checks(m)) return st;
   std::vector<uint32_t> sym;  // codec_symbols (det-token lib.rs:150-180)
   sym.reserve(len);
@@ -400,6 +402,7 @@ det_status det_compress(det_model* m, const uint8_t* input, size_t len, uint32_t
 // one), then the canonical re-encode through the chunked encoder.
 det_status det_decompress(det_model* m, const uint8_t* dtlz, size_t len, uint8_t** out, size_t* out_len) {
   if (!m || (!dtlz && len) || !out || !out_len) return DET_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(m->mu);  // the model's cached session and piece table
   // DtlzHeader::decode (file.rs:58-90)
   if (len < 56) return DET_ERR_FILE_TOO_SHORT;
   if (std::memcmp(dtlz, "DTLZ", 4) != 0) return DET_ERR_FILE_BAD_MAGIC;

@@ -3,6 +3,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -200,10 +201,15 @@ struct det_model {
   size_t weight_bytes = 0;  // device bytes of all weight matrices
   det_stats agg{};          // stats of finished sessions
   det::ProfTags prof_agg;   // per-kernel profile of finished sessions
-  // session reused by the model-level entry points (encode / decode /
-  // logits hash) so repeated calls skip allocation, RoPE table and graph
-  // capture; those entry points are not re-entrant on one model
+  // session reused by the model-level codec entry points (compress,
+  // decompress, encode symbols) so repeated calls skip allocation, RoPE
+  // table and graph capture
   det_session* cached = nullptr;
+  // serialises those entry points (they share `cached`) and guards the
+  // statistics aggregates: callers may use one model from several host
+  // threads, as the reference's immutable model allows; their codec calls
+  // then run one after another
+  std::recursive_mutex mu;
   // tensor parallelism: `tp` on the model det_model_load_tp returns (its
   // sessions are tensor-parallel); `shard` on the per-part models that view
   // the replicas' weights (cfg then holds this part's head and FFN counts)

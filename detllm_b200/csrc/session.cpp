@@ -114,8 +114,11 @@ void free_session(det_session* s) {
   if (s->tp) tp_session_release(s);
   cudaSetDevice(s->m->device);
   det_model* owner = s->owner ? s->owner : s->m;
-  add_stats(&owner->agg, s->stats);
-  add_prof(&owner->prof_agg, s->prof);
+  {
+    std::lock_guard<std::recursive_mutex> lk(owner->mu);
+    add_stats(&owner->agg, s->stats);
+    add_prof(&owner->prof_agg, s->prof);
+  }
   for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
   for (void* p : s->allocations) cudaFree(p);
   if (s->graph_dev1.exec) cudaGraphExecDestroy(s->graph_dev1.exec);
@@ -1151,6 +1154,7 @@ det_status det_session_stats(det_session* s, det_stats* out, int reset) {
 
 det_status det_model_stats(det_model* m, det_stats* out, int reset) {
   if (!m || !out) return DET_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(m->mu);
   *out = m->agg;
   if (m->cached) {  // include the live cached session
     add_stats(out, m->cached->stats);
@@ -1162,6 +1166,7 @@ det_status det_model_stats(det_model* m, det_stats* out, int reset) {
 
 det_status det_model_profile(det_model* m, char* out, size_t cap, int reset) {
   if (!m || (!out && cap)) return DET_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::recursive_mutex> lk(m->mu);
   ProfTags p = m->prof_agg;
   if (m->cached) {
     add_prof(&p, m->cached->prof);

@@ -15,7 +15,10 @@
  *
  * Threading: a det_session is used by one host thread at a time.  Sessions on
  * different devices may run concurrently.  A det_model may back several
- * sessions on its device.
+ * sessions on its device and may be shared by host threads: its model-level
+ * codec calls (det_compress, det_decompress, det_encode_symbols) share one
+ * session cached in the model, so concurrent calls on one model run one
+ * after another.  det_model_free must not race with any call on the model.
  */
 #ifndef DETGPU_H
 #define DETGPU_H

@@ -307,6 +307,37 @@ def test_decompress_rejections(D, oracle, fixtures):
     assert e.value.code == 48
 
 
+def test_codec_calls_from_several_host_threads(D, oracle, models):
+    # the reference's model is immutable (&self), so callers may share one
+    # model between threads; the library's codec calls share a session
+    # cached in the model and run one after another, with the bytes of
+    # sequential calls
+    import threading
+
+    g = models["q8_0"]
+    m = D.Model(g)
+    inputs = [S.markov_text(300 + 40 * i, seed=80 + i) for i in range(6)]
+    want = [D.compress(m, x, 48) for x in inputs]
+    got, back, errors = [None] * len(inputs), [None] * len(inputs), []
+
+    def work(i):
+        try:
+            got[i] = D.compress(m, inputs[i], 48)
+            back[i] = D.decompress(m, got[i])
+        except Exception as e:  # reported below
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(len(inputs))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    assert got == want and back == inputs
+    assert want[0] == oracle.compress(g, inputs[0], 48)
+    m.close()
+
+
 def test_encode_rejects_invalid_windows(D, oracle, fixtures):
     # det-cli main.rs:1264-1287: n_ctx 0, overlap == n_ctx and n_ctx above
     # the model's context length fail with the window error, as the oracle does
