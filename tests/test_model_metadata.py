@@ -11,6 +11,7 @@ C ABI) on a GPU, with the same table.
 """
 import math
 
+import numpy as np
 import pytest
 
 from detllm_b200 import synth as S
@@ -90,6 +91,30 @@ def test_oracle_refuses_metadata_like_the_reference(oracle, base):
         with pytest.raises(oracle.OracleError) as e:
             oracle.Model(g)
         assert e.value.code == want, name
+
+
+def test_oracle_config_defaults_and_attention_scale(oracle):
+    # det-model :4377-4430: head_dim = d / heads, attention scale
+    # 1 / sqrt(head_dim) (f32 sqrt, then f32 division) unless
+    # attention.scale is given, RoPE base 10,000 when the key is absent
+    spec = S.ModelSpec(n_layer=1, d=64, d_ff=128, n_head=2, n_head_kv=1, vocab=300, ctx=32, rope_base=5e5, seed=72)
+    g = S.build_gguf(spec)
+    m = oracle.Model(g)
+    assert m.info.head_dim == 32 and m.info.head_count == 2 and m.info.head_count_kv == 1
+    assert m.info.block_count == 1 and m.info.embedding_length == 64 and m.info.feed_forward_length == 128
+    assert m.info.context_length == 32 and m.vocab == 300
+    want = np.float32(1.0) / np.sqrt(np.float32(32.0))
+    assert np.float32(m.info.attention_scale).view(np.uint32) == want.view(np.uint32)
+    assert m.info.rope_freq_base == 5e5
+    base_logits = m.logits([1, 2, 3])
+    m.close()
+    m = oracle.Model(S.with_metadata(g, [], drop=lambda k: k == "llama.rope.freq_base"))
+    assert m.info.rope_freq_base == 10000.0
+    m.close()
+    m = oracle.Model(S.with_metadata(g, [("llama.attention.scale", S.GV_F32, 0.125)]))
+    assert m.info.attention_scale == 0.125
+    assert not np.array_equal(m.logits([1, 2, 3]), base_logits)  # the scale reaches the scores
+    m.close()
 
 
 def test_oracle_refuses_token_ids_outside_the_vocabulary(oracle, base):
