@@ -24,6 +24,7 @@ typedef struct {
     int escapes;
 } wstate;
 
+/* next_window_start (det-cli main.rs:772-778) */
 static size_t next_window_start(size_t pos, size_t ws, size_t n_ctx, size_t overlap) {
     size_t d = pos > ws ? pos - ws : 0;
     if (d >= n_ctx) return pos > overlap ? pos - overlap : 0;
@@ -102,6 +103,7 @@ static int ws_decode_symbol(wstate* w, rc_dec* d, uint32_t* symbol) {
     return rc_dec_advance(d, r.cum, r.freq, r.total);
 }
 
+/* validate_window (det-cli main.rs:810-826) */
 static int validate_window(size_t n_ctx, size_t overlap, size_t model_ctx) {
     if (n_ctx == 0 || n_ctx > model_ctx || overlap >= n_ctx) return REF_ERR_WINDOW;
     return REF_OK;

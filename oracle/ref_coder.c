@@ -107,6 +107,7 @@ int coder_decoder_freqs(const float* logits, size_t n, size_t tail, uint32_t* fr
     return REF_OK;
 }
 
+/* logits_to_decoder_distribution_impl + DecoderDistribution::total (det-coder cdf.rs:201-245, 388) */
 int ref_decoder_total(const float* logits, size_t n, int byte_escapes, uint64_t* total) {
     uint32_t* f = (uint32_t*)malloc(sizeof(uint32_t) * (n ? n : 1));
     if (!f) return REF_ERR_ALLOC;

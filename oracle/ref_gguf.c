@@ -317,6 +317,7 @@ void gg_free(gg_file* f) {
     memset(f, 0, sizeof *f);
 }
 
+/* Gguf::metadata_value (det-gguf lib.rs:278-281) */
 const gg_kv* gg_find(const gg_file* f, const char* key) {
     for (size_t i = 0; i < f->n_kv; i++)
         if (strcmp(f->kv[i].key, key) == 0) return &f->kv[i];
@@ -353,12 +354,14 @@ int gg_str_eq(const gg_file* f, const char* key, const char* want, int* eq) {
     return GG_OK;
 }
 
+/* Gguf::tensor (det-gguf lib.rs:305-313): a duplicate name is an error */
 int gg_find_tensor(const gg_file* f, const char* name, const gg_tensor** out) {
     for (size_t i = 0; i < f->n_tensors; i++)
         if (strcmp(f->tensors[i].name, name) == 0) { *out = &f->tensors[i]; return GG_OK; }
     return GG_TENSOR_NOT_FOUND;
 }
 
+/* Gguf::tensor_data (det-gguf lib.rs:314-338) */
 int gg_tensor_data(const gg_file* f, const uint8_t* bytes, const char* name, const uint8_t** data, size_t* len) {
     const gg_tensor* t;
     int st = gg_find_tensor(f, name, &t);

@@ -233,6 +233,7 @@ static void gemv_range(void* p, size_t b, size_t e) {
     }
 }
 
+/* WeightMatrix::needs_q8a (det-model lib.rs:488-490) */
 static int needs_q8a(const ref_matrix* m) {
     return m->type == GT_Q8_0 || m->type == GT_Q4_0 || m->type == GT_Q4_K;
 }
@@ -470,6 +471,7 @@ static int build_rope(const ref_config* c, size_t positions, float* cs, float* s
     return REF_OK;
 }
 
+/* RopeTables::llama + KvCache::new + ForwardWorkspace (det-model lib.rs:813-846, 849, 963-1031) */
 int ref_state_init(ref_state* s, const ref_model* m, size_t n_ctx) {
     memset(s, 0, sizeof *s);
     const ref_config* c = &m->cfg;
@@ -583,6 +585,7 @@ int ref_forward_one(ref_state* s, size_t token, size_t pos) {
 }
 
 /* ---- loading --------------------------------------------------------------------- */
+/* read_f32_vector and the dense (F32 / F16) matrix readers (det-model lib.rs:1694, 1793-1795) */
 static int read_dense(const gg_file* g, const uint8_t* bytes, const char* name, const gg_tensor* t, float** out) {
     const uint8_t* data;
     size_t len;
@@ -917,6 +920,7 @@ fail:
 }
 
 /* ---- public entry points ------------------------------------------------------- */
+/* F32Llama::from_gguf (det-model lib.rs:1035) */
 int ref_model_load(const uint8_t* gguf, size_t len, ref_model** out) {
     gg_file g;
     int gs = gg_parse(gguf, len, &g);

@@ -39,12 +39,14 @@ float ref_dot_f32(const float* x, const float* y, size_t n) {
     return finish_8lane(acc);
 }
 
+/* sum_f32_ref (det-num reduce.rs:14-23): 8 lane chains, fixed combine tree */
 float ref_sum_f32(const float* x, size_t n) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (size_t i = 0; i < n; i++) acc[i & 7] += x[i];
     return finish_8lane(acc);
 }
 
+/* sum_squares_f32_ref (det-num reduce.rs:25-38) */
 float ref_sum_squares_f32(const float* x, size_t n) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (size_t i = 0; i < n; i++) acc[i & 7] += x[i] * x[i];
@@ -260,6 +262,7 @@ static double k_sin(double x, double y, int iy) {
     return x - ((z * (0.5 * y - v * r) - y) - v * S1);
 }
 
+/* k_cos (det-num vendored_libm/k_cos.rs:54) */
 static double k_cos(double x, double y) {
     const double C1 = 4.16666666666666019037e-02;
     const double C2 = -1.38888888888741095749e-03;
@@ -413,6 +416,7 @@ double ref_sin_f64(double x) {
     }
 }
 
+/* cos (det-num vendored_libm/cos.rs:48) */
 double ref_cos_f64(double x) {
     uint32_t ix = (uint32_t)(d2u(x) >> 32) & 0x7fffffffu;
     if (ix <= 0x3fe921fbu) {
@@ -485,6 +489,7 @@ static const uint32_t SHA_K[64] = {
 
 static inline uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
 
+/* Sha256::compress (det-num hash.rs:78): FIPS 180-4 block function */
 static void sha_compress(uint32_t st[8], const uint8_t blk[64]) {
     uint32_t w[64];
     for (int i = 0; i < 16; i++)
