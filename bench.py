@@ -116,6 +116,18 @@ LAYERS = 0  # --layers: cut the headline model's layer count (profiling captures
 PROFILE_ANY_LAYERS = False  # --decode-profile: --layers applies to the profiled configuration
 
 
+def generator_digest():
+    """First 8 hex digits of the SHA-256 of the synthetic GGUF generator's
+    sources: a cached model file is reused only if the same generator made it."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for rel in ("detllm_b200/csrc/synth.c", "detllm_b200/synth.py"):
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:8]
+
+
 def model_bytes(config, rank=0, ws=1):
     """The seeded GGUF of `config`, built once per box (rank 0) into /tmp."""
     import dataclasses
@@ -125,7 +137,8 @@ def model_bytes(config, rank=0, ws=1):
     spec = S.CONFIGS[config]
     if LAYERS and (config == HEADLINE or PROFILE_ANY_LAYERS):
         spec = dataclasses.replace(spec, n_layer=LAYERS)
-    path = os.path.join(tempfile.gettempdir(), f"detllm_bench_{config}_L{spec.n_layer}_s{spec.seed}.gguf")
+    path = os.path.join(tempfile.gettempdir(),
+                        f"detllm_bench_{config}_L{spec.n_layer}_s{spec.seed}_g{generator_digest()}.gguf")
     if rank == 0 and not os.path.exists(path):
         t = time.time()
         data = S.build_gguf(spec)
